@@ -1,0 +1,337 @@
+"""Benchmark: ZoomKV sparse decode step at the Qwen3-8B shape, 32k context.
+
+Workload (the benchmark's config 1): 36 layers x (32 query / 8 KV heads,
+head_dim 128), batch 8, context 32768 = 32640 retrieval tokens in 16-token
+pages (KIVI 4-bit keys, 4-bit values, group 32) + a 128-token bf16 residual
+window, Quest budget 2048 tokens (128 pages).  One step = the sparse
+decode-attention of one token for all 36 layers; every layer is one fused
+launch (score -> select -> attend), the 36 launches captured in one CUDA
+graph.  Synthetic seeded K/V/q (no datasets or checkpoints in the image);
+per-step inputs (~13 GB) exceed L2 (126 MB), so no L2 flush is needed.
+
+Multi-GPU: KV-head sharding with weak scaling -- each rank owns 8/N KV heads
+of a global batch of 8*N sequences (64 (batch, head) rows per GPU); no
+collective on the data path.  Timing: CUDA events on the launching stream,
+barrier + synchronize around the timed steps, max over ranks.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LAYERS, BATCH, KV_HEADS, Q_HEADS, HEAD_DIM = 36, 8, 8, 32, 128
+CONTEXT, RESIDUAL, BUDGET, PAGE = 32768, 128, 2048, 16
+N_RETRIEVAL = CONTEXT - RESIDUAL
+N_PAGES = N_RETRIEVAL // PAGE
+NK = BUDGET // PAGE
+G = Q_HEADS // KV_HEADS
+METRIC = "sparse decode-step HBM GB/s (% of peak) & tokens/s at Qwen3-8B shape, 32k ctx"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def config(n_gpus):
+    return {"workload": "config1: Qwen3-8B-shape sparse decode step (page mode)", "layers": LAYERS,
+            "global_batch": BATCH * n_gpus, "kv_heads_per_gpu": KV_HEADS // n_gpus, "q_heads": Q_HEADS,
+            "head_dim": HEAD_DIM, "context": CONTEXT, "page": PAGE, "budget_tokens": BUDGET, "residual": RESIDUAL,
+            "kivi_bits": 4, "value_group": 32, "parallelism": f"kv-head shard x{n_gpus}",
+            "l2": "inputs per step ~13 GB >> L2 126 MB (no flush needed)"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int):
+        self.index, self.samples, self.proc = index, [], None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        mhz = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            for n, v in zip(names, s[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------------- CPU arms
+def cpu_sample_layer(seed: int, threads: int):
+    """One layer of page-mode cache built by the oracle's encoder on the host:
+    8 distinct full-size rows (one sequence x 8 KV heads), tiled so every
+    host thread has rows to decode.  Returns the oracle's page-decode inputs."""
+    import oracle as O
+    rng = np.random.default_rng(seed)
+    R = KV_HEADS
+    # keys/values drawn directly on the host for the CPU sample (N(0,1), 4
+    # outlier channels x10 per head; RoPE is immaterial to CPU timing)
+    k = rng.standard_normal((R, N_RETRIEVAL + RESIDUAL, HEAD_DIM), dtype=np.float32)
+    for r in range(R):
+        k[r, :, rng.choice(HEAD_DIM, 4, replace=False)] *= 10.0
+    v = rng.standard_normal((R, N_RETRIEVAL + RESIDUAL, HEAD_DIM), dtype=np.float32)
+    kb, vb = O.f32_to_bf16(k), O.f32_to_bf16(v)
+    mn, mx, _, kc = O.kivi_encode_chunks(kb[:, :N_RETRIEVAL])
+    codes, meta = O.vquant_tokens(vb[:, :N_RETRIEVAL])
+    vc, vm = O.page_layout_values(codes, meta)
+    q = O.f32_to_bf16(rng.standard_normal((R, G, HEAD_DIM), dtype=np.float32))
+    near_k = np.ascontiguousarray(kb[:, N_RETRIEVAL:])
+    near_v = np.ascontiguousarray(vb[:, N_RETRIEVAL:])
+    reps = max(1, -(-threads // R))
+    tile = lambda a: np.ascontiguousarray(np.concatenate([a] * reps, axis=0)) if reps > 1 else a
+    d = dict(q=q, mn=mn, mx=mx, kc=kc, vc=vc, vm=vm, near_k=near_k, near_v=near_v)
+    return {k: tile(v) for k, v in d.items()}
+
+
+def cpu_decode(data, threads):
+    import oracle as O
+    t0 = time.perf_counter()
+    O.page_decode(data["q"], data["mn"], data["mx"], None, data["kc"], data["vc"], data["vm"], data["near_k"],
+                  data["near_v"], N_PAGES, NK, RESIDUAL, 1.0 / HEAD_DIM ** 0.5, threads=threads)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(threads, target_s=12.0):
+    """Time the oracle port of the path on a bounded sample: full-size rows
+    (32k context) of one layer, batch 1 x 8 heads, repeated; extrapolated to
+    the 36-layer step of batch 8 (tokens/s)."""
+    data = cpu_sample_layer(1, threads)
+    rows = data["q"].shape[0]
+    cpu_decode(data, threads)  # warm
+    times = []
+    t_end = time.perf_counter() + target_s
+    while time.perf_counter() < t_end or len(times) < 2:
+        times.append(cpu_decode(data, threads))
+    per_row = min(times) / rows
+    step = per_row * BATCH * KV_HEADS * LAYERS
+    return {"value": BATCH / step, "unit": "tokens/s", "cores": min(threads, rows), "kind": "port",
+            "sample": f"oracle page decode of {rows} full-size (32k ctx) rows of one layer x {len(times)} reps, "
+                      f"best rep, scaled to the 36-layer step of batch 8",
+            "ms_per_step": step * 1e3}
+
+
+def run_reference(args, n_gpus, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    data = cpu_sample_layer(1, threads)
+    rows = data["q"].shape[0]
+    for _ in range(args.warmup):
+        cpu_decode(data, threads)
+    times = [cpu_decode(data, threads) for _ in range(args.steps)]
+    per_row = sum(times) / len(times) / rows
+    global_batch = BATCH * n_gpus
+    step_s = per_row * global_batch * KV_HEADS * LAYERS  # the whole job's step on this host
+    value = global_batch / step_s
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": n_gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config(n_gpus),
+            "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": min(threads, rows), "kind": "port",
+                             "sample": f"each step = oracle page decode of {rows} full-size (32k ctx) rows of one "
+                                       "layer, scaled to the 36-layer step of the global batch"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------- GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    n_gpus = max(world, 1)
+    if args.impl == "reference":
+        run_reference(args, n_gpus, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    from zoomkv_revision_b200 import ops
+    from zoomkv_revision_b200 import workload as W
+
+    heads = KV_HEADS // n_gpus if KV_HEADS % n_gpus == 0 else KV_HEADS
+    bs = BATCH * n_gpus if KV_HEADS % n_gpus == 0 else BATCH
+    rows = bs * heads
+    layers = args.layers
+    caches, qs, outs = [], [], []
+    for l in range(layers):
+        pc, _ = W.build_page_cache(1000 * rank + l, bs, heads, N_RETRIEVAL, RESIDUAL, dev)
+        caches.append(pc)
+        g = torch.Generator(device=dev).manual_seed(77 + l + 1000 * rank)
+        qs.append(W.synth_query(g, bs, heads * G, dev))
+        outs.append(torch.empty(bs, 1, heads * G, HEAD_DIM, dtype=torch.bfloat16, device=dev))
+    torch.cuda.synchronize()
+    layer_structs = [pc.layer() for pc in caches]
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        for l in range(layers):
+            ops.page_decode(qs[l], layer_structs[l], N_PAGES, NK, RESIDUAL, out=outs[l], status=status)
+
+    with torch.cuda.stream(stream):
+        step()  # warm / load
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        graph.replay()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        barrier()
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            ev1.record(stream)
+        barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device status {int(status.item())} (bounded wait expired)")
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    # e2e through the public op with host buffers: H2D of q, D2H of out per layer
+    q_host = [q.cpu().pin_memory() for q in qs]
+    o_host = [torch.empty_like(o, device="cpu").pin_memory() for o in outs]
+    q_dev = [torch.empty_like(q) for q in qs]
+
+    def e2e_step():
+        for l in range(layers):
+            q_dev[l].copy_(q_host[l], non_blocking=True)
+            ops.page_decode(q_dev[l], layer_structs[l], N_PAGES, NK, RESIDUAL, out=outs[l], status=status)
+            o_host[l].copy_(outs[l], non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, args.steps // 2)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+    barrier()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+
+    peak, peak_kind = load_peaks()
+    bytes_launch = W.page_algorithmic_bytes(rows, N_PAGES, NK, RESIDUAL, G)
+    launch_s = ms / 1e3 / layers
+    achieved = bytes_launch / launch_s / 1e9
+    # head-sharded ranks all serve the same global batch; non-divisible N runs replicas
+    global_batch = bs if heads * n_gpus == KV_HEADS else BATCH * n_gpus
+    tokens_s = global_batch / (ms_max / 1e3)
+    e2e_tokens = global_batch / (e2e_ms / 1e3)
+    h2d = sum(q.numel() * 2 for q in qs)
+    d2h = sum(o.numel() * 2 for o in outs)
+    line = {
+        "metric": METRIC, "value": tokens_s, "unit": "tokens/s", "n_gpus": n_gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config(n_gpus),
+        "hbm_gbs_per_gpu": achieved, "hbm_frac_of_peak": achieved / peak,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "kernel": "page_decode_kernel",
+                     "bytes_per_launch": bytes_launch, "launch_us": launch_s * 1e6, "traffic": None},
+        "e2e": {"value": e2e_tokens, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": layers * args.steps,
+        "clocks": clk.summary(),
+    }
+    prof = os.path.join(ROOT, "profiles", "page_decode_traffic.json")
+    if os.path.exists(prof):
+        with open(prof) as f:
+            line["roofline"]["traffic"] = json.load(f).get("traffic_bytes_per_launch")
+    if rank == 0 and n_gpus == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(os.cpu_count() or 1)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

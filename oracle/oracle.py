@@ -1,0 +1,279 @@
+"""ctypes front-end of the C oracle (oracle/zkv_oracle.c) plus numpy helpers.
+
+TEST INFRASTRUCTURE ONLY: this module is the checker used by tests/, by
+__graft_entry__.smoke() and by bench.py's CPU-baseline legs.  It never runs
+on the product path.  Each wrapper names the reference function it restates
+(paths relative to runtime/zoomkv_urania_runtime_20261011/).
+
+bf16 arrays are numpy uint16 bit patterns throughout.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libzkv_oracle.so")
+
+__all__ = [
+    "build_oracle", "lib", "bf16_to_f32", "f32_to_bf16", "kivi_encode_chunks", "vquant_tokens",
+    "quest_score", "topk_f32", "topk_i32", "chunk_density", "mask_from_topk", "kivi_qk",
+    "topk_gather_concat", "attn_dense", "page_decode", "lse_merge", "kivi_dequant_chunk",
+    "vdequant_tokens", "page_layout_values",
+]
+
+
+def build_oracle(force: bool = False) -> str:
+    if force or not os.path.exists(LIB_PATH) or \
+            os.path.getmtime(LIB_PATH) < os.path.getmtime(os.path.join(HERE, "zkv_oracle.c")):
+        subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+_LIB = None
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            build_oracle()
+        _LIB = ctypes.CDLL(LIB_PATH)
+    return _LIB
+
+
+def _p(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"], "oracle arrays must be C-contiguous"
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+# ----------------------------------------------------------------- bf16 utils
+def bf16_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16(f: np.ndarray) -> np.ndarray:
+    u = np.ascontiguousarray(f, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+# ----------------------------------------------------------------- encode
+def kivi_encode_chunks(keys: np.ndarray, chunk: int = 16):
+    """keys [..., n_chunks*chunk, D] bf16 -> (min, max, centroid [..., n_chunks, D],
+    packed [..., n_chunks, D/8, chunk] int32).  Restates
+    _compute_and_store_chunk_minmax + _kivi_pack_chunks for aligned chunks."""
+    L = lib()
+    keys = np.ascontiguousarray(keys, dtype=np.uint16)
+    *lead, T, D = keys.shape
+    nc = T // chunk
+    flat = np.ascontiguousarray(keys.reshape(-1, T, D)[:, :nc * chunk])
+    R = flat.shape[0]
+    mn = np.empty((R, nc, D), np.uint16)
+    mx = np.empty_like(mn)
+    ce = np.empty_like(mn)
+    pk = np.empty((R, nc, D // 8, chunk), np.int32)
+    L.orc_kivi_encode_rows(_p(flat), R, nc * chunk, D, chunk, _p(mn), _p(mx), _p(ce), _p(pk))
+    shp = tuple(lead)
+    return (mn.reshape(shp + (nc, D)), mx.reshape(shp + (nc, D)), ce.reshape(shp + (nc, D)),
+            pk.reshape(shp + (nc, D // 8, chunk)))
+
+
+def vquant_tokens(v: np.ndarray, group: int = 32):
+    """v [..., D] bf16 -> (codes [..., D/8] int32, meta [..., D/group, 2] bf16)."""
+    L = lib()
+    v = np.ascontiguousarray(v, dtype=np.uint16)
+    D = v.shape[-1]
+    flat = v.reshape(-1, D)
+    codes = np.empty((flat.shape[0], D // 8), np.int32)
+    meta = np.empty((flat.shape[0], D // group, 2), np.uint16)
+    L.orc_vquant_rows(_p(flat), ctypes.c_int64(flat.shape[0]), D, group, _p(codes), _p(meta))
+    return codes.reshape(v.shape[:-1] + (D // 8,)), meta.reshape(v.shape[:-1] + (D // group, 2))
+
+
+def _scale_ladder(mn: np.ndarray, mx: np.ndarray) -> np.ndarray:
+    diff = f32_to_bf16(bf16_to_f32(mx) - bf16_to_f32(mn))
+    return f32_to_bf16(bf16_to_f32(diff) / np.float32(15.0))
+
+
+def _dequant_ladder(codes: np.ndarray, scale: np.ndarray, zero: np.ndarray) -> np.ndarray:
+    prod = f32_to_bf16(codes.astype(np.float32) * bf16_to_f32(scale))
+    return f32_to_bf16(bf16_to_f32(prod) + bf16_to_f32(zero))
+
+
+def kivi_dequant_chunk(packed: np.ndarray, mn: np.ndarray, mx: np.ndarray) -> np.ndarray:
+    """packed [..., D/8, chunk] + per-chunk mn/mx [..., D] -> keys [..., chunk, D] bf16
+    (dequant_kcache_4bit, cache_hub/kivi/qk_dot.py:253-305)."""
+    npk, chunk = packed.shape[-2:]
+    w = packed.astype(np.uint32).swapaxes(-1, -2)                       # [..., chunk, D/8]
+    codes = (w[..., None] >> (4 * np.arange(8, dtype=np.uint32))) & 15  # [..., chunk, D/8, 8]
+    codes = codes.reshape(w.shape[:-1] + (npk * 8,))
+    scale = _scale_ladder(mn, mx)[..., None, :]
+    return _dequant_ladder(codes, scale, mn[..., None, :])
+
+
+def vdequant_tokens(codes: np.ndarray, meta: np.ndarray) -> np.ndarray:
+    """codes [..., D/8] int32 + meta [..., D/32, 2] -> values [..., D] bf16."""
+    w = codes.astype(np.uint32)
+    c = ((w[..., None] >> (4 * np.arange(8, dtype=np.uint32))) & 15).reshape(w.shape[:-1] + (w.shape[-1] * 8,))
+    grp = c.shape[-1] // meta.shape[-2]
+    scale = np.repeat(meta[..., 0], grp, axis=-1)
+    zero = np.repeat(meta[..., 1], grp, axis=-1)
+    return _dequant_ladder(c, scale, zero)
+
+
+# ----------------------------------------------------------------- scoring / top-k
+def quest_score(raw_q, mn, mx, valid=None, n_chunks=None):
+    """raw_q [R,128], mn/mx [R,n_max,128] bf16 -> scores [R,n_chunks] fp32."""
+    L = lib()
+    raw_q = np.ascontiguousarray(raw_q, np.uint16).reshape(-1, 128)
+    R = raw_q.shape[0]
+    mn = np.ascontiguousarray(mn, np.uint16).reshape(R, -1, 128)
+    mx = np.ascontiguousarray(mx, np.uint16).reshape(R, -1, 128)
+    n_max = mn.shape[1]
+    n_chunks = n_max if n_chunks is None else int(n_chunks)
+    v = None if valid is None else np.ascontiguousarray(valid, np.uint8).reshape(R, n_max)
+    out = np.empty((R, n_chunks), np.float32)
+    L.orc_quest_score(_p(raw_q), _p(mn), _p(mx), _p(v), _p(out), R, n_chunks, n_max)
+    return out
+
+
+def topk_f32(scores: np.ndarray, k: int) -> np.ndarray:
+    L = lib()
+    s = np.ascontiguousarray(scores, np.float32)
+    R, n = s.reshape(-1, s.shape[-1]).shape
+    out = np.empty((R, k), np.int64)
+    L.orc_topk_f32(_p(s), R, n, ctypes.c_int64(n), k, _p(out))
+    return out.reshape(s.shape[:-1] + (k,))
+
+
+def topk_i32(vals: np.ndarray, k: int) -> np.ndarray:
+    L = lib()
+    s = np.ascontiguousarray(vals, np.int32)
+    R, n = s.reshape(-1, s.shape[-1]).shape
+    out = np.empty((R, k), np.int64)
+    L.orc_topk_i32(_p(s), R, n, ctypes.c_int64(n), k, _p(out))
+    return out.reshape(s.shape[:-1] + (k,))
+
+
+def chunk_density(chunk_ids, centroid, raw_q, n_chunks=None):
+    L = lib()
+    ids = np.ascontiguousarray(chunk_ids, np.int64)
+    R, nk = ids.reshape(-1, ids.shape[-1]).shape
+    cent = np.ascontiguousarray(centroid, np.uint16).reshape(R, -1, 128)
+    n_max = cent.shape[1]
+    q = np.ascontiguousarray(raw_q, np.uint16).reshape(R, 128)
+    out = np.empty((R, nk), np.float32)
+    L.orc_chunk_density(_p(ids), _p(cent), _p(q), _p(out), R, nk,
+                        n_max if n_chunks is None else int(n_chunks), n_max)
+    return out.reshape(ids.shape)
+
+
+def mask_from_topk(positions, nk):
+    L = lib()
+    p = np.ascontiguousarray(positions, np.int64)
+    R, nd = p.reshape(-1, p.shape[-1]).shape
+    m = np.empty((R, nk), np.uint8)
+    L.orc_mask_from_topk(_p(p), _p(m), R, nd, nk)
+    return m.reshape(p.shape[:-1] + (nk,))
+
+
+def kivi_qk(chunk_ids, dense, packed, mn, mx, raw_q, dense_topk, sparse_topk, chunk=16):
+    L = lib()
+    ids = np.ascontiguousarray(chunk_ids, np.int64)
+    R, nk = ids.reshape(-1, ids.shape[-1]).shape
+    dm = np.ascontiguousarray(dense, np.uint8).reshape(R, nk)
+    pk = np.ascontiguousarray(packed, np.int32).reshape(R, -1, 16, chunk)
+    mn = np.ascontiguousarray(mn, np.uint16).reshape(R, -1, 128)
+    mx = np.ascontiguousarray(mx, np.uint16).reshape(R, -1, 128)
+    q = np.ascontiguousarray(raw_q, np.uint16).reshape(R, 128)
+    sc = np.empty((R, nk * chunk), np.float32)
+    ix = np.empty((R, nk * chunk), np.int64)
+    L.orc_kivi_qk(_p(ids), _p(dm), _p(pk), pk.shape[1], _p(mn), _p(mx), mn.shape[1], _p(q), R, nk,
+                  chunk, dense_topk, sparse_topk, _p(sc), _p(ix))
+    return sc.reshape(ids.shape[:-1] + (nk * chunk,)), ix.reshape(ids.shape[:-1] + (nk * chunk,))
+
+
+def topk_gather_concat(scores, lut, skipped, k):
+    L = lib()
+    s = np.ascontiguousarray(scores, np.float32)
+    R, n = s.reshape(-1, s.shape[-1]).shape
+    lu = np.ascontiguousarray(lut, np.int64).reshape(R, n)
+    sk = np.ascontiguousarray(skipped, np.int64).reshape(R, -1)
+    out = np.empty((R, k + sk.shape[1]), np.int64)
+    L.orc_topk_gather_concat(_p(s), _p(lu), _p(sk), _p(out), R, n, k, sk.shape[1],
+                             ctypes.c_int64(out.shape[1]))
+    return out.reshape(s.shape[:-1] + (out.shape[1],))
+
+
+def attn_dense(q: np.ndarray, K: np.ndarray, V: np.ndarray, scale: float):
+    """q [G,D] fp32, K/V [n,D] fp32 -> (out [G,D] fp32, lse [G]) in fp64."""
+    L = lib()
+    q = np.ascontiguousarray(q, np.float32)
+    K = np.ascontiguousarray(K, np.float32)
+    V = np.ascontiguousarray(V, np.float32)
+    G, D = q.shape
+    out = np.empty((G, D), np.float32)
+    lse = np.empty((G,), np.float32)
+    L.orc_attn_dense(_p(q), _p(K), _p(V), K.shape[0], G, D, ctypes.c_float(scale), _p(out), _p(lse))
+    return out, lse
+
+
+def page_decode(q, mn, mx, valid, kcodes, vcodes, vmeta, nearK, nearV, n_c, nk, n_near,
+                scale, threads=1):
+    """Rows = flattened (batch, kv_head).  See zkv_oracle.h:orc_page_decode."""
+    L = lib()
+    q = np.ascontiguousarray(q, np.uint16)
+    R, G, D = q.shape
+    arrs = [np.ascontiguousarray(a) for a in (mn, mx, kcodes, vcodes, vmeta, nearK, nearV)]
+    mn, mx, kcodes, vcodes, vmeta, nearK, nearV = arrs
+    n_max = mn.shape[1]
+    near_ld = nearK.shape[1]
+    v = None if valid is None else np.ascontiguousarray(valid, np.uint8)
+    out = np.empty((R, G, D), np.uint16)
+    lse = np.empty((R, G), np.float32)
+    sel = np.empty((R, nk), np.int64)
+    L.orc_page_decode(_p(q), _p(mn), _p(mx), _p(v), _p(kcodes), _p(vcodes), _p(vmeta), _p(nearK),
+                      _p(nearV), R, G, n_max, n_c, nk, near_ld, n_near, ctypes.c_float(scale),
+                      _p(out), _p(lse), _p(sel), int(threads))
+    return out, lse, sel
+
+
+def lse_merge(a, la, b, lb):
+    L = lib()
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    R, dim = a.reshape(-1, a.shape[-1]).shape
+    la = np.ascontiguousarray(la, np.float32).reshape(R)
+    lb = np.ascontiguousarray(lb, np.float32).reshape(R)
+    out = np.empty((R, dim), np.float32)
+    lo = np.empty((R,), np.float32)
+    L.orc_lse_merge(_p(a), _p(la), _p(b), _p(lb), _p(out), _p(lo), R, dim)
+    return out.reshape(a.shape), lo
+
+
+# ----------------------------------------------------------------- layouts
+def page_layout_values(codes: np.ndarray, meta: np.ndarray):
+    """Per-token value codes [R, T, D/8] + meta [R, T, D/32, 2] (T % 16 == 0)
+    -> page layout vcodes_t [R, T/16, D, 2] int32 and vmeta [R, T/16, 2, D/32, 16]
+    (the layout zkv_vquant_encode writes and the page-mode attention reads)."""
+    R, T, W = codes.shape
+    D = W * 8
+    w = codes.astype(np.uint32)
+    c = ((w[..., None] >> (4 * np.arange(8, dtype=np.uint32))) & 15).reshape(R, T, D)
+    P = T // 16
+    c = c.reshape(R, P, 16, D)
+    sh = (4 * np.arange(8, dtype=np.uint32))[:, None]
+    w0 = (c[:, :, :8, :].astype(np.uint32) << sh).sum(axis=2, dtype=np.uint64).astype(np.uint32)
+    w1 = (c[:, :, 8:, :].astype(np.uint32) << sh).sum(axis=2, dtype=np.uint64).astype(np.uint32)
+    vcodes_t = np.stack([w0, w1], axis=-1).view(np.int32)
+    m = meta.reshape(R, P, 16, D // 32, 2)
+    vmeta = np.ascontiguousarray(m.transpose(0, 1, 4, 3, 2))
+    return np.ascontiguousarray(vcodes_t), vmeta

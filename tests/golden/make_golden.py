@@ -1,0 +1,225 @@
+"""Generate golden fixtures from the reference's own PyTorch implementation.
+
+Run in a container where the reference snapshot is mounted (CPU torch is
+enough):
+
+    python tests/golden/make_golden.py --ref /root/reference
+
+It imports the ZoomKV runtime's pure-PyTorch functions, drives them on small
+seeded inputs and stores inputs + outputs as .npz files next to this script.
+The fixtures are committed; the tests only read them (the reference is not
+needed at test time).  bf16 tensors are stored as uint16 bit patterns.
+
+Functions pinned (paths relative to runtime/zoomkv_urania_runtime_20261011/):
+  * polar_cache._compute_and_store_chunk_minmax / _kivi_pack_chunks
+    (cache_hub/polar_cache_quest_density_single_layer_kivi.py:2025-2157,
+    :1965-2020) driven through a stub object, several calls with carry
+  * quant_pack.pack_kcache_4bit / unpack_kcache_4bit (cache_hub/kivi/quant_pack.py)
+  * qk_dot.dequant_kcache_4bit / partial_chunk_kivi_qk_ref (cache_hub/kivi/qk_dot.py)
+  * QuestPytorch.quest_chunk_score (cache_hub/quest/quest_ops.py:22-31)
+  * polar_cache._partial_chunk_density_scores_torch (:2246-2262)
+  * lse_merge_torch (cache_hub/lse_merge/lse_merge.py:79-119)
+  * candidate-budget arithmetic _quest_aligned_candidate_tokens /
+    _quest_candidate_ratio / _refresh_quest_chunk_cache (:1798-1925)
+"""
+from __future__ import annotations
+
+import argparse
+import functools
+import json
+import os
+import sys
+import types
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+RUNTIME = "runtime/zoomkv_urania_runtime_20261011"
+
+
+def bf16_bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().contiguous().to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def synth_keys(gen: torch.Generator, shape, outliers=4, scale=10.0) -> torch.Tensor:
+    """K ~ N(0,1) with `outliers` random channels per head scaled x10 (bf16)."""
+    k = torch.randn(shape, generator=gen, dtype=torch.float32)
+    heads, dim = shape[1], shape[-1]
+    for h in range(heads):
+        ch = torch.randperm(dim, generator=gen)[:outliers]
+        k[:, h, ..., ch] *= scale
+    return k.to(torch.bfloat16)
+
+
+def make_stub(zmod, bs, kv, n_max, chunk=16, dim=128, layers=1):
+    pc = zmod.polar_cache
+    s = types.SimpleNamespace()
+    s._use_quest_chunk_coarse = True
+    s.quest_chunk_size = chunk
+    s._kivi_bits = 4
+    s._chunk_n_max = n_max
+    s._chunk_carry_count = [0] * layers
+    s._chunk_valid_end = [0] * layers
+    s._chunk_carry_keys = [torch.zeros(bs, kv, chunk - 1, dim, dtype=torch.bfloat16) for _ in range(layers)]
+    s._chunk_merge_buffer = [torch.zeros(bs, kv, chunk, dim, dtype=torch.bfloat16) for _ in range(layers)]
+    s._chunk_key_min_gpu = [torch.zeros(bs, kv, n_max, dim, dtype=torch.bfloat16) for _ in range(layers)]
+    s._chunk_key_max_gpu = [torch.zeros(bs, kv, n_max, dim, dtype=torch.bfloat16) for _ in range(layers)]
+    s._chunk_key_centroid_gpu = [torch.zeros(bs, kv, n_max, dim, dtype=torch.bfloat16) for _ in range(layers)]
+    s._chunk_valid_mask_gpu = [torch.zeros(bs, kv, n_max, dtype=torch.bool) for _ in range(layers)]
+    s.key_kivi_packed_gpu = [torch.zeros(bs, kv, n_max, dim // 8, chunk, dtype=torch.int32) for _ in range(layers)]
+    s._kivi_pack_chunks = functools.partial(pc._kivi_pack_chunks, s)
+    s._compute_and_store_chunk_minmax = functools.partial(pc._compute_and_store_chunk_minmax, s)
+    return s
+
+
+def gen_encode(zmod, out):
+    """Prefill of 75 retrieval tokens, then updates of 30, 7, 40 tokens
+    (exercises aligned chunks, carry append, carry merge, tail carry)."""
+    g = torch.Generator().manual_seed(1234)
+    bs, kv, dim, chunk = 2, 2, 128, 16
+    seg = [75, 30, 7, 40]
+    total = sum(seg)
+    keys = synth_keys(g, (bs, kv, total, dim))
+    n_max = (total + chunk - 1) // chunk + 1
+    s = make_stub(zmod, bs, kv, n_max)
+    start = 0
+    carries = []
+    for n in seg:
+        s._compute_and_store_chunk_minmax(0, keys[:, :, start:start + n, :].contiguous(), abs_token_start=start)
+        start += n
+        carries.append(s._chunk_carry_count[0])
+    np.savez_compressed(
+        os.path.join(out, "encode_carry.npz"),
+        keys=bf16_bits(keys), segments=np.array(seg), carries=np.array(carries),
+        chunk_min=bf16_bits(s._chunk_key_min_gpu[0]), chunk_max=bf16_bits(s._chunk_key_max_gpu[0]),
+        centroid=bf16_bits(s._chunk_key_centroid_gpu[0]),
+        valid=s._chunk_valid_mask_gpu[0].numpy().astype(np.uint8),
+        packed=s.key_kivi_packed_gpu[0].numpy(), valid_end=np.array(s._chunk_valid_end[0]),
+        carry_keys=bf16_bits(s._chunk_carry_keys[0]), n_max=np.array(n_max))
+
+
+def gen_pack(out):
+    from cache_hub.kivi.quant_pack import pack_kcache_4bit, unpack_kcache_4bit
+    g = torch.Generator().manual_seed(7)
+    bs, kv, T, dim, chunk = 1, 2, 64, 128, 16
+    keys = synth_keys(g, (bs, kv, T, dim))
+    kc = keys.view(bs, kv, T // chunk, chunk, dim)
+    mn, mx = kc.amin(dim=3), kc.amax(dim=3)
+    # a flat channel (max == min) exercises the 1e-8 divisor clamp
+    keys2 = keys.clone()
+    keys2[:, :, :chunk, 5] = 0.75
+    mn2, mx2 = keys2.view(bs, kv, T // chunk, chunk, dim).amin(3), keys2.view(bs, kv, T // chunk, chunk, dim).amax(3)
+    packed, scale = pack_kcache_4bit(keys2, mn2, mx2, chunk)
+    approx = unpack_kcache_4bit(packed, mn2, mx2, chunk)
+    np.savez_compressed(
+        os.path.join(out, "kivi_pack.npz"),
+        keys=bf16_bits(keys2), chunk_min=bf16_bits(mn2), chunk_max=bf16_bits(mx2),
+        packed=packed.numpy(), scale=bf16_bits(scale), approx=bf16_bits(approx))
+    del mn, mx
+
+
+def gen_kivi_qk(out):
+    from cache_hub.kivi.qk_dot import dequant_kcache_4bit, partial_chunk_kivi_qk_ref
+    from cache_hub.kivi.quant_pack import pack_kcache_4bit
+    g = torch.Generator().manual_seed(99)
+    bs, kv, n_chunks, chunk, dim, nk = 2, 2, 24, 16, 128, 10
+    keys = synth_keys(g, (bs, kv, n_chunks * chunk, dim))
+    kc = keys.view(bs, kv, n_chunks, chunk, dim)
+    mn, mx = kc.amin(dim=3).contiguous(), kc.amax(dim=3).contiguous()
+    packed_tm, _ = pack_kcache_4bit(keys, mn, mx, chunk)              # [bs,kv,T,16]
+    packed_cm = packed_tm.view(bs, kv, n_chunks, chunk, dim // 8).transpose(-1, -2).contiguous()
+    raw_q = torch.randn(bs, kv, dim, generator=g).to(torch.bfloat16)
+    chunk_ids = torch.stack([torch.randperm(n_chunks, generator=g)[:nk] for _ in range(bs * kv)]).view(bs, kv, nk)
+    dense = torch.rand(bs, kv, nk, generator=g) < 0.4
+    kch = dequant_kcache_4bit(packed_cm, mn, mx, chunk_ids, chunk)
+    sc, ix = partial_chunk_kivi_qk_ref(chunk_ids, dense, packed_cm, mn, mx, raw_q,
+                                       group_size=chunk, dense_topk=16, sparse_topk=8)
+    np.savez_compressed(
+        os.path.join(out, "kivi_qk.npz"),
+        keys=bf16_bits(keys), chunk_min=bf16_bits(mn), chunk_max=bf16_bits(mx), packed=packed_cm.numpy(),
+        raw_q=bf16_bits(raw_q), chunk_ids=chunk_ids.numpy(), dense=dense.numpy().astype(np.uint8),
+        dequant=bf16_bits(kch), ref_scores=sc.numpy(), ref_idx=ix.numpy())
+
+
+def gen_quest_density(zmod, out):
+    from cache_hub.quest.quest_ops import QuestPytorch
+    g = torch.Generator().manual_seed(5)
+    bs, kv, n_max, n_chunks, dim, chunk = 2, 2, 40, 37, 128, 16
+    keys = synth_keys(g, (bs, kv, n_max * chunk, dim))
+    kc = keys.view(bs, kv, n_max, chunk, dim)
+    mn, mx = kc.amin(3).contiguous(), kc.amax(3).contiguous()
+    cent = kc.mean(3).contiguous()
+    valid = torch.ones(bs, kv, n_max, dtype=torch.bool)
+    valid[:, :, 3] = False
+    q = torch.randn(bs, kv, 4, dim, generator=g).to(torch.bfloat16)
+    raw_q = q.mean(dim=2)
+    scores = torch.empty(bs, kv, n_chunks, dtype=torch.float32)
+    QuestPytorch().quest_chunk_score(raw_q, mn, mx, scores, n_chunks, valid)
+    ids = torch.stack([torch.randperm(n_chunks, generator=g)[:12] for _ in range(bs * kv)]).view(bs, kv, 12)
+    ids[0, 0, 0] = -1                     # invalid ids -> -1e30
+    ids[1, 1, 2] = n_max + 3
+    dens = torch.empty(bs, kv, 12)
+    zmod.polar_cache._partial_chunk_density_scores_torch(ids, cent, raw_q, dens)
+    np.savez_compressed(
+        os.path.join(out, "quest_density.npz"),
+        q=bf16_bits(q), raw_q=bf16_bits(raw_q), chunk_min=bf16_bits(mn), chunk_max=bf16_bits(mx),
+        centroid=bf16_bits(cent), valid=valid.numpy().astype(np.uint8), n_chunks=np.array(n_chunks),
+        quest_scores=scores.numpy(), density_ids=ids.numpy(), density=dens.numpy())
+
+
+def gen_lse(out):
+    from cache_hub.lse_merge.lse_merge import lse_merge_torch
+    g = torch.Generator().manual_seed(3)
+    bs, heads, dim = 3, 32, 128
+    a = torch.randn(bs, 1, heads, dim, generator=g).to(torch.bfloat16)
+    b = torch.randn(bs, 1, heads, dim, generator=g).to(torch.bfloat16)
+    la = torch.randn(bs, heads, 1, generator=g) * 3
+    lb = torch.randn(bs, heads, 1, generator=g) * 3
+    m = lse_merge_torch(a, la, b, lb)
+    np.savez_compressed(os.path.join(out, "lse_merge.npz"), a=bf16_bits(a), b=bf16_bits(b),
+                        la=la.numpy(), lb=lb.numpy(), merged=bf16_bits(m))
+
+
+def gen_host_logic(zmod, out):
+    """Candidate budget / nk / n_dense / skipped tail under the production
+    ZoomKV knobs (run/eval_math_aime.py:212-236) and under a forced budget."""
+    pc = zmod.polar_cache
+    rows = []
+    for force in (None, 2048, 1024):
+        s = types.SimpleNamespace(
+            quest_chunk_size=16, quest_coarse_candidate_ratio=0.4, _dynamic_cand_enabled=True,
+            _dynamic_cand_thresholds=[5000, 10001], _dynamic_cand_ratios=[0.7, 0.5, 0.4],
+            _force_cand_tokens=force, cds_dense_ratio=0.3)
+        s._quest_candidate_ratio = functools.partial(pc._quest_candidate_ratio, s)
+        for kv_len in [0, 1, 15, 16, 17, 100, 1000, 4095, 4999, 5000, 5001, 10000, 10001, 10002,
+                       20000, 32640, 32768, 65536, 131072]:
+            tgt = pc._quest_aligned_candidate_tokens(s, kv_len)
+            n_chunks = kv_len // 16
+            nk = max(1, min(n_chunks, tgt // 16)) if kv_len >= 16 else 0
+            n_dense = max(1, int(nk * 0.3)) if nk else 0
+            rows.append(dict(force=force, kv_len=kv_len, cand_tokens=tgt, n_chunks=n_chunks, nk=nk,
+                             n_dense=n_dense, skipped=kv_len - n_chunks * 16))
+    with open(os.path.join(out, "host_logic.json"), "w") as f:
+        json.dump(rows, f, indent=0)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--out", default=HERE)
+    a = ap.parse_args()
+    sys.path.insert(0, os.path.join(a.ref, RUNTIME))
+    torch.set_num_threads(1)
+    import cache_hub.polar_cache_quest_density_single_layer_kivi as zmod
+    gen_encode(zmod, a.out)
+    gen_pack(a.out)
+    gen_kivi_qk(a.out)
+    gen_quest_density(zmod, a.out)
+    gen_lse(a.out)
+    gen_host_logic(zmod, a.out)
+    print("golden fixtures written to", a.out)
+
+
+if __name__ == "__main__":
+    main()

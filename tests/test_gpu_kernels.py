@@ -1,0 +1,241 @@
+"""GPU parity tests: every libzkv kernel against the CPU oracle (bit-exact for
+integer / index / bf16-ladder work, tolerance for attention outputs)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from conftest import from_u16, golden, to_u16
+from zoomkv_revision_b200 import ops
+from zoomkv_revision_b200 import workload as W
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+ATOL, MEAN_REL = 2e-2, 1e-2   # attention output tolerance (bf16)
+
+
+def close(out, ref):
+    out = np.asarray(out, np.float64)
+    ref = np.asarray(ref, np.float64)
+    err = np.abs(out - ref)
+    mean_rel = err.mean() / max(np.abs(ref).mean(), 1e-12)
+    assert err.max() <= ATOL, f"max abs err {err.max():.3e}"
+    assert mean_rel <= MEAN_REL, f"mean rel err {mean_rel:.3e}"
+    return err.max(), mean_rel
+
+
+def rand_keys(seed, bs, h, T):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return W.synth_keys(g, bs, h, T, DEV)
+
+
+# ------------------------------------------------------------------ encode
+def test_kivi_encode_golden_carry_fixture():
+    g = golden("encode_carry.npz")
+    nf = int(g["valid_end"])
+    bs, kv = g["keys"].shape[:2]
+    pc = W.alloc_page_cache(bs, kv, int(g["n_max"]), 1, DEV)
+    ops.kivi_encode_chunks(from_u16(g["keys"][:, :, :nf * 16]), pc.chunk_min, pc.chunk_max, pc.centroid, pc.valid,
+                           pc.kcodes, 0)
+    torch.cuda.synchronize()
+    assert (to_u16(pc.chunk_min)[:, :, :nf] == g["chunk_min"][:, :, :nf]).all()
+    assert (to_u16(pc.chunk_max)[:, :, :nf] == g["chunk_max"][:, :, :nf]).all()
+    assert (to_u16(pc.centroid)[:, :, :nf] == g["centroid"][:, :, :nf]).all()
+    assert (pc.kcodes.cpu().numpy()[:, :, :nf] == g["packed"][:, :, :nf]).all()
+    assert pc.valid[:, :, :nf].all() and not pc.valid[:, :, nf:].any()
+
+
+@pytest.mark.parametrize("chunk_start,n_chunks", [(0, 40), (5, 17)])
+def test_kivi_encode_matches_oracle(chunk_start, n_chunks):
+    k = rand_keys(11 + chunk_start, 2, 3, 16 * n_chunks)
+    n_max = chunk_start + n_chunks + 3
+    pc = W.alloc_page_cache(2, 3, n_max, 1, DEV)
+    ops.kivi_encode_chunks(k, pc.chunk_min, pc.chunk_max, pc.centroid, pc.valid, pc.kcodes, chunk_start)
+    torch.cuda.synchronize()
+    mn, mx, ce, pk = O.kivi_encode_chunks(to_u16(k))
+    sl = slice(chunk_start, chunk_start + n_chunks)
+    assert (to_u16(pc.chunk_min)[:, :, sl] == mn).all()
+    assert (to_u16(pc.chunk_max)[:, :, sl] == mx).all()
+    assert (to_u16(pc.centroid)[:, :, sl] == ce).all()
+    assert (pc.kcodes.cpu().numpy()[:, :, sl] == pk).all()
+
+
+def test_vquant_encode_matches_oracle_with_mid_page_appends():
+    g = torch.Generator(device=DEV).manual_seed(5)
+    v = W.synth_values(g, 2, 2, 48, DEV)
+    n_pages = 3
+    vc = torch.zeros(2, 2, n_pages, 128, 2, dtype=torch.int32, device=DEV)
+    vm = torch.zeros(2, 2, n_pages, 2, 4, 16, dtype=torch.bfloat16, device=DEV)
+    for lo, hi in ((0, 20), (20, 23), (23, 48)):
+        ops.vquant_encode(v[:, :, lo:hi], vc, vm, lo)
+    torch.cuda.synchronize()
+    codes, meta = O.vquant_tokens(to_u16(v).reshape(4, 48, 128))
+    ref_c, ref_m = O.page_layout_values(codes, meta)
+    assert (vc.cpu().numpy().reshape(ref_c.shape) == ref_c).all()
+    assert (to_u16(vm).reshape(ref_m.shape) == ref_m).all()
+
+
+# ------------------------------------------------------------------ selection
+def test_quest_score_bit_exact():
+    rows_bs, h, n_max, n_c = 2, 4, 97, 90
+    k = rand_keys(3, rows_bs, h, 16 * n_max)
+    pc = W.alloc_page_cache(rows_bs, h, n_max, 1, DEV)
+    ops.kivi_encode_chunks(k, pc.chunk_min, pc.chunk_max, pc.centroid, pc.valid, pc.kcodes, 0)
+    pc.valid[0, 1, 7] = False
+    q = torch.randn(rows_bs, h, 128, device=DEV).to(torch.bfloat16)
+    scores = torch.empty(rows_bs, h, n_c, device=DEV)
+    ops.quest_chunk_score(q, pc.chunk_min, pc.chunk_max, scores, n_c, pc.valid)
+    torch.cuda.synchronize()
+    ref = O.quest_score(to_u16(q), to_u16(pc.chunk_min), to_u16(pc.chunk_max),
+                        pc.valid.cpu().numpy().astype(np.uint8), n_c)
+    got = scores.cpu().numpy().reshape(ref.shape)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    assert np.isneginf(got.reshape(2, 4, n_c)[0, 1, 7])
+
+
+@pytest.mark.parametrize("L,k", [(2040, 128), (777, 100), (64, 64), (50, 80), (9000, 1)])
+def test_float_topk_deterministic(L, k):
+    g = torch.Generator(device=DEV).manual_seed(L + k)
+    s = torch.randn(6, L, generator=g, device=DEV)
+    s[0, : L // 2] = 0.5            # heavy ties
+    s[1, ::3] = -float("inf")
+    s[2] = 1.0                      # all equal -> lowest indices
+    out = ops.float_topk(s, min(k, L) if L >= k else L, None) if L >= k else None
+    if L >= k:
+        ref = O.topk_f32(s.cpu().numpy(), k)
+        assert np.array_equal(out.cpu().numpy(), ref)
+    else:
+        # len <= k path (naive fill with -1), exercised through the C ABI
+        o = torch.empty(6, k, dtype=torch.int64, device=DEV)
+        from zoomkv_revision_b200._lib import check, lib
+        check(lib().zkv_topk_f32(s.data_ptr(), 6, L, L, k, o.data_ptr(), torch.cuda.current_stream().cuda_stream),
+              "topk")
+        assert np.array_equal(o.cpu().numpy(), O.topk_f32(s.cpu().numpy(), k))
+
+
+def test_radix_topk_i32():
+    g = torch.Generator(device=DEV).manual_seed(1)
+    v = torch.randint(0, 97, (2, 3, 5000), generator=g, device=DEV, dtype=torch.int32)
+    out = ops.radix_topk_3d(v, 700)
+    assert np.array_equal(out.cpu().numpy(), O.topk_i32(v.cpu().numpy(), 700))
+
+
+def test_density_and_mask_bit_exact():
+    gq = golden("quest_density.npz")
+    ids = torch.from_numpy(gq["density_ids"]).to(DEV)
+    cent = from_u16(gq["centroid"])
+    q = from_u16(gq["raw_q"])
+    out = torch.empty(ids.shape, device=DEV)
+    ops.partial_chunk_density_scores_cuda(ids, cent, q, out)
+    ref = O.chunk_density(gq["density_ids"], gq["centroid"], gq["raw_q"])
+    got = out.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    # vs the reference's own torch (fp32) values: same up to summation order
+    assert np.abs(got - gq["density"]).max() < 1e-5
+    pos = ops.float_topk_3d(out, 3)
+    mask = torch.zeros(ids.shape, dtype=torch.bool, device=DEV)
+    ops.dense_mask_from_topk_cuda(pos, mask)
+    assert np.array_equal(mask.cpu().numpy().astype(np.uint8), O.mask_from_topk(pos.cpu().numpy(), ids.shape[2]))
+
+
+@pytest.mark.parametrize("dense_topk,sparse_topk", [(8, 8), (16, 8), (16, 16)])
+def test_kivi_qk_bit_exact(dense_topk, sparse_topk):
+    gk = golden("kivi_qk.npz")
+    n_max = gk["chunk_min"].shape[2]
+    packed_full = torch.zeros(2, 2, n_max + 5, 16, 16, dtype=torch.int32, device=DEV)
+    packed_full[:, :, :n_max] = torch.from_numpy(gk["packed"]).to(DEV)
+    packed = packed_full[:, :, :n_max]            # chunk-axis slice, as the reference passes it
+    ids = torch.from_numpy(gk["chunk_ids"]).to(DEV)
+    ids[1, 0, 3] = n_max + 2                      # out of range -> -1e30
+    dense = torch.from_numpy(gk["dense"]).to(DEV).bool()
+    nk = ids.shape[2]
+    sc = torch.empty(2, 2, nk * 16, device=DEV)
+    ix = torch.empty(2, 2, nk * 16, dtype=torch.int64, device=DEV)
+    ops.partial_chunk_kivi_qk_dense_sparse_cuda(ids, dense, packed, from_u16(gk["chunk_min"]),
+                                                from_u16(gk["chunk_max"]), from_u16(gk["raw_q"]), dense_topk,
+                                                sparse_topk, 16, sc, ix)
+    torch.cuda.synchronize()
+    rs, ri = O.kivi_qk(ids.cpu().numpy(), gk["dense"], gk["packed"], gk["chunk_min"], gk["chunk_max"], gk["raw_q"],
+                       dense_topk, sparse_topk)
+    assert np.array_equal(sc.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    assert np.array_equal(ix.cpu().numpy(), ri)
+
+
+def test_topk_gather_concat():
+    g = torch.Generator(device=DEV).manual_seed(2)
+    bs, kv, L, k, sk = 2, 3, 1600, 100, 12
+    s = torch.randn(bs, kv, L, generator=g, device=DEV)
+    s[0, 0, 10:40] = 3.0
+    lut = torch.randint(0, 100000, (bs, kv, L), generator=g, device=DEV)
+    skipped_buf = torch.arange(bs * kv * 512, device=DEV).view(bs, kv, 512)
+    skipped = skipped_buf[:, :, :sk]              # strided view, as in the reference
+    out = torch.full((bs, kv, k + 512), -7, dtype=torch.int64, device=DEV)
+    ops.float_topk_gather_concat_3d(s, lut, skipped, out, k)
+    ref = O.topk_gather_concat(s.cpu().numpy(), lut.cpu().numpy(), skipped.contiguous().cpu().numpy(), k)
+    assert np.array_equal(out[:, :, :k + sk].cpu().numpy(), ref)
+    # L <= k naive path
+    out2 = torch.zeros(bs, kv, 64, dtype=torch.int64, device=DEV)
+    ops.float_topk_gather_concat_3d(s[:, :, :40].contiguous(), lut[:, :, :40].contiguous(), skipped[:, :, :0], out2, 40)
+    assert np.array_equal(out2[:, :, :40].cpu().numpy(), lut[:, :, :40].cpu().numpy())
+
+
+# ------------------------------------------------------------------ attention
+def gather_rows(K, idx):
+    return K[idx]
+
+
+@pytest.mark.parametrize("split", [1, 2, 4, 8])
+def test_attn_rows_matches_oracle(split):
+    g = torch.Generator(device=DEV).manual_seed(9)
+    bs, H, G, cap = 2, 2, 4, 300
+    K = W.synth_keys(g, bs, H, cap, DEV)
+    V = W.synth_values(g, bs, H, cap, DEV)
+    q = W.synth_query(g, bs, H * G, DEV)
+    sel = torch.stack([torch.randperm(200, generator=g, device=DEV)[:37] for _ in range(bs * H)]).view(bs, H, 37)
+    out = ops.attn_rows(q, K, V, seg0=(0, 4), sel=sel, sel_offset=4, seg1=(250, 290), split=split)
+    lse = torch.empty(bs * H, G, device=DEV)
+    ops.attn_rows(q, K, V, seg0=(0, 4), sel=sel, sel_offset=4, seg1=(250, 290), split=split, lse=lse)
+    torch.cuda.synchronize()
+    Kf, Vf, qf = (O.bf16_to_f32(to_u16(t)) for t in (K, V, q))
+    for b in range(bs):
+        for h in range(H):
+            idx = np.concatenate([np.arange(0, 4), sel[b, h].cpu().numpy() + 4, np.arange(250, 290)])
+            ro, rl = O.attn_dense(qf[b, 0, h * G:(h + 1) * G], Kf[b, h][idx], Vf[b, h][idx], 1 / np.sqrt(128))
+            close(O.bf16_to_f32(to_u16(out[b, 0, h * G:(h + 1) * G])), ro)
+            assert np.abs(lse.cpu().numpy()[b * H + h] - rl).max() < 1e-3
+
+
+@pytest.mark.parametrize("cluster", [1, 2, 4, 8])
+@pytest.mark.parametrize("n_retrieval,nk,n_near", [(16 * 300, 24, 37), (16 * 97, 97, 0), (16 * 130, 16, 128)])
+def test_page_decode_matches_oracle(cluster, n_retrieval, nk, n_near):
+    bs, H, G = 2, 2, 4
+    pc, _ = W.build_page_cache(7, bs, H, n_retrieval, n_near, DEV)
+    g = torch.Generator(device=DEV).manual_seed(17)
+    q = W.synth_query(g, bs, H * G, DEV)
+    sel = torch.empty(bs * H, nk, dtype=torch.int64, device=DEV)
+    lse = torch.empty(bs * H, G, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = ops.page_decode(q, pc.layer(), pc.n_c, nk, n_near, lse=lse, sel_out=sel, status=status, cluster=cluster)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    R = bs * H
+    ro, rl, rsel = O.page_decode(
+        to_u16(q).reshape(R, G, 128), to_u16(pc.chunk_min).reshape(R, -1, 128), to_u16(pc.chunk_max).reshape(R, -1, 128),
+        pc.valid.cpu().numpy().astype(np.uint8).reshape(R, -1), pc.kcodes.cpu().numpy().reshape(R, -1, 16, 16),
+        pc.vcodes_t.cpu().numpy().reshape(R, -1, 128, 2), to_u16(pc.vmeta).reshape(R, -1, 2, 4, 16),
+        to_u16(pc.near_k).reshape(R, pc.near_k.shape[2], 128), to_u16(pc.near_v).reshape(R, pc.near_k.shape[2], 128),
+        pc.n_c, nk, n_near, 1 / np.sqrt(128), threads=4)
+    assert np.array_equal(sel.cpu().numpy(), rsel)
+    close(O.bf16_to_f32(to_u16(out)).reshape(R, G, 128), O.bf16_to_f32(ro))
+    assert np.abs(lse.cpu().numpy() - rl).max() < 1e-3
+
+
+def test_lse_merge_golden():
+    gl = golden("lse_merge.npz")
+    a, b = from_u16(gl["a"]), from_u16(gl["b"])
+    la, lb = torch.from_numpy(gl["la"]).to(DEV), torch.from_numpy(gl["lb"]).to(DEV)
+    m = ops.lse_merge_cuda(a, la, b, lb)
+    got = O.bf16_to_f32(to_u16(m))
+    ref = O.bf16_to_f32(gl["merged"])
+    assert np.abs(got - ref).max() <= 2 ** -7 * np.abs(ref).max()
+    assert (to_u16(m) == gl["merged"]).mean() > 0.99

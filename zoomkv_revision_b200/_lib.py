@@ -1,0 +1,88 @@
+"""ctypes binding of libzkv.so (the C ABI declared in include/zkv.h).
+
+The library is loaded from the package directory.  There is no fallback: if
+the shared object is missing, cannot be loaded, or a call returns a non-zero
+status, a RuntimeError is raised.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libzkv.so")
+
+ZKV_OK = 0
+ZKV_ERR_TIMEOUT = 6
+
+_c_void_p = ctypes.c_void_p
+_i32 = ctypes.c_int
+_i64 = ctypes.c_int64
+_f32 = ctypes.c_float
+
+
+class ZkvPageLayer(ctypes.Structure):
+    """Mirror of `zkv_page_layer` (include/zkv.h)."""
+    _fields_ = [
+        ("chunk_min", _c_void_p), ("chunk_max", _c_void_p), ("valid", _c_void_p),
+        ("kcodes", _c_void_p), ("vcodes_t", _c_void_p), ("vmeta", _c_void_p),
+        ("near_k", _c_void_p), ("near_v", _c_void_p), ("near_ld", _i64),
+    ]
+
+
+# name -> argtypes (restype is int status unless noted)
+_SIGNATURES = {
+    "zkv_kivi_encode": [_c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                        _c_void_p, _c_void_p],
+    "zkv_vquant_encode": [_c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p],
+    "zkv_quest_score": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p],
+    "zkv_topk_f32": [_c_void_p, _i32, _i32, _i64, _i32, _c_void_p, _c_void_p],
+    "zkv_topk_i32": [_c_void_p, _i32, _i32, _i64, _i32, _c_void_p, _c_void_p],
+    "zkv_chunk_density": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _c_void_p],
+    "zkv_mask_from_topk": [_c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p],
+    "zkv_kivi_qk": [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _c_void_p, _i32, _c_void_p, _i32, _i32, _i32,
+                    _i32, _c_void_p, _c_void_p, _i64, _c_void_p],
+    "zkv_topk_gather_concat": [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p, _i32, _i32, _i32, _i32, _i64, _c_void_p],
+    "zkv_attn_rows": [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _i32, _i64, _i64,
+                      _i32, _i32, _f32, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p],
+    "zkv_page_decode": [_c_void_p, ctypes.POINTER(ZkvPageLayer), _i32, _i32, _i32, _i32, _i32, _i32, _f32, _c_void_p,
+                        _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p],
+    "zkv_lse_merge": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p],
+    "zkv_lse_merge_n": [_c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p],
+    "zkv_version": [],
+    "zkv_status_string": [_i32],
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def exported_symbols() -> list[str]:
+    return sorted(_SIGNATURES)
+
+
+def lib() -> ctypes.CDLL:
+    """Load libzkv.so (raises if absent -- the CUDA path has no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"libzkv.so not found at {LIB_PATH}; build it with "
+                    "`python -m zoomkv_revision_b200.build` (no CPU fallback exists)")
+            h = ctypes.CDLL(LIB_PATH)
+            for name, argt in _SIGNATURES.items():
+                fn = getattr(h, name)
+                fn.argtypes = argt
+                fn.restype = ctypes.c_char_p if name == "zkv_status_string" else ctypes.c_int
+            _lib = h
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != ZKV_OK:
+        msg = lib().zkv_status_string(int(status)).decode()
+        raise RuntimeError(f"{what} failed: status {status} ({msg})")

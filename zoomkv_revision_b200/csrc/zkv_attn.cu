@@ -1,0 +1,753 @@
+// zkv_attn.cu -- decode attention for the ZoomKV sparse path.
+//
+//  * zkv_page_decode: one fused launch per layer.  A thread-block cluster of
+//    CS CTAs owns one (batch, kv_head) row:
+//      phase 1  each CTA streams its share of the Quest min/max metadata with
+//               1-D TMA bulk copies (4-stage mbarrier ring) and scores chunks;
+//      phase 2  scores are exchanged through distributed shared memory and
+//               every CTA runs the same deterministic radix top-k;
+//      phase 3  each warp double-buffers its pages (4-bit K, 4-bit V, scales)
+//               with bulk copies and runs QK^T / PV on mma.sync m16n8k16,
+//               dequantising in registers (no bf16 K/V copy is written);
+//      phase 4  warp partials merge in shared memory, CTA partials merge
+//               through distributed shared memory on cluster rank 0.
+//  * zkv_attn_rows: the reference-mode attention over raw bf16 rows gathered
+//    by index (sink / selected / near zones), same warp core and merge.
+//  * zkv_lse_merge / zkv_lse_merge_n: log-sum-exp combine of partials.
+#include "zkv_common.cuh"
+
+namespace zkv {
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = 32 * kAttnWarps;
+constexpr int kRawStride = 136;  // bf16 per padded staged row (272 B, conflict-free B-fragment loads)
+constexpr int kSlotBytes = 4608; // per-warp staging slot (2 per warp)
+// KIVI page slot: kc [16][16] i32 @0, vc [128][2] i32 @1024, vmeta @2048,
+//                 min @2304, max @2560, scale (computed) @2816
+constexpr int kPageTx = 1024 + 1024 + 256 + 256 + 256;
+// RAW8 slot: K rows [8][136] bf16 @0, V rows @2176
+constexpr int kRawV = 8 * kRawStride * 2;
+constexpr int kStages = 4;       // phase-1 ring
+constexpr int kStageChunks = 16; // chunks per stage (2 per half-warp pair per warp)
+constexpr int kRegionBytes = 2 * kAttnWarps * kSlotBytes;  // 36 KB (>= ring 32 KB)
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+struct WarpAttn {
+    float m;          // running max (log2 units) of head g = lane/4
+    float l;          // running sum over this lane's tokens
+    float o[8][4];    // O^T accumulators, m-tile j = dims 16j..16j+15
+    uint32_t qa[8][2];// A fragments of Q (rows = heads), k-step s
+};
+
+__device__ __forceinline__ void warp_attn_init(WarpAttn& st, const uint16_t* q_s, int G) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        if (g < G) {
+            st.qa[s][0] = *reinterpret_cast<const uint32_t*>(q_s + g * kHeadDim + 16 * s + 2 * tig);
+            st.qa[s][1] = *reinterpret_cast<const uint32_t*>(q_s + g * kHeadDim + 16 * s + 8 + 2 * tig);
+        } else {
+            st.qa[s][0] = 0;
+            st.qa[s][1] = 0;
+        }
+    }
+    st.m = -INFINITY;
+    st.l = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) st.o[j][e] = 0.f;
+}
+
+// Online-softmax update with the 4 scores (tokens 2tig, 2tig+1, 8+2tig,
+// 9+2tig) of head g; returns the B fragment of P^T for the PV product.
+__device__ __forceinline__ void warp_softmax(WarpAttn& st, float (&x)[4], int G, uint32_t& b0, uint32_t& b1) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+    float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mnew = fmaxf(st.m, mx);
+    const float alpha = (st.m == -INFINITY) ? 0.f : ex2(st.m - mnew);
+    float p[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p[i] = (x[i] == -INFINITY) ? 0.f : ex2(x[i] - mnew);
+    st.l = st.l * alpha + ((p[0] + p[1]) + (p[2] + p[3]));
+    st.m = mnew;
+    const float a0 = __shfl_sync(0xffffffffu, alpha, (2 * tig) * 4);
+    const float a1 = __shfl_sync(0xffffffffu, alpha, (2 * tig + 1) * 4);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        st.o[j][0] *= a0;
+        st.o[j][1] *= a1;
+        st.o[j][2] *= a0;
+        st.o[j][3] *= a1;
+    }
+    if (g < G) {
+        b0 = pack_bf162(p[0], p[1]);
+        b1 = pack_bf162(p[2], p[3]);
+    } else {
+        b0 = 0;
+        b1 = 0;
+    }
+}
+
+// KIVI page: 16 tokens, 4-bit K (chunk-major) + 4-bit V (page-transposed).
+__device__ __forceinline__ void warp_page_kivi(WarpAttn& st, uint8_t* slot, int G, float sl2) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+    // per-dim KIVI scale of this chunk: bf16(bf16(max - min) / 15)
+    {
+        const uint16_t* mn = reinterpret_cast<const uint16_t*>(slot + 2304);
+        const uint16_t* mx = reinterpret_cast<const uint16_t*>(slot + 2560);
+        uint16_t* sc = reinterpret_cast<uint16_t*>(slot + 2816);
+        const uint2 a = *reinterpret_cast<const uint2*>(mn + 4 * lane);
+        const uint2 b = *reinterpret_cast<const uint2*>(mx + 4 * lane);
+        const uint16_t s0 = kivi_scale_bits((uint16_t)(a.x & 0xffff), (uint16_t)(b.x & 0xffff));
+        const uint16_t s1 = kivi_scale_bits((uint16_t)(a.x >> 16), (uint16_t)(b.x >> 16));
+        const uint16_t s2 = kivi_scale_bits((uint16_t)(a.y & 0xffff), (uint16_t)(b.y & 0xffff));
+        const uint16_t s3 = kivi_scale_bits((uint16_t)(a.y >> 16), (uint16_t)(b.y >> 16));
+        *reinterpret_cast<uint2*>(sc + 4 * lane) =
+            make_uint2((uint32_t)s0 | ((uint32_t)s1 << 16), (uint32_t)s2 | ((uint32_t)s3 << 16));
+        __syncwarp();
+    }
+    const int32_t* kc = reinterpret_cast<const int32_t*>(slot);
+    const uint32_t* mn2 = reinterpret_cast<const uint32_t*>(slot + 2304);
+    const uint32_t* sc2 = reinterpret_cast<const uint32_t*>(slot + 2816);
+    float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        const __nv_bfloat162 sA = bits_bf162(sc2[8 * s + tig]);
+        const __nv_bfloat162 sB = bits_bf162(sc2[8 * s + 4 + tig]);
+        const __nv_bfloat162 mA = bits_bf162(mn2[8 * s + tig]);
+        const __nv_bfloat162 mB = bits_bf162(mn2[8 * s + 4 + tig]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int n = 8 * h + g;
+            const uint32_t w0 = (uint32_t)kc[(2 * s) * kChunk + n];
+            const uint32_t w1 = (uint32_t)kc[(2 * s + 1) * kChunk + n];
+            const uint32_t b0 = bf162_bits(dequant2(codes2_to_bf162(w0 >> (8 * tig), w0 >> (8 * tig + 4)), sA, mA));
+            const uint32_t b1 = bf162_bits(dequant2(codes2_to_bf162(w1 >> (8 * tig), w1 >> (8 * tig + 4)), sB, mB));
+            mma_bf16_16816(sacc[h], st.qa[s][0], 0u, st.qa[s][1], 0u, b0, b1);
+        }
+    }
+    float x[4] = {sacc[0][0] * sl2, sacc[0][1] * sl2, sacc[1][0] * sl2, sacc[1][1] * sl2};
+    uint32_t pb0, pb1;
+    warp_softmax(st, x, G, pb0, pb1);
+    const uint2* vc = reinterpret_cast<const uint2*>(slot + 1024);
+    const uint32_t* vs = reinterpret_cast<const uint32_t*>(slot + 2048);
+    const uint32_t* vz = vs + 32;
+#pragma unroll
+    for (int gp = 0; gp < kVGroups; ++gp) {
+        const __nv_bfloat162 sLo = bits_bf162(vs[gp * 8 + tig]);
+        const __nv_bfloat162 sHi = bits_bf162(vs[gp * 8 + 4 + tig]);
+        const __nv_bfloat162 zLo = bits_bf162(vz[gp * 8 + tig]);
+        const __nv_bfloat162 zHi = bits_bf162(vz[gp * 8 + 4 + tig]);
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+            const int j = 2 * gp + jj;
+            const int d = 16 * j + g;
+            const uint2 wa = vc[d];
+            const uint2 wb = vc[d + 8];
+            const uint32_t a0 = bf162_bits(dequant2(codes2_to_bf162(wa.x >> (8 * tig), wa.x >> (8 * tig + 4)), sLo, zLo));
+            const uint32_t a2 = bf162_bits(dequant2(codes2_to_bf162(wa.y >> (8 * tig), wa.y >> (8 * tig + 4)), sHi, zHi));
+            const uint32_t a1 = bf162_bits(dequant2(codes2_to_bf162(wb.x >> (8 * tig), wb.x >> (8 * tig + 4)), sLo, zLo));
+            const uint32_t a3 = bf162_bits(dequant2(codes2_to_bf162(wb.y >> (8 * tig), wb.y >> (8 * tig + 4)), sHi, zHi));
+            mma_bf16_16816(st.o[j], a0, a1, a2, a3, pb0, pb1);
+        }
+    }
+}
+
+// RAW8 item: up to 8 raw bf16 token rows (padded stride); bit t of `present`
+// says whether token t is real (absent rows were zero-filled).
+__device__ __forceinline__ void warp_page_raw8(WarpAttn& st, const uint8_t* slot, unsigned present, int G, float sl2) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+    const uint16_t* K = reinterpret_cast<const uint16_t*>(slot);
+    const uint16_t* V = reinterpret_cast<const uint16_t*>(slot + kRawV);
+    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(K + g * kRawStride + 16 * s + 2 * tig);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(K + g * kRawStride + 16 * s + 8 + 2 * tig);
+        mma_bf16_16816(sacc, st.qa[s][0], 0u, st.qa[s][1], 0u, b0, b1);
+    }
+    float x[4] = {((present >> (2 * tig)) & 1u) ? sacc[0] * sl2 : -INFINITY,
+                  ((present >> (2 * tig + 1)) & 1u) ? sacc[1] * sl2 : -INFINITY, -INFINITY, -INFINITY};
+    uint32_t pb0, pb1;
+    warp_softmax(st, x, G, pb0, pb1);
+    pb1 = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int d = 16 * j + g;
+        const uint32_t a0 = (uint32_t)V[(2 * tig) * kRawStride + d] | ((uint32_t)V[(2 * tig + 1) * kRawStride + d] << 16);
+        const uint32_t a1 =
+            (uint32_t)V[(2 * tig) * kRawStride + d + 8] | ((uint32_t)V[(2 * tig + 1) * kRawStride + d + 8] << 16);
+        mma_bf16_16816(st.o[j], a0, a1, 0u, 0u, pb0, pb1);
+    }
+}
+
+// Warp-level issue of a KIVI page into `slot` (lane 0 issues all copies).
+__device__ __forceinline__ void issue_kivi_page(uint8_t* slot, uint64_t* bar, const zkv_page_layer& L, int64_t row,
+                                                int n_max, int64_t c) {
+    if ((threadIdx.x & 31) == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive_expect_tx(bar, kPageTx);
+        const int64_t pc = row * n_max + c;
+        bulk_g2s(slot, L.kcodes + pc * (kWords * kChunk), 1024, bar);
+        bulk_g2s(slot + 1024, L.vcodes_t + pc * (kHeadDim * 2), 1024, bar);
+        bulk_g2s(slot + 2048, reinterpret_cast<const uint16_t*>(L.vmeta) + pc * (2 * kVGroups * kChunk), 256, bar);
+        bulk_g2s(slot + 2304, reinterpret_cast<const uint16_t*>(L.chunk_min) + pc * kHeadDim, 256, bar);
+        bulk_g2s(slot + 2560, reinterpret_cast<const uint16_t*>(L.chunk_max) + pc * kHeadDim, 256, bar);
+    }
+}
+
+// Warp-level issue of up to 8 raw rows: row_of(t) gives the token row
+// pointer offset (in tokens) or -1 when token t of the item is absent.
+template <typename RowOf>
+__device__ __forceinline__ void issue_raw8(uint8_t* slot, uint64_t* bar, const uint16_t* kbase, const uint16_t* vbase,
+                                           RowOf row_of) {
+    const int lane = threadIdx.x & 31;
+    const int t = lane & 7;
+    const int64_t tok = row_of(t);
+    const unsigned present = __ballot_sync(0xffffffffu, tok >= 0) & 0xffu;
+    const int n_present = __popc(present);
+    // zero rows of absent tokens (V must be finite: masked p = 0 multiplies it)
+    for (int i = lane; i < 8 * 16 * 2; i += 32) {
+        const int rowi = (i >> 4) & 7, part = i >> 7, col = i & 15;
+        if (!((present >> rowi) & 1u))
+            *reinterpret_cast<uint4*>(slot + part * kRawV + rowi * kRawStride * 2 + col * 16) = make_uint4(0, 0, 0, 0);
+    }
+    if (lane == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive_expect_tx(bar, (uint32_t)n_present * 512u);
+    }
+    __syncwarp();
+    if (tok >= 0) {
+        if (lane < 8) bulk_g2s(slot + t * kRawStride * 2, kbase + tok * kHeadDim, 256, bar);
+        else if (lane < 16) bulk_g2s(slot + kRawV + t * kRawStride * 2, vbase + tok * kHeadDim, 256, bar);
+    }
+}
+
+// Merge the warps' states into a CTA partial (m, l, o unnormalised) in smem.
+// `scratch` >= kAttnWarps * (8 * 128 + 16) floats.  Caller syncs before.
+__device__ void cta_merge(const WarpAttn& st, int G, float* scratch, float* cm, float* cl, float* co) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, tig = lane & 3;
+    float l = st.l;
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    float* wm = scratch + warp * (8 * kHeadDim + 16);
+    float* wl = wm + 8;
+    float* wo = wm + 16;
+    if (tig == 0 && g < 8) {
+        wm[g] = st.m;
+        wl[g] = l;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int d = 16 * j + g;
+        const int h0 = 2 * tig, h1 = 2 * tig + 1;
+        if (h0 < G) {
+            wo[h0 * kHeadDim + d] = st.o[j][0];
+            wo[h0 * kHeadDim + d + 8] = st.o[j][2];
+        }
+        if (h1 < G) {
+            wo[h1 * kHeadDim + d] = st.o[j][1];
+            wo[h1 * kHeadDim + d + 8] = st.o[j][3];
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * kHeadDim; i += kAttnThreads) {
+        const int h = i / kHeadDim, d = i % kHeadDim;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, scratch[w * (8 * kHeadDim + 16) + h]);
+        float Ls = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float* b = scratch + w * (8 * kHeadDim + 16);
+            const float wt = (b[h] == -INFINITY) ? 0.f : ex2(b[h] - M);
+            Ls += wt * b[8 + h];
+            O += wt * b[16 + h * kHeadDim + d];
+        }
+        co[h * kHeadDim + d] = O;
+        if (d == 0) {
+            cm[h] = M;
+            cl[h] = Ls;
+        }
+    }
+}
+
+// Rank 0 of the cluster combines the CS CTA partials and writes out / lse.
+__device__ void cluster_finalize(cg::cluster_group& cluster, int CS, int G, float* cm, float* cl, float* co,
+                                 uint16_t* out_row, float* lse_row) {
+    if (cluster.block_rank() != 0) return;
+    for (int i = threadIdx.x; i < G * kHeadDim; i += kAttnThreads) {
+        const int h = i / kHeadDim, d = i % kHeadDim;
+        float M = -INFINITY;
+        for (int r = 0; r < CS; ++r) M = fmaxf(M, *cluster.map_shared_rank(cm + h, r));
+        float Ls = 0.f, O = 0.f;
+        for (int r = 0; r < CS; ++r) {
+            const float mr = *cluster.map_shared_rank(cm + h, r);
+            const float wt = (mr == -INFINITY) ? 0.f : ex2(mr - M);
+            Ls += wt * *cluster.map_shared_rank(cl + h, r);
+            O += wt * *cluster.map_shared_rank(co + h * kHeadDim + d, r);
+        }
+        const float v = Ls > 0.f ? O / Ls : 0.f;
+        out_row[h * kHeadDim + d] = f2bfbits(v);
+        if (d == 0 && lse_row) lse_row[h] = (Ls > 0.f) ? (M + __log2f(Ls)) * 0.69314718055994531f : -INFINITY;
+    }
+}
+
+// ---------------------------------------------------------------- page decode
+struct PageArgs {
+    const uint16_t* q;
+    zkv_page_layer L;
+    int G, n_max, n_c, nk, n_near, n_c_pad, per, pp, pn;
+    float sl2;
+    uint16_t* out;
+    float* lse;
+    int64_t* sel_out;
+    int32_t* status;
+};
+
+__global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const PageArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int CS = (int)cluster.num_blocks();
+    const int rank = (int)cluster.block_rank();
+    const int64_t row = blockIdx.x / CS;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+    uint8_t* region = smem;
+    float* sc_all = reinterpret_cast<float*>(smem + kRegionBytes);
+    int* sel_s = reinterpret_cast<int*>(sc_all + a.n_c_pad);
+    uint16_t* q_s = reinterpret_cast<uint16_t*>(sel_s + ((a.nk + 3) & ~3));
+    uint16_t* rq_s = q_s + 8 * kHeadDim;
+    float* cm = reinterpret_cast<float*>(rq_s + kHeadDim);
+    float* cl = cm + 8;
+    float* co = cl + 8;
+    int* hist = reinterpret_cast<int*>(co + 8 * kHeadDim);
+    int* misc = hist + 256;
+    int* scan = misc + 4;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(scan + 2 * kAttnThreads);  // [kStages] + [warps][2]
+    __shared__ int s_failed;
+
+    if (threadIdx.x == 0) {
+        s_failed = 0;
+        for (int i = 0; i < kStages + 2 * kAttnWarps; ++i) mbar_init(bars + i, 1);
+        mbar_fence_init();
+    }
+    // query + GQA-mean query (compute() :1622-1626: bf16 mean over the group)
+    for (int i = threadIdx.x; i < a.G * kHeadDim; i += kAttnThreads) q_s[i] = a.q[row * a.G * kHeadDim + i];
+    __syncthreads();
+    for (int d = threadIdx.x; d < kHeadDim; d += kAttnThreads) {
+        float acc = 0.f;
+        for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, bfbits2f(q_s[g * kHeadDim + d]));
+        rq_s[d] = f2bfbits(__fdiv_rn(acc, (float)a.G));
+    }
+    __syncthreads();
+
+    // ------------------------------------------------ phase 1: Quest scores
+    const int c0 = rank * a.per;
+    const int c1 = min(a.n_c, c0 + a.per);
+    const int n_my = max(0, c1 - c0);
+    const int n_blk = (n_my + kStageChunks - 1) / kStageChunks;
+    const uint16_t* gmin = reinterpret_cast<const uint16_t*>(a.L.chunk_min) + (row * a.n_max) * kHeadDim;
+    const uint16_t* gmax = reinterpret_cast<const uint16_t*>(a.L.chunk_max) + (row * a.n_max) * kHeadDim;
+    constexpr int kStageHalf = kStageChunks * kHeadDim * 2;  // bytes of min rows per stage
+    auto issue_stage = [&](int b) {
+        const int s = b % kStages;
+        const int cc = c0 + b * kStageChunks;
+        const int nch = min(kStageChunks, c1 - cc);
+        uint8_t* dst = region + s * (2 * kStageHalf);
+        mbar_arrive_expect_tx(bars + s, (uint32_t)nch * kHeadDim * 2 * 2);
+        bulk_g2s(dst, gmin + (int64_t)cc * kHeadDim, nch * kHeadDim * 2, bars + s);
+        bulk_g2s(dst + kStageHalf, gmax + (int64_t)cc * kHeadDim, nch * kHeadDim * 2, bars + s);
+    };
+    if (threadIdx.x == 0)
+        for (int b = 0; b < min(kStages, n_blk); ++b) issue_stage(b);
+    {
+        const int hl = lane & 15, half = lane >> 4;
+        const uint4 qv = *reinterpret_cast<const uint4*>(rq_s + 8 * hl);
+        bool ok = true;
+        for (int b = 0; b < n_blk; ++b) {
+            const int s = b % kStages;
+            if (!mbar_wait(bars + s, (uint32_t)((b / kStages) & 1), a.status)) ok = false;
+            const uint8_t* src = region + s * (2 * kStageHalf);
+            const int cc = c0 + b * kStageChunks;
+            const int nch = min(kStageChunks, c1 - cc);
+#pragma unroll
+            for (int u = 0; u < kStageChunks / (2 * kAttnWarps); ++u) {
+                const int lc = (warp * (kStageChunks / kAttnWarps)) + 2 * u + half;
+                uint4 mn = make_uint4(0, 0, 0, 0), mx = mn;
+                if (lc < nch) {
+                    mn = *reinterpret_cast<const uint4*>(src + lc * kHeadDim * 2 + 16 * hl);
+                    mx = *reinterpret_cast<const uint4*>(src + kStageHalf + lc * kHeadDim * 2 + 16 * hl);
+                }
+                const float sc = quest_half(qv, mn, mx);
+                if (hl == 0 && lc < nch) {
+                    const int c = cc + lc;
+                    const bool v = !a.L.valid || a.L.valid[row * a.n_max + c];
+                    sc_all[c] = (ok && v) ? sc : -INFINITY;
+                }
+            }
+            __syncthreads();
+            if (threadIdx.x == 0 && b + kStages < n_blk) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue_stage(b + kStages);
+            }
+        }
+        if (!ok) atomicOr(&s_failed, 1);
+    }
+
+    // ------------------------------------------------ phase 2: exchange + select
+    cluster.sync();
+    for (int p = 0; p < CS; ++p) {
+        if (p == rank) continue;
+        const int lo = p * a.per, hi = min(a.n_c, lo + a.per);
+        const float* rsc = cluster.map_shared_rank(sc_all, p);
+        for (int i = lo + 4 * threadIdx.x; i < hi; i += 4 * kAttnThreads) {
+            if (i + 4 <= hi) {
+                *reinterpret_cast<float4*>(sc_all + i) = *reinterpret_cast<const float4*>(rsc + i);
+            } else {
+                for (int e = i; e < hi; ++e) sc_all[e] = rsc[e];
+            }
+        }
+    }
+    __syncthreads();
+    {
+        auto key = [&](int i) { return ordered_u32(sc_all[i]); };
+        if (a.n_c <= a.nk) {
+            for (int i = threadIdx.x; i < a.nk; i += kAttnThreads) sel_s[i] = i < a.n_c ? i : 0;
+            __syncthreads();
+        } else {
+            uint32_t thr;
+            int take_eq;
+            block_radix_select<kAttnThreads>(key, a.n_c, a.nk, hist, misc, &thr, &take_eq);
+            block_select_compact<kAttnThreads>(key, a.n_c, thr, take_eq, scan, [&](int pos, int i) { sel_s[pos] = i; });
+        }
+    }
+    if (a.sel_out && rank == 0)
+        for (int i = threadIdx.x; i < a.nk; i += kAttnThreads) a.sel_out[row * a.nk + i] = sel_s[i];
+
+    // ------------------------------------------------ phase 3: attention
+    WarpAttn st;
+    warp_attn_init(st, q_s, a.G);
+    const int p_lo = rank * a.pp, p_hi = min(a.nk, p_lo + a.pp);
+    const int n_lo = rank * a.pn, n_hi = min(a.n_near, n_lo + a.pn);
+    const int n_pages = max(0, p_hi - p_lo);
+    const int n_raw = max(0, (n_hi - n_lo + 7) / 8);
+    const int n_items = n_pages + n_raw;
+    const uint16_t* nk_base = reinterpret_cast<const uint16_t*>(a.L.near_k) + row * a.L.near_ld * kHeadDim;
+    const uint16_t* nv_base = reinterpret_cast<const uint16_t*>(a.L.near_v) + row * a.L.near_ld * kHeadDim;
+    uint8_t* wslot[2] = {region + (2 * warp) * kSlotBytes, region + (2 * warp + 1) * kSlotBytes};
+    uint64_t* wbar = bars + kStages + 2 * warp;
+    __syncthreads();  // the ring region is reused as warp slots
+    auto issue_item = [&](int it, int k) {
+        if (it < n_pages) {
+            issue_kivi_page(wslot[k], wbar + k, a.L, row, a.n_max, sel_s[p_lo + it]);
+        } else {
+            const int base = n_lo + 8 * (it - n_pages);
+            issue_raw8(wslot[k], wbar + k, nk_base, nv_base,
+                       [&](int t) -> int64_t { return (base + t < n_hi) ? (int64_t)(base + t) : -1; });
+        }
+    };
+    {
+        int mine = 0;
+        for (int it = warp; it < n_items; it += kAttnWarps) ++mine;
+        if (mine > 0) issue_item(warp, 0);
+        if (mine > 1) issue_item(warp + kAttnWarps, 1);
+        bool ok = true;
+        for (int i = 0; i < mine; ++i) {
+            const int it = warp + i * kAttnWarps;
+            const int k = i & 1;
+            if (!mbar_wait(wbar + k, (uint32_t)((i >> 1) & 1), a.status)) ok = false;
+            if (ok) {
+                if (it < n_pages) {
+                    warp_page_kivi(st, wslot[k], a.G, a.sl2);
+                } else {
+                    const int base = n_lo + 8 * (it - n_pages);
+                    warp_page_raw8(st, wslot[k], (1u << min(8, n_hi - base)) - 1u, a.G, a.sl2);
+                }
+            }
+            __syncwarp();
+            if (i + 2 < mine) issue_item(it + 2 * kAttnWarps, k);
+        }
+        if (!ok && lane == 0) atomicOr(&s_failed, 1);
+    }
+
+    // ------------------------------------------------ phase 4: merge
+    __syncthreads();
+    cta_merge(st, a.G, reinterpret_cast<float*>(region), cm, cl, co);
+    cluster.sync();
+    cluster_finalize(cluster, CS, a.G, cm, cl, co, a.out + row * a.G * kHeadDim, a.lse ? a.lse + row * a.G : nullptr);
+    cluster.sync();
+    if (threadIdx.x == 0 && s_failed) set_status(a.status, ZKV_ERR_TIMEOUT);
+}
+
+// ---------------------------------------------------------------- raw rows
+struct RowsArgs {
+    const uint16_t* q;
+    const uint16_t* keys;
+    const uint16_t* values;
+    int64_t kv_ld_row, kv_cap;
+    int G;
+    int s0_lo, s0_n, n_sel, s1_lo, s1_n;
+    const int64_t* sel;
+    int64_t sel_ld, sel_off;
+    int ipc;  // 8-token items per CTA
+    float sl2;
+    uint16_t* out;
+    float* lse;
+    int32_t* status;
+};
+
+__global__ void __launch_bounds__(kAttnThreads, 4) attn_rows_kernel(const RowsArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int CS = (int)cluster.num_blocks();
+    const int rank = (int)cluster.block_rank();
+    const int64_t row = blockIdx.x / CS;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* region = smem;
+    uint16_t* q_s = reinterpret_cast<uint16_t*>(smem + kRegionBytes);
+    float* cm = reinterpret_cast<float*>(q_s + 8 * kHeadDim);
+    float* cl = cm + 8;
+    float* co = cl + 8;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(co + 8 * kHeadDim);
+    __shared__ int s_failed;
+    if (threadIdx.x == 0) {
+        s_failed = 0;
+        for (int i = 0; i < 2 * kAttnWarps; ++i) mbar_init(bars + i, 1);
+        mbar_fence_init();
+    }
+    for (int i = threadIdx.x; i < a.G * kHeadDim; i += kAttnThreads) q_s[i] = a.q[row * a.G * kHeadDim + i];
+    __syncthreads();
+    const int total = a.s0_n + a.n_sel + a.s1_n;
+    const int n_items_all = (total + 7) / 8;
+    const int it_lo = rank * a.ipc, it_hi = min(n_items_all, it_lo + a.ipc);
+    const uint16_t* kb = a.keys + row * a.kv_ld_row;
+    const uint16_t* vb = a.values + row * a.kv_ld_row;
+    const int64_t* selr = a.sel ? a.sel + row * a.sel_ld : nullptr;
+    auto token_row = [&](int i) -> int64_t {
+        if (i >= total) return -1;
+        int64_t t;
+        if (i < a.s0_n) t = a.s0_lo + i;
+        else if (i < a.s0_n + a.n_sel) t = selr[i - a.s0_n] + a.sel_off;
+        else t = a.s1_lo + (i - a.s0_n - a.n_sel);
+        return (t >= 0 && t < a.kv_cap) ? t : -1;
+    };
+    WarpAttn st;
+    warp_attn_init(st, q_s, a.G);
+    uint8_t* wslot[2] = {region + (2 * warp) * kSlotBytes, region + (2 * warp + 1) * kSlotBytes};
+    uint64_t* wbar = bars + 2 * warp;
+    int mine = 0;
+    for (int it = it_lo + warp; it < it_hi; it += kAttnWarps) ++mine;
+    auto issue_item = [&](int it, int k) {
+        issue_raw8(wslot[k], wbar + k, kb, vb, [&](int t) { return token_row(8 * it + t); });
+    };
+    if (mine > 0) issue_item(it_lo + warp, 0);
+    if (mine > 1) issue_item(it_lo + warp + kAttnWarps, 1);
+    bool ok = true;
+    for (int i = 0; i < mine; ++i) {
+        const int it = it_lo + warp + i * kAttnWarps;
+        const int k = i & 1;
+        if (!mbar_wait(wbar + k, (uint32_t)((i >> 1) & 1), a.status)) ok = false;
+        const int64_t tr = token_row(8 * it + (lane & 7));
+        const unsigned pres = __ballot_sync(0xffffffffu, tr >= 0) & 0xffu;
+        if (ok) warp_page_raw8(st, wslot[k], pres, a.G, a.sl2);
+        __syncwarp();
+        if (i + 2 < mine) issue_item(it + 2 * kAttnWarps, k);
+    }
+    if (!ok && lane == 0) atomicOr(&s_failed, 1);
+    __syncthreads();
+    cta_merge(st, a.G, reinterpret_cast<float*>(region), cm, cl, co);
+    cluster.sync();
+    cluster_finalize(cluster, CS, a.G, cm, cl, co, a.out + row * a.G * kHeadDim, a.lse ? a.lse + row * a.G : nullptr);
+    cluster.sync();
+    if (threadIdx.x == 0 && s_failed) set_status(a.status, ZKV_ERR_TIMEOUT);
+}
+
+// ---------------------------------------------------------------- LSE merge
+__global__ void lse_merge_kernel(const uint16_t* __restrict__ a, const float* __restrict__ la,
+                                 const uint16_t* __restrict__ b, const float* __restrict__ lb,
+                                 uint16_t* __restrict__ out, float* __restrict__ lse_out, int rows, int dim) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= (int64_t)rows * dim) return;
+    const int r = (int)(i / dim);
+    const float m = fmaxf(la[r], lb[r]);
+    const float wa = expf(la[r] - m), wb = expf(lb[r] - m);
+    const float den = wa + wb;
+    out[i] = f2bfbits((wa * bfbits2f(a[i]) + wb * bfbits2f(b[i])) / den);
+    if (lse_out && (i % dim) == 0) lse_out[r] = m + logf(den);
+}
+
+__global__ void lse_merge_n_kernel(const float* __restrict__ parts, const float* __restrict__ lses, int n, int rows,
+                                   int dim, uint16_t* __restrict__ out, float* __restrict__ lse_out) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= (int64_t)rows * dim) return;
+    const int r = (int)(i / dim);
+    float m = -INFINITY;
+    for (int p = 0; p < n; ++p) m = fmaxf(m, lses[(int64_t)p * rows + r]);
+    float den = 0.f, acc = 0.f;
+    for (int p = 0; p < n; ++p) {
+        const float lp = lses[(int64_t)p * rows + r];
+        const float w = (lp == -INFINITY) ? 0.f : expf(lp - m);
+        den += w;
+        acc += w * parts[(int64_t)p * rows * dim + i];
+    }
+    out[i] = f2bfbits(den > 0.f ? acc / den : 0.f);
+    if (lse_out && (i % dim) == 0) lse_out[r] = den > 0.f ? m + logf(den) : -INFINITY;
+}
+
+}  // namespace zkv
+
+using namespace zkv;
+
+static int pick_cluster(int requested, int rows) {
+    if (requested == 1 || requested == 2 || requested == 4 || requested == 8) return requested;
+    (void)rows;
+    return 8;
+}
+
+static int launch_clustered(const void* fn, int rows, int CS, size_t smem, cudaStream_t stream, void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(rows * CS), 1, 1);
+    cfg.blockDim = dim3(kAttnThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)CS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // raise the dynamic shared-memory limit once per (kernel, device, size)
+    static thread_local const void* last_fn[4] = {nullptr, nullptr, nullptr, nullptr};
+    static thread_local size_t last_smem[4] = {0, 0, 0, 0};
+    static thread_local int last_dev[4] = {-1, -1, -1, -1};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int slot = -1;
+    for (int i = 0; i < 4; ++i)
+        if (last_fn[i] == fn && last_dev[i] == dev) slot = i;
+    if (slot < 0 || last_smem[slot] < smem) {
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return ZKV_ERR_LAUNCH;
+        if (slot < 0) {
+            for (int i = 0; i < 4; ++i)
+                if (!last_fn[i]) {
+                    slot = i;
+                    break;
+                }
+            if (slot < 0) slot = 0;
+        }
+        last_fn[slot] = fn;
+        last_dev[slot] = dev;
+        last_smem[slot] = smem;
+    }
+    if (cudaLaunchKernelExC(&cfg, fn, args) != cudaSuccess) return ZKV_ERR_LAUNCH;
+    return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH;
+}
+
+extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max, int n_c,
+                               int nk, int n_near, float scale, void* out, float* lse, int64_t* sel_out,
+                               int32_t* status, int cluster, void* stream) {
+    if (!q || !layer || !out || rows < 0 || G < 1 || G > 8 || n_c < 0 || n_c > n_max || nk < 1 || n_near < 0)
+        return ZKV_ERR_ARG;
+    if (nk > n_c && n_c > 0) return ZKV_ERR_ARG;
+    if (n_near > layer->near_ld) return ZKV_ERR_ARG;
+    if (n_c > 16384 || nk > 2048) return ZKV_ERR_CAPACITY;
+    if (rows == 0) return ZKV_OK;
+    const zkv_page_layer& L = *layer;
+    if (!L.chunk_min || !L.chunk_max || !L.kcodes || !L.vcodes_t || !L.vmeta || (n_near > 0 && (!L.near_k || !L.near_v)))
+        return ZKV_ERR_ARG;
+    if (((uintptr_t)L.chunk_min & 15) || ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)L.kcodes & 15) ||
+        ((uintptr_t)L.vcodes_t & 15) || ((uintptr_t)L.vmeta & 15) || ((uintptr_t)L.near_k & 15) ||
+        ((uintptr_t)L.near_v & 15) || ((uintptr_t)q & 3))
+        return ZKV_ERR_ALIGN;
+    const int CS = pick_cluster(cluster, rows);
+    PageArgs a;
+    a.q = (const uint16_t*)q;
+    a.L = L;
+    a.G = G;
+    a.n_max = n_max;
+    a.n_c = n_c;
+    a.nk = n_c > 0 ? nk : 0;
+    a.n_near = n_near;
+    a.n_c_pad = (n_c + 3) & ~3;
+    a.per = ((n_c + CS - 1) / CS + 3) & ~3;
+    a.pp = (a.nk + CS - 1) / CS;
+    a.pn = ((n_near + CS - 1) / CS + 7) & ~7;
+    a.sl2 = scale * 1.4426950408889634f;
+    a.out = (uint16_t*)out;
+    a.lse = lse;
+    a.sel_out = sel_out;
+    a.status = status;
+    const size_t smem = kRegionBytes + (size_t)a.n_c_pad * 4 + (size_t)((a.nk + 3) & ~3) * 4 + 9 * kHeadDim * 2 +
+                        (16 + 8 * kHeadDim) * 4 + (256 + 4 + 2 * kAttnThreads) * 4 +
+                        (kStages + 2 * kAttnWarps) * 8 + 16;
+    void* args[] = {&a};
+    return launch_clustered((const void*)page_decode_kernel, rows, CS, smem, (cudaStream_t)stream, args);
+}
+
+extern "C" int zkv_attn_rows(const void* q, const void* keys, const void* values, int64_t kv_ld_row, int rows, int G,
+                             int seg0_lo, int seg0_hi, const int64_t* sel, int n_sel, int64_t sel_ld,
+                             int64_t sel_offset, int seg1_lo, int seg1_hi, float scale, void* out, float* lse,
+                             int split, int32_t* status, void* stream) {
+    if (!q || !keys || !values || !out || rows < 0 || G < 1 || G > 8 || kv_ld_row < kHeadDim) return ZKV_ERR_ARG;
+    if (seg0_hi < seg0_lo || seg1_hi < seg1_lo || n_sel < 0 || (n_sel > 0 && (!sel || sel_ld < n_sel)))
+        return ZKV_ERR_ARG;
+    if (rows == 0) return ZKV_OK;
+    if (((uintptr_t)keys & 15) || ((uintptr_t)values & 15) || (kv_ld_row % 8) || ((uintptr_t)q & 3))
+        return ZKV_ERR_ALIGN;
+    const int CS = pick_cluster(split, rows);
+    RowsArgs a;
+    a.q = (const uint16_t*)q;
+    a.keys = (const uint16_t*)keys;
+    a.values = (const uint16_t*)values;
+    a.kv_ld_row = kv_ld_row;
+    a.kv_cap = kv_ld_row / kHeadDim;
+    a.G = G;
+    a.s0_lo = seg0_lo;
+    a.s0_n = seg0_hi - seg0_lo;
+    a.n_sel = n_sel;
+    a.s1_lo = seg1_lo;
+    a.s1_n = seg1_hi - seg1_lo;
+    a.sel = sel;
+    a.sel_ld = sel_ld;
+    a.sel_off = sel_offset;
+    const int total = a.s0_n + a.n_sel + a.s1_n;
+    a.ipc = ((total + 7) / 8 + CS - 1) / CS;
+    a.sl2 = scale * 1.4426950408889634f;
+    a.out = (uint16_t*)out;
+    a.lse = lse;
+    a.status = status;
+    const size_t smem = kRegionBytes + 8 * kHeadDim * 2 + (16 + 8 * kHeadDim) * 4 + 2 * kAttnWarps * 8 + 16;
+    void* args[] = {&a};
+    return launch_clustered((const void*)attn_rows_kernel, rows, CS, smem, (cudaStream_t)stream, args);
+}
+
+extern "C" int zkv_lse_merge(const void* a, const float* la, const void* b, const float* lb, void* out,
+                             float* lse_out, int rows, int dim, void* stream) {
+    if (rows < 0 || dim <= 0) return ZKV_ERR_ARG;
+    if (rows == 0) return ZKV_OK;
+    const int64_t n = (int64_t)rows * dim;
+    lse_merge_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        (const uint16_t*)a, la, (const uint16_t*)b, lb, (uint16_t*)out, lse_out, rows, dim);
+    return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH;
+}
+
+extern "C" int zkv_lse_merge_n(const float* parts, const float* lses, int n, int rows, int dim, void* out,
+                               float* lse_out, void* stream) {
+    if (rows < 0 || dim <= 0 || n < 1) return ZKV_ERR_ARG;
+    if (rows == 0) return ZKV_OK;
+    const int64_t tot = (int64_t)rows * dim;
+    lse_merge_n_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, (cudaStream_t)stream>>>(parts, lses, n, rows, dim,
+                                                                                       (uint16_t*)out, lse_out);
+    return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH;
+}

@@ -1,0 +1,295 @@
+// zkv_common.cuh -- shared device helpers for the libzkv sm_100a kernels:
+// bf16 arithmetic ladders, TMA bulk copies with mbarrier completion and
+// bounded waits, thread-block-cluster helpers, mma.sync fragments and a
+// deterministic block-wide radix select.
+#pragma once
+
+#include <cooperative_groups.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/zkv.h"
+
+namespace cg = cooperative_groups;
+
+namespace zkv {
+
+constexpr int kHeadDim = 128;
+constexpr int kChunk = 16;           // Quest chunk == KIVI key group == page
+constexpr int kWords = kHeadDim / 8; // int32 words of 4-bit codes per token
+constexpr int kVGroups = kHeadDim / 32;
+// Bounded spin: test_wait polls with a short sleep; ~2^20 polls is well
+// under a second, after which the kernel records ZKV_ERR_TIMEOUT.
+constexpr uint32_t kMaxPolls = 1u << 20;
+
+// ------------------------------------------------------------ bf16 ladder
+__device__ __forceinline__ float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float bfbits2f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
+__device__ __forceinline__ uint16_t f2bfbits(float f) {
+    __nv_bfloat16 h = __float2bfloat16_rn(f);
+    return *reinterpret_cast<uint16_t*>(&h);
+}
+
+// KIVI scale bf16(bf16(mx - mn) / 15): fp32 ops on bf16 operands rounded once
+// to bf16 equal the correctly rounded bf16 ops (24 >= 2*8 + 2).
+__device__ __forceinline__ uint16_t kivi_scale_bits(uint16_t mn, uint16_t mx) {
+    uint16_t diff = f2bfbits(__fsub_rn(bfbits2f(mx), bfbits2f(mn)));
+    return f2bfbits(__fdiv_rn(bfbits2f(diff), 15.0f));
+}
+
+// code = rint(clamp(bf16(bf16(x - mn) / max(scale, 1e-8)), 0, 15))
+__device__ __forceinline__ uint32_t kivi_code(uint16_t x, uint16_t mn, uint16_t scale) {
+    float sc = bfbits2f(scale);
+    float safe = bfbits2f(f2bfbits(sc > 1e-8f ? sc : 1e-8f));
+    float d1 = bfbits2f(f2bfbits(__fsub_rn(bfbits2f(x), bfbits2f(mn))));
+    float y = bfbits2f(f2bfbits(__fdiv_rn(d1, safe)));
+    y = fminf(fmaxf(y, 0.0f), 15.0f);
+    return (uint32_t)__float2int_rn(y);
+}
+
+// Two 4-bit codes -> exact bf16x2 (c_lo, c_hi): OR into the mantissa of
+// bf16(128) then subtract 128 (exact).
+__device__ __forceinline__ __nv_bfloat162 codes2_to_bf162(uint32_t lo, uint32_t hi) {
+    uint32_t v = (lo & 0xFu) | ((hi & 0xFu) << 16) | 0x43004300u;
+    __nv_bfloat162 r = *reinterpret_cast<__nv_bfloat162*>(&v);
+    const uint32_t k128 = 0x43004300u;
+    return __hsub2(r, *reinterpret_cast<const __nv_bfloat162*>(&k128));
+}
+
+// bf16(bf16(c * s) + z) on a pair (two bf16 ops, no FMA) -- the reference
+// dequant ladder (kivi_qk_dot.cu:264-275).
+__device__ __forceinline__ __nv_bfloat162 dequant2(__nv_bfloat162 c, __nv_bfloat162 s, __nv_bfloat162 z) {
+    return __hadd2(__hmul2(c, s), z);
+}
+
+__device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+__device__ __forceinline__ __nv_bfloat162 bits_bf162(uint32_t v) { return *reinterpret_cast<__nv_bfloat162*>(&v); }
+
+__device__ __forceinline__ uint32_t ordered_u32(float x) {
+    uint32_t b = __float_as_uint(x);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// ------------------------------------------------------------ status
+__device__ __forceinline__ void set_status(int32_t* status, int code) {
+    if (status) atomicExch(status, code);
+}
+
+// ------------------------------------------------------------ mbarrier / TMA bulk
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for phase `parity` of `bar`; false (and status set) on expiry.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status) {
+    if (mbar_test(bar, parity)) return true;
+    for (uint32_t it = 0; it < kMaxPolls; ++it) {
+        __nanosleep(64);
+        if (mbar_test(bar, parity)) return true;
+    }
+    set_status(status, ZKV_ERR_TIMEOUT);
+    return false;
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (bytes % 16 == 0,
+// both addresses 16-byte aligned).  Never a multicast form.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ------------------------------------------------------------ mma.sync bf16
+// D(16x8 f32) += A(16x16 bf16, row) * B(16x8 bf16, col)
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return bf162_bits(v);
+}
+
+// ------------------------------------------------------------ block radix select
+// Deterministic top-k over n uint32 keys (larger key = better): after the
+// call, *thr_out is the k-th largest key and *take_eq_out how many elements
+// equal to it are taken (lowest indices first).  KeyFn(i) returns key i.
+// All NT threads call it; scratch hist[256] + misc[4] in shared memory.
+template <int NT, typename KeyFn>
+__device__ void block_radix_select(KeyFn key, int n, int k, int* hist, int* misc, uint32_t* thr_out,
+                                   int* take_eq_out) {
+    uint32_t prefix = 0, mask = 0;
+    int remaining = k;
+#pragma unroll 1
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += NT) hist[i] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += NT) {
+            uint32_t kk = key(i);
+            if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & 255u], 1);
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            // lane l owns bins [8l, 8l+8); suffix sums from the top bin down.
+            const int lane = threadIdx.x;
+            int local[8];
+            int tot = 0;
+#pragma unroll
+            for (int j = 7; j >= 0; --j) {
+                tot += hist[8 * lane + j];
+                local[j] = tot;  // count of bins >= 8*lane+j within this lane
+            }
+            // exclusive suffix over higher lanes
+            int incl = tot;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                int v = __shfl_down_sync(0xffffffffu, incl, off);
+                if (lane + off < 32) incl += v;
+            }
+            int above = incl - tot;  // count in bins of higher lanes
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                int ge = above + local[j];
+                int gt = ge - hist[8 * lane + j];
+                if (gt < remaining && ge >= remaining) {
+                    misc[0] = 8 * lane + j;
+                    misc[1] = gt;
+                }
+            }
+        }
+        __syncthreads();
+        const uint32_t digit = (uint32_t)misc[0];
+        remaining -= misc[1];
+        prefix |= digit << shift;
+        mask |= 255u << shift;
+        __syncthreads();
+    }
+    *thr_out = prefix;
+    *take_eq_out = remaining;
+}
+
+// Writes the selected indices (key > thr, plus the first take_eq with
+// key == thr) in ascending index order: out(pos, index).  Contiguous
+// per-thread ranges + block exclusive scan.  scan scratch: 2*NT ints.
+template <int NT, typename KeyFn, typename OutFn>
+__device__ void block_select_compact(KeyFn key, int n, uint32_t thr, int take_eq, int* scan, OutFn out) {
+    const int per = (n + NT - 1) / NT;
+    const int lo = threadIdx.x * per;
+    const int hi = min(n, lo + per);
+    int gt = 0, eq = 0;
+    for (int i = lo; i < hi; ++i) {
+        uint32_t kk = key(i);
+        gt += kk > thr;
+        eq += kk == thr;
+    }
+    // block exclusive scan of (gt, eq)
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int sg = gt, se = eq;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        int a = __shfl_up_sync(0xffffffffu, sg, off);
+        int b = __shfl_up_sync(0xffffffffu, se, off);
+        if (lane >= off) {
+            sg += a;
+            se += b;
+        }
+    }
+    if (lane == 31) {
+        scan[warp] = sg;
+        scan[NT + warp] = se;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ag = 0, ae = 0;
+        for (int w = 0; w < NT / 32; ++w) {
+            int tg = scan[w], te = scan[NT + w];
+            scan[w] = ag;
+            scan[NT + w] = ae;
+            ag += tg;
+            ae += te;
+        }
+    }
+    __syncthreads();
+    int gbefore = scan[warp] + sg - gt;
+    int ebefore = scan[NT + warp] + se - eq;
+    for (int i = lo; i < hi; ++i) {
+        uint32_t kk = key(i);
+        if (kk > thr) {
+            out(gbefore + min(ebefore, take_eq), i);
+            ++gbefore;
+        } else if (kk == thr) {
+            if (ebefore < take_eq) out(gbefore + ebefore, i);
+            ++ebefore;
+        }
+    }
+    __syncthreads();
+}
+
+// ----------------------------------------------------------- Quest score
+// Half-warp per chunk: lane hl (0..15) loads dims [8hl, 8hl+8) of q, min and
+// max as one 16-byte vector each.  The reference kernel's operation order
+// (thread t: ((f0+f1)+f2)+f3 over dims 4t..4t+3, then an xor tree with
+// offsets 16,8,4,2,1) maps onto two partials per lane and xor offsets
+// 8,4,2,1 plus a final in-lane add, so the fp32 result is bit-identical.
+__device__ __forceinline__ float quest_half(uint4 qv, uint4 mnv, uint4 mxv) {
+    const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+    const uint32_t nw[4] = {mnv.x, mnv.y, mnv.z, mnv.w};
+    const uint32_t xw[4] = {mxv.x, mxv.y, mxv.z, mxv.w};
+    float c[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int wi = 2 * h + (j >> 1);
+            const int sh = (j & 1) * 16;
+            const float q = __uint_as_float(((qw[wi] >> sh) & 0xffffu) << 16);
+            const float a = __fmul_rn(q, __uint_as_float(((nw[wi] >> sh) & 0xffffu) << 16));
+            const float b = __fmul_rn(q, __uint_as_float(((xw[wi] >> sh) & 0xffffu) << 16));
+            const float f = fmaxf(a, b);
+            acc = (j == 0) ? f : __fadd_rn(acc, f);
+        }
+        c[h] = acc;
+    }
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1) {
+        c[0] = __fadd_rn(c[0], __shfl_xor_sync(0xffffffffu, c[0], off));
+        c[1] = __fadd_rn(c[1], __shfl_xor_sync(0xffffffffu, c[1], off));
+    }
+    return __fadd_rn(c[0], c[1]);
+}
+
+}  // namespace zkv
