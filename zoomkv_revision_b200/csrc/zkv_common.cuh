@@ -57,10 +57,13 @@ __device__ __forceinline__ __nv_bfloat162 codes2_to_bf162(uint32_t lo, uint32_t 
     return __hsub2(r, *reinterpret_cast<const __nv_bfloat162*>(&k128));
 }
 
-// bf16(bf16(c * s) + z) on a pair (two bf16 ops, no FMA) -- the reference
-// dequant ladder (kivi_qk_dot.cu:264-275).
+// bf16(bf16(c * s) + z) on a pair: two separately rounded bf16 ops -- the
+// dequant of the reference's PyTorch path (qk_dot.py:304) and the documented
+// intent of kivi_qk_dot.cu:264-275.  The `_rn` forms stop ptxas from
+// contracting the pair into one fma.bf16x2 (plain __hmul2/__hadd2 lower to
+// mul/add.bf16x2 without a rounding qualifier, which ptxas may fuse).
 __device__ __forceinline__ __nv_bfloat162 dequant2(__nv_bfloat162 c, __nv_bfloat162 s, __nv_bfloat162 z) {
-    return __hadd2(__hmul2(c, s), z);
+    return __hadd2_rn(__hmul2_rn(c, s), z);
 }
 
 __device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }

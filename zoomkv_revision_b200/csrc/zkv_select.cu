@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(128) kivi_qk_kernel(const int64_t* __restrict_
             for (int p = 0; p < 4; ++p) {
                 const __nv_bfloat162 c2 = codes2_to_bf162(w >> (8 * p), w >> (8 * p + 4));
                 const __nv_bfloat162 k2 = dequant2(c2, bits_bf162(s_sc[local][4 * i + p]), bits_bf162(s_mn[local][4 * i + p]));
-                const __nv_bfloat162 pr = __hmul2(k2, bits_bf162(q2[4 * i + p]));
+                const __nv_bfloat162 pr = __hmul2_rn(k2, bits_bf162(q2[4 * i + p]));
                 acc = __fadd_rn(acc, __low2float(pr));
                 acc = __fadd_rn(acc, __high2float(pr));
             }
