@@ -194,6 +194,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--soak", type=float, default=1.5, help="seconds of load before timing (clock sampling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -255,13 +256,22 @@ def main():
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
+        # keep the GPU under the same load for ~1.5 s so the clock sampler
+        # sees the steady state the timed steps run in (extra warm-up)
+        t_soak = time.perf_counter() + args.soak
+        while time.perf_counter() < t_soak:
+            for _ in range(20):
+                graph.replay()
+            torch.cuda.synchronize()
         barrier()
+        torch.cuda.nvtx.range_push("zkv_step")
         with torch.cuda.stream(stream):
             ev0.record(stream)
             for _ in range(args.steps):
                 graph.replay()
             ev1.record(stream)
         barrier()
+        torch.cuda.nvtx.range_pop()
     ms = ev0.elapsed_time(ev1) / args.steps
     if int(status.item()) != 0:
         raise RuntimeError(f"device status {int(status.item())} (bounded wait expired)")

@@ -239,3 +239,38 @@ def test_lse_merge_golden():
     ref = O.bf16_to_f32(gl["merged"])
     assert np.abs(got - ref).max() <= 2 ** -7 * np.abs(ref).max()
     assert (to_u16(m) == gl["merged"]).mean() > 0.99
+
+
+@pytest.mark.parametrize("mode", ["ties", "invalid", "mixed_sign", "n_c_gt_2048"])
+def test_page_decode_selection_edge_cases(mode):
+    """Selection paths of the fused kernel: all-equal scores (heavy-tie
+    fallback, lowest ids win), invalid chunks (-inf), mixed-sign scores
+    (float-valued bucketing) and n_c beyond the register-resident select."""
+    bs, H, G = 1, 2, 4
+    n_ret = 16 * (2600 if mode == "n_c_gt_2048" else 400)
+    nk = 64
+    pc, _ = W.build_page_cache(11, bs, H, n_ret, 16, DEV)
+    g = torch.Generator(device=DEV).manual_seed(5)
+    q = W.synth_query(g, bs, H * G, DEV)
+    if mode == "ties":
+        q.zero_()
+    elif mode == "invalid":
+        pc.valid.copy_(torch.rand(pc.valid.shape, generator=g, device=DEV) > 0.3)
+    elif mode == "mixed_sign":
+        pc.chunk_min.copy_(torch.randn(pc.chunk_min.shape, generator=g, device=DEV).to(torch.bfloat16))
+        pc.chunk_max.copy_(pc.chunk_min)
+    sel = torch.empty(bs * H, nk, dtype=torch.int64, device=DEV)
+    out = ops.page_decode(q, pc.layer(), pc.n_c, nk, 16, sel_out=sel, cluster=8)
+    torch.cuda.synchronize()
+    R = bs * H
+    ro, _, rsel = O.page_decode(
+        to_u16(q).reshape(R, G, 128), to_u16(pc.chunk_min).reshape(R, -1, 128), to_u16(pc.chunk_max).reshape(R, -1, 128),
+        pc.valid.cpu().numpy().astype(np.uint8).reshape(R, -1), pc.kcodes.cpu().numpy().reshape(R, -1, 16, 16),
+        pc.vcodes_t.cpu().numpy().reshape(R, -1, 128, 2), to_u16(pc.vmeta).reshape(R, -1, 2, 4, 16),
+        to_u16(pc.near_k).reshape(R, -1, 128), to_u16(pc.near_v).reshape(R, -1, 128),
+        pc.n_c, nk, 16, 1 / np.sqrt(128), threads=4)
+    assert np.array_equal(sel.cpu().numpy(), rsel)
+    if mode == "ties":
+        assert (rsel == np.arange(nk)).all()
+    if mode != "mixed_sign":  # mixed-sign metadata is not a real key range; selection only
+        close(O.bf16_to_f32(to_u16(out)).reshape(R, G, 128), O.bf16_to_f32(ro))

@@ -27,9 +27,7 @@ constexpr int kSlotBytes = 4608; // per-warp staging slot (2 per warp)
 constexpr int kPageTx = 1024 + 1024 + 256 + 256 + 256;
 // RAW8 slot: K rows [8][136] bf16 @0, V rows @2176
 constexpr int kRawV = 8 * kRawStride * 2;
-constexpr int kStages = 4;       // phase-1 ring
-constexpr int kStageChunks = 16; // chunks per stage (2 per half-warp pair per warp)
-constexpr int kRegionBytes = 2 * kAttnWarps * kSlotBytes;  // 36 KB (>= ring 32 KB)
+constexpr int kRegionBytes = 2 * kAttnWarps * kSlotBytes;  // 36 KB: phase-1 rings / page slots / merge
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -117,11 +115,13 @@ __device__ __forceinline__ void warp_page_kivi(WarpAttn& st, uint8_t* slot, int 
     const int32_t* kc = reinterpret_cast<const int32_t*>(slot);
     const uint32_t* mn2 = reinterpret_cast<const uint32_t*>(slot + 2304);
     const uint32_t* sc2 = reinterpret_cast<const uint32_t*>(slot + 2816);
+    const uint32_t sel = nib_sel(tig);
     float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
         const __nv_bfloat162 sA = bits_bf162(sc2[8 * s + tig]);
         const __nv_bfloat162 sB = bits_bf162(sc2[8 * s + 4 + tig]);
+        const __nv_bfloat162 nA = neg128(sA), nB = neg128(sB);
         const __nv_bfloat162 mA = bits_bf162(mn2[8 * s + tig]);
         const __nv_bfloat162 mB = bits_bf162(mn2[8 * s + 4 + tig]);
 #pragma unroll
@@ -129,8 +129,8 @@ __device__ __forceinline__ void warp_page_kivi(WarpAttn& st, uint8_t* slot, int 
             const int n = 8 * h + g;
             const uint32_t w0 = (uint32_t)kc[(2 * s) * kChunk + n];
             const uint32_t w1 = (uint32_t)kc[(2 * s + 1) * kChunk + n];
-            const uint32_t b0 = bf162_bits(dequant2(codes2_to_bf162(w0 >> (8 * tig), w0 >> (8 * tig + 4)), sA, mA));
-            const uint32_t b1 = bf162_bits(dequant2(codes2_to_bf162(w1 >> (8 * tig), w1 >> (8 * tig + 4)), sB, mB));
+            const uint32_t b0 = bf162_bits(dequant2_w(w0, sel, sA, nA, mA));
+            const uint32_t b1 = bf162_bits(dequant2_w(w1, sel, sB, nB, mB));
             mma_bf16_16816(sacc[h], st.qa[s][0], 0u, st.qa[s][1], 0u, b0, b1);
         }
     }
@@ -144,6 +144,7 @@ __device__ __forceinline__ void warp_page_kivi(WarpAttn& st, uint8_t* slot, int 
     for (int gp = 0; gp < kVGroups; ++gp) {
         const __nv_bfloat162 sLo = bits_bf162(vs[gp * 8 + tig]);
         const __nv_bfloat162 sHi = bits_bf162(vs[gp * 8 + 4 + tig]);
+        const __nv_bfloat162 nLo = neg128(sLo), nHi = neg128(sHi);
         const __nv_bfloat162 zLo = bits_bf162(vz[gp * 8 + tig]);
         const __nv_bfloat162 zHi = bits_bf162(vz[gp * 8 + 4 + tig]);
 #pragma unroll
@@ -152,10 +153,10 @@ __device__ __forceinline__ void warp_page_kivi(WarpAttn& st, uint8_t* slot, int 
             const int d = 16 * j + g;
             const uint2 wa = vc[d];
             const uint2 wb = vc[d + 8];
-            const uint32_t a0 = bf162_bits(dequant2(codes2_to_bf162(wa.x >> (8 * tig), wa.x >> (8 * tig + 4)), sLo, zLo));
-            const uint32_t a2 = bf162_bits(dequant2(codes2_to_bf162(wa.y >> (8 * tig), wa.y >> (8 * tig + 4)), sHi, zHi));
-            const uint32_t a1 = bf162_bits(dequant2(codes2_to_bf162(wb.x >> (8 * tig), wb.x >> (8 * tig + 4)), sLo, zLo));
-            const uint32_t a3 = bf162_bits(dequant2(codes2_to_bf162(wb.y >> (8 * tig), wb.y >> (8 * tig + 4)), sHi, zHi));
+            const uint32_t a0 = bf162_bits(dequant2_w(wa.x, sel, sLo, nLo, zLo));
+            const uint32_t a2 = bf162_bits(dequant2_w(wa.y, sel, sHi, nHi, zHi));
+            const uint32_t a1 = bf162_bits(dequant2_w(wb.x, sel, sLo, nLo, zLo));
+            const uint32_t a3 = bf162_bits(dequant2_w(wb.y, sel, sHi, nHi, zHi));
             mma_bf16_16816(st.o[j], a0, a1, a2, a3, pb0, pb1);
         }
     }
@@ -193,7 +194,6 @@ __device__ __forceinline__ void warp_page_raw8(WarpAttn& st, const uint8_t* slot
 __device__ __forceinline__ void issue_kivi_page(uint8_t* slot, uint64_t* bar, const zkv_page_layer& L, int64_t row,
                                                 int n_max, int64_t c) {
     if ((threadIdx.x & 31) == 0) {
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_arrive_expect_tx(bar, kPageTx);
         const int64_t pc = row * n_max + c;
         bulk_g2s(slot, L.kcodes + pc * (kWords * kChunk), 1024, bar);
@@ -220,10 +220,7 @@ __device__ __forceinline__ void issue_raw8(uint8_t* slot, uint64_t* bar, const u
         if (!((present >> rowi) & 1u))
             *reinterpret_cast<uint4*>(slot + part * kRawV + rowi * kRawStride * 2 + col * 16) = make_uint4(0, 0, 0, 0);
     }
-    if (lane == 0) {
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive_expect_tx(bar, (uint32_t)n_present * 512u);
-    }
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)n_present * 512u);
     __syncwarp();
     if (tok >= 0) {
         if (lane < 8) bulk_g2s(slot + t * kRawStride * 2, kbase + tok * kHeadDim, 256, bar);
@@ -280,24 +277,40 @@ __device__ void cta_merge(const WarpAttn& st, int G, float* scratch, float* cm, 
     }
 }
 
-// Rank 0 of the cluster combines the CS CTA partials and writes out / lse.
-__device__ void cluster_finalize(cg::cluster_group& cluster, int CS, int G, float* cm, float* cl, float* co,
-                                 uint16_t* out_row, float* lse_row) {
-    if (cluster.block_rank() != 0) return;
+// Cluster combine: every CTA pushes its partial (m, l, o) into rank 0's
+// receive area with distributed-shared-memory stores (no remote-load latency
+// chains), then rank 0 merges locally and writes out / lse.  `recv` is rank
+// 0's staging region (free once all CTAs passed the first cluster barrier).
+__device__ void cluster_merge(cg::cluster_group& cluster, int CS, int G, const float* cm, const float* cl,
+                              const float* co, float* recv, uint16_t* out_row, float* lse_row) {
+    constexpr int kPart = 16 + 8 * kHeadDim;  // m[8], l[8], o[8][128]
+    const int rank = (int)cluster.block_rank();
+    cluster.sync();  // every CTA finished phase 3 and its CTA merge
+    {
+        float* dst = cluster.map_shared_rank(recv, 0) + rank * kPart;
+        if (threadIdx.x < 8) {
+            dst[threadIdx.x] = cm[threadIdx.x];
+            dst[8 + threadIdx.x] = cl[threadIdx.x];
+        }
+        for (int i = threadIdx.x; i < G * kHeadDim / 4; i += kAttnThreads)
+            reinterpret_cast<float4*>(dst + 16)[i] = reinterpret_cast<const float4*>(co)[i];
+    }
+    cluster.sync();  // partials visible in rank 0
+    if (rank != 0) return;
     for (int i = threadIdx.x; i < G * kHeadDim; i += kAttnThreads) {
-        const int h = i / kHeadDim, d = i % kHeadDim;
+        const int h = i / kHeadDim;
         float M = -INFINITY;
-        for (int r = 0; r < CS; ++r) M = fmaxf(M, *cluster.map_shared_rank(cm + h, r));
+        for (int r = 0; r < CS; ++r) M = fmaxf(M, recv[r * kPart + h]);
         float Ls = 0.f, O = 0.f;
         for (int r = 0; r < CS; ++r) {
-            const float mr = *cluster.map_shared_rank(cm + h, r);
-            const float wt = (mr == -INFINITY) ? 0.f : ex2(mr - M);
-            Ls += wt * *cluster.map_shared_rank(cl + h, r);
-            O += wt * *cluster.map_shared_rank(co + h * kHeadDim + d, r);
+            const float* b = recv + r * kPart;
+            const float wt = (b[h] == -INFINITY) ? 0.f : ex2(b[h] - M);
+            Ls += wt * b[8 + h];
+            O += wt * b[16 + i];
         }
-        const float v = Ls > 0.f ? O / Ls : 0.f;
-        out_row[h * kHeadDim + d] = f2bfbits(v);
-        if (d == 0 && lse_row) lse_row[h] = (Ls > 0.f) ? (M + __log2f(Ls)) * 0.69314718055994531f : -INFINITY;
+        out_row[i] = f2bfbits(Ls > 0.f ? O / Ls : 0.f);
+        if ((i % kHeadDim) == 0 && lse_row)
+            lse_row[h] = (Ls > 0.f) ? (M + __log2f(Ls)) * 0.69314718055994531f : -INFINITY;
     }
 }
 
@@ -330,16 +343,22 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
     float* cl = cm + 8;
     float* co = cl + 8;
     int* hist = reinterpret_cast<int*>(co + 8 * kHeadDim);
-    int* misc = hist + 256;
-    int* scan = misc + 4;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(scan + 2 * kAttnThreads);  // [kStages] + [warps][2]
+    int* misc = hist + 512;
+    int* scan = misc + 8;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(scan + 2 * kAttnThreads);  // [warps][2] phase 1, [warps][2] phase 3
     __shared__ int s_failed;
+    __shared__ uint32_t s_mm[2 + 2 * 16];  // own (min, max) key; gathered per cluster rank
 
     if (threadIdx.x == 0) {
         s_failed = 0;
-        for (int i = 0; i < kStages + 2 * kAttnWarps; ++i) mbar_init(bars + i, 1);
+        s_mm[0] = 0xffffffffu;
+        s_mm[1] = 0u;
+        for (int i = 0; i < 4 * kAttnWarps; ++i) mbar_init(bars + i, 1);
         mbar_fence_init();
     }
+    // Split cluster barrier: arrive now, wait before the first remote
+    // shared-memory store, so every peer CTA is known to be running.
+    cluster.barrier_arrive();
     // query + GQA-mean query (compute() :1622-1626: bf16 mean over the group)
     for (int i = threadIdx.x; i < a.G * kHeadDim; i += kAttnThreads) q_s[i] = a.q[row * a.G * kHeadDim + i];
     __syncthreads();
@@ -351,83 +370,113 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
     __syncthreads();
 
     // ------------------------------------------------ phase 1: Quest scores
+    // Each warp streams blocks of 8 chunks (2 KiB of min + 2 KiB of max rows)
+    // through its own 2-slot ring; warps run independently.
+    constexpr int kBlk = 8;
     const int c0 = rank * a.per;
     const int c1 = min(a.n_c, c0 + a.per);
     const int n_my = max(0, c1 - c0);
-    const int n_blk = (n_my + kStageChunks - 1) / kStageChunks;
+    const int n_blk = (n_my + kBlk - 1) / kBlk;
     const uint16_t* gmin = reinterpret_cast<const uint16_t*>(a.L.chunk_min) + (row * a.n_max) * kHeadDim;
     const uint16_t* gmax = reinterpret_cast<const uint16_t*>(a.L.chunk_max) + (row * a.n_max) * kHeadDim;
-    constexpr int kStageHalf = kStageChunks * kHeadDim * 2;  // bytes of min rows per stage
-    auto issue_stage = [&](int b) {
-        const int s = b % kStages;
-        const int cc = c0 + b * kStageChunks;
-        const int nch = min(kStageChunks, c1 - cc);
-        uint8_t* dst = region + s * (2 * kStageHalf);
-        mbar_arrive_expect_tx(bars + s, (uint32_t)nch * kHeadDim * 2 * 2);
-        bulk_g2s(dst, gmin + (int64_t)cc * kHeadDim, nch * kHeadDim * 2, bars + s);
-        bulk_g2s(dst + kStageHalf, gmax + (int64_t)cc * kHeadDim, nch * kHeadDim * 2, bars + s);
-    };
-    if (threadIdx.x == 0)
-        for (int b = 0; b < min(kStages, n_blk); ++b) issue_stage(b);
     {
+        uint8_t* ring = region + warp * (2 * kSlotBytes);
+        uint64_t* rbar = bars + 2 * warp;
+        auto issue_blk = [&](int b, int k) {
+            if (lane == 0) {
+                const int cc = c0 + b * kBlk;
+                const int nch = min(kBlk, c1 - cc);
+                uint8_t* dst = ring + k * 4096;
+                mbar_arrive_expect_tx(rbar + k, (uint32_t)nch * kHeadDim * 2 * 2);
+                bulk_g2s(dst, gmin + (int64_t)cc * kHeadDim, nch * kHeadDim * 2, rbar + k);
+                bulk_g2s(dst + 2048, gmax + (int64_t)cc * kHeadDim, nch * kHeadDim * 2, rbar + k);
+            }
+        };
+        int mine = 0;
+        for (int b = warp; b < n_blk; b += kAttnWarps) ++mine;
+        if (mine > 0) issue_blk(warp, 0);
+        if (mine > 1) issue_blk(warp + kAttnWarps, 1);
         const int hl = lane & 15, half = lane >> 4;
         const uint4 qv = *reinterpret_cast<const uint4*>(rq_s + 8 * hl);
         bool ok = true;
-        for (int b = 0; b < n_blk; ++b) {
-            const int s = b % kStages;
-            if (!mbar_wait(bars + s, (uint32_t)((b / kStages) & 1), a.status)) ok = false;
-            const uint8_t* src = region + s * (2 * kStageHalf);
-            const int cc = c0 + b * kStageChunks;
-            const int nch = min(kStageChunks, c1 - cc);
+        uint32_t klo = 0xffffffffu, khi = 0u;
+        for (int i = 0; i < mine; ++i) {
+            const int b = warp + i * kAttnWarps;
+            const int k = i & 1;
+            if (!mbar_wait(rbar + k, (uint32_t)((i >> 1) & 1), a.status)) ok = false;
+            const uint8_t* src = ring + k * 4096;
+            const int cc = c0 + b * kBlk;
+            const int nch = min(kBlk, c1 - cc);
 #pragma unroll
-            for (int u = 0; u < kStageChunks / (2 * kAttnWarps); ++u) {
-                const int lc = (warp * (kStageChunks / kAttnWarps)) + 2 * u + half;
+            for (int u = 0; u < kBlk / 2; ++u) {
+                const int lc = 2 * u + half;
                 uint4 mn = make_uint4(0, 0, 0, 0), mx = mn;
                 if (lc < nch) {
                     mn = *reinterpret_cast<const uint4*>(src + lc * kHeadDim * 2 + 16 * hl);
-                    mx = *reinterpret_cast<const uint4*>(src + kStageHalf + lc * kHeadDim * 2 + 16 * hl);
+                    mx = *reinterpret_cast<const uint4*>(src + 2048 + lc * kHeadDim * 2 + 16 * hl);
                 }
                 const float sc = quest_half(qv, mn, mx);
                 if (hl == 0 && lc < nch) {
                     const int c = cc + lc;
                     const bool v = !a.L.valid || a.L.valid[row * a.n_max + c];
-                    sc_all[c] = (ok && v) ? sc : -INFINITY;
+                    const float val = (ok && v) ? sc : -INFINITY;
+                    sc_all[c] = val;
+                    const uint32_t kk = ordered_u32(val);
+                    if (kk > kOrderedNegInf) klo = min(klo, kk);
+                    khi = max(khi, kk);
                 }
             }
-            __syncthreads();
-            if (threadIdx.x == 0 && b + kStages < n_blk) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                issue_stage(b + kStages);
-            }
+            __syncwarp();
+            if (i + 2 < mine) issue_blk(b + 2 * kAttnWarps, k);
         }
-        if (!ok) atomicOr(&s_failed, 1);
-    }
-
-    // ------------------------------------------------ phase 2: exchange + select
-    cluster.sync();
-    for (int p = 0; p < CS; ++p) {
-        if (p == rank) continue;
-        const int lo = p * a.per, hi = min(a.n_c, lo + a.per);
-        const float* rsc = cluster.map_shared_rank(sc_all, p);
-        for (int i = lo + 4 * threadIdx.x; i < hi; i += 4 * kAttnThreads) {
-            if (i + 4 <= hi) {
-                *reinterpret_cast<float4*>(sc_all + i) = *reinterpret_cast<const float4*>(rsc + i);
-            } else {
-                for (int e = i; e < hi; ++e) sc_all[e] = rsc[e];
-            }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            klo = min(klo, __shfl_xor_sync(0xffffffffu, klo, off));
+            khi = max(khi, __shfl_xor_sync(0xffffffffu, khi, off));
         }
+        if (lane == 0) {
+            atomicMin(&s_mm[0], klo);
+            atomicMax(&s_mm[1], khi);
+        }
+        if (!ok && lane == 0) atomicOr(&s_failed, 1);
     }
     __syncthreads();
-    {
-        auto key = [&](int i) { return ordered_u32(sc_all[i]); };
-        if (a.n_c <= a.nk) {
-            for (int i = threadIdx.x; i < a.nk; i += kAttnThreads) sel_s[i] = i < a.n_c ? i : 0;
-            __syncthreads();
+    cluster.barrier_wait();
+    if (threadIdx.x < CS) {
+        uint32_t* rmm = cluster.map_shared_rank(s_mm, (int)threadIdx.x);
+        rmm[2 + 2 * rank] = s_mm[0];
+        rmm[3 + 2 * rank] = s_mm[1];
+    }
+    // push this CTA's score range into every peer's score array
+    for (int p = 1; p < CS; ++p) {
+        const int dst_rank = (rank + p) % CS;
+        float* rsc = cluster.map_shared_rank(sc_all, dst_rank);
+        for (int i = c0 + 4 * threadIdx.x; i < c1; i += 4 * kAttnThreads) {
+            if (i + 4 <= c1) {
+                *reinterpret_cast<float4*>(rsc + i) = *reinterpret_cast<const float4*>(sc_all + i);
+            } else {
+                for (int e = i; e < c1; ++e) rsc[e] = sc_all[e];
+            }
+        }
+    }
+
+    // ------------------------------------------------ phase 2: select
+    cluster.sync();
+    if (a.n_c <= a.nk) {
+        for (int i = threadIdx.x; i < a.nk; i += kAttnThreads) sel_s[i] = i < a.n_c ? i : 0;
+        __syncthreads();
+    } else {
+        uint32_t lo = 0xffffffffu, hi = 0u;
+        for (int r = 0; r < CS; ++r) {
+            lo = min(lo, s_mm[2 + 2 * r]);
+            hi = max(hi, s_mm[3 + 2 * r]);
+        }
+        if (a.n_c <= 16 * kAttnThreads) {
+            block_topk_small<kAttnThreads>(sc_all, a.n_c, a.nk, lo, hi, hist, misc, scan,
+                                           [&](int pos, int i) { sel_s[pos] = i; });
         } else {
-            uint32_t thr;
-            int take_eq;
-            block_radix_select<kAttnThreads>(key, a.n_c, a.nk, hist, misc, &thr, &take_eq);
-            block_select_compact<kAttnThreads>(key, a.n_c, thr, take_eq, scan, [&](int pos, int i) { sel_s[pos] = i; });
+            block_topk<kAttnThreads, true>([&](int i) { return ordered_u32(sc_all[i]); }, a.n_c, a.nk, hist, misc,
+                                           scan, [&](int pos, int i) { sel_s[pos] = i; }, true, lo, hi);
         }
     }
     if (a.sel_out && rank == 0)
@@ -444,8 +493,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
     const uint16_t* nk_base = reinterpret_cast<const uint16_t*>(a.L.near_k) + row * a.L.near_ld * kHeadDim;
     const uint16_t* nv_base = reinterpret_cast<const uint16_t*>(a.L.near_v) + row * a.L.near_ld * kHeadDim;
     uint8_t* wslot[2] = {region + (2 * warp) * kSlotBytes, region + (2 * warp + 1) * kSlotBytes};
-    uint64_t* wbar = bars + kStages + 2 * warp;
-    __syncthreads();  // the ring region is reused as warp slots
+    uint64_t* wbar = bars + 2 * kAttnWarps + 2 * warp;
     auto issue_item = [&](int it, int k) {
         if (it < n_pages) {
             issue_kivi_page(wslot[k], wbar + k, a.L, row, a.n_max, sel_s[p_lo + it]);
@@ -482,9 +530,8 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
     // ------------------------------------------------ phase 4: merge
     __syncthreads();
     cta_merge(st, a.G, reinterpret_cast<float*>(region), cm, cl, co);
-    cluster.sync();
-    cluster_finalize(cluster, CS, a.G, cm, cl, co, a.out + row * a.G * kHeadDim, a.lse ? a.lse + row * a.G : nullptr);
-    cluster.sync();
+    cluster_merge(cluster, CS, a.G, cm, cl, co, reinterpret_cast<float*>(region), a.out + row * a.G * kHeadDim,
+                  a.lse ? a.lse + row * a.G : nullptr);
     if (threadIdx.x == 0 && s_failed) set_status(a.status, ZKV_ERR_TIMEOUT);
 }
 
@@ -565,9 +612,8 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_rows_kernel(const RowsAr
     if (!ok && lane == 0) atomicOr(&s_failed, 1);
     __syncthreads();
     cta_merge(st, a.G, reinterpret_cast<float*>(region), cm, cl, co);
-    cluster.sync();
-    cluster_finalize(cluster, CS, a.G, cm, cl, co, a.out + row * a.G * kHeadDim, a.lse ? a.lse + row * a.G : nullptr);
-    cluster.sync();
+    cluster_merge(cluster, CS, a.G, cm, cl, co, reinterpret_cast<float*>(region), a.out + row * a.G * kHeadDim,
+                  a.lse ? a.lse + row * a.G : nullptr);
     if (threadIdx.x == 0 && s_failed) set_status(a.status, ZKV_ERR_TIMEOUT);
 }
 
@@ -689,8 +735,8 @@ extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int r
     a.sel_out = sel_out;
     a.status = status;
     const size_t smem = kRegionBytes + (size_t)a.n_c_pad * 4 + (size_t)((a.nk + 3) & ~3) * 4 + 9 * kHeadDim * 2 +
-                        (16 + 8 * kHeadDim) * 4 + (256 + 4 + 2 * kAttnThreads) * 4 +
-                        (kStages + 2 * kAttnWarps) * 8 + 16;
+                        (16 + 8 * kHeadDim) * 4 + (512 + 8 + 2 * kAttnThreads) * 4 +
+                        (4 * kAttnWarps) * 8 + 16;
     void* args[] = {&a};
     return launch_clustered((const void*)page_decode_kernel, rows, CS, smem, (cudaStream_t)stream, args);
 }

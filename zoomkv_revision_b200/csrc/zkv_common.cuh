@@ -48,6 +48,8 @@ __device__ __forceinline__ uint32_t kivi_code(uint16_t x, uint16_t mn, uint16_t 
     return (uint32_t)__float2int_rn(y);
 }
 
+__device__ __forceinline__ __nv_bfloat162 bits_bf162_pre(uint32_t v) { return *reinterpret_cast<__nv_bfloat162*>(&v); }
+
 // Two 4-bit codes -> exact bf16x2 (c_lo, c_hi): OR into the mantissa of
 // bf16(128) then subtract 128 (exact).
 __device__ __forceinline__ __nv_bfloat162 codes2_to_bf162(uint32_t lo, uint32_t hi) {
@@ -64,6 +66,25 @@ __device__ __forceinline__ __nv_bfloat162 codes2_to_bf162(uint32_t lo, uint32_t 
 // mul/add.bf16x2 without a rounding qualifier, which ptxas may fuse).
 __device__ __forceinline__ __nv_bfloat162 dequant2(__nv_bfloat162 c, __nv_bfloat162 s, __nv_bfloat162 z) {
     return __hadd2_rn(__hmul2_rn(c, s), z);
+}
+
+// Same ladder from packed nibbles in 5 instructions per pair.  Byte b of w
+// holds codes (c_lo, c_hi) = nibbles (2b, 2b+1); one byte-permute of (w,
+// w >> 4) with selector nib_sel(b) puts c_lo in the low nibble of byte 0 and
+// c_hi in the low nibble of byte 2, and a LOP3 makes bf16x2(128 + c_lo,
+// 128 + c_hi).  fma.rn((128 + c), s, -128 s) is bf16(c * s) exactly (one
+// rounding of the exact product c*s) and the add rounds once more:
+// bf16(bf16(c*s) + z), bit-identical to dequant2.
+__device__ __forceinline__ uint32_t nib_sel(int byte) { return (uint32_t)byte | ((uint32_t)(byte + 4) << 8); }
+__device__ __forceinline__ __nv_bfloat162 dequant2_w(uint32_t w, uint32_t sel, __nv_bfloat162 s,
+                                                      __nv_bfloat162 neg128s, __nv_bfloat162 z) {
+    const uint32_t x = __byte_perm(w, w >> 4, sel);
+    const uint32_t v = (x & 0x000F000Fu) | 0x43004300u;
+    return __hadd2_rn(__hfma2(bits_bf162_pre(v), s, neg128s), z);
+}
+__device__ __forceinline__ __nv_bfloat162 neg128(__nv_bfloat162 s) {
+    const uint32_t m = 0xC300C300u;  // bf16x2(-128, -128)
+    return __hmul2_rn(s, bits_bf162_pre(m));
 }
 
 __device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
@@ -258,6 +279,344 @@ __device__ void block_select_compact(KeyFn key, int n, uint32_t thr, int take_eq
             ++ebefore;
         }
     }
+    __syncthreads();
+}
+
+// ------------------------------------------------------------ fast deterministic top-k
+__device__ __forceinline__ float float_of_ordered(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+constexpr uint32_t kOrderedNegInf = 0x007fffffu;  // ordered_u32(-inf)
+
+// Writes the k best of n keys (larger key first, ties to the lowest index) in
+// ascending index order via out(pos, index).  Precondition 0 < k < n.
+//
+// Value-bucketed pivot select: (1) min/max of the keys (or the caller's),
+// (2) a 256-bin histogram with equal-width bins, monotone in the key: over
+// (key - min) >> shift when all keys share a sign (the ordered-u32 key is
+// then piecewise linear in the value), else over the float value (fp32 keys
+// only; -inf goes to bin 0); (3) the bin b* holding the k-th best; (4) that
+// bin's elements ranked exactly -> pivot (T_key, T_idx); (5) one ballot
+// compaction of bin > b* || (bin == b* && (key > T_key || (key == T_key &&
+// idx <= T_idx))).  Each thread keeps up to 16 keys in registers across the
+// passes (n <= 16 * NT); beyond that the passes re-read the keys.  When the
+// pivot bin holds more than NT elements (heavy ties) the 4-round radix select
+// runs instead; both give the same set.  Passes walk per-warp contiguous
+// segments with lane-consecutive indices (conflict-free; ballots keep the
+// order).  Scratch: hist[256], misc[8], scan[2*NT].
+template <int NT, bool kFloatKeys, typename KeyFn, typename OutFn>
+__device__ void block_topk(KeyFn key, int n, int k, int* hist, int* misc, int* scan, OutFn out,
+                           bool have_range = false, uint32_t lo_in = 0, uint32_t hi_in = 0) {
+    constexpr int NW = NT / 32;
+    constexpr int E = 16;  // keys per thread kept in registers
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int S = ((n + NW - 1) / NW + 31) & ~31;
+    const int seg0 = warp * S, seg1 = min(n, seg0 + S);
+    const bool in_regs = S <= 32 * E;
+    uint32_t kr[E];
+    if (in_regs) {
+#pragma unroll
+        for (int u = 0; u < E; ++u) {
+            const int idx = seg0 + 32 * u + lane;
+            kr[u] = idx < seg1 ? key(idx) : 0u;
+        }
+    }
+    auto key_at = [&](int u, int j0) -> uint32_t {
+        const int idx = j0 + 32 * u + lane;
+        return idx < seg1 ? key(idx) : 0u;
+    };
+    for (int i = tid; i < 256; i += NT) hist[i] = 0;
+    if (tid == 0) misc[3] = 0;
+    uint32_t lo = lo_in, hi = hi_in;
+    if (!have_range) {
+        lo = 0xffffffffu;
+        hi = 0u;
+        for (int j0 = seg0; j0 < seg1; j0 += 32 * E) {
+#pragma unroll
+            for (int u = 0; u < E; ++u) {
+                const uint32_t kk = in_regs ? kr[u] : key_at(u, j0);
+                if (j0 + 32 * u + lane < seg1) {
+                    if (!kFloatKeys || kk > kOrderedNegInf) lo = min(lo, kk);
+                    hi = max(hi, kk);
+                }
+            }
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, off));
+            hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, off));
+        }
+        if (lane == 0) {
+            scan[warp] = (int)lo;
+            scan[NW + warp] = (int)hi;
+        }
+        __syncthreads();
+        lo = 0xffffffffu;
+        hi = 0u;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            lo = min(lo, (uint32_t)scan[w]);
+            hi = max(hi, (uint32_t)scan[NW + w]);
+        }
+    } else {
+        __syncthreads();
+    }
+    const bool same_sign = !kFloatKeys || ((lo ^ hi) & 0x80000000u) == 0u;
+    const uint32_t span = hi > lo ? hi - lo : 0u;
+    const int bits = span ? 32 - __clz(span) : 0;
+    const int sh = bits > 8 ? bits - 8 : 0;
+    const float flo = float_of_ordered(lo), fhi = float_of_ordered(hi);
+    const float inv = (hi > lo) ? 256.0f / (fhi - flo) : 0.0f;
+    auto bucket = [&](uint32_t kk) -> uint32_t {
+        if (same_sign) return kk >= lo ? min((kk - lo) >> sh, 255u) : 0u;
+        if (kk <= kOrderedNegInf || hi <= lo) return 0u;
+        const float b = (float_of_ordered(kk) - flo) * inv;
+        return b >= 255.0f ? 255u : (b > 0.0f ? (uint32_t)b : 0u);
+    };
+    // pass A: histogram
+    for (int j0 = seg0; j0 < seg1; j0 += 32 * E) {
+#pragma unroll
+        for (int u = 0; u < E; ++u) {
+            const uint32_t kk = in_regs ? kr[u] : key_at(u, j0);
+            if (j0 + 32 * u + lane < seg1) atomicAdd(&hist[bucket(kk)], 1);
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int local[8];
+        int tot = 0;
+#pragma unroll
+        for (int j = 7; j >= 0; --j) {
+            tot += hist[8 * lane + j];
+            local[j] = tot;
+        }
+        int incl = tot;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int v = __shfl_down_sync(0xffffffffu, incl, off);
+            if (lane + off < 32) incl += v;
+        }
+        const int above = incl - tot;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int ge = above + local[j];
+            const int gt = ge - hist[8 * lane + j];
+            if (gt < k && ge >= k) {
+                misc[0] = 8 * lane + j;
+                misc[1] = gt;
+                misc[2] = hist[8 * lane + j];
+            }
+        }
+    }
+    __syncthreads();
+    const uint32_t bstar = (uint32_t)misc[0];
+    const int rem = k - misc[1];
+    const int m = misc[2];
+    if (m > NT - NW) {  // heavy ties (pivot bin too large for the rank step)
+        uint32_t tk;
+        int take_eq;
+        block_radix_select<NT>(key, n, k, hist, misc, &tk, &take_eq);
+        block_select_compact<NT>(key, n, tk, take_eq, scan, out);
+        return;
+    }
+    // pass B: gather the pivot bin, count elements of higher bins per warp
+    int above_cnt = 0;
+    for (int j0 = seg0; j0 < seg1; j0 += 32 * E) {
+#pragma unroll
+        for (int u = 0; u < E; ++u) {
+            const int idx = j0 + 32 * u + lane;
+            const uint32_t kk = in_regs ? kr[u] : key_at(u, j0);
+            const uint32_t b = idx < seg1 ? bucket(kk) : 0u;
+            above_cnt += __popc(__ballot_sync(0xffffffffu, idx < seg1 && b > bstar));
+            if (idx < seg1 && b == bstar) {
+                const int p = atomicAdd(&misc[3], 1);
+                scan[p] = (int)kk;
+                scan[NT + p] = idx;
+            }
+        }
+    }
+    __syncthreads();
+    // rank the pivot bin; each selected pivot-bin element adds to its warp's count
+    __shared__ int s_pw[NW];
+    if (tid < NW) s_pw[tid] = 0;
+    __syncthreads();
+    if (tid < m) {
+        const uint32_t mk = (uint32_t)scan[tid];
+        const int mi = scan[NT + tid];
+        int rank = 0;
+        for (int j = 0; j < m; ++j) {
+            const uint32_t kj = (uint32_t)scan[j];
+            const int ij = scan[NT + j];
+            rank += (kj > mk) || (kj == mk && ij < mi);
+        }
+        if (rank < rem) atomicAdd(&s_pw[mi / S], 1);
+        if (rank == rem - 1) {
+            misc[4] = (int)mk;
+            misc[5] = mi;
+        }
+    }
+    if (lane == 0) scan[2 * NT - NW + warp] = above_cnt;  // tail of scan: candidates use < NT - NW slots
+    __syncthreads();
+    const uint32_t tk = (uint32_t)misc[4];
+    const int ti = misc[5];
+    int pos = 0;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) pos += (w < warp) ? scan[2 * NT - NW + w] + s_pw[w] : 0;
+    // pass C: ordered write
+    const unsigned lt = (1u << lane) - 1u;
+    for (int j0 = seg0; j0 < seg1; j0 += 32 * E) {
+#pragma unroll
+        for (int u = 0; u < E; ++u) {
+            const int idx = j0 + 32 * u + lane;
+            const uint32_t kk = in_regs ? kr[u] : key_at(u, j0);
+            const uint32_t b = bucket(kk);
+            const bool f = idx < seg1 && (b > bstar || (b == bstar && (kk > tk || (kk == tk && idx <= ti))));
+            const unsigned bal = __ballot_sync(0xffffffffu, f);
+            if (f) out(pos + __popc(bal & lt), idx);
+            pos += __popc(bal);
+        }
+    }
+    __syncthreads();
+}
+
+
+// Small-n form of block_topk over fp32 scores in shared memory (n <= 16 NT):
+// each thread keeps 16 contiguous keys in registers (float4 loads), 512-bin
+// histogram, rank of the pivot bin, and a per-thread-count + warp-scan
+// compaction (no per-element ballots).  Same selected set and output order
+// as block_topk.  lo/hi: min finite key and max key (ordered u32).
+// Scratch: hist[512], misc[8], scan[2*NT].
+template <int NT, typename OutFn>
+__device__ void block_topk_small(const float* sc, int n, int k, uint32_t lo, uint32_t hi, int* hist, int* misc,
+                                 int* scan, OutFn out) {
+    constexpr int NW = NT / 32, E = 16, NB = 512;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int base = tid * E;
+    uint32_t kr[E];
+#pragma unroll
+    for (int v = 0; v < E / 4; ++v) {
+        float4 f = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        if (base + 4 * v < n) f = reinterpret_cast<const float4*>(sc + base)[v];
+        kr[4 * v + 0] = ordered_u32(f.x);
+        kr[4 * v + 1] = ordered_u32(f.y);
+        kr[4 * v + 2] = ordered_u32(f.z);
+        kr[4 * v + 3] = ordered_u32(f.w);
+    }
+    for (int i = tid; i < NB; i += NT) hist[i] = 0;
+    if (tid == 0) misc[3] = 0;
+    const bool same_sign = ((lo ^ hi) & 0x80000000u) == 0u;
+    const uint32_t span = hi > lo ? hi - lo : 0u;
+    const int bits = span ? 32 - __clz(span) : 0;
+    const int sh = bits > 9 ? bits - 9 : 0;
+    const float flo = float_of_ordered(lo), fhi = float_of_ordered(hi);
+    const float inv = (hi > lo) ? (float)NB / (fhi - flo) : 0.0f;
+    uint32_t bk[E];
+#pragma unroll
+    for (int u = 0; u < E; ++u) {
+        const uint32_t kk = kr[u];
+        uint32_t b;
+        if (same_sign) {
+            b = kk >= lo ? min((kk - lo) >> sh, (uint32_t)(NB - 1)) : 0u;
+        } else if (kk <= kOrderedNegInf || hi <= lo) {
+            b = 0u;
+        } else {
+            const float fb = (float_of_ordered(kk) - flo) * inv;
+            b = fb >= (float)(NB - 1) ? (uint32_t)(NB - 1) : (fb > 0.0f ? (uint32_t)fb : 0u);
+        }
+        bk[u] = b;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < E; ++u)
+        if (base + u < n) atomicAdd(&hist[bk[u]], 1);
+    __syncthreads();
+    if (warp == 0) {
+        constexpr int PL = NB / 32;
+        int local[PL];
+        int tot = 0;
+#pragma unroll
+        for (int j = PL - 1; j >= 0; --j) {
+            tot += hist[PL * lane + j];
+            local[j] = tot;
+        }
+        int incl = tot;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int v = __shfl_down_sync(0xffffffffu, incl, off);
+            if (lane + off < 32) incl += v;
+        }
+        const int above = incl - tot;
+#pragma unroll
+        for (int j = 0; j < PL; ++j) {
+            const int ge = above + local[j];
+            const int gt = ge - hist[PL * lane + j];
+            if (gt < k && ge >= k) {
+                misc[0] = PL * lane + j;
+                misc[1] = gt;
+                misc[2] = hist[PL * lane + j];
+            }
+        }
+    }
+    __syncthreads();
+    const uint32_t bstar = (uint32_t)misc[0];
+    const int rem = k - misc[1];
+    const int m = misc[2];
+    if (m > NT) {  // heavy ties: exact radix path over the same keys
+        auto key = [&](int i) { return ordered_u32(sc[i]); };
+        uint32_t tk;
+        int take_eq;
+        block_radix_select<NT>(key, n, k, hist, misc, &tk, &take_eq);
+        block_select_compact<NT>(key, n, tk, take_eq, scan, out);
+        return;
+    }
+#pragma unroll
+    for (int u = 0; u < E; ++u)
+        if (base + u < n && bk[u] == bstar) {
+            const int p = atomicAdd(&misc[3], 1);
+            scan[p] = (int)kr[u];
+            scan[NT + p] = base + u;
+        }
+    __syncthreads();
+    if (tid < m) {
+        const uint32_t mk = (uint32_t)scan[tid];
+        const int mi = scan[NT + tid];
+        int rank = 0;
+        for (int j = 0; j < m; ++j) {
+            const uint32_t kj = (uint32_t)scan[j];
+            const int ij = scan[NT + j];
+            rank += (kj > mk) || (kj == mk && ij < mi);
+        }
+        if (rank == rem - 1) {
+            misc[4] = (int)mk;
+            misc[5] = mi;
+        }
+    }
+    __syncthreads();
+    const uint32_t tk = (uint32_t)misc[4];
+    const int ti = misc[5];
+    int cnt = 0;
+    unsigned fl = 0;
+#pragma unroll
+    for (int u = 0; u < E; ++u) {
+        const bool f = base + u < n &&
+                       (bk[u] > bstar || (bk[u] == bstar && (kr[u] > tk || (kr[u] == tk && base + u <= ti))));
+        fl |= (unsigned)f << u;
+        cnt += f;
+    }
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += v;
+    }
+    if (lane == 31) scan[warp] = incl;
+    __syncthreads();
+    int pos = incl - cnt;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) pos += (w < warp) ? scan[w] : 0;
+#pragma unroll
+    for (int u = 0; u < E; ++u)
+        if ((fl >> u) & 1u) out(pos++, base + u);
     __syncthreads();
 }
 

@@ -41,13 +41,13 @@ __global__ void __launch_bounds__(256) quest_score_kernel(const uint16_t* __rest
 }
 
 // ----------------------------------------------------------- top-k
-constexpr int kTopkThreads = 512;
+constexpr int kTopkThreads = 256;
 
 template <typename KeyOf>
 __global__ void __launch_bounds__(kTopkThreads) topk_kernel(KeyOf keyof, int len, int64_t row_stride, int k,
                                                             int64_t* __restrict__ out) {
     __shared__ int hist[256];
-    __shared__ int misc[4];
+    __shared__ int misc[8];
     __shared__ int scan[2 * kTopkThreads];
     const int r = blockIdx.x;
     int64_t* o = out + (int64_t)r * k;
@@ -56,17 +56,16 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(KeyOf keyof, int len
         return;
     }
     auto key = [&](int i) { return keyof(r, (int64_t)r * row_stride + i); };
-    uint32_t thr;
-    int take_eq;
-    block_radix_select<kTopkThreads>(key, len, k, hist, misc, &thr, &take_eq);
-    block_select_compact<kTopkThreads>(key, len, thr, take_eq, scan, [&](int pos, int i) { o[pos] = i; });
+    block_topk<kTopkThreads, KeyOf::kFloat>(key, len, k, hist, misc, scan, [&](int pos, int i) { o[pos] = i; });
 }
 
 struct F32Key {
+    static constexpr bool kFloat = true;
     const float* p;
     __device__ uint32_t operator()(int, int64_t i) const { return ordered_u32(p[i]); }
 };
 struct I32Key {
+    static constexpr bool kFloat = false;
     const int32_t* p;
     __device__ uint32_t operator()(int, int64_t i) const { return ((uint32_t)p[i]) ^ 0x80000000u; }
 };
@@ -208,7 +207,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_gather_concat_kernel(const 
                                                                           int64_t* __restrict__ out, int L, int k,
                                                                           int sk, int64_t out_ld) {
     __shared__ int hist[256];
-    __shared__ int misc[4];
+    __shared__ int misc[8];
     __shared__ int scan[2 * kTopkThreads];
     const int r = blockIdx.x;
     int64_t* o = out + (int64_t)r * out_ld;
@@ -220,10 +219,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_gather_concat_kernel(const 
     }
     const float* s = scores + (int64_t)r * L;
     auto key = [&](int i) { return ordered_u32(s[i]); };
-    uint32_t thr;
-    int take_eq;
-    block_radix_select<kTopkThreads>(key, L, k, hist, misc, &thr, &take_eq);
-    block_select_compact<kTopkThreads>(key, L, thr, take_eq, scan, [&](int pos, int i) { o[pos] = lu[i]; });
+    block_topk<kTopkThreads, true>(key, L, k, hist, misc, scan, [&](int pos, int i) { o[pos] = lu[i]; });
 }
 
 }  // namespace zkv
