@@ -163,15 +163,16 @@ typedef struct zkv_page_layer {
     const int32_t* kcodes;  /* [rows][n_max][16][16] int32 (A-1 layout)     */
     const int32_t* vcodes_t;/* [rows][n_max][128][2] int32                   */
     const void* vmeta;      /* [rows][n_max][2][4][16] bf16                 */
-    const void* near_k;     /* [rows][near_ld][128] bf16 (residual window)  */
-    const void* near_v;     /* [rows][near_ld][128] bf16                    */
+    const void* near_k;     /* [rows][near_ld][128] bf16 raw rows (sink +   */
+    const void* near_v;     /*   residual window), row r at r*near_ld*128   */
     int64_t near_ld;        /* token capacity of the near buffers            */
 } zkv_page_layer;
 
 /* One fused launch per layer: GQA-mean query -> Quest scores over n_c
  * chunks -> top nk chunks (ties to the lowest id) -> attention of the G
  * query heads over [selected pages (4-bit K and V, dequantised in registers)
- * U the n_near residual bf16 rows] -> (out, lse).  A cluster of `cluster`
+ * U the raw bf16 rows [0, n_sink) U [near_start, near_start + n_near) of the
+ * near buffers] -> (out, lse).  A cluster of `cluster`
  * CTAs shares one row: scores and partial softmax states move through
  * distributed shared memory.  This is the HBM-resident form of
  * polar_cache.compute's retrieval branch with page selection
@@ -182,9 +183,10 @@ typedef struct zkv_page_layer {
  *   status: device int32 set to ZKV_ERR_TIMEOUT if a bounded wait expires
  *   (may be NULL); cluster in {1, 2, 4, 8} (0 = automatic).              */
 int zkv_page_decode(const void* q, const zkv_page_layer* layer, int rows,
-                    int G, int n_max, int n_c, int nk, int n_near, float scale,
-                    void* out, float* lse, int64_t* sel_out, int32_t* status,
-                    int cluster, void* stream);
+                    int G, int n_max, int n_c, int nk, int n_sink,
+                    int near_start, int n_near, float scale, void* out,
+                    float* lse, int64_t* sel_out, int32_t* status, int cluster,
+                    void* stream);
 
 /* Merge two attention partials by log-sum-exp (fp32 math, bf16 out).
  * Replaces lse_merge_cuda (cache_hub/lse_merge/lse_merge.cu:44-101).

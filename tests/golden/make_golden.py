@@ -21,6 +21,9 @@ Functions pinned (paths relative to runtime/zoomkv_urania_runtime_20261011/):
   * lse_merge_torch (cache_hub/lse_merge/lse_merge.py:79-119)
   * candidate-budget arithmetic _quest_aligned_candidate_tokens /
     _quest_candidate_ratio / _refresh_quest_chunk_cache (:1798-1925)
+  * the offload-bookkeeping state machine: _prefill_lockstep_batch,
+    decode_update_kv_cache, _update_polar_index, get_region_indices
+    (:880-1004, :1516-1583, :1379-1512, :1173-1259) driven step by step
 """
 from __future__ import annotations
 
@@ -204,6 +207,113 @@ def gen_host_logic(zmod, out):
         json.dump(rows, f, indent=0)
 
 
+class _Ev:
+    def record(self, *a):
+        pass
+
+    def wait(self, *a):
+        pass
+
+    def synchronize(self):
+        pass
+
+
+def gen_schedule(zmod, out):
+    """Drive the reference's own prefill / decode_update / flush / region code
+    (offload bookkeeping) on CPU tensors through a stub, for 2 layers, batch 2,
+    2 KV heads: record per-step state and the final chunk metadata."""
+    pc = zmod.polar_cache
+    L, bs, H, D = 2, 2, 2, 128
+    sink, local, interval = 4, 32, 24
+    prefill, steps, max_new = 107, 100, 120
+    g = torch.Generator().manual_seed(2024)
+    total_tokens = prefill + steps
+    keys = synth_keys(g, (bs, H, total_tokens, D))            # [bs, H, T, D] per layer 0
+    keys1 = synth_keys(g, (bs, H, total_tokens, D))
+    vals = torch.randn(bs, H, total_tokens, D, generator=g).to(torch.bfloat16)
+    layer_keys = [keys, keys1]
+    s = make_stub(zmod, bs, H, (prefill + max_new + 15) // 16, layers=L)
+    s.layer_num, s.batch_size, s.kv_head, s.head_dim, s.dtype = L, bs, H, D, torch.bfloat16
+    s.sink_size, s.local_size, s.steady_size = sink, local, sink + local
+    s.dynamic_update_interval = interval
+    s.max_new_length = max_new
+    s.input_length = prefill
+    s.valid_start = [0, 0]
+    s.enable_offload = True
+    s.gpu_kv_capacity = sink + local + interval
+    s.cpu_kv_capacity = prefill + max_new - sink - local
+    s.unified_keys_gpu = [torch.zeros(bs, H, s.gpu_kv_capacity, D, dtype=torch.bfloat16) for _ in range(L)]
+    s.unified_values_gpu = [torch.zeros(bs, H, s.gpu_kv_capacity, D, dtype=torch.bfloat16) for _ in range(L)]
+    s.unified_keys_cpu = [torch.zeros(bs, H, s.cpu_kv_capacity, D, dtype=torch.bfloat16) for _ in range(L)]
+    s.unified_values_cpu = [torch.zeros(bs, H, s.cpu_kv_capacity, D, dtype=torch.bfloat16) for _ in range(L)]
+    s._offload_keys_buffer = [torch.zeros(bs, H, interval, D, dtype=torch.bfloat16) for _ in range(L)]
+    s._offload_values_buffer = [torch.zeros(bs, H, interval, D, dtype=torch.bfloat16) for _ in range(L)]
+    s.cpu_valid_end = [0] * L
+    s._inflight_offload_buffers = [None] * L
+    s._layer_offload_inflight = [False] * L
+    s._main_events = [_Ev() for _ in range(L)]
+    s._copy_events = [_Ev() for _ in range(L)]
+    s._copy_stream = None
+    s._actual_retrieval_length = None
+    s.current_seq_len = [0] * L
+    s.context = 0
+    s._decode_step_counter = 0
+    s._cached_region_total_len = -1
+    s._cached_region_info = None
+    s._arange_buffer = torch.arange(prefill + max_new)
+    s._debug_flush = False
+    s.device = torch.device("cpu")
+    s.final_topk = 100
+    s.MAX_SKIPPED_INDICES = 512
+    s._chunk_skipped_indices_gpu = [torch.zeros(bs, H, 512, dtype=torch.int64) for _ in range(L)]
+    s._chunk_skipped_count = [0] * L
+    s._quest_scores_buffer = torch.empty(bs * H * s._chunk_n_max)
+    s.cds_dense_ratio = 0.3
+    s.quest_coarse_candidate_ratio = 0.4
+    s._dynamic_cand_enabled = True
+    s._dynamic_cand_thresholds, s._dynamic_cand_ratios = [5000, 10001], [0.7, 0.5, 0.4]
+    s._force_cand_tokens = None
+    s._topk_keys_buffer = None
+    for name in ("_refresh_quest_chunk_cache", "_refresh_live_skipped_indices", "_quest_aligned_candidate_tokens",
+                 "_quest_candidate_ratio", "_compute_local_start", "get_region_indices", "_update_polar_index",
+                 "decode_update_kv_cache", "_sync_layer_offload", "_prefill_lockstep_batch"):
+        setattr(s, name, functools.partial(getattr(pc, name), s))
+    s._sync_offload_copies = lambda: None
+    # prefill: pre-set the retrieval length so the stub never allocates pinned host buffers
+    retrieval = max(sink, prefill - local) - sink
+    s._actual_retrieval_length = retrieval
+    s._refresh_quest_chunk_cache(retrieval)
+    for l in range(L):
+        k4 = layer_keys[l][:, :, :prefill].transpose(1, 2).contiguous()   # [bs, T, H, D]
+        v4 = vals[:, :, :prefill].transpose(1, 2).contiguous()
+        s._prefill_lockstep_batch(k4, v4, l)
+    trace = []
+    for t in range(steps):
+        pos = prefill + t
+        for l in range(L):
+            k1 = layer_keys[l][:, :, pos:pos + 1].transpose(1, 2).contiguous()
+            v1 = vals[:, :, pos:pos + 1].transpose(1, 2).contiguous()
+            s.decode_update_kv_cache(k1, v1, l)
+            reg = s.get_region_indices(l)
+            trace.append(dict(step=t, layer=l, total_len=int(reg["total_len"]),
+                              retrieval_length=int(reg["retrieval_length"]), local_len=int(reg["local_len"]),
+                              cpu_valid_end=int(s.cpu_valid_end[l]), actual=int(s._actual_retrieval_length),
+                              nk=int(s._cached_quest_nk), n_chunks=int(s._cached_quest_n_chunks),
+                              skipped=int(s._chunk_skipped_count[l]), carry=int(s._chunk_carry_count[l])))
+    np.savez_compressed(
+        os.path.join(out, "schedule.npz"),
+        keys0=bf16_bits(keys), keys1=bf16_bits(keys1), values=bf16_bits(vals),
+        chunk_min=np.stack([bf16_bits(s._chunk_key_min_gpu[l]) for l in range(L)]),
+        chunk_max=np.stack([bf16_bits(s._chunk_key_max_gpu[l]) for l in range(L)]),
+        centroid=np.stack([bf16_bits(s._chunk_key_centroid_gpu[l]) for l in range(L)]),
+        packed=np.stack([s.key_kivi_packed_gpu[l].numpy() for l in range(L)]),
+        valid=np.stack([s._chunk_valid_mask_gpu[l].numpy().astype(np.uint8) for l in range(L)]),
+        skipped_idx=np.stack([s._chunk_skipped_indices_gpu[l].numpy() for l in range(L)]),
+        params=np.array([L, bs, H, sink, local, interval, prefill, steps, max_new]))
+    with open(os.path.join(out, "schedule_trace.json"), "w") as f:
+        json.dump(trace, f)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -218,6 +328,7 @@ def main():
     gen_quest_density(zmod, a.out)
     gen_lse(a.out)
     gen_host_logic(zmod, a.out)
+    gen_schedule(zmod, a.out)
     print("golden fixtures written to", a.out)
 
 

@@ -46,8 +46,8 @@ _SIGNATURES = {
     "zkv_topk_gather_concat": [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p, _i32, _i32, _i32, _i32, _i64, _c_void_p],
     "zkv_attn_rows": [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _i32, _i64, _i64,
                       _i32, _i32, _f32, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p],
-    "zkv_page_decode": [_c_void_p, ctypes.POINTER(ZkvPageLayer), _i32, _i32, _i32, _i32, _i32, _i32, _f32, _c_void_p,
-                        _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p],
+    "zkv_page_decode": [_c_void_p, ctypes.POINTER(ZkvPageLayer), _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32,
+                        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p],
     "zkv_lse_merge": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p],
     "zkv_lse_merge_n": [_c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p],
     "zkv_version": [],

@@ -318,7 +318,7 @@ __device__ void cluster_merge(cg::cluster_group& cluster, int CS, int G, const f
 struct PageArgs {
     const uint16_t* q;
     zkv_page_layer L;
-    int G, n_max, n_c, nk, n_near, n_c_pad, per, pp, pn;
+    int G, n_max, n_c, nk, n_sink, near_start, n_near, n_c_pad, per, pp, pn;
     float sl2;
     uint16_t* out;
     float* lse;
@@ -486,7 +486,8 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
     WarpAttn st;
     warp_attn_init(st, q_s, a.G);
     const int p_lo = rank * a.pp, p_hi = min(a.nk, p_lo + a.pp);
-    const int n_lo = rank * a.pn, n_hi = min(a.n_near, n_lo + a.pn);
+    const int n_raw_all = a.n_sink + a.n_near;
+    const int n_lo = rank * a.pn, n_hi = min(n_raw_all, n_lo + a.pn);
     const int n_pages = max(0, p_hi - p_lo);
     const int n_raw = max(0, (n_hi - n_lo + 7) / 8);
     const int n_items = n_pages + n_raw;
@@ -499,8 +500,11 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
             issue_kivi_page(wslot[k], wbar + k, a.L, row, a.n_max, sel_s[p_lo + it]);
         } else {
             const int base = n_lo + 8 * (it - n_pages);
-            issue_raw8(wslot[k], wbar + k, nk_base, nv_base,
-                       [&](int t) -> int64_t { return (base + t < n_hi) ? (int64_t)(base + t) : -1; });
+            issue_raw8(wslot[k], wbar + k, nk_base, nv_base, [&](int t) -> int64_t {
+                const int v = base + t;
+                if (v >= n_hi) return -1;
+                return v < a.n_sink ? (int64_t)v : (int64_t)(a.near_start + v - a.n_sink);
+            });
         }
     };
     {
@@ -701,16 +705,18 @@ static int launch_clustered(const void* fn, int rows, int CS, size_t smem, cudaS
 }
 
 extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max, int n_c,
-                               int nk, int n_near, float scale, void* out, float* lse, int64_t* sel_out,
-                               int32_t* status, int cluster, void* stream) {
-    if (!q || !layer || !out || rows < 0 || G < 1 || G > 8 || n_c < 0 || n_c > n_max || nk < 1 || n_near < 0)
+                               int nk, int n_sink, int near_start, int n_near, float scale, void* out, float* lse,
+                               int64_t* sel_out, int32_t* status, int cluster, void* stream) {
+    if (!q || !layer || !out || rows < 0 || G < 1 || G > 8 || n_c < 0 || n_c > n_max || nk < 1 || n_near < 0 ||
+        n_sink < 0 || near_start < 0)
         return ZKV_ERR_ARG;
     if (nk > n_c && n_c > 0) return ZKV_ERR_ARG;
-    if (n_near > layer->near_ld) return ZKV_ERR_ARG;
+    if ((int64_t)near_start + n_near > layer->near_ld || n_sink > layer->near_ld) return ZKV_ERR_ARG;
     if (n_c > 16384 || nk > 2048) return ZKV_ERR_CAPACITY;
     if (rows == 0) return ZKV_OK;
     const zkv_page_layer& L = *layer;
-    if (!L.chunk_min || !L.chunk_max || !L.kcodes || !L.vcodes_t || !L.vmeta || (n_near > 0 && (!L.near_k || !L.near_v)))
+    if (!L.chunk_min || !L.chunk_max || !L.kcodes || !L.vcodes_t || !L.vmeta ||
+        (n_near + n_sink > 0 && (!L.near_k || !L.near_v)))
         return ZKV_ERR_ARG;
     if (((uintptr_t)L.chunk_min & 15) || ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)L.kcodes & 15) ||
         ((uintptr_t)L.vcodes_t & 15) || ((uintptr_t)L.vmeta & 15) || ((uintptr_t)L.near_k & 15) ||
@@ -724,11 +730,13 @@ extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int r
     a.n_max = n_max;
     a.n_c = n_c;
     a.nk = n_c > 0 ? nk : 0;
+    a.n_sink = n_sink;
+    a.near_start = near_start;
     a.n_near = n_near;
     a.n_c_pad = (n_c + 3) & ~3;
     a.per = ((n_c + CS - 1) / CS + 3) & ~3;
     a.pp = (a.nk + CS - 1) / CS;
-    a.pn = ((n_near + CS - 1) / CS + 7) & ~7;
+    a.pn = ((n_sink + n_near + CS - 1) / CS + 7) & ~7;
     a.sl2 = scale * 1.4426950408889634f;
     a.out = (uint16_t*)out;
     a.lse = lse;

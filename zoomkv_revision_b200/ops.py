@@ -344,9 +344,12 @@ class PageLayer:
             near_k.shape[2])
 
 
-def page_decode(q, layer: PageLayer, n_c: int, nk: int, n_near: int, *, scale=None, out=None, lse=None, sel_out=None,
-                status=None, cluster=0):
-    """Fused page-mode decode: q [bs,1,H*G,128] -> out [bs,1,H*G,128]."""
+def page_decode(q, layer: PageLayer, n_c: int, nk: int, n_near: int, *, n_sink: int = 0, near_start: int = 0,
+                scale=None, out=None, lse=None, sel_out=None, status=None, cluster=0):
+    """Fused page-mode decode: q [bs,1,H*G,128] -> out [bs,1,H*G,128].
+
+    Raw rows attended besides the selected pages: [0, n_sink) and
+    [near_start, near_start + n_near) of the layer's near buffers."""
     cmin = layer.tensors[0]
     bs, H, n_max, D = cmin.shape
     G = q.shape[2] // H
@@ -354,7 +357,7 @@ def page_decode(q, layer: PageLayer, n_c: int, nk: int, n_near: int, *, scale=No
     if out is None:
         out = torch.empty(bs, 1, H * G, D, dtype=torch.bfloat16, device=q.device)
     scale = (1.0 / D ** 0.5) if scale is None else float(scale)
-    check(lib().zkv_page_decode(_p(qc), ctypes.byref(layer.struct), bs * H, G, n_max, int(n_c), int(nk), int(n_near),
-                                scale, _p(out), _p(lse), _p(sel_out), _p(status), int(cluster), _stream(q)),
-          "zkv_page_decode")
+    check(lib().zkv_page_decode(_p(qc), ctypes.byref(layer.struct), bs * H, G, n_max, int(n_c), int(nk), int(n_sink),
+                                int(near_start), int(n_near), scale, _p(out), _p(lse), _p(sel_out), _p(status),
+                                int(cluster), _stream(q)), "zkv_page_decode")
     return out
