@@ -3,7 +3,8 @@
 //  * zkv_page_decode: one fused launch per layer.  A thread-block cluster of
 //    CS CTAs owns one (batch, kv_head) row:
 //      phase 1  each CTA streams its share of the Quest min/max metadata with
-//               1-D TMA bulk copies (4-stage mbarrier ring) and scores chunks;
+//               1-D TMA bulk copies (a 2-slot mbarrier ring per warp) and
+//               scores chunks;
 //      phase 2  scores are exchanged through distributed shared memory and
 //               every CTA runs the same deterministic radix top-k;
 //      phase 3  each warp double-buffers its pages (4-bit K, 4-bit V, scales)
