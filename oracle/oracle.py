@@ -22,13 +22,15 @@ __all__ = [
     "build_oracle", "lib", "bf16_to_f32", "f32_to_bf16", "kivi_encode_chunks", "vquant_tokens",
     "quest_score", "topk_f32", "topk_i32", "chunk_density", "mask_from_topk", "kivi_qk",
     "topk_gather_concat", "attn_dense", "page_decode", "lse_merge", "kivi_dequant_chunk",
-    "vdequant_tokens", "page_layout_values",
+    "vdequant_tokens", "page_layout_values", "rq_mag_tables", "rq_encode", "rq_query", "collision_weights",
+    "collision_count", "update_cache_cnt_sorted", "rerank4", "coarse2bit", "rq_query_4bit", "popcount_est",
+    "exact_ip",
 ]
 
 
 def build_oracle(force: bool = False) -> str:
-    if force or not os.path.exists(LIB_PATH) or \
-            os.path.getmtime(LIB_PATH) < os.path.getmtime(os.path.join(HERE, "zkv_oracle.c")):
+    srcs = [os.path.join(HERE, f) for f in ("zkv_oracle.c", "zkv_oracle_rabitq.c", "zkv_oracle.h")]
+    if force or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < max(map(os.path.getmtime, srcs)):
         subprocess.run(["make", "-s", "-C", HERE], check=True)
     return LIB_PATH
 
@@ -277,3 +279,160 @@ def page_layout_values(codes: np.ndarray, meta: np.ndarray):
     m = meta.reshape(R, P, 16, D // 32, 2)
     vmeta = np.ascontiguousarray(m.transpose(0, 1, 4, 3, 2))
     return np.ascontiguousarray(vcodes_t), vmeta
+
+
+# ----------------------------------------------------------------- ParisKV / RaBitQ
+# Token-major layouts: codes [R, cap, 16] u8, packed [R, cap, 64] u8,
+# weight [R, cap, 16] bf16, factor [R, cap] f32, hist [R, 16, 256] i32.
+def rq_mag_tables():
+    thr = np.empty(7, np.uint16)
+    cen = np.empty(8, np.uint16)
+    lib().orc_rq_mag_tables(_p(thr), _p(cen))
+    return thr, cen
+
+
+def rq_encode(keys: np.ndarray, signs: np.ndarray):
+    """keys [R, T, 128] bf16 -> codes, packed, weight, factor, hist
+    (ParisKV batch_encode + _count_cluster_keys)."""
+    keys = np.ascontiguousarray(keys, dtype=np.uint16)
+    R, T, D = keys.shape
+    codes = np.zeros((R, T, 16), np.uint8)
+    packed = np.zeros((R, T, 64), np.uint8)
+    weight = np.zeros((R, T, 16), np.uint16)
+    factor = np.zeros((R, T), np.float32)
+    hist = np.zeros((R, 16, 256), np.int32)
+    L = lib()
+    L.orc_rq_encode_rows.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_int64] + [ctypes.c_void_p] * 6
+    L.orc_rq_encode_rows(_p(keys), T * D, R, T, 0, T, _p(np.ascontiguousarray(signs, np.uint16)), _p(codes),
+                         _p(packed), _p(weight), _p(factor), _p(hist))
+    return codes, packed, weight, factor, hist
+
+
+def rq_query(q: np.ndarray, signs: np.ndarray):
+    """q [R, G, 128] bf16 -> (q_blocks [R, 128] bf16, q_norm [R] bf16, q_mean [R, 128] bf16)."""
+    q = np.ascontiguousarray(q, dtype=np.uint16)
+    R, G, D = q.shape
+    qb = np.empty((R, D), np.uint16)
+    qn = np.empty(R, np.uint16)
+    qm = np.empty((R, D), np.uint16)
+    L = lib()
+    L.orc_rq_query.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int] + [ctypes.c_void_p] * 4
+    L.orc_rq_query(_p(q), R, G, _p(np.ascontiguousarray(signs, np.uint16)), _p(qb), _p(qn), _p(qm))
+    return qb, qn, qm
+
+
+def collision_weights(q_blocks: np.ndarray, hist: np.ndarray, targets) -> np.ndarray:
+    """-> table [R, 16, 256] u8 of per-bucket tier hits."""
+    q_blocks = np.ascontiguousarray(q_blocks, np.uint16).reshape(-1, 128)
+    R = q_blocks.shape[0]
+    t = np.ascontiguousarray(targets, np.int64)
+    table = np.empty((R, 16, 256), np.uint8)
+    L = lib()
+    L.orc_collision_weights.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                        ctypes.c_void_p]
+    L.orc_collision_weights(_p(q_blocks), _p(np.ascontiguousarray(hist, np.int32)), R, _p(t), len(t), _p(table))
+    return table
+
+
+def collision_count(table: np.ndarray, codes: np.ndarray, kv_len: int | None = None) -> np.ndarray:
+    codes = np.ascontiguousarray(codes, np.uint8)
+    R, cap, _ = codes.shape
+    kv_len = cap if kv_len is None else kv_len
+    cnt = np.empty((R, kv_len), np.int32)
+    L = lib()
+    L.orc_collision_count.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_void_p]
+    L.orc_collision_count(_p(np.ascontiguousarray(table, np.uint8)), _p(codes), cap, R, kv_len, _p(cnt))
+    return cnt
+
+
+def update_cache_cnt_sorted(sorted_ids, hist, codes_bm, targets) -> np.ndarray:
+    """update_cache_cnt_overall_ref with given sorted ids; codes block-major [R, B, kv_len]."""
+    sorted_ids = np.ascontiguousarray(sorted_ids, np.int64)
+    R, B, K = sorted_ids.shape
+    codes_bm = np.ascontiguousarray(codes_bm, np.int32)
+    kv_len = codes_bm.shape[-1]
+    t = np.ascontiguousarray(targets, np.int64)
+    cnt = np.empty((R, kv_len), np.int32)
+    L = lib()
+    L.orc_update_cache_cnt_sorted.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 4 + [ctypes.c_void_p,
+                                                                                          ctypes.c_int, ctypes.c_void_p]
+    L.orc_update_cache_cnt_sorted(_p(sorted_ids), _p(np.ascontiguousarray(hist, np.int32)), _p(codes_bm), R, B, K,
+                                  kv_len, _p(t), len(t), _p(cnt))
+    return cnt
+
+
+def rerank4(cand, packed, weight, q_blocks, q_norm, cen8=None) -> np.ndarray:
+    """Sequential-bf16 4-bit RaBitQ scores [R, C] bf16 of candidate keys."""
+    cand = np.ascontiguousarray(cand, np.int64)
+    R, C = cand.shape
+    packed = np.ascontiguousarray(packed, np.uint8)
+    cap = packed.shape[1]
+    if cen8 is None:
+        cen8 = rq_mag_tables()[1]
+    out = np.empty((R, C), np.uint16)
+    L = lib()
+    L.orc_rerank4.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64] + \
+        [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_void_p]
+    L.orc_rerank4(_p(cand), C, _p(packed), _p(np.ascontiguousarray(weight, np.uint16)), cap,
+                  _p(np.ascontiguousarray(q_blocks, np.uint16)), _p(np.ascontiguousarray(q_norm, np.uint16)),
+                  _p(np.ascontiguousarray(cen8, np.uint16)), R, _p(out))
+    return out
+
+
+def coarse2bit(packed, q_signs, q_mags, kv_len: int | None = None) -> np.ndarray:
+    packed = np.ascontiguousarray(packed, np.uint8)
+    R, cap, _ = packed.shape
+    kv_len = cap if kv_len is None else kv_len
+    out = np.empty((R, kv_len), np.int32)
+    L = lib()
+    L.orc_coarse2bit.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                 ctypes.c_int, ctypes.c_void_p]
+    L.orc_coarse2bit(_p(packed), cap, _p(np.ascontiguousarray(q_signs, np.uint8)),
+                     _p(np.ascontiguousarray(q_mags, np.uint8)), R, kv_len, _p(out))
+    return out
+
+
+def rq_query_4bit(q_blocks, q_norm):
+    q_blocks = np.ascontiguousarray(q_blocks, np.uint16).reshape(-1, 128)
+    R = q_blocks.shape[0]
+    planes = np.empty((R, 4, 16), np.uint8)
+    qp = np.empty((R, 4), np.float32)
+    L = lib()
+    L.orc_rq_query_4bit.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+    L.orc_rq_query_4bit(_p(q_blocks), _p(np.ascontiguousarray(q_norm, np.uint16)), R, _p(planes), _p(qp))
+    return planes, qp
+
+
+def popcount_est(cand, codes, factor, planes, qparams):
+    """-> (est [R, C] f32, ints [R, C, 2] i32 = (I, P)); cand None = all keys."""
+    codes = np.ascontiguousarray(codes, np.uint8)
+    R, cap, _ = codes.shape
+    if cand is not None:
+        cand = np.ascontiguousarray(cand, np.int64)
+        C = cand.shape[1]
+    else:
+        C = cap
+    est = np.empty((R, C), np.float32)
+    ints = np.empty((R, C, 2), np.int32)
+    L = lib()
+    L.orc_popcount_est.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+    L.orc_popcount_est(_p(cand), C, _p(codes), _p(np.ascontiguousarray(factor, np.float32)), cap,
+                       _p(np.ascontiguousarray(planes, np.uint8)), _p(np.ascontiguousarray(qparams, np.float32)), R,
+                       _p(est), _p(ints))
+    return est, ints
+
+
+def exact_ip(idx, keys, q) -> np.ndarray:
+    """idx [R, n] -> fp32 <keys[r, idx], q[r]> (lane-tree order); keys [R, T, 128] bf16."""
+    idx = np.ascontiguousarray(idx, np.int64)
+    keys = np.ascontiguousarray(keys, np.uint16)
+    R, n = idx.shape
+    out = np.empty((R, n), np.float32)
+    L = lib()
+    L.orc_exact_ip.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                               ctypes.c_int, ctypes.c_void_p]
+    L.orc_exact_ip(_p(idx), n, _p(keys), keys.shape[1] * 128, _p(np.ascontiguousarray(q, np.uint16)), R, _p(out))
+    return out

@@ -132,6 +132,41 @@ void orc_lse_merge(const float* a, const float* la, const float* b,
                    const float* lb, float* out, float* lse_out, int rows,
                    int dim);
 
+/* ---- ParisKV / RaBitQ retrieval (zkv_oracle_rabitq.c); token-major layouts:
+ * codes [rows][cap][16] u8, packed [rows][cap][16][4] u8, weight
+ * [rows][cap][16] bf16, factor [rows][cap] f32, hist [rows][16][256] i32. */
+void orc_rq_mag_tables(uint16_t* thr7, uint16_t* cen8);
+/* batch_encode, cache_hub/polar_cache.py:1130-1198 (one key).            */
+void orc_rq_encode_key(const uint16_t* key, const uint16_t* signs, uint8_t* codes, uint8_t* packed,
+                       uint16_t* weight, float* factor);
+void orc_rq_encode_rows(const uint16_t* keys, int64_t ld_row, int rows, int n_tok, int tok_start, int64_t cap,
+                        const uint16_t* signs, uint8_t* codes, uint8_t* packed, uint16_t* weight, float* factor,
+                        int32_t* hist);
+/* GQA mean + _encode_query_blocks, cache_hub/polar_cache.py:1108-1127.    */
+void orc_rq_query(const uint16_t* q, int rows, int G, const uint16_t* signs, uint16_t* q_blocks, uint16_t* q_norm,
+                  uint16_t* q_mean);
+/* get_cache_cnt_fused, cache_hub/polar_cache.py:1688-1728 (weights).     */
+void orc_collision_weights(const uint16_t* q_blocks, const int32_t* hist, int rows, const int64_t* targets,
+                           int n_tiers, uint8_t* table);
+/* update_cache_cnt_kernel, collision_fused/collision.cu:161-245.         */
+void orc_collision_count(const uint8_t* table, const uint8_t* codes, int64_t cap, int rows, int kv_len, int32_t* cnt);
+/* update_cache_cnt_overall_ref, collision_fused/collision_test.py:89-121. */
+void orc_update_cache_cnt_sorted(const int64_t* sorted_ids, const int32_t* hist, const int32_t* codes, int rows,
+                                 int B, int K, int kv_len, const int64_t* targets, int n_tiers, int32_t* cnt);
+/* partial_rerank_kernel, rerank/rerank.cu:52-143.                        */
+void orc_rerank4(const int64_t* cand, int C, const uint8_t* packed, const uint16_t* weight, int64_t cap,
+                 const uint16_t* q_blocks, const uint16_t* q_norm, const uint16_t* cen8, int rows,
+                 uint16_t* scores);
+/* coarse_2bit_score_kernel, rerank/coarse_2bit_score.cu:86-156.          */
+void orc_coarse2bit(const uint8_t* packed, int64_t cap, const uint8_t* q_signs, const uint8_t* q_mags, int rows,
+                    int kv_len, int32_t* out);
+/* 1-bit x 4-bit popcount estimator (RaBitQ paper; no reference code).    */
+void orc_rq_query_4bit(const uint16_t* q_blocks, const uint16_t* q_norm, int rows, uint8_t* planes, float* qparams);
+void orc_popcount_est(const int64_t* cand, int C, const uint8_t* codes, const float* factor, int64_t cap,
+                      const uint8_t* planes, const float* qparams, int rows, float* est, int32_t* ints);
+void orc_exact_ip(const int64_t* idx, int n, const uint16_t* keys, int64_t ld_row, const uint16_t* q, int rows,
+                  float* out);
+
 #ifdef __cplusplus
 }
 #endif

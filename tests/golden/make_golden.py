@@ -24,6 +24,13 @@ Functions pinned (paths relative to runtime/zoomkv_urania_runtime_20261011/):
   * the offload-bookkeeping state machine: _prefill_lockstep_batch,
     decode_update_kv_cache, _update_polar_index, get_region_indices
     (:880-1004, :1516-1583, :1379-1512, :1173-1259) driven step by step
+  * ParisKV (cache_hub/polar_cache.py): batch_encode (:1130-1198),
+    _count_cluster_keys (:1203-1226), _encode_query_blocks (:1108-1127) and
+    the bucket ordering of get_cache_cnt_fused (:1688-1728), with the sign
+    codebook read from turboquant/codebooks/*.json
+  * update_cache_cnt_overall_ref / generate_test_input
+    (cache_hub/collision_fused/collision_test.py:17-121)
+  * python_rabitq_scores / make_inputs (cache_hub/rerank/test_rerank_topk.py:27-111)
 """
 from __future__ import annotations
 
@@ -314,6 +321,79 @@ def gen_schedule(zmod, out):
         json.dump(trace, f)
 
 
+def rabitq_stub(pmod, signs):
+    """The fields of ParisKV's polar_cache that batch_encode and
+    _encode_query_blocks read (cache_hub/polar_cache.py:262-273, :428)."""
+    st = types.SimpleNamespace()
+    st.quantizer = types.SimpleNamespace(B=16, m=8, srht_diagonal_signs=[signs])
+    st.polar_B, st.polar_m, st.polar_K_omega = 16, 8, 256
+    st._hadamard_scale = 1.0 / np.sqrt(128)
+    st._mag_thresholds = torch.tensor([0.0843, 0.1698, 0.2578, 0.3499, 0.4487, 0.5585, 0.6901], dtype=torch.bfloat16)
+    st._mag_centers = torch.tensor([0.0420, 0.1266, 0.2130, 0.3025, 0.3973, 0.5001, 0.6169, 0.7633],
+                                   dtype=torch.bfloat16)
+    st._bitpack_shifts = (1 << torch.arange(8, dtype=torch.uint8))
+    st._pack_4bit_codes = types.MethodType(pmod.polar_cache._pack_4bit_codes, st)
+    return st
+
+
+def gen_rabitq(pmod, ref_root, out):
+    """ParisKV encode + query + collision ordering (config-2 shapes, reduced N)."""
+    pc = pmod.polar_cache
+    torch.manual_seed(42)  # the reference seeds the SRHT signs with 42 (:81-90; CPU generator here)
+    signs = torch.randint(0, 2, (128,), dtype=torch.bfloat16) * 2 - 1
+    st = rabitq_stub(pmod, signs)
+    g = torch.Generator().manual_seed(7)
+    bs, H, N, G = 2, 2, 1024, 4
+    spread = torch.exp(torch.randn(bs, H, N, 1, generator=g) * 0.5)   # norm spread
+    keys = (torch.randn(bs, H, N, 128, generator=g) * spread).to(torch.bfloat16)
+    codebook, weight, packed = pc.batch_encode(st, keys)
+    hist = pc._count_cluster_keys(st, codebook, "cpu")
+    q = torch.randn(bs, 1, H * G, 128, generator=g).to(torch.bfloat16)
+    q_avg = q[:, 0].view(bs, H, G, 128).mean(dim=2)
+    q_blocks, q_norm = pc._encode_query_blocks(st, q_avg)
+    with open(os.path.join(ref_root, RUNTIME, "turboquant/codebooks/codebook_d128_m8_Kr1_Kw256_rabitq_sign.json")) as f:
+        signs_cb = torch.tensor(json.load(f)["angular_signs"], dtype=torch.int8)
+    V_T = torch.where(signs_cb >= 0, 1, -1).to(torch.bfloat16).T.contiguous()       # [8, 256]
+    scores = torch.matmul(q_blocks, V_T)                                             # [bs,H,16,256] bf16
+    sorted_ids = scores.argsort(dim=-1, descending=True, stable=True)                # ties -> lower id
+    sys.path.insert(0, os.path.join(ref_root, RUNTIME, "cache_hub/collision_fused"))
+    import collision_test as ct  # noqa: E402  (imports only torch / triton at module level)
+    coll = 0.25
+    tiers = [0.05, 0.15, 0.30, 0.50, 0.75, 1.0]
+    targets = [int(np.ceil(N * coll * r)) for r in tiers]
+    cnt = ct.update_cache_cnt_overall_ref(sorted_ids, hist, codebook.to(torch.int32), tiers, N, coll)
+    np.savez_compressed(
+        os.path.join(out, "rabitq_encode.npz"), keys=bf16_bits(keys), signs=bf16_bits(signs),
+        codes=codebook.permute(0, 1, 3, 2).contiguous().numpy(), weight=bf16_bits(weight.permute(0, 1, 3, 2)),
+        packed=packed.permute(0, 1, 3, 2, 4).contiguous().numpy(), hist=hist.numpy(), q=bf16_bits(q),
+        q_mean=bf16_bits(q_avg), q_blocks=bf16_bits(q_blocks), q_norm=bf16_bits(q_norm),
+        bucket_scores=bf16_bits(scores), sorted_ids=sorted_ids.numpy().astype(np.int16),
+        targets=np.array(targets, np.int64), cnt=cnt.numpy())
+    # the collision reference's own generator (random orders / counts), seed 42
+    sid, ckc, cb, tr, kv_len, cr = ct.generate_test_input(bs=1, kv_heads=8, B=16, num_clusters=256, kv_len=1024,
+                                                          collision_ratio=0.2)
+    cnt2 = ct.update_cache_cnt_overall_ref(sid, ckc, cb, tr, kv_len, cr)
+    np.savez_compressed(
+        os.path.join(out, "collision_ref.npz"), sorted_ids=sid.numpy().astype(np.int16), hist=ckc.numpy(),
+        codes=cb.numpy().astype(np.uint8), targets=np.array([int(np.ceil(kv_len * r * cr)) for r in tr], np.int64),
+        cnt=cnt2.numpy())
+
+
+def gen_rerank4(ref_root, out):
+    """Sequential-bf16 RaBitQ rerank scores from the reference's own test."""
+    sys.path.insert(0, os.path.join(ref_root, RUNTIME, "cache_hub/rerank"))
+    import test_rerank_topk as tr  # noqa: E402
+    cases = {}
+    for i, (seed, kv_len, cand) in enumerate([(42, 256, 64), (77, 1024, 256), (999, 512, 512)]):
+        ci, k4, kw, qb, qn, mc = tr.make_inputs(1, 2, 16, 8, kv_len, cand, "cpu", seed=seed)
+        sc = tr.python_rabitq_scores(ci, k4, kw, qb, qn, mc, 16, 8)
+        cases.update({f"c{i}_cand": ci.numpy(), f"c{i}_packed": k4.permute(0, 1, 3, 2, 4).contiguous().numpy(),
+                      f"c{i}_weight": bf16_bits(kw.permute(0, 1, 3, 2)), f"c{i}_q_blocks": bf16_bits(qb),
+                      f"c{i}_q_norm": bf16_bits(qn), f"c{i}_scores": bf16_bits(sc)})
+    cases["centers"] = bf16_bits(mc)
+    np.savez_compressed(os.path.join(out, "rerank4.npz"), **cases)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -329,6 +409,9 @@ def main():
     gen_lse(a.out)
     gen_host_logic(zmod, a.out)
     gen_schedule(zmod, a.out)
+    import cache_hub.polar_cache as pmod
+    gen_rabitq(pmod, a.ref, a.out)
+    gen_rerank4(a.ref, a.out)
     print("golden fixtures written to", a.out)
 
 
