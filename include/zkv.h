@@ -200,6 +200,92 @@ int zkv_lse_merge(const void* a, const float* la, const void* b,
 int zkv_lse_merge_n(const float* parts, const float* lses, int n, int rows,
                     int dim, void* out, float* lse_out, void* stream);
 
+/* ------------------------------------------------- ParisKV / RaBitQ path */
+/* Per-key retrieval codes of ParisKV (cache_hub/polar_cache.py), D = 128
+ * split into 16 blocks of 8 dims.  Every tensor is addressed as
+ * base + row*X_row + block*X_blk + token*X_tok (units in the comments), so
+ * both this build's token-major layout (blk 1, tok 16) and the reference's
+ * block-major layout (blk cap, tok 1) can be passed.
+ *   codes   1-bit sign codes, one byte per block (bit j = dim 8b+j >= 0)
+ *   packed  4-bit codes, one 4-byte word per block, byte i = v_{2i+1}<<4 | v_{2i},
+ *           v = sign<<3 | magnitude  (units: 4-byte words)
+ *   weight  bf16 per block (r_b / alpha_b) * |k|
+ *   factor  fp32 per key |k| / <xbar, o'> for the popcount estimator (may be NULL)
+ *   hist    [rows][16][256] int32 bucket sizes (cluster_key_counts; may be NULL) */
+typedef struct zkv_rq_layout {
+    uint8_t* codes;
+    int64_t codes_row, codes_blk, codes_tok;
+    uint32_t* packed;
+    int64_t packed_row, packed_blk, packed_tok;
+    void* weight;
+    int64_t weight_row, weight_blk, weight_tok;
+    float* factor;
+    int64_t factor_row;
+    int32_t* hist;
+} zkv_rq_layout;
+
+/* Encode keys [tok_start, tok_start+n_tok) of every row (raw bf16 rows at
+ * keys + r*keys_ld_row + t*128) into `lay`, adding them to lay->hist.
+ * signs [128] bf16 (+-1, the SRHT diagonal).  Replaces batch_encode +
+ * _count_cluster_keys (cache_hub/polar_cache.py:1130-1198, :1203-1226).  */
+int zkv_rq_encode(const void* keys, int64_t keys_ld_row, int rows, int n_tok,
+                  int tok_start, const void* signs, const zkv_rq_layout* lay,
+                  void* stream);
+
+/* Query side: GQA mean of q [rows][G][128] bf16, then normalise + SRHT:
+ * q_blocks [rows][128] bf16, q_norm [rows] bf16, q_mean [rows][128] bf16
+ * (may be NULL).  Replaces _encode_query_blocks (polar_cache.py:1108-1127).
+ * When planes != NULL also the 4-bit query of the popcount estimator:
+ * planes [rows][4][16] u8, qparams [rows][4] fp32 {lo, delta, sum, |q|}. */
+int zkv_rq_query(const void* q, int rows, int G, const void* signs,
+                 void* q_blocks, void* q_norm, void* q_mean, uint8_t* planes,
+                 float* qparams, void* stream);
+
+/* Fused collision count + coarse top-C (get_cache_cnt_fused +
+ * _coarse_filter_truncate, polar_cache.py:1688-1747; collision.cu:72-245;
+ * radix_topk.cu:157-240).  Per (row, block) the 256 buckets are ordered by
+ * bf16 score q_b . V[c] (descending, ties to the lower bucket), a key's
+ * count is the number of tiers t whose prefix (before[rank] < targets[t])
+ * holds its bucket, summed over the 16 blocks.  idx_out [rows][C] receives
+ * the C keys of highest count (ties to the lower index) in ascending index
+ * order; cnt_out [rows][kv_len] int32 (may be NULL) the counts.  With
+ * idx_out NULL only the counts are produced (update_cache_cnt).
+ * 1 <= C <= kv_len; n_tiers <= 8; reads lay->codes and lay->hist.        */
+int zkv_collision_topk(const void* q_blocks, const zkv_rq_layout* lay,
+                       int rows, int kv_len, const int64_t* targets,
+                       int n_tiers, int C, int64_t* idx_out, int32_t* cnt_out,
+                       void* stream);
+
+/* 4-bit RaBitQ rerank of candidate keys cand [rows][C] (rerank.cu:52-143,
+ * sequential bf16 as python_rabitq_scores) -> scores [rows][C] bf16 (may be
+ * NULL) and, when F > 0, the F best candidates' key ids (ties to the lower
+ * candidate position, ascending position order) in final [rows][F]
+ * (polar_cache.py:1750-1832 topk + gather).  centers [8] bf16.           */
+int zkv_rq_rerank4(const int64_t* cand, int C, const zkv_rq_layout* lay,
+                   const void* q_blocks, const void* q_norm,
+                   const void* centers, int rows, void* scores, int F,
+                   int64_t* final_out, void* stream);
+
+/* 2-bit-plane popcount coarse score (coarse_2bit_score.cu:86-156):
+ * out [rows][kv_len] int32 from lay->packed and the query's sign /
+ * magnitude-high bit planes q_signs, q_mags [rows][16] u8.               */
+int zkv_coarse2bit(const zkv_rq_layout* lay, const uint8_t* q_signs,
+                   const uint8_t* q_mags, int rows, int kv_len, int32_t* out,
+                   void* stream);
+
+/* 1-bit x 4-bit popcount estimator rerank (RaBitQ; no reference kernel):
+ * estimates <k, q> for cand [rows][C] (NULL = keys 0..C-1) from lay->codes
+ * and lay->factor with the 4-bit query (planes, qparams), keeps the K best
+ * (ties to the lower position) in sel_out [rows][K] (key ids, ascending),
+ * est_out [rows][C] fp32 (may be NULL); when keys != NULL also the exact
+ * fp32 inner products of the selected raw bf16 keys with q_mean
+ * [rows][128] in ip_out [rows][K].                                        */
+int zkv_rq_popcount_topk(const int64_t* cand, int C, const zkv_rq_layout* lay,
+                         const uint8_t* planes, const float* qparams,
+                         int rows, int K, int64_t* sel_out, float* est_out,
+                         const void* keys, int64_t keys_ld_row,
+                         const void* q_mean, float* ip_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -31,6 +31,18 @@ class ZkvPageLayer(ctypes.Structure):
     ]
 
 
+class ZkvRqLayout(ctypes.Structure):
+    """Mirror of `zkv_rq_layout` (include/zkv.h)."""
+    _fields_ = [
+        ("codes", _c_void_p), ("codes_row", _i64), ("codes_blk", _i64), ("codes_tok", _i64),
+        ("packed", _c_void_p), ("packed_row", _i64), ("packed_blk", _i64), ("packed_tok", _i64),
+        ("weight", _c_void_p), ("weight_row", _i64), ("weight_blk", _i64), ("weight_tok", _i64),
+        ("factor", _c_void_p), ("factor_row", _i64), ("hist", _c_void_p),
+    ]
+
+
+_RQ = ctypes.POINTER(ZkvRqLayout)
+
 # name -> argtypes (restype is int status unless noted)
 _SIGNATURES = {
     "zkv_kivi_encode": [_c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
@@ -50,6 +62,14 @@ _SIGNATURES = {
                         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p],
     "zkv_lse_merge": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p],
     "zkv_lse_merge_n": [_c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p],
+    "zkv_rq_encode": [_c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _RQ, _c_void_p],
+    "zkv_rq_query": [_c_void_p, _i32, _i32] + [_c_void_p] * 7,
+    "zkv_collision_topk": [_c_void_p, _RQ, _i32, _i32, _c_void_p, _i32, _i32, _c_void_p, _c_void_p, _c_void_p],
+    "zkv_rq_rerank4": [_c_void_p, _i32, _RQ, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p, _i32, _c_void_p,
+                       _c_void_p],
+    "zkv_coarse2bit": [_RQ, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _c_void_p],
+    "zkv_rq_popcount_topk": [_c_void_p, _i32, _RQ, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _c_void_p, _c_void_p,
+                             _i64, _c_void_p, _c_void_p, _c_void_p],
     "zkv_version": [],
     "zkv_status_string": [_i32],
 }

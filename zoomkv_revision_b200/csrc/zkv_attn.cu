@@ -664,47 +664,6 @@ static int pick_cluster(int requested, int rows) {
     return 8;
 }
 
-static int launch_clustered(const void* fn, int rows, int CS, size_t smem, cudaStream_t stream, void** args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(rows * CS), 1, 1);
-    cfg.blockDim = dim3(kAttnThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)CS;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    // raise the dynamic shared-memory limit once per (kernel, device, size)
-    static thread_local const void* last_fn[4] = {nullptr, nullptr, nullptr, nullptr};
-    static thread_local size_t last_smem[4] = {0, 0, 0, 0};
-    static thread_local int last_dev[4] = {-1, -1, -1, -1};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int slot = -1;
-    for (int i = 0; i < 4; ++i)
-        if (last_fn[i] == fn && last_dev[i] == dev) slot = i;
-    if (slot < 0 || last_smem[slot] < smem) {
-        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return ZKV_ERR_LAUNCH;
-        if (slot < 0) {
-            for (int i = 0; i < 4; ++i)
-                if (!last_fn[i]) {
-                    slot = i;
-                    break;
-                }
-            if (slot < 0) slot = 0;
-        }
-        last_fn[slot] = fn;
-        last_dev[slot] = dev;
-        last_smem[slot] = smem;
-    }
-    if (cudaLaunchKernelExC(&cfg, fn, args) != cudaSuccess) return ZKV_ERR_LAUNCH;
-    return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH;
-}
-
 extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max, int n_c,
                                int nk, int n_sink, int near_start, int n_near, float scale, void* out, float* lse,
                                int64_t* sel_out, int32_t* status, int cluster, void* stream) {
@@ -747,7 +706,7 @@ extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int r
                         (16 + 8 * kHeadDim) * 4 + (512 + 8 + 2 * kAttnThreads) * 4 +
                         (4 * kAttnWarps) * 8 + 16;
     void* args[] = {&a};
-    return launch_clustered((const void*)page_decode_kernel, rows, CS, smem, (cudaStream_t)stream, args);
+    return launch_clustered((const void*)page_decode_kernel, rows * CS, kAttnThreads, CS, smem, (cudaStream_t)stream, args);
 }
 
 extern "C" int zkv_attn_rows(const void* q, const void* keys, const void* values, int64_t kv_ld_row, int rows, int G,
@@ -784,7 +743,7 @@ extern "C" int zkv_attn_rows(const void* q, const void* keys, const void* values
     a.status = status;
     const size_t smem = kRegionBytes + 8 * kHeadDim * 2 + (16 + 8 * kHeadDim) * 4 + 2 * kAttnWarps * 8 + 16;
     void* args[] = {&a};
-    return launch_clustered((const void*)attn_rows_kernel, rows, CS, smem, (cudaStream_t)stream, args);
+    return launch_clustered((const void*)attn_rows_kernel, rows * CS, kAttnThreads, CS, smem, (cudaStream_t)stream, args);
 }
 
 extern "C" int zkv_lse_merge(const void* a, const float* la, const void* b, const float* lb, void* out,

@@ -655,3 +655,49 @@ __device__ __forceinline__ float quest_half(uint4 qv, uint4 mnv, uint4 mxv) {
 }
 
 }  // namespace zkv
+
+static inline int launch_status() { return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH; }
+
+// Launch `nblocks` CTAs of `nthreads` in clusters of CS (cudaLaunchKernelExC),
+// raising the kernel's dynamic shared-memory limit once per (kernel, device).
+static int launch_clustered(const void* fn, int nblocks, int nthreads, int CS, size_t smem, cudaStream_t stream,
+                            void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)nblocks, 1, 1);
+    cfg.blockDim = dim3((unsigned)nthreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)CS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // raise the dynamic shared-memory limit once per (kernel, device, size)
+    static thread_local const void* last_fn[4] = {nullptr, nullptr, nullptr, nullptr};
+    static thread_local size_t last_smem[4] = {0, 0, 0, 0};
+    static thread_local int last_dev[4] = {-1, -1, -1, -1};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int slot = -1;
+    for (int i = 0; i < 4; ++i)
+        if (last_fn[i] == fn && last_dev[i] == dev) slot = i;
+    if (slot < 0 || last_smem[slot] < smem) {
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return ZKV_ERR_LAUNCH;
+        if (slot < 0) {
+            for (int i = 0; i < 4; ++i)
+                if (!last_fn[i]) {
+                    slot = i;
+                    break;
+                }
+            if (slot < 0) slot = 0;
+        }
+        last_fn[slot] = fn;
+        last_dev[slot] = dev;
+        last_smem[slot] = smem;
+    }
+    if (cudaLaunchKernelExC(&cfg, fn, args) != cudaSuccess) return ZKV_ERR_LAUNCH;
+    return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH;
+}

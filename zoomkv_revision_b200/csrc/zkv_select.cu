@@ -226,7 +226,6 @@ __global__ void __launch_bounds__(kTopkThreads) topk_gather_concat_kernel(const 
 
 using namespace zkv;
 
-static inline int launch_status() { return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH; }
 
 extern "C" int zkv_quest_score(const void* raw_q, const void* chunk_min, const void* chunk_max, const uint8_t* valid,
                                float* scores, int rows, int n_chunks, int n_max, void* stream) {

@@ -19,6 +19,14 @@ kivi_encode_chunks                     polar_cache._compute_and_store_chunk_minm
 attn_rows                              h2d_gather_kv + torch.cat + flash_attn_with_kvcache
 page_decode                            (fused page-mode decode; no single counterpart)
 vquant_encode                          (per-token 4-bit values; no counterpart)
+RqLayout / rq_encode / batch_encode    cache_hub/polar_cache.py batch_encode (:1130-1198)
+                                       + _count_cluster_keys (:1203-1226)
+rq_query                               cache_hub/polar_cache.py _encode_query_blocks (:1108-1127)
+get_cache_cnt_fused                    cache_hub/polar_cache.py:1688-1728 (collision.cu)
+collision_topk                         get_cache_cnt_fused + _coarse_filter_truncate (:1730-1747)
+partial_rerank_cuda                    cache_hub/rerank/rerank.py:352-400 (+ topk/gather :1750-1832)
+coarse_2bit_score_cuda                 cache_hub/rerank/rerank.py:636-690
+rq_popcount_topk                       (1-bit x 4-bit popcount rerank + exact IP; no counterpart)
 =====================================  ==============================================
 
 Errors follow the reference: wrong dtype -> TypeError, wrong shape / range ->
@@ -38,7 +46,8 @@ __all__ = [
     "quest_chunk_score", "float_topk", "float_topk_3d", "radix_topk_3d", "partial_chunk_density_scores_cuda",
     "dense_mask_from_topk_cuda", "partial_chunk_kivi_qk_dense_sparse_cuda", "float_topk_gather_concat_3d",
     "lse_merge_cuda", "lse_merge_n", "kivi_encode_chunks", "vquant_encode", "attn_rows", "page_decode",
-    "PageLayer",
+    "PageLayer", "RqLayout", "rq_encode", "batch_encode", "rq_query", "get_cache_cnt_fused", "collision_topk",
+    "partial_rerank_cuda", "coarse_2bit_score_cuda", "rq_popcount_topk", "MAG_CENTERS", "MAG_THRESHOLDS",
 ]
 
 
@@ -361,3 +370,217 @@ def page_decode(q, layer: PageLayer, n_c: int, nk: int, n_near: int, *, n_sink: 
                                 int(near_start), int(n_near), scale, _p(out), _p(lse), _p(sel_out), _p(status),
                                 int(cluster), _stream(q)), "zkv_page_decode")
     return out
+
+
+# ----------------------------------------------------------------- ParisKV / RaBitQ
+# Magnitude thresholds / reconstruction centres (cache_hub/polar_cache.py:267-270)
+MAG_THRESHOLDS = (0.0843, 0.1698, 0.2578, 0.3499, 0.4487, 0.5585, 0.6901)
+MAG_CENTERS = (0.0420, 0.1266, 0.2130, 0.3025, 0.3973, 0.5001, 0.6169, 0.7633)
+
+
+def _row_stride(name, t, lead=2):
+    """Stride that flattens the leading `lead` dims of t into rows."""
+    if lead == 2 and t.dim() >= 2 and t.shape[0] > 1 and t.stride(0) != t.shape[1] * t.stride(1):
+        raise ValueError(f"{name}: batch and head dims must flatten into rows")
+    return t.stride(lead - 1)
+
+
+class RqLayout:
+    """Per-key ParisKV codes of one layer (device tensors) + the C struct.
+
+    Token-major (this build, `alloc`): codes [rows, cap, 16] u8, packed
+    [rows, cap, 16] int32 (one word = one block's 8 nibbles), weight
+    [rows, cap, 16] bf16, factor [rows, cap] f32, hist [rows, 16, 256] i32.
+    Block-major (the reference's tensors, `from_reference`): codebook
+    [bs, H, 16, len] u8, key_4bit [bs, H, 16, len, 4] u8, key_block_weight
+    [bs, H, 16, len] bf16 (views sliced along len are accepted)."""
+
+    def __init__(self, codes, packed, weight, factor, hist, strides):
+        self.codes, self.packed, self.weight, self.factor, self.hist = codes, packed, weight, factor, hist
+        (cr, cb, ct), (pr, pb, pt), (wr, wb, wt), fr = strides
+        self._s = _lib.ZkvRqLayout(
+            _p(codes), cr, cb, ct, _p(packed), pr, pb, pt, _p(weight), wr, wb, wt, _p(factor), fr, _p(hist))
+
+    @classmethod
+    def alloc(cls, rows: int, cap: int, device) -> "RqLayout":
+        z = dict(device=device)
+        codes = torch.zeros(rows, cap, 16, dtype=torch.uint8, **z)
+        packed = torch.zeros(rows, cap, 16, dtype=torch.int32, **z)
+        weight = torch.zeros(rows, cap, 16, dtype=torch.bfloat16, **z)
+        factor = torch.zeros(rows, cap, dtype=torch.float32, **z)
+        hist = torch.zeros(rows, 16, 256, dtype=torch.int32, **z)
+        return cls(codes, packed, weight, factor, hist,
+                   ((cap * 16, 1, 16), (cap * 16, 1, 16), (cap * 16, 1, 16), cap))
+
+    @classmethod
+    def from_reference(cls, codebook, key_4bit=None, key_block_weight=None, cluster_key_counts=None) -> "RqLayout":
+        _cuda(("codebook", codebook), ("key_4bit", key_4bit), ("key_block_weight", key_block_weight),
+              ("cluster_key_counts", cluster_key_counts))
+        _dtype("codebook", codebook, torch.uint8)
+        cs = (_row_stride("codebook", codebook), codebook.stride(2), codebook.stride(3))
+        ps = ws = (0, 0, 0)
+        if key_4bit is not None:
+            _dtype("key_4bit", key_4bit, torch.uint8)
+            if key_4bit.shape[-1] != 4 or key_4bit.stride(-1) != 1 or key_4bit.data_ptr() % 4:
+                raise ValueError("key_4bit must be [bs, H, 16, len, 4] with 4-byte aligned contiguous blocks")
+            ps = tuple(x // 4 for x in (_row_stride("key_4bit", key_4bit), key_4bit.stride(2), key_4bit.stride(3)))
+        if key_block_weight is not None:
+            _dtype("key_block_weight", key_block_weight, torch.bfloat16)
+            ws = (_row_stride("key_block_weight", key_block_weight), key_block_weight.stride(2),
+                  key_block_weight.stride(3))
+        hist = None
+        if cluster_key_counts is not None:
+            _dtype("cluster_key_counts", cluster_key_counts, torch.int32)
+            _contig("cluster_key_counts", cluster_key_counts)
+            hist = cluster_key_counts
+        return cls(codebook, key_4bit, key_block_weight, None, hist, (cs, ps, ws, 0))
+
+    @property
+    def struct(self):
+        return ctypes.byref(self._s)
+
+
+def rq_encode(keys, signs, lay: RqLayout, tok_start: int = 0):
+    """Encode keys [rows, T, 128] (or [bs, H, T, 128]) bf16 into `lay` at
+    tokens [tok_start, tok_start + T) and add them to lay.hist."""
+    _cuda(("keys", keys), ("signs", signs))
+    _dtype("keys", keys, torch.bfloat16)
+    _dtype("signs", signs, torch.bfloat16)
+    if keys.stride(-1) != 1 or keys.shape[-1] != 128:
+        raise ValueError("keys must be [..., T, 128] with a contiguous last dim")
+    if keys.dim() == 4:
+        ld, rows, T = _row_stride("keys", keys), keys.shape[0] * keys.shape[1], keys.shape[2]
+        if keys.stride(2) != 128:
+            raise ValueError("keys tokens must be contiguous rows of 128")
+    else:
+        ld, rows, T = keys.stride(0), keys.shape[0], keys.shape[1]
+    check(lib().zkv_rq_encode(_p(keys), ld, rows, T, tok_start, _p(signs.contiguous()), lay.struct, _stream(keys)),
+          "zkv_rq_encode")
+
+
+def batch_encode(Y, signs):
+    """Reference-layout form of ParisKV batch_encode: Y [bs, H, len, 128] bf16
+    -> (codebook [bs,H,16,len] u8, block_weight [bs,H,16,len] bf16,
+    packed_4bit [bs,H,16,len,4] u8, cluster_key_counts [bs,H,16,256] i32)."""
+    bs, H, T, _ = Y.shape
+    z = dict(device=Y.device)
+    codebook = torch.empty(bs, H, 16, T, dtype=torch.uint8, **z)
+    weight = torch.empty(bs, H, 16, T, dtype=torch.bfloat16, **z)
+    packed = torch.empty(bs, H, 16, T, 4, dtype=torch.uint8, **z)
+    counts = torch.zeros(bs, H, 16, 256, dtype=torch.int32, **z)
+    lay = RqLayout.from_reference(codebook, packed, weight, counts)
+    rq_encode(Y, signs, lay)
+    return codebook, weight, packed, counts
+
+
+def rq_query(q, signs, group: int = 4, *, planes: bool = False):
+    """q [bs, 1, H*G, 128] or [rows, G, 128] bf16 -> dict(q_blocks [rows,128],
+    q_norm [rows], q_mean [rows,128] bf16; planes [rows,4,16] u8 and qparams
+    [rows,4] f32 when planes=True)."""
+    _cuda(("q", q), ("signs", signs))
+    _dtype("q", q, torch.bfloat16)
+    q = q.contiguous()
+    rows = q.numel() // (group * 128)
+    dev = q.device
+    out = dict(q_blocks=torch.empty(rows, 128, dtype=torch.bfloat16, device=dev),
+               q_norm=torch.empty(rows, dtype=torch.bfloat16, device=dev),
+               q_mean=torch.empty(rows, 128, dtype=torch.bfloat16, device=dev))
+    pl = qp = None
+    if planes:
+        pl = out["planes"] = torch.empty(rows, 4, 16, dtype=torch.uint8, device=dev)
+        qp = out["qparams"] = torch.empty(rows, 4, dtype=torch.float32, device=dev)
+    check(lib().zkv_rq_query(_p(q), rows, group, _p(signs.contiguous()), _p(out["q_blocks"]), _p(out["q_norm"]),
+                             _p(out["q_mean"]), _p(pl), _p(qp), _stream(q)), "zkv_rq_query")
+    return out
+
+
+_TIER_RATIOS = (0.05, 0.15, 0.30, 0.50, 0.75, 1.0)
+
+
+def tier_targets(kv_len: int, collision_ratio: float, tier_ratios=_TIER_RATIOS):
+    """ceil(kv_len * collision_ratio * r) per tier (polar_cache.py:1711-1712)."""
+    import math
+    return [int(math.ceil(kv_len * collision_ratio * r)) for r in tier_ratios]
+
+
+def _targets_tensor(targets):
+    t = torch.tensor(list(targets), dtype=torch.int64)
+    return t, t.numel()
+
+
+def get_cache_cnt_fused(q_blocks, lay: RqLayout, kv_len: int, targets, out=None):
+    """cache_cnt [rows, kv_len] int32 (update_cache_cnt with the bucket order
+    computed from q_blocks)."""
+    rows = q_blocks.numel() // 128
+    if out is None:
+        out = torch.empty(rows, kv_len, dtype=torch.int32, device=q_blocks.device)
+    t, nt = _targets_tensor(targets)
+    check(lib().zkv_collision_topk(_p(q_blocks.contiguous()), lay.struct, rows, kv_len, t.data_ptr(), nt, 0, None,
+                                   _p(out), _stream(q_blocks)), "zkv_collision_topk")
+    return out
+
+
+def collision_topk(q_blocks, lay: RqLayout, kv_len: int, targets, C: int, idx_out=None, cnt_out=None):
+    """Top-C keys by collision count (ties to the lower index), ascending
+    index order: [rows, C] int64."""
+    rows = q_blocks.numel() // 128
+    if idx_out is None:
+        idx_out = torch.empty(rows, C, dtype=torch.int64, device=q_blocks.device)
+    t, nt = _targets_tensor(targets)
+    check(lib().zkv_collision_topk(_p(q_blocks.contiguous()), lay.struct, rows, kv_len, t.data_ptr(), nt, C,
+                                   _p(idx_out), _p(cnt_out), _stream(q_blocks)), "zkv_collision_topk")
+    return idx_out
+
+
+def partial_rerank_cuda(coarse_indices, lay: RqLayout, q_blocks, q_norm, mag_centers=None, final_topk: int = 0,
+                        scores_out=None, final_out=None):
+    """4-bit RaBitQ scores [rows, C] bf16 of coarse_indices [rows, C] (the
+    reference's partial_rerank_cuda); with final_topk > 0 also the top-F key
+    ids [rows, F] (ties to the lower candidate position, ascending order)."""
+    _cuda(("coarse_indices", coarse_indices), ("q_blocks", q_blocks), ("q_norm", q_norm))
+    _dtype("coarse_indices", coarse_indices, torch.int64)
+    ci = coarse_indices.contiguous()
+    C = ci.shape[-1]
+    rows = ci.numel() // C
+    dev = ci.device
+    if mag_centers is None:
+        mag_centers = torch.tensor(MAG_CENTERS, dtype=torch.bfloat16, device=dev)
+    if scores_out is None:
+        scores_out = torch.empty(rows, C, dtype=torch.bfloat16, device=dev)
+    if final_topk > 0 and final_out is None:
+        final_out = torch.empty(rows, final_topk, dtype=torch.int64, device=dev)
+    check(lib().zkv_rq_rerank4(_p(ci), C, lay.struct, _p(q_blocks.contiguous()), _p(q_norm.contiguous()),
+                               _p(mag_centers.contiguous()), rows, _p(scores_out), final_topk,
+                               _p(final_out) if final_topk > 0 else None, _stream(ci)), "zkv_rq_rerank4")
+    return (scores_out, final_out) if final_topk > 0 else scores_out
+
+
+def coarse_2bit_score_cuda(lay: RqLayout, q_signs, q_mags, kv_len: int, out=None):
+    """int32 [rows, kv_len] 2-bit-plane popcount scores (coarse_2bit_score.cu)."""
+    rows = q_signs.numel() // 16
+    if out is None:
+        out = torch.empty(rows, kv_len, dtype=torch.int32, device=q_signs.device)
+    check(lib().zkv_coarse2bit(lay.struct, _p(q_signs.contiguous()), _p(q_mags.contiguous()), rows, kv_len, _p(out),
+                               _stream(q_signs)), "zkv_coarse2bit")
+    return out
+
+
+def rq_popcount_topk(cand, lay: RqLayout, planes, qparams, K: int, *, C: int | None = None, keys=None,
+                     q_mean=None, est_out=None):
+    """Popcount-estimate rerank: keep the K best of cand [rows, C] (None = keys
+    0..C-1), return (sel [rows, K] int64 ascending, est [rows, C] f32 or None,
+    ip [rows, K] f32 exact <k, q_mean> or None)."""
+    rows = planes.shape[0]
+    dev = planes.device
+    if cand is not None:
+        cand = cand.contiguous()
+        C = cand.shape[-1]
+    sel = torch.empty(rows, K, dtype=torch.int64, device=dev)
+    ip = None
+    ld = 0
+    if keys is not None:
+        ip = torch.empty(rows, K, dtype=torch.float32, device=dev)
+        ld = keys.stride(0) if keys.dim() == 3 else _row_stride("keys", keys)
+    check(lib().zkv_rq_popcount_topk(_p(cand), C, lay.struct, _p(planes), _p(qparams), rows, K, _p(sel), _p(est_out),
+                                     _p(keys), ld, _p(q_mean), _p(ip), _stream(planes)), "zkv_rq_popcount_topk")
+    return sel, est_out, ip
