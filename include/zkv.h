@@ -20,6 +20,7 @@
 #ifndef ZKV_H
 #define ZKV_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -132,6 +133,43 @@ int zkv_topk_gather_concat(const float* scores, const int64_t* lut,
                            const int64_t* skipped, int64_t sk_ld, int64_t* out,
                            int rows, int L, int k, int sk, int64_t out_ld,
                            void* stream);
+
+/* ------------------------------------------------- reference-mode chain */
+
+/* Chunk index of one layer for the reference-mode chain; every tensor is
+ * [rows][n_max][...]: chunk_min/max/centroid [..][128] bf16, valid u8 (or
+ * NULL), packed [..][16][16] int32 (chunk-major KIVI keys).              */
+typedef struct zkv_ref_layer {
+    const void* chunk_min;
+    const void* chunk_max;
+    const void* centroid;
+    const uint8_t* valid;
+    const int32_t* packed;
+} zkv_ref_layer;
+
+/* Bytes of workspace zkv_reference_select needs (0 on bad arguments).    */
+size_t zkv_reference_select_ws_bytes(int rows, int n_chunks, int nk,
+                                     int n_dense);
+
+/* The retrieval chain of polar_cache.compute for one layer as one call on
+ * one stream (cache_hub/polar_cache_quest_density_single_layer_kivi.py:
+ * 1589-1775 minus the attention): raw_q = GQA mean of q [rows][G][128]
+ * bf16; Quest scores of chunks [0, n_chunks); top-nk chunks; CDS density
+ * and top-n_dense dense mask; KIVI stage 2 over packed chunks
+ * [0, n_valid_chunks); global top-k token ids + skipped tail into
+ * final_out [rows][final_ld] (same results as the single-op entry points
+ * above, called in that order).  Intermediates live in `workspace`
+ * (256-byte aligned, >= zkv_reference_select_ws_bytes bytes; every byte
+ * read is written first by the same call).  raw_q_out [rows][128] bf16 may
+ * be NULL.  dense_topk, sparse_topk in [1, 16].                           */
+int zkv_reference_select(const void* q, int G, const zkv_ref_layer* layer,
+                         int rows, int n_max, int n_chunks,
+                         int n_valid_chunks, int nk, int n_dense,
+                         int dense_topk, int sparse_topk, int k,
+                         const int64_t* skipped, int64_t sk_ld, int sk,
+                         int64_t* final_out, int64_t final_ld,
+                         void* raw_q_out, void* workspace, size_t ws_bytes,
+                         void* stream);
 
 /* ------------------------------------------------------------ attention */
 

@@ -21,6 +21,13 @@ def declared():
     return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\**(zkv_\w+)\s*\(", src, flags=re.M)))
 
 
+def test_reference_select_ws_bytes():
+    lib = _lib.lib()
+    n = lib.zkv_reference_select_ws_bytes(64, 2040, 816, 244)
+    assert n % 256 == 0 and n >= 64 * (128 * 2 + 2040 * 4 + 816 * (8 + 4 + 1 + 16 * 12) + 244 * 8)
+    assert lib.zkv_reference_select_ws_bytes(-1, 1, 1, 1) == 0
+
+
 def test_every_declared_symbol_is_exported_and_bound():
     names = declared()
     assert len(names) >= 20
@@ -35,7 +42,8 @@ def test_every_declared_symbol_is_exported_and_bound():
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
 def test_struct_layouts_match_c(tmp_path):
-    structs = {"zkv_page_layer": _lib.ZkvPageLayer, "zkv_rq_layout": _lib.ZkvRqLayout}
+    structs = {"zkv_page_layer": _lib.ZkvPageLayer, "zkv_rq_layout": _lib.ZkvRqLayout,
+               "zkv_ref_layer": _lib.ZkvRefLayer}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void){"]
     for cname, cls in structs.items():
         lines.append(f'printf("%zu\\n", sizeof({cname}));')

@@ -41,6 +41,12 @@ class ZkvRqLayout(ctypes.Structure):
     ]
 
 
+class ZkvRefLayer(ctypes.Structure):
+    """Mirror of `zkv_ref_layer` (include/zkv.h)."""
+    _fields_ = [("chunk_min", _c_void_p), ("chunk_max", _c_void_p), ("centroid", _c_void_p), ("valid", _c_void_p),
+                ("packed", _c_void_p)]
+
+
 _RQ = ctypes.POINTER(ZkvRqLayout)
 
 # name -> argtypes (restype is int status unless noted)
@@ -70,9 +76,14 @@ _SIGNATURES = {
     "zkv_coarse2bit": [_RQ, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _c_void_p],
     "zkv_rq_popcount_topk": [_c_void_p, _i32, _RQ, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _c_void_p, _c_void_p,
                              _i64, _c_void_p, _c_void_p, _c_void_p],
+    "zkv_reference_select_ws_bytes": [_i32, _i32, _i32, _i32],
+    "zkv_reference_select": [_c_void_p, _i32, ctypes.POINTER(ZkvRefLayer)] + [_i32] * 9 +
+                            [_c_void_p, _i64, _i32, _c_void_p, _i64, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
     "zkv_version": [],
     "zkv_status_string": [_i32],
 }
+
+_RESTYPES = {"zkv_status_string": ctypes.c_char_p, "zkv_reference_select_ws_bytes": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib = None
@@ -97,7 +108,7 @@ def lib() -> ctypes.CDLL:
             for name, argt in _SIGNATURES.items():
                 fn = getattr(h, name)
                 fn.argtypes = argt
-                fn.restype = ctypes.c_char_p if name == "zkv_status_string" else ctypes.c_int
+                fn.restype = _RESTYPES.get(name, ctypes.c_int)
             _lib = h
     return _lib
 

@@ -18,6 +18,7 @@ kivi_encode_chunks                     polar_cache._compute_and_store_chunk_minm
                                        _kivi_pack_chunks (aligned chunks)
 attn_rows                              h2d_gather_kv + torch.cat + flash_attn_with_kvcache
 page_decode                            (fused page-mode decode; no single counterpart)
+reference_select                       polar_cache.compute retrieval chain (REF:1589-1775) as one call
 vquant_encode                          (per-token 4-bit values; no counterpart)
 RqLayout / rq_encode / batch_encode    cache_hub/polar_cache.py batch_encode (:1130-1198)
                                        + _count_cluster_keys (:1203-1226)
@@ -46,7 +47,7 @@ __all__ = [
     "quest_chunk_score", "float_topk", "float_topk_3d", "radix_topk_3d", "partial_chunk_density_scores_cuda",
     "dense_mask_from_topk_cuda", "partial_chunk_kivi_qk_dense_sparse_cuda", "float_topk_gather_concat_3d",
     "lse_merge_cuda", "lse_merge_n", "kivi_encode_chunks", "vquant_encode", "attn_rows", "page_decode",
-    "PageLayer", "RqLayout", "rq_encode", "batch_encode", "rq_query", "get_cache_cnt_fused", "collision_topk",
+    "PageLayer", "reference_select", "reference_select_ws_bytes", "RqLayout", "rq_encode", "batch_encode", "rq_query", "get_cache_cnt_fused", "collision_topk",
     "partial_rerank_cuda", "coarse_2bit_score_cuda", "rq_popcount_topk", "MAG_CENTERS", "MAG_THRESHOLDS",
 ]
 
@@ -255,6 +256,47 @@ def float_topk_gather_concat_3d(scores, lut, skipped, out, k):
     check(lib().zkv_topk_gather_concat(_p(s), _p(lu), _p(skipped) if sk > 0 else None, sk_ld, _p(out), bs * kv, L,
                                        int(k), sk, out.shape[2], _stream(s)), "zkv_topk_gather_concat")
     return out
+
+
+# ----------------------------------------------------------------- one-call retrieval chain
+def reference_select_ws_bytes(rows: int, n_chunks: int, nk: int, n_dense: int) -> int:
+    return int(lib().zkv_reference_select_ws_bytes(rows, n_chunks, nk, n_dense))
+
+
+def reference_select(q, chunk_min, chunk_max, centroid, chunk_valid, packed, n_chunks: int, n_valid_chunks: int,
+                     nk: int, n_dense: int, dense_topk: int, sparse_topk: int, k: int, skipped, final_out, workspace,
+                     raw_q_out=None):
+    """The reference-mode retrieval chain of one layer in one C call:
+    q [bs, 1, H*G, 128] bf16; chunk tensors [bs, H, n_max, ...]; skipped
+    [bs, H, >= sk] int64 (sk = skipped.shape[2]); final_out [bs, H, >= k+sk]
+    int64; workspace uint8 CUDA tensor of >= reference_select_ws_bytes(...)."""
+    bs, H, n_max = chunk_min.shape[:3]
+    rows = bs * H
+    G = q.shape[-2] // H
+    for name, t in (("q", q), ("chunk_min", chunk_min), ("chunk_max", chunk_max), ("centroid", centroid)):
+        _dtype(name, t, torch.bfloat16)
+        _contig(name, t)
+    _dtype("packed", packed, torch.int32)
+    _contig("packed", packed)
+    _dtype("final_out", final_out, torch.int64)
+    _contig("final_out", final_out)
+    _dtype("workspace", workspace, torch.uint8)
+    sk = skipped.shape[2] if skipped is not None else 0
+    sk_ld = 0
+    if sk > 0:
+        _dtype("skipped", skipped, torch.int64)
+        if skipped.stride(2) != 1 or skipped.stride(0) != H * skipped.stride(1):
+            skipped = skipped.contiguous()
+        sk_ld = skipped.stride(1)
+    valid = None
+    if chunk_valid is not None:
+        valid = chunk_valid if chunk_valid.dtype == torch.uint8 else chunk_valid.view(torch.uint8)
+    layer = _lib.ZkvRefLayer(_p(chunk_min), _p(chunk_max), _p(centroid), _p(valid), _p(packed))
+    check(lib().zkv_reference_select(_p(q), G, ctypes.byref(layer), rows, n_max, n_chunks, n_valid_chunks, nk,
+                                     n_dense, dense_topk, sparse_topk, k, _p(skipped) if sk > 0 else None, sk_ld, sk,
+                                     _p(final_out), final_out.shape[-1], _p(raw_q_out), _p(workspace),
+                                     workspace.numel(), _stream(q)), "zkv_reference_select")
+    return final_out
 
 
 # ----------------------------------------------------------------- merge

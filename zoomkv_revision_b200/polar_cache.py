@@ -328,14 +328,9 @@ class polar_cache:
             d = dict(device=dev)
             F = final_topk
             self._scratch[dev] = dict(
-                # flat buffers; per-step views are carved contiguously
-                scores=torch.empty(bs * H * nm, dtype=torch.float32, **d),
-                chunk_idx=torch.empty(bs * H * nm, dtype=torch.int64, **d),
-                density=torch.empty(bs * H * nm, dtype=torch.float32, **d),
-                dense_pos=torch.empty(bs * H * nm, dtype=torch.int64, **d),
-                dense_mask=torch.empty(bs * H * nm, dtype=torch.bool, **d),
-                out_scores=torch.empty(bs * H * nm * CHUNK, dtype=torch.float32, **d),
-                out_indices=torch.empty(bs * H * nm * CHUNK, dtype=torch.int64, **d),
+                # intermediates of the one-call retrieval chain, sized for the
+                # largest plan (n_chunks = nk = n_dense = n_max)
+                workspace=torch.empty(ops.reference_select_ws_bytes(bs * H, nm, nm, nm), dtype=torch.uint8, **d),
                 final=torch.empty(bs, H, F + self.MAX_SKIPPED_INDICES, dtype=torch.int64, **d),
                 skipped=torch.zeros(bs, H, self.MAX_SKIPPED_INDICES, dtype=torch.int64, **d),
                 status=torch.zeros(1, dtype=torch.int32, **d),
@@ -491,33 +486,13 @@ class polar_cache:
         n_valid_chunks = valid_length // CHUNK
         if self.attention_mode == "page":
             return self._compute_page(q, l, n_chunks, nk, valid_length, total)
-        bs, H = self.batch_size, self.kv_head
-
-        def view(name, k):
-            return sc[name][:bs * H * k].view(bs, H, k)
-
-        raw_q = q[:, 0].view(bs, H, self.group_size, self.head_dim).mean(dim=2)
-        torch.cuda.nvtx.range_push("stage1_chunk_pick")
-        scores = view("scores", n_chunks)
-        ops.quest_chunk_score(raw_q, self.chunk_min[l], self.chunk_max[l], scores, n_chunks, self.chunk_valid[l])
-        chunk_idx = ops.float_topk_3d(scores, nk, out=view("chunk_idx", nk))
-        torch.cuda.nvtx.range_pop()
-        torch.cuda.nvtx.range_push("stage2_cds")
-        dense_topk = max(1, min(self.cfg["dense_topk"], CHUNK))
-        sparse_topk = max(1, min(self.cfg["sparse_topk"], CHUNK))
-        density = view("density", nk)
-        ops.partial_chunk_density_scores_cuda(chunk_idx, self.chunk_centroid[l], raw_q, density)
-        pos = ops.float_topk_3d(density, n_dense, out=view("dense_pos", n_dense))
-        mask = view("dense_mask", nk)
-        ops.dense_mask_from_topk_cuda(pos, mask)
-        out_scores = view("out_scores", nk * CHUNK)
-        out_indices = view("out_indices", nk * CHUNK)
-        ops.partial_chunk_kivi_qk_dense_sparse_cuda(chunk_idx, mask, self.kivi_packed[l][:, :, :n_valid_chunks],
-                                                    self.chunk_min[l], self.chunk_max[l], raw_q, dense_topk,
-                                                    sparse_topk, CHUNK, out_scores, out_indices)
+        torch.cuda.nvtx.range_push("stage1_stage2_select")
         k = min(self.final_topk, nk * CHUNK)
         final = sc["final"]
-        ops.float_topk_gather_concat_3d(out_scores, out_indices, sc["skipped"][:, :, :skipped], final, k)
+        ops.reference_select(q, self.chunk_min[l], self.chunk_max[l], self.chunk_centroid[l], self.chunk_valid[l],
+                             self.kivi_packed[l], n_chunks, n_valid_chunks, nk, n_dense,
+                             max(1, min(self.cfg["dense_topk"], CHUNK)), max(1, min(self.cfg["sparse_topk"], CHUNK)),
+                             k, sc["skipped"][:, :, :skipped], final, sc["workspace"])
         torch.cuda.nvtx.range_pop()
         torch.cuda.nvtx.range_push("compute_attention")
         # sink + selected retrieval tokens + near zone [local_start, total)
