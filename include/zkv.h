@@ -171,6 +171,34 @@ int zkv_reference_select(const void* q, int G, const zkv_ref_layer* layer,
                          void* raw_q_out, void* workspace, size_t ws_bytes,
                          void* stream);
 
+/* Capacity of the library-owned buffer of zkv_reference_select_noalloc.  */
+#define ZKV_REFERENCE_SELECT_NOALLOC_MAX_BYTES (16u << 20)
+
+/* zkv_reference_select with the intermediates in a library-owned device
+ * buffer (a static device array, one per device) instead of a caller
+ * workspace; allocates nothing.  No reference counterpart: the reference
+ * allocates its intermediates through torch.  For callers that cannot
+ * allocate device memory: hosts that bind only this C ABI and own no device
+ * allocator (cgo, JNI, plain C), and decode loops that must not call
+ * cudaMalloc, which can synchronise the device.
+ *   Limit: zkv_reference_select_ws_bytes(rows, n_chunks, nk, n_dense) <=
+ *   ZKV_REFERENCE_SELECT_NOALLOC_MAX_BYTES (16 MiB), else ZKV_ERR_CAPACITY
+ *   (e.g. 64 rows x 2048 chunks with nk = 816, n_dense = 244 needs ~12 MB).
+ *   Setup: the first call on each device looks the buffer's address up
+ *   (cudaGetSymbolAddress on the current device, which must be the
+ *   stream's device); make that first call before any stream capture.
+ *   Calls that overlap on one device (concurrent streams or host threads)
+ *   race on the one buffer: serialise them.  Nothing needs clearing: every
+ *   byte the chain reads is written first by the same call.               */
+int zkv_reference_select_noalloc(const void* q, int G,
+                                 const zkv_ref_layer* layer, int rows,
+                                 int n_max, int n_chunks, int n_valid_chunks,
+                                 int nk, int n_dense, int dense_topk,
+                                 int sparse_topk, int k,
+                                 const int64_t* skipped, int64_t sk_ld,
+                                 int sk, int64_t* final_out, int64_t final_ld,
+                                 void* raw_q_out, void* stream);
+
 /* ------------------------------------------------------------ attention */
 
 /* GQA decode attention over raw bf16 K/V rows gathered by index, fused with

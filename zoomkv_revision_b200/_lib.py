@@ -79,6 +79,8 @@ _SIGNATURES = {
     "zkv_reference_select_ws_bytes": [_i32, _i32, _i32, _i32],
     "zkv_reference_select": [_c_void_p, _i32, ctypes.POINTER(ZkvRefLayer)] + [_i32] * 9 +
                             [_c_void_p, _i64, _i32, _c_void_p, _i64, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
+    "zkv_reference_select_noalloc": [_c_void_p, _i32, ctypes.POINTER(ZkvRefLayer)] + [_i32] * 9 +
+                                    [_c_void_p, _i64, _i32, _c_void_p, _i64, _c_void_p, _c_void_p],
     "zkv_version": [],
     "zkv_status_string": [_i32],
 }
