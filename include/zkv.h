@@ -147,6 +147,12 @@ typedef struct zkv_ref_layer {
     const int32_t* packed;
 } zkv_ref_layer;
 
+/* raw_q [rows][128] = bf16(fp32 sum of the G query heads in head order / G)
+ * of q [rows][G][128] bf16: the GQA-mean query of polar_cache.compute
+ * (cache_hub/polar_cache_quest_density_single_layer_kivi.py:1622-1625),
+ * computed exactly as zkv_page_decode and zkv_reference_select do.       */
+int zkv_gqa_mean(const void* q, int rows, int G, void* raw_q, void* stream);
+
 /* Bytes of workspace zkv_reference_select needs (0 on bad arguments).    */
 size_t zkv_reference_select_ws_bytes(int rows, int n_chunks, int nk,
                                      int n_dense);
@@ -252,6 +258,21 @@ int zkv_page_decode(const void* q, const zkv_page_layer* layer, int rows,
                     int G, int n_max, int n_c, int nk, int n_sink,
                     int near_start, int n_near, float scale, void* out,
                     float* lse, int64_t* sel_out, int32_t* status, int cluster,
+                    void* stream);
+
+/* Attention over externally selected pages (the sequence-split step):
+ * the layer buffer holds pages [sel_lo, sel_hi) of the sequence as its
+ * pages 0..; of the global page ids sel [rows][n_sel] (-1 = none) those in
+ * [sel_lo, sel_hi) are attended, plus the n_sink / n_near raw rows as in
+ * zkv_page_decode (pass 0 on ranks that own none).  Writes the normalised
+ * partial to out (bf16) or out_f32 (fp32, [rows][G][128]) and lse [rows][G]
+ * (natural log; -inf when a row attended nothing) for an LSE merge.
+ * n_sel <= 4096.  Same kernel and numerics as zkv_page_decode's phase 3-4. */
+int zkv_page_attend(const void* q, const zkv_page_layer* layer, int rows,
+                    int G, int n_max, const int64_t* sel, int n_sel,
+                    int64_t sel_lo, int64_t sel_hi, int n_sink,
+                    int near_start, int n_near, float scale, void* out,
+                    float* out_f32, float* lse, int32_t* status, int cluster,
                     void* stream);
 
 /* Merge two attention partials by log-sum-exp (fp32 math, bf16 out).

@@ -1,0 +1,126 @@
+"""GPU: sequence-split page decode (zoomkv_revision_b200.seqsplit) against
+the single-device fused page decode: same selected pages (exact), output
+within the attention tolerance (bit-identical at world size 1).  Ranks are
+emulated on one GPU; a real NCCL run needs >= 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from zoomkv_revision_b200 import ops
+from zoomkv_revision_b200 import seqsplit as S
+from zoomkv_revision_b200 import workload as W
+
+pytestmark = pytest.mark.gpu
+G = 4
+
+
+def _setup(seed, bs, H, n_c, n_near, dev):
+    pc, _ = W.build_page_cache(seed, bs, H, n_c * 16, n_near, dev)
+    q = W.synth_query(torch.Generator(device=dev).manual_seed(seed + 7), bs, H * G, dev)
+    return pc, q
+
+
+def _close(out, ref):
+    o, r = out.float(), ref.float()
+    err = (o - r).abs()
+    assert err.max() <= 2e-2 and err.mean() / r.abs().mean() <= 1e-2, (float(err.max()), float(err.mean()))
+
+
+def test_world1_bit_identical_to_page_decode():
+    dev = torch.device("cuda", 0)
+    bs, H, n_c, nk, n_near = 2, 4, 700, 96, 64
+    pc, q = _setup(1, bs, H, n_c, n_near, dev)
+    sel = torch.empty(bs * H, nk, dtype=torch.int64, device=dev)
+    ref = ops.page_decode(q, pc.layer(), n_c, nk, n_near, sel_out=sel)
+    bufs = S.SplitBuffers.alloc(bs, H, G, n_c, nk, 1, dev)
+    out, s = S.decode_step(q, pc.layer(), n_c, nk, bufs, rank=0, world=1, n_near=n_near)
+    torch.cuda.synchronize()
+    assert torch.equal(s.view(bs * H, nk), sel)
+    assert torch.equal(out, ref)
+    assert int(bufs.status.item()) == 0
+
+
+@pytest.mark.parametrize("world,bs,H,n_c,nk,n_near", [(2, 1, 8, 1001, 64, 128), (3, 2, 2, 500, 120, 16),
+                                                      (4, 1, 8, 8184, 256, 128), (8, 1, 8, 8184, 256, 128)])
+def test_emulated_ranks_match_page_decode(world, bs, H, n_c, nk, n_near):
+    """Each emulated rank scores only its own pages and attends only the
+    selected pages it owns; the merge of the partials equals the fused
+    single-device decode (config-3 shape: 131072 context, budget 4096)."""
+    dev = torch.device("cuda", 0)
+    pc, q = _setup(world * 10 + nk, bs, H, n_c, n_near, dev)
+    sel_ref = torch.empty(bs * H, nk, dtype=torch.int64, device=dev)
+    ref = ops.page_decode(q, pc.layer(), n_c, nk, n_near, sel_out=sel_ref)
+    be = S.CudaBackend()
+    per = S.split_range(n_c, world, 0)[2]
+    raw_q = be.raw_q(q, H)
+    rows = []
+    layers = []
+    for r in range(world):
+        lo, hi, _ = S.split_range(n_c, world, r)
+        lay = S.local_layer(pc.layer(), lo, hi)
+        layers.append((lo, hi, lay))
+        sc = torch.full((bs, H, per), -float("inf"), device=dev)
+        be.local_scores(raw_q, lay, hi - lo, torch.empty(bs * H * per, device=dev), sc)
+        rows.append(sc)
+    row = torch.cat(rows, dim=2)
+    sel = be.global_topk(row, nk, torch.empty(bs, H, nk, dtype=torch.int64, device=dev))
+    parts = torch.empty(world, bs * H * G, 128, device=dev)
+    lses = torch.empty(world, bs * H * G, device=dev)
+    for r, (lo, hi, lay) in enumerate(layers):
+        part = torch.empty(bs, H * G, 128, device=dev)
+        lse = torch.empty(bs, H * G, device=dev)
+        be.attend(q, lay, sel, lo, hi, 0, 0, n_near if r == 0 else 0, part, lse, None)
+        parts[r] = part.view(-1, 128)
+        lses[r] = lse.view(-1)
+    out = torch.empty(bs, 1, H * G, 128, dtype=torch.bfloat16, device=dev)
+    be.merge(parts, lses, out.view(-1, 128))
+    torch.cuda.synchronize()
+    assert torch.equal(sel.view(bs * H, nk), sel_ref)
+    _close(out, ref)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_rank(rank, world, port, path):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        bs, H, n_c, nk, n_near = 1, 8, 2047, 128, 128
+        pc, q = _setup(3, bs, H, n_c, n_near, dev)
+        lo, hi, per = S.split_range(n_c, world, rank)
+        bufs = S.SplitBuffers.alloc(bs, H, G, per, nk, world, dev)
+        out, sel = S.decode_step(q, S.local_layer(pc.layer(), lo, hi), n_c, nk, bufs, rank=rank, world=world,
+                                 n_near=n_near)
+        ref_sel = torch.empty(bs * H, nk, dtype=torch.int64, device=dev)
+        ref = ops.page_decode(q, pc.layer(), n_c, nk, n_near, sel_out=ref_sel)
+        torch.cuda.synchronize()
+        np.savez(os.path.join(path, f"r{rank}.npz"), out=out.float().cpu().numpy(), ref=ref.float().cpu().numpy(),
+                 sel=sel.cpu().numpy(), ref_sel=ref_sel.cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_nccl_world2(tmp_path):
+    env = {"NCCL_NVLS_ENABLE": "0"}
+    os.environ.update(env)
+    mp.start_processes(_nccl_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    res = [np.load(os.path.join(tmp_path, f"r{r}.npz")) for r in range(2)]
+    for r in res:
+        assert np.array_equal(r["sel"].reshape(r["ref_sel"].shape), r["ref_sel"])
+        assert np.array_equal(r["out"], res[0]["out"])
+        _close(torch.from_numpy(r["out"]), torch.from_numpy(r["ref"]))

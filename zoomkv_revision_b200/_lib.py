@@ -81,6 +81,9 @@ _SIGNATURES = {
                             [_c_void_p, _i64, _i32, _c_void_p, _i64, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
     "zkv_reference_select_noalloc": [_c_void_p, _i32, ctypes.POINTER(ZkvRefLayer)] + [_i32] * 9 +
                                     [_c_void_p, _i64, _i32, _c_void_p, _i64, _c_void_p, _c_void_p],
+    "zkv_gqa_mean": [_c_void_p, _i32, _i32, _c_void_p, _c_void_p],
+    "zkv_page_attend": [_c_void_p, ctypes.POINTER(ZkvPageLayer), _i32, _i32, _i32, _c_void_p, _i32, _i64, _i64, _i32,
+                        _i32, _i32, _f32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p],
     "zkv_version": [],
     "zkv_status_string": [_i32],
 }

@@ -283,7 +283,8 @@ __device__ void cta_merge(const WarpAttn& st, int G, float* scratch, float* cm, 
 // chains), then rank 0 merges locally and writes out / lse.  `recv` is rank
 // 0's staging region (free once all CTAs passed the first cluster barrier).
 __device__ void cluster_merge(cg::cluster_group& cluster, int CS, int G, const float* cm, const float* cl,
-                              const float* co, float* recv, uint16_t* out_row, float* lse_row) {
+                              const float* co, float* recv, uint16_t* out_row, float* lse_row,
+                              float* out_f32_row = nullptr) {
     constexpr int kPart = 16 + 8 * kHeadDim;  // m[8], l[8], o[8][128]
     const int rank = (int)cluster.block_rank();
     cluster.sync();  // every CTA finished phase 3 and its CTA merge
@@ -309,7 +310,12 @@ __device__ void cluster_merge(cg::cluster_group& cluster, int CS, int G, const f
             Ls += wt * b[8 + h];
             O += wt * b[16 + i];
         }
-        out_row[i] = f2bfbits(Ls > 0.f ? O / Ls : 0.f);
+        const float o = Ls > 0.f ? O / Ls : 0.f;
+        if (out_f32_row) {
+            out_f32_row[i] = o;
+        } else {
+            out_row[i] = f2bfbits(o);
+        }
         if ((i % kHeadDim) == 0 && lse_row)
             lse_row[h] = (Ls > 0.f) ? (M + __log2f(Ls)) * 0.69314718055994531f : -INFINITY;
     }
@@ -325,6 +331,11 @@ struct PageArgs {
     float* lse;
     int64_t* sel_out;
     int32_t* status;
+    // external selection (sequence split): global page ids [rows][nk]; the
+    // ids in [sel_lo, sel_hi) are this layer buffer's pages id - sel_lo
+    const int64_t* sel_in;
+    int64_t sel_lo, sel_hi;
+    float* out_f32;  // fp32 partial output instead of bf16 (may be NULL)
 };
 
 __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const PageArgs a) {
@@ -463,7 +474,23 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
 
     // ------------------------------------------------ phase 2: select
     cluster.sync();
-    if (a.n_c <= a.nk) {
+    __shared__ int s_nsel;
+    if (a.sel_in) {  // the pages this buffer owns, in list order
+        if (warp == 0) {
+            const int64_t* sr = a.sel_in + row * a.nk;
+            int base = 0;
+            for (int j0 = 0; j0 < a.nk; j0 += 32) {
+                const int j = j0 + lane;
+                const int64_t id = j < a.nk ? sr[j] : -1;
+                const bool own = id >= a.sel_lo && id < a.sel_hi && id - a.sel_lo < a.n_max;
+                const unsigned bal = __ballot_sync(0xffffffffu, own);
+                if (own) sel_s[base + __popc(bal & ((1u << lane) - 1u))] = (int)(id - a.sel_lo);
+                base += __popc(bal);
+            }
+            if (lane == 0) s_nsel = base;
+        }
+        __syncthreads();
+    } else if (a.n_c <= a.nk) {
         for (int i = threadIdx.x; i < a.nk; i += kAttnThreads) sel_s[i] = i < a.n_c ? i : 0;
         __syncthreads();
     } else {
@@ -480,13 +507,15 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
                                            scan, [&](int pos, int i) { sel_s[pos] = i; }, true, lo, hi);
         }
     }
-    if (a.sel_out && rank == 0)
+    if (a.sel_out && rank == 0 && !a.sel_in)
         for (int i = threadIdx.x; i < a.nk; i += kAttnThreads) a.sel_out[row * a.nk + i] = sel_s[i];
 
     // ------------------------------------------------ phase 3: attention
     WarpAttn st;
     warp_attn_init(st, q_s, a.G);
-    const int p_lo = rank * a.pp, p_hi = min(a.nk, p_lo + a.pp);
+    const int nsel = a.sel_in ? s_nsel : a.nk;
+    const int pp = a.sel_in ? (nsel + CS - 1) / CS : a.pp;
+    const int p_lo = rank * pp, p_hi = min(nsel, p_lo + pp);
     const int n_raw_all = a.n_sink + a.n_near;
     const int n_lo = rank * a.pn, n_hi = min(n_raw_all, n_lo + a.pn);
     const int n_pages = max(0, p_hi - p_lo);
@@ -535,8 +564,9 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
     // ------------------------------------------------ phase 4: merge
     __syncthreads();
     cta_merge(st, a.G, reinterpret_cast<float*>(region), cm, cl, co);
-    cluster_merge(cluster, CS, a.G, cm, cl, co, reinterpret_cast<float*>(region), a.out + row * a.G * kHeadDim,
-                  a.lse ? a.lse + row * a.G : nullptr);
+    cluster_merge(cluster, CS, a.G, cm, cl, co, reinterpret_cast<float*>(region),
+                  a.out ? a.out + row * a.G * kHeadDim : nullptr, a.lse ? a.lse + row * a.G : nullptr,
+                  a.out_f32 ? a.out_f32 + row * a.G * kHeadDim : nullptr);
     if (threadIdx.x == 0 && s_failed) set_status(a.status, ZKV_ERR_TIMEOUT);
 }
 
@@ -658,6 +688,11 @@ __global__ void lse_merge_n_kernel(const float* __restrict__ parts, const float*
 
 using namespace zkv;
 
+static size_t page_smem(const PageArgs& a) {
+    return kRegionBytes + (size_t)a.n_c_pad * 4 + (size_t)((a.nk + 3) & ~3) * 4 + 9 * kHeadDim * 2 +
+           (16 + 8 * kHeadDim) * 4 + (512 + 8 + 2 * kAttnThreads) * 4 + (4 * kAttnWarps) * 8 + 16;
+}
+
 static int pick_cluster(int requested, int rows) {
     if (requested == 1 || requested == 2 || requested == 4 || requested == 8) return requested;
     (void)rows;
@@ -702,11 +737,59 @@ extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int r
     a.lse = lse;
     a.sel_out = sel_out;
     a.status = status;
-    const size_t smem = kRegionBytes + (size_t)a.n_c_pad * 4 + (size_t)((a.nk + 3) & ~3) * 4 + 9 * kHeadDim * 2 +
-                        (16 + 8 * kHeadDim) * 4 + (512 + 8 + 2 * kAttnThreads) * 4 +
-                        (4 * kAttnWarps) * 8 + 16;
+    a.sel_in = nullptr;
+    a.sel_lo = a.sel_hi = 0;
+    a.out_f32 = nullptr;
     void* args[] = {&a};
-    return launch_clustered((const void*)page_decode_kernel, rows * CS, kAttnThreads, CS, smem, (cudaStream_t)stream, args);
+    return launch_clustered((const void*)page_decode_kernel, rows * CS, kAttnThreads, CS, page_smem(a),
+                            (cudaStream_t)stream, args);
+}
+
+extern "C" int zkv_page_attend(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max,
+                               const int64_t* sel, int n_sel, int64_t sel_lo, int64_t sel_hi, int n_sink,
+                               int near_start, int n_near, float scale, void* out, float* out_f32, float* lse,
+                               int32_t* status, int cluster, void* stream) {
+    if (!q || !layer || (!out && !out_f32) || !sel || rows < 0 || G < 1 || G > 8 || n_sel < 1 || n_near < 0 ||
+        n_sink < 0 || near_start < 0 || sel_hi < sel_lo)
+        return ZKV_ERR_ARG;
+    if ((int64_t)near_start + n_near > layer->near_ld || n_sink > layer->near_ld) return ZKV_ERR_ARG;
+    if (n_sel > 4096) return ZKV_ERR_CAPACITY;
+    if (rows == 0) return ZKV_OK;
+    const zkv_page_layer& L = *layer;
+    if (!L.kcodes || !L.vcodes_t || !L.vmeta || !L.chunk_min || !L.chunk_max ||
+        (n_near + n_sink > 0 && (!L.near_k || !L.near_v)))
+        return ZKV_ERR_ARG;
+    if (((uintptr_t)L.chunk_min & 15) || ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)L.kcodes & 15) ||
+        ((uintptr_t)L.vcodes_t & 15) || ((uintptr_t)L.vmeta & 15) || ((uintptr_t)L.near_k & 15) ||
+        ((uintptr_t)L.near_v & 15) || ((uintptr_t)q & 3))
+        return ZKV_ERR_ALIGN;
+    const int CS = pick_cluster(cluster, rows);
+    PageArgs a;
+    a.q = (const uint16_t*)q;
+    a.L = L;
+    a.G = G;
+    a.n_max = n_max;
+    a.n_c = 0;  // no scoring phase
+    a.nk = n_sel;
+    a.n_sink = n_sink;
+    a.near_start = near_start;
+    a.n_near = n_near;
+    a.n_c_pad = 0;
+    a.per = 0;
+    a.pp = (n_sel + CS - 1) / CS;
+    a.pn = ((n_sink + n_near + CS - 1) / CS + 7) & ~7;
+    a.sl2 = scale * 1.4426950408889634f;
+    a.out = (uint16_t*)out;
+    a.lse = lse;
+    a.sel_out = nullptr;
+    a.status = status;
+    a.sel_in = sel;
+    a.sel_lo = sel_lo;
+    a.sel_hi = sel_hi;
+    a.out_f32 = out_f32;
+    void* args[] = {&a};
+    return launch_clustered((const void*)page_decode_kernel, rows * CS, kAttnThreads, CS, page_smem(a),
+                            (cudaStream_t)stream, args);
 }
 
 extern "C" int zkv_attn_rows(const void* q, const void* keys, const void* values, int64_t kv_ld_row, int rows, int G,

@@ -58,6 +58,14 @@ inline RefWs ref_ws_layout(int rows, int n_chunks, int nk, int n_dense) {
 
 }  // namespace
 
+extern "C" int zkv_gqa_mean(const void* q, int rows, int G, void* raw_q, void* stream) {
+    if (!q || !raw_q || rows < 0 || G < 1) return ZKV_ERR_ARG;
+    if (((uintptr_t)q & 7) || ((uintptr_t)raw_q & 7)) return ZKV_ERR_ALIGN;
+    if (rows == 0) return ZKV_OK;
+    gqa_mean_kernel<<<(rows + 7) / 8, 256, 0, (cudaStream_t)stream>>>((const uint16_t*)q, rows, G, (uint16_t*)raw_q);
+    return launch_status();
+}
+
 extern "C" size_t zkv_reference_select_ws_bytes(int rows, int n_chunks, int nk, int n_dense) {
     if (rows < 0 || n_chunks < 0 || nk < 0 || n_dense < 0) return 0;
     return ref_ws_layout(rows, n_chunks, nk, n_dense).total;

@@ -47,7 +47,7 @@ __all__ = [
     "quest_chunk_score", "float_topk", "float_topk_3d", "radix_topk_3d", "partial_chunk_density_scores_cuda",
     "dense_mask_from_topk_cuda", "partial_chunk_kivi_qk_dense_sparse_cuda", "float_topk_gather_concat_3d",
     "lse_merge_cuda", "lse_merge_n", "kivi_encode_chunks", "vquant_encode", "attn_rows", "page_decode",
-    "PageLayer", "reference_select", "reference_select_ws_bytes", "RqLayout", "rq_encode", "batch_encode", "rq_query", "get_cache_cnt_fused", "collision_topk",
+    "PageLayer", "page_attend", "gqa_mean", "reference_select", "reference_select_ws_bytes", "RqLayout", "rq_encode", "batch_encode", "rq_query", "get_cache_cnt_fused", "collision_topk",
     "partial_rerank_cuda", "coarse_2bit_score_cuda", "rq_popcount_topk", "MAG_CENTERS", "MAG_THRESHOLDS",
 ]
 
@@ -82,29 +82,33 @@ def _p(t):
 def quest_chunk_score(raw_q, chunk_min, chunk_max, scores_out, n_chunks, chunk_valid=None):
     """scores_out[b,h,c] = sum_d max(q*max, q*min) for c < n_chunks (in place).
 
-    raw_q [bs,kv,128] bf16; chunk_min/max [bs,kv,n_max,128] bf16;
-    scores_out: n_chunks*bs*kv fp32 elements laid out [bs,kv,n_chunks];
-    chunk_valid [bs,kv,n_max] bool or None.
+    raw_q [bs,kv,128] bf16; chunk_min/max [bs,kv,n_max,128] bf16 (or views
+    of a chunk range of such buffers); scores_out: n_chunks*bs*kv fp32
+    elements laid out [bs,kv,n_chunks]; chunk_valid [bs,kv,n_max] bool or None.
     """
     _cuda(("raw_q", raw_q), ("chunk_min", chunk_min), ("chunk_max", chunk_max), ("scores", scores_out),
           ("valid", chunk_valid))
-    for n, t in (("raw_q", raw_q), ("chunk_min", chunk_min), ("chunk_max", chunk_max)):
+    _dtype("raw_q", raw_q, torch.bfloat16)
+    _contig("raw_q", raw_q)
+    for n, t in (("chunk_min", chunk_min), ("chunk_max", chunk_max)):
         _dtype(n, t, torch.bfloat16)
-        _contig(n, t)
+        if t.stride(3) != 1 or t.stride(2) != 128 or t.stride(0) != t.shape[1] * t.stride(1):
+            raise ValueError(f"{n} must be a chunk range of a contiguous [bs, kv, n_max, 128] buffer")
     _dtype("scores_out", scores_out, torch.float32)
     _contig("scores_out", scores_out)
     if raw_q.shape[-1] != 128:
         raise ValueError("quest_chunk_score: only head_dim==128 is supported")
     bs, kv = raw_q.shape[0], raw_q.shape[1]
-    n_max = chunk_min.shape[2]
+    n_max = chunk_min.stride(1) // 128
     n_chunks = int(n_chunks)
-    if n_chunks > n_max:
+    if n_chunks > chunk_min.shape[2]:
         raise ValueError("n_chunks must <= chunk_n_max")
     if scores_out.numel() < bs * kv * n_chunks:
         raise ValueError("scores_out too small")
     if chunk_valid is not None:
         _dtype("chunk_valid", chunk_valid, torch.bool)
-        _contig("chunk_valid", chunk_valid)
+        if chunk_valid.stride(2) != 1 or chunk_valid.stride(1) != n_max:
+            raise ValueError("chunk_valid must match chunk_min's layout")
     check(lib().zkv_quest_score(_p(raw_q), _p(chunk_min), _p(chunk_max), _p(chunk_valid), _p(scores_out), bs * kv,
                                 n_chunks, n_max, _stream(raw_q)), "zkv_quest_score")
 
@@ -411,6 +415,41 @@ def page_decode(q, layer: PageLayer, n_c: int, nk: int, n_near: int, *, n_sink: 
     check(lib().zkv_page_decode(_p(qc), ctypes.byref(layer.struct), bs * H, G, n_max, int(n_c), int(nk), int(n_sink),
                                 int(near_start), int(n_near), scale, _p(out), _p(lse), _p(sel_out), _p(status),
                                 int(cluster), _stream(q)), "zkv_page_decode")
+    return out
+
+
+def page_attend(q, layer: PageLayer, sel, sel_lo: int, sel_hi: int, *, n_sink: int = 0, near_start: int = 0,
+                n_near: int = 0, scale=None, out=None, out_f32=None, lse=None, status=None, cluster=0):
+    """Attention over externally selected pages (sequence split): sel
+    [bs, H, n_sel] global page ids; this layer buffer holds pages
+    [sel_lo, sel_hi).  Returns out_f32 [bs, H*G, 128] fp32 when given, else
+    bf16 out [bs, 1, H*G, 128]; lse [bs, H*G] fp32 (natural log) if given."""
+    cmin = layer.tensors[0]
+    bs, H, _, D = cmin.shape
+    n_max = cmin.stride(1) // D   # row stride in pages (views of a chunk range keep the full stride)
+    G = q.shape[2] // H
+    _dtype("sel", sel, torch.int64)
+    _contig("sel", sel)
+    qc = q.contiguous()
+    if out is None and out_f32 is None:
+        out = torch.empty(bs, 1, H * G, D, dtype=torch.bfloat16, device=q.device)
+    scale = (1.0 / D ** 0.5) if scale is None else float(scale)
+    check(lib().zkv_page_attend(_p(qc), ctypes.byref(layer.struct), bs * H, G, n_max, _p(sel), sel.shape[-1],
+                                int(sel_lo), int(sel_hi), int(n_sink), int(near_start), int(n_near), scale, _p(out),
+                                _p(out_f32), _p(lse), _p(status), int(cluster), _stream(q)), "zkv_page_attend")
+    return out_f32 if out_f32 is not None else out
+
+
+def gqa_mean(q, heads: int, out=None):
+    """raw_q [bs, H, 128] bf16 = GQA mean of q [bs, 1, H*G, 128] (fp32 sum in
+    head order / G, as the fused kernels compute it)."""
+    _dtype("q", q, torch.bfloat16)
+    qc = q.contiguous()
+    bs = qc.shape[0]
+    G = qc.shape[-2] // heads
+    if out is None:
+        out = torch.empty(bs, heads, 128, dtype=torch.bfloat16, device=q.device)
+    check(lib().zkv_gqa_mean(_p(qc), bs * heads, G, _p(out), _stream(q)), "zkv_gqa_mean")
     return out
 
 
