@@ -29,6 +29,12 @@ constexpr int kPageTx = 1024 + 1024 + 256 + 256 + 256;
 // RAW8 slot: K rows [8][136] bf16 @0, V rows @2176
 constexpr int kRawV = 8 * kRawStride * 2;
 constexpr int kRegionBytes = 2 * kAttnWarps * kSlotBytes;  // 36 KB: phase-1 rings / page slots / merge
+// page-decode phase 3: 3 slots per warp of 3 KiB (a KIVI page + its computed
+// scale, or a RAW4 item of up to 4 raw rows) so each warp keeps 3 items in flight
+constexpr int kPSlotBytes = 3072;
+constexpr int kPSlots = 3;
+constexpr int kRaw4V = 4 * kRawStride * 2;  // V rows of a RAW4 slot
+static_assert(kAttnWarps * kPSlots * kPSlotBytes <= kRegionBytes, "page slots exceed the region");
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -117,25 +123,33 @@ __device__ __forceinline__ void warp_page_kivi(WarpAttn& st, uint8_t* slot, int 
     const uint32_t* mn2 = reinterpret_cast<const uint32_t*>(slot + 2304);
     const uint32_t* sc2 = reinterpret_cast<const uint32_t*>(slot + 2816);
     const uint32_t sel = nib_sel(tig);
-    float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    // S = Q K^T over 8 k-steps of 16 dims; the two k-halves accumulate
+    // separately (4 independent MMA chains of 4 instead of 2 of 8) and are
+    // added at the end.
+    float sacc[2][2][4] = {};  // [k-half][token tile][fragment]
 #pragma unroll
-    for (int s = 0; s < 8; ++s) {
-        const __nv_bfloat162 sA = bits_bf162(sc2[8 * s + tig]);
-        const __nv_bfloat162 sB = bits_bf162(sc2[8 * s + 4 + tig]);
-        const __nv_bfloat162 nA = neg128(sA), nB = neg128(sB);
-        const __nv_bfloat162 mA = bits_bf162(mn2[8 * s + tig]);
-        const __nv_bfloat162 mB = bits_bf162(mn2[8 * s + 4 + tig]);
+    for (int s4 = 0; s4 < 4; ++s4) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int n = 8 * h + g;
-            const uint32_t w0 = (uint32_t)kc[(2 * s) * kChunk + n];
-            const uint32_t w1 = (uint32_t)kc[(2 * s + 1) * kChunk + n];
-            const uint32_t b0 = bf162_bits(dequant2_w(w0, sel, sA, nA, mA));
-            const uint32_t b1 = bf162_bits(dequant2_w(w1, sel, sB, nB, mB));
-            mma_bf16_16816(sacc[h], st.qa[s][0], 0u, st.qa[s][1], 0u, b0, b1);
+        for (int kh = 0; kh < 2; ++kh) {
+            const int s = s4 + 4 * kh;
+            const __nv_bfloat162 sA = bits_bf162(sc2[8 * s + tig]);
+            const __nv_bfloat162 sB = bits_bf162(sc2[8 * s + 4 + tig]);
+            const __nv_bfloat162 nA = neg128(sA), nB = neg128(sB);
+            const __nv_bfloat162 mA = bits_bf162(mn2[8 * s + tig]);
+            const __nv_bfloat162 mB = bits_bf162(mn2[8 * s + 4 + tig]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int n = 8 * h + g;
+                const uint32_t w0 = (uint32_t)kc[(2 * s) * kChunk + n];
+                const uint32_t w1 = (uint32_t)kc[(2 * s + 1) * kChunk + n];
+                const uint32_t b0 = bf162_bits(dequant2_w(w0, sel, sA, nA, mA));
+                const uint32_t b1 = bf162_bits(dequant2_w(w1, sel, sB, nB, mB));
+                mma_bf16_16816(sacc[kh][h], st.qa[s][0], 0u, st.qa[s][1], 0u, b0, b1);
+            }
         }
     }
-    float x[4] = {sacc[0][0] * sl2, sacc[0][1] * sl2, sacc[1][0] * sl2, sacc[1][1] * sl2};
+    float x[4] = {(sacc[0][0][0] + sacc[1][0][0]) * sl2, (sacc[0][0][1] + sacc[1][0][1]) * sl2,
+                  (sacc[0][1][0] + sacc[1][1][0]) * sl2, (sacc[0][1][1] + sacc[1][1][1]) * sl2};
     uint32_t pb0, pb1;
     warp_softmax(st, x, G, pb0, pb1);
     const uint2* vc = reinterpret_cast<const uint2*>(slot + 1024);
@@ -188,6 +202,65 @@ __device__ __forceinline__ void warp_page_raw8(WarpAttn& st, const uint8_t* slot
         const uint32_t a1 =
             (uint32_t)V[(2 * tig) * kRawStride + d + 8] | ((uint32_t)V[(2 * tig + 1) * kRawStride + d + 8] << 16);
         mma_bf16_16816(st.o[j], a0, a1, 0u, 0u, pb0, pb1);
+    }
+}
+
+// RAW4 item: up to 4 raw bf16 token rows (padded stride); bit t of `present`
+// says whether token t is real (absent rows were zero-filled).  Tokens 4..7
+// of the m16n8k16 tiles are zero operands.
+__device__ __forceinline__ void warp_page_raw4(WarpAttn& st, const uint8_t* slot, unsigned present, int G, float sl2) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+    const uint16_t* K = reinterpret_cast<const uint16_t*>(slot);
+    const uint16_t* V = reinterpret_cast<const uint16_t*>(slot + kRaw4V);
+    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        uint32_t b0 = 0u, b1 = 0u;
+        if (g < 4) {
+            b0 = *reinterpret_cast<const uint32_t*>(K + g * kRawStride + 16 * s + 2 * tig);
+            b1 = *reinterpret_cast<const uint32_t*>(K + g * kRawStride + 16 * s + 8 + 2 * tig);
+        }
+        mma_bf16_16816(sacc, st.qa[s][0], 0u, st.qa[s][1], 0u, b0, b1);
+    }
+    const bool lo = tig < 2;
+    float x[4] = {(lo && ((present >> (2 * tig)) & 1u)) ? sacc[0] * sl2 : -INFINITY,
+                  (lo && ((present >> (2 * tig + 1)) & 1u)) ? sacc[1] * sl2 : -INFINITY, -INFINITY, -INFINITY};
+    uint32_t pb0, pb1;
+    warp_softmax(st, x, G, pb0, pb1);
+    pb1 = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int d = 16 * j + g;
+        uint32_t a0 = 0u, a1 = 0u;
+        if (lo) {
+            a0 = (uint32_t)V[(2 * tig) * kRawStride + d] | ((uint32_t)V[(2 * tig + 1) * kRawStride + d] << 16);
+            a1 = (uint32_t)V[(2 * tig) * kRawStride + d + 8] | ((uint32_t)V[(2 * tig + 1) * kRawStride + d + 8] << 16);
+        }
+        mma_bf16_16816(st.o[j], a0, a1, 0u, 0u, pb0, pb1);
+    }
+}
+
+// Warp-level issue of up to 4 raw rows into a RAW4 slot: row_of(t) gives the
+// token row offset (in tokens) or -1 when token t of the item is absent.
+template <typename RowOf>
+__device__ __forceinline__ void issue_raw4(uint8_t* slot, uint64_t* bar, const uint16_t* kbase, const uint16_t* vbase,
+                                           RowOf row_of) {
+    const int lane = threadIdx.x & 31;
+    const int t = lane & 3;
+    const int64_t tok = row_of(t);
+    const unsigned present = __ballot_sync(0xffffffffu, tok >= 0) & 0xfu;
+    const int n_present = __popc(present);
+    // zero rows of absent tokens (V must be finite: masked p = 0 multiplies it)
+    for (int i = lane; i < 4 * 16 * 2; i += 32) {
+        const int rowi = (i >> 4) & 3, part = i >> 6, col = i & 15;
+        if (!((present >> rowi) & 1u))
+            *reinterpret_cast<uint4*>(slot + part * kRaw4V + rowi * kRawStride * 2 + col * 16) = make_uint4(0, 0, 0, 0);
+    }
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)n_present * 512u);
+    __syncwarp();
+    if (tok >= 0) {
+        if (lane < 4) bulk_g2s(slot + t * kRawStride * 2, kbase + tok * kHeadDim, 256, bar);
+        else if (lane < 8) bulk_g2s(slot + kRaw4V + t * kRawStride * 2, vbase + tok * kHeadDim, 256, bar);
     }
 }
 
@@ -357,7 +430,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
     int* hist = reinterpret_cast<int*>(co + 8 * kHeadDim);
     int* misc = hist + 512;
     int* scan = misc + 8;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(scan + 2 * kAttnThreads);  // [warps][2] phase 1, [warps][2] phase 3
+    uint64_t* bars = reinterpret_cast<uint64_t*>(scan + 2 * kAttnThreads);  // [warps][2] phase 1, [warps][3] phase 3
     __shared__ int s_failed;
     __shared__ uint32_t s_mm[2 + 2 * 16];  // own (min, max) key; gathered per cluster rank
 
@@ -365,12 +438,13 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
         s_failed = 0;
         s_mm[0] = 0xffffffffu;
         s_mm[1] = 0u;
-        for (int i = 0; i < 4 * kAttnWarps; ++i) mbar_init(bars + i, 1);
+        for (int i = 0; i < (2 + kPSlots) * kAttnWarps; ++i) mbar_init(bars + i, 1);
         mbar_fence_init();
     }
     // Split cluster barrier: arrive now, wait before the first remote
     // shared-memory store, so every peer CTA is known to be running.
     cluster.barrier_arrive();
+    grid_dep_wait();  // inputs may come from the previous kernel on the stream
     // query + GQA-mean query (compute() :1622-1626: bf16 mean over the group)
     for (int i = threadIdx.x; i < a.G * kHeadDim; i += kAttnThreads) q_s[i] = a.q[row * a.G * kHeadDim + i];
     __syncthreads();
@@ -519,18 +593,20 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
     const int n_raw_all = a.n_sink + a.n_near;
     const int n_lo = rank * a.pn, n_hi = min(n_raw_all, n_lo + a.pn);
     const int n_pages = max(0, p_hi - p_lo);
-    const int n_raw = max(0, (n_hi - n_lo + 7) / 8);
+    const int n_raw = max(0, (n_hi - n_lo + 3) / 4);
     const int n_items = n_pages + n_raw;
     const uint16_t* nk_base = reinterpret_cast<const uint16_t*>(a.L.near_k) + row * a.L.near_ld * kHeadDim;
     const uint16_t* nv_base = reinterpret_cast<const uint16_t*>(a.L.near_v) + row * a.L.near_ld * kHeadDim;
-    uint8_t* wslot[2] = {region + (2 * warp) * kSlotBytes, region + (2 * warp + 1) * kSlotBytes};
-    uint64_t* wbar = bars + 2 * kAttnWarps + 2 * warp;
+    uint8_t* wslot[kPSlots];
+#pragma unroll
+    for (int k = 0; k < kPSlots; ++k) wslot[k] = region + (kPSlots * warp + k) * kPSlotBytes;
+    uint64_t* wbar = bars + 2 * kAttnWarps + kPSlots * warp;
     auto issue_item = [&](int it, int k) {
         if (it < n_pages) {
             issue_kivi_page(wslot[k], wbar + k, a.L, row, a.n_max, sel_s[p_lo + it]);
         } else {
-            const int base = n_lo + 8 * (it - n_pages);
-            issue_raw8(wslot[k], wbar + k, nk_base, nv_base, [&](int t) -> int64_t {
+            const int base = n_lo + 4 * (it - n_pages);
+            issue_raw4(wslot[k], wbar + k, nk_base, nv_base, [&](int t) -> int64_t {
                 const int v = base + t;
                 if (v >= n_hi) return -1;
                 return v < a.n_sink ? (int64_t)v : (int64_t)(a.near_start + v - a.n_sink);
@@ -540,28 +616,30 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
     {
         int mine = 0;
         for (int it = warp; it < n_items; it += kAttnWarps) ++mine;
-        if (mine > 0) issue_item(warp, 0);
-        if (mine > 1) issue_item(warp + kAttnWarps, 1);
+#pragma unroll
+        for (int k = 0; k < kPSlots; ++k)
+            if (k < mine) issue_item(warp + k * kAttnWarps, k);
         bool ok = true;
         for (int i = 0; i < mine; ++i) {
             const int it = warp + i * kAttnWarps;
-            const int k = i & 1;
-            if (!mbar_wait(wbar + k, (uint32_t)((i >> 1) & 1), a.status)) ok = false;
+            const int k = i % kPSlots;
+            if (!mbar_wait(wbar + k, (uint32_t)((i / kPSlots) & 1), a.status)) ok = false;
             if (ok) {
                 if (it < n_pages) {
                     warp_page_kivi(st, wslot[k], a.G, a.sl2);
                 } else {
-                    const int base = n_lo + 8 * (it - n_pages);
-                    warp_page_raw8(st, wslot[k], (1u << min(8, n_hi - base)) - 1u, a.G, a.sl2);
+                    const int base = n_lo + 4 * (it - n_pages);
+                    warp_page_raw4(st, wslot[k], (1u << min(4, n_hi - base)) - 1u, a.G, a.sl2);
                 }
             }
             __syncwarp();
-            if (i + 2 < mine) issue_item(it + 2 * kAttnWarps, k);
+            if (i + kPSlots < mine) issue_item(it + kPSlots * kAttnWarps, k);
         }
         if (!ok && lane == 0) atomicOr(&s_failed, 1);
     }
 
     // ------------------------------------------------ phase 4: merge
+    grid_dep_launch_next();
     __syncthreads();
     cta_merge(st, a.G, reinterpret_cast<float*>(region), cm, cl, co);
     cluster_merge(cluster, CS, a.G, cm, cl, co, reinterpret_cast<float*>(region),
@@ -690,7 +768,7 @@ using namespace zkv;
 
 static size_t page_smem(const PageArgs& a) {
     return kRegionBytes + (size_t)a.n_c_pad * 4 + (size_t)((a.nk + 3) & ~3) * 4 + 9 * kHeadDim * 2 +
-           (16 + 8 * kHeadDim) * 4 + (512 + 8 + 2 * kAttnThreads) * 4 + (4 * kAttnWarps) * 8 + 16;
+           (16 + 8 * kHeadDim) * 4 + (512 + 8 + 2 * kAttnThreads) * 4 + ((2 + kPSlots) * kAttnWarps) * 8 + 16;
 }
 
 static int pick_cluster(int requested, int rows) {
@@ -731,7 +809,7 @@ extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int r
     a.n_c_pad = (n_c + 3) & ~3;
     a.per = ((n_c + CS - 1) / CS + 3) & ~3;
     a.pp = (a.nk + CS - 1) / CS;
-    a.pn = ((n_sink + n_near + CS - 1) / CS + 7) & ~7;
+    a.pn = ((n_sink + n_near + CS - 1) / CS + 3) & ~3;
     a.sl2 = scale * 1.4426950408889634f;
     a.out = (uint16_t*)out;
     a.lse = lse;
@@ -742,7 +820,7 @@ extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int r
     a.out_f32 = nullptr;
     void* args[] = {&a};
     return launch_clustered((const void*)page_decode_kernel, rows * CS, kAttnThreads, CS, page_smem(a),
-                            (cudaStream_t)stream, args);
+                            (cudaStream_t)stream, args, /*pdl=*/true);
 }
 
 extern "C" int zkv_page_attend(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max,
@@ -777,7 +855,7 @@ extern "C" int zkv_page_attend(const void* q, const zkv_page_layer* layer, int r
     a.n_c_pad = 0;
     a.per = 0;
     a.pp = (n_sel + CS - 1) / CS;
-    a.pn = ((n_sink + n_near + CS - 1) / CS + 7) & ~7;
+    a.pn = ((n_sink + n_near + CS - 1) / CS + 3) & ~3;
     a.sl2 = scale * 1.4426950408889634f;
     a.out = (uint16_t*)out;
     a.lse = lse;
@@ -789,7 +867,7 @@ extern "C" int zkv_page_attend(const void* q, const zkv_page_layer* layer, int r
     a.out_f32 = out_f32;
     void* args[] = {&a};
     return launch_clustered((const void*)page_decode_kernel, rows * CS, kAttnThreads, CS, page_smem(a),
-                            (cudaStream_t)stream, args);
+                            (cudaStream_t)stream, args, /*pdl=*/true);
 }
 
 extern "C" int zkv_attn_rows(const void* q, const void* keys, const void* values, int64_t kv_ld_row, int rows, int G,
