@@ -50,11 +50,13 @@ int zkv_version(void);
  *   keys      row r, token t at keys + r*keys_ld_row + t*128 (bf16)
  *   chunk_min, chunk_max, centroid  [rows][n_max][128] bf16 (centroid may be NULL)
  *   valid     [rows][n_max] uint8 (may be NULL; set to 1)
- *   packed    [rows][n_max][16][16] int32 (chunk-major A-1 layout)      */
+ *   packed    [rows][n_max][16][16] int32 (chunk-major A-1 layout)
+ *   kscale    [rows][n_max][128] bf16 KIVI scale bf16(bf16(max-min)/15) per
+ *             chunk and dim (may be NULL; the page-mode attention reads it) */
 int zkv_kivi_encode(const void* keys, int64_t keys_ld_row, int rows,
                     int n_chunks, int chunk_start, int n_max, void* chunk_min,
                     void* chunk_max, void* centroid, uint8_t* valid,
-                    int32_t* packed, void* stream);
+                    int32_t* packed, void* kscale, void* stream);
 
 /* Per-token 4-bit value quantisation (group 32 along head_dim), written for
  * tokens [tok_start, tok_start + n_tokens) of each row in the page layout the
@@ -238,6 +240,7 @@ typedef struct zkv_page_layer {
     const void* near_k;     /* [rows][near_ld][128] bf16 raw rows (sink +   */
     const void* near_v;     /*   residual window), row r at r*near_ld*128   */
     int64_t near_ld;        /* token capacity of the near buffers            */
+    const void* kscale;     /* [rows][n_max][128] bf16 KIVI scales           */
 } zkv_page_layer;
 
 /* One fused launch per layer: GQA-mean query -> Quest scores over n_c

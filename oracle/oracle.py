@@ -22,7 +22,7 @@ __all__ = [
     "build_oracle", "lib", "bf16_to_f32", "f32_to_bf16", "kivi_encode_chunks", "vquant_tokens",
     "quest_score", "topk_f32", "topk_i32", "chunk_density", "mask_from_topk", "kivi_qk",
     "topk_gather_concat", "attn_dense", "page_decode", "lse_merge", "kivi_dequant_chunk",
-    "vdequant_tokens", "page_layout_values", "rq_mag_tables", "rq_encode", "rq_query", "collision_weights",
+    "vdequant_tokens", "page_layout_values", "kivi_scale", "rq_mag_tables", "rq_encode", "rq_query", "collision_weights",
     "collision_count", "update_cache_cnt_sorted", "rerank4", "coarse2bit", "rq_query_4bit", "popcount_est",
     "exact_ip",
 ]
@@ -98,6 +98,11 @@ def vquant_tokens(v: np.ndarray, group: int = 32):
     meta = np.empty((flat.shape[0], D // group, 2), np.uint16)
     L.orc_vquant_rows(_p(flat), ctypes.c_int64(flat.shape[0]), D, group, _p(codes), _p(meta))
     return codes.reshape(v.shape[:-1] + (D // 8,)), meta.reshape(v.shape[:-1] + (D // group, 2))
+
+
+def kivi_scale(mn: np.ndarray, mx: np.ndarray) -> np.ndarray:
+    """KIVI key scale bf16(bf16(mx - mn) / 15) per chunk and dim (quant_pack.py:64)."""
+    return _scale_ladder(mn, mx)
 
 
 def _scale_ladder(mn: np.ndarray, mx: np.ndarray) -> np.ndarray:

@@ -50,10 +50,12 @@ def test_kivi_encode_matches_oracle(chunk_start, n_chunks):
     k = rand_keys(11 + chunk_start, 2, 3, 16 * n_chunks)
     n_max = chunk_start + n_chunks + 3
     pc = W.alloc_page_cache(2, 3, n_max, 1, DEV)
-    ops.kivi_encode_chunks(k, pc.chunk_min, pc.chunk_max, pc.centroid, pc.valid, pc.kcodes, chunk_start)
+    ops.kivi_encode_chunks(k, pc.chunk_min, pc.chunk_max, pc.centroid, pc.valid, pc.kcodes, chunk_start,
+                           kscale=pc.kscale)
     torch.cuda.synchronize()
     mn, mx, ce, pk = O.kivi_encode_chunks(to_u16(k))
     sl = slice(chunk_start, chunk_start + n_chunks)
+    assert (to_u16(pc.kscale)[:, :, sl] == O.kivi_scale(mn, mx)).all()
     assert (to_u16(pc.chunk_min)[:, :, sl] == mn).all()
     assert (to_u16(pc.chunk_max)[:, :, sl] == mx).all()
     assert (to_u16(pc.centroid)[:, :, sl] == ce).all()

@@ -27,7 +27,7 @@ class ZkvPageLayer(ctypes.Structure):
     _fields_ = [
         ("chunk_min", _c_void_p), ("chunk_max", _c_void_p), ("valid", _c_void_p),
         ("kcodes", _c_void_p), ("vcodes_t", _c_void_p), ("vmeta", _c_void_p),
-        ("near_k", _c_void_p), ("near_v", _c_void_p), ("near_ld", _i64),
+        ("near_k", _c_void_p), ("near_v", _c_void_p), ("near_ld", _i64), ("kscale", _c_void_p),
     ]
 
 
@@ -52,7 +52,7 @@ _RQ = ctypes.POINTER(ZkvRqLayout)
 # name -> argtypes (restype is int status unless noted)
 _SIGNATURES = {
     "zkv_kivi_encode": [_c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
-                        _c_void_p, _c_void_p],
+                        _c_void_p, _c_void_p, _c_void_p],
     "zkv_vquant_encode": [_c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p],
     "zkv_quest_score": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p],
     "zkv_topk_f32": [_c_void_p, _i32, _i32, _i64, _i32, _c_void_p, _c_void_p],

@@ -24,7 +24,7 @@ constexpr int kAttnThreads = 32 * kAttnWarps;
 constexpr int kRawStride = 136;  // bf16 per padded staged row (272 B, conflict-free B-fragment loads)
 constexpr int kSlotBytes = 4608; // per-warp staging slot (2 per warp)
 // KIVI page slot: kc [16][16] i32 @0, vc [128][2] i32 @1024, vmeta @2048,
-//                 min @2304, max @2560, scale (computed) @2816
+//                 min @2304, KIVI scale @2560 (2816 B)
 constexpr int kPageTx = 1024 + 1024 + 256 + 256 + 256;
 // RAW8 slot: K rows [8][136] bf16 @0, V rows @2176
 constexpr int kRawV = 8 * kRawStride * 2;
@@ -104,24 +104,9 @@ __device__ __forceinline__ void warp_softmax(WarpAttn& st, float (&x)[4], int G,
 // KIVI page: 16 tokens, 4-bit K (chunk-major) + 4-bit V (page-transposed).
 __device__ __forceinline__ void warp_page_kivi(WarpAttn& st, uint8_t* slot, int G, float sl2) {
     const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
-    // per-dim KIVI scale of this chunk: bf16(bf16(max - min) / 15)
-    {
-        const uint16_t* mn = reinterpret_cast<const uint16_t*>(slot + 2304);
-        const uint16_t* mx = reinterpret_cast<const uint16_t*>(slot + 2560);
-        uint16_t* sc = reinterpret_cast<uint16_t*>(slot + 2816);
-        const uint2 a = *reinterpret_cast<const uint2*>(mn + 4 * lane);
-        const uint2 b = *reinterpret_cast<const uint2*>(mx + 4 * lane);
-        const uint16_t s0 = kivi_scale_bits((uint16_t)(a.x & 0xffff), (uint16_t)(b.x & 0xffff));
-        const uint16_t s1 = kivi_scale_bits((uint16_t)(a.x >> 16), (uint16_t)(b.x >> 16));
-        const uint16_t s2 = kivi_scale_bits((uint16_t)(a.y & 0xffff), (uint16_t)(b.y & 0xffff));
-        const uint16_t s3 = kivi_scale_bits((uint16_t)(a.y >> 16), (uint16_t)(b.y >> 16));
-        *reinterpret_cast<uint2*>(sc + 4 * lane) =
-            make_uint2((uint32_t)s0 | ((uint32_t)s1 << 16), (uint32_t)s2 | ((uint32_t)s3 << 16));
-        __syncwarp();
-    }
     const int32_t* kc = reinterpret_cast<const int32_t*>(slot);
     const uint32_t* mn2 = reinterpret_cast<const uint32_t*>(slot + 2304);
-    const uint32_t* sc2 = reinterpret_cast<const uint32_t*>(slot + 2816);
+    const uint32_t* sc2 = reinterpret_cast<const uint32_t*>(slot + 2560);  // per-dim KIVI scale
     const uint32_t sel = nib_sel(tig);
     // S = Q K^T over 8 k-steps of 16 dims; the two k-halves accumulate
     // separately (4 independent MMA chains of 4 instead of 2 of 8) and are
@@ -274,7 +259,7 @@ __device__ __forceinline__ void issue_kivi_page(uint8_t* slot, uint64_t* bar, co
         bulk_g2s(slot + 1024, L.vcodes_t + pc * (kHeadDim * 2), 1024, bar);
         bulk_g2s(slot + 2048, reinterpret_cast<const uint16_t*>(L.vmeta) + pc * (2 * kVGroups * kChunk), 256, bar);
         bulk_g2s(slot + 2304, reinterpret_cast<const uint16_t*>(L.chunk_min) + pc * kHeadDim, 256, bar);
-        bulk_g2s(slot + 2560, reinterpret_cast<const uint16_t*>(L.chunk_max) + pc * kHeadDim, 256, bar);
+        bulk_g2s(slot + 2560, reinterpret_cast<const uint16_t*>(L.kscale) + pc * kHeadDim, 256, bar);
     }
 }
 
@@ -788,10 +773,11 @@ extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int r
     if (n_c > 16384 || nk > 2048) return ZKV_ERR_CAPACITY;
     if (rows == 0) return ZKV_OK;
     const zkv_page_layer& L = *layer;
-    if (!L.chunk_min || !L.chunk_max || !L.kcodes || !L.vcodes_t || !L.vmeta ||
+    if (!L.chunk_min || !L.chunk_max || !L.kscale || !L.kcodes || !L.vcodes_t || !L.vmeta ||
         (n_near + n_sink > 0 && (!L.near_k || !L.near_v)))
         return ZKV_ERR_ARG;
-    if (((uintptr_t)L.chunk_min & 15) || ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)L.kcodes & 15) ||
+    if (((uintptr_t)L.chunk_min & 15) || ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)L.kscale & 15) ||
+        ((uintptr_t)L.kcodes & 15) ||
         ((uintptr_t)L.vcodes_t & 15) || ((uintptr_t)L.vmeta & 15) || ((uintptr_t)L.near_k & 15) ||
         ((uintptr_t)L.near_v & 15) || ((uintptr_t)q & 3))
         return ZKV_ERR_ALIGN;
@@ -834,10 +820,11 @@ extern "C" int zkv_page_attend(const void* q, const zkv_page_layer* layer, int r
     if (n_sel > 4096) return ZKV_ERR_CAPACITY;
     if (rows == 0) return ZKV_OK;
     const zkv_page_layer& L = *layer;
-    if (!L.kcodes || !L.vcodes_t || !L.vmeta || !L.chunk_min || !L.chunk_max ||
+    if (!L.kcodes || !L.vcodes_t || !L.vmeta || !L.chunk_min || !L.chunk_max || !L.kscale ||
         (n_near + n_sink > 0 && (!L.near_k || !L.near_v)))
         return ZKV_ERR_ARG;
-    if (((uintptr_t)L.chunk_min & 15) || ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)L.kcodes & 15) ||
+    if (((uintptr_t)L.chunk_min & 15) || ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)L.kscale & 15) ||
+        ((uintptr_t)L.kcodes & 15) ||
         ((uintptr_t)L.vcodes_t & 15) || ((uintptr_t)L.vmeta & 15) || ((uintptr_t)L.near_k & 15) ||
         ((uintptr_t)L.near_v & 15) || ((uintptr_t)q & 3))
         return ZKV_ERR_ALIGN;

@@ -19,7 +19,7 @@ __global__ void __launch_bounds__(256) kivi_encode_kernel(const uint16_t* __rest
                                                           int rows, int n_chunks, int chunk_start, int n_max,
                                                           uint16_t* __restrict__ cmin, uint16_t* __restrict__ cmax,
                                                           uint16_t* __restrict__ cent, uint8_t* __restrict__ valid,
-                                                          int32_t* __restrict__ packed) {
+                                                          int32_t* __restrict__ packed, uint16_t* __restrict__ kscale) {
     const int lane = threadIdx.x & 31;
     const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int n_warps = gridDim.x * (blockDim.x >> 5);
@@ -61,6 +61,9 @@ __global__ void __launch_bounds__(256) kivi_encode_kernel(const uint16_t* __rest
         if (cent)
             *reinterpret_cast<uint2*>(cent + mrow) =
                 make_uint2((uint32_t)ce[0] | ((uint32_t)ce[1] << 16), (uint32_t)ce[2] | ((uint32_t)ce[3] << 16));
+        if (kscale)
+            *reinterpret_cast<uint2*>(kscale + mrow) =
+                make_uint2((uint32_t)sc[0] | ((uint32_t)sc[1] << 16), (uint32_t)sc[2] | ((uint32_t)sc[3] << 16));
         // codes: lane holds 4 dims = half a word; pair lanes (2w, 2w+1) form word w.
         int32_t* pk = packed + ((int64_t)r * n_max + chunk_start + c) * (kWords * kChunk);
 #pragma unroll
@@ -149,17 +152,17 @@ using namespace zkv;
 
 extern "C" int zkv_kivi_encode(const void* keys, int64_t keys_ld_row, int rows, int n_chunks, int chunk_start,
                                int n_max, void* chunk_min, void* chunk_max, void* centroid, uint8_t* valid,
-                               int32_t* packed, void* stream) {
+                               int32_t* packed, void* kscale, void* stream) {
     if (rows < 0 || n_chunks < 0 || chunk_start < 0 || chunk_start + n_chunks > n_max) return ZKV_ERR_ARG;
     if (rows == 0 || n_chunks == 0) return ZKV_OK;
     if (!keys || !chunk_min || !chunk_max || !packed) return ZKV_ERR_ARG;
     if (((uintptr_t)keys & 7) || (keys_ld_row & 3) || ((uintptr_t)chunk_min & 7) || ((uintptr_t)chunk_max & 7) ||
-        (centroid && ((uintptr_t)centroid & 7)) || ((uintptr_t)packed & 3))
+        (centroid && ((uintptr_t)centroid & 7)) || (kscale && ((uintptr_t)kscale & 7)) || ((uintptr_t)packed & 3))
         return ZKV_ERR_ALIGN;
     const int64_t jobs = (int64_t)rows * n_chunks;
     kivi_encode_kernel<<<grid_for(jobs, 8), 256, 0, (cudaStream_t)stream>>>(
         (const uint16_t*)keys, keys_ld_row, rows, n_chunks, chunk_start, n_max, (uint16_t*)chunk_min,
-        (uint16_t*)chunk_max, (uint16_t*)centroid, valid, packed);
+        (uint16_t*)chunk_max, (uint16_t*)centroid, valid, packed, (uint16_t*)kscale);
     return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH;
 }
 

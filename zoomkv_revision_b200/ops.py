@@ -332,10 +332,11 @@ def lse_merge_n(parts: torch.Tensor, lses: torch.Tensor, out: torch.Tensor, lse_
 
 
 # ----------------------------------------------------------------- encode
-def kivi_encode_chunks(keys, chunk_min, chunk_max, chunk_centroid, chunk_valid, packed, chunk_start: int):
+def kivi_encode_chunks(keys, chunk_min, chunk_max, chunk_centroid, chunk_valid, packed, chunk_start: int,
+                       kscale=None):
     """Write metadata + KIVI codes of the aligned chunks of `keys` [bs,kv,T,128]
     (T % 16 == 0; token stride 128) at chunk indices chunk_start.. of the
-    [bs,kv,n_max,...] buffers."""
+    [bs,kv,n_max,...] buffers (+ the KIVI scales when kscale is given)."""
     _dtype("keys", keys, torch.bfloat16)
     bs, kv, T, D = keys.shape
     if D != 128 or T % 16:
@@ -346,7 +347,8 @@ def kivi_encode_chunks(keys, chunk_min, chunk_max, chunk_centroid, chunk_valid, 
     for n, t in (("chunk_min", chunk_min), ("chunk_max", chunk_max), ("packed", packed)):
         _contig(n, t)
     check(lib().zkv_kivi_encode(_p(keys), keys.stride(1), bs * kv, T // 16, int(chunk_start), n_max, _p(chunk_min),
-                                _p(chunk_max), _p(chunk_centroid), _p(chunk_valid), _p(packed), _stream(keys)),
+                                _p(chunk_max), _p(chunk_centroid), _p(chunk_valid), _p(packed), _p(kscale),
+                                _stream(keys)),
           "zkv_kivi_encode")
 
 
@@ -392,11 +394,11 @@ def attn_rows(q, keys, values, *, seg0=(0, 0), sel=None, sel_offset=0, seg1=(0, 
 class PageLayer:
     """Tensors of one layer of the page-mode cache ([bs, H, ...] each)."""
 
-    def __init__(self, chunk_min, chunk_max, valid, kcodes, vcodes_t, vmeta, near_k, near_v):
-        self.tensors = (chunk_min, chunk_max, valid, kcodes, vcodes_t, vmeta, near_k, near_v)
+    def __init__(self, chunk_min, chunk_max, valid, kcodes, vcodes_t, vmeta, near_k, near_v, kscale):
+        self.tensors = (chunk_min, chunk_max, valid, kcodes, vcodes_t, vmeta, near_k, near_v, kscale)
         self.struct = _lib.ZkvPageLayer(
             _p(chunk_min), _p(chunk_max), _p(valid), _p(kcodes), _p(vcodes_t), _p(vmeta), _p(near_k), _p(near_v),
-            near_k.shape[2])
+            near_k.shape[2], _p(kscale))
 
 
 def page_decode(q, layer: PageLayer, n_c: int, nk: int, n_near: int, *, n_sink: int = 0, near_start: int = 0,

@@ -308,7 +308,7 @@ class polar_cache:
         bs, H, D, nm = batch_size, num_key_value_heads, head_dim, self._n_max
         self.keys, self.values = [], []
         self.chunk_min, self.chunk_max, self.chunk_centroid, self.chunk_valid, self.kivi_packed = [], [], [], [], []
-        self.vcodes_t, self.vmeta = [], []
+        self.vcodes_t, self.vmeta, self.kscale = [], [], []
         for l in range(layer_num):
             d = dict(device=self._layer_dev[l])
             self.keys.append(torch.zeros(bs, H, self.cap, D, dtype=torch.bfloat16, **d))
@@ -321,6 +321,7 @@ class polar_cache:
             if self.attention_mode == "page":
                 self.vcodes_t.append(torch.zeros(bs, H, nm, D, 2, dtype=torch.int32, **d))
                 self.vmeta.append(torch.zeros(bs, H, nm, 2, 4, 16, dtype=torch.bfloat16, **d))
+                self.kscale.append(torch.zeros(bs, H, nm, D, dtype=torch.bfloat16, **d))
         # per-device scratch for the decode pipeline (preallocated: no
         # allocation on the decode path)
         self._scratch = {}
@@ -374,7 +375,8 @@ class polar_cache:
         s = self.sink_size
         k = self.keys[l][rows, :, s + tok_lo:s + tok_hi]
         ops.kivi_encode_chunks(k, self.chunk_min[l][rows], self.chunk_max[l][rows], self.chunk_centroid[l][rows],
-                               self.chunk_valid[l][rows], self.kivi_packed[l][rows], tok_lo // CHUNK)
+                               self.chunk_valid[l][rows], self.kivi_packed[l][rows], tok_lo // CHUNK,
+                               kscale=self.kscale[l][rows] if self.attention_mode == "page" else None)
         if self.attention_mode == "page":
             v = self.values[l][rows, :, s + tok_lo:s + tok_hi]
             ops.vquant_encode(v, self.vcodes_t[l][rows], self.vmeta[l][rows], tok_lo)
@@ -508,7 +510,7 @@ class polar_cache:
         if self._page_layers[l] is None:
             self._page_layers[l] = ops.PageLayer(self.chunk_min[l], self.chunk_max[l], self.chunk_valid[l],
                                                  self.kivi_packed[l], self.vcodes_t[l], self.vmeta[l], self.keys[l],
-                                                 self.values[l])
+                                                 self.values[l], self.kscale[l])
         s = self.sink_size
         near_start = s + n_chunks * CHUNK
         return ops.page_decode(q, self._page_layers[l], n_chunks, nk, total - near_start, n_sink=s,

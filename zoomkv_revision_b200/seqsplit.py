@@ -140,4 +140,4 @@ def local_layer(layer: ops.PageLayer, lo: int, hi: int) -> ops.PageLayer:
     """View of pages [lo, hi) of a full layer as a rank-local layer."""
     t = layer.tensors
     cut = [x[:, :, lo:max(hi, lo + 1)] for x in t[:6]]
-    return ops.PageLayer(*cut, t[6], t[7])
+    return ops.PageLayer(*cut, t[6], t[7], t[8][:, :, lo:max(hi, lo + 1)])

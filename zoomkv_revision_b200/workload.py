@@ -71,6 +71,7 @@ class PageCache:
     kcodes: torch.Tensor      # [bs,H,n_max,16,16] int32
     vcodes_t: torch.Tensor    # [bs,H,n_max,128,2] int32
     vmeta: torch.Tensor       # [bs,H,n_max,2,4,16] bf16
+    kscale: torch.Tensor      # [bs,H,n_max,128] bf16 KIVI key scales
     near_k: torch.Tensor      # [bs,H,near_cap,128] bf16
     near_v: torch.Tensor
     n_c: int
@@ -78,7 +79,7 @@ class PageCache:
 
     def layer(self) -> ops.PageLayer:
         return ops.PageLayer(self.chunk_min, self.chunk_max, self.valid, self.kcodes, self.vcodes_t, self.vmeta,
-                             self.near_k, self.near_v)
+                             self.near_k, self.near_v, self.kscale)
 
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in (self.chunk_min, self.chunk_max, self.kcodes, self.vcodes_t,
@@ -95,6 +96,7 @@ def alloc_page_cache(bs: int, heads: int, n_max: int, near_cap: int, device) -> 
         kcodes=torch.zeros(bs, heads, n_max, 16, 16, dtype=torch.int32, **z),
         vcodes_t=torch.zeros(bs, heads, n_max, HEAD_DIM, 2, dtype=torch.int32, **z),
         vmeta=torch.zeros(bs, heads, n_max, 2, 4, 16, dtype=torch.bfloat16, **z),
+        kscale=torch.zeros(bs, heads, n_max, HEAD_DIM, dtype=torch.bfloat16, **z),
         near_k=torch.zeros(bs, heads, near_cap, HEAD_DIM, dtype=torch.bfloat16, **z),
         near_v=torch.zeros(bs, heads, near_cap, HEAD_DIM, dtype=torch.bfloat16, **z),
         n_c=0, n_near=0)
@@ -117,7 +119,8 @@ def build_page_cache(seed: int, bs: int, heads: int, n_retrieval: int, n_near: i
         g2 = torch.Generator(device=device).manual_seed(seed * 1000003 + t0)
         k = synth_keys(g2, bs, heads, t1 - t0, device, pos0=t0, channels=chans)
         v = synth_values(g2, bs, heads, t1 - t0, device)
-        ops.kivi_encode_chunks(k, pc.chunk_min, pc.chunk_max, pc.centroid, pc.valid, pc.kcodes, t0 // CHUNK)
+        ops.kivi_encode_chunks(k, pc.chunk_min, pc.chunk_max, pc.centroid, pc.valid, pc.kcodes, t0 // CHUNK,
+                               kscale=pc.kscale)
         ops.vquant_encode(v, pc.vcodes_t, pc.vmeta, t0)
         if keep_raw:
             raw_k.append(k)
