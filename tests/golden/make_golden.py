@@ -31,6 +31,8 @@ Functions pinned (paths relative to runtime/zoomkv_urania_runtime_20261011/):
   * update_cache_cnt_overall_ref / generate_test_input
     (cache_hub/collision_fused/collision_test.py:17-121)
   * python_rabitq_scores / make_inputs (cache_hub/rerank/test_rerank_topk.py:27-111)
+  * ParisKV's prefill / decode_update / flush state machine
+    (cache_hub/polar_cache.py:523-657, 837-853, 919-1065) driven step by step
 """
 from __future__ import annotations
 
@@ -379,6 +381,82 @@ def gen_rabitq(pmod, ref_root, out):
         cnt=cnt2.numpy())
 
 
+def gen_pariskv_schedule(pmod, out):
+    """Drive ParisKV's own prefill / decode_update / _update_polar_index /
+    get_region_indices (cache_hub/polar_cache.py:523-657, 837-853, 919-1065)
+    on CPU tensors through a stub: 2 layers, batch 2, 2 KV heads; record the
+    per-step state and the final retrieval codes and bucket counts."""
+    pc = pmod.polar_cache
+    L, bs, H, D = 2, 2, 2, 128
+    sink, local, interval = 4, 40, 24
+    prefill, steps, max_new = 150, 100, 120
+    g = torch.Generator().manual_seed(77)
+    T = prefill + steps
+    layer_keys = [(torch.randn(bs, H, T, D, generator=g) * 1.5).to(torch.bfloat16) for _ in range(L)]
+    vals = torch.randn(bs, H, T, D, generator=g).to(torch.bfloat16)
+    torch.manual_seed(42)
+    signs = torch.randint(0, 2, (128,), dtype=torch.bfloat16) * 2 - 1
+    s = rabitq_stub(pmod, signs)
+    cap = prefill + max_new
+    s.layer_num, s.batch_size, s.kv_head, s.head_dim, s.dtype = L, bs, H, D, torch.bfloat16
+    s.sink_size, s.local_size, s.steady_size = sink, local, sink + local
+    s.dynamic_update_interval = interval
+    s.input_length, s.max_new_length = prefill, max_new
+    s.valid_start = [0, 0]
+    s.enable_offload = True
+    s.gpu_kv_capacity = sink + local + interval
+    s.unified_keys_gpu = [torch.zeros(bs, H, s.gpu_kv_capacity, D, dtype=torch.bfloat16) for _ in range(L)]
+    s.unified_values_gpu = [torch.zeros(bs, H, s.gpu_kv_capacity, D, dtype=torch.bfloat16) for _ in range(L)]
+    s.unified_keys_cpu = [torch.zeros(bs, H, cap, D, dtype=torch.bfloat16) for _ in range(L)]
+    s.unified_values_cpu = [torch.zeros(bs, H, cap, D, dtype=torch.bfloat16) for _ in range(L)]
+    s._offload_keys_buffer = [torch.zeros(bs, H, interval, D, dtype=torch.bfloat16) for _ in range(L)]
+    s._offload_values_buffer = [torch.zeros(bs, H, interval, D, dtype=torch.bfloat16) for _ in range(L)]
+    s.codebook_gpu = [torch.zeros(bs, H, 16, cap, dtype=torch.uint8) for _ in range(L)]
+    s.key_block_weight_gpu = [torch.zeros(bs, H, 16, cap, dtype=torch.bfloat16) for _ in range(L)]
+    s.key_4bit_packed_gpu = [torch.zeros(bs, H, 16, cap, 4, dtype=torch.uint8) for _ in range(L)]
+    s.cluster_key_counts_gpu = [torch.zeros(bs, H, 16, 256, dtype=torch.int32) for _ in range(L)]
+    s.cpu_valid_end = [0] * L
+    s._inflight_offload_buffers = [None] * L
+    s._layer_offload_inflight = [False] * L
+    s._main_events = [_Ev() for _ in range(L)]
+    s._copy_events = [_Ev() for _ in range(L)]
+    s._copy_stream = None
+    s.current_seq_len = [0] * L
+    s.context = 0
+    s._decode_step_counter = 0
+    s.final_topk = 100
+    s.device = torch.device("cpu")
+    s._actual_retrieval_length = max(sink, prefill - local) - sink   # skips the pinned-buffer allocation
+    for name in ("batch_encode", "_count_cluster_keys", "_compute_local_start", "get_region_indices",
+                 "_update_polar_index", "decode_update_kv_cache", "_sync_layer_offload", "_prefill_lockstep_batch"):
+        setattr(s, name, functools.partial(getattr(pc, name), s))
+    s._sync_offload_copies = lambda: None
+    for l in range(L):
+        s._prefill_lockstep_batch(layer_keys[l][:, :, :prefill].transpose(1, 2).contiguous(),
+                                  vals[:, :, :prefill].transpose(1, 2).contiguous(), l)
+    trace = []
+    for t in range(steps):
+        pos = prefill + t
+        for l in range(L):
+            s.decode_update_kv_cache(layer_keys[l][:, :, pos:pos + 1].transpose(1, 2).contiguous(),
+                                     vals[:, :, pos:pos + 1].transpose(1, 2).contiguous(), l)
+            reg = s.get_region_indices(l)
+            trace.append([t, l, int(reg["total_len"]), int(reg["retrieval_length"]), int(reg["local_len"]),
+                          int(s.cpu_valid_end[l]), int(s._actual_retrieval_length)])
+    n = s._actual_retrieval_length
+    np.savez_compressed(
+        os.path.join(out, "pariskv_schedule.npz"),
+        keys=np.stack([bf16_bits(k) for k in layer_keys]), values=bf16_bits(vals), signs=bf16_bits(signs),
+        trace=np.array(trace, np.int64), params=np.array([L, bs, H, sink, local, interval, prefill, steps, max_new]),
+        codes=np.stack([s.codebook_gpu[l][:, :, :, sink:sink + n].permute(0, 1, 3, 2).contiguous().numpy()
+                        for l in range(L)]),
+        weight=np.stack([bf16_bits(s.key_block_weight_gpu[l][:, :, :, sink:sink + n].permute(0, 1, 3, 2))
+                         for l in range(L)]),
+        packed=np.stack([s.key_4bit_packed_gpu[l][:, :, :, sink:sink + n].permute(0, 1, 3, 2, 4).contiguous().numpy()
+                         for l in range(L)]),
+        hist=np.stack([s.cluster_key_counts_gpu[l].numpy() for l in range(L)]))
+
+
 def gen_rerank4(ref_root, out):
     """Sequential-bf16 RaBitQ rerank scores from the reference's own test."""
     sys.path.insert(0, os.path.join(ref_root, RUNTIME, "cache_hub/rerank"))
@@ -411,6 +489,7 @@ def main():
     gen_schedule(zmod, a.out)
     import cache_hub.polar_cache as pmod
     gen_rabitq(pmod, a.ref, a.out)
+    gen_pariskv_schedule(pmod, a.out)
     gen_rerank4(a.ref, a.out)
     print("golden fixtures written to", a.out)
 

@@ -480,9 +480,20 @@ class RqLayout:
 
     def __init__(self, codes, packed, weight, factor, hist, strides):
         self.codes, self.packed, self.weight, self.factor, self.hist = codes, packed, weight, factor, hist
+        self._strides = strides
         (cr, cb, ct), (pr, pb, pt), (wr, wb, wt), fr = strides
         self._s = _lib.ZkvRqLayout(
             _p(codes), cr, cb, ct, _p(packed), pr, pb, pt, _p(weight), wr, wb, wt, _p(factor), fr, _p(hist))
+
+    def tokens(self, lo: int) -> "RqLayout":
+        """The same layout with token 0 at token `lo` (token-major buffers of
+        `alloc`): kernels then index keys relative to `lo`."""
+        (cr, cb, ct), (pr, pb, pt), (wr, wb, wt), fr = self._strides
+        if not (cb == 1 and ct == 16 and pb == 1 and pt == 16):
+            raise ValueError("tokens(): token-major layouts only")
+        v = RqLayout(self.codes[:, lo:], self.packed[:, lo:], self.weight[:, lo:],
+                     None if self.factor is None else self.factor[:, lo:], self.hist, self._strides)
+        return v
 
     @classmethod
     def alloc(cls, rows: int, cap: int, device) -> "RqLayout":
