@@ -691,19 +691,19 @@ static int launch_clustered(const void* fn, int nblocks, int nthreads, int CS, s
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
     // raise the dynamic shared-memory limit once per (kernel, device, size)
-    static thread_local const void* last_fn[4] = {nullptr, nullptr, nullptr, nullptr};
-    static thread_local size_t last_smem[4] = {0, 0, 0, 0};
-    static thread_local int last_dev[4] = {-1, -1, -1, -1};
+    static thread_local const void* last_fn[8] = {};
+    static thread_local size_t last_smem[8] = {};
+    static thread_local int last_dev[8] = {-1, -1, -1, -1, -1, -1, -1, -1};
     int dev = 0;
     cudaGetDevice(&dev);
     int slot = -1;
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 8; ++i)
         if (last_fn[i] == fn && last_dev[i] == dev) slot = i;
     if (slot < 0 || last_smem[slot] < smem) {
         if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return ZKV_ERR_LAUNCH;
         if (slot < 0) {
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 8; ++i)
                 if (!last_fn[i]) {
                     slot = i;
                     break;

@@ -363,45 +363,110 @@ __device__ __forceinline__ void collision_table(const CollArgs& a, int row, int 
     }
 }
 
-__global__ void __launch_bounds__(256) collision_topk_kernel(const CollArgs a) {
+// Sum of the 16 per-block tier weights of one token's codes (one byte per
+// block, block b at byte b of the 16-byte record).
+__device__ __forceinline__ int count16(const uint8_t* table, const uint4 w) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    int c = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t x = ws[j];
+        const uint8_t* t = table + 4 * j * kK;
+        c += (int)t[x & 0xffu] + (int)t[kK + __byte_perm(x, 0u, 0x4441u)] +
+             (int)t[2 * kK + __byte_perm(x, 0u, 0x4442u)] + (int)t[3 * kK + (x >> 24)];
+    }
+    return c;
+}
+
+// Exclusive prefix, in place, of v[0..nv) over the CTA (thread t owns a
+// contiguous run of entries); returns the total.
+__device__ __forceinline__ int block_excl_scan_array(int* v, int nv, int* scratch) {
+    const int E = (nv + 255) / 256;
+    const int e0 = min(nv, (int)threadIdx.x * E), e1 = min(nv, e0 + E);
+    int s = 0;
+    for (int e = e0; e < e1; ++e) s += v[e];
+    int tot;
+    int run = block_excl_scan<256>(s, scratch, &tot);
+    for (int e = e0; e < e1; ++e) {
+        const int x = v[e];
+        v[e] = run;
+        run += x;
+    }
+    __syncthreads();
+    return tot;
+}
+
+// One cluster of CS CTAs per row, CTA r counting keys [r*per, (r+1)*per).
+// The 16 per-block weight tables are built once per cluster (block b by CTA
+// b % CS) and pushed to every peer through distributed shared memory.
+__global__ void __launch_bounds__(256, 4) collision_topk_kernel(const CollArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     uint8_t* table = smem;                                     // [16][256]
     int* hist = reinterpret_cast<int*>(smem + kB * kK);        // [kCntBins] (pad 136)
     int* gh = hist + 136;                                      // global histogram [136]
     int* scratch = gh + 136;                                   // 40
     int* misc = scratch + 40;                                  // 24: vstar, n_gt, eq_r[8], gt_r[8]
-    uint8_t* cnts = reinterpret_cast<uint8_t*>(misc + 24);     // [per]
+    uint8_t* cnts = reinterpret_cast<uint8_t*>(misc + 24);     // [per] (padded to 16)
     cg::cluster_group cluster = cg::this_cluster();
     const int CS = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
     const int row = blockIdx.x / CS;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int k0 = rank * a.per;
     const int n = max(0, min(a.kv_len, k0 + a.per) - k0);
+    const int nch = (n + 31) / 32;                             // 32-key chunks
+    uint32_t* gtm = reinterpret_cast<uint32_t*>(cnts + ((a.per + 15) & ~15));  // [nch] masks
+    uint32_t* eqm = gtm + nch;
+    int* eqc = reinterpret_cast<int*>(eqm + nch);              // [nch] scanned counts
+    int* selc = eqc + nch;
 
-    for (int b = warp; b < kB; b += 8) collision_table(a, row, b, table);
+    cluster.barrier_arrive();  // peers are running before the first remote store
+    for (int b = rank + CS * warp; b < kB; b += CS * 8) collision_table(a, row, b, table);
     for (int i = tid; i < 136; i += 256) hist[i] = 0;
     if (tid < 24) misc[tid] = 0;
-    __syncthreads();
+    cluster.barrier_wait();
+    for (int b = rank + CS * warp; b < kB; b += CS * 8) {
+        __syncwarp();
+        const uint4* src = reinterpret_cast<const uint4*>(table + b * kK);
+        for (int t = lane; t < 16 * CS; t += 32) {
+            const int p = t >> 4;
+            if (p != rank) reinterpret_cast<uint4*>(cluster.map_shared_rank(table, p) + b * kK)[t & 15] = src[t & 15];
+        }
+    }
+    cluster.sync();  // every table is complete in every CTA
 
     const bool tokmajor = a.L.codes_blk == 1 && a.L.codes_tok == 16;
     const uint8_t* cb = a.L.codes + row * a.L.codes_row;
-    for (int i = tid; i < n; i += 256) {
-        const int64_t k = k0 + i;
-        int c = 0;
-        if (tokmajor) {
-            const uint4 w = *reinterpret_cast<const uint4*>(cb + k * 16);
-            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    if (tokmajor) {
+        constexpr int U = 4;  // tokens per thread in flight
+        const uint4* c4 = reinterpret_cast<const uint4*>(cb) + k0;
+        for (int base = 0; base < n; base += 256 * U) {
+            uint4 w[U];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
+            for (int u = 0; u < U; ++u) {
+                const int i = base + u * 256 + tid;
+                w[u] = i < n ? __ldcs(c4 + i) : make_uint4(0u, 0u, 0u, 0u);
+            }
 #pragma unroll
-                for (int e = 0; e < 4; ++e) c += table[(4 * j + e) * kK + ((ws[j] >> (8 * e)) & 0xffu)];
-        } else {
+            for (int u = 0; u < U; ++u) {
+                const int i = base + u * 256 + tid;
+                if (i < n) {
+                    const int c = count16(table, w[u]);
+                    cnts[i] = (uint8_t)c;
+                    atomicAdd(&hist[c], 1);
+                    if (a.cnt_out) a.cnt_out[(int64_t)row * a.kv_len + k0 + i] = c;
+                }
+            }
+        }
+    } else {
+        for (int i = tid; i < n; i += 256) {
+            const int64_t k = k0 + i;
+            int c = 0;
 #pragma unroll
             for (int b = 0; b < kB; ++b) c += table[b * kK + cb[b * a.L.codes_blk + k * a.L.codes_tok]];
+            cnts[i] = (uint8_t)c;
+            atomicAdd(&hist[c], 1);
+            if (a.cnt_out) a.cnt_out[(int64_t)row * a.kv_len + k] = c;
         }
-        cnts[i] = (uint8_t)c;
-        atomicAdd(&hist[c], 1);
-        if (a.cnt_out) a.cnt_out[(int64_t)row * a.kv_len + k] = c;
     }
     if (!a.idx_out) return;  // counts only (uniform over the cluster)
     __syncthreads();
@@ -476,26 +541,33 @@ __global__ void __launch_bounds__(256) collision_topk_kernel(const CollArgs a) {
         }
         need_eq -= t;
     }
-    // ordered compaction of this CTA's keys, contiguous segment per thread
-    const int S = (n + 255) / 256;
-    const int s0 = min(n, tid * S), s1 = min(n, s0 + S);
-    int eqc = 0, gtc = 0;
-    for (int i = s0; i < s1; ++i) {
-        const int c = cnts[i];
-        eqc += c == vstar;
-        gtc += c > vstar;
+    // ordered compaction of this CTA's keys in 32-key chunks: per-chunk
+    // (> vstar, == vstar) ballots, a scan of the equal counts (ties go to
+    // the lowest keys), a scan of the selected counts, then the writes
+    for (int e = warp; e < nch; e += 8) {
+        const int i = 32 * e + lane;
+        const int c = i < n ? (int)cnts[i] : -1;
+        const uint32_t g = __ballot_sync(0xffffffffu, c > vstar), q = __ballot_sync(0xffffffffu, c == vstar);
+        if (lane == 0) {
+            gtm[e] = g;
+            eqm[e] = q;
+            eqc[e] = __popc(q);
+        }
     }
-    int tot;
-    const int eq_base = block_excl_scan<256>(eqc, scratch, &tot);
-    const int selc = gtc + max(0, min(eqc, take_eq - eq_base));
-    const int pos0 = block_excl_scan<256>(selc, scratch, &tot);
-    int64_t* out = a.idx_out + (int64_t)row * a.C + off + pos0;
-    int er = eq_base, p = 0;
-    for (int i = s0; i < s1; ++i) {
-        const int c = cnts[i];
-        bool sel = c > vstar;
-        if (c == vstar) sel = er++ < take_eq;
-        if (sel) out[p++] = k0 + i;
+    __syncthreads();
+    block_excl_scan_array(eqc, nch, scratch);
+    for (int e = tid; e < nch; e += 256)
+        selc[e] = __popc(gtm[e]) + max(0, min(__popc(eqm[e]), take_eq - eqc[e]));
+    __syncthreads();
+    block_excl_scan_array(selc, nch, scratch);
+    int64_t* out = a.idx_out + (int64_t)row * a.C + off;
+    const uint32_t lt = (1u << lane) - 1u;
+    for (int e = warp; e < nch; e += 8) {
+        const uint32_t q = eqm[e];
+        const bool sel = ((gtm[e] >> lane) & 1u) ||
+                         (((q >> lane) & 1u) && eqc[e] + __popc(q & lt) < take_eq);
+        const uint32_t sm = __ballot_sync(0xffffffffu, sel);
+        if (sel) out[selc[e] + __popc(sm & lt)] = k0 + 32 * e + lane;
     }
 }
 
@@ -511,14 +583,20 @@ struct Rerank4Args {
     int64_t* final_out;
 };
 
-__global__ void __launch_bounds__(256) rerank4_kernel(const Rerank4Args a) {
+// A cluster of CS CTAs per row: every CTA scores a contiguous slice of the
+// candidates and pushes its fp32 scores into rank 0's shared array (DSMEM);
+// rank 0 then selects the top F.
+__global__ void __launch_bounds__(256, 4) rerank4_kernel(const Rerank4Args a) {
     extern __shared__ __align__(16) uint8_t smem[];
     float* lut = reinterpret_cast<float*>(smem);           // [128 dims][16 nibbles] bf16-valued products
     int* hist = reinterpret_cast<int*>(lut + 128 * 16);    // 256
     int* misc = hist + 256;                                // 8
     int* scan = misc + 8;                                  // 512
-    float* sc = reinterpret_cast<float*>(scan + 512);      // [C]
-    const int row = blockIdx.x, tid = threadIdx.x;
+    float* sc = reinterpret_cast<float*>(scan + 512);      // [C] (used on rank 0)
+    cg::cluster_group cluster = cg::this_cluster();
+    const int CS = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
+    const int row = blockIdx.x / CS, tid = threadIdx.x;
+    cluster.barrier_arrive();  // peers are running before the first remote store
     const uint16_t* qb = a.qb + (int64_t)row * kHeadDim;
     for (int i = tid; i < 128 * 16; i += 256) {
         const int d = i >> 4, nib = i & 15;
@@ -526,11 +604,15 @@ __global__ void __launch_bounds__(256) rerank4_kernel(const Rerank4Args a) {
         lut[i] = rbf(__fmul_rn((nib & 8) ? v : -v, bfbits2f(qb[d])));
     }
     __syncthreads();
+    cluster.barrier_wait();
+    float* sc0 = cluster.map_shared_rank(sc, 0);
     const float qn = bfbits2f(a.qn[row]);
     const bool tokmajor = a.L.packed_blk == 1 && a.L.packed_tok == 16 && a.L.weight_blk == 1 && a.L.weight_tok == 16;
     const uint32_t* pk = a.L.packed + row * a.L.packed_row;
     const uint16_t* wt = reinterpret_cast<const uint16_t*>(a.L.weight) + row * a.L.weight_row;
-    for (int i = tid; i < a.C; i += 256) {
+    const int per = (a.C + CS - 1) / CS;
+    const int i0 = rank * per, i1 = min(a.C, i0 + per);
+    for (int i = i0 + tid; i < i1; i += 256) {
         const int64_t k = a.cand[(int64_t)row * a.C + i];
         uint32_t pw[kB];
         uint16_t wv[kB];
@@ -570,10 +652,10 @@ __global__ void __launch_bounds__(256) rerank4_kernel(const Rerank4Args a) {
         }
         const uint16_t s = f2bfbits(__fmul_rn(res, qn));
         if (a.scores) a.scores[(int64_t)row * a.C + i] = s;
-        sc[i] = __fadd_rn(bfbits2f(s), 0.0f);  // -0 -> +0 for the selection
+        sc0[i] = __fadd_rn(bfbits2f(s), 0.0f);  // -0 -> +0 for the selection
     }
-    if (a.F <= 0) return;
-    __syncthreads();
+    cluster.sync();  // every slice is in rank 0's array
+    if (rank != 0 || a.F <= 0) return;
     int64_t* fo = a.final_out + (int64_t)row * a.F;
     const int64_t* cr = a.cand + (int64_t)row * a.C;
     if (a.F >= a.C) {
@@ -631,14 +713,22 @@ struct PopArgs {
     float* ip_out;
 };
 
-__global__ void __launch_bounds__(256) popcount_topk_kernel(const PopArgs a) {
+// A cluster of CS CTAs per row.  Every CTA estimates a contiguous slice of
+// the candidates and pushes the estimates into rank 0's shared array; rank 0
+// selects the top K and pushes each selected candidate position to the CTA
+// that owns output slot pos (slots split into CS contiguous runs); every CTA
+// then takes the exact inner products of its run.
+__global__ void __launch_bounds__(256, 4) popcount_topk_kernel(const PopArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     int* hist = reinterpret_cast<int*>(smem);   // 256
     int* misc = hist + 256;                     // 8
     int* scan = misc + 8;                       // 512
-    float* sc = reinterpret_cast<float*>(scan + 512);            // [C]
-    int* selpos = reinterpret_cast<int*>(sc + ((a.C + 3) & ~3)); // [K]
-    const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float* sc = reinterpret_cast<float*>(scan + 512);            // [C] (used on rank 0)
+    int* selpos = reinterpret_cast<int*>(sc + ((a.C + 3) & ~3)); // [perK]: this CTA's output run
+    cg::cluster_group cluster = cg::this_cluster();
+    const int CS = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
+    const int row = blockIdx.x / CS, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    cluster.barrier_arrive();  // peers are running before the first remote store
     uint32_t pl[4][4];
     {
         const uint4* p = reinterpret_cast<const uint4*>(a.planes + (int64_t)row * 64);
@@ -654,8 +744,13 @@ __global__ void __launch_bounds__(256) popcount_topk_kernel(const PopArgs a) {
     const float d2 = __fmul_rn(2.0f, delta), l2 = __fmul_rn(2.0f, lo);
     const bool tokmajor = a.L.codes_blk == 1 && a.L.codes_tok == 16;
     const uint8_t* cb = a.L.codes + row * a.L.codes_row;
-    for (int i = tid; i < a.C; i += 256) {
-        const int64_t k = a.cand ? a.cand[(int64_t)row * a.C + i] : i;
+    const int64_t* cr = a.cand ? a.cand + (int64_t)row * a.C : nullptr;
+    const int perC = (a.C + CS - 1) / CS;
+    const int c_lo = rank * perC, c_hi = min(a.C, c_lo + perC);
+    cluster.barrier_wait();
+    float* sc0 = cluster.map_shared_rank(sc, 0);
+    for (int i = c_lo + tid; i < c_hi; i += 256) {
+        const int64_t k = cr ? cr[i] : i;
         uint32_t x[4];
         if (tokmajor) {
             const uint4 v = *reinterpret_cast<const uint4*>(cb + k * 16);
@@ -679,36 +774,52 @@ __global__ void __launch_bounds__(256) popcount_topk_kernel(const PopArgs a) {
         const float num = __fsub_rn(__fadd_rn(__fmul_rn(d2, (float)I), __fmul_rn(l2, (float)P)), c0);
         const float e = __fmul_rn(__fmul_rn(__fmul_rn(num, kInvSqrtD), a.L.factor[row * a.L.factor_row + k]), qn);
         if (a.est_out) a.est_out[(int64_t)row * a.C + i] = e;
-        sc[i] = __fadd_rn(e, 0.0f);
+        sc0[i] = __fadd_rn(e, 0.0f);
     }
-    __syncthreads();
-    const int64_t* cr = a.cand ? a.cand + (int64_t)row * a.C : nullptr;
-    int64_t* so = a.sel_out + (int64_t)row * a.K;
-    if (a.K >= a.C) {
-        for (int i = tid; i < a.K; i += 256) {
-            so[i] = i < a.C ? (cr ? cr[i] : i) : -1;
-            selpos[i] = i < a.C ? i : -1;
+    cluster.sync();  // every estimate is in rank 0's array
+    const int kk = min(a.K, a.C);
+    const int perK = (kk + CS - 1) / CS;
+    if (rank == 0) {
+        int64_t* so = a.sel_out + (int64_t)row * a.K;
+        auto emit = [&](int pos, int i) {
+            so[pos] = cr ? cr[i] : i;
+            if (a.keys) cluster.map_shared_rank(selpos, pos / perK)[pos % perK] = i;
+        };
+        if (a.K >= a.C) {
+            for (int i = tid; i < a.K; i += 256) {
+                if (i < a.C) emit(i, i);
+                else so[i] = -1;
+            }
+        } else {
+            block_topk<256, true>([&](int i) { return ordered_u32(sc[i]); }, a.C, a.K, hist, misc, scan, emit);
         }
-    } else {
-        block_topk<256, true>([&](int i) { return ordered_u32(sc[i]); }, a.C, a.K, hist, misc, scan,
-                              [&](int pos, int i) {
-                                  so[pos] = cr ? cr[i] : i;
-                                  selpos[pos] = i;
-                              });
     }
-    if (!a.keys) return;
-    __syncthreads();
+    if (!a.keys) return;  // uniform over the cluster
+    cluster.sync();  // every CTA holds its run of selected positions
     float qv[4];
     load_bf16x4(a.q_mean + (int64_t)row * kHeadDim + 4 * lane, qv);
-    const int kk = min(a.K, a.C);
-    for (int j = warp; j < kk; j += 8) {
-        const int i = selpos[j];
-        const int64_t k = cr ? cr[i] : i;
-        float kv[4];
-        load_bf16x4(a.keys + row * a.keys_ld + k * kHeadDim + 4 * lane, kv);
-        const float s = warp_sum_tree(sum4(__fmul_rn(kv[0], qv[0]), __fmul_rn(kv[1], qv[1]), __fmul_rn(kv[2], qv[2]),
-                                           __fmul_rn(kv[3], qv[3])));
-        if (lane == 0) a.ip_out[(int64_t)row * a.K + j] = s;
+    const int j_lo = rank * perK, j_hi = min(kk, j_lo + perK);
+    constexpr int U = 8;  // candidates per warp in flight (one 256-byte row each)
+    for (int j0 = j_lo + warp * U; j0 < j_hi; j0 += 8 * U) {
+        uint2 raw[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int j = j0 + u;
+            raw[u] = make_uint2(0, 0);
+            if (j < j_hi) {
+                const int i = selpos[j - j_lo];
+                const int64_t k = cr ? cr[i] : i;
+                raw[u] = *reinterpret_cast<const uint2*>(a.keys + row * a.keys_ld + k * kHeadDim + 4 * lane);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const float k0 = bfbits2f((uint16_t)(raw[u].x & 0xffffu)), k1 = bfbits2f((uint16_t)(raw[u].x >> 16));
+            const float k2 = bfbits2f((uint16_t)(raw[u].y & 0xffffu)), k3 = bfbits2f((uint16_t)(raw[u].y >> 16));
+            const float s = warp_sum_tree(sum4(__fmul_rn(k0, qv[0]), __fmul_rn(k1, qv[1]), __fmul_rn(k2, qv[2]),
+                                               __fmul_rn(k3, qv[3])));
+            if (lane == 0 && j0 + u < j_hi) a.ip_out[(int64_t)row * a.K + j0 + u] = s;
+        }
     }
 }
 
@@ -719,6 +830,18 @@ using namespace zkv;
 using namespace zkv::rq;
 
 static bool lay_ok(const zkv_rq_layout* L) { return L != nullptr; }
+
+// CTAs per row for the candidate kernels: enough to cover ~4 resident CTAs
+// on every SM in one wave, at most 8 (portable cluster), at least 256
+// candidates per CTA.
+static int cluster_size_for(int rows, int C) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int cs = (4 * sms) / (rows > 0 ? rows : 1);
+    const int by_c = (C + 255) / 256;
+    cs = cs < by_c ? cs : by_c;
+    return cs < 1 ? 1 : (cs > 8 ? 8 : cs);
+}
 
 extern "C" int zkv_rq_encode(const void* keys, int64_t keys_ld_row, int rows, int n_tok, int tok_start,
                              const void* signs, const zkv_rq_layout* lay, void* stream) {
@@ -756,10 +879,13 @@ extern "C" int zkv_collision_topk(const void* q_blocks, const zkv_rq_layout* lay
     if (lay->codes_blk == 1 && lay->codes_tok == 16 && (((uintptr_t)lay->codes & 15) || (lay->codes_row & 15)))
         return ZKV_ERR_ALIGN;
     if (rows == 0) return ZKV_OK;
-    int CS = (kv_len + 8191) / 8192;
-    CS = CS < 1 ? 1 : (CS > 8 ? 8 : CS);
+    int CS = cluster_size_for(rows, (kv_len + 3) / 4);  // >= 1024 keys per CTA
+    const int need = (kv_len + 131071) / 131072;       // shared-memory bound on keys per CTA
+    CS = CS < need ? (need > 8 ? 8 : need) : CS;
     const int per = (kv_len + CS - 1) / CS;
-    const size_t smem = (size_t)kB * kK + (136 + 136 + 40 + 24) * sizeof(int) + (size_t)per;
+    const size_t nch = ((size_t)per + 31) / 32;
+    const size_t smem = (size_t)kB * kK + (136 + 136 + 40 + 24) * sizeof(int) + (((size_t)per + 15) & ~(size_t)15) +
+                        nch * 16;
     if (smem > 200 * 1024) return ZKV_ERR_CAPACITY;
     CollArgs a;
     a.qb = (const uint16_t*)q_blocks;
@@ -790,11 +916,9 @@ extern "C" int zkv_rq_rerank4(const int64_t* cand, int C, const zkv_rq_layout* l
     if (smem > 200 * 1024) return ZKV_ERR_CAPACITY;
     Rerank4Args a{cand, C, F, *lay, (const uint16_t*)q_blocks, (const uint16_t*)q_norm, (const uint16_t*)centers,
                   (uint16_t*)scores, final_out};
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(rerank4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-        return ZKV_ERR_LAUNCH;
-    rerank4_kernel<<<rows, 256, smem, (cudaStream_t)stream>>>(a);
-    return launch_status();
+    const int CS = cluster_size_for(rows, C);
+    void* args[] = {&a};
+    return launch_clustered((const void*)rerank4_kernel, rows * CS, 256, CS, smem, (cudaStream_t)stream, args);
 }
 
 extern "C" int zkv_coarse2bit(const zkv_rq_layout* lay, const uint8_t* q_signs, const uint8_t* q_mags, int rows,
@@ -819,14 +943,13 @@ extern "C" int zkv_rq_popcount_topk(const int64_t* cand, int C, const zkv_rq_lay
     if (lay->codes_blk == 1 && lay->codes_tok == 16 && (((uintptr_t)lay->codes & 15) || (lay->codes_row & 15)))
         return ZKV_ERR_ALIGN;
     if (rows == 0) return ZKV_OK;
-    const size_t smem = (256 + 8 + 512) * sizeof(int) + (size_t)((C + 3) & ~3) * sizeof(float) + (size_t)K * sizeof(int);
+    const int CS = cluster_size_for(rows, C);
+    const int kk = K < C ? K : C;
+    const size_t smem = (256 + 8 + 512) * sizeof(int) + (size_t)((C + 3) & ~3) * sizeof(float) +
+                        (size_t)((kk + CS - 1) / CS) * sizeof(int);
     if (smem > 200 * 1024) return ZKV_ERR_CAPACITY;
     PopArgs a{cand, C, K, *lay, planes, qparams, sel_out, est_out, (const uint16_t*)keys, keys_ld_row,
               (const uint16_t*)q_mean, ip_out};
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(popcount_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
-        return ZKV_ERR_LAUNCH;
-    popcount_topk_kernel<<<rows, 256, smem, (cudaStream_t)stream>>>(a);
-    return launch_status();
+    void* args[] = {&a};
+    return launch_clustered((const void*)popcount_topk_kernel, rows * CS, 256, CS, smem, (cudaStream_t)stream, args);
 }
