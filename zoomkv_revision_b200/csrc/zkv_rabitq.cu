@@ -38,6 +38,60 @@ __constant__ uint32_t c_cen_bits[8] = {0x3D2C0000u, 0x3E020000u, 0x3E5A0000u, 0x
 
 __device__ __forceinline__ float rbf(float x) { return bfbits2f(f2bfbits(x)); }
 
+// (min finite, max) ordered key of sc[0..n) into range[0..1] (CTA-wide;
+// ends with a barrier).
+template <int NT>
+__device__ __forceinline__ void block_key_range(const float* sc, int n, uint32_t* range) {
+    uint32_t lo = 0xffffffffu, hi = 0u;
+    for (int i = threadIdx.x; i < n; i += NT) {
+        const uint32_t k = ordered_u32(sc[i]);
+        if (k > kOrderedNegInf) lo = min(lo, k);
+        hi = max(hi, k);
+    }
+    if (threadIdx.x == 0) {
+        range[0] = 0xffffffffu;
+        range[1] = 0u;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+        hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    if ((threadIdx.x & 31) == 0) {
+        atomicMin(range, lo);
+        atomicMax(range + 1, hi);
+    }
+    __syncthreads();
+}
+
+// Folds every thread's (min, max) ordered key into rank 0's lohi[0..1]
+// (one remote atomic pair per warp).
+__device__ __forceinline__ void cluster_fold_range(cg::cluster_group& cluster, uint32_t* lohi, uint32_t lo,
+                                                   uint32_t hi) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+        hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    if ((threadIdx.x & 31) == 0) {
+        uint32_t* r = cluster.map_shared_rank(lohi, 0);
+        atomicMin(r, lo);
+        atomicMax(r + 1, hi);
+    }
+}
+
+__device__ __forceinline__ int warp_excl_scan(int v) {
+    const int lane = threadIdx.x & 31;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += t;
+    }
+    return x - v;
+}
+
 __device__ __forceinline__ float warp_sum_tree(float v) {
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
@@ -396,6 +450,22 @@ __device__ __forceinline__ int block_excl_scan_array(int* v, int nv, int* scratc
     return tot;
 }
 
+// Bit j of gm / qm: key i+j (j < 16, i+j < n) has count > vstar / == vstar.
+__device__ __forceinline__ void chunk_masks(const uint8_t* cnts, int i, int n, int vstar, uint32_t& gm,
+                                            uint32_t& qm) {
+    const uint4 w = *reinterpret_cast<const uint4*>(cnts + i);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    gm = 0u;
+    qm = 0u;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const int c = (int)((ws[j >> 2] >> (8 * (j & 3))) & 0xffu);
+        const bool in = i + j < n;
+        gm |= (in && c > vstar) ? (1u << j) : 0u;
+        qm |= (in && c == vstar) ? (1u << j) : 0u;
+    }
+}
+
 // One cluster of CS CTAs per row, CTA r counting keys [r*per, (r+1)*per).
 // The 16 per-block weight tables are built once per cluster (block b by CTA
 // b % CS) and pushed to every peer through distributed shared memory.
@@ -406,18 +476,18 @@ __global__ void __launch_bounds__(256, 4) collision_topk_kernel(const CollArgs a
     int* gh = hist + 136;                                      // global histogram [136]
     int* scratch = gh + 136;                                   // 40
     int* misc = scratch + 40;                                  // 24: vstar, n_gt, eq_r[8], gt_r[8]
-    uint8_t* cnts = reinterpret_cast<uint8_t*>(misc + 24);     // [per] (padded to 16)
+    uint8_t* cnts = reinterpret_cast<uint8_t*>(misc + 24);     // [per] (padded to 512)
     cg::cluster_group cluster = cg::this_cluster();
     const int CS = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
     const int row = blockIdx.x / CS;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int k0 = rank * a.per;
     const int n = max(0, min(a.kv_len, k0 + a.per) - k0);
-    const int nch = (n + 31) / 32;                             // 32-key chunks
-    uint32_t* gtm = reinterpret_cast<uint32_t*>(cnts + ((a.per + 15) & ~15));  // [nch] masks
-    uint32_t* eqm = gtm + nch;
-    int* eqc = reinterpret_cast<int*>(eqm + nch);              // [nch] scanned counts
-    int* selc = eqc + nch;
+    const int nch = (n + 511) / 512;                           // 512-key chunks
+    int* gtc = reinterpret_cast<int*>(cnts + ((a.per + 511) & ~511));  // [nch] counts > vstar
+    int* eqn = gtc + nch;                                      // [nch] counts == vstar
+    int* eqb = eqn + nch;                                      // [nch] exclusive prefix of eqn
+    int* selb = eqb + nch;                                     // [nch] exclusive prefix of selected
 
     cluster.barrier_arrive();  // peers are running before the first remote store
     for (int b = rank + CS * warp; b < kB; b += CS * 8) collision_table(a, row, b, table);
@@ -541,33 +611,39 @@ __global__ void __launch_bounds__(256, 4) collision_topk_kernel(const CollArgs a
         }
         need_eq -= t;
     }
-    // ordered compaction of this CTA's keys in 32-key chunks: per-chunk
-    // (> vstar, == vstar) ballots, a scan of the equal counts (ties go to
-    // the lowest keys), a scan of the selected counts, then the writes
+    // ordered compaction of this CTA's keys in 512-key chunks (lane l owns
+    // keys 16l..16l+15 of a chunk, one 16-byte shared load): per-chunk
+    // (> vstar, == vstar) counts, a scan of the equal counts (ties go to the
+    // lowest keys), a scan of the selected counts, then the writes
     for (int e = warp; e < nch; e += 8) {
-        const int i = 32 * e + lane;
-        const int c = i < n ? (int)cnts[i] : -1;
-        const uint32_t g = __ballot_sync(0xffffffffu, c > vstar), q = __ballot_sync(0xffffffffu, c == vstar);
+        const int i = 512 * e + 16 * lane;
+        uint32_t gm, qm;
+        chunk_masks(cnts, i, n, vstar, gm, qm);
+        const int g = __reduce_add_sync(0xffffffffu, __popc(gm));
+        const int q = __reduce_add_sync(0xffffffffu, __popc(qm));
         if (lane == 0) {
-            gtm[e] = g;
-            eqm[e] = q;
-            eqc[e] = __popc(q);
+            gtc[e] = g;
+            eqn[e] = q;
+            eqb[e] = q;
         }
     }
     __syncthreads();
-    block_excl_scan_array(eqc, nch, scratch);
-    for (int e = tid; e < nch; e += 256)
-        selc[e] = __popc(gtm[e]) + max(0, min(__popc(eqm[e]), take_eq - eqc[e]));
+    block_excl_scan_array(eqb, nch, scratch);
+    for (int e = tid; e < nch; e += 256) selb[e] = gtc[e] + max(0, min(eqn[e], take_eq - eqb[e]));
     __syncthreads();
-    block_excl_scan_array(selc, nch, scratch);
+    block_excl_scan_array(selb, nch, scratch);
     int64_t* out = a.idx_out + (int64_t)row * a.C + off;
-    const uint32_t lt = (1u << lane) - 1u;
     for (int e = warp; e < nch; e += 8) {
-        const uint32_t q = eqm[e];
-        const bool sel = ((gtm[e] >> lane) & 1u) ||
-                         (((q >> lane) & 1u) && eqc[e] + __popc(q & lt) < take_eq);
-        const uint32_t sm = __ballot_sync(0xffffffffu, sel);
-        if (sel) out[selc[e] + __popc(sm & lt)] = k0 + 32 * e + lane;
+        const int i = 512 * e + 16 * lane;
+        uint32_t gm, qm;
+        chunk_masks(cnts, i, n, vstar, gm, qm);
+        int qr = eqb[e] + warp_excl_scan((int)__popc(qm));
+        uint32_t sm = gm;
+        for (uint32_t r = qm; r; r &= r - 1u) {  // equal keys in order, while ties remain
+            if (qr++ < take_eq) sm |= r & (0u - r);
+        }
+        int p = selb[e] + warp_excl_scan((int)__popc(sm));
+        for (uint32_t r = sm; r; r &= r - 1u) out[p++] = k0 + i + (__ffs(r) - 1);
     }
 }
 
@@ -589,14 +665,21 @@ struct Rerank4Args {
 __global__ void __launch_bounds__(256, 4) rerank4_kernel(const Rerank4Args a) {
     extern __shared__ __align__(16) uint8_t smem[];
     float* lut = reinterpret_cast<float*>(smem);           // [128 dims][16 nibbles] bf16-valued products
-    int* hist = reinterpret_cast<int*>(lut + 128 * 16);    // 256
-    int* misc = hist + 256;                                // 8
+    int* hist = reinterpret_cast<int*>(lut + 128 * 16);    // 512
+    int* misc = hist + 512;                                // 8
     int* scan = misc + 8;                                  // 512
-    float* sc = reinterpret_cast<float*>(scan + 512);      // [C] (used on rank 0)
+    uint32_t* lohi = reinterpret_cast<uint32_t*>(scan + 512);  // 4: min / max ordered score (rank 0)
+    float* sc = reinterpret_cast<float*>(lohi + 4);        // [C] (rank 0)
+    int* sel = reinterpret_cast<int*>(sc + ((a.C + 3) & ~3));  // [F] selected positions (rank 0)
+    int* ck = sel + ((a.F + 3) & ~3);                      // [perC] key ids of this CTA's slice
     cg::cluster_group cluster = cg::this_cluster();
     const int CS = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
     const int row = blockIdx.x / CS, tid = threadIdx.x;
     cluster.barrier_arrive();  // peers are running before the first remote store
+    const int per = (a.C + CS - 1) / CS;
+    const int i0 = rank * per, i1 = min(a.C, i0 + per);
+    const int64_t* cr = a.cand + (int64_t)row * a.C;
+    for (int i = i0 + tid; i < i1; i += 256) ck[i - i0] = (int)cr[i];
     const uint16_t* qb = a.qb + (int64_t)row * kHeadDim;
     for (int i = tid; i < 128 * 16; i += 256) {
         const int d = i >> 4, nib = i & 15;
@@ -610,10 +693,8 @@ __global__ void __launch_bounds__(256, 4) rerank4_kernel(const Rerank4Args a) {
     const bool tokmajor = a.L.packed_blk == 1 && a.L.packed_tok == 16 && a.L.weight_blk == 1 && a.L.weight_tok == 16;
     const uint32_t* pk = a.L.packed + row * a.L.packed_row;
     const uint16_t* wt = reinterpret_cast<const uint16_t*>(a.L.weight) + row * a.L.weight_row;
-    const int per = (a.C + CS - 1) / CS;
-    const int i0 = rank * per, i1 = min(a.C, i0 + per);
     for (int i = i0 + tid; i < i1; i += 256) {
-        const int64_t k = a.cand[(int64_t)row * a.C + i];
+        const int64_t k = ck[i - i0];
         uint32_t pw[kB];
         uint16_t wv[kB];
         if (tokmajor) {
@@ -657,13 +738,18 @@ __global__ void __launch_bounds__(256, 4) rerank4_kernel(const Rerank4Args a) {
     cluster.sync();  // every slice is in rank 0's array
     if (rank != 0 || a.F <= 0) return;
     int64_t* fo = a.final_out + (int64_t)row * a.F;
-    const int64_t* cr = a.cand + (int64_t)row * a.C;
     if (a.F >= a.C) {
         for (int i = tid; i < a.F; i += 256) fo[i] = i < a.C ? cr[i] : -1;
         return;
     }
-    block_topk<256, true>([&](int i) { return ordered_u32(sc[i]); }, a.C, a.F, hist, misc, scan,
-                          [&](int pos, int i) { fo[pos] = cr[i]; });
+    if (a.C <= 16 * 256) {
+        block_key_range<256>(sc, a.C, lohi);
+        block_topk_small<256>(sc, a.C, a.F, lohi[0], lohi[1], hist, misc, scan, [&](int pos, int i) { sel[pos] = i; });
+    } else
+        block_topk<256, true>([&](int i) { return ordered_u32(sc[i]); }, a.C, a.F, hist, misc, scan,
+                              [&](int pos, int i) { sel[pos] = i; });
+    __syncthreads();
+    for (int pos = tid; pos < a.F; pos += 256) fo[pos] = cr[sel[pos]];
 }
 
 // ------------------------------------------------------------------ 2-bit coarse score
@@ -713,22 +799,42 @@ struct PopArgs {
     float* ip_out;
 };
 
+// Popcount estimate of one candidate from its 16 code bytes.
+__device__ __forceinline__ float popcount_est(const uint32_t (&x)[4], const uint32_t (&pl)[4][4], float d2, float l2,
+                                              float c0, float factor, float qn) {
+    int I = 0, P = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        P += __popc(x[j]);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) I += __popc(x[j] & pl[p][j]) << p;
+    }
+    const float num = __fsub_rn(__fadd_rn(__fmul_rn(d2, (float)I), __fmul_rn(l2, (float)P)), c0);
+    return __fmul_rn(__fmul_rn(__fmul_rn(num, kInvSqrtD), factor), qn);
+}
+
 // A cluster of CS CTAs per row.  Every CTA estimates a contiguous slice of
 // the candidates and pushes the estimates into rank 0's shared array; rank 0
-// selects the top K and pushes each selected candidate position to the CTA
-// that owns output slot pos (slots split into CS contiguous runs); every CTA
-// then takes the exact inner products of its run.
+// selects the top K, writes their key ids and pushes each id to the CTA that
+// owns output slot pos (slots split into CS contiguous runs); every CTA then
+// takes the exact inner products of its run.
 __global__ void __launch_bounds__(256, 4) popcount_topk_kernel(const PopArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
-    int* hist = reinterpret_cast<int*>(smem);   // 256
-    int* misc = hist + 256;                     // 8
+    int* hist = reinterpret_cast<int*>(smem);   // 512
+    int* misc = hist + 512;                     // 8
     int* scan = misc + 8;                       // 512
-    float* sc = reinterpret_cast<float*>(scan + 512);            // [C] (used on rank 0)
-    int* selpos = reinterpret_cast<int*>(sc + ((a.C + 3) & ~3)); // [perK]: this CTA's output run
+    uint32_t* lohi = reinterpret_cast<uint32_t*>(scan + 512);   // 4: min / max ordered estimate (rank 0)
+    float* sc = reinterpret_cast<float*>(lohi + 4);              // [C] (rank 0)
+    int* sel = reinterpret_cast<int*>(sc + ((a.C + 3) & ~3));    // [K] selected positions (rank 0)
+    int* selk = sel + ((a.K + 3) & ~3);                          // [perK]: key ids of this CTA's run
     cg::cluster_group cluster = cg::this_cluster();
     const int CS = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
     const int row = blockIdx.x / CS, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    cluster.barrier_arrive();  // peers are running before the first remote store
+    if (rank == 0 && tid == 0) {
+        lohi[0] = 0xffffffffu;
+        lohi[1] = 0u;
+    }
+    cluster.barrier_arrive();  // peers are running (and rank 0's lohi set) before the first remote op
     uint32_t pl[4][4];
     {
         const uint4* p = reinterpret_cast<const uint4*>(a.planes + (int64_t)row * 64);
@@ -744,18 +850,51 @@ __global__ void __launch_bounds__(256, 4) popcount_topk_kernel(const PopArgs a) 
     const float d2 = __fmul_rn(2.0f, delta), l2 = __fmul_rn(2.0f, lo);
     const bool tokmajor = a.L.codes_blk == 1 && a.L.codes_tok == 16;
     const uint8_t* cb = a.L.codes + row * a.L.codes_row;
+    const float* fr = a.L.factor + row * a.L.factor_row;
     const int64_t* cr = a.cand ? a.cand + (int64_t)row * a.C : nullptr;
     const int perC = (a.C + CS - 1) / CS;
     const int c_lo = rank * perC, c_hi = min(a.C, c_lo + perC);
     cluster.barrier_wait();
     float* sc0 = cluster.map_shared_rank(sc, 0);
-    for (int i = c_lo + tid; i < c_hi; i += 256) {
-        const int64_t k = cr ? cr[i] : i;
-        uint32_t x[4];
-        if (tokmajor) {
-            const uint4 v = *reinterpret_cast<const uint4*>(cb + k * 16);
-            x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
-        } else {
+    uint32_t klo = 0xffffffffu, khi = 0u;
+    if (tokmajor) {
+        constexpr int U = 4;  // candidates per thread in flight
+        for (int base = c_lo; base < c_hi; base += 256 * U) {
+            int64_t kx[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = base + u * 256 + tid;
+                kx[u] = i < c_hi ? (cr ? cr[i] : i) : -1;
+            }
+            uint4 v[U];
+            float f[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                v[u] = make_uint4(0u, 0u, 0u, 0u);
+                f[u] = 0.0f;
+                if (kx[u] >= 0) {
+                    v[u] = *reinterpret_cast<const uint4*>(cb + kx[u] * 16);
+                    f[u] = fr[kx[u]];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = base + u * 256 + tid;
+                if (i < c_hi) {
+                    const uint32_t x[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+                    const float er = popcount_est(x, pl, d2, l2, c0, f[u], qn);
+                    if (a.est_out) a.est_out[(int64_t)row * a.C + i] = er;
+                    const float e = __fadd_rn(er, 0.0f);  // -0 -> +0 for the selection
+                    sc0[i] = e;
+                    klo = min(klo, ordered_u32(e));
+                    khi = max(khi, ordered_u32(e));
+                }
+            }
+        }
+    } else {
+        for (int i = c_lo + tid; i < c_hi; i += 256) {
+            const int64_t k = cr ? cr[i] : i;
+            uint32_t x[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 uint32_t w = 0;
@@ -763,54 +902,56 @@ __global__ void __launch_bounds__(256, 4) popcount_topk_kernel(const PopArgs a) 
                 for (int e = 0; e < 4; ++e) w |= (uint32_t)cb[(4 * j + e) * a.L.codes_blk + k * a.L.codes_tok] << (8 * e);
                 x[j] = w;
             }
+            const float er = popcount_est(x, pl, d2, l2, c0, fr[k], qn);
+            if (a.est_out) a.est_out[(int64_t)row * a.C + i] = er;
+            const float e = __fadd_rn(er, 0.0f);
+            sc0[i] = e;
+            klo = min(klo, ordered_u32(e));
+            khi = max(khi, ordered_u32(e));
         }
-        int I = 0, P = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            P += __popc(x[j]);
-#pragma unroll
-            for (int p = 0; p < 4; ++p) I += __popc(x[j] & pl[p][j]) << p;
-        }
-        const float num = __fsub_rn(__fadd_rn(__fmul_rn(d2, (float)I), __fmul_rn(l2, (float)P)), c0);
-        const float e = __fmul_rn(__fmul_rn(__fmul_rn(num, kInvSqrtD), a.L.factor[row * a.L.factor_row + k]), qn);
-        if (a.est_out) a.est_out[(int64_t)row * a.C + i] = e;
-        sc0[i] = __fadd_rn(e, 0.0f);
     }
-    cluster.sync();  // every estimate is in rank 0's array
+    cluster_fold_range(cluster, lohi, klo, khi);
+    cluster.sync();  // every estimate (and the key range) is in rank 0's shared memory
     const int kk = min(a.K, a.C);
     const int perK = (kk + CS - 1) / CS;
     if (rank == 0) {
         int64_t* so = a.sel_out + (int64_t)row * a.K;
-        auto emit = [&](int pos, int i) {
-            so[pos] = cr ? cr[i] : i;
-            if (a.keys) cluster.map_shared_rank(selpos, pos / perK)[pos % perK] = i;
-        };
         if (a.K >= a.C) {
             for (int i = tid; i < a.K; i += 256) {
-                if (i < a.C) emit(i, i);
+                if (i < a.C) sel[i] = i;
                 else so[i] = -1;
             }
         } else {
-            block_topk<256, true>([&](int i) { return ordered_u32(sc[i]); }, a.C, a.K, hist, misc, scan, emit);
+            if (a.C <= 16 * 256)
+                block_topk_small<256>(sc, a.C, a.K, lohi[0], lohi[1], hist, misc, scan,
+                                      [&](int pos, int i) { sel[pos] = i; });
+            else
+                block_topk<256, true>([&](int i) { return ordered_u32(sc[i]); }, a.C, a.K, hist, misc, scan,
+                                      [&](int pos, int i) { sel[pos] = i; });
+        }
+        __syncthreads();
+        // positions -> key ids (independent loads), pushed to the owner of each slot
+        for (int pos = tid; pos < kk; pos += 256) {
+            const int i = sel[pos];
+            const int64_t k = cr ? cr[i] : i;
+            so[pos] = k;
+            if (a.keys) cluster.map_shared_rank(selk, pos / perK)[pos % perK] = (int)k;
         }
     }
     if (!a.keys) return;  // uniform over the cluster
-    cluster.sync();  // every CTA holds its run of selected positions
+    cluster.sync();  // every CTA holds the key ids of its run
     float qv[4];
     load_bf16x4(a.q_mean + (int64_t)row * kHeadDim + 4 * lane, qv);
     const int j_lo = rank * perK, j_hi = min(kk, j_lo + perK);
     constexpr int U = 8;  // candidates per warp in flight (one 256-byte row each)
+    const uint16_t* kr = a.keys + row * a.keys_ld + 4 * lane;
     for (int j0 = j_lo + warp * U; j0 < j_hi; j0 += 8 * U) {
         uint2 raw[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int j = j0 + u;
             raw[u] = make_uint2(0, 0);
-            if (j < j_hi) {
-                const int i = selpos[j - j_lo];
-                const int64_t k = cr ? cr[i] : i;
-                raw[u] = *reinterpret_cast<const uint2*>(a.keys + row * a.keys_ld + k * kHeadDim + 4 * lane);
-            }
+            if (j < j_hi) raw[u] = *reinterpret_cast<const uint2*>(kr + (int64_t)selk[j - j_lo] * kHeadDim);
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -883,8 +1024,8 @@ extern "C" int zkv_collision_topk(const void* q_blocks, const zkv_rq_layout* lay
     const int need = (kv_len + 131071) / 131072;       // shared-memory bound on keys per CTA
     CS = CS < need ? (need > 8 ? 8 : need) : CS;
     const int per = (kv_len + CS - 1) / CS;
-    const size_t nch = ((size_t)per + 31) / 32;
-    const size_t smem = (size_t)kB * kK + (136 + 136 + 40 + 24) * sizeof(int) + (((size_t)per + 15) & ~(size_t)15) +
+    const size_t nch = ((size_t)per + 511) / 512;
+    const size_t smem = (size_t)kB * kK + (136 + 136 + 40 + 24) * sizeof(int) + (((size_t)per + 511) & ~(size_t)511) +
                         nch * 16;
     if (smem > 200 * 1024) return ZKV_ERR_CAPACITY;
     CollArgs a;
@@ -912,11 +1053,12 @@ extern "C" int zkv_rq_rerank4(const int64_t* cand, int C, const zkv_rq_layout* l
                 (lay->weight_row & 7)))
         return ZKV_ERR_ALIGN;
     if (rows == 0) return ZKV_OK;
-    const size_t smem = (128 * 16 + 256 + 8 + 512) * sizeof(float) + (size_t)((C + 3) & ~3) * sizeof(float);
+    const int CS = cluster_size_for(rows, C);
+    const size_t smem = (128 * 16 + 512 + 8 + 512 + 4) * sizeof(float) + (size_t)((C + 3) & ~3) * sizeof(float) +
+                        (size_t)((F + 3) & ~3) * sizeof(int) + (size_t)((C + CS - 1) / CS) * sizeof(int);
     if (smem > 200 * 1024) return ZKV_ERR_CAPACITY;
     Rerank4Args a{cand, C, F, *lay, (const uint16_t*)q_blocks, (const uint16_t*)q_norm, (const uint16_t*)centers,
                   (uint16_t*)scores, final_out};
-    const int CS = cluster_size_for(rows, C);
     void* args[] = {&a};
     return launch_clustered((const void*)rerank4_kernel, rows * CS, 256, CS, smem, (cudaStream_t)stream, args);
 }
@@ -945,8 +1087,8 @@ extern "C" int zkv_rq_popcount_topk(const int64_t* cand, int C, const zkv_rq_lay
     if (rows == 0) return ZKV_OK;
     const int CS = cluster_size_for(rows, C);
     const int kk = K < C ? K : C;
-    const size_t smem = (256 + 8 + 512) * sizeof(int) + (size_t)((C + 3) & ~3) * sizeof(float) +
-                        (size_t)((kk + CS - 1) / CS) * sizeof(int);
+    const size_t smem = (512 + 8 + 512 + 4) * sizeof(int) + (size_t)((C + 3) & ~3) * sizeof(float) +
+                        (size_t)((K + 3) & ~3) * sizeof(int) + (size_t)((kk + CS - 1) / CS) * sizeof(int);
     if (smem > 200 * 1024) return ZKV_ERR_CAPACITY;
     PopArgs a{cand, C, K, *lay, planes, qparams, sel_out, est_out, (const uint16_t*)keys, keys_ld_row,
               (const uint16_t*)q_mean, ip_out};
