@@ -263,6 +263,22 @@ int zkv_page_decode(const void* q, const zkv_page_layer* layer, int rows,
                     float* lse, int64_t* sel_out, int32_t* status, int cluster,
                     void* stream);
 
+/* Long-context form of zkv_page_decode for few rows (same results): the
+ * GQA-mean query and the Quest scores of all n_c chunks are computed by
+ * kernels that spread over every SM (zkv_gqa_mean, zkv_quest_score) into
+ * `workspace`, then the fused kernel reads the scores, selects in two
+ * levels (each cluster CTA's top nk, then the top nk of those) and attends.
+ * Falls back to zkv_page_decode where the fused kernel selects in one level
+ * (n_c <= 2048, cluster 1, nk >= n_c).  workspace: device, 256-byte
+ * aligned, ws_bytes >= zkv_page_decode_split_ws_bytes(rows, n_c).        */
+size_t zkv_page_decode_split_ws_bytes(int rows, int n_c);
+int zkv_page_decode_split(const void* q, const zkv_page_layer* layer, int rows,
+                          int G, int n_max, int n_c, int nk, int n_sink,
+                          int near_start, int n_near, float scale, void* out,
+                          float* lse, int64_t* sel_out, int32_t* status,
+                          int cluster, void* workspace, size_t ws_bytes,
+                          void* stream);
+
 /* Attention over externally selected pages (the sequence-split step):
  * the layer buffer holds pages [sel_lo, sel_hi) of the sequence as its
  * pages 0..; of the global page ids sel [rows][n_sel] (-1 = none) those in

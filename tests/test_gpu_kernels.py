@@ -243,14 +243,19 @@ def test_lse_merge_golden():
     assert (to_u16(m) == gl["merged"]).mean() > 0.99
 
 
-@pytest.mark.parametrize("mode", ["ties", "invalid", "mixed_sign", "n_c_gt_2048"])
-def test_page_decode_selection_edge_cases(mode):
+@pytest.mark.parametrize("mode,n_c,nk", [("ties", 400, 64), ("invalid", 400, 64), ("mixed_sign", 400, 64),
+                                         ("plain", 2600, 64), ("ties", 2600, 64), ("invalid", 2600, 64),
+                                         ("mixed_sign", 2600, 64), ("plain", 2050, 300), ("mostly_invalid", 2050, 300),
+                                         ("plain", 8184, 256)])
+def test_page_decode_selection_edge_cases(mode, n_c, nk):
     """Selection paths of the fused kernel: all-equal scores (heavy-tie
     fallback, lowest ids win), invalid chunks (-inf), mixed-sign scores
-    (float-valued bucketing) and n_c beyond the register-resident select."""
+    (float-valued bucketing); n_c > 2048 takes the two-level select (per-CTA
+    top nk, then the top nk of the cluster's candidates), including a last
+    CTA with fewer than nk chunks (padded candidate slots) and fewer finite
+    scores than nk (-inf chunks selected by lowest id)."""
     bs, H, G = 1, 2, 4
-    n_ret = 16 * (2600 if mode == "n_c_gt_2048" else 400)
-    nk = 64
+    n_ret = 16 * n_c
     pc, _ = W.build_page_cache(11, bs, H, n_ret, 16, DEV)
     g = torch.Generator(device=DEV).manual_seed(5)
     q = W.synth_query(g, bs, H * G, DEV)
@@ -258,12 +263,17 @@ def test_page_decode_selection_edge_cases(mode):
         q.zero_()
     elif mode == "invalid":
         pc.valid.copy_(torch.rand(pc.valid.shape, generator=g, device=DEV) > 0.3)
+    elif mode == "mostly_invalid":
+        pc.valid.copy_(torch.rand(pc.valid.shape, generator=g, device=DEV) > 0.95)
     elif mode == "mixed_sign":
         pc.chunk_min.copy_(torch.randn(pc.chunk_min.shape, generator=g, device=DEV).to(torch.bfloat16))
         pc.chunk_max.copy_(pc.chunk_min)
     sel = torch.empty(bs * H, nk, dtype=torch.int64, device=DEV)
-    out = ops.page_decode(q, pc.layer(), pc.n_c, nk, 16, sel_out=sel, cluster=8)
+    out = ops.page_decode(q, pc.layer(), pc.n_c, nk, 16, sel_out=sel, cluster=8, split=False)
+    sel2 = torch.empty_like(sel)  # long-context form: scores from the all-SM kernel
+    out2 = ops.page_decode(q, pc.layer(), pc.n_c, nk, 16, sel_out=sel2, cluster=8, split=True)
     torch.cuda.synchronize()
+    assert torch.equal(sel2, sel) and torch.equal(out2, out)
     R = bs * H
     ro, _, rsel = O.page_decode(
         to_u16(q).reshape(R, G, 128), to_u16(pc.chunk_min).reshape(R, -1, 128), to_u16(pc.chunk_max).reshape(R, -1, 128),

@@ -66,6 +66,10 @@ _SIGNATURES = {
                       _i32, _i32, _f32, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p],
     "zkv_page_decode": [_c_void_p, ctypes.POINTER(ZkvPageLayer), _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32,
                         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p],
+    "zkv_page_decode_split_ws_bytes": [_i32, _i32],
+    "zkv_page_decode_split": [_c_void_p, ctypes.POINTER(ZkvPageLayer), _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+                              _f32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p, ctypes.c_size_t,
+                              _c_void_p],
     "zkv_lse_merge": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p],
     "zkv_lse_merge_n": [_c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p],
     "zkv_rq_encode": [_c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _RQ, _c_void_p],
@@ -88,7 +92,8 @@ _SIGNATURES = {
     "zkv_status_string": [_i32],
 }
 
-_RESTYPES = {"zkv_status_string": ctypes.c_char_p, "zkv_reference_select_ws_bytes": ctypes.c_size_t}
+_RESTYPES = {"zkv_status_string": ctypes.c_char_p, "zkv_reference_select_ws_bytes": ctypes.c_size_t,
+             "zkv_page_decode_split_ws_bytes": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib = None

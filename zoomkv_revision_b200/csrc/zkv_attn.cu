@@ -384,6 +384,9 @@ struct PageArgs {
     const uint16_t* q;
     zkv_page_layer L;
     int G, n_max, n_c, nk, n_sink, near_start, n_near, n_c_pad, per, pp, pn;
+    int n_cand;     // two-level select: CS * nk candidate slots (0 = one-level)
+    const float* sc_in;  // two-level only: precomputed chunk scores [rows][sc_ld] (NULL = score here)
+    int64_t sc_ld;
     float sl2;
     uint16_t* out;
     float* lse;
@@ -396,6 +399,9 @@ struct PageArgs {
     float* out_f32;  // fp32 partial output instead of bf16 (may be NULL)
 };
 
+// kTwoLevel: the select runs in two levels over a.n_cand candidates (a
+// separate instantiation keeps the one-level kernel's code unchanged).
+template <bool kTwoLevel>
 __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const PageArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     cg::cluster_group cluster = cg::this_cluster();
@@ -406,7 +412,9 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
 
     uint8_t* region = smem;
     float* sc_all = reinterpret_cast<float*>(smem + kRegionBytes);
-    int* sel_s = reinterpret_cast<int*>(sc_all + a.n_c_pad);
+    float* cand_sc = sc_all + a.n_c_pad;                              // [n_cand] two-level candidates
+    int* cand_id = reinterpret_cast<int*>(cand_sc + (kTwoLevel ? a.n_cand : 0));
+    int* sel_s = cand_id + (kTwoLevel ? a.n_cand : 0);
     uint16_t* q_s = reinterpret_cast<uint16_t*>(sel_s + ((a.nk + 3) & ~3));
     uint16_t* rq_s = q_s + 8 * kHeadDim;
     float* cm = reinterpret_cast<float*>(rq_s + kHeadDim);
@@ -450,9 +458,29 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
     const int n_blk = (n_my + kBlk - 1) / kBlk;
     const uint16_t* gmin = reinterpret_cast<const uint16_t*>(a.L.chunk_min) + (row * a.n_max) * kHeadDim;
     const uint16_t* gmax = reinterpret_cast<const uint16_t*>(a.L.chunk_max) + (row * a.n_max) * kHeadDim;
-    {
+    if (kTwoLevel && a.sc_in) {  // scores from the all-SM scoring kernel
+        const float* src = a.sc_in + row * a.sc_ld;
+        uint32_t klo = 0xffffffffu, khi = 0u;
+        for (int c = c0 + (int)threadIdx.x; c < c1; c += kAttnThreads) {
+            const float val = src[c];
+            sc_all[c] = val;
+            const uint32_t kk = ordered_u32(val);
+            if (kk > kOrderedNegInf) klo = min(klo, kk);
+            khi = max(khi, kk);
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            klo = min(klo, __shfl_xor_sync(0xffffffffu, klo, off));
+            khi = max(khi, __shfl_xor_sync(0xffffffffu, khi, off));
+        }
+        if (lane == 0) {
+            atomicMin(&s_mm[0], klo);
+            atomicMax(&s_mm[1], khi);
+        }
+    } else {
+        constexpr int R = 2;
         uint8_t* ring = region + warp * (2 * kSlotBytes);
-        uint64_t* rbar = bars + 2 * warp;
+        uint64_t* rbar = bars + R * warp;
         auto issue_blk = [&](int b, int k) {
             if (lane == 0) {
                 const int cc = c0 + b * kBlk;
@@ -465,16 +493,15 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
         };
         int mine = 0;
         for (int b = warp; b < n_blk; b += kAttnWarps) ++mine;
-        if (mine > 0) issue_blk(warp, 0);
-        if (mine > 1) issue_blk(warp + kAttnWarps, 1);
+        for (int k = 0; k < R && k < mine; ++k) issue_blk(warp + k * kAttnWarps, k);
         const int hl = lane & 15, half = lane >> 4;
         const uint4 qv = *reinterpret_cast<const uint4*>(rq_s + 8 * hl);
         bool ok = true;
         uint32_t klo = 0xffffffffu, khi = 0u;
         for (int i = 0; i < mine; ++i) {
             const int b = warp + i * kAttnWarps;
-            const int k = i & 1;
-            if (!mbar_wait(rbar + k, (uint32_t)((i >> 1) & 1), a.status)) ok = false;
+            const int k = i % R;
+            if (!mbar_wait(rbar + k, (uint32_t)((i / R) & 1), a.status)) ok = false;
             const uint8_t* src = ring + k * 4096;
             const int cc = c0 + b * kBlk;
             const int nch = min(kBlk, c1 - cc);
@@ -498,7 +525,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
                 }
             }
             __syncwarp();
-            if (i + 2 < mine) issue_blk(b + 2 * kAttnWarps, k);
+            if (i + R < mine) issue_blk(b + R * kAttnWarps, k);
         }
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) {
@@ -518,8 +545,43 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
         rmm[2 + 2 * rank] = s_mm[0];
         rmm[3 + 2 * rank] = s_mm[1];
     }
+    if (kTwoLevel) {
+        // two-level select, level 1: this CTA's top nk (ties to the lowest
+        // chunk), as (score, chunk) pairs in chunk order, into slot `rank` of
+        // every CTA's candidate list; padding keys order below -inf.  The
+        // global top nk is a subset of the union, and the list is in chunk
+        // order, so level 2 picks the same set in the same order.
+        float* my_sc = cand_sc + rank * a.nk;
+        int* my_id = cand_id + rank * a.nk;
+        if (n_my > a.nk) {
+            auto emit = [&](int pos, int i) {
+                my_sc[pos] = sc_all[c0 + i];
+                my_id[pos] = c0 + i;
+            };
+            if (n_my <= 16 * kAttnThreads)
+                block_topk_small<kAttnThreads>(sc_all + c0, n_my, a.nk, s_mm[0], s_mm[1], hist, misc, scan, emit);
+            else
+                block_topk<kAttnThreads, true>([&](int i) { return ordered_u32(sc_all[c0 + i]); }, n_my, a.nk, hist,
+                                               misc, scan, emit, true, s_mm[0], s_mm[1]);
+        } else {
+            for (int i = threadIdx.x; i < a.nk; i += kAttnThreads) {
+                my_sc[i] = i < n_my ? sc_all[c0 + i] : __uint_as_float(0xffffffffu);
+                my_id[i] = i < n_my ? c0 + i : 0;
+            }
+        }
+        __syncthreads();
+        for (int p = 1; p < CS; ++p) {
+            const int dst_rank = (rank + p) % CS;
+            float* rs = cluster.map_shared_rank(my_sc, dst_rank);
+            int* ri = cluster.map_shared_rank(my_id, dst_rank);
+            for (int i = threadIdx.x; i < a.nk; i += kAttnThreads) {
+                rs[i] = my_sc[i];
+                ri[i] = my_id[i];
+            }
+        }
+    }
     // push this CTA's score range into every peer's score array
-    for (int p = 1; p < CS; ++p) {
+    for (int p = 1; p < CS && !kTwoLevel; ++p) {
         const int dst_rank = (rank + p) % CS;
         float* rsc = cluster.map_shared_rank(sc_all, dst_rank);
         for (int i = c0 + 4 * threadIdx.x; i < c1; i += 4 * kAttnThreads) {
@@ -558,7 +620,15 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
             lo = min(lo, s_mm[2 + 2 * r]);
             hi = max(hi, s_mm[3 + 2 * r]);
         }
-        if (a.n_c <= 16 * kAttnThreads) {
+        if (kTwoLevel) {  // level 2 over the CS * nk candidates
+            if (a.n_cand <= 16 * kAttnThreads)
+                block_topk_small<kAttnThreads>(cand_sc, a.n_cand, a.nk, lo, hi, hist, misc, scan,
+                                               [&](int pos, int i) { sel_s[pos] = cand_id[i]; });
+            else
+                block_topk<kAttnThreads, true>([&](int i) { return ordered_u32(cand_sc[i]); }, a.n_cand, a.nk, hist,
+                                               misc, scan, [&](int pos, int i) { sel_s[pos] = cand_id[i]; }, true, lo,
+                                               hi);
+        } else if (a.n_c <= 16 * kAttnThreads) {
             block_topk_small<kAttnThreads>(sc_all, a.n_c, a.nk, lo, hi, hist, misc, scan,
                                            [&](int pos, int i) { sel_s[pos] = i; });
         } else {
@@ -752,8 +822,9 @@ __global__ void lse_merge_n_kernel(const float* __restrict__ parts, const float*
 using namespace zkv;
 
 static size_t page_smem(const PageArgs& a) {
-    return kRegionBytes + (size_t)a.n_c_pad * 4 + (size_t)((a.nk + 3) & ~3) * 4 + 9 * kHeadDim * 2 +
-           (16 + 8 * kHeadDim) * 4 + (512 + 8 + 2 * kAttnThreads) * 4 + ((2 + kPSlots) * kAttnWarps) * 8 + 16;
+    return kRegionBytes + (size_t)a.n_c_pad * 4 + (size_t)a.n_cand * 8 + (size_t)((a.nk + 3) & ~3) * 4 +
+           9 * kHeadDim * 2 + (16 + 8 * kHeadDim) * 4 + (512 + 8 + 2 * kAttnThreads) * 4 +
+           ((2 + kPSlots) * kAttnWarps) * 8 + 16;
 }
 
 static int pick_cluster(int requested, int rows) {
@@ -762,9 +833,10 @@ static int pick_cluster(int requested, int rows) {
     return 8;
 }
 
-extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max, int n_c,
-                               int nk, int n_sink, int near_start, int n_near, float scale, void* out, float* lse,
-                               int64_t* sel_out, int32_t* status, int cluster, void* stream) {
+static int page_decode_impl(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max, int n_c, int nk,
+                            int n_sink, int near_start, int n_near, float scale, void* out, float* lse,
+                            int64_t* sel_out, int32_t* status, int cluster, const float* sc_in, int64_t sc_ld,
+                            void* stream) {
     if (!q || !layer || !out || rows < 0 || G < 1 || G > 8 || n_c < 0 || n_c > n_max || nk < 1 || n_near < 0 ||
         n_sink < 0 || near_start < 0)
         return ZKV_ERR_ARG;
@@ -795,6 +867,10 @@ extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int r
     a.n_c_pad = (n_c + 3) & ~3;
     a.per = ((n_c + CS - 1) / CS + 3) & ~3;
     a.pp = (a.nk + CS - 1) / CS;
+    // past 16 keys per thread the one-level select re-reads shared memory
+    a.n_cand = (CS > 1 && n_c > 16 * kAttnThreads && a.nk < n_c) ? ((CS * a.nk + 3) & ~3) : 0;
+    a.sc_in = a.n_cand ? sc_in : nullptr;
+    a.sc_ld = sc_ld;
     a.pn = ((n_sink + n_near + CS - 1) / CS + 3) & ~3;
     a.sl2 = scale * 1.4426950408889634f;
     a.out = (uint16_t*)out;
@@ -805,8 +881,46 @@ extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int r
     a.sel_lo = a.sel_hi = 0;
     a.out_f32 = nullptr;
     void* args[] = {&a};
-    return launch_clustered((const void*)page_decode_kernel, rows * CS, kAttnThreads, CS, page_smem(a),
-                            (cudaStream_t)stream, args, /*pdl=*/true);
+    return launch_clustered(a.n_cand ? (const void*)page_decode_kernel<true> : (const void*)page_decode_kernel<false>,
+                            rows * CS, kAttnThreads, CS, page_smem(a), (cudaStream_t)stream, args, /*pdl=*/true);
+}
+
+extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max, int n_c,
+                               int nk, int n_sink, int near_start, int n_near, float scale, void* out, float* lse,
+                               int64_t* sel_out, int32_t* status, int cluster, void* stream) {
+    return page_decode_impl(q, layer, rows, G, n_max, n_c, nk, n_sink, near_start, n_near, scale, out, lse, sel_out,
+                            status, cluster, nullptr, 0, stream);
+}
+
+// workspace: raw_q [rows][128] bf16 | scores [rows][n_c] fp32 (256-byte aligned parts)
+static size_t split_ws_raw_bytes(int rows) { return (((size_t)rows * kHeadDim * 2) + 255) & ~(size_t)255; }
+
+extern "C" size_t zkv_page_decode_split_ws_bytes(int rows, int n_c) {
+    if (rows < 0 || n_c < 0) return 0;
+    return split_ws_raw_bytes(rows) + (((size_t)rows * n_c * 4 + 255) & ~(size_t)255);
+}
+
+extern "C" int zkv_page_decode_split(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max, int n_c,
+                                     int nk, int n_sink, int near_start, int n_near, float scale, void* out,
+                                     float* lse, int64_t* sel_out, int32_t* status, int cluster, void* workspace,
+                                     size_t ws_bytes, void* stream) {
+    const int CS = pick_cluster(cluster, rows);
+    // the split form only pays where the fused kernel takes the two-level select
+    if (!(CS > 1 && n_c > 16 * kAttnThreads && nk < n_c) || rows <= 0 || !layer || n_c > n_max || n_c > 16384)
+        return zkv_page_decode(q, layer, rows, G, n_max, n_c, nk, n_sink, near_start, n_near, scale, out, lse, sel_out,
+                               status, cluster, stream);
+    if (!q || !workspace || ws_bytes < zkv_page_decode_split_ws_bytes(rows, n_c) || G < 1 || G > 8)
+        return ZKV_ERR_ARG;
+    if (((uintptr_t)workspace & 255) || ((uintptr_t)q & 7)) return ZKV_ERR_ALIGN;
+    uint8_t* ws = (uint8_t*)workspace;
+    void* raw_q = ws;
+    float* scores = (float*)(ws + split_ws_raw_bytes(rows));
+    int rc = zkv_gqa_mean(q, rows, G, raw_q, stream);
+    if (rc != ZKV_OK) return rc;
+    rc = zkv_quest_score(raw_q, layer->chunk_min, layer->chunk_max, layer->valid, scores, rows, n_c, n_max, stream);
+    if (rc != ZKV_OK) return rc;
+    return page_decode_impl(q, layer, rows, G, n_max, n_c, nk, n_sink, near_start, n_near, scale, out, lse, sel_out,
+                            status, cluster, scores, n_c, stream);
 }
 
 extern "C" int zkv_page_attend(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max,
@@ -842,6 +956,9 @@ extern "C" int zkv_page_attend(const void* q, const zkv_page_layer* layer, int r
     a.n_c_pad = 0;
     a.per = 0;
     a.pp = (n_sel + CS - 1) / CS;
+    a.n_cand = 0;
+    a.sc_in = nullptr;
+    a.sc_ld = 0;
     a.pn = ((n_sink + n_near + CS - 1) / CS + 3) & ~3;
     a.sl2 = scale * 1.4426950408889634f;
     a.out = (uint16_t*)out;
@@ -853,7 +970,7 @@ extern "C" int zkv_page_attend(const void* q, const zkv_page_layer* layer, int r
     a.sel_hi = sel_hi;
     a.out_f32 = out_f32;
     void* args[] = {&a};
-    return launch_clustered((const void*)page_decode_kernel, rows * CS, kAttnThreads, CS, page_smem(a),
+    return launch_clustered((const void*)page_decode_kernel<false>, rows * CS, kAttnThreads, CS, page_smem(a),
                             (cudaStream_t)stream, args, /*pdl=*/true);
 }
 

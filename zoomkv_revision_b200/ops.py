@@ -401,12 +401,34 @@ class PageLayer:
             near_k.shape[2], _p(kscale))
 
 
+_SPLIT_WS: dict = {}
+_SM_COUNT: dict = {}
+
+
+def _sm_count(dev) -> int:
+    i = dev.index if dev.index is not None else torch.cuda.current_device()
+    if i not in _SM_COUNT:
+        _SM_COUNT[i] = torch.cuda.get_device_properties(i).multi_processor_count
+    return _SM_COUNT[i]
+
+
+def page_decode_split_ws_bytes(rows: int, n_c: int) -> int:
+    return int(lib().zkv_page_decode_split_ws_bytes(int(rows), int(n_c)))
+
+
 def page_decode(q, layer: PageLayer, n_c: int, nk: int, n_near: int, *, n_sink: int = 0, near_start: int = 0,
-                scale=None, out=None, lse=None, sel_out=None, status=None, cluster=0):
+                scale=None, out=None, lse=None, sel_out=None, status=None, cluster=0, split=None, workspace=None):
     """Fused page-mode decode: q [bs,1,H*G,128] -> out [bs,1,H*G,128].
 
     Raw rows attended besides the selected pages: [0, n_sink) and
-    [near_start, near_start + n_near) of the layer's near buffers."""
+    [near_start, near_start + n_near) of the layer's near buffers.
+
+    split: None picks the long-context form (zkv_page_decode_split: Quest
+    scores on every SM, then the fused select + attention) when the rows'
+    clusters fill at most half of the SMs and n_c > 2048; True / False force
+    it on / off (results are identical).  workspace: optional uint8 device
+    tensor for the split form (default: one cached buffer per device, so
+    concurrent calls on different streams should pass their own)."""
     cmin = layer.tensors[0]
     bs, H, n_max, D = cmin.shape
     G = q.shape[2] // H
@@ -414,7 +436,25 @@ def page_decode(q, layer: PageLayer, n_c: int, nk: int, n_near: int, *, n_sink: 
     if out is None:
         out = torch.empty(bs, 1, H * G, D, dtype=torch.bfloat16, device=q.device)
     scale = (1.0 / D ** 0.5) if scale is None else float(scale)
-    check(lib().zkv_page_decode(_p(qc), ctypes.byref(layer.struct), bs * H, G, n_max, int(n_c), int(nk), int(n_sink),
+    rows = bs * H
+    if split is None:
+        cs = cluster if cluster in (1, 2, 4, 8) else 8
+        split = cs > 1 and n_c > 2048 and nk < n_c and 2 * rows * cs <= _sm_count(q.device)
+    if split:
+        need = page_decode_split_ws_bytes(rows, n_c)
+        if workspace is None:
+            key = q.device.index if q.device.index is not None else torch.cuda.current_device()
+            ws = _SPLIT_WS.get(key)
+            if ws is None or ws.numel() < need:
+                ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+                _SPLIT_WS[key] = ws
+            workspace = ws
+        check(lib().zkv_page_decode_split(_p(qc), ctypes.byref(layer.struct), rows, G, n_max, int(n_c), int(nk),
+                                          int(n_sink), int(near_start), int(n_near), scale, _p(out), _p(lse),
+                                          _p(sel_out), _p(status), int(cluster), _p(workspace),
+                                          int(workspace.numel()), _stream(q)), "zkv_page_decode_split")
+        return out
+    check(lib().zkv_page_decode(_p(qc), ctypes.byref(layer.struct), rows, G, n_max, int(n_c), int(nk), int(n_sink),
                                 int(near_start), int(n_near), scale, _p(out), _p(lse), _p(sel_out), _p(status),
                                 int(cluster), _stream(q)), "zkv_page_decode")
     return out
