@@ -82,6 +82,15 @@ int zkv_quest_score(const void* raw_q, const void* chunk_min,
                     const void* chunk_max, const uint8_t* valid, float* scores,
                     int rows, int n_chunks, int n_max, void* stream);
 
+/* zkv_quest_score with the GQA mean folded in: q [rows][G][128] bf16
+ * (16-byte aligned); raw_q = bf16(fp32 sum of the G heads in head order /
+ * G) is formed per CTA (polar_cache compute() :1622-1626 + the Quest score
+ * of quest_chunk_score.cu).                                              */
+int zkv_quest_score_gqa(const void* q, int G, const void* chunk_min,
+                        const void* chunk_max, const uint8_t* valid,
+                        float* scores, int rows, int n_chunks, int n_max,
+                        void* stream);
+
 /* Top-k over fp32 rows.  Replaces float_topk_3d
  * (cache_hub/topk/float_topk.cu:280-346).  Selects the k largest by the
  * order-preserving u32 key, ties to the lowest index, and writes them in
@@ -264,9 +273,9 @@ int zkv_page_decode(const void* q, const zkv_page_layer* layer, int rows,
                     void* stream);
 
 /* Long-context form of zkv_page_decode for few rows (same results): the
- * GQA-mean query and the Quest scores of all n_c chunks are computed by
- * kernels that spread over every SM (zkv_gqa_mean, zkv_quest_score) into
- * `workspace`, then the fused kernel reads the scores, selects in two
+ * Quest scores of all n_c chunks are computed by a kernel that spreads
+ * over every SM (zkv_quest_score_gqa) into `workspace`, then the fused
+ * kernel reads the scores, selects in two
  * levels (each cluster CTA's top nk, then the top nk of those) and attends.
  * Falls back to zkv_page_decode where the fused kernel selects in one level
  * (n_c <= 2048, cluster 1, nk >= n_c).  workspace: device, 256-byte

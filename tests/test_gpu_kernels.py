@@ -286,3 +286,18 @@ def test_page_decode_selection_edge_cases(mode, n_c, nk):
         assert (rsel == np.arange(nk)).all()
     if mode != "mixed_sign":  # mixed-sign metadata is not a real key range; selection only
         close(O.bf16_to_f32(to_u16(out)).reshape(R, G, 128), O.bf16_to_f32(ro))
+
+
+def test_quest_score_gqa_equals_mean_then_score():
+    """The folded GQA mean reproduces gqa_mean + quest_chunk_score bit for bit."""
+    bs, H, G, n_c = 2, 4, 4, 300
+    pc, _ = W.build_page_cache(21, bs, H, 16 * n_c, 16, DEV)
+    pc.valid.copy_(torch.rand(pc.valid.shape, device=DEV) > 0.2)
+    q = W.synth_query(torch.Generator(device=DEV).manual_seed(3), bs, H * G, DEV)
+    raw_q = ops.gqa_mean(q, H)
+    ref = torch.empty(bs, H, n_c, device=DEV)
+    ops.quest_chunk_score(raw_q, pc.chunk_min, pc.chunk_max, ref, n_c, chunk_valid=pc.valid)
+    got = torch.empty_like(ref)
+    ops.quest_chunk_score_gqa(q, pc.chunk_min, pc.chunk_max, got, n_c, chunk_valid=pc.valid)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int32), ref.view(torch.int32))

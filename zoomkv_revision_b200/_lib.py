@@ -55,6 +55,7 @@ _SIGNATURES = {
                         _c_void_p, _c_void_p, _c_void_p],
     "zkv_vquant_encode": [_c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p],
     "zkv_quest_score": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p],
+    "zkv_quest_score_gqa": [_c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p],
     "zkv_topk_f32": [_c_void_p, _i32, _i32, _i64, _i32, _c_void_p, _c_void_p],
     "zkv_topk_i32": [_c_void_p, _i32, _i32, _i64, _i32, _c_void_p, _c_void_p],
     "zkv_chunk_density": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _c_void_p],

@@ -892,12 +892,10 @@ extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int r
                             status, cluster, nullptr, 0, stream);
 }
 
-// workspace: raw_q [rows][128] bf16 | scores [rows][n_c] fp32 (256-byte aligned parts)
-static size_t split_ws_raw_bytes(int rows) { return (((size_t)rows * kHeadDim * 2) + 255) & ~(size_t)255; }
-
+// workspace: scores [rows][n_c] fp32
 extern "C" size_t zkv_page_decode_split_ws_bytes(int rows, int n_c) {
     if (rows < 0 || n_c < 0) return 0;
-    return split_ws_raw_bytes(rows) + (((size_t)rows * n_c * 4 + 255) & ~(size_t)255);
+    return ((size_t)rows * n_c * 4 + 255) & ~(size_t)255;
 }
 
 extern "C" int zkv_page_decode_split(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max, int n_c,
@@ -911,13 +909,10 @@ extern "C" int zkv_page_decode_split(const void* q, const zkv_page_layer* layer,
                                status, cluster, stream);
     if (!q || !workspace || ws_bytes < zkv_page_decode_split_ws_bytes(rows, n_c) || G < 1 || G > 8)
         return ZKV_ERR_ARG;
-    if (((uintptr_t)workspace & 255) || ((uintptr_t)q & 7)) return ZKV_ERR_ALIGN;
-    uint8_t* ws = (uint8_t*)workspace;
-    void* raw_q = ws;
-    float* scores = (float*)(ws + split_ws_raw_bytes(rows));
-    int rc = zkv_gqa_mean(q, rows, G, raw_q, stream);
-    if (rc != ZKV_OK) return rc;
-    rc = zkv_quest_score(raw_q, layer->chunk_min, layer->chunk_max, layer->valid, scores, rows, n_c, n_max, stream);
+    if (((uintptr_t)workspace & 255) || ((uintptr_t)q & 15)) return ZKV_ERR_ALIGN;
+    float* scores = (float*)workspace;
+    const int rc = zkv_quest_score_gqa(q, G, layer->chunk_min, layer->chunk_max, layer->valid, scores, rows, n_c,
+                                       n_max, stream);
     if (rc != ZKV_OK) return rc;
     return page_decode_impl(q, layer, rows, G, n_max, n_c, nk, n_sink, near_start, n_near, scale, out, lse, sel_out,
                             status, cluster, scores, n_c, stream);

@@ -10,11 +10,32 @@ __global__ void __launch_bounds__(256) quest_score_kernel(const uint16_t* __rest
                                                           const uint16_t* __restrict__ cmin,
                                                           const uint16_t* __restrict__ cmax,
                                                           const uint8_t* __restrict__ valid,
-                                                          float* __restrict__ scores, int n_chunks, int n_max) {
+                                                          float* __restrict__ scores, int n_chunks, int n_max,
+                                                          const uint16_t* __restrict__ q = nullptr, int G = 0) {
     const int r = blockIdx.y;
     const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
     const int warp = threadIdx.x >> 5;
-    const uint4 qv = *reinterpret_cast<const uint4*>(raw_q + (int64_t)r * kHeadDim + 8 * hl);
+    uint4 qv;
+    if (q) {  // GQA mean of the row's G query heads (fp32 sum in head order, / G, bf16)
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int g = 0; g < G; ++g) {
+            const uint4 v = *reinterpret_cast<const uint4*>(q + ((int64_t)r * G + g) * kHeadDim + 8 * hl);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc[2 * j] = __fadd_rn(acc[2 * j], bfbits2f((uint16_t)(w[j] & 0xffffu)));
+                acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], bfbits2f((uint16_t)(w[j] >> 16)));
+            }
+        }
+        uint32_t m[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            m[j] = (uint32_t)f2bfbits(__fdiv_rn(acc[2 * j], (float)G)) |
+                   ((uint32_t)f2bfbits(__fdiv_rn(acc[2 * j + 1], (float)G)) << 16);
+        qv = make_uint4(m[0], m[1], m[2], m[3]);
+    } else {
+        qv = *reinterpret_cast<const uint4*>(raw_q + (int64_t)r * kHeadDim + 8 * hl);
+    }
     const int base = (blockIdx.x * 8 + warp) * (2 * UNROLL);
     uint4 mn[UNROLL], mx[UNROLL];
 #pragma unroll
@@ -237,6 +258,20 @@ extern "C" int zkv_quest_score(const void* raw_q, const void* chunk_min, const v
     quest_score_kernel<U><<<grid, 256, 0, (cudaStream_t)stream>>>((const uint16_t*)raw_q, (const uint16_t*)chunk_min,
                                                                   (const uint16_t*)chunk_max, valid, scores, n_chunks,
                                                                   n_max);
+    return launch_status();
+}
+
+extern "C" int zkv_quest_score_gqa(const void* q, int G, const void* chunk_min, const void* chunk_max,
+                                   const uint8_t* valid, float* scores, int rows, int n_chunks, int n_max,
+                                   void* stream) {
+    if (!q || G < 1 || G > 64 || rows < 0 || n_chunks < 0 || n_chunks > n_max || rows > 65535) return ZKV_ERR_ARG;
+    if (rows == 0 || n_chunks == 0) return ZKV_OK;
+    if (((uintptr_t)q & 15) || ((uintptr_t)chunk_min & 15) || ((uintptr_t)chunk_max & 15)) return ZKV_ERR_ALIGN;
+    constexpr int U = 4;
+    dim3 grid((n_chunks + 8 * 2 * U - 1) / (8 * 2 * U), rows);
+    quest_score_kernel<U><<<grid, 256, 0, (cudaStream_t)stream>>>(nullptr, (const uint16_t*)chunk_min,
+                                                                  (const uint16_t*)chunk_max, valid, scores, n_chunks,
+                                                                  n_max, (const uint16_t*)q, G);
     return launch_status();
 }
 

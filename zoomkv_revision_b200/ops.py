@@ -113,6 +113,31 @@ def quest_chunk_score(raw_q, chunk_min, chunk_max, scores_out, n_chunks, chunk_v
                                 n_chunks, n_max, _stream(raw_q)), "zkv_quest_score")
 
 
+def quest_chunk_score_gqa(q, chunk_min, chunk_max, scores_out, n_chunks, chunk_valid=None):
+    """quest_chunk_score with the GQA mean folded into the kernel: q
+    [bs, 1, kv*G, 128] bf16 (the decode query) instead of raw_q."""
+    _cuda(("q", q), ("chunk_min", chunk_min), ("chunk_max", chunk_max), ("scores", scores_out),
+          ("valid", chunk_valid))
+    _dtype("q", q, torch.bfloat16)
+    _contig("q", q)
+    for n, t in (("chunk_min", chunk_min), ("chunk_max", chunk_max)):
+        _dtype(n, t, torch.bfloat16)
+        if t.stride(3) != 1 or t.stride(2) != 128 or t.stride(0) != t.shape[1] * t.stride(1):
+            raise ValueError(f"{n} must be a chunk range of a contiguous [bs, kv, n_max, 128] buffer")
+    _dtype("scores_out", scores_out, torch.float32)
+    _contig("scores_out", scores_out)
+    bs, kv = chunk_min.shape[0], chunk_min.shape[1]
+    G = q.shape[2] // kv
+    n_max = chunk_min.stride(1) // 128
+    n_chunks = int(n_chunks)
+    if n_chunks > chunk_min.shape[2] or scores_out.numel() < bs * kv * n_chunks:
+        raise ValueError("n_chunks / scores_out size")
+    if chunk_valid is not None:
+        _dtype("chunk_valid", chunk_valid, torch.bool)
+    check(lib().zkv_quest_score_gqa(_p(q), G, _p(chunk_min), _p(chunk_max), _p(chunk_valid), _p(scores_out), bs * kv,
+                                    n_chunks, n_max, _stream(q)), "zkv_quest_score_gqa")
+
+
 # ----------------------------------------------------------------- top-k
 def float_topk(scores: torch.Tensor, k: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """Top-k indices [B, k] int64 of fp32 [B, L] (ties -> lowest index, ascending)."""
