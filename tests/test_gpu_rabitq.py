@@ -153,9 +153,12 @@ def test_rerank4_matches_reference_scores():
         assert np.array_equal(fin.cpu().numpy(), np.take_along_axis(g[f"c{i}_cand"].reshape(H, C), sel, 1)), i
 
 
-def test_rerank4_token_layout_vs_oracle():
+@pytest.mark.parametrize("N,C,F", [(5000, 1500, 100), (8000, 5000, 300)])
+def test_rerank4_token_layout_vs_oracle(N, C, F):
+    """Cluster-split scoring; rank 0 selects with the small-n select up to
+    4096 candidates and the general select beyond."""
     rng = np.random.default_rng(11)
-    R, N, C, F = 3, 5000, 1500, 100
+    R = 3
     keys = O.f32_to_bf16((rng.standard_normal((R, N, 128)) * rng.uniform(0.2, 3, (R, N, 1))).astype(np.float32))
     signs = O.f32_to_bf16(np.where(rng.random(128) < 0.5, -1.0, 1.0).astype(np.float32))
     q = O.f32_to_bf16(rng.standard_normal((R, 4, 128)).astype(np.float32))
@@ -192,7 +195,7 @@ def test_coarse2bit_vs_oracle(layout):
     assert np.array_equal(out.cpu().numpy(), O.coarse2bit(packed, qs, qm))
 
 
-@pytest.mark.parametrize("N,C,K", [(4096, None, 1024), (20000, 4096, 1024), (3000, 700, 700)])
+@pytest.mark.parametrize("N,C,K", [(4096, None, 1024), (20000, 4096, 1024), (3000, 700, 700), (8000, 6000, 1000)])
 def test_popcount_topk_vs_oracle(N, C, K):
     rng = np.random.default_rng(N + K)
     R = 3

@@ -340,8 +340,16 @@ struct CollArgs {
 // Tier-hit weight of every bucket of block b (one warp): bucket scores,
 // bitonic sort of (desc score, bucket id), prefix of bucket sizes in that
 // order, weight = #tiers whose target exceeds the prefix.
-__device__ __forceinline__ void collision_table(const CollArgs& a, int row, int b, uint8_t* table) {
+__device__ __forceinline__ void collision_table(const CollArgs& a, int row, int b, uint8_t* table, int* hs) {
     const int lane = threadIdx.x & 31;
+    const int32_t* h = a.L.hist + ((int64_t)row * kB + b) * kK;
+    int hpre[8];  // bucket sizes in bucket order, loaded alongside the query block
+    {
+        const int4 h0 = *reinterpret_cast<const int4*>(h + 8 * lane);
+        const int4 h1 = *reinterpret_cast<const int4*>(h + 8 * lane + 4);
+        hpre[0] = h0.x; hpre[1] = h0.y; hpre[2] = h0.z; hpre[3] = h0.w;
+        hpre[4] = h1.x; hpre[5] = h1.y; hpre[6] = h1.z; hpre[7] = h1.w;
+    }
     float q[kM];
     {
         const uint4 r = *reinterpret_cast<const uint4*>(a.qb + (int64_t)row * kHeadDim + kM * b);
@@ -393,12 +401,15 @@ __device__ __forceinline__ void collision_table(const CollArgs& a, int row, int 
             }
         }
     }
-    const int32_t* h = a.L.hist + ((int64_t)row * kB + b) * kK;
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < 8; ++r) hs[8 * lane + r] = hpre[r];
+    __syncwarp();
     int hv[8];
     long long lsum = 0;
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
-        hv[r] = h[key[r] & 0xffu];
+        hv[r] = hs[key[r] & 0xffu];
         lsum += hv[r];
     }
     long long incl = lsum;
@@ -476,7 +487,9 @@ __global__ void __launch_bounds__(256, 4) collision_topk_kernel(const CollArgs a
     int* gh = hist + 136;                                      // global histogram [136]
     int* scratch = gh + 136;                                   // 40
     int* misc = scratch + 40;                                  // 24: vstar, n_gt, eq_r[8], gt_r[8]
-    uint8_t* cnts = reinterpret_cast<uint8_t*>(misc + 24);     // [per] (padded to 512)
+    int* hs = misc + 24;                                       // [8 warps][256] bucket sizes (table build)
+    int* ghall = hs + 8 * kK;                                  // [CS][136] every CTA's histogram
+    uint8_t* cnts = reinterpret_cast<uint8_t*>(ghall + 8 * 136);  // [per] (padded to 512)
     cg::cluster_group cluster = cg::this_cluster();
     const int CS = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
     const int row = blockIdx.x / CS;
@@ -490,7 +503,7 @@ __global__ void __launch_bounds__(256, 4) collision_topk_kernel(const CollArgs a
     int* selb = eqb + nch;                                     // [nch] exclusive prefix of selected
 
     cluster.barrier_arrive();  // peers are running before the first remote store
-    for (int b = rank + CS * warp; b < kB; b += CS * 8) collision_table(a, row, b, table);
+    for (int b = rank + CS * warp; b < kB; b += CS * 8) collision_table(a, row, b, table, hs + warp * kK);
     for (int i = tid; i < 136; i += 256) hist[i] = 0;
     if (tid < 24) misc[tid] = 0;
     cluster.barrier_wait();
@@ -540,12 +553,16 @@ __global__ void __launch_bounds__(256, 4) collision_topk_kernel(const CollArgs a
     }
     if (!a.idx_out) return;  // counts only (uniform over the cluster)
     __syncthreads();
-    cluster.sync();  // every CTA's histogram is complete
-
-    // global histogram over the cluster (remote reads)
+    // push this CTA's histogram into slot `rank` of every CTA; after the
+    // barrier all reads are local and no remote access follows
+    for (int i = tid; i < CS * kCntBins; i += 256) {
+        const int p = i / kCntBins, v = i - p * kCntBins;
+        cluster.map_shared_rank(ghall, p)[rank * 136 + v] = hist[v];
+    }
+    cluster.sync();
     for (int v = tid; v < kCntBins; v += 256) {
         int s = 0;
-        for (int r = 0; r < CS; ++r) s += cluster.map_shared_rank(hist, r)[v];
+        for (int r = 0; r < CS; ++r) s += ghall[r * 136 + v];
         gh[v] = s;
     }
     __syncthreads();
@@ -580,8 +597,8 @@ __global__ void __launch_bounds__(256, 4) collision_topk_kernel(const CollArgs a
     }
     __syncthreads();
     const int vstar = misc[0];
-    if (warp < CS) {  // per-rank (> vstar, == vstar) counts (remote reads)
-        const int* hr = cluster.map_shared_rank(hist, warp);
+    if (warp < CS) {  // per-rank (> vstar, == vstar) counts
+        const int* hr = ghall + warp * 136;
         int gt = 0, eq = 0;
         for (int v = lane; v < kCntBins; v += 32) {
             const int x = hr[v];
@@ -599,7 +616,6 @@ __global__ void __launch_bounds__(256, 4) collision_topk_kernel(const CollArgs a
         }
     }
     __syncthreads();
-    cluster.sync();  // no remote reads after this point
 
     int need_eq = a.C - misc[1], off = 0, take_eq = 0;
     for (int r = 0; r <= rank; ++r) {
@@ -1025,8 +1041,8 @@ extern "C" int zkv_collision_topk(const void* q_blocks, const zkv_rq_layout* lay
     CS = CS < need ? (need > 8 ? 8 : need) : CS;
     const int per = (kv_len + CS - 1) / CS;
     const size_t nch = ((size_t)per + 511) / 512;
-    const size_t smem = (size_t)kB * kK + (136 + 136 + 40 + 24) * sizeof(int) + (((size_t)per + 511) & ~(size_t)511) +
-                        nch * 16;
+    const size_t smem = (size_t)kB * kK + (136 + 136 + 40 + 24 + 8 * kK + 8 * 136) * sizeof(int) +
+                        (((size_t)per + 511) & ~(size_t)511) + nch * 16;
     if (smem > 200 * 1024) return ZKV_ERR_CAPACITY;
     CollArgs a;
     a.qb = (const uint16_t*)q_blocks;
