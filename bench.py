@@ -315,9 +315,14 @@ def run_config3(args):
             layer_loop()
         step = graph.replay
     else:
-        def step():
+        def layer_loop():
             for l in range(layers):
                 S.decode_step(qs[l], layers_local[l], n_c, nk, bufs[l], rank=rank, world=world, n_near=n_near)
+
+        # eager: capturing these NCCL all-gathers in a CUDA graph hung on
+        # this pool, so the multi-GPU step is not captured
+        step = layer_loop
+        mode = "eager"
 
     with torch.cuda.stream(stream):
         step()
@@ -332,7 +337,7 @@ def run_config3(args):
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "config3", "layers": layers, "batch": bs, "context": ctx, "budget_tokens": budget,
-                       "parallelism": f"sequence split x{world}" if world > 1 else
+                       "parallelism": f"sequence split x{world} ({mode})" if world > 1 else
                        "single GPU: all-SM Quest scores + fused two-level select/attention, CUDA graph",
                        "l2": "bytes per step ~1.4 GB > L2"},
             "roofline": {"bound": "hbm", "achieved_per_gpu": ach / world, "peak": peak, "unit": "GB/s",
