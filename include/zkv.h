@@ -272,10 +272,12 @@ int zkv_page_decode(const void* q, const zkv_page_layer* layer, int rows,
                     float* lse, int64_t* sel_out, int32_t* status, int cluster,
                     void* stream);
 
-/* Long-context form of zkv_page_decode for few rows (same results): the
- * Quest scores of all n_c chunks are computed by a kernel that spreads
- * over every SM (zkv_quest_score_gqa) into `workspace`, then the fused
- * kernel reads the scores, selects in two
+/* Long-context form of zkv_page_decode for few rows (same selection; the
+ * output can differ by fp32 rounding): the Quest scores of all n_c chunks
+ * are computed by a kernel that spreads over every SM
+ * (zkv_quest_score_gqa) into `workspace`; then the fused kernel, with up to
+ * 4 clusters per row that each attend a share of the selected pages, merged
+ * by zkv_lse_merge_n; the fused kernel reads the scores, selects in two
  * levels (each cluster CTA's top nk, then the top nk of those) and attends.
  * Falls back to zkv_page_decode where the fused kernel selects in one level
  * (n_c <= 2048, cluster 1, nk >= n_c).  workspace: device, 256-byte

@@ -246,7 +246,7 @@ def test_lse_merge_golden():
 @pytest.mark.parametrize("mode,n_c,nk", [("ties", 400, 64), ("invalid", 400, 64), ("mixed_sign", 400, 64),
                                          ("plain", 2600, 64), ("ties", 2600, 64), ("invalid", 2600, 64),
                                          ("mixed_sign", 2600, 64), ("plain", 2050, 300), ("mostly_invalid", 2050, 300),
-                                         ("plain", 8184, 256)])
+                                         ("plain", 8184, 256), ("plain", 2600, 3)])
 def test_page_decode_selection_edge_cases(mode, n_c, nk):
     """Selection paths of the fused kernel: all-equal scores (heavy-tie
     fallback, lowest ids win), invalid chunks (-inf), mixed-sign scores
@@ -273,7 +273,11 @@ def test_page_decode_selection_edge_cases(mode, n_c, nk):
     sel2 = torch.empty_like(sel)  # long-context form: scores from the all-SM kernel
     out2 = ops.page_decode(q, pc.layer(), pc.n_c, nk, 16, sel_out=sel2, cluster=8, split=True)
     torch.cuda.synchronize()
-    assert torch.equal(sel2, sel) and torch.equal(out2, out)
+    # same selection; with n_c > 2048 the split form spreads the pages of a row
+    # over several clusters and merges their (out, lse) -> fp32 rounding only
+    assert torch.equal(sel2, sel)
+    if n_c <= 2048:
+        assert torch.equal(out2, out)
     R = bs * H
     ro, _, rsel = O.page_decode(
         to_u16(q).reshape(R, G, 128), to_u16(pc.chunk_min).reshape(R, -1, 128), to_u16(pc.chunk_max).reshape(R, -1, 128),
@@ -286,6 +290,7 @@ def test_page_decode_selection_edge_cases(mode, n_c, nk):
         assert (rsel == np.arange(nk)).all()
     if mode != "mixed_sign":  # mixed-sign metadata is not a real key range; selection only
         close(O.bf16_to_f32(to_u16(out)).reshape(R, G, 128), O.bf16_to_f32(ro))
+        close(O.bf16_to_f32(to_u16(out2)).reshape(R, G, 128), O.bf16_to_f32(ro))
 
 
 def test_quest_score_gqa_equals_mean_then_score():

@@ -387,6 +387,8 @@ struct PageArgs {
     int n_cand;     // two-level select: CS * nk candidate slots (0 = one-level)
     const float* sc_in;  // two-level only: precomputed chunk scores [rows][sc_ld] (NULL = score here)
     int64_t sc_ld;
+    int parts;           // two-level only: clusters per row, each attends 1/parts of the selected
+                         // pages; > 1 writes fp32 partials [part][rows] to out_f32 / lse
     float sl2;
     uint16_t* out;
     float* lse;
@@ -407,7 +409,9 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
     cg::cluster_group cluster = cg::this_cluster();
     const int CS = (int)cluster.num_blocks();
     const int rank = (int)cluster.block_rank();
-    const int64_t row = blockIdx.x / CS;
+    const int64_t cid = blockIdx.x / CS;
+    const int64_t row = kTwoLevel ? cid / a.parts : cid;
+    const int part = kTwoLevel ? (int)(cid % a.parts) : 0;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
     uint8_t* region = smem;
@@ -636,16 +640,20 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
                                            scan, [&](int pos, int i) { sel_s[pos] = i; }, true, lo, hi);
         }
     }
-    if (a.sel_out && rank == 0 && !a.sel_in)
+    if (a.sel_out && rank == 0 && part == 0 && !a.sel_in)
         for (int i = threadIdx.x; i < a.nk; i += kAttnThreads) a.sel_out[row * a.nk + i] = sel_s[i];
 
     // ------------------------------------------------ phase 3: attention
     WarpAttn st;
     warp_attn_init(st, q_s, a.G);
     const int nsel = a.sel_in ? s_nsel : a.nk;
-    const int pp = a.sel_in ? (nsel + CS - 1) / CS : a.pp;
-    const int p_lo = rank * pp, p_hi = min(nsel, p_lo + pp);
-    const int n_raw_all = a.n_sink + a.n_near;
+    // this cluster's share of the selection list (the whole list unless parts > 1)
+    const int part_pp = kTwoLevel ? (nsel + a.parts - 1) / a.parts : nsel;
+    const int part_lo = kTwoLevel ? min(nsel, part * part_pp) : 0;
+    const int part_hi = kTwoLevel ? min(nsel, part_lo + part_pp) : nsel;
+    const int pp = a.sel_in ? (nsel + CS - 1) / CS : (kTwoLevel ? (part_hi - part_lo + CS - 1) / CS : a.pp);
+    const int p_lo = part_lo + rank * pp, p_hi = min(part_hi, p_lo + pp);
+    const int n_raw_all = part == 0 ? a.n_sink + a.n_near : 0;  // raw rows: part 0 only
     const int n_lo = rank * a.pn, n_hi = min(n_raw_all, n_lo + a.pn);
     const int n_pages = max(0, p_hi - p_lo);
     const int n_raw = max(0, (n_hi - n_lo + 3) / 4);
@@ -697,9 +705,10 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
     grid_dep_launch_next();
     __syncthreads();
     cta_merge(st, a.G, reinterpret_cast<float*>(region), cm, cl, co);
+    const int64_t orow = kTwoLevel ? (int64_t)part * (gridDim.x / (CS * a.parts)) + row : row;
     cluster_merge(cluster, CS, a.G, cm, cl, co, reinterpret_cast<float*>(region),
-                  a.out ? a.out + row * a.G * kHeadDim : nullptr, a.lse ? a.lse + row * a.G : nullptr,
-                  a.out_f32 ? a.out_f32 + row * a.G * kHeadDim : nullptr);
+                  a.out ? a.out + orow * a.G * kHeadDim : nullptr, a.lse ? a.lse + orow * a.G : nullptr,
+                  a.out_f32 ? a.out_f32 + orow * a.G * kHeadDim : nullptr);
     if (threadIdx.x == 0 && s_failed) set_status(a.status, ZKV_ERR_TIMEOUT);
 }
 
@@ -836,9 +845,9 @@ static int pick_cluster(int requested, int rows) {
 static int page_decode_impl(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max, int n_c, int nk,
                             int n_sink, int near_start, int n_near, float scale, void* out, float* lse,
                             int64_t* sel_out, int32_t* status, int cluster, const float* sc_in, int64_t sc_ld,
-                            void* stream) {
-    if (!q || !layer || !out || rows < 0 || G < 1 || G > 8 || n_c < 0 || n_c > n_max || nk < 1 || n_near < 0 ||
-        n_sink < 0 || near_start < 0)
+                            int parts, float* out_f32, void* stream) {
+    if (!q || !layer || (!out && !out_f32) || rows < 0 || G < 1 || G > 8 || n_c < 0 || n_c > n_max || nk < 1 ||
+        n_near < 0 || n_sink < 0 || near_start < 0)
         return ZKV_ERR_ARG;
     if (nk > n_c && n_c > 0) return ZKV_ERR_ARG;
     if ((int64_t)near_start + n_near > layer->near_ld || n_sink > layer->near_ld) return ZKV_ERR_ARG;
@@ -871,6 +880,7 @@ static int page_decode_impl(const void* q, const zkv_page_layer* layer, int rows
     a.n_cand = (CS > 1 && n_c > 16 * kAttnThreads && a.nk < n_c) ? ((CS * a.nk + 3) & ~3) : 0;
     a.sc_in = a.n_cand ? sc_in : nullptr;
     a.sc_ld = sc_ld;
+    a.parts = a.n_cand ? parts : 1;
     a.pn = ((n_sink + n_near + CS - 1) / CS + 3) & ~3;
     a.sl2 = scale * 1.4426950408889634f;
     a.out = (uint16_t*)out;
@@ -879,23 +889,31 @@ static int page_decode_impl(const void* q, const zkv_page_layer* layer, int rows
     a.status = status;
     a.sel_in = nullptr;
     a.sel_lo = a.sel_hi = 0;
-    a.out_f32 = nullptr;
+    a.out_f32 = out_f32;
     void* args[] = {&a};
     return launch_clustered(a.n_cand ? (const void*)page_decode_kernel<true> : (const void*)page_decode_kernel<false>,
-                            rows * CS, kAttnThreads, CS, page_smem(a), (cudaStream_t)stream, args, /*pdl=*/true);
+                            rows * a.parts * CS, kAttnThreads, CS, page_smem(a), (cudaStream_t)stream, args,
+                            /*pdl=*/true);
 }
 
 extern "C" int zkv_page_decode(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max, int n_c,
                                int nk, int n_sink, int near_start, int n_near, float scale, void* out, float* lse,
                                int64_t* sel_out, int32_t* status, int cluster, void* stream) {
+    if (!out) return ZKV_ERR_ARG;
     return page_decode_impl(q, layer, rows, G, n_max, n_c, nk, n_sink, near_start, n_near, scale, out, lse, sel_out,
-                            status, cluster, nullptr, 0, stream);
+                            status, cluster, nullptr, 0, 1, nullptr, stream);
 }
 
-// workspace: scores [rows][n_c] fp32
+// workspace: scores [rows][n_c] fp32 | part outputs [parts][rows][G][128] fp32 | part lse [parts][rows][G]
+// (sized for parts <= kMaxParts, G <= 8)
+constexpr int kMaxParts = 4;
+static size_t split_ws_scores_bytes(int rows, int n_c) { return ((size_t)rows * n_c * 4 + 255) & ~(size_t)255; }
+static size_t split_ws_parts_bytes(int rows) { return ((size_t)kMaxParts * rows * 8 * kHeadDim * 4 + 255) & ~(size_t)255; }
+
 extern "C" size_t zkv_page_decode_split_ws_bytes(int rows, int n_c) {
     if (rows < 0 || n_c < 0) return 0;
-    return ((size_t)rows * n_c * 4 + 255) & ~(size_t)255;
+    return split_ws_scores_bytes(rows, n_c) + split_ws_parts_bytes(rows) +
+           (((size_t)kMaxParts * rows * 8 * 4 + 255) & ~(size_t)255);
 }
 
 extern "C" int zkv_page_decode_split(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max, int n_c,
@@ -910,12 +928,25 @@ extern "C" int zkv_page_decode_split(const void* q, const zkv_page_layer* layer,
     if (!q || !workspace || ws_bytes < zkv_page_decode_split_ws_bytes(rows, n_c) || G < 1 || G > 8)
         return ZKV_ERR_ARG;
     if (((uintptr_t)workspace & 255) || ((uintptr_t)q & 15)) return ZKV_ERR_ALIGN;
-    float* scores = (float*)workspace;
-    const int rc = zkv_quest_score_gqa(q, G, layer->chunk_min, layer->chunk_max, layer->valid, scores, rows, n_c,
-                                       n_max, stream);
+    uint8_t* ws = (uint8_t*)workspace;
+    float* scores = (float*)ws;
+    float* part_out = (float*)(ws + split_ws_scores_bytes(rows, n_c));
+    float* part_lse = (float*)(ws + split_ws_scores_bytes(rows, n_c) + split_ws_parts_bytes(rows));
+    int rc = zkv_quest_score_gqa(q, G, layer->chunk_min, layer->chunk_max, layer->valid, scores, rows, n_c, n_max,
+                                 stream);
     if (rc != ZKV_OK) return rc;
-    return page_decode_impl(q, layer, rows, G, n_max, n_c, nk, n_sink, near_start, n_near, scale, out, lse, sel_out,
-                            status, cluster, scores, n_c, stream);
+    // clusters per row: spread the attention over about half of the SMs' CTA slots
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int parts = (2 * sms) / (rows * CS);
+    parts = parts < 1 ? 1 : (parts > kMaxParts ? kMaxParts : parts);
+    if (parts == 1)
+        return page_decode_impl(q, layer, rows, G, n_max, n_c, nk, n_sink, near_start, n_near, scale, out, lse,
+                                sel_out, status, cluster, scores, n_c, 1, nullptr, stream);
+    rc = page_decode_impl(q, layer, rows, G, n_max, n_c, nk, n_sink, near_start, n_near, scale, nullptr, part_lse,
+                          sel_out, status, cluster, scores, n_c, parts, part_out, stream);
+    if (rc != ZKV_OK) return rc;
+    return zkv_lse_merge_n(part_out, part_lse, parts, rows * G, kHeadDim, out, lse, stream);
 }
 
 extern "C" int zkv_page_attend(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max,
@@ -954,6 +985,7 @@ extern "C" int zkv_page_attend(const void* q, const zkv_page_layer* layer, int r
     a.n_cand = 0;
     a.sc_in = nullptr;
     a.sc_ld = 0;
+    a.parts = 1;
     a.pn = ((n_sink + n_near + CS - 1) / CS + 3) & ~3;
     a.sl2 = scale * 1.4426950408889634f;
     a.out = (uint16_t*)out;

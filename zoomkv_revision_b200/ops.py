@@ -451,7 +451,9 @@ def page_decode(q, layer: PageLayer, n_c: int, nk: int, n_near: int, *, n_sink: 
     split: None picks the long-context form (zkv_page_decode_split: Quest
     scores on every SM, then the fused select + attention) when the rows'
     clusters fill at most half of the SMs and n_c > 2048; True / False force
-    it on / off (results are identical).  workspace: optional uint8 device
+    it on / off (same selection; the split form may spread a row's pages over
+    several clusters and merge their (out, lse), so the output can differ from
+    the fused form by fp32 rounding).  workspace: optional uint8 device
     tensor for the split form (default: one cached buffer per device, so
     concurrent calls on different streams should pass their own)."""
     cmin = layer.tensors[0]
