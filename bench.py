@@ -330,6 +330,10 @@ def run_config3(args):
     with ClockSampler(local_rank) as clk:
         ms = _timed(step, args.steps, args.warmup, stream, world)
     bytes_step = layers * W.page_algorithmic_bytes(bs * H, n_c, nk, n_near, G)
+    if world == 1:
+        launches = layers * args.steps * ops.page_decode_plan(bs * H, n_c, nk, device=dev)["launches"]
+    else:  # per layer: GQA mean, local scores, global top-k, attend, LSE merge (+ NCCL all-gathers)
+        launches = layers * args.steps * 5
     peak, kind = load_peaks()
     ach = bytes_step / (ms / 1e3) / 1e9
     line = {"metric": "config3 sparse decode tokens/s at Qwen3-4B shape, 131072 ctx (sequence split)",
@@ -340,6 +344,7 @@ def run_config3(args):
                        "parallelism": f"sequence split x{world} ({mode})" if world > 1 else
                        "single GPU: all-SM Quest scores + fused two-level select/attention, CUDA graph",
                        "l2": "bytes per step ~1.4 GB > L2"},
+            "gpu_launches": launches,
             "roofline": {"bound": "hbm", "achieved_per_gpu": ach / world, "peak": peak, "unit": "GB/s",
                          "frac_per_gpu": ach / world / peak, "peak_kind": kind, "bytes_per_step": bytes_step},
             "clocks": clk.summary()}

@@ -379,6 +379,26 @@ __device__ void cluster_merge(cg::cluster_group& cluster, int CS, int G, const f
     }
 }
 
+// One copy of each select in the binary for both levels of the two-level
+// select (that instantiation stalls on instruction fetch; the one-level one
+// keeps its select inline, where a call measured ~1 us slower).  Top k of sc[0..n) (ties to the
+// lowest index, ascending index order): out_id[pos] = id_in ? id_in[i] :
+// id_base + i, and out_sc[pos] = sc[i] when out_sc != NULL.  sc is 16-byte
+// aligned; lo / hi: min finite and max ordered key.
+__device__ __noinline__ void select_pairs(const float* sc, int n, int k, uint32_t lo, uint32_t hi, int* hist,
+                                          int* misc, int* scan, const int* id_in, int id_base, float* out_sc,
+                                          int* out_id) {
+    auto emit = [&](int pos, int i) {
+        if (out_sc) out_sc[pos] = sc[i];
+        out_id[pos] = id_in ? id_in[i] : id_base + i;
+    };
+    if (n <= 16 * kAttnThreads)
+        block_topk_small<kAttnThreads>(sc, n, k, lo, hi, hist, misc, scan, emit);
+    else
+        block_topk<kAttnThreads, true>([&](int i) { return ordered_u32(sc[i]); }, n, k, hist, misc, scan, emit, true,
+                                       lo, hi);
+}
+
 // ---------------------------------------------------------------- page decode
 struct PageArgs {
     const uint16_t* q;
@@ -558,15 +578,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
         float* my_sc = cand_sc + rank * a.nk;
         int* my_id = cand_id + rank * a.nk;
         if (n_my > a.nk) {
-            auto emit = [&](int pos, int i) {
-                my_sc[pos] = sc_all[c0 + i];
-                my_id[pos] = c0 + i;
-            };
-            if (n_my <= 16 * kAttnThreads)
-                block_topk_small<kAttnThreads>(sc_all + c0, n_my, a.nk, s_mm[0], s_mm[1], hist, misc, scan, emit);
-            else
-                block_topk<kAttnThreads, true>([&](int i) { return ordered_u32(sc_all[c0 + i]); }, n_my, a.nk, hist,
-                                               misc, scan, emit, true, s_mm[0], s_mm[1]);
+            select_pairs(sc_all + c0, n_my, a.nk, s_mm[0], s_mm[1], hist, misc, scan, nullptr, c0, my_sc, my_id);
         } else {
             for (int i = threadIdx.x; i < a.nk; i += kAttnThreads) {
                 my_sc[i] = i < n_my ? sc_all[c0 + i] : __uint_as_float(0xffffffffu);
@@ -625,14 +637,8 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
             hi = max(hi, s_mm[3 + 2 * r]);
         }
         if (kTwoLevel) {  // level 2 over the CS * nk candidates
-            if (a.n_cand <= 16 * kAttnThreads)
-                block_topk_small<kAttnThreads>(cand_sc, a.n_cand, a.nk, lo, hi, hist, misc, scan,
-                                               [&](int pos, int i) { sel_s[pos] = cand_id[i]; });
-            else
-                block_topk<kAttnThreads, true>([&](int i) { return ordered_u32(cand_sc[i]); }, a.n_cand, a.nk, hist,
-                                               misc, scan, [&](int pos, int i) { sel_s[pos] = cand_id[i]; }, true, lo,
-                                               hi);
-        } else if (a.n_c <= 16 * kAttnThreads) {
+            select_pairs(cand_sc, a.n_cand, a.nk, lo, hi, hist, misc, scan, cand_id, 0, nullptr, sel_s);
+        } else if (a.n_c <= 16 * kAttnThreads) {  // inline here: a call costs ~1 us at config 1
             block_topk_small<kAttnThreads>(sc_all, a.n_c, a.nk, lo, hi, hist, misc, scan,
                                            [&](int pos, int i) { sel_s[pos] = i; });
         } else {

@@ -441,6 +441,21 @@ def page_decode_split_ws_bytes(rows: int, n_c: int) -> int:
     return int(lib().zkv_page_decode_split_ws_bytes(int(rows), int(n_c)))
 
 
+def page_decode_plan(rows: int, n_c: int, nk: int, cluster: int = 0, split=None, device=None) -> dict:
+    """How page_decode runs a layer: {'split': bool, 'parts': clusters per
+    row, 'launches': kernels per call} (the rule zkv_page_decode_split and
+    page_decode apply)."""
+    dev = torch.device("cuda") if device is None else torch.device(device)
+    cs = cluster if cluster in (1, 2, 4, 8) else 8
+    two_level = cs > 1 and n_c > 2048 and nk < n_c
+    if split is None:
+        split = two_level and 2 * rows * cs <= _sm_count(dev)
+    if not (split and two_level):
+        return {"split": False, "parts": 1, "launches": 1}
+    parts = max(1, min(4, (2 * _sm_count(dev)) // (rows * cs)))
+    return {"split": True, "parts": parts, "launches": 3 if parts > 1 else 2}
+
+
 def page_decode(q, layer: PageLayer, n_c: int, nk: int, n_near: int, *, n_sink: int = 0, near_start: int = 0,
                 scale=None, out=None, lse=None, sel_out=None, status=None, cluster=0, split=None, workspace=None):
     """Fused page-mode decode: q [bs,1,H*G,128] -> out [bs,1,H*G,128].
