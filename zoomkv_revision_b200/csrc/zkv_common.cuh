@@ -521,33 +521,37 @@ __device__ void block_topk_small(const float* sc, int n, int k, uint32_t lo, uin
     const int sh = bits > 9 ? bits - 9 : 0;
     const float flo = float_of_ordered(lo), fhi = float_of_ordered(hi);
     const float inv = (hi > lo) ? (float)NB / (fhi - flo) : 0.0f;
+    // Straight-line bucket loops (one uniform branch): any bucketing that is
+    // monotone in the key and shared by all passes gives the exact selection.
     uint32_t bk[E];
+    if (same_sign) {
 #pragma unroll
-    for (int u = 0; u < E; ++u) {
-        const uint32_t kk = kr[u];
-        uint32_t b;
-        if (same_sign) {
-            b = kk >= lo ? min((kk - lo) >> sh, (uint32_t)(NB - 1)) : 0u;
-        } else if (kk <= kOrderedNegInf || hi <= lo) {
-            b = 0u;
-        } else {
-            const float fb = (float_of_ordered(kk) - flo) * inv;
-            b = fb >= (float)(NB - 1) ? (uint32_t)(NB - 1) : (fb > 0.0f ? (uint32_t)fb : 0u);
+        for (int u = 0; u < E; ++u) {
+            const uint32_t kk = kr[u];
+            bk[u] = kk >= lo ? min((kk - lo) >> sh, (uint32_t)(NB - 1)) : 0u;
         }
-        bk[u] = b;
+    } else {
+        // -inf, NaN-patterned keys below it, and every key when hi <= lo
+        // (inv == 0) clamp to bucket 0
+#pragma unroll
+        for (int u = 0; u < E; ++u) {
+            const float fb = fminf(fmaxf((float_of_ordered(kr[u]) - flo) * inv, 0.0f), (float)(NB - 1));
+            bk[u] = (uint32_t)fb;
+        }
     }
     __syncthreads();
 #pragma unroll
     for (int u = 0; u < E; ++u)
         if (base + u < n) atomicAdd(&hist[bk[u]], 1);
     __syncthreads();
-    if (warp == 0) {
-        constexpr int PL = NB / 32;
+    {   // bin of the k-th best: suffix counts, every warp scanning NB / NW bins
+        constexpr int PL = NB / NT;  // bins per thread
+        const int b0 = PL * tid;
         int local[PL];
         int tot = 0;
 #pragma unroll
         for (int j = PL - 1; j >= 0; --j) {
-            tot += hist[PL * lane + j];
+            tot += hist[b0 + j];
             local[j] = tot;
         }
         int incl = tot;
@@ -556,15 +560,19 @@ __device__ void block_topk_small(const float* sc, int n, int k, uint32_t lo, uin
             const int v = __shfl_down_sync(0xffffffffu, incl, off);
             if (lane + off < 32) incl += v;
         }
-        const int above = incl - tot;
+        if (lane == 0) scan[2 * NT - NW + warp] = incl;  // warp totals (scan[] tail is free here)
+        __syncthreads();
+        int above = incl - tot;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) above += w > warp ? scan[2 * NT - NW + w] : 0;
 #pragma unroll
         for (int j = 0; j < PL; ++j) {
             const int ge = above + local[j];
-            const int gt = ge - hist[PL * lane + j];
+            const int gt = ge - hist[b0 + j];
             if (gt < k && ge >= k) {
-                misc[0] = PL * lane + j;
+                misc[0] = b0 + j;
                 misc[1] = gt;
-                misc[2] = hist[PL * lane + j];
+                misc[2] = hist[b0 + j];
             }
         }
     }
@@ -580,13 +588,23 @@ __device__ void block_topk_small(const float* sc, int n, int k, uint32_t lo, uin
         block_select_compact<NT>(key, n, tk, take_eq, scan, out);
         return;
     }
+    uint32_t pm = 0u, gm = 0u;  // this thread's pivot-bin keys (few) and keys of higher bins
 #pragma unroll
-    for (int u = 0; u < E; ++u)
-        if (base + u < n && bk[u] == bstar) {
-            const int p = atomicAdd(&misc[3], 1);
-            scan[p] = (int)kr[u];
-            scan[NT + p] = base + u;
-        }
+    for (int u = 0; u < E; ++u) {
+        pm |= (uint32_t)(base + u < n && bk[u] == bstar) << u;
+        gm |= (uint32_t)(base + u < n && bk[u] > bstar) << u;
+    }
+    const uint32_t pm_all = pm;
+    while (pm) {
+        const int u = __ffs(pm) - 1;
+        pm &= pm - 1u;
+        uint32_t kv = 0u;
+#pragma unroll
+        for (int j = 0; j < E; ++j) kv = j == u ? kr[j] : kv;
+        const int p = atomicAdd(&misc[3], 1);
+        scan[p] = (int)kv;
+        scan[NT + p] = base + u;
+    }
     __syncthreads();
     if (tid < m) {
         const uint32_t mk = (uint32_t)scan[tid];
@@ -605,15 +623,15 @@ __device__ void block_topk_small(const float* sc, int n, int k, uint32_t lo, uin
     __syncthreads();
     const uint32_t tk = (uint32_t)misc[4];
     const int ti = misc[5];
-    int cnt = 0;
-    unsigned fl = 0;
+    unsigned fl = gm;  // higher bins, plus the pivot-bin keys ranked at or above (tk, ti)
+    for (uint32_t r = pm_all; r; r &= r - 1u) {
+        const int u = __ffs(r) - 1;
+        uint32_t kv = 0u;
 #pragma unroll
-    for (int u = 0; u < E; ++u) {
-        const bool f = base + u < n &&
-                       (bk[u] > bstar || (bk[u] == bstar && (kr[u] > tk || (kr[u] == tk && base + u <= ti))));
-        fl |= (unsigned)f << u;
-        cnt += f;
+        for (int j = 0; j < E; ++j) kv = j == u ? kr[j] : kv;
+        if (kv > tk || (kv == tk && base + u <= ti)) fl |= 1u << u;
     }
+    const int cnt = __popc(fl);
     int incl = cnt;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
