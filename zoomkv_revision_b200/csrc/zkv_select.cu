@@ -63,18 +63,60 @@ __global__ void __launch_bounds__(256) quest_score_kernel(const uint16_t* __rest
 
 // ----------------------------------------------------------- top-k
 constexpr int kTopkThreads = 256;
+constexpr int kTopkSmall = 16 * kTopkThreads;  // float rows up to this length take the small-n select
+
+// Stages a float row into shared memory and returns its (min finite, max)
+// ordered keys (CTA-wide; ends with a barrier).
+__device__ __forceinline__ void stage_row(const float* __restrict__ src, int len, float* sc, uint32_t* lohi,
+                                          uint32_t& lo, uint32_t& hi) {
+    if (threadIdx.x == 0) {
+        lohi[0] = 0xffffffffu;
+        lohi[1] = 0u;
+    }
+    uint32_t l = 0xffffffffu, h = 0u;
+    for (int i = threadIdx.x; i < len; i += kTopkThreads) {
+        const float v = src[i];
+        sc[i] = v;
+        const uint32_t kk = ordered_u32(v);
+        if (kk > kOrderedNegInf) l = min(l, kk);
+        h = max(h, kk);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        l = min(l, __shfl_xor_sync(0xffffffffu, l, o));
+        h = max(h, __shfl_xor_sync(0xffffffffu, h, o));
+    }
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) {
+        atomicMin(&lohi[0], l);
+        atomicMax(&lohi[1], h);
+    }
+    __syncthreads();
+    lo = lohi[0];
+    hi = lohi[1];
+}
 
 template <typename KeyOf>
 __global__ void __launch_bounds__(kTopkThreads) topk_kernel(KeyOf keyof, int len, int64_t row_stride, int k,
                                                             int64_t* __restrict__ out) {
-    __shared__ int hist[256];
+    __shared__ int hist[512];
     __shared__ int misc[8];
     __shared__ int scan[2 * kTopkThreads];
+    __shared__ __align__(16) float sc[KeyOf::kFloat ? kTopkSmall : 4];
+    __shared__ uint32_t lohi[2];
     const int r = blockIdx.x;
     int64_t* o = out + (int64_t)r * k;
     if (len <= k) {
         for (int i = threadIdx.x; i < k; i += kTopkThreads) o[i] = i < len ? i : -1;
         return;
+    }
+    if constexpr (KeyOf::kFloat) {
+        if (len <= kTopkSmall) {  // same set and order as the general select, fewer barrier phases
+            uint32_t lo, hi;
+            stage_row(keyof.p + (int64_t)r * row_stride, len, sc, lohi, lo, hi);
+            block_topk_small<kTopkThreads>(sc, len, k, lo, hi, hist, misc, scan, [&](int pos, int i) { o[pos] = i; });
+            return;
+        }
     }
     auto key = [&](int i) { return keyof(r, (int64_t)r * row_stride + i); };
     block_topk<kTopkThreads, KeyOf::kFloat>(key, len, k, hist, misc, scan, [&](int pos, int i) { o[pos] = i; });
@@ -227,9 +269,12 @@ __global__ void __launch_bounds__(kTopkThreads) topk_gather_concat_kernel(const 
                                                                           int64_t sk_ld,
                                                                           int64_t* __restrict__ out, int L, int k,
                                                                           int sk, int64_t out_ld) {
-    __shared__ int hist[256];
+    __shared__ int hist[512];
     __shared__ int misc[8];
     __shared__ int scan[2 * kTopkThreads];
+    __shared__ __align__(16) float sc[kTopkSmall];
+    __shared__ int pos_s[kTopkSmall];
+    __shared__ uint32_t lohi[2];
     const int r = blockIdx.x;
     int64_t* o = out + (int64_t)r * out_ld;
     const int64_t* lu = lut + (int64_t)r * L;
@@ -239,6 +284,14 @@ __global__ void __launch_bounds__(kTopkThreads) topk_gather_concat_kernel(const 
         return;
     }
     const float* s = scores + (int64_t)r * L;
+    if (L <= kTopkSmall) {
+        uint32_t lo, hi;
+        stage_row(s, L, sc, lohi, lo, hi);
+        block_topk_small<kTopkThreads>(sc, L, k, lo, hi, hist, misc, scan, [&](int pos, int i) { pos_s[pos] = i; });
+        // the selected positions, then the ids as independent loads
+        for (int p = threadIdx.x; p < k; p += kTopkThreads) o[p] = lu[pos_s[p]];
+        return;
+    }
     auto key = [&](int i) { return ordered_u32(s[i]); };
     block_topk<kTopkThreads, true>(key, L, k, hist, misc, scan, [&](int pos, int i) { o[pos] = lu[i]; });
 }
