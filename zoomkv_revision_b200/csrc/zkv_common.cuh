@@ -687,6 +687,10 @@ __device__ __forceinline__ float quest_half(uint4 qv, uint4 mnv, uint4 mxv) {
 
 static inline int launch_status() { return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH; }
 
+// Internal launchers shared across translation units (not part of the C ABI).
+int quest_score_gqa_into(const void* q, int G, const void* chunk_min, const void* chunk_max, const uint8_t* valid,
+                         float* scores, void* raw_q_out, int rows, int n_chunks, int n_max, cudaStream_t stream);
+
 // Launch `nblocks` CTAs of `nthreads` in clusters of CS (cudaLaunchKernelExC),
 // raising the kernel's dynamic shared-memory limit once per (kernel, device).
 // `pdl`: programmatic dependent launch -- the grid may be scheduled while the

@@ -95,14 +95,22 @@ extern "C" int zkv_reference_select(const void* q, int G, const zkv_ref_layer* L
     float* ksc = reinterpret_cast<float*>(ws + w.kscores);
     int64_t* kix = reinterpret_cast<int64_t*>(ws + w.kidx);
     cudaStream_t st = (cudaStream_t)stream;
-    gqa_mean_kernel<<<(rows + 7) / 8, 256, 0, st>>>((const uint16_t*)q, rows, G, raw_q);
-    int s = launch_status();
-    if (s) return s;
-    // Stage 1: Quest upper bounds over the retrieval chunks, top-nk chunks
-    if ((s = zkv_quest_score(raw_q, L->chunk_min, L->chunk_max, L->valid, scores, rows, n_chunks, n_max, stream)))
-        return s;
+    int s;
+    // Stage 1: the GQA-mean query (recorded for stage 2) and the Quest upper
+    // bounds over the retrieval chunks in one launch; top-nk chunks
+    if (((uintptr_t)q & 15) == 0) {
+        if ((s = quest_score_gqa_into(q, G, L->chunk_min, L->chunk_max, L->valid, scores, raw_q, rows, n_chunks, n_max,
+                                      st)))
+            return s;
+    } else {
+        gqa_mean_kernel<<<(rows + 7) / 8, 256, 0, st>>>((const uint16_t*)q, rows, G, raw_q);
+        if ((s = launch_status())) return s;
+        if ((s = zkv_quest_score(raw_q, L->chunk_min, L->chunk_max, L->valid, scores, rows, n_chunks, n_max, stream)))
+            return s;
+    }
     if ((s = zkv_topk_f32(scores, rows, n_chunks, n_chunks, nk, ids, stream))) return s;
-    // Stage 2 (CDS): centroid density, top-n_dense -> dense mask, KIVI qk per chunk
+    // Stage 2 (CDS): centroid density, top-n_dense -> dense mask, KIVI qk per chunk.  (A one-CTA-per-row
+    // fusion of the first three measured slower: one row's density loads need the whole grid in flight.)
     if ((s = zkv_chunk_density(ids, L->centroid, raw_q, dens, rows, nk, n_chunks, n_max, stream))) return s;
     if ((s = zkv_topk_f32(dens, rows, nk, nk, n_dense, pos, stream))) return s;
     if ((s = zkv_mask_from_topk(pos, mask, rows, n_dense, nk, stream))) return s;

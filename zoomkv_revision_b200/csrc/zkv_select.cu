@@ -11,7 +11,8 @@ __global__ void __launch_bounds__(256) quest_score_kernel(const uint16_t* __rest
                                                           const uint16_t* __restrict__ cmax,
                                                           const uint8_t* __restrict__ valid,
                                                           float* __restrict__ scores, int n_chunks, int n_max,
-                                                          const uint16_t* __restrict__ q = nullptr, int G = 0) {
+                                                          const uint16_t* __restrict__ q = nullptr, int G = 0,
+                                                          uint16_t* __restrict__ raw_q_out = nullptr) {
     const int r = blockIdx.y;
     const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
     const int warp = threadIdx.x >> 5;
@@ -33,6 +34,8 @@ __global__ void __launch_bounds__(256) quest_score_kernel(const uint16_t* __rest
             m[j] = (uint32_t)f2bfbits(__fdiv_rn(acc[2 * j], (float)G)) |
                    ((uint32_t)f2bfbits(__fdiv_rn(acc[2 * j + 1], (float)G)) << 16);
         qv = make_uint4(m[0], m[1], m[2], m[3]);
+        if (raw_q_out && blockIdx.x == 0 && warp == 0 && half == 0)  // one CTA per row records it
+            *reinterpret_cast<uint4*>(raw_q_out + (int64_t)r * kHeadDim + 8 * hl) = qv;
     } else {
         qv = *reinterpret_cast<const uint4*>(raw_q + (int64_t)r * kHeadDim + 8 * hl);
     }
@@ -314,18 +317,26 @@ extern "C" int zkv_quest_score(const void* raw_q, const void* chunk_min, const v
     return launch_status();
 }
 
+int quest_score_gqa_into(const void* q, int G, const void* chunk_min, const void* chunk_max, const uint8_t* valid,
+                         float* scores, void* raw_q_out, int rows, int n_chunks, int n_max, cudaStream_t stream) {
+    if (!q || G < 1 || G > 64 || rows < 0 || n_chunks < 0 || n_chunks > n_max || rows > 65535) return ZKV_ERR_ARG;
+    if (rows == 0 || n_chunks == 0) return ZKV_OK;
+    if (((uintptr_t)q & 15) || ((uintptr_t)chunk_min & 15) || ((uintptr_t)chunk_max & 15) ||
+        ((uintptr_t)raw_q_out & 15))
+        return ZKV_ERR_ALIGN;
+    constexpr int U = 4;
+    dim3 grid((n_chunks + 8 * 2 * U - 1) / (8 * 2 * U), rows);
+    quest_score_kernel<U><<<grid, 256, 0, stream>>>(nullptr, (const uint16_t*)chunk_min, (const uint16_t*)chunk_max,
+                                                    valid, scores, n_chunks, n_max, (const uint16_t*)q, G,
+                                                    (uint16_t*)raw_q_out);
+    return launch_status();
+}
+
 extern "C" int zkv_quest_score_gqa(const void* q, int G, const void* chunk_min, const void* chunk_max,
                                    const uint8_t* valid, float* scores, int rows, int n_chunks, int n_max,
                                    void* stream) {
-    if (!q || G < 1 || G > 64 || rows < 0 || n_chunks < 0 || n_chunks > n_max || rows > 65535) return ZKV_ERR_ARG;
-    if (rows == 0 || n_chunks == 0) return ZKV_OK;
-    if (((uintptr_t)q & 15) || ((uintptr_t)chunk_min & 15) || ((uintptr_t)chunk_max & 15)) return ZKV_ERR_ALIGN;
-    constexpr int U = 4;
-    dim3 grid((n_chunks + 8 * 2 * U - 1) / (8 * 2 * U), rows);
-    quest_score_kernel<U><<<grid, 256, 0, (cudaStream_t)stream>>>(nullptr, (const uint16_t*)chunk_min,
-                                                                  (const uint16_t*)chunk_max, valid, scores, n_chunks,
-                                                                  n_max, (const uint16_t*)q, G);
-    return launch_status();
+    return quest_score_gqa_into(q, G, chunk_min, chunk_max, valid, scores, nullptr, rows, n_chunks, n_max,
+                                (cudaStream_t)stream);
 }
 
 extern "C" int zkv_topk_f32(const float* scores, int rows, int len, int64_t row_stride, int k, int64_t* out,
