@@ -195,6 +195,19 @@ def run_reference(args, n_gpus, rank):
 
 
 # --------------------------------------------------------------------- configs 2 and 3
+def _soak(fn, seconds, stream):
+    """Run fn on stream for about `seconds` (inside the clock sampler, so the
+    sampled clocks are those under this load)."""
+    import time as _t
+    import torch
+    end = _t.perf_counter() + seconds
+    with torch.cuda.stream(stream):
+        while _t.perf_counter() < end:
+            for _ in range(20):
+                fn()
+            torch.cuda.synchronize()
+
+
 def _timed(fn, steps, warmup, stream, dist_world=1):
     import torch
     import torch.distributed as dist
@@ -254,6 +267,7 @@ def run_config2(args):
         call()
     step = graph.replay
     with ClockSampler(0) as clk:
+        _soak(step, args.soak, stream)
         ms = _timed(step, args.steps, args.warmup, stream)
     per_row = N * 16 + C * (16 + 4) + K * HEAD_DIM * 2 + 16 * 256 * 4 + G * HEAD_DIM * 2
     bytes_call = R * per_row
@@ -314,6 +328,7 @@ def run_config1_reference(args):
     with torch.cuda.graph(graph, stream=stream):
         layer_loop()
     with ClockSampler(0) as clk:
+        _soak(graph.replay, args.soak, stream)
         ms = _timed(graph.replay, args.steps, args.warmup, stream)
     if int(status.item()) != 0:
         raise RuntimeError(f"device status {int(status.item())} (bounded wait expired)")
@@ -393,6 +408,8 @@ def run_config3(args):
         step()
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as clk:
+        if world == 1:  # ranks would run different iteration counts of the collectives
+            _soak(step, args.soak, stream)
         ms = _timed(step, args.steps, args.warmup, stream, world)
     bytes_step = layers * W.page_algorithmic_bytes(bs * H, n_c, nk, n_near, G)
     if world == 1:
