@@ -347,7 +347,7 @@ def run_config1_reference(args):
                    "l2": "8 distinct layer buffers of ~1.5 GB >> L2"},
         "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
                      "peak_kind": kind, "bytes_per_step": bytes_step},
-        "gpu_launches": layers * args.steps * 8,  # 7 in the select chain + attn_rows
+        "gpu_launches": layers * args.steps * 7,  # 6 in the select chain + attn_rows
         "clocks": clk.summary()}), flush=True)
 
 

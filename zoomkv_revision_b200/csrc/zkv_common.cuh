@@ -690,6 +690,7 @@ static inline int launch_status() { return cudaGetLastError() == cudaSuccess ? Z
 // Internal launchers shared across translation units (not part of the C ABI).
 int quest_score_gqa_into(const void* q, int G, const void* chunk_min, const void* chunk_max, const uint8_t* valid,
                          float* scores, void* raw_q_out, int rows, int n_chunks, int n_max, cudaStream_t stream);
+int topk_mask_launch(const float* dens, int rows, int nk, int n_dense, uint8_t* mask, cudaStream_t stream);
 
 // Launch `nblocks` CTAs of `nthreads` in clusters of CS (cudaLaunchKernelExC),
 // raising the kernel's dynamic shared-memory limit once per (kernel, device).

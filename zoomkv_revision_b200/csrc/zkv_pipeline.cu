@@ -112,8 +112,12 @@ extern "C" int zkv_reference_select(const void* q, int G, const zkv_ref_layer* L
     // Stage 2 (CDS): centroid density, top-n_dense -> dense mask, KIVI qk per chunk.  (A one-CTA-per-row
     // fusion of the first three measured slower: one row's density loads need the whole grid in flight.)
     if ((s = zkv_chunk_density(ids, L->centroid, raw_q, dens, rows, nk, n_chunks, n_max, stream))) return s;
-    if ((s = zkv_topk_f32(dens, rows, nk, nk, n_dense, pos, stream))) return s;
-    if ((s = zkv_mask_from_topk(pos, mask, rows, n_dense, nk, stream))) return s;
+    if (nk <= 4096) {  // top-n_dense written straight as the mask
+        if ((s = topk_mask_launch(dens, rows, nk, n_dense, mask, st))) return s;
+    } else {
+        if ((s = zkv_topk_f32(dens, rows, nk, nk, n_dense, pos, stream))) return s;
+        if ((s = zkv_mask_from_topk(pos, mask, rows, n_dense, nk, stream))) return s;
+    }
     if ((s = zkv_kivi_qk(ids, mask, L->packed, n_valid_chunks, n_max, L->chunk_min, L->chunk_max, n_max, raw_q, rows,
                          nk, dense_topk, sparse_topk, ksc, kix, (int64_t)nk * kChunk, stream)))
         return s;

@@ -125,6 +125,25 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(KeyOf keyof, int len
     block_topk<kTopkThreads, KeyOf::kFloat>(key, len, k, hist, misc, scan, [&](int pos, int i) { o[pos] = i; });
 }
 
+// The top n_dense positions of one row of density scores written straight as
+// the dense mask (mask[r][p] = 1 for the selected p, 0 elsewhere): top-k +
+// mask_from_topk in one launch, same selection as topk_kernel.
+__global__ void __launch_bounds__(kTopkThreads) topk_mask_kernel(const float* __restrict__ dens, int nk, int n_dense,
+                                                                 uint8_t* __restrict__ mask) {
+    __shared__ int hist[512];
+    __shared__ int misc[8];
+    __shared__ int scan[2 * kTopkThreads];
+    __shared__ __align__(16) float sc[kTopkSmall];
+    __shared__ uint32_t lohi[2];
+    const int r = blockIdx.x;
+    uint8_t* m = mask + (int64_t)r * nk;
+    for (int i = threadIdx.x; i < nk; i += kTopkThreads) m[i] = n_dense >= nk ? 1 : 0;
+    if (n_dense >= nk) return;
+    uint32_t lo, hi;
+    stage_row(dens + (int64_t)r * nk, nk, sc, lohi, lo, hi);  // its barriers order the zeroing first
+    block_topk_small<kTopkThreads>(sc, nk, n_dense, lo, hi, hist, misc, scan, [&](int, int i) { m[i] = 1; });
+}
+
 struct F32Key {
     static constexpr bool kFloat = true;
     const float* p;
@@ -362,6 +381,13 @@ extern "C" int zkv_chunk_density(const int64_t* chunk_ids, const void* centroid,
     const int64_t jobs = (int64_t)rows * nk;
     density_kernel<<<(unsigned)((jobs + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
         chunk_ids, (const uint16_t*)centroid, (const uint16_t*)raw_q, out, rows, nk, n_chunks, n_max);
+    return launch_status();
+}
+
+int topk_mask_launch(const float* dens, int rows, int nk, int n_dense, uint8_t* mask, cudaStream_t stream) {
+    if (rows < 0 || nk < 1 || n_dense < 1 || nk > kTopkSmall) return ZKV_ERR_ARG;
+    if (rows == 0) return ZKV_OK;
+    topk_mask_kernel<<<rows, kTopkThreads, 0, stream>>>(dens, nk, n_dense, mask);
     return launch_status();
 }
 
