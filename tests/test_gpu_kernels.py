@@ -306,3 +306,28 @@ def test_quest_score_gqa_equals_mean_then_score():
     ops.quest_chunk_score_gqa(q, pc.chunk_min, pc.chunk_max, got, n_c, chunk_valid=pc.valid)
     torch.cuda.synchronize()
     assert torch.equal(got.view(torch.int32), ref.view(torch.int32))
+
+
+@pytest.mark.parametrize("G,cluster", [(2, 8), (8, 8), (4, 4)])
+def test_page_decode_split_group_and_cluster_variants(G, cluster):
+    """The long-context split form at other GQA group sizes and cluster
+    sizes: same selection as the fused form, output within the attention
+    tolerance of the oracle."""
+    bs, H, n_c, nk = 1, 2, 2600, 64
+    pc, _ = W.build_page_cache(31 + G, bs, H, 16 * n_c, 16, DEV)
+    q = W.synth_query(torch.Generator(device=DEV).manual_seed(9 + G), bs, H * G, DEV)
+    R = bs * H
+    sel = torch.empty(R, nk, dtype=torch.int64, device=DEV)
+    sel2 = torch.empty_like(sel)
+    ops.page_decode(q, pc.layer(), pc.n_c, nk, 16, sel_out=sel, cluster=cluster, split=False)
+    out2 = ops.page_decode(q, pc.layer(), pc.n_c, nk, 16, sel_out=sel2, cluster=cluster, split=True)
+    torch.cuda.synchronize()
+    assert torch.equal(sel2, sel)
+    ro, _, rsel = O.page_decode(
+        to_u16(q).reshape(R, G, 128), to_u16(pc.chunk_min).reshape(R, -1, 128), to_u16(pc.chunk_max).reshape(R, -1, 128),
+        pc.valid.cpu().numpy().astype(np.uint8).reshape(R, -1), pc.kcodes.cpu().numpy().reshape(R, -1, 16, 16),
+        pc.vcodes_t.cpu().numpy().reshape(R, -1, 128, 2), to_u16(pc.vmeta).reshape(R, -1, 2, 4, 16),
+        to_u16(pc.near_k).reshape(R, -1, 128), to_u16(pc.near_v).reshape(R, -1, 128),
+        pc.n_c, nk, 16, 1 / np.sqrt(128), threads=4)
+    assert np.array_equal(sel.cpu().numpy(), rsel)
+    close(O.bf16_to_f32(to_u16(out2)).reshape(R, G, 128), O.bf16_to_f32(ro))
