@@ -24,6 +24,9 @@ Two further workloads print their own line (not the headline):
   --config 3   Qwen3-4B shape, batch 1, 131072 context, budget 4096: the fused
                page decode on 1 GPU; under torchrun the sequence split across
                ranks with NCCL score / partial all-gathers (strong scaling)
+  --config 5   the offload tier: config-1 layer shape with the retrieval zone
+               in host-pinned memory, selected rows gathered over the host
+               link, then attention
 """
 from __future__ import annotations
 
@@ -285,6 +288,66 @@ def run_config2(args):
         "gpu_launches": 3 * args.steps, "clocks": clk.summary()}), flush=True)
 
 
+def run_offload(args):
+    """Offload tier at the config-1 layer shape: 64 (batch, head) rows whose
+    32,640-token retrieval zone lives in host-pinned memory; one step = one
+    layer's zkv_h2d_gather_kv of the 2048 selected rows per (batch, head)
+    (K and V, 67 MB over the host link) followed by the GQA attention over
+    sink + gathered + near rows in HBM.  The roofline denominator is the
+    host->device copy bandwidth of pinned memory measured in the same run."""
+    import torch
+    from zoomkv_revision_b200 import ops
+    dev = torch.device("cuda", 0)
+    bs, H, N, F, s, near = BATCH, KV_HEADS, N_RETRIEVAL, BUDGET, 4, RESIDUAL
+    R = bs * H
+    g = torch.Generator().manual_seed(5)
+    host_k = torch.randn(bs, H, N, HEAD_DIM, generator=g).to(torch.bfloat16).pin_memory()
+    host_v = torch.randn(bs, H, N, HEAD_DIM, generator=g).to(torch.bfloat16).pin_memory()
+    sel = torch.sort(torch.rand(R, N, generator=g).argsort(dim=1)[:, :F], dim=1).values.reshape(bs, H, F).to(dev)
+    W = s + F + near
+    win_k = torch.randn(bs, H, W, HEAD_DIM, device=dev).to(torch.bfloat16)
+    win_v = torch.randn(bs, H, W, HEAD_DIM, device=dev).to(torch.bfloat16)
+    q = torch.randn(bs, 1, H * G, HEAD_DIM, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def gather():
+        ops.h2d_gather_rows(host_k, host_v, sel, win_k, win_v, dst_offset=s, status=status)
+
+    def layer():
+        gather()
+        ops.attn_rows(q, win_k, win_v, seg0=(0, s + F), seg1=(s + F, W), out=out, status=status)
+
+    # host-link peak of this box: pinned host -> device copy of 512 MiB
+    src = torch.empty(512 << 20, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    ms_copy = _timed(lambda: dst.copy_(src, non_blocking=True), 5, 3, stream)
+    peak = src.numel() / (ms_copy / 1e3) / 1e9
+    del src, dst
+    with ClockSampler(0) as clk:
+        _soak(layer, args.soak, stream)
+        ms_g = _timed(gather, args.steps, args.warmup, stream)
+        ms_l = _timed(layer, args.steps, args.warmup, stream)
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device status {int(status.item())}")
+    moved = R * F * HEAD_DIM * 2 * 2
+    ach = moved / (ms_g / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "offload tier: decode tokens/s at the config-1 layer shape with the retrieval zone in host memory",
+        "value": bs / (LAYERS * ms_l / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_l, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "offload: config-1 layer, 2048 selected rows per (batch, head) from host-pinned memory",
+                   "rows": R, "host_tokens_per_row": N, "selected": F, "near": near, "sink": s,
+                   "step": "one layer (gather + attention); tokens/s = batch / (36 x layer time)",
+                   "l2": "host reads use ld.global.cv (re-fetched every step)"},
+        "gather_ms": ms_g, "layer_ms": ms_l,
+        "roofline": {"bound": "host link", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                     "peak_kind": "pinned host->device copy of 512 MiB measured in this run",
+                     "bytes_per_launch": moved},
+        "gpu_launches": 2 * args.steps, "clocks": clk.summary()}), flush=True)
+
+
 def run_config1_reference(args):
     """Config-1 shape in the drop-in's default (reference) mode with the
     production knobs: one layer = zkv_reference_select (Quest -> top-nk ->
@@ -447,7 +510,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--soak", type=float, default=1.5, help="seconds of load before timing (clock sampling)")
-    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3])
+    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 5],
+                    help="5: the offload tier (retrieval zone in host-pinned memory)")
     ap.add_argument("--mode", default="page", choices=["page", "reference"],
                     help="config 1 only: page mode (the headline) or the drop-in's default reference mode")
     args = ap.parse_args()
@@ -460,6 +524,9 @@ def main():
         return
     if args.config == 3 and args.impl == "ours":
         run_config3(args)
+        return
+    if args.config == 5 and args.impl == "ours":
+        run_offload(args)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -34,6 +34,7 @@ extern "C" {
 #define ZKV_ERR_LAUNCH 4      /* CUDA launch / attribute error                 */
 #define ZKV_ERR_UNSUPPORTED 5 /* unsupported configuration                     */
 #define ZKV_ERR_TIMEOUT 6     /* device-side bounded wait expired (status word) */
+#define ZKV_ERR_RANGE 7       /* device-side index outside its range (status word) */
 
 const char* zkv_status_string(int status);
 /* Library version (major*10000 + minor*100 + patch). */
@@ -402,6 +403,43 @@ int zkv_rq_popcount_topk(const int64_t* cand, int C, const zkv_rq_layout* lay,
                          int rows, int K, int64_t* sel_out, float* est_out,
                          const void* keys, int64_t keys_ld_row,
                          const void* q_mean, float* ip_out, void* stream);
+
+/* ------------------------------------------------------------ offload tier */
+
+/* Gather of selected K/V rows from host-pinned memory into device memory,
+ * read by the SMs over the host link (zero-copy through the unified address
+ * space).  Replaces h2d_gather_kv (cache_hub/gather_trans/trans_h2d.py:65-105,
+ * trans_h2d.cu:83-205).  Per row r (= b * kv_heads + h) and j < n_sel:
+ *   dst[r][dst_off + j][:] = src[r][idx[r*idx_ld + j] + src_off][:]
+ *   src_k, src_v  host-pinned [rows][src_len][128] bf16 (cudaHostAlloc or
+ *                 cudaHostRegister memory; anything else -> ZKV_ERR_ARG)
+ *   idx           device [rows][idx_ld] int64 (idx_ld 0: one list for all rows)
+ *   dst_k, dst_v  device [rows][dst_len][128] bf16, dst_off + n_sel <= dst_len
+ * The reference's call is dst_off = 0, src_off = 0, n_sel = idx_ld = topk.
+ * An index outside [0, src_len) is not dereferenced: its row is skipped and
+ * ZKV_ERR_RANGE is written to `status` (may be NULL).                      */
+int zkv_h2d_gather_kv(const void* src_k, const void* src_v, int rows,
+                      int64_t src_len, const int64_t* idx, int64_t idx_ld,
+                      int n_sel, int64_t src_off, void* dst_k, void* dst_v,
+                      int64_t dst_len, int64_t dst_off, int32_t* status,
+                      void* stream);
+
+/* Variable-K form writing into a flash-attention varlen packed buffer.
+ * Replaces h2d_gather_kv_packed (trans_h2d.py:108-161,
+ * trans_h2d.cu:228-283).  For vh < rows and slot < global_k with
+ * slot < cu_topk[vh+1] - cu_topk[vh]:
+ *   dst[cu_k[vh] + sl_end + slot][:] = src[vh][idx[cu_topk[vh] + slot]][:]
+ *   idx      device [total_topk] int64;  cu_topk, cu_k  device [rows+1] int32
+ *   dst_k, dst_v  device [n_dst][128] bf16
+ * Rows [cu_k[vh], cu_k[vh] + sl_end) of every segment are not written.  A
+ * source index or destination row out of range is skipped and reported as
+ * ZKV_ERR_RANGE in `status`.  global_k <= 0 copies nothing.               */
+int zkv_h2d_gather_kv_packed(const void* src_k, const void* src_v, int rows,
+                             int64_t src_len, const int64_t* idx,
+                             const int32_t* cu_topk, const int32_t* cu_k,
+                             int sl_end, int global_k, void* dst_k,
+                             void* dst_v, int64_t n_dst, int32_t* status,
+                             void* stream);
 
 #ifdef __cplusplus
 }

@@ -24,7 +24,7 @@ __all__ = [
     "topk_gather_concat", "attn_dense", "page_decode", "lse_merge", "kivi_dequant_chunk",
     "vdequant_tokens", "page_layout_values", "kivi_scale", "rq_mag_tables", "rq_encode", "rq_query", "collision_weights",
     "collision_count", "update_cache_cnt_sorted", "rerank4", "coarse2bit", "rq_query_4bit", "popcount_est",
-    "exact_ip",
+    "exact_ip", "h2d_gather", "h2d_gather_packed",
 ]
 
 
@@ -440,4 +440,34 @@ def exact_ip(idx, keys, q) -> np.ndarray:
     L.orc_exact_ip.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
                                ctypes.c_int, ctypes.c_void_p]
     L.orc_exact_ip(_p(idx), n, _p(keys), keys.shape[1] * 128, _p(np.ascontiguousarray(q, np.uint16)), R, _p(out))
+    return out
+
+
+def h2d_gather(src: np.ndarray, idx: np.ndarray, dst: np.ndarray) -> np.ndarray:
+    """Dense offload gather, cache_hub/gather_trans/trans_h2d.cu:83-140:
+    dst[b, h, j] = src[b, h, idx[b, h, j]] for j < topk; rows j >= topk of
+    dst keep their contents.  src [bs,H,L,128], idx [bs,H,topk], dst
+    [bs,H,>=topk,128] (any element type; a row copy)."""
+    out = dst.copy()
+    bs, H, topk = idx.shape
+    for b in range(bs):
+        for h in range(H):
+            out[b, h, :topk] = src[b, h, idx[b, h]]
+    return out
+
+
+def h2d_gather_packed(src: np.ndarray, idx: np.ndarray, cu_topk: np.ndarray, cu_k: np.ndarray, sl_end: int,
+                      global_k: int, dst: np.ndarray) -> np.ndarray:
+    """Varlen offload gather, trans_h2d.cu:228-283: for vh = b*H + h and
+    slot < min(global_k, cu_topk[vh+1] - cu_topk[vh]):
+    dst[cu_k[vh] + sl_end + slot] = src[b, h, idx[cu_topk[vh] + slot]]."""
+    out = dst.copy()
+    bs, H = src.shape[:2]
+    for vh in range(bs * H):
+        st, n = int(cu_topk[vh]), int(cu_topk[vh + 1] - cu_topk[vh])
+        n = min(n, int(global_k))
+        if n <= 0:
+            continue
+        d0 = int(cu_k[vh]) + sl_end
+        out[d0:d0 + n] = src[vh // H, vh % H, idx[st:st + n]]
     return out

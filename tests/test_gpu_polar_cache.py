@@ -18,6 +18,10 @@ DEV = "cuda"
 
 
 def set_env(monkeypatch, mode):
+    """mode: 'reference', 'page', or 'host' (reference attention with the
+    retrieval zone in host-pinned memory)."""
+    monkeypatch.setenv("ZKV_HOST_RETRIEVAL", "1" if mode == "host" else "0")
+    mode = "reference" if mode == "host" else mode
     env = {"POLAR_QUEST_CHUNK": "16", "POLAR_QUEST_CAND_RATIO": "0.4", "POLAR_QUEST_DYNAMIC_CAND_RATIO": "1",
            "POLAR_QUEST_DYNAMIC_CAND_THRESHOLDS": "5000,10001", "POLAR_QUEST_DYNAMIC_CAND_RATIOS": "0.7,0.5,0.4",
            "POLAR_CDS_DENSE_RATIO": "0.3", "POLAR_CDS_DENSE_TOPK": "16", "POLAR_CDS_SPARSE_TOPK": "8",
@@ -78,7 +82,7 @@ def close(out, ref):
     assert err.max() <= 2e-2 and err.mean() / np.abs(ref).mean() <= 1e-2, (err.max(), err.mean())
 
 
-@pytest.mark.parametrize("mode", ["reference", "page"])
+@pytest.mark.parametrize("mode", ["reference", "page", "host"])
 def test_polar_cache_replays_reference_and_matches_oracle(monkeypatch, mode):
     set_env(monkeypatch, mode)
     g = np.load(os.path.join(GOLDEN, "schedule.npz"))
@@ -105,7 +109,7 @@ def test_polar_cache_replays_reference_and_matches_oracle(monkeypatch, mode):
                 total = cache.current_seq_len[l]
                 kl = to_u16(keys[l][:, :, :total])
                 vl = to_u16(vals[:, :, :total])
-                if mode == "reference":
+                if mode in ("reference", "host"):
                     ref, _ = oracle_reference_compute(cache, l, q, kl, vl, cache.final_topk)
                     close(O.bf16_to_f32(to_u16(out)).reshape(ref.shape), ref)
                 else:
@@ -147,6 +151,75 @@ def test_polar_cache_full_attention_branch(monkeypatch):
     vals = from_u16(g["values"])
     cache.prefill_update_kv_cache(None, keys[:, :, :107].transpose(1, 2).contiguous(),
                                   vals[:, :, :107].transpose(1, 2).contiguous(), 0, 0)
+    q = torch.randn(bs, 1, 4 * H, 128, device=DEV).to(torch.bfloat16)
+    out = cache.compute(q, 0)
+    qf = O.bf16_to_f32(to_u16(q)).reshape(bs, 4 * H, 128)
+    Kf = O.bf16_to_f32(to_u16(keys[:, :, :107]))
+    Vf = O.bf16_to_f32(to_u16(vals[:, :, :107]))
+    for b in range(bs):
+        for h in range(H):
+            ro, _ = O.attn_dense(qf[b, h * 4:(h + 1) * 4], Kf[b, h], Vf[b, h], 1 / np.sqrt(128))
+            close(O.bf16_to_f32(to_u16(out[b, 0, h * 4:(h + 1) * 4])), ro)
+
+
+def test_host_retrieval_tier_equals_hbm_cache(monkeypatch):
+    """The offload tier (retrieval rows in host-pinned memory, gathered over
+    the host link) selects the same rows and returns the same output as the
+    HBM-resident cache, step for step across flushes; the host zone holds
+    exactly the retrieval rows."""
+    g = np.load(os.path.join(GOLDEN, "schedule.npz"))
+    L, bs, H, sink, local, interval, prefill, steps, max_new = (int(x) for x in g["params"])
+    caches = {}
+    for mode in ("reference", "host"):
+        set_env(monkeypatch, mode)
+        caches[mode] = make_cache(g)
+    hb, ho = caches["reference"], caches["host"]
+    assert ho.host_tier and not hb.host_tier and ho.keys[0].is_pinned()
+    keys = [from_u16(g["keys0"]), from_u16(g["keys1"])]
+    vals = from_u16(g["values"])
+    for c in (hb, ho):
+        for l in range(L):
+            c.prefill_update_kv_cache(None, keys[l][:, :, :prefill].transpose(1, 2).contiguous(),
+                                      vals[:, :, :prefill].transpose(1, 2).contiguous(), l, 0)
+    gen = torch.Generator(device=DEV).manual_seed(8)
+    for t in range(steps):
+        pos = prefill + t
+        for l in range(L):
+            for c in (hb, ho):
+                c.decode_update_kv_cache(keys[l][:, :, pos:pos + 1].transpose(1, 2).contiguous(),
+                                         vals[:, :, pos:pos + 1].transpose(1, 2).contiguous(), l)
+            if t % 7 == 0:
+                q = torch.randn(bs, 1, 4 * H, 128, generator=gen, device=DEV).to(torch.bfloat16)
+                a, b = hb.compute(q, l), ho.compute(q, l)
+                torch.cuda.synchronize()
+                n_chunks, nk, _, skipped = ho.sched.plan
+                min_total = max(ho.FULL_ATTENTION_THRESHOLD, sink + local + 2 * ho.final_topk)
+                if ho.current_seq_len[l] >= min_total and n_chunks > 0:  # the retrieval branch ran
+                    n = min(ho.final_topk, nk * 16) + skipped
+                    assert torch.equal(hb._scratch[hb.device]["final"][:, :, :n],
+                                       ho._scratch[ho.device]["final"][:, :, :n])
+                assert torch.equal(a, b), (t, l)
+    assert int(ho._scratch[ho.device]["status"].item()) == 0
+    r = ho.sched.actual_retrieval
+    for l in range(L):
+        assert torch.equal(ho.keys[l][:, :, sink:sink + r], keys[l][:, :, sink:sink + r].cpu())
+        assert torch.equal(ho.values[l][:, :, sink:sink + r], vals[:, :, sink:sink + r].cpu())
+        for name in ("chunk_min", "chunk_max", "chunk_centroid", "kivi_packed"):
+            assert torch.equal(getattr(hb, name)[l], getattr(ho, name)[l])
+
+
+def test_host_retrieval_full_attention_branch(monkeypatch):
+    """Below the retrieval threshold the offload tier gathers every host row
+    and attends all stored tokens."""
+    set_env(monkeypatch, "host")
+    g = np.load(os.path.join(GOLDEN, "schedule.npz"))
+    cache = make_cache(g, final_topk=100)
+    bs, H = 2, 2
+    keys = from_u16(g["keys0"])
+    vals = from_u16(g["values"])
+    cache.prefill_update_kv_cache(None, keys[:, :, :107].transpose(1, 2).contiguous(),
+                                  vals[:, :, :107].transpose(1, 2).contiguous(), 0, 0)
+    assert cache.win_base[0] > cache.sink_size  # some rows live only on the host
     q = torch.randn(bs, 1, 4 * H, 128, device=DEV).to(torch.bfloat16)
     out = cache.compute(q, 0)
     qf = O.bf16_to_f32(to_u16(q)).reshape(bs, 4 * H, 128)

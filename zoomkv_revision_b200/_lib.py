@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(_HERE, "libzkv.so")
 
 ZKV_OK = 0
 ZKV_ERR_TIMEOUT = 6
+ZKV_ERR_RANGE = 7
 
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int
@@ -63,6 +64,10 @@ _SIGNATURES = {
     "zkv_kivi_qk": [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _c_void_p, _i32, _c_void_p, _i32, _i32, _i32,
                     _i32, _c_void_p, _c_void_p, _i64, _c_void_p],
     "zkv_topk_gather_concat": [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p, _i32, _i32, _i32, _i32, _i64, _c_void_p],
+    "zkv_h2d_gather_kv": [_c_void_p, _c_void_p, _i32, _i64, _c_void_p, _i64, _i32, _i64, _c_void_p, _c_void_p, _i64,
+                          _i64, _c_void_p, _c_void_p],
+    "zkv_h2d_gather_kv_packed": [_c_void_p, _c_void_p, _i32, _i64, _c_void_p, _c_void_p, _c_void_p, _i32, _i32,
+                                 _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p],
     "zkv_attn_rows": [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i32, _c_void_p, _i32, _i64, _i64,
                       _i32, _i32, _f32, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p],
     "zkv_page_decode": [_c_void_p, ctypes.POINTER(ZkvPageLayer), _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32,

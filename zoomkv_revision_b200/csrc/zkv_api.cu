@@ -10,6 +10,7 @@ extern "C" const char* zkv_status_string(int status) {
         case ZKV_ERR_LAUNCH: return "CUDA launch or attribute error";
         case ZKV_ERR_UNSUPPORTED: return "unsupported configuration";
         case ZKV_ERR_TIMEOUT: return "device-side bounded wait expired";
+        case ZKV_ERR_RANGE: return "device-side index outside its range";
         default: return "unknown status";
     }
 }

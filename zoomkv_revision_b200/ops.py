@@ -17,6 +17,7 @@ lse_merge_cuda                         cache_hub/lse_merge/lse_merge.py:122-144
 kivi_encode_chunks                     polar_cache._compute_and_store_chunk_minmax +
                                        _kivi_pack_chunks (aligned chunks)
 attn_rows                              h2d_gather_kv + torch.cat + flash_attn_with_kvcache
+h2d_gather_kv / h2d_gather_kv_packed   cache_hub/gather_trans/trans_h2d.py:65-161 (offload tier)
 page_decode                            (fused page-mode decode; no single counterpart)
 reference_select                       polar_cache.compute retrieval chain (REF:1589-1775) as one call
 vquant_encode                          (per-token 4-bit values; no counterpart)
@@ -47,6 +48,7 @@ __all__ = [
     "quest_chunk_score", "float_topk", "float_topk_3d", "radix_topk_3d", "partial_chunk_density_scores_cuda",
     "dense_mask_from_topk_cuda", "partial_chunk_kivi_qk_dense_sparse_cuda", "float_topk_gather_concat_3d",
     "lse_merge_cuda", "lse_merge_n", "kivi_encode_chunks", "vquant_encode", "attn_rows", "page_decode",
+    "h2d_gather_kv", "h2d_gather_kv_packed", "h2d_gather_rows",
     "PageLayer", "page_attend", "gqa_mean", "reference_select", "reference_select_ws_bytes", "RqLayout", "rq_encode", "batch_encode", "rq_query", "get_cache_cnt_fused", "collision_topk",
     "partial_rerank_cuda", "coarse_2bit_score_cuda", "rq_popcount_topk", "MAG_CENTERS", "MAG_THRESHOLDS",
 ]
@@ -414,6 +416,102 @@ def attn_rows(q, keys, values, *, seg0=(0, 0), sel=None, sel_offset=0, seg1=(0, 
                               sp, n_sel, sel_ld, int(sel_offset), int(seg1[0]), int(seg1[1]), scale, _p(out),
                               _p(lse), int(split), _p(status), _stream(q)), "zkv_attn_rows")
     return out
+
+
+# ----------------------------------------------------------------- offload tier (host-pinned rows)
+def _require(cond, msg):
+    if not cond:
+        raise AssertionError(msg)
+
+
+def _pinned_src(src_k, src_v):
+    _require(src_k.shape == src_v.shape, "src_k_caches and src_v_caches must have the same shape")
+    _require(src_k.dim() == 4 and src_k.shape[-1] == 128, "src caches must be [bs, heads, kv_len, 128]")
+    _require(not src_k.is_cuda and not src_v.is_cuda, "src caches must be CPU tensors")
+    _require(src_k.is_pinned() and src_v.is_pinned(), "src caches must be host-pinned (pin_memory=True)")
+    _require(src_k.dtype == torch.bfloat16 and src_v.dtype == torch.bfloat16, "src caches must be bfloat16")
+    _require(src_k.is_contiguous() and src_v.is_contiguous(), "src caches must be contiguous")
+
+
+def h2d_gather_kv(src_k_caches, src_v_caches, selected_indices, dst_k_caches, dst_v_caches, status=None):
+    """dst[b,h,j] = src[b,h,selected_indices[b,h,j]] for j < topk, K and V.
+
+    Reference: cache_hub/gather_trans/trans_h2d.py:65-105 (same checks, as
+    AssertionError).  src_* host-pinned [bs,heads,kv_len,128] bf16;
+    selected_indices CUDA [bs,heads,topk] int64; dst_* CUDA
+    [bs,heads,max_topk >= topk,128] bf16; rows j >= topk are not written.
+    An index outside [0, kv_len) is skipped and reported through `status`
+    (int32 CUDA word, ZKV_ERR_RANGE) when one is given."""
+    _pinned_src(src_k_caches, src_v_caches)
+    bs, heads, kv_len, dim = src_k_caches.shape
+    _require(selected_indices.dim() == 3 and tuple(selected_indices.shape[:2]) == (bs, heads),
+             "selected_indices must be [bs, heads, topk]")
+    topk = selected_indices.shape[2]
+    _require(dst_k_caches.shape == dst_v_caches.shape, "dst_k_caches and dst_v_caches must have the same shape")
+    _require(dst_k_caches.dim() == 4 and tuple(dst_k_caches.shape[:2]) == (bs, heads) and dst_k_caches.shape[3] == dim,
+             "dst caches must be [bs, heads, max_topk, 128]")
+    _require(dst_k_caches.shape[-2] >= topk, "dst caches hold fewer rows than topk")
+    _require(dst_k_caches.is_cuda and dst_v_caches.is_cuda and selected_indices.is_cuda,
+             "dst caches and selected_indices must be CUDA tensors")
+    _require(dst_k_caches.dtype == torch.bfloat16 and dst_v_caches.dtype == torch.bfloat16,
+             "dst caches must be bfloat16")
+    _require(selected_indices.dtype == torch.int64, "selected_indices must be int64")
+    _require(dst_k_caches.is_contiguous() and dst_v_caches.is_contiguous() and selected_indices.is_contiguous(),
+             "dst caches and selected_indices must be contiguous")
+    check(lib().zkv_h2d_gather_kv(_p(src_k_caches), _p(src_v_caches), bs * heads, kv_len, _p(selected_indices), topk,
+                                  topk, 0, _p(dst_k_caches), _p(dst_v_caches), dst_k_caches.shape[2], 0, _p(status),
+                                  _stream(dst_k_caches)), "zkv_h2d_gather_kv")
+
+
+def h2d_gather_kv_packed(src_k_caches, src_v_caches, dst_k_packed, dst_v_packed, indices_packed, cu_seqlens_topk,
+                         cu_seqlens_k, sl_end: int, global_k: int, status=None):
+    """Variable-K gather into a flash-attention varlen packed buffer.
+
+    Reference: cache_hub/gather_trans/trans_h2d.py:108-161.  For every
+    vh = b*heads + h, rows [cu_seqlens_k[vh] + sl_end, cu_seqlens_k[vh+1]) of
+    dst_*_packed [total_k,128] receive src[b,h,indices_packed[cu_seqlens_topk
+    [vh] + slot]] for slot < min(global_k, segment length); the first sl_end
+    rows of every segment are left as they are."""
+    _pinned_src(src_k_caches, src_v_caches)
+    bs, heads, kv_len, dim = src_k_caches.shape
+    V = bs * heads
+    _require(dst_k_packed.is_cuda and dst_v_packed.is_cuda, "dst_*_packed must be CUDA tensors")
+    _require(indices_packed.is_cuda and cu_seqlens_topk.is_cuda and cu_seqlens_k.is_cuda,
+             "indices and cu_seqlens must be CUDA tensors")
+    _require(dst_k_packed.dtype == torch.bfloat16 and dst_v_packed.dtype == torch.bfloat16,
+             "dst_*_packed must be bfloat16")
+    _require(indices_packed.dtype == torch.int64, "indices_packed must be int64")
+    _require(cu_seqlens_topk.dtype == torch.int32 and cu_seqlens_k.dtype == torch.int32, "cu_seqlens must be int32")
+    _require(dst_k_packed.is_contiguous() and dst_v_packed.is_contiguous(), "dst_*_packed must be contiguous")
+    _require(dst_k_packed.dim() == 2 and dst_k_packed.shape[1] == dim, "dst_*_packed must be [total_k, 128]")
+    _require(dst_v_packed.shape == dst_k_packed.shape, "dst_k_packed and dst_v_packed must have the same shape")
+    _require(cu_seqlens_topk.shape[0] == V + 1 and cu_seqlens_k.shape[0] == V + 1, "cu_seqlens must be [V + 1]")
+    _require(indices_packed.dim() == 1, "indices_packed must be 1-D")
+    _require(indices_packed.is_contiguous() and cu_seqlens_topk.is_contiguous() and cu_seqlens_k.is_contiguous(),
+             "indices and cu_seqlens must be contiguous")
+    check(lib().zkv_h2d_gather_kv_packed(_p(src_k_caches), _p(src_v_caches), V, kv_len, _p(indices_packed),
+                                         _p(cu_seqlens_topk), _p(cu_seqlens_k), int(sl_end), int(global_k),
+                                         _p(dst_k_packed), _p(dst_v_packed), dst_k_packed.shape[0], _p(status),
+                                         _stream(dst_k_packed)), "zkv_h2d_gather_kv_packed")
+
+
+def h2d_gather_rows(src_k, src_v, sel, dst_k, dst_v, *, n_sel=None, src_offset=0, dst_offset=0, status=None):
+    """Offload-tier gather with offsets: dst[b,h,dst_offset+j] =
+    src[b,h,sel[b,h,j]+src_offset] for j < n_sel.  src_* host-pinned
+    [bs,H,cap,128]; dst_* CUDA [bs,H,dst_len,128] (row-contiguous, any
+    leading strides equal); sel CUDA [bs,H,>=n_sel] int64 with unit last
+    stride."""
+    bs, H, cap, _ = src_k.shape
+    n = sel.shape[2] if n_sel is None else int(n_sel)
+    if dst_k.stride(3) != 1 or dst_k.stride(2) != 128 or dst_k.stride(0) != H * dst_k.stride(1):
+        raise ValueError("dst_k must be [bs,H,len,128] with contiguous rows")
+    if dst_v.stride() != dst_k.stride():
+        raise ValueError("dst_k and dst_v must share a layout")
+    if sel.stride(2) != 1 or sel.stride(0) != H * sel.stride(1):
+        raise ValueError("sel must be [bs,H,n] with unit last stride")
+    check(lib().zkv_h2d_gather_kv(_p(src_k), _p(src_v), bs * H, cap, _p(sel), sel.stride(1), n, int(src_offset),
+                                  _p(dst_k), _p(dst_v), dst_k.stride(1) // 128, int(dst_offset), _p(status),
+                                  _stream(dst_k)), "zkv_h2d_gather_kv")
 
 
 class PageLayer:

@@ -29,7 +29,19 @@ B200 layout: every layer keeps ONE absolute-position K/V buffer in HBM
 flush only encodes the newly completed chunks in place -- no D2H copy and no
 local-window slide; the reference's offload bookkeeping (`cpu_valid_end`)
 is kept so zone boundaries are identical.  The `enable_offload` keyword is
-accepted and selects that bookkeeping; the data never leaves HBM.
+accepted and selects that bookkeeping.
+
+Offload tier (env ZKV_HOST_RETRIEVAL=1, reference attention mode, with
+enable_offload=True): for contexts beyond HBM the raw rows of the retrieval
+zone live in host-pinned memory (`keys` / `values`, absolute positions),
+as in the reference (REF:519-611).  HBM keeps one window per layer
+(`win_k` / `win_v`): [sink | staging | near], the near part holding every
+token from the first unencoded chunk on.  A flush copies the rows that join
+the retrieval zone to the host, encodes the completed chunks from the
+window and slides it (REF:1379-1512); compute() gathers the selected rows
+from the host into the staging rows (zkv_h2d_gather_kv, the replacement of
+trans_h2d.cu) and attends [sink + staged] and the near rows of the window.
+The chunk metadata and KIVI codes stay in HBM.
 
 Attention modes (env ZKV_ATTENTION_MODE):
   "reference" (default)  attention over the raw bf16 rows of the selected
@@ -76,6 +88,7 @@ def env_config(final_topk: int = 100) -> dict:
         kivi_bits=int(e.get("POLAR_KIVI_BITS", "4")),
         stage1=e.get("POLAR_QUEST_STAGE1", "1") not in ("0", "false", "False", ""),
         attention_mode=e.get("ZKV_ATTENTION_MODE", "reference").strip().lower(),
+        host_retrieval=e.get("ZKV_HOST_RETRIEVAL", "0") in _TRUE,
     )
     if cfg["dynamic"]:
         try:
@@ -294,6 +307,12 @@ class polar_cache:
         self.quest_chunk_size = self.cfg["chunk"]
         self.MAX_SKIPPED_INDICES = self.cfg["max_skipped"]
         self.attention_mode = self.cfg["attention_mode"]
+        self.host_tier = self.cfg["host_retrieval"]
+        if self.host_tier and not enable_offload:
+            raise ValueError("ZKV_HOST_RETRIEVAL=1 needs enable_offload=True (the offload zone bookkeeping)")
+        if self.host_tier and self.attention_mode != "reference":
+            raise ValueError("the host-pinned retrieval zone serves ZKV_ATTENTION_MODE=reference; page mode reads "
+                             "4-bit pages from HBM and never the raw retrieval rows")
         self.sched = CacheSchedule(layer_num, sink_size, local_size, self.dynamic_update_interval, self.input_length,
                                    self.cfg, offload=enable_offload)
         self.context = 0
@@ -307,12 +326,25 @@ class polar_cache:
         self.device = self._layer_dev[0]
         bs, H, D, nm = batch_size, num_key_value_heads, head_dim, self._n_max
         self.keys, self.values = [], []
+        self.win_k, self.win_v, self.win_base = [], [], [sink_size] * layer_num
+        # offload-tier window: staging rows for the gathered selection (or,
+        # below the retrieval threshold, every host row) + the near rows
+        min_total = max(full_attention_threshold, sink_size + local_size + final_topk * 2)
+        self._stage = min(self.cap, max(final_topk + self.MAX_SKIPPED_INDICES, min_total))
+        self._near_cap = local_size + self.dynamic_update_interval + 2 * CHUNK
         self.chunk_min, self.chunk_max, self.chunk_centroid, self.chunk_valid, self.kivi_packed = [], [], [], [], []
         self.vcodes_t, self.vmeta, self.kscale = [], [], []
         for l in range(layer_num):
             d = dict(device=self._layer_dev[l])
-            self.keys.append(torch.zeros(bs, H, self.cap, D, dtype=torch.bfloat16, **d))
-            self.values.append(torch.zeros(bs, H, self.cap, D, dtype=torch.bfloat16, **d))
+            if self.host_tier:
+                self.keys.append(torch.zeros(bs, H, self.cap, D, dtype=torch.bfloat16, pin_memory=True))
+                self.values.append(torch.zeros(bs, H, self.cap, D, dtype=torch.bfloat16, pin_memory=True))
+                W = sink_size + self._stage + self._near_cap
+                self.win_k.append(torch.zeros(bs, H, W, D, dtype=torch.bfloat16, **d))
+                self.win_v.append(torch.zeros(bs, H, W, D, dtype=torch.bfloat16, **d))
+            else:
+                self.keys.append(torch.zeros(bs, H, self.cap, D, dtype=torch.bfloat16, **d))
+                self.values.append(torch.zeros(bs, H, self.cap, D, dtype=torch.bfloat16, **d))
             self.chunk_min.append(torch.zeros(bs, H, nm, D, dtype=torch.bfloat16, **d))
             self.chunk_max.append(torch.zeros(bs, H, nm, D, dtype=torch.bfloat16, **d))
             self.chunk_centroid.append(torch.zeros(bs, H, nm, D, dtype=torch.bfloat16, **d))
@@ -366,14 +398,15 @@ class polar_cache:
                 sc["skipped"][:, :, :skipped].copy_(
                     torch.arange(n_chunks * CHUNK, kv_len, dtype=torch.int64, device=sc["skipped"].device))
 
-    def _encode_range(self, l: int, rows: slice, tok_lo: int, tok_hi: int) -> None:
+    def _encode_range(self, l: int, rows: slice, tok_lo: int, tok_hi: int, src_k=None) -> None:
         """Encode the retrieval-zone tokens [tok_lo, tok_hi) (zone coordinates,
         both multiples of 16) of layer l: chunk min/max/mean + KIVI codes
-        (+ 4-bit values in page mode)."""
+        (+ 4-bit values in page mode).  src_k: the keys of exactly those
+        tokens when they are not read from the HBM cache (offload tier)."""
         if tok_hi <= tok_lo:
             return
         s = self.sink_size
-        k = self.keys[l][rows, :, s + tok_lo:s + tok_hi]
+        k = self.keys[l][rows, :, s + tok_lo:s + tok_hi] if src_k is None else src_k
         ops.kivi_encode_chunks(k, self.chunk_min[l][rows], self.chunk_max[l][rows], self.chunk_centroid[l][rows],
                                self.chunk_valid[l][rows], self.kivi_packed[l][rows], tok_lo // CHUNK,
                                kscale=self.kscale[l][rows] if self.attention_mode == "page" else None)
@@ -412,17 +445,54 @@ class polar_cache:
             raise RuntimeError(f"prefill of {n} tokens exceeds the cache capacity {self.cap}")
         kk = key_states[:, vs:seq_len].transpose(1, 2).to(torch.bfloat16)
         vv = value_states[:, vs:seq_len].transpose(1, 2).to(torch.bfloat16)
-        self.keys[layer_idx][rows, :, :n].copy_(kk)
-        self.values[layer_idx][rows, :, :n].copy_(vv)
+        if not self.host_tier:
+            self.keys[layer_idx][rows, :, :n].copy_(kk)
+            self.values[layer_idx][rows, :, :n].copy_(vv)
         first = self.sched.actual_retrieval is None
-        _, _, (lo, hi) = self.sched.prefill(layer_idx, seq_len, vs)
+        _, r_len, (lo, hi) = self.sched.prefill(layer_idx, seq_len, vs)
         if first:
             self._refresh_skipped()
-        self._encode_range(layer_idx, rows, lo, hi)
+        if self.host_tier:
+            self._prefill_host(layer_idx, rows, kk, vv, n, r_len, hi)
+            s = self.sink_size
+            self._encode_range(layer_idx, rows, lo, hi, src_k=kk[:, :, s + lo:s + hi])
+        else:
+            self._encode_range(layer_idx, rows, lo, hi)
         last_call = (layer_idx == self.layer_num - 1) and (bsz > 1 or batch_idx + bsz == self.batch_size)
         if last_call:
             self.context += n
         return key_states[:, vs:], value_states[:, vs:]
+
+    def _prefill_host(self, l, rows, kk, vv, n, r_len, enc_hi):
+        """Offload tier: sink rows to the window, retrieval rows to the host
+        zone, and every token from the first unencoded chunk on to the near
+        part of the window."""
+        s = self.sink_size
+        ns = min(s, n)
+        self.win_k[l][rows, :, :ns].copy_(kk[:, :, :ns])
+        self.win_v[l][rows, :, :ns].copy_(vv[:, :, :ns])
+        if r_len > 0:
+            self.keys[l][rows, :, s:s + r_len].copy_(kk[:, :, s:s + r_len])
+            self.values[l][rows, :, s:s + r_len].copy_(vv[:, :, s:s + r_len])
+        base = s + enc_hi
+        m = max(0, n - base)
+        if m > self._near_cap:
+            raise RuntimeError(f"prefill leaves {m} unencoded tokens; the near window holds {self._near_cap}")
+        off = s + self._stage
+        self.win_k[l][rows, :, off:off + m].copy_(kk[:, :, base:base + m])
+        self.win_v[l][rows, :, off:off + m].copy_(vv[:, :, base:base + m])
+        self.win_base[l] = base
+
+    def _win_slot(self, l: int, pos: int) -> int:
+        """Window row of absolute position pos (offload tier)."""
+        s = self.sink_size
+        if pos < s:
+            return pos
+        j = pos - self.win_base[l]
+        if j < 0 or j >= self._near_cap:
+            raise RuntimeError(f"position {pos} is outside the near window of layer {l} "
+                               f"(base {self.win_base[l]}, capacity {self._near_cap})")
+        return s + self._stage + j
 
     def sync(self, layer_idx, batch_idx):
         """REF:2789-2793: nothing to wait for (no host copies)."""
@@ -438,8 +508,13 @@ class polar_cache:
         if pos >= self.cap:
             raise RuntimeError(f"KV write is outside the cache: layer={layer_idx}, current={pos}, "
                                f"capacity={self.cap}")
-        self.keys[layer_idx][:, :, pos].copy_(key_states[:, 0])
-        self.values[layer_idx][:, :, pos].copy_(value_states[:, 0])
+        if self.host_tier:
+            w = self._win_slot(layer_idx, pos)
+            self.win_k[layer_idx][:, :, w].copy_(key_states[:, 0])
+            self.win_v[layer_idx][:, :, w].copy_(value_states[:, 0])
+        else:
+            self.keys[layer_idx][:, :, pos].copy_(key_states[:, 0])
+            self.values[layer_idx][:, :, pos].copy_(value_states[:, 0])
         self.sched.append(layer_idx)
         if layer_idx == self.layer_num - 1:
             self.context += 1
@@ -450,10 +525,31 @@ class polar_cache:
         encode the chunks the new tokens complete.  The live carry of the
         previous flush is read from the same buffer, so every chunk matches
         the reference's carry-merged chunk byte for byte."""
+        old_r = self.sched.actual_retrieval
         lo, hi, _ = self.sched.flush()
         self._refresh_skipped()
+        if not self.host_tier:
+            for l in range(self.layer_num):
+                self._encode_range(l, self._rows(None), lo, hi)
+            return
+        s, new_r = self.sink_size, self.sched.actual_retrieval
+        off = s + self._stage
         for l in range(self.layer_num):
-            self._encode_range(l, self._rows(None), lo, hi)
+            base, total = self.win_base[l], self.current_seq_len[l]
+            wk, wv = self.win_k[l], self.win_v[l]
+            # rows that joined the retrieval zone -> host zone (the D2H offload)
+            a, b = s + old_r - base, s + new_r - base
+            self.keys[l][:, :, s + old_r:s + new_r].copy_(wk[:, :, off + a:off + b])
+            self.values[l][:, :, s + old_r:s + new_r].copy_(wv[:, :, off + a:off + b])
+            # the completed chunks start at the window base (s + lo == base)
+            self._encode_range(l, self._rows(None), lo, hi, src_k=wk[:, :, off:off + hi - lo])
+            # slide: the window now starts at the first unencoded token
+            nb = s + hi
+            m = total - nb
+            if nb > base and m > 0:
+                wk[:, :, off:off + m].copy_(wk[:, :, off + nb - base:off + nb - base + m].clone())
+                wv[:, :, off:off + m].copy_(wv[:, :, off + nb - base:off + nb - base + m].clone())
+            self.win_base[l] = nb
 
     # ------------------------------------------------------------------ regions
     def get_region_indices(self, layer_idx, device=None):
@@ -483,6 +579,8 @@ class polar_cache:
         q = queries if queries.is_contiguous() else queries.contiguous()
         if total < min_total or valid_length <= 0 or not self.cfg["stage1"]:
             # full attention over every stored token (REF:1631-1646, 1280-1334)
+            if self.host_tier:
+                return self._full_attention_host(q, l, total, sc)
             return ops.attn_rows(q, self.keys[l], self.values[l], seg0=(0, total), status=sc["status"])
         n_chunks, nk, n_dense, skipped = self.sched.plan
         n_valid_chunks = valid_length // CHUNK
@@ -496,6 +594,21 @@ class polar_cache:
                              max(1, min(self.cfg["dense_topk"], CHUNK)), max(1, min(self.cfg["sparse_topk"], CHUNK)),
                              k, sc["skipped"][:, :, :skipped], final, sc["workspace"])
         torch.cuda.nvtx.range_pop()
+        if self.host_tier:
+            # REF:1710-1750: the selected rows come over the host link into
+            # the staging rows; attention reads [sink + staged] and the near
+            # rows of the window
+            torch.cuda.nvtx.range_push("h2d_gather_kv")
+            n = k + skipped
+            ops.h2d_gather_rows(self.keys[l], self.values[l], final, self.win_k[l], self.win_v[l], n_sel=n,
+                                src_offset=s, dst_offset=s, status=sc["status"])
+            torch.cuda.nvtx.range_pop()
+            torch.cuda.nvtx.range_push("compute_attention")
+            off, base = s + self._stage, self.win_base[l]
+            out = ops.attn_rows(q, self.win_k[l], self.win_v[l], seg0=(0, s + n),
+                                seg1=(off + local_start - base, off + total - base), status=sc["status"])
+            torch.cuda.nvtx.range_pop()
+            return out
         torch.cuda.nvtx.range_push("compute_attention")
         # sink + selected retrieval tokens + near zone [local_start, total)
         # (REF:1752-1761: the all-GPU gather uses the same three segments)
@@ -503,6 +616,22 @@ class polar_cache:
                             sel_offset=s, seg1=(local_start, total), status=sc["status"])
         torch.cuda.nvtx.range_pop()
         return out
+
+    def _full_attention_host(self, q, l, total, sc):
+        """Offload tier below the retrieval threshold: every host row
+        [sink, window base) is gathered into the staging rows, then attention
+        covers sink + staged + the near rows."""
+        s, base = self.sink_size, self.win_base[l]
+        n_h = max(0, base - s) if total > s else 0
+        if n_h > self._stage:
+            raise RuntimeError(f"full attention over {n_h} host rows exceeds the {self._stage} staging rows")
+        if n_h > 0:
+            ar = self._scratch[self._layer_dev[l]]["arange"][:n_h].expand(self.batch_size, self.kv_head, n_h)
+            ops.h2d_gather_rows(self.keys[l], self.values[l], ar, self.win_k[l], self.win_v[l], src_offset=s,
+                                dst_offset=s, status=sc["status"])
+        off = s + self._stage
+        return ops.attn_rows(q, self.win_k[l], self.win_v[l], seg0=(0, min(total, s) + n_h),
+                             seg1=(off, off + max(0, total - base)), status=sc["status"])
 
     def _compute_page(self, q, l, n_chunks, nk, valid_length, total):
         """Fused page-mode decode over the encoded chunks; the carry tail and
