@@ -432,12 +432,11 @@ def run_config3(args):
     layers, bs, H, ctx, budget = args.layers, 1, KV_HEADS, 131072, 4096
     n_c, nk, n_near = (ctx - RESIDUAL) // PAGE, budget // PAGE, RESIDUAL
     lo, hi, per = S.split_range(n_c, world, rank)
-    caches, qs, bufs = [], [], []
+    caches, qs = [], []
     for l in range(layers):
         pc, _ = W.build_page_cache(5000 + l, bs, H, n_c * PAGE, n_near, dev)   # same data on every rank
         caches.append(pc)
         qs.append(W.synth_query(torch.Generator(device=dev).manual_seed(900 + l), bs, H * G, dev))
-        bufs.append(S.SplitBuffers.alloc(bs, H, G, per, nk, world, dev))
     layers_local = [S.local_layer(pc.layer(), lo, hi) for pc in caches]
     full_layers = [pc.layer() for pc in caches]
     stream = torch.cuda.Stream(device=dev)
@@ -458,14 +457,23 @@ def run_config3(args):
             layer_loop()
         step = graph.replay
     else:
+        # the exchanges go through peer memory (zkv_peer_put / zkv_peer_wait
+        # over NVLink, buffers shared once by CUDA IPC): no collective on the
+        # data path, so the 36-layer step is captured in one CUDA graph
+        pg = S.PeerGroup(bs, H, G, n_c, nk, world, rank, dev)
+
         def layer_loop():
             for l in range(layers):
-                S.decode_step(qs[l], layers_local[l], n_c, nk, bufs[l], rank=rank, world=world, n_near=n_near)
+                S.decode_step_p2p(qs[l], layers_local[l], pg, n_near=n_near)
 
-        # eager: capturing these NCCL all-gathers in a CUDA graph hung on
-        # this pool, so the multi-GPU step is not captured
-        step = layer_loop
-        mode = "eager"
+        with torch.cuda.stream(stream):
+            layer_loop()  # every rank runs the same puts and waits
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            layer_loop()
+        step = graph.replay
+        mode = "peer-memory exchange over NVLink, CUDA graph"
 
     with torch.cuda.stream(stream):
         step()
@@ -477,8 +485,10 @@ def run_config3(args):
     bytes_step = layers * W.page_algorithmic_bytes(bs * H, n_c, nk, n_near, G)
     if world == 1:
         launches = layers * args.steps * ops.page_decode_plan(bs * H, n_c, nk, device=dev)["launches"]
-    else:  # per layer: GQA mean, local scores, global top-k, attend, LSE merge (+ NCCL all-gathers)
-        launches = layers * args.steps * 5
+    else:  # per layer: scores, put, wait, top-k, attend, put, wait, LSE merge
+        launches = layers * args.steps * 8
+        if int(pg.status.item()) != 0:
+            raise RuntimeError(f"peer wait expired (status {int(pg.status.item())})")
     peak, kind = load_peaks()
     ach = bytes_step / (ms / 1e3) / 1e9
     line = {"metric": "config3 sparse decode tokens/s at Qwen3-4B shape, 131072 ctx (sequence split)",
@@ -494,6 +504,8 @@ def run_config3(args):
                          "frac_per_gpu": ach / world / peak, "peak_kind": kind, "bytes_per_step": bytes_step},
             "clocks": clk.summary()}
     if world > 1:
+        del graph
+        pg.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:

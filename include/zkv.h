@@ -441,6 +441,52 @@ int zkv_h2d_gather_kv_packed(const void* src_k, const void* src_v, int rows,
                              void* dst_v, int64_t n_dst, int32_t* status,
                              void* stream);
 
+/* ------------------------------------------------------------ peer exchange */
+
+/* The exchange steps of the sequence-split decode over peer memory (NVLink
+ * P2P stores), replacing the NCCL all-gathers of the score rows and of the
+ * partial (out, lse) (no reference counterpart: the reference runs on one
+ * device).  One buffer per rank, shared through CUDA IPC:
+ *   zkv_peer_alloc   cudaMalloc'd, zeroed buffer + its IPC handle
+ *                    (zkv_peer_handle_bytes() bytes, to be sent to peers);
+ *   zkv_peer_open    a peer's handle -> device pointer in this process;
+ *   zkv_peer_close / zkv_peer_free  release a mapping / the own buffer.   */
+int zkv_peer_handle_bytes(void);
+int zkv_peer_alloc(size_t bytes, void** ptr, void* handle);
+int zkv_peer_open(const void* handle, void** ptr);
+int zkv_peer_close(void* ptr);
+int zkv_peer_free(void* ptr);
+
+/* One strided segment of a put: `rows` rows of `row_bytes` from
+ * src + r*src_ld_bytes to peer_base + dst_off_bytes + r*dst_ld_bytes (all
+ * multiples of 4).                                                        */
+typedef struct zkv_peer_seg {
+    const void* src;
+    int64_t src_ld_bytes;
+    int64_t dst_off_bytes;
+    int64_t dst_ld_bytes;
+    int64_t row_bytes;
+    int32_t rows;
+    int32_t pad;
+} zkv_peer_seg;
+
+/* Copy 1-2 segments into every peer's buffer (peer_base[p], p < world, a
+ * host array of device pointers; peer_base[rank] is this rank's own
+ * buffer), then raise the flag word `rank` of the uint32 flag array at
+ * byte offset flag_off of every peer buffer to *epoch + 1 (release, system
+ * scope) once all stores are done.  `epoch`, `done`: device words of this
+ * rank (done = 0 initially; the kernel returns it to 0).  chunks: CTAs per
+ * peer (0 = 4).                                                           */
+int zkv_peer_put(const zkv_peer_seg* segs, int n_seg, void* const* peer_base,
+                 int64_t flag_off, int rank, int world, uint32_t* epoch,
+                 uint32_t* done, int chunks, void* stream);
+
+/* Wait until flags[0..world) (this rank's flag array) all reach *epoch + 1
+ * (acquire, system scope), then advance *epoch.  The wait is bounded: on
+ * expiry ZKV_ERR_TIMEOUT is written to `status` and the kernel returns.    */
+int zkv_peer_wait(const uint32_t* flags, uint32_t* epoch, int world,
+                  int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,7 +43,7 @@ def test_every_declared_symbol_is_exported_and_bound():
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
 def test_struct_layouts_match_c(tmp_path):
     structs = {"zkv_page_layer": _lib.ZkvPageLayer, "zkv_rq_layout": _lib.ZkvRqLayout,
-               "zkv_ref_layer": _lib.ZkvRefLayer}
+               "zkv_ref_layer": _lib.ZkvRefLayer, "zkv_peer_seg": _lib.ZkvPeerSeg}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void){"]
     for cname, cls in structs.items():
         lines.append(f'printf("%zu\\n", sizeof({cname}));')
@@ -70,3 +70,7 @@ def test_status_on_bad_arguments_without_gpu():
     assert lib.zkv_topk_f32(None, -1, 10, 10, 1, None, None) == 1
     assert lib.zkv_rq_encode(None, 128, 1, 1, 0, None, None, None) == 1
     assert lib.zkv_collision_topk(None, None, 1, 1, None, 1, 1, None, None, None) == 1
+    assert lib.zkv_h2d_gather_kv(None, None, 1, 1, None, 1, 1, 0, None, None, 1, 0, None, None) == 1
+    assert lib.zkv_peer_put(None, 1, None, 0, 0, 1, None, None, 0, None) == 1
+    assert lib.zkv_peer_wait(None, None, 1, None, None) == 1
+    assert lib.zkv_peer_handle_bytes() == 64

@@ -124,3 +124,115 @@ def test_nccl_world2(tmp_path):
         assert np.array_equal(r["sel"].reshape(r["ref_sel"].shape), r["ref_sel"])
         assert np.array_equal(r["out"], res[0]["out"])
         _close(torch.from_numpy(r["out"]), torch.from_numpy(r["ref"]))
+
+
+def test_p2p_world1_matches_nccl_form_and_replays_in_a_graph():
+    """The peer-memory transport at world size 1 (put into the own buffer,
+    wait on the own flag): identical to the collective form, and correct
+    across repeated steps and CUDA-graph replays (device-resident epochs)."""
+    dev = torch.device("cuda", 0)
+    bs, H, n_c, nk, n_near = 1, 8, 1500, 128, 64
+    pcs = [_setup(40 + i, bs, H, n_c, n_near, dev) for i in range(3)]
+    pg = S.PeerGroup(bs, H, G, n_c, nk, 1, 0, dev)
+    try:
+        refs = []
+        for pc, q in pcs:
+            bufs = S.SplitBuffers.alloc(bs, H, G, n_c, nk, 1, dev)
+            o, s = S.decode_step(q, pc.layer(), n_c, nk, bufs, rank=0, world=1, n_near=n_near)
+            refs.append((o.clone(), s.clone()))
+        for _ in range(2):  # eager, twice (epochs advance)
+            for (pc, q), (ro, rs) in zip(pcs, refs):
+                o, s = S.decode_step_p2p(q, pc.layer(), pg, n_near=n_near)
+                torch.cuda.synchronize()
+                assert torch.equal(s, rs) and torch.equal(o, ro)
+        stream = torch.cuda.Stream(device=dev)
+        outs = [torch.empty_like(refs[0][0]) for _ in pcs]
+
+        def loop():
+            for i, (pc, q) in enumerate(pcs):
+                o, _ = S.decode_step_p2p(q, pc.layer(), pg, n_near=n_near)
+                outs[i].copy_(o)
+
+        with torch.cuda.stream(stream):
+            loop()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            loop()
+        for _ in range(3):
+            graph.replay()
+            torch.cuda.synchronize()
+            for o, (ro, _) in zip(outs, refs):
+                assert torch.equal(o, ro)
+        del graph
+        assert int(pg.status.item()) == 0
+    finally:
+        pg.close()
+
+
+def _p2p_rank(rank, world, port, path):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    # gloo only carries the IPC handles and barriers; the data path is P2P
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    pg = None
+    try:
+        bs, H, n_c, nk, n_near = 1, 8, 8184, 256, 128
+        pcs = [_setup(60 + i, bs, H, n_c, n_near, dev) for i in range(2)]
+        pg = S.PeerGroup(bs, H, G, n_c, nk, world, rank, dev)
+        lo, hi = pg.lo, pg.hi
+        res = {}
+        for i, (pc, q) in enumerate(pcs):
+            out, sel = S.decode_step_p2p(q, S.local_layer(pc.layer(), lo, hi), pg, n_near=n_near)
+            ref_sel = torch.empty(bs * H, nk, dtype=torch.int64, device=dev)
+            ref = ops.page_decode(q, pc.layer(), n_c, nk, n_near, sel_out=ref_sel)
+            torch.cuda.synchronize()
+            res[f"out{i}"], res[f"ref{i}"] = out.float().cpu().numpy(), ref.float().cpu().numpy()
+            res[f"sel{i}"], res[f"ref_sel{i}"] = sel.cpu().numpy(), ref_sel.cpu().numpy()
+        # the two layers as one CUDA graph, replayed
+        stream = torch.cuda.Stream(device=dev)
+        outs = [torch.empty(bs, 1, H * G, 128, dtype=torch.bfloat16, device=dev) for _ in pcs]
+
+        def loop():
+            for i, (pc, q) in enumerate(pcs):
+                o, _ = S.decode_step_p2p(q, S.local_layer(pc.layer(), lo, hi), pg, n_near=n_near)
+                outs[i].copy_(o)
+
+        with torch.cuda.stream(stream):
+            loop()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            loop()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        for i in range(len(pcs)):
+            res[f"graph{i}"] = outs[i].float().cpu().numpy()
+        res["status"] = np.array([int(pg.status.item())])
+        del graph
+        np.savez(os.path.join(path, f"p{rank}.npz"), **res)
+    finally:
+        if pg is not None:
+            pg.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_p2p_world2(tmp_path):
+    """Two ranks, one per GPU, exchanging scores and partials through peer
+    memory: the selection equals the single-device selection exactly, the
+    output is the same on both ranks and within tolerance of the fused
+    single-device decode, eager and replayed as a CUDA graph."""
+    mp.start_processes(_p2p_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    res = [np.load(os.path.join(tmp_path, f"p{r}.npz")) for r in range(2)]
+    for r in res:
+        assert int(r["status"][0]) == 0
+        for i in range(2):
+            assert np.array_equal(r[f"sel{i}"].reshape(r[f"ref_sel{i}"].shape), r[f"ref_sel{i}"])
+            assert np.array_equal(r[f"out{i}"], res[0][f"out{i}"])
+            assert np.array_equal(r[f"graph{i}"], r[f"out{i}"])
+            _close(torch.from_numpy(r[f"out{i}"]), torch.from_numpy(r[f"ref{i}"]))

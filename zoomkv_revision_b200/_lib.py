@@ -48,6 +48,12 @@ class ZkvRefLayer(ctypes.Structure):
                 ("packed", _c_void_p)]
 
 
+class ZkvPeerSeg(ctypes.Structure):
+    """Mirror of `zkv_peer_seg` (include/zkv.h)."""
+    _fields_ = [("src", _c_void_p), ("src_ld_bytes", _i64), ("dst_off_bytes", _i64), ("dst_ld_bytes", _i64),
+                ("row_bytes", _i64), ("rows", _i32), ("pad", _i32)]
+
+
 _RQ = ctypes.POINTER(ZkvRqLayout)
 
 # name -> argtypes (restype is int status unless noted)
@@ -64,6 +70,14 @@ _SIGNATURES = {
     "zkv_kivi_qk": [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _c_void_p, _i32, _c_void_p, _i32, _i32, _i32,
                     _i32, _c_void_p, _c_void_p, _i64, _c_void_p],
     "zkv_topk_gather_concat": [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p, _i32, _i32, _i32, _i32, _i64, _c_void_p],
+    "zkv_peer_handle_bytes": [],
+    "zkv_peer_alloc": [ctypes.c_size_t, ctypes.POINTER(_c_void_p), _c_void_p],
+    "zkv_peer_open": [_c_void_p, ctypes.POINTER(_c_void_p)],
+    "zkv_peer_close": [_c_void_p],
+    "zkv_peer_free": [_c_void_p],
+    "zkv_peer_put": [ctypes.POINTER(ZkvPeerSeg), _i32, ctypes.POINTER(_c_void_p), _i64, _i32, _i32, _c_void_p,
+                     _c_void_p, _i32, _c_void_p],
+    "zkv_peer_wait": [_c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p],
     "zkv_h2d_gather_kv": [_c_void_p, _c_void_p, _i32, _i64, _c_void_p, _i64, _i32, _i64, _c_void_p, _c_void_p, _i64,
                           _i64, _c_void_p, _c_void_p],
     "zkv_h2d_gather_kv_packed": [_c_void_p, _c_void_p, _i32, _i64, _c_void_p, _c_void_p, _c_void_p, _i32, _i32,

@@ -1,0 +1,189 @@
+// zkv_peer.cu -- the exchange steps of the sequence-split decode over peer
+// memory (NVLink P2P), without a collective library on the data path.
+//
+// Every rank allocates one buffer with zkv_peer_alloc and shares its IPC
+// handle; each rank opens the others' handles (zkv_peer_open), so every
+// rank holds a device pointer into every peer's buffer.  An exchange step
+// is then two launches on the rank's stream:
+//
+//   zkv_peer_put   copies this rank's slice into slot `rank` of every
+//                  peer's buffer with plain stores over NVLink, and, once
+//                  every CTA's stores are done, raises this rank's flag in
+//                  every peer to epoch + 1 (release at system scope);
+//   zkv_peer_wait  one warp polls (acquire, system scope) until the flags of
+//                  all ranks reach epoch + 1, then advances the local epoch.
+//
+// The epoch lives in device memory and only the wait advances it, so a
+// captured CUDA graph replays correctly.  Every rank runs the same sequence
+// of puts and waits, so epochs agree across ranks.  A wait gives up after
+// kMaxPolls polls (well under a second of sleeping polls), records
+// ZKV_ERR_TIMEOUT in the status word and returns, so a rank that never
+// arrives ends in a host-side error, not a hung GPU.  No TMA and no
+// multicast are used: the copies are 4-byte thread stores.
+#include <cstring>
+
+#include "zkv_common.cuh"
+
+namespace zkv {
+namespace {
+
+constexpr int kPutThreads = 256;
+constexpr int kMaxPeers = 8;
+constexpr int kMaxSegs = 2;
+
+struct PutSeg {
+    const uint32_t* src;  // [rows][src_ld] words
+    int64_t src_ld, dst_ld, dst_off;  // words
+    int rows, row_words;
+};
+
+struct PutArgs {
+    PutSeg seg[kMaxSegs];
+    int n_seg;
+    uint32_t* dst[kMaxPeers];    // base of every peer's buffer (this rank's mapping)
+    uint32_t* flag[kMaxPeers];   // this rank's flag word inside every peer's buffer
+    const uint32_t* epoch;       // local
+    uint32_t* done;              // local counter of finished CTAs (0 between launches)
+    int world;
+    int chunks;                  // CTAs per peer
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// CTA (p, c) copies chunk c of every segment to peer p; the last CTA to
+// finish raises the flags.
+__global__ void __launch_bounds__(kPutThreads) peer_put_kernel(const PutArgs a) {
+    const int p = blockIdx.x / a.chunks, c = blockIdx.x - p * a.chunks;
+    uint32_t* dst = a.dst[p];
+    for (int s = 0; s < a.n_seg; ++s) {
+        const PutSeg g = a.seg[s];
+        const int64_t total = (int64_t)g.rows * g.row_words;
+        const int64_t per = (total + a.chunks - 1) / a.chunks;
+        const int64_t i0 = (int64_t)c * per, i1 = min(total, i0 + per);
+        for (int64_t i = i0 + threadIdx.x; i < i1; i += kPutThreads) {
+            const int64_t r = i / g.row_words, w = i - r * g.row_words;
+            dst[g.dst_off + r * g.dst_ld + w] = __ldg(g.src + r * g.src_ld + w);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();  // this CTA's peer stores before its arrival
+        const uint32_t prev = atomicAdd(a.done, 1u);
+        if (prev == gridDim.x - 1) {  // every CTA's stores are visible system-wide
+            __threadfence_system();
+            const uint32_t target = *a.epoch + 1u;
+            for (int q = 0; q < a.world; ++q) st_release_sys(a.flag[q], target);
+            *a.done = 0u;
+        }
+    }
+}
+
+__global__ void peer_wait_kernel(const uint32_t* flags, uint32_t* epoch, int world, int32_t* status) {
+    const int lane = threadIdx.x;
+    const uint32_t target = *epoch + 1u;
+    bool ok = true;
+    if (lane < world) {
+        uint32_t polls = 0;
+        while ((int32_t)(ld_acquire_sys(flags + lane) - target) < 0) {
+            if (++polls > kMaxPolls) {
+                ok = false;
+                break;
+            }
+            __nanosleep(256);
+        }
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (lane == 0) {
+        if (!ok) set_status(status, ZKV_ERR_TIMEOUT);
+        __threadfence();
+        *epoch = target;
+    }
+}
+
+}  // namespace
+}  // namespace zkv
+
+using namespace zkv;
+
+extern "C" int zkv_peer_alloc(size_t bytes, void** ptr, void* handle) {
+    if (!ptr || !handle || bytes == 0) return ZKV_ERR_ARG;
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return ZKV_ERR_LAUNCH;
+    }
+    cudaIpcMemHandle_t h;
+    if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(p);
+        return ZKV_ERR_LAUNCH;
+    }
+    memcpy(handle, &h, sizeof(h));
+    *ptr = p;
+    return ZKV_OK;
+}
+
+extern "C" int zkv_peer_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int zkv_peer_open(const void* handle, void** ptr) {
+    if (!handle || !ptr) return ZKV_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    if (cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        return ZKV_ERR_LAUNCH;
+    }
+    return ZKV_OK;
+}
+
+extern "C" int zkv_peer_close(void* ptr) {
+    if (!ptr) return ZKV_ERR_ARG;
+    return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH;
+}
+
+extern "C" int zkv_peer_free(void* ptr) {
+    if (!ptr) return ZKV_ERR_ARG;
+    return cudaFree(ptr) == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH;
+}
+
+extern "C" int zkv_peer_put(const zkv_peer_seg* segs, int n_seg, void* const* peer_base, int64_t flag_off,
+                            int rank, int world, uint32_t* epoch, uint32_t* done, int chunks, void* stream) {
+    if (!segs || n_seg < 1 || n_seg > kMaxSegs || !peer_base || world < 1 || world > kMaxPeers || rank < 0 ||
+        rank >= world || !epoch || !done || flag_off < 0 || (flag_off & 3) || chunks < 0)
+        return ZKV_ERR_ARG;
+    PutArgs a = {};
+    for (int s = 0; s < n_seg; ++s) {
+        const zkv_peer_seg& g = segs[s];
+        if (!g.src || g.rows < 0 || g.row_bytes < 0 || (g.row_bytes & 3) || (g.src_ld_bytes & 3) ||
+            (g.dst_ld_bytes & 3) || (g.dst_off_bytes & 3) || ((uintptr_t)g.src & 3) ||
+            (g.rows > 1 && (g.src_ld_bytes < g.row_bytes || g.dst_ld_bytes < g.row_bytes)))
+            return ZKV_ERR_ARG;
+        a.seg[s] = {reinterpret_cast<const uint32_t*>(g.src), g.src_ld_bytes / 4, g.dst_ld_bytes / 4,
+                    g.dst_off_bytes / 4, (int)g.rows, (int)(g.row_bytes / 4)};
+    }
+    a.n_seg = n_seg;
+    for (int p = 0; p < world; ++p) {
+        if (!peer_base[p] || ((uintptr_t)peer_base[p] & 15)) return ZKV_ERR_ARG;
+        a.dst[p] = reinterpret_cast<uint32_t*>(peer_base[p]);
+        a.flag[p] = reinterpret_cast<uint32_t*>(static_cast<char*>(peer_base[p]) + flag_off) + rank;
+    }
+    a.epoch = epoch;
+    a.done = done;
+    a.world = world;
+    a.chunks = chunks > 0 ? chunks : 4;
+    peer_put_kernel<<<world * a.chunks, kPutThreads, 0, (cudaStream_t)stream>>>(a);
+    return launch_status();
+}
+
+extern "C" int zkv_peer_wait(const uint32_t* flags, uint32_t* epoch, int world, int32_t* status, void* stream) {
+    if (!flags || !epoch || world < 1 || world > kMaxPeers) return ZKV_ERR_ARG;
+    peer_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flags, epoch, world, status);
+    return launch_status();
+}

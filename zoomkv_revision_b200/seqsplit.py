@@ -13,9 +13,19 @@ rank 0 also holds the sink and near rows.  One decode step per layer:
      rows), producing a normalised fp32 partial and its log-sum-exp;
   5. all-gather of the partials, then a local log-sum-exp merge.
 
-The collectives are plain NCCL all-gathers (no data-path collective inside
-a kernel).  The compute steps go through a backend object; the product
-backend is `CudaBackend` (libzkv kernels, no CPU path).  Reference: the
+Two transports carry the exchanges of steps 2 and 5:
+
+  * `decode_step_p2p` (the product on NVLink): every rank writes its slice
+    straight into every peer's buffer with stores over NVLink and raises a
+    flag there (zkv_peer_put); the consumer waits on its flags with a
+    bounded poll (zkv_peer_wait).  The buffers are shared once through CUDA
+    IPC (`PeerGroup`); a layer is 8 launches, none of them a collective, and
+    the step can be captured in a CUDA graph (the epochs live on the device);
+  * `decode_step` with NCCL all-gathers (any backend torch.distributed
+    offers; also the CPU/gloo form the host-logic tests run).
+
+The compute steps go through a backend object; the product backend is
+`CudaBackend` (libzkv kernels, no CPU path).  Reference: the
 sequence split replaces the single-device gather of polar_cache.compute
 (cache_hub/polar_cache_quest_density_single_layer_kivi.py:1589-1775) for
 contexts beyond one device; the merge is lse_merge (lse_merge/lse_merge.py).
@@ -28,7 +38,9 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
-from . import ops
+import ctypes
+
+from . import _lib, ops
 
 
 def _all_gather(out, inp, group=None):
@@ -141,3 +153,142 @@ def local_layer(layer: ops.PageLayer, lo: int, hi: int) -> ops.PageLayer:
     t = layer.tensors
     cut = [x[:, :, lo:max(hi, lo + 1)] for x in t[:6]]
     return ops.PageLayer(*cut, t[6], t[7], t[8][:, :, lo:max(hi, lo + 1)])
+
+
+# --------------------------------------------------------------------------- peer-memory transport
+class _CudaArray:
+    """A raw device pointer exposed as a CUDA array (torch.as_tensor wraps it
+    without a copy; the owner keeps the allocation alive)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 2, "strides": None}
+
+
+def _view(ptr: int, shape, dtype, device):
+    typestr = {torch.float32: "<f4", torch.int32: "<i4"}[dtype]
+    return torch.as_tensor(_CudaArray(ptr, shape, typestr), device=device)
+
+
+_FLAGS_A, _FLAGS_B, _EPOCH, _DONE, _HEADER = 0, 32, 64, 68, 256
+
+
+class PeerGroup:
+    """One IPC-shared buffer per rank for the split decode's exchanges.
+
+    Byte layout (every rank the same): a 256-byte header (flags of the
+    score exchange at 0, flags of the partial exchange at 32 -- one uint32
+    per rank --, the device epoch at 64, the put kernel's CTA counter at
+    68), then
+      row    [rows][world*per] fp32  score row; rank r writes columns
+                                     [r*per, r*per + n_loc_r), the rest -inf
+      parts  [world][rows*G][128] fp32, lses [world][rows*G] fp32.
+    Rank-local staging (scores, selection, partials, output) is ordinary
+    torch memory.  Handles travel once through torch.distributed
+    (all_gather_object on `group`)."""
+
+    def __init__(self, bs, H, G, n_c, nk, world, rank, device, group=None):
+        self.bs, self.H, self.G, self.nk, self.world, self.rank = bs, H, G, nk, world, rank
+        self.device = torch.device(device)
+        self.lo, self.hi, self.per = split_range(n_c, world, rank)
+        self.n_c, self.n_loc = n_c, self.hi - self.lo
+        rows = bs * H
+        self.rows = rows
+        L = _lib.lib()
+        a256 = lambda x: (x + 255) // 256 * 256
+        self.off_row = _HEADER
+        self.off_parts = self.off_row + a256(rows * world * self.per * 4)
+        self.off_lses = self.off_parts + a256(world * rows * G * 128 * 4)
+        total = self.off_lses + a256(world * rows * G * 4)
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_char * L.zkv_peer_handle_bytes())()
+        _lib.check(L.zkv_peer_alloc(total, ctypes.byref(ptr), handle), "zkv_peer_alloc")
+        self.base = ptr.value
+        self._opened = []
+        handles = [None] * world
+        if world > 1:
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        bases = []
+        for r in range(world):
+            if r == rank:
+                bases.append(self.base)
+                continue
+            p = ctypes.c_void_p()
+            _lib.check(L.zkv_peer_open(handles[r], ctypes.byref(p)), "zkv_peer_open")
+            self._opened.append(p.value)
+            bases.append(p.value)
+        self.peer_base = (ctypes.c_void_p * world)(*bases)
+        dev = self.device
+        self.row = _view(self.base + self.off_row, (bs, H, world * self.per), torch.float32, dev)
+        self.parts = _view(self.base + self.off_parts, (world, rows * G, 128), torch.float32, dev)
+        self.lses = _view(self.base + self.off_lses, (world, rows * G), torch.float32, dev)
+        self.row.fill_(-math.inf)
+        self.flags_a = self.base + _FLAGS_A
+        self.flags_b = self.base + _FLAGS_B
+        self.epoch = self.base + _EPOCH
+        self.done = self.base + _DONE
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.local = torch.empty(max(1, rows * self.n_loc), **f32)
+        self.sel = torch.empty(bs, H, nk, dtype=torch.int64, device=dev)
+        self.part = torch.empty(bs, H * G, 128, **f32)
+        self.lse = torch.empty(bs, H * G, **f32)
+        self.out = torch.empty(bs, 1, H * G, 128, dtype=torch.bfloat16, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        S = _lib.ZkvPeerSeg
+        self._seg_scores = (S * 1)(S(self.local.data_ptr(), self.n_loc * 4, self.off_row + rank * self.per * 4,
+                                     world * self.per * 4, self.n_loc * 4, rows if self.n_loc > 0 else 0, 0))
+        pb = rows * G * 128 * 4
+        self._seg_parts = (S * 2)(S(self.part.data_ptr(), pb, self.off_parts + rank * pb, pb, pb, 1, 0),
+                                  S(self.lse.data_ptr(), rows * G * 4, self.off_lses + rank * rows * G * 4,
+                                    rows * G * 4, rows * G * 4, 1, 0))
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier(group=group)  # every mapping is open before the first put
+        self._group = group
+
+    def _put(self, segs, n_seg, flag_off, stream):
+        _lib.check(_lib.lib().zkv_peer_put(segs, n_seg, self.peer_base, flag_off, self.rank, self.world,
+                                           self.epoch, self.done, 0, stream), "zkv_peer_put")
+
+    def _wait(self, flags, stream):
+        _lib.check(_lib.lib().zkv_peer_wait(flags, self.epoch, self.world, self.status.data_ptr(), stream),
+                   "zkv_peer_wait")
+
+    def close(self):
+        """Unmap the peers and free the own buffer (after a barrier, so no
+        peer still writes into it)."""
+        if self.base is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self._group)
+        L = _lib.lib()
+        for p in self._opened:
+            L.zkv_peer_close(ctypes.c_void_p(p))
+        self._opened = []
+        self.row = self.parts = self.lses = None
+        L.zkv_peer_free(ctypes.c_void_p(self.base))
+        self.base = None
+
+
+def decode_step_p2p(q, layer: ops.PageLayer, pg: PeerGroup, *, n_sink: int = 0, near_start: int = 0,
+                    n_near: int = 0):
+    """decode_step over peer memory: score own pages -> put scores into every
+    peer's score row -> wait -> top-nk -> attend own selected pages -> put the
+    partial (out, lse) into every peer -> wait -> LSE merge.  Returns the
+    merged output [bs, 1, H*G, 128] bf16 (same on every rank) and the
+    selected global page ids [bs, H, nk]."""
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    if pg.n_loc > 0:
+        cmin, cmax, valid = layer.tensors[0], layer.tensors[1], layer.tensors[2]
+        ops.quest_chunk_score_gqa(q, cmin, cmax, pg.local, pg.n_loc, valid)
+    pg._put(pg._seg_scores, 1, _FLAGS_A, stream)
+    pg._wait(pg.flags_a, stream)
+    ops.float_topk_3d(pg.row, pg.nk, out=pg.sel)
+    own_raw = pg.rank == 0
+    ops.page_attend(q, layer, pg.sel, pg.lo, pg.hi, n_sink=n_sink if own_raw else 0, near_start=near_start,
+                    n_near=n_near if own_raw else 0, out_f32=pg.part, lse=pg.lse, status=pg.status)
+    pg._put(pg._seg_parts, 2, _FLAGS_B, stream)
+    pg._wait(pg.flags_b, stream)
+    ops.lse_merge_n(pg.parts, pg.lses, pg.out.view(-1, 128))
+    return pg.out, pg.sel
