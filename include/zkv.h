@@ -441,6 +441,27 @@ int zkv_h2d_gather_kv_packed(const void* src_k, const void* src_v, int rows,
                              void* dst_v, int64_t n_dst, int32_t* status,
                              void* stream);
 
+/* The select + attend step of the sequence split, fused: the top nk of a
+ * precomputed score row (scores [rows][sc_ld], n_c entries: the whole
+ * sequence's chunk scores, -inf past its end) by the cluster two-level
+ * select, then attention over the selected pages in [own_lo, own_hi) --
+ * held by this layer buffer as pages id - own_lo -- plus n_sink / n_near
+ * raw rows, spread over `parts` clusters per row (1..4).  Writes per-part
+ * normalised partials out_f32 [parts][rows][G][128] and lse
+ * [parts][rows][G] (natural log; -inf for a part with nothing to attend),
+ * to be merged with zkv_lse_merge_n together with the other ranks'.
+ * sel_out (may be NULL): the global selection [rows][nk].  Requires
+ * nk < n_c and a cluster of 2..8 CTAs.  Replaces the float_topk_3d +
+ * page attention pair of the split step (no reference counterpart: the
+ * reference runs on one device).                                          */
+int zkv_page_decode_scored(const void* q, const zkv_page_layer* layer,
+                           int rows, int G, int n_max, const float* scores,
+                           int64_t sc_ld, int n_c, int nk, int64_t own_lo,
+                           int64_t own_hi, int n_sink, int near_start,
+                           int n_near, float scale, int parts, float* out_f32,
+                           float* lse, int64_t* sel_out, int32_t* status,
+                           int cluster, void* stream);
+
 /* ------------------------------------------------------------ peer exchange */
 
 /* The exchange steps of the sequence-split decode over peer memory (NVLink
@@ -476,7 +497,7 @@ typedef struct zkv_peer_seg {
  * byte offset flag_off of every peer buffer to *epoch + 1 (release, system
  * scope) once all stores are done.  `epoch`, `done`: device words of this
  * rank (done = 0 initially; the kernel returns it to 0).  chunks: CTAs per
- * peer (0 = 4).                                                           */
+ * peer (0 = automatic: 32 up to 2 ranks, 128 / world beyond).             */
 int zkv_peer_put(const zkv_peer_seg* segs, int n_seg, void* const* peer_base,
                  int64_t flag_off, int rank, int world, uint32_t* epoch,
                  uint32_t* done, int chunks, void* stream);

@@ -83,6 +83,42 @@ def test_emulated_ranks_match_page_decode(world, bs, H, n_c, nk, n_near):
     _close(out, ref)
 
 
+@pytest.mark.parametrize("world,n_c,nk,parts", [(2, 1001, 64, 1), (2, 8184, 256, 4), (4, 8184, 256, 2),
+                                                 (8, 8184, 256, 4)])
+def test_scored_select_attend_own_ranges(world, n_c, nk, parts):
+    """zkv_page_decode_scored, as each rank of a sequence split runs it (ranks
+    emulated one after another; nothing waits): the top nk of the whole
+    score row, attention over the own selected pages only, partials of every
+    rank and cluster merged -> the single-device selection exactly and its
+    output within tolerance."""
+    dev = torch.device("cuda", 0)
+    bs, H, n_near = 1, 8, 128
+    pc, q = _setup(world * 100 + n_c, bs, H, n_c, n_near, dev)
+    sel_ref = torch.empty(bs * H, nk, dtype=torch.int64, device=dev)
+    ref = ops.page_decode(q, pc.layer(), n_c, nk, n_near, sel_out=sel_ref)
+    per = S.split_range(n_c, world, 0)[2]
+    row = torch.full((bs, H, world * per), -float("inf"), device=dev)
+    local = torch.empty(bs * H * n_c, device=dev)
+    lay = pc.layer()
+    ops.quest_chunk_score_gqa(q, lay.tensors[0], lay.tensors[1], local, n_c, lay.tensors[2])
+    row[:, :, :n_c] = local.view(bs, H, n_c)
+    rows = bs * H
+    parts_all = torch.empty(world * parts, rows * G, 128, device=dev)
+    lses_all = torch.empty(world * parts, rows * G, device=dev)
+    for r in range(world):
+        lo, hi, _ = S.split_range(n_c, world, r)
+        sel = torch.empty(bs, H, nk, dtype=torch.int64, device=dev)
+        ops.page_decode_scored(q, S.local_layer(lay, lo, hi), row, world * per, nk, lo, hi, parts,
+                               parts_all[r * parts:(r + 1) * parts], lses_all[r * parts:(r + 1) * parts],
+                               n_near=n_near if r == 0 else 0, sel_out=sel)
+        torch.cuda.synchronize()
+        assert torch.equal(sel.view(rows, nk), sel_ref)
+    out = torch.empty(bs, 1, H * G, 128, dtype=torch.bfloat16, device=dev)
+    ops.lse_merge_n(parts_all, lses_all, out.view(-1, 128))
+    torch.cuda.synchronize()
+    _close(out, ref)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -128,8 +164,11 @@ def test_nccl_world2(tmp_path):
 
 def test_p2p_world1_matches_nccl_form_and_replays_in_a_graph():
     """The peer-memory transport at world size 1 (put into the own buffer,
-    wait on the own flag): identical to the collective form, and correct
-    across repeated steps and CUDA-graph replays (device-resident epochs)."""
+    wait on the own flag): the same selection as the collective form, the
+    output within tolerance of the fused single-device decode (the select +
+    attend kernel spreads a row over several clusters, merged by LSE), and
+    correct across repeated steps and CUDA-graph replays (device-resident
+    epochs)."""
     dev = torch.device("cuda", 0)
     bs, H, n_c, nk, n_near = 1, 8, 1500, 128, 64
     pcs = [_setup(40 + i, bs, H, n_c, n_near, dev) for i in range(3)]
@@ -138,15 +177,22 @@ def test_p2p_world1_matches_nccl_form_and_replays_in_a_graph():
         refs = []
         for pc, q in pcs:
             bufs = S.SplitBuffers.alloc(bs, H, G, n_c, nk, 1, dev)
-            o, s = S.decode_step(q, pc.layer(), n_c, nk, bufs, rank=0, world=1, n_near=n_near)
-            refs.append((o.clone(), s.clone()))
-        for _ in range(2):  # eager, twice (epochs advance)
-            for (pc, q), (ro, rs) in zip(pcs, refs):
+            _, s = S.decode_step(q, pc.layer(), n_c, nk, bufs, rank=0, world=1, n_near=n_near)
+            ref = ops.page_decode(q, pc.layer(), n_c, nk, n_near)
+            refs.append((ref, s.clone()))
+        first = []
+        for it in range(2):  # eager, twice (epochs advance)
+            for i, ((pc, q), (ref, rs)) in enumerate(zip(pcs, refs)):
                 o, s = S.decode_step_p2p(q, pc.layer(), pg, n_near=n_near)
                 torch.cuda.synchronize()
-                assert torch.equal(s, rs) and torch.equal(o, ro)
+                assert torch.equal(s, rs)
+                _close(o, ref)
+                if it == 0:
+                    first.append(o.clone())
+                else:
+                    assert torch.equal(o, first[i])
         stream = torch.cuda.Stream(device=dev)
-        outs = [torch.empty_like(refs[0][0]) for _ in pcs]
+        outs = [torch.empty_like(first[0]) for _ in pcs]
 
         def loop():
             for i, (pc, q) in enumerate(pcs):
@@ -162,8 +208,8 @@ def test_p2p_world1_matches_nccl_form_and_replays_in_a_graph():
         for _ in range(3):
             graph.replay()
             torch.cuda.synchronize()
-            for o, (ro, _) in zip(outs, refs):
-                assert torch.equal(o, ro)
+            for o, f in zip(outs, first):
+                assert torch.equal(o, f)
         del graph
         assert int(pg.status.item()) == 0
     finally:

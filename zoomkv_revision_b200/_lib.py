@@ -70,6 +70,9 @@ _SIGNATURES = {
     "zkv_kivi_qk": [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p, _c_void_p, _i32, _c_void_p, _i32, _i32, _i32,
                     _i32, _c_void_p, _c_void_p, _i64, _c_void_p],
     "zkv_topk_gather_concat": [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p, _i32, _i32, _i32, _i32, _i64, _c_void_p],
+    "zkv_page_decode_scored": [_c_void_p, ctypes.POINTER(ZkvPageLayer), _i32, _i32, _i32, _c_void_p, _i64, _i32,
+                               _i32, _i64, _i64, _i32, _i32, _i32, _f32, _i32, _c_void_p, _c_void_p, _c_void_p,
+                               _c_void_p, _i32, _c_void_p],
     "zkv_peer_handle_bytes": [],
     "zkv_peer_alloc": [ctypes.c_size_t, ctypes.POINTER(_c_void_p), _c_void_p],
     "zkv_peer_open": [_c_void_p, ctypes.POINTER(_c_void_p)],

@@ -419,6 +419,11 @@ struct PageArgs {
     const int64_t* sel_in;
     int64_t sel_lo, sel_hi;
     float* out_f32;  // fp32 partial output instead of bf16 (may be NULL)
+    // two-level scored mode of the sequence split: of the selected global
+    // page ids, attend those in [own_lo, own_hi), this buffer's pages
+    // id - own_lo (own = 0: attend every selected page)
+    int own;
+    int64_t own_lo, own_hi;
 };
 
 // kTwoLevel: the select runs in two levels over a.n_cand candidates (a
@@ -648,11 +653,28 @@ __global__ void __launch_bounds__(kAttnThreads, 4) page_decode_kernel(const Page
     }
     if (a.sel_out && rank == 0 && part == 0 && !a.sel_in)
         for (int i = threadIdx.x; i < a.nk; i += kAttnThreads) a.sel_out[row * a.nk + i] = sel_s[i];
+    if (kTwoLevel && a.own) {  // keep the selected pages this buffer holds, in list order
+        __syncthreads();
+        if (warp == 0) {
+            int base = 0;
+            for (int j0 = 0; j0 < a.nk; j0 += 32) {
+                const int j = j0 + lane;
+                const int id = j < a.nk ? sel_s[j] : -1;
+                const bool mine = id >= a.own_lo && id < a.own_hi;
+                const unsigned bal = __ballot_sync(0xffffffffu, mine);
+                // in place: every write goes below j0 + 32, after the group's reads
+                if (mine) sel_s[base + __popc(bal & ((1u << lane) - 1u))] = (int)(id - a.own_lo);
+                base += __popc(bal);
+            }
+            if (lane == 0) s_nsel = base;
+        }
+        __syncthreads();
+    }
 
     // ------------------------------------------------ phase 3: attention
     WarpAttn st;
     warp_attn_init(st, q_s, a.G);
-    const int nsel = a.sel_in ? s_nsel : a.nk;
+    const int nsel = (a.sel_in || (kTwoLevel && a.own)) ? s_nsel : a.nk;
     // this cluster's share of the selection list (the whole list unless parts > 1)
     const int part_pp = kTwoLevel ? (nsel + a.parts - 1) / a.parts : nsel;
     const int part_lo = kTwoLevel ? min(nsel, part * part_pp) : 0;
@@ -851,9 +873,12 @@ static int pick_cluster(int requested, int rows) {
 static int page_decode_impl(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max, int n_c, int nk,
                             int n_sink, int near_start, int n_near, float scale, void* out, float* lse,
                             int64_t* sel_out, int32_t* status, int cluster, const float* sc_in, int64_t sc_ld,
-                            int parts, float* out_f32, void* stream) {
-    if (!q || !layer || (!out && !out_f32) || rows < 0 || G < 1 || G > 8 || n_c < 0 || n_c > n_max || nk < 1 ||
-        n_near < 0 || n_sink < 0 || near_start < 0)
+                            int parts, float* out_f32, void* stream, int64_t own_lo = 0, int64_t own_hi = -1) {
+    // own mode (own_hi >= own_lo): n_c counts the score row's entries, which
+    // may run past this buffer's pages; the buffer holds [own_lo, own_hi)
+    const bool own = own_hi >= own_lo;
+    if (!q || !layer || (!out && !out_f32) || rows < 0 || G < 1 || G > 8 || n_c < 0 || nk < 1 ||
+        n_near < 0 || n_sink < 0 || near_start < 0 || (!own && n_c > n_max) || (own && own_hi - own_lo > n_max))
         return ZKV_ERR_ARG;
     if (nk > n_c && n_c > 0) return ZKV_ERR_ARG;
     if ((int64_t)near_start + n_near > layer->near_ld || n_sink > layer->near_ld) return ZKV_ERR_ARG;
@@ -883,7 +908,8 @@ static int page_decode_impl(const void* q, const zkv_page_layer* layer, int rows
     a.per = ((n_c + CS - 1) / CS + 3) & ~3;
     a.pp = (a.nk + CS - 1) / CS;
     // past 16 keys per thread the one-level select re-reads shared memory
-    a.n_cand = (CS > 1 && n_c > 16 * kAttnThreads && a.nk < n_c) ? ((CS * a.nk + 3) & ~3) : 0;
+    a.n_cand = (CS > 1 && (n_c > 16 * kAttnThreads || own) && a.nk < n_c) ? ((CS * a.nk + 3) & ~3) : 0;
+    if (own && !a.n_cand) return ZKV_ERR_UNSUPPORTED;  // own mode runs the two-level scored path
     a.sc_in = a.n_cand ? sc_in : nullptr;
     a.sc_ld = sc_ld;
     a.parts = a.n_cand ? parts : 1;
@@ -896,6 +922,9 @@ static int page_decode_impl(const void* q, const zkv_page_layer* layer, int rows
     a.sel_in = nullptr;
     a.sel_lo = a.sel_hi = 0;
     a.out_f32 = out_f32;
+    a.own = own ? 1 : 0;
+    a.own_lo = own_lo;
+    a.own_hi = own ? own_hi : 0;
     void* args[] = {&a};
     return launch_clustered(a.n_cand ? (const void*)page_decode_kernel<true> : (const void*)page_decode_kernel<false>,
                             rows * a.parts * CS, kAttnThreads, CS, page_smem(a), (cudaStream_t)stream, args,
@@ -955,6 +984,19 @@ extern "C" int zkv_page_decode_split(const void* q, const zkv_page_layer* layer,
     return zkv_lse_merge_n(part_out, part_lse, parts, rows * G, kHeadDim, out, lse, stream);
 }
 
+extern "C" int zkv_page_decode_scored(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max,
+                                      const float* scores, int64_t sc_ld, int n_c, int nk, int64_t own_lo,
+                                      int64_t own_hi, int n_sink, int near_start, int n_near, float scale, int parts,
+                                      float* out_f32, float* lse, int64_t* sel_out, int32_t* status, int cluster,
+                                      void* stream) {
+    if (!scores || !out_f32 || !lse || sc_ld < n_c || parts < 1 || parts > kMaxParts || own_lo < 0 ||
+        own_hi < own_lo || nk >= n_c || pick_cluster(cluster, rows) < 2)
+        return ZKV_ERR_ARG;
+    if ((uintptr_t)scores & 3) return ZKV_ERR_ALIGN;
+    return page_decode_impl(q, layer, rows, G, n_max, n_c, nk, n_sink, near_start, n_near, scale, nullptr, lse,
+                            sel_out, status, cluster, scores, sc_ld, parts, out_f32, stream, own_lo, own_hi);
+}
+
 extern "C" int zkv_page_attend(const void* q, const zkv_page_layer* layer, int rows, int G, int n_max,
                                const int64_t* sel, int n_sel, int64_t sel_lo, int64_t sel_hi, int n_sink,
                                int near_start, int n_near, float scale, void* out, float* out_f32, float* lse,
@@ -1001,6 +1043,8 @@ extern "C" int zkv_page_attend(const void* q, const zkv_page_layer* layer, int r
     a.sel_in = sel;
     a.sel_lo = sel_lo;
     a.sel_hi = sel_hi;
+    a.own = 0;
+    a.own_lo = a.own_hi = 0;
     a.out_f32 = out_f32;
     void* args[] = {&a};
     return launch_clustered((const void*)page_decode_kernel<false>, rows * CS, kAttnThreads, CS, page_smem(a),

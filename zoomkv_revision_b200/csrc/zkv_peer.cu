@@ -19,7 +19,7 @@
 // kMaxPolls polls (well under a second of sleeping polls), records
 // ZKV_ERR_TIMEOUT in the status word and returns, so a rank that never
 // arrives ends in a host-side error, not a hung GPU.  No TMA and no
-// multicast are used: the copies are 4-byte thread stores.
+// multicast are used: the copies are 16- or 4-byte thread stores.
 #include <cstring>
 
 #include "zkv_common.cuh"
@@ -57,19 +57,29 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     return v;
 }
 
-// CTA (p, c) copies chunk c of every segment to peer p; the last CTA to
-// finish raises the flags.
+// CTA (p, c) copies slice c of every row of every segment to peer p (16-byte
+// stores where the segment's rows are 16-byte aligned, 4-byte ones
+// otherwise); the last CTA to finish raises the flags.
 __global__ void __launch_bounds__(kPutThreads) peer_put_kernel(const PutArgs a) {
     const int p = blockIdx.x / a.chunks, c = blockIdx.x - p * a.chunks;
     uint32_t* dst = a.dst[p];
     for (int s = 0; s < a.n_seg; ++s) {
         const PutSeg g = a.seg[s];
-        const int64_t total = (int64_t)g.rows * g.row_words;
-        const int64_t per = (total + a.chunks - 1) / a.chunks;
-        const int64_t i0 = (int64_t)c * per, i1 = min(total, i0 + per);
-        for (int64_t i = i0 + threadIdx.x; i < i1; i += kPutThreads) {
-            const int64_t r = i / g.row_words, w = i - r * g.row_words;
-            dst[g.dst_off + r * g.dst_ld + w] = __ldg(g.src + r * g.src_ld + w);
+        const bool vec = ((g.src_ld | g.dst_ld | g.dst_off | g.row_words) & 3) == 0 &&
+                         ((uintptr_t)g.src & 15) == 0;
+        const int unit = vec ? 4 : 1;
+        const int units = g.row_words / unit;
+        const int per = (units + a.chunks - 1) / a.chunks;
+        const int u0 = c * per, u1 = min(units, u0 + per);
+        for (int r = 0; r < g.rows; ++r) {
+            const uint32_t* sr = g.src + (int64_t)r * g.src_ld;
+            uint32_t* dr = dst + g.dst_off + (int64_t)r * g.dst_ld;
+            if (vec) {
+                for (int u = u0 + threadIdx.x; u < u1; u += kPutThreads)
+                    reinterpret_cast<uint4*>(dr)[u] = __ldg(reinterpret_cast<const uint4*>(sr) + u);
+            } else {
+                for (int u = u0 + threadIdx.x; u < u1; u += kPutThreads) dr[u] = __ldg(sr + u);
+            }
         }
     }
     __syncthreads();
@@ -177,7 +187,7 @@ extern "C" int zkv_peer_put(const zkv_peer_seg* segs, int n_seg, void* const* pe
     a.epoch = epoch;
     a.done = done;
     a.world = world;
-    a.chunks = chunks > 0 ? chunks : 4;
+    a.chunks = chunks > 0 ? chunks : (world <= 2 ? 32 : 128 / world);
     peer_put_kernel<<<world * a.chunks, kPutThreads, 0, (cudaStream_t)stream>>>(a);
     return launch_status();
 }

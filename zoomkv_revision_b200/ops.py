@@ -48,7 +48,7 @@ __all__ = [
     "quest_chunk_score", "float_topk", "float_topk_3d", "radix_topk_3d", "partial_chunk_density_scores_cuda",
     "dense_mask_from_topk_cuda", "partial_chunk_kivi_qk_dense_sparse_cuda", "float_topk_gather_concat_3d",
     "lse_merge_cuda", "lse_merge_n", "kivi_encode_chunks", "vquant_encode", "attn_rows", "page_decode",
-    "h2d_gather_kv", "h2d_gather_kv_packed", "h2d_gather_rows",
+    "h2d_gather_kv", "h2d_gather_kv_packed", "h2d_gather_rows", "page_decode_scored",
     "PageLayer", "page_attend", "gqa_mean", "reference_select", "reference_select_ws_bytes", "RqLayout", "rq_encode", "batch_encode", "rq_query", "get_cache_cnt_fused", "collision_topk",
     "partial_rerank_cuda", "coarse_2bit_score_cuda", "rq_popcount_topk", "MAG_CENTERS", "MAG_THRESHOLDS",
 ]
@@ -620,6 +620,30 @@ def page_attend(q, layer: PageLayer, sel, sel_lo: int, sel_hi: int, *, n_sink: i
                                 int(sel_lo), int(sel_hi), int(n_sink), int(near_start), int(n_near), scale, _p(out),
                                 _p(out_f32), _p(lse), _p(status), int(cluster), _stream(q)), "zkv_page_attend")
     return out_f32 if out_f32 is not None else out
+
+
+def page_decode_scored(q, layer: PageLayer, scores, n_c: int, nk: int, own_lo: int, own_hi: int, parts: int,
+                       out_f32, lse, *, n_sink: int = 0, near_start: int = 0, n_near: int = 0, scale=None,
+                       sel_out=None, status=None, cluster=0):
+    """Select + attend step of the sequence split: top nk of the score row
+    scores [bs, H, >= n_c] fp32 (global chunk ids), attention over the
+    selected pages in [own_lo, own_hi) that this layer buffer holds (page
+    id - own_lo) plus the raw rows, over `parts` clusters per row.  Writes
+    out_f32 [parts, bs*H*G, 128] and lse [parts, bs*H*G] partials."""
+    cmin = layer.tensors[0]
+    bs, H, _, D = cmin.shape
+    n_max = cmin.stride(1) // D
+    G = q.shape[2] // H
+    _dtype("scores", scores, torch.float32)
+    if scores.stride(-1) != 1 or scores.stride(0) != H * scores.stride(1):
+        raise ValueError("scores must be [bs, H, n] with unit last stride")
+    qc = q.contiguous()
+    scale = (1.0 / D ** 0.5) if scale is None else float(scale)
+    check(lib().zkv_page_decode_scored(_p(qc), ctypes.byref(layer.struct), bs * H, G, n_max, _p(scores),
+                                       scores.stride(1), int(n_c), int(nk), int(own_lo), int(own_hi), int(n_sink),
+                                       int(near_start), int(n_near), scale, int(parts), _p(out_f32), _p(lse),
+                                       _p(sel_out), _p(status), int(cluster), _stream(q)), "zkv_page_decode_scored")
+    return out_f32
 
 
 def gqa_mean(q, heads: int, out=None):

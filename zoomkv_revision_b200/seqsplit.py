@@ -182,7 +182,8 @@ class PeerGroup:
     68), then
       row    [rows][world*per] fp32  score row; rank r writes columns
                                      [r*per, r*per + n_loc_r), the rest -inf
-      parts  [world][rows*G][128] fp32, lses [world][rows*G] fp32.
+      parts  [world*P][rows*G][128] fp32, lses [world*P][rows*G] fp32:
+             rank r's P per-cluster partials at slots r*P .. r*P + P - 1.
     Rank-local staging (scores, selection, partials, output) is ordinary
     torch memory.  Handles travel once through torch.distributed
     (all_gather_object on `group`)."""
@@ -194,12 +195,16 @@ class PeerGroup:
         self.n_c, self.n_loc = n_c, self.hi - self.lo
         rows = bs * H
         self.rows = rows
+        # clusters per row of the select + attend kernel (as the split form:
+        # about two CTA waves' worth of clusters)
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.P = P = max(1, min(4, (2 * sms) // (rows * 8)))
         L = _lib.lib()
         a256 = lambda x: (x + 255) // 256 * 256
         self.off_row = _HEADER
         self.off_parts = self.off_row + a256(rows * world * self.per * 4)
-        self.off_lses = self.off_parts + a256(world * rows * G * 128 * 4)
-        total = self.off_lses + a256(world * rows * G * 4)
+        self.off_lses = self.off_parts + a256(world * P * rows * G * 128 * 4)
+        total = self.off_lses + a256(world * P * rows * G * 4)
         ptr = ctypes.c_void_p()
         handle = (ctypes.c_char * L.zkv_peer_handle_bytes())()
         _lib.check(L.zkv_peer_alloc(total, ctypes.byref(ptr), handle), "zkv_peer_alloc")
@@ -220,8 +225,8 @@ class PeerGroup:
         self.peer_base = (ctypes.c_void_p * world)(*bases)
         dev = self.device
         self.row = _view(self.base + self.off_row, (bs, H, world * self.per), torch.float32, dev)
-        self.parts = _view(self.base + self.off_parts, (world, rows * G, 128), torch.float32, dev)
-        self.lses = _view(self.base + self.off_lses, (world, rows * G), torch.float32, dev)
+        self.parts = _view(self.base + self.off_parts, (world * P, rows * G, 128), torch.float32, dev)
+        self.lses = _view(self.base + self.off_lses, (world * P, rows * G), torch.float32, dev)
         self.row.fill_(-math.inf)
         self.flags_a = self.base + _FLAGS_A
         self.flags_b = self.base + _FLAGS_B
@@ -230,17 +235,16 @@ class PeerGroup:
         f32 = dict(dtype=torch.float32, device=dev)
         self.local = torch.empty(max(1, rows * self.n_loc), **f32)
         self.sel = torch.empty(bs, H, nk, dtype=torch.int64, device=dev)
-        self.part = torch.empty(bs, H * G, 128, **f32)
-        self.lse = torch.empty(bs, H * G, **f32)
+        self.part = torch.empty(P, rows * G, 128, **f32)
+        self.lse = torch.empty(P, rows * G, **f32)
         self.out = torch.empty(bs, 1, H * G, 128, dtype=torch.bfloat16, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         S = _lib.ZkvPeerSeg
         self._seg_scores = (S * 1)(S(self.local.data_ptr(), self.n_loc * 4, self.off_row + rank * self.per * 4,
                                      world * self.per * 4, self.n_loc * 4, rows if self.n_loc > 0 else 0, 0))
-        pb = rows * G * 128 * 4
+        pb, lb = P * rows * G * 128 * 4, P * rows * G * 4
         self._seg_parts = (S * 2)(S(self.part.data_ptr(), pb, self.off_parts + rank * pb, pb, pb, 1, 0),
-                                  S(self.lse.data_ptr(), rows * G * 4, self.off_lses + rank * rows * G * 4,
-                                    rows * G * 4, rows * G * 4, 1, 0))
+                                  S(self.lse.data_ptr(), lb, self.off_lses + rank * lb, lb, lb, 1, 0))
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier(group=group)  # every mapping is open before the first put
@@ -274,20 +278,21 @@ class PeerGroup:
 def decode_step_p2p(q, layer: ops.PageLayer, pg: PeerGroup, *, n_sink: int = 0, near_start: int = 0,
                     n_near: int = 0):
     """decode_step over peer memory: score own pages -> put scores into every
-    peer's score row -> wait -> top-nk -> attend own selected pages -> put the
-    partial (out, lse) into every peer -> wait -> LSE merge.  Returns the
-    merged output [bs, 1, H*G, 128] bf16 (same on every rank) and the
-    selected global page ids [bs, H, nk]."""
+    peer's score row -> wait -> select + attend the own selected pages in one
+    kernel (zkv_page_decode_scored, P clusters per row) -> put the P partial
+    (out, lse) into every peer -> wait -> LSE merge of all world*P partials.
+    Returns the merged output [bs, 1, H*G, 128] bf16 (same on every rank)
+    and the selected global page ids [bs, H, nk]."""
     stream = torch.cuda.current_stream(q.device).cuda_stream
     if pg.n_loc > 0:
         cmin, cmax, valid = layer.tensors[0], layer.tensors[1], layer.tensors[2]
         ops.quest_chunk_score_gqa(q, cmin, cmax, pg.local, pg.n_loc, valid)
     pg._put(pg._seg_scores, 1, _FLAGS_A, stream)
     pg._wait(pg.flags_a, stream)
-    ops.float_topk_3d(pg.row, pg.nk, out=pg.sel)
     own_raw = pg.rank == 0
-    ops.page_attend(q, layer, pg.sel, pg.lo, pg.hi, n_sink=n_sink if own_raw else 0, near_start=near_start,
-                    n_near=n_near if own_raw else 0, out_f32=pg.part, lse=pg.lse, status=pg.status)
+    ops.page_decode_scored(q, layer, pg.row, pg.world * pg.per, pg.nk, pg.lo, pg.hi, pg.P, pg.part, pg.lse,
+                           n_sink=n_sink if own_raw else 0, near_start=near_start, n_near=n_near if own_raw else 0,
+                           sel_out=pg.sel, status=pg.status)
     pg._put(pg._seg_parts, 2, _FLAGS_B, stream)
     pg._wait(pg.flags_b, stream)
     ops.lse_merge_n(pg.parts, pg.lses, pg.out.view(-1, 128))
