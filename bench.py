@@ -23,7 +23,8 @@ Two further workloads print their own line (not the headline):
                candidates -> popcount estimate -> top 1024 -> exact bf16 IP
   --config 3   Qwen3-4B shape, batch 1, 131072 context, budget 4096: the fused
                page decode on 1 GPU; under torchrun the sequence split across
-               ranks with NCCL score / partial all-gathers (strong scaling)
+               ranks, scores and partials exchanged through NVLink peer
+               memory (strong scaling)
   --config 5   the offload tier: config-1 layer shape with the retrieval zone
                in host-pinned memory, selected rows gathered over the host
                link, then attention
@@ -485,8 +486,8 @@ def run_config3(args):
     bytes_step = layers * W.page_algorithmic_bytes(bs * H, n_c, nk, n_near, G)
     if world == 1:
         launches = layers * args.steps * ops.page_decode_plan(bs * H, n_c, nk, device=dev)["launches"]
-    else:  # per layer: scores, put, wait, top-k, attend, put, wait, LSE merge
-        launches = layers * args.steps * 8
+    else:  # per layer: scores, exchange, select + attend, exchange, LSE merge
+        launches = layers * args.steps * 5
         if int(pg.status.item()) != 0:
             raise RuntimeError(f"peer wait expired (status {int(pg.status.item())})")
     peak, kind = load_peaks()

@@ -502,6 +502,15 @@ int zkv_peer_put(const zkv_peer_seg* segs, int n_seg, void* const* peer_base,
                  int64_t flag_off, int rank, int world, uint32_t* epoch,
                  uint32_t* done, int chunks, void* stream);
 
+/* zkv_peer_put followed by the wait of the same phase in one launch: the
+ * CTA that raises the flags then polls this rank's flag array (at flag_off
+ * in peer_base[rank]) until all ranks reach *epoch + 1 and advances *epoch;
+ * bounded like zkv_peer_wait (ZKV_ERR_TIMEOUT in `status`).               */
+int zkv_peer_exchange(const zkv_peer_seg* segs, int n_seg,
+                      void* const* peer_base, int64_t flag_off, int rank,
+                      int world, uint32_t* epoch, uint32_t* done, int chunks,
+                      int32_t* status, void* stream);
+
 /* Wait until flags[0..world) (this rank's flag array) all reach *epoch + 1
  * (acquire, system scope), then advance *epoch.  The wait is bounded: on
  * expiry ZKV_ERR_TIMEOUT is written to `status` and the kernel returns.    */

@@ -13,6 +13,9 @@
 //   zkv_peer_wait  one warp polls (acquire, system scope) until the flags of
 //                  all ranks reach epoch + 1, then advances the local epoch.
 //
+// zkv_peer_exchange is the two in one launch: the CTA that raises the flags
+// then waits for every rank's flags and advances the epoch.
+//
 // The epoch lives in device memory and only the wait advances it, so a
 // captured CUDA graph replays correctly.  Every rank runs the same sequence
 // of puts and waits, so epochs agree across ranks.  A wait gives up after
@@ -44,6 +47,9 @@ struct PutArgs {
     uint32_t* flag[kMaxPeers];   // this rank's flag word inside every peer's buffer
     const uint32_t* epoch;       // local
     uint32_t* done;              // local counter of finished CTAs (0 between launches)
+    const uint32_t* wait_flags;  // exchange form: this rank's flag array of the phase (NULL: put only)
+    uint32_t* epoch_rw;          // exchange form: the epoch the last CTA advances
+    int32_t* status;
     int world;
     int chunks;                  // CTAs per peer
 };
@@ -91,6 +97,21 @@ __global__ void __launch_bounds__(kPutThreads) peer_put_kernel(const PutArgs a) 
             const uint32_t target = *a.epoch + 1u;
             for (int q = 0; q < a.world; ++q) st_release_sys(a.flag[q], target);
             *a.done = 0u;
+            if (a.wait_flags) {  // exchange form: this CTA also waits for every rank's put
+                bool ok = true;
+                for (int q = 0; q < a.world && ok; ++q) {
+                    uint32_t polls = 0;
+                    while ((int32_t)(ld_acquire_sys(a.wait_flags + q) - target) < 0) {
+                        if (++polls > kMaxPolls) {
+                            ok = false;
+                            break;
+                        }
+                        __nanosleep(128);
+                    }
+                }
+                if (!ok) set_status(a.status, ZKV_ERR_TIMEOUT);
+                *a.epoch_rw = target;
+            }
         }
     }
 }
@@ -163,8 +184,9 @@ extern "C" int zkv_peer_free(void* ptr) {
     return cudaFree(ptr) == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH;
 }
 
-extern "C" int zkv_peer_put(const zkv_peer_seg* segs, int n_seg, void* const* peer_base, int64_t flag_off,
-                            int rank, int world, uint32_t* epoch, uint32_t* done, int chunks, void* stream) {
+static int peer_put_launch(const zkv_peer_seg* segs, int n_seg, void* const* peer_base, int64_t flag_off, int rank,
+                           int world, uint32_t* epoch, uint32_t* done, int chunks, bool exchange, int32_t* status,
+                           void* stream) {
     if (!segs || n_seg < 1 || n_seg > kMaxSegs || !peer_base || world < 1 || world > kMaxPeers || rank < 0 ||
         rank >= world || !epoch || !done || flag_off < 0 || (flag_off & 3) || chunks < 0)
         return ZKV_ERR_ARG;
@@ -186,10 +208,25 @@ extern "C" int zkv_peer_put(const zkv_peer_seg* segs, int n_seg, void* const* pe
     }
     a.epoch = epoch;
     a.done = done;
+    a.wait_flags = exchange ? reinterpret_cast<const uint32_t*>(static_cast<char*>(peer_base[rank]) + flag_off)
+                            : nullptr;
+    a.epoch_rw = exchange ? epoch : nullptr;
+    a.status = status;
     a.world = world;
     a.chunks = chunks > 0 ? chunks : (world <= 2 ? 32 : 128 / world);
     peer_put_kernel<<<world * a.chunks, kPutThreads, 0, (cudaStream_t)stream>>>(a);
     return launch_status();
+}
+
+extern "C" int zkv_peer_put(const zkv_peer_seg* segs, int n_seg, void* const* peer_base, int64_t flag_off,
+                            int rank, int world, uint32_t* epoch, uint32_t* done, int chunks, void* stream) {
+    return peer_put_launch(segs, n_seg, peer_base, flag_off, rank, world, epoch, done, chunks, false, nullptr, stream);
+}
+
+extern "C" int zkv_peer_exchange(const zkv_peer_seg* segs, int n_seg, void* const* peer_base, int64_t flag_off,
+                                 int rank, int world, uint32_t* epoch, uint32_t* done, int chunks, int32_t* status,
+                                 void* stream) {
+    return peer_put_launch(segs, n_seg, peer_base, flag_off, rank, world, epoch, done, chunks, true, status, stream);
 }
 
 extern "C" int zkv_peer_wait(const uint32_t* flags, uint32_t* epoch, int world, int32_t* status, void* stream) {

@@ -17,10 +17,11 @@ Two transports carry the exchanges of steps 2 and 5:
 
   * `decode_step_p2p` (the product on NVLink): every rank writes its slice
     straight into every peer's buffer with stores over NVLink and raises a
-    flag there (zkv_peer_put); the consumer waits on its flags with a
-    bounded poll (zkv_peer_wait).  The buffers are shared once through CUDA
-    IPC (`PeerGroup`); a layer is 8 launches, none of them a collective, and
-    the step can be captured in a CUDA graph (the epochs live on the device);
+    flag there, and the same launch then waits on its own flags with a
+    bounded poll (zkv_peer_exchange).  The buffers are shared once through
+    CUDA IPC (`PeerGroup`).  A layer is 5 launches -- scores, exchange,
+    select + attend, exchange, merge -- none of them a collective, and the
+    step can be captured in a CUDA graph (the epochs live on the device);
   * `decode_step` with NCCL all-gathers (any backend torch.distributed
     offers; also the CPU/gloo form the host-logic tests run).
 
@@ -254,6 +255,11 @@ class PeerGroup:
         _lib.check(_lib.lib().zkv_peer_put(segs, n_seg, self.peer_base, flag_off, self.rank, self.world,
                                            self.epoch, self.done, 0, stream), "zkv_peer_put")
 
+    def _exchange(self, segs, n_seg, flag_off, stream):
+        _lib.check(_lib.lib().zkv_peer_exchange(segs, n_seg, self.peer_base, flag_off, self.rank, self.world,
+                                                self.epoch, self.done, 0, self.status.data_ptr(), stream),
+                   "zkv_peer_exchange")
+
     def _wait(self, flags, stream):
         _lib.check(_lib.lib().zkv_peer_wait(flags, self.epoch, self.world, self.status.data_ptr(), stream),
                    "zkv_peer_wait")
@@ -287,13 +293,11 @@ def decode_step_p2p(q, layer: ops.PageLayer, pg: PeerGroup, *, n_sink: int = 0, 
     if pg.n_loc > 0:
         cmin, cmax, valid = layer.tensors[0], layer.tensors[1], layer.tensors[2]
         ops.quest_chunk_score_gqa(q, cmin, cmax, pg.local, pg.n_loc, valid)
-    pg._put(pg._seg_scores, 1, _FLAGS_A, stream)
-    pg._wait(pg.flags_a, stream)
+    pg._exchange(pg._seg_scores, 1, _FLAGS_A, stream)
     own_raw = pg.rank == 0
     ops.page_decode_scored(q, layer, pg.row, pg.world * pg.per, pg.nk, pg.lo, pg.hi, pg.P, pg.part, pg.lse,
                            n_sink=n_sink if own_raw else 0, near_start=near_start, n_near=n_near if own_raw else 0,
                            sel_out=pg.sel, status=pg.status)
-    pg._put(pg._seg_parts, 2, _FLAGS_B, stream)
-    pg._wait(pg.flags_b, stream)
+    pg._exchange(pg._seg_parts, 2, _FLAGS_B, stream)
     ops.lse_merge_n(pg.parts, pg.lses, pg.out.view(-1, 128))
     return pg.out, pg.sel
