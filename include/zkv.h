@@ -497,7 +497,7 @@ typedef struct zkv_peer_seg {
  * byte offset flag_off of every peer buffer to *epoch + 1 (release, system
  * scope) once all stores are done.  `epoch`, `done`: device words of this
  * rank (done = 0 initially; the kernel returns it to 0).  chunks: CTAs per
- * peer (0 = automatic: 32 up to 2 ranks, 128 / world beyond).             */
+ * peer (0 = automatic: 8 up to 2 ranks, 2 beyond).                        */
 int zkv_peer_put(const zkv_peer_seg* segs, int n_seg, void* const* peer_base,
                  int64_t flag_off, int rank, int world, uint32_t* epoch,
                  uint32_t* done, int chunks, void* stream);

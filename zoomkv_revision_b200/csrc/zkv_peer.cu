@@ -63,8 +63,33 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     return v;
 }
 
+// Copy `items` (row, unit) pairs of one segment: item i is unit u0 + i % cnt
+// of row i / cnt; every thread issues U loads before its stores.
+template <typename T>
+__device__ __forceinline__ void put_items(const T* __restrict__ src, T* __restrict__ dst, int64_t src_ld,
+                                          int64_t dst_ld, int u0, int cnt, int items) {
+    constexpr int U = 4;
+    for (int base = threadIdx.x; base < items; base += kPutThreads * U) {
+        T v[U];
+        int64_t d[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int i = base + k * kPutThreads;
+            d[k] = -1;
+            if (i < items) {
+                const int r = i / cnt, u = u0 + i - r * cnt;
+                v[k] = __ldg(src + r * src_ld + u);
+                d[k] = r * dst_ld + u;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k)
+            if (d[k] >= 0) dst[d[k]] = v[k];
+    }
+}
+
 // CTA (p, c) copies slice c of every row of every segment to peer p (16-byte
-// stores where the segment's rows are 16-byte aligned, 4-byte ones
+// units where the segment's rows are 16-byte aligned, 4-byte ones
 // otherwise); the last CTA to finish raises the flags.
 __global__ void __launch_bounds__(kPutThreads) peer_put_kernel(const PutArgs a) {
     const int p = blockIdx.x / a.chunks, c = blockIdx.x - p * a.chunks;
@@ -76,17 +101,13 @@ __global__ void __launch_bounds__(kPutThreads) peer_put_kernel(const PutArgs a) 
         const int unit = vec ? 4 : 1;
         const int units = g.row_words / unit;
         const int per = (units + a.chunks - 1) / a.chunks;
-        const int u0 = c * per, u1 = min(units, u0 + per);
-        for (int r = 0; r < g.rows; ++r) {
-            const uint32_t* sr = g.src + (int64_t)r * g.src_ld;
-            uint32_t* dr = dst + g.dst_off + (int64_t)r * g.dst_ld;
-            if (vec) {
-                for (int u = u0 + threadIdx.x; u < u1; u += kPutThreads)
-                    reinterpret_cast<uint4*>(dr)[u] = __ldg(reinterpret_cast<const uint4*>(sr) + u);
-            } else {
-                for (int u = u0 + threadIdx.x; u < u1; u += kPutThreads) dr[u] = __ldg(sr + u);
-            }
-        }
+        const int u0 = min(units, c * per), cnt = min(units, u0 + per) - u0;
+        if (cnt <= 0) continue;
+        if (vec)
+            put_items(reinterpret_cast<const uint4*>(g.src), reinterpret_cast<uint4*>(dst + g.dst_off),
+                      g.src_ld / 4, g.dst_ld / 4, u0, cnt, g.rows * cnt);
+        else
+            put_items(g.src, dst + g.dst_off, g.src_ld, g.dst_ld, u0, cnt, g.rows * cnt);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -213,7 +234,7 @@ static int peer_put_launch(const zkv_peer_seg* segs, int n_seg, void* const* pee
     a.epoch_rw = exchange ? epoch : nullptr;
     a.status = status;
     a.world = world;
-    a.chunks = chunks > 0 ? chunks : (world <= 2 ? 32 : 128 / world);
+    a.chunks = chunks > 0 ? chunks : (world <= 2 ? 8 : 2);
     peer_put_kernel<<<world * a.chunks, kPutThreads, 0, (cudaStream_t)stream>>>(a);
     return launch_status();
 }
