@@ -136,3 +136,29 @@ def test_seqsplit_world2_matches_single_device(tmp_path, case):
     ref = O.bf16_to_f32(ro)
     err = np.abs(out - ref)
     assert err.max() <= 2e-2 and err.mean() / np.abs(ref).mean() <= 1e-2, (err.max(), err.mean())
+
+
+@pytest.mark.parametrize("world,rows,n_c", [(1, 8, 8184), (2, 8, 8184), (3, 2, 1001), (8, 8, 8184), (8, 64, 2040)])
+def test_peer_buffer_layout(world, rows, n_c):
+    """The shared buffer of the peer-memory transport: the flag arrays, the
+    epoch and the CTA counter fit the header; regions are 256-byte aligned and
+    disjoint; every rank's score slice and partial slots land inside their
+    region and do not overlap another rank's."""
+    from zoomkv_revision_b200 import seqsplit as S
+    G, P = 4, 4
+    per = S.split_range(n_c, world, 0)[2]
+    lay = S.peer_layout(rows, G, per, world, P)
+    assert S._FLAGS_A + 4 * 8 <= S._FLAGS_B and S._FLAGS_B + 4 * 8 <= S._EPOCH and S._DONE + 4 <= S._HEADER
+    assert all(lay[k] % 256 == 0 for k in ("row", "parts", "lses", "total"))
+    assert lay["row"] + rows * world * per * 4 <= lay["parts"]
+    assert lay["parts"] + world * P * rows * G * 128 * 4 <= lay["lses"]
+    assert lay["lses"] + world * P * rows * G * 4 <= lay["total"]
+    covered = set()
+    for r in range(world):
+        lo, hi, _ = S.split_range(n_c, world, r)
+        assert 0 <= hi - lo <= per
+        # score slice of rank r: columns [r*per, r*per + n_loc) of every row
+        cols = set(range(r * per, r * per + (hi - lo)))
+        assert not (cols & covered)
+        covered |= cols
+    assert covered == set(range(n_c))  # every chunk has exactly one owner; columns past n_c stay -inf

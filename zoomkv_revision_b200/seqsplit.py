@@ -174,6 +174,17 @@ def _view(ptr: int, shape, dtype, device):
 _FLAGS_A, _FLAGS_B, _EPOCH, _DONE, _HEADER = 0, 32, 64, 68, 256
 
 
+def peer_layout(rows: int, G: int, per: int, world: int, P: int) -> dict:
+    """Byte offsets of the shared buffer (the same on every rank): header,
+    score row [rows][world*per] fp32, partial outputs [world*P][rows*G][128]
+    fp32, partial lse [world*P][rows*G] fp32; every region 256-byte aligned."""
+    a256 = lambda x: (x + 255) // 256 * 256
+    off_row = _HEADER
+    off_parts = off_row + a256(rows * world * per * 4)
+    off_lses = off_parts + a256(world * P * rows * G * 128 * 4)
+    return {"row": off_row, "parts": off_parts, "lses": off_lses, "total": off_lses + a256(world * P * rows * G * 4)}
+
+
 class PeerGroup:
     """One IPC-shared buffer per rank for the split decode's exchanges.
 
@@ -201,11 +212,8 @@ class PeerGroup:
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.P = P = max(1, min(4, (2 * sms) // (rows * 8)))
         L = _lib.lib()
-        a256 = lambda x: (x + 255) // 256 * 256
-        self.off_row = _HEADER
-        self.off_parts = self.off_row + a256(rows * world * self.per * 4)
-        self.off_lses = self.off_parts + a256(world * P * rows * G * 128 * 4)
-        total = self.off_lses + a256(world * P * rows * G * 4)
+        lay = peer_layout(rows, G, self.per, world, P)
+        self.off_row, self.off_parts, self.off_lses, total = lay["row"], lay["parts"], lay["lses"], lay["total"]
         ptr = ctypes.c_void_p()
         handle = (ctypes.c_char * L.zkv_peer_handle_bytes())()
         _lib.check(L.zkv_peer_alloc(total, ctypes.byref(ptr), handle), "zkv_peer_alloc")
