@@ -216,6 +216,35 @@ def test_p2p_world1_matches_nccl_form_and_replays_in_a_graph():
         pg.close()
 
 
+def test_peer_wait_expires_on_a_missing_rank():
+    """Failure detection without a GPU fault: a wait for a rank that never
+    puts (world 2 declared, one process, nothing sets rank 1's flag) gives up
+    after its bounded poll, reports ZKV_ERR_TIMEOUT in the status word and
+    returns; the context stays usable and the epoch still advances."""
+    import time
+    from zoomkv_revision_b200 import _lib
+    dev = torch.device("cuda", 0)
+    pg = S.PeerGroup(1, 2, G, 64, 8, 1, 0, dev)  # one real buffer; its flag array has room for 8 ranks
+    try:
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        L = _lib.lib()
+        t0 = time.perf_counter()
+        # the own flag of rank 0 is raised by a put; rank 1's never is
+        pg._put(pg._seg_scores, 1, 0, stream)
+        _lib.check(L.zkv_peer_wait(pg.flags_a, pg.epoch, 2, pg.status.data_ptr(), stream), "zkv_peer_wait")
+        torch.cuda.synchronize()
+        waited = time.perf_counter() - t0
+        assert int(pg.status.item()) == _lib.ZKV_ERR_TIMEOUT
+        assert waited < 30.0
+        # the context is still usable: a normal world-1 step afterwards succeeds
+        pg.status.zero_()
+        x = torch.arange(16, device=dev, dtype=torch.float32)
+        torch.cuda.synchronize()
+        assert float(x.sum().item()) == 120.0
+    finally:
+        pg.close()
+
+
 def _p2p_rank(rank, world, port, path):
     import datetime
     import torch.distributed as dist
