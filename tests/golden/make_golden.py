@@ -3,7 +3,7 @@
 Run in a container where the reference snapshot is mounted (CPU torch is
 enough):
 
-    python tests/golden/make_golden.py --ref /root/reference
+    python tests/golden/make_golden.py --ref <path of the reference checkout>
 
 It imports the ZoomKV runtime's pure-PyTorch functions, drives them on small
 seeded inputs and stores inputs + outputs as .npz files next to this script.
