@@ -92,3 +92,38 @@ def test_skipped_overflow_raises(monkeypatch):
     cfg = dict(cfg, max_skipped=4)
     with pytest.raises(RuntimeError):
         P.quest_chunk_plan(16 * 3 + 9, cfg)
+
+
+@pytest.mark.parametrize("sink,local,interval,prefill,steps", [
+    (4, 32, 24, 107, 300),      # the reference trace's shape, long
+    (4, 128, 512, 4000, 2000),  # production-like local / interval
+    (0, 64, 64, 500, 600),      # no sink
+    (16, 256, 256, 100, 900),   # prompt shorter than sink + local
+    (4, 40, 24, 77, 500),       # odd sizes: ragged chunk tails at every flush
+])
+def test_offload_window_invariants(monkeypatch, sink, local, interval, prefill, steps):
+    """The offload tier's HBM window, replayed through the real schedule:
+    the window base (first unencoded token) is where every flush's encode
+    range starts, the local window never starts before it, every appended
+    token fits the near part, and the gathered selection fits the staging
+    rows (the arithmetic polar_cache uses with ZKV_HOST_RETRIEVAL=1)."""
+    cfg = zoomkv_cfg(None, monkeypatch)
+    F = 100
+    cap = prefill + steps
+    stage, near_cap = P.offload_window(sink, local, interval, F, cfg["max_skipped"], 2000, cap)
+    s = P.CacheSchedule(1, sink, local, interval, prefill, cfg, offload=True)
+    _, r_len, (lo, hi) = s.prefill(0, prefill, 0)
+    base = sink + hi
+    assert lo == 0 and prefill - base <= near_cap or prefill <= sink
+    for _ in range(steps):
+        if s.flush_due(0):
+            lo, hi, _ = s.flush()
+            assert sink + lo == base           # the completed chunks start at the window base
+            base = sink + hi
+        pos = s.append(0)
+        if pos >= sink:
+            assert 0 <= pos - base < near_cap  # the appended token has a window row
+        r_len, local_start, _ = s.region(0)
+        assert local_start >= base or r_len == 0
+        n_chunks, nk, _, skipped = s.plan
+        assert min(F, nk * 16) + skipped <= stage

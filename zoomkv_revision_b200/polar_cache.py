@@ -255,6 +255,18 @@ class CacheSchedule:
         return region(self.current_seq_len[layer], cpu_len, self.input_length, self.sink, self.local, self.interval)
 
 
+def offload_window(sink: int, local: int, interval: int, final_topk: int, max_skipped: int, threshold: int,
+                   cap: int):
+    """(stage, near_cap) of the offload tier's HBM window [sink | stage |
+    near]: stage rows hold the gathered selection (final_topk + skipped) or,
+    below the retrieval threshold, every host row; the near part holds every
+    token from the first unencoded chunk on -- at most local + interval
+    tokens of near zone plus a chunk's skipped tail plus the appended token."""
+    min_total = max(threshold, sink + local + final_topk * 2)
+    stage = min(cap, max(final_topk + max_skipped, min_total))
+    return stage, local + interval + 2 * CHUNK
+
+
 # --------------------------------------------------------------------------- the cache
 class polar_cache:
     """ZoomKV sparse decode-attention cache (see module docstring)."""
@@ -329,9 +341,8 @@ class polar_cache:
         self.win_k, self.win_v, self.win_base = [], [], [sink_size] * layer_num
         # offload-tier window: staging rows for the gathered selection (or,
         # below the retrieval threshold, every host row) + the near rows
-        min_total = max(full_attention_threshold, sink_size + local_size + final_topk * 2)
-        self._stage = min(self.cap, max(final_topk + self.MAX_SKIPPED_INDICES, min_total))
-        self._near_cap = local_size + self.dynamic_update_interval + 2 * CHUNK
+        self._stage, self._near_cap = offload_window(sink_size, local_size, self.dynamic_update_interval, final_topk,
+                                                     self.MAX_SKIPPED_INDICES, full_attention_threshold, self.cap)
         self.chunk_min, self.chunk_max, self.chunk_centroid, self.chunk_valid, self.kivi_packed = [], [], [], [], []
         self.vcodes_t, self.vmeta, self.kscale = [], [], []
         for l in range(layer_num):
