@@ -136,3 +136,49 @@ def test_srht_signs_follow_reference_recipe_and_keep_rng_state():
     torch.manual_seed(42)
     ref = torch.randint(0, 2, (128,), device=DEV, dtype=torch.bfloat16) * 2 - 1
     assert torch.equal(s, ref)
+
+
+@pytest.mark.parametrize("threshold", [0, 10 ** 6])
+def test_pariskv_host_tier_equals_hbm_cache(monkeypatch, threshold):
+    """The offload tier of the ParisKV drop-in (ZKV_HOST_RETRIEVAL=1: raw
+    retrieval rows in host-pinned memory, the final rows gathered over the
+    host link) returns the same output, selects the same rows and writes the
+    same codes as the HBM-resident cache, step for step across flushes --
+    through the retrieval branch (threshold 0) and the full-attention branch
+    (threshold above every length)."""
+    g = np.load(os.path.join(GOLDEN, "pariskv_schedule.npz"))
+    L, bs, H, sink, local, interval, prefill, steps, max_new = (int(x) for x in g["params"])
+    caches = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("ZKV_HOST_RETRIEVAL", mode)
+        caches[mode] = _make(g, threshold=threshold)
+    hb, ho = caches["0"], caches["1"]
+    assert ho.host_tier and not hb.host_tier and ho.keys[0].is_pinned()
+    keys = from_u16(g["keys"]).to(DEV)
+    vals = from_u16(g["values"]).to(DEV)
+    for c in (hb, ho):
+        for l in range(L):
+            c.prefill_update_kv_cache(None, keys[l, :, :, :prefill].transpose(1, 2).contiguous(),
+                                      vals[:, :, :prefill].transpose(1, 2).contiguous(), l, 0)
+    gen = torch.Generator(device=DEV).manual_seed(5)
+    for t in range(steps):
+        pos = prefill + t
+        for l in range(L):
+            for c in (hb, ho):
+                c.decode_update_kv_cache(keys[l, :, :, pos:pos + 1].transpose(1, 2).contiguous(),
+                                         vals[:, :, pos:pos + 1].transpose(1, 2).contiguous(), l)
+            if t % 9 == 0:
+                q = torch.randn(bs, 1, 4 * H, 128, generator=gen, device=DEV).to(torch.bfloat16)
+                a, b = hb.compute(q, l), ho.compute(q, l)
+                torch.cuda.synchronize()
+                assert torch.equal(a, b), (t, l)
+                if threshold == 0 and hb._last_topk_indices is not None:
+                    assert torch.equal(hb._last_topk_indices, ho._last_topk_indices)
+    for s in (hb._status.values(), ho._status.values()):
+        assert all(int(x.item()) == 0 for x in s)
+    n = ho._actual_retrieval_length
+    for l in range(L):
+        assert torch.equal(ho.keys[l][:, :, sink:sink + n], keys[l, :, :, sink:sink + n].cpu())
+        assert torch.equal(ho.values[l][:, :, sink:sink + n], vals[:, :, sink:sink + n].cpu())
+        for name in ("codes", "packed", "weight", "hist"):
+            assert torch.equal(getattr(hb.layouts[l], name), getattr(ho.layouts[l], name)), name

@@ -23,8 +23,11 @@ relative to runtime/zoomkv_urania_runtime_20261011/):
     local tokens, with the adaptive ratios of `_get_adaptive_ratios`
     (REF:1457-1525) and its POLAR_* overrides.
 
-B200 layout: one absolute-position K/V buffer per layer in HBM (no host
-offload; `cpu_valid_end` keeps its bookkeeping meaning) and the retrieval
+B200 layout: one absolute-position K/V buffer per layer in HBM by default
+(`cpu_valid_end` keeps its bookkeeping meaning); with ZKV_HOST_RETRIEVAL=1
+the raw retrieval rows live in host-pinned memory, as the reference keeps
+them, and the final rows are gathered over the host link (zkv_h2d_gather_kv)
+into an HBM window before attention.  The retrieval
 codes token-major ([rows, cap, 16]) so the candidate gather reads 64 + 32
 contiguous bytes per key.  Selections break ties by the lower index; the
 reference's torch.topk / radix top-k leave ties unspecified.
@@ -154,11 +157,31 @@ class polar_cache:
         self.device = devs[0]
         self.quantizer = types.SimpleNamespace(srht_diagonal_signs=[srht_signs(self.device)], B=16, m=8)
         bs, H, D, cap = batch_size, num_key_value_heads, head_dim, max_length
+        # offload tier (env ZKV_HOST_RETRIEVAL=1, with enable_offload): the raw
+        # retrieval rows live in host-pinned memory (`keys` / `values`,
+        # absolute positions); HBM keeps the codes and one window per layer
+        # [sink | staging | near], the near part from the end of the
+        # retrieval zone on (encoding is per token, so that is also the local
+        # start).  compute() gathers the final rows into the staging rows.
+        self.host_tier = os.environ.get("ZKV_HOST_RETRIEVAL", "0") in ("1", "true", "True", "yes", "on")
+        if self.host_tier and not enable_offload:
+            raise ValueError("ZKV_HOST_RETRIEVAL=1 needs enable_offload=True (the offload zone bookkeeping)")
+        min_total = max(full_attention_threshold, sink_size + local_size + final_topk * 2)
+        self._stage = min(cap, max(final_topk, min_total))
+        self._near_cap = local_size + self.dynamic_update_interval + 8
+        self.win_k, self.win_v, self.win_base = [], [], [sink_size] * layer_num
         self.keys, self.values, self.layouts = [], [], []
         for l in range(layer_num):
             d = devs[l]
-            self.keys.append(torch.zeros(bs, H, cap, D, dtype=torch.bfloat16, device=d))
-            self.values.append(torch.zeros(bs, H, cap, D, dtype=torch.bfloat16, device=d))
+            if self.host_tier:
+                self.keys.append(torch.zeros(bs, H, cap, D, dtype=torch.bfloat16, pin_memory=True))
+                self.values.append(torch.zeros(bs, H, cap, D, dtype=torch.bfloat16, pin_memory=True))
+                W = sink_size + self._stage + self._near_cap
+                self.win_k.append(torch.zeros(bs, H, W, D, dtype=torch.bfloat16, device=d))
+                self.win_v.append(torch.zeros(bs, H, W, D, dtype=torch.bfloat16, device=d))
+            else:
+                self.keys.append(torch.zeros(bs, H, cap, D, dtype=torch.bfloat16, device=d))
+                self.values.append(torch.zeros(bs, H, cap, D, dtype=torch.bfloat16, device=d))
             self.layouts.append(ops.RqLayout.alloc(bs * H, cap, d))
         self._centers = {d: torch.tensor(ops.MAG_CENTERS, dtype=torch.bfloat16, device=d) for d in set(devs)}
         self._status = {d: torch.zeros(1, dtype=torch.int32, device=d) for d in set(devs)}
@@ -169,13 +192,25 @@ class polar_cache:
         s = self.quantizer.srht_diagonal_signs[0]
         return s if s.device == dev else s.to(dev)
 
-    def _encode(self, l: int, tok_lo: int, tok_hi: int) -> None:
+    def _encode(self, l: int, tok_lo: int, tok_hi: int, src=None) -> None:
         """Retrieval codes of tokens [tok_lo, tok_hi) (absolute) of layer l,
-        added to the bucket histogram (batch_encode + _count_cluster_keys)."""
+        added to the bucket histogram (batch_encode + _count_cluster_keys).
+        src: the keys of exactly those tokens when they are not read from the
+        HBM cache (offload tier)."""
         if tok_hi <= tok_lo:
             return
-        k = self.keys[l][:, :, tok_lo:tok_hi]   # [bs, H, n, 128] view of the absolute buffer
+        k = self.keys[l][:, :, tok_lo:tok_hi] if src is None else src   # [bs, H, n, 128]
         ops.rq_encode(k, self._signs(k.device), self.layouts[l], tok_start=tok_lo)
+
+    def _win_slot(self, l: int, pos: int) -> int:
+        """Window row of absolute position pos (offload tier)."""
+        s = self.sink_size
+        if pos < s:
+            return pos
+        j = pos - self.win_base[l]
+        if j < 0 or j >= self._near_cap:
+            raise RuntimeError(f"position {pos} is outside the near window of layer {l}")
+        return s + self._stage + j
 
     def get_region_indices(self, layer_idx, device=None):
         """REF:837-853: zones from the committed retrieval boundary."""
@@ -207,16 +242,35 @@ class polar_cache:
         l = layer_idx
         seq_len = key_states.shape[1]
         n = seq_len - vs
-        self.keys[l][:, :, :n].copy_(key_states[:, vs:].transpose(1, 2))
-        self.values[l][:, :, :n].copy_(value_states[:, vs:].transpose(1, 2))
+        kk, vv = key_states[:, vs:].transpose(1, 2), value_states[:, vs:].transpose(1, 2)
         retrieval_start = self.sink_size
         retrieval_end = max(retrieval_start, n - self.local_size)
         retrieval = retrieval_end - retrieval_start
+        if self.host_tier:
+            s = self.sink_size
+            ns = min(s, n)
+            self.win_k[l][:, :, :ns].copy_(kk[:, :, :ns])
+            self.win_v[l][:, :, :ns].copy_(vv[:, :, :ns])
+            if retrieval > 0:
+                self.keys[l][:, :, s:retrieval_end].copy_(kk[:, :, s:retrieval_end])
+                self.values[l][:, :, s:retrieval_end].copy_(vv[:, :, s:retrieval_end])
+            base = max(s, retrieval_end)
+            m = max(0, n - base)
+            if m > self._near_cap:
+                raise RuntimeError(f"prefill leaves {m} near tokens; the window holds {self._near_cap}")
+            off = s + self._stage
+            self.win_k[l][:, :, off:off + m].copy_(kk[:, :, base:base + m])
+            self.win_v[l][:, :, off:off + m].copy_(vv[:, :, base:base + m])
+            self.win_base[l] = base
+        else:
+            self.keys[l][:, :, :n].copy_(kk)
+            self.values[l][:, :, :n].copy_(vv)
         if self._actual_retrieval_length is None:
             self._actual_retrieval_length = retrieval
         self.current_seq_len[l] = n
         if retrieval > 0:
-            self._encode(l, retrieval_start, retrieval_end)
+            self._encode(l, retrieval_start, retrieval_end,
+                         src=kk[:, :, retrieval_start:retrieval_end].contiguous() if self.host_tier else None)
             self.cpu_valid_end[l] = retrieval
         if l == self.layer_num - 1:
             self.context += n
@@ -234,7 +288,21 @@ class polar_cache:
         assert num > 0, f"flush of {num} tokens"
         self._actual_retrieval_length = new_end - self.sink_size
         for l in range(self.layer_num):
-            self._encode(l, old_end, new_end)
+            if self.host_tier:
+                # the window starts at old_end: encode from it, move the rows to
+                # the host zone, slide the window to new_end
+                off, total = self.sink_size + self._stage, self.current_seq_len[l]
+                wk, wv = self.win_k[l], self.win_v[l]
+                self._encode(l, old_end, new_end, src=wk[:, :, off:off + num])
+                self.keys[l][:, :, old_end:new_end].copy_(wk[:, :, off:off + num])
+                self.values[l][:, :, old_end:new_end].copy_(wv[:, :, off:off + num])
+                m = total - new_end
+                if m > 0:
+                    wk[:, :, off:off + m].copy_(wk[:, :, off + num:off + num + m].clone())
+                    wv[:, :, off:off + m].copy_(wv[:, :, off + num:off + num + m].clone())
+                self.win_base[l] = new_end
+            else:
+                self._encode(l, old_end, new_end)
             self.cpu_valid_end[l] += num
         self.steady_size = self.sink_size + self.local_size
 
@@ -248,8 +316,13 @@ class polar_cache:
                 self._update_polar_index()
         if current >= self.max_length:
             raise RuntimeError(f"cache full ({self.max_length} tokens)")
-        self.keys[layer_idx][:, :, current].copy_(key_states[:, 0])
-        self.values[layer_idx][:, :, current].copy_(value_states[:, 0])
+        if self.host_tier:
+            w = self._win_slot(layer_idx, current)
+            self.win_k[layer_idx][:, :, w].copy_(key_states[:, 0])
+            self.win_v[layer_idx][:, :, w].copy_(value_states[:, 0])
+        else:
+            self.keys[layer_idx][:, :, current].copy_(key_states[:, 0])
+            self.values[layer_idx][:, :, current].copy_(value_states[:, 0])
         self.current_seq_len[layer_idx] = current + 1
         if layer_idx == 0:
             self._decode_step_counter += 1
@@ -268,6 +341,18 @@ class polar_cache:
         status = self._status[dev]
         min_total = max(self.FULL_ATTENTION_THRESHOLD, self.sink_size + self.local_size + self.final_topk * 2)
         if total < min_total or valid <= 0:
+            if self.host_tier:
+                s, base = self.sink_size, self.win_base[l]
+                n_h = max(0, base - s) if total > s else 0
+                if n_h > self._stage:
+                    raise RuntimeError(f"full attention over {n_h} host rows exceeds the {self._stage} staging rows")
+                if n_h > 0:
+                    ar = torch.arange(n_h, dtype=torch.int64, device=dev).expand(self.batch_size, self.kv_head, n_h)
+                    ops.h2d_gather_rows(self.keys[l], self.values[l], ar, self.win_k[l], self.win_v[l], src_offset=s,
+                                        dst_offset=s, status=status)
+                off = s + self._stage
+                return ops.attn_rows(q, self.win_k[l], self.win_v[l], seg0=(0, min(total, s) + n_h),
+                                     seg1=(off, off + max(0, total - base)), status=status)
             return ops.attn_rows(q, self.keys[l], self.values[l], seg0=(0, total), status=status)
         cand_ratio, coll_ratio = _adaptive_ratios(valid)
         C = max(1, int(math.ceil(valid * cand_ratio)))
@@ -280,6 +365,13 @@ class polar_cache:
         self._last_topk_indices = final
         local_start = min(total, self.sink_size + valid)
         bs = self.batch_size
+        if self.host_tier:  # the F final rows come over the host link into the staging rows
+            s, base = self.sink_size, self.win_base[l]
+            ops.h2d_gather_rows(self.keys[l], self.values[l], final.view(bs, self.kv_head, F), self.win_k[l],
+                                self.win_v[l], src_offset=s, dst_offset=s, status=status)
+            off = s + self._stage
+            return ops.attn_rows(q, self.win_k[l], self.win_v[l], seg0=(0, s + F),
+                                 seg1=(off + local_start - base, off + total - base), status=status)
         return ops.attn_rows(q, self.keys[l], self.values[l], seg0=(0, min(self.sink_size, total)),
                              sel=final.view(bs, self.kv_head, F), sel_offset=self.sink_size,
                              seg1=(local_start, total), status=status)
