@@ -291,6 +291,48 @@ int zkv_page_decode_split(const void* q, const zkv_page_layer* layer, int rows,
                           int cluster, void* workspace, size_t ws_bytes,
                           void* stream);
 
+/* Per-layer tensors of the raw-page cache: Quest metadata + the raw bf16
+ * K/V rows at absolute token positions (the reference's unified cache). */
+typedef struct zkv_raw_layer {
+    const void* chunk_min;  /* [rows][n_max][128] bf16                      */
+    const void* chunk_max;  /* [rows][n_max][128] bf16                      */
+    const uint8_t* valid;   /* [rows][n_max] or NULL                        */
+    const void* keys;       /* raw rows: row r, token t at                  */
+    const void* values;     /*   base + r*kv_ld_row + t*128 (bf16)          */
+    int64_t kv_ld_row;      /* elements per row, a multiple of 128          */
+    int64_t page_base;      /* token position of chunk 0 (the sink size)    */
+} zkv_raw_layer;
+
+/* Bytes of workspace zkv_page_decode_raw needs.                          */
+size_t zkv_page_decode_raw_ws_bytes(int rows, int n_c, int nk, int n_sink,
+                                    int n_near);
+
+/* Page-mode decode over the RAW bf16 rows of the selected pages, one
+ * launch per layer: GQA-mean query -> Quest scores of chunks [0, n_c) ->
+ * top nk chunks (ties to the lowest id, ascending) -> attention of the G
+ * query heads over [selected chunks' 16 raw rows each, at token
+ * page_base + 16 c] U [0, n_sink) U [near_start, near_start + n_near) ->
+ * (out, lse).  This is polar_cache.compute's retrieval branch in page mode
+ * (dense_topk = sparse_topk = 16, final_topk = budget): the reference
+ * attends the raw rows of the selected chunks
+ * (cache_hub/polar_cache_quest_density_single_layer_kivi.py:1589-1775,
+ * :1734-1750; quest_chunk_score.cu:106-154; float_topk.cu:280-346;
+ * attn_hub/flash_attn_compat.py:44-99).  A persistent grid takes score
+ * tiles, per-row selects and page-attend tiles from one queue; pages move by
+ * 2-D TMA tensor copies.  nk <= n_c (nk == n_c: every chunk, no select).
+ *   q [rows][G][128] bf16; out [rows][G][128] bf16; lse [rows][G] fp32
+ *   natural log (may be NULL); sel_out [rows][nk] int64 or NULL;
+ *   status: device int32 set to ZKV_ERR_TIMEOUT if a bounded wait expires;
+ *   workspace: device, 256-byte aligned, >= zkv_page_decode_raw_ws_bytes,
+ *   ZERO-FILLED before its first use (every call leaves its control words
+ *   at zero again); calls sharing a workspace must not overlap on the GPU.
+ *   Limits: n_c <= 16384, rows * kv_ld_row / 128 < 2^31.                 */
+int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, int rows,
+                        int G, int n_max, int n_c, int nk, int n_sink,
+                        int near_start, int n_near, float scale, void* out,
+                        float* lse, int64_t* sel_out, int32_t* status,
+                        void* workspace, size_t ws_bytes, void* stream);
+
 /* Attention over externally selected pages (the sequence-split step):
  * the layer buffer holds pages [sel_lo, sel_hi) of the sequence as its
  * pages 0..; of the global page ids sel [rows][n_sel] (-1 = none) those in

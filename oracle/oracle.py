@@ -24,7 +24,7 @@ __all__ = [
     "topk_gather_concat", "attn_dense", "page_decode", "lse_merge", "kivi_dequant_chunk",
     "vdequant_tokens", "page_layout_values", "kivi_scale", "rq_mag_tables", "rq_encode", "rq_query", "collision_weights",
     "collision_count", "update_cache_cnt_sorted", "rerank4", "coarse2bit", "rq_query_4bit", "popcount_est",
-    "exact_ip", "h2d_gather", "h2d_gather_packed",
+    "exact_ip", "h2d_gather", "h2d_gather_packed", "page_decode_raw",
 ]
 
 
@@ -251,6 +251,31 @@ def page_decode(q, mn, mx, valid, kcodes, vcodes, vmeta, nearK, nearV, n_c, nk, 
                       _p(nearV), R, G, n_max, n_c, nk, near_ld, n_near, ctypes.c_float(scale),
                       _p(out), _p(lse), _p(sel), int(threads))
     return out, lse, sel
+
+
+def page_decode_raw(q, mn, mx, valid, keys, values, n_c, nk, *, page_base=0, n_sink=0, near_start=0, n_near=0,
+                    scale=1.0 / np.sqrt(128), threads=1):
+    """Page mode over raw rows (see zkv_oracle.h:orc_page_decode_raw).
+    q [R,G,128] bf16; mn/mx [R,n_max,128]; keys/values [R,cap,128] bf16
+    (absolute token positions).  Returns (out [R,G,128] bf16, lse [R,G],
+    sel [R,nk])."""
+    L = lib()
+    q = np.ascontiguousarray(q, np.uint16)
+    R, G, D = q.shape
+    mn = np.ascontiguousarray(mn, np.uint16).reshape(R, -1, D)
+    mx = np.ascontiguousarray(mx, np.uint16).reshape(R, -1, D)
+    keys = np.ascontiguousarray(keys, np.uint16).reshape(R, -1, D)
+    values = np.ascontiguousarray(values, np.uint16).reshape(R, -1, D)
+    n_max, cap = mn.shape[1], keys.shape[1]
+    v = None if valid is None else np.ascontiguousarray(valid, np.uint8).reshape(R, n_max)
+    nsel = nk if n_c > 0 else 0
+    out = np.empty((R, G, D), np.uint16)
+    lse = np.empty((R, G), np.float32)
+    sel = np.empty((R, max(nsel, 1)), np.int64)
+    L.orc_page_decode_raw(_p(q), _p(mn), _p(mx), _p(v), _p(keys), _p(values), ctypes.c_int64(cap),
+                          ctypes.c_int64(page_base), R, G, n_max, int(n_c), int(nk), int(n_sink), int(near_start),
+                          int(n_near), ctypes.c_float(scale), _p(out), _p(lse), _p(sel), int(threads))
+    return out, lse, sel[:, :nsel]
 
 
 def lse_merge(a, la, b, lb):

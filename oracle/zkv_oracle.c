@@ -475,6 +475,112 @@ void orc_page_decode(const uint16_t* q, const uint16_t* mn, const uint16_t* mx,
     for (t = 1; t < threads; ++t) pthread_join(tids[t], NULL);
 }
 
+/* ---------------- page mode over raw rows ---------------- */
+static void raw_row(const uint16_t* q, const uint16_t* mn, const uint16_t* mx,
+                    const uint8_t* valid, const uint16_t* keys, const uint16_t* values,
+                    int64_t page_base, int G, int n_max, int n_c, int nk, int n_sink,
+                    int near_start, int n_near, float scale, uint16_t* out, float* lse,
+                    int64_t* sel) {
+    const int D = 128, C = 16;
+    uint16_t raw_q[128];
+    int d, g, i, t;
+    for (d = 0; d < D; ++d) {
+        float acc = 0.0f;
+        for (g = 0; g < G; ++g) acc += orc_bf2f(q[g * D + d]);
+        raw_q[d] = orc_f2bf(acc / (float)G);
+    }
+    const int nsel = n_c > 0 ? nk : 0;
+    int64_t* chosen = (int64_t*)malloc(sizeof(int64_t) * (size_t)(nsel > 0 ? nsel : 1));
+    if (nsel > 0 && nsel < n_c) {
+        float* scores = (float*)malloc(sizeof(float) * (size_t)n_c);
+        orc_quest_score(raw_q, mn, mx, valid, scores, 1, n_c, n_max);
+        orc_topk_f32(scores, 1, n_c, n_c, nsel, chosen);
+        free(scores);
+    } else {
+        for (i = 0; i < nsel; ++i) chosen[i] = i;
+    }
+    if (sel) memcpy(sel, chosen, sizeof(int64_t) * (size_t)nsel);
+    const int n = nsel * C + n_sink + n_near;
+    float* K = (float*)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1) * D);
+    float* V = (float*)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1) * D);
+    int row = 0;
+    for (t = 0; t < n_sink; ++t, ++row)
+        for (d = 0; d < D; ++d) {
+            K[(size_t)row * D + d] = orc_bf2f(keys[(size_t)t * D + d]);
+            V[(size_t)row * D + d] = orc_bf2f(values[(size_t)t * D + d]);
+        }
+    for (i = 0; i < nsel; ++i)
+        for (t = 0; t < C; ++t, ++row) {
+            const size_t tok = (size_t)(page_base + chosen[i] * C + t);
+            for (d = 0; d < D; ++d) {
+                K[(size_t)row * D + d] = orc_bf2f(keys[tok * D + d]);
+                V[(size_t)row * D + d] = orc_bf2f(values[tok * D + d]);
+            }
+        }
+    for (t = 0; t < n_near; ++t, ++row)
+        for (d = 0; d < D; ++d) {
+            const size_t tok = (size_t)(near_start + t);
+            K[(size_t)row * D + d] = orc_bf2f(keys[tok * D + d]);
+            V[(size_t)row * D + d] = orc_bf2f(values[tok * D + d]);
+        }
+    float qf[8 * 128];
+    float of[8 * 128];
+    for (i = 0; i < G * D; ++i) qf[i] = orc_bf2f(q[i]);
+    orc_attn_dense(qf, K, V, n, G, D, scale, of, lse);
+    for (i = 0; i < G * D; ++i) out[i] = orc_f2bf(of[i]);
+    free(chosen);
+    free(K);
+    free(V);
+}
+
+typedef struct {
+    const uint16_t *q, *mn, *mx;
+    const uint8_t* valid;
+    const uint16_t *keys, *values;
+    int64_t cap, page_base;
+    int rows, G, n_max, n_c, nk, n_sink, near_start, n_near, tid, nthreads;
+    float scale;
+    uint16_t* out;
+    float* lse;
+    int64_t* sel;
+} raw_job_t;
+
+static void* raw_worker(void* arg) {
+    const raw_job_t* j = (const raw_job_t*)arg;
+    const int D = 128;
+    const int nsel = j->n_c > 0 ? j->nk : 0;
+    int r;
+    for (r = j->tid; r < j->rows; r += j->nthreads)
+        raw_row(j->q + (size_t)r * j->G * D, j->mn + (size_t)r * j->n_max * D, j->mx + (size_t)r * j->n_max * D,
+                j->valid ? j->valid + (size_t)r * j->n_max : NULL, j->keys + (size_t)r * j->cap * D,
+                j->values + (size_t)r * j->cap * D, j->page_base, j->G, j->n_max, j->n_c, j->nk, j->n_sink,
+                j->near_start, j->n_near, j->scale, j->out + (size_t)r * j->G * D, j->lse + (size_t)r * j->G,
+                j->sel ? j->sel + (size_t)r * nsel : NULL);
+    return NULL;
+}
+
+void orc_page_decode_raw(const uint16_t* q, const uint16_t* mn, const uint16_t* mx,
+                         const uint8_t* valid, const uint16_t* keys,
+                         const uint16_t* values, int64_t cap, int64_t page_base,
+                         int rows, int G, int n_max, int n_c, int nk, int n_sink,
+                         int near_start, int n_near, float scale, uint16_t* out,
+                         float* lse, int64_t* sel, int threads) {
+    raw_job_t jobs[256];
+    pthread_t tids[256];
+    int t;
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    if (threads > rows) threads = rows > 0 ? rows : 1;
+    for (t = 0; t < threads; ++t) {
+        raw_job_t j = {q, mn, mx, valid, keys, values, cap, page_base, rows, G, n_max, n_c, nk,
+                       n_sink, near_start, n_near, t, threads, scale, out, lse, sel};
+        jobs[t] = j;
+    }
+    for (t = 1; t < threads; ++t) pthread_create(&tids[t], NULL, raw_worker, &jobs[t]);
+    raw_worker(&jobs[0]);
+    for (t = 1; t < threads; ++t) pthread_join(tids[t], NULL);
+}
+
 /* ---------------- LSE merge ---------------- */
 void orc_lse_merge(const float* a, const float* la, const float* b,
                    const float* lb, float* out, float* lse_out, int rows,

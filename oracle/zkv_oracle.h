@@ -118,6 +118,24 @@ void orc_page_decode(const uint16_t* q, const uint16_t* mn, const uint16_t* mx,
                      int near_ld, int n_near, float scale, uint16_t* out,
                      float* lse, int64_t* sel, int threads);
 
+/* Page-mode decode over RAW bf16 rows, the reference's page mode
+ * (polar_cache.compute with dense_topk = sparse_topk = 16 and final_topk =
+ * budget: cache_hub/polar_cache_quest_density_single_layer_kivi.py:1589-1775;
+ * the selected chunks' raw rows are gathered and attended with the sink and
+ * near rows at :1734-1750).  Per row: GQA-mean query (:1622-1626) -> Quest
+ * scores (quest_chunk_score.cu:75-98 order) -> top nk chunks (lowest index
+ * on ties; nk == n_c keeps every chunk) -> fp64 softmax attention over the
+ * 16 raw rows of each selected chunk (token page_base + 16 c + t), the sink
+ * rows [0, n_sink) and the near rows [near_start, near_start + n_near).
+ *   keys/values: row r, token t at base + (r*cap + t)*D (bf16)
+ *   out [rows][G][D] bf16, lse [rows][G] natural log, sel [rows][nk] or NULL */
+void orc_page_decode_raw(const uint16_t* q, const uint16_t* mn, const uint16_t* mx,
+                         const uint8_t* valid, const uint16_t* keys,
+                         const uint16_t* values, int64_t cap, int64_t page_base,
+                         int rows, int G, int n_max, int n_c, int nk, int n_sink,
+                         int near_start, int n_near, float scale, uint16_t* out,
+                         float* lse, int64_t* sel, int threads);
+
 /* Batch forms: keys [rows][T][D] (T % chunk == 0) -> mn/mx/centroid
  * [rows][T/chunk][D], packed [rows][T/chunk][D/8][chunk];
  * values [n_tokens][D] -> codes [n_tokens][D/8], meta [n_tokens][D/group][2]. */

@@ -32,6 +32,14 @@ class ZkvPageLayer(ctypes.Structure):
     ]
 
 
+class ZkvRawLayer(ctypes.Structure):
+    """Mirror of `zkv_raw_layer` (include/zkv.h)."""
+    _fields_ = [
+        ("chunk_min", _c_void_p), ("chunk_max", _c_void_p), ("valid", _c_void_p),
+        ("keys", _c_void_p), ("values", _c_void_p), ("kv_ld_row", _i64), ("page_base", _i64),
+    ]
+
+
 class ZkvRqLayout(ctypes.Structure):
     """Mirror of `zkv_rq_layout` (include/zkv.h)."""
     _fields_ = [
@@ -95,6 +103,9 @@ _SIGNATURES = {
     "zkv_page_decode_split": [_c_void_p, ctypes.POINTER(ZkvPageLayer), _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                               _f32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p, ctypes.c_size_t,
                               _c_void_p],
+    "zkv_page_decode_raw_ws_bytes": [_i32, _i32, _i32, _i32, _i32],
+    "zkv_page_decode_raw": [_c_void_p, ctypes.POINTER(ZkvRawLayer), _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+                            _f32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
     "zkv_lse_merge": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p],
     "zkv_lse_merge_n": [_c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p],
     "zkv_rq_encode": [_c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _RQ, _c_void_p],
@@ -118,7 +129,7 @@ _SIGNATURES = {
 }
 
 _RESTYPES = {"zkv_status_string": ctypes.c_char_p, "zkv_reference_select_ws_bytes": ctypes.c_size_t,
-             "zkv_page_decode_split_ws_bytes": ctypes.c_size_t}
+             "zkv_page_decode_split_ws_bytes": ctypes.c_size_t, "zkv_page_decode_raw_ws_bytes": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib = None

@@ -1,0 +1,752 @@
+// zkv_raw.cu -- page-mode decode over the RAW bf16 rows of the selected pages,
+// one persistent launch per layer.
+//
+// The reference's page mode (polar_cache.compute with dense_topk = sparse_topk
+// = 16 and final_topk = budget, cache_hub/polar_cache_quest_density_single_
+// layer_kivi.py:1589-1775) scores every 16-token chunk with Quest, keeps the
+// top nk chunks and runs flash-attention over sink + the selected chunks' raw
+// K/V rows + the near window (:1734-1750, attn_hub/flash_attn_compat.py:44-99).
+// This kernel does all of it in one launch with no bf16 K/V copy:
+//
+//  * Work items come from one queue (a global counter), in this order:
+//      phase A, row by row: the row's Quest score tiles (128 chunks, 64 KiB of
+//        min/max each) and the row's attend tiles that hold only raw rows
+//        (sink / near, which need no selection);
+//      phase B, row by row: the attend tiles that hold selected pages.
+//    A CTA takes the next item when it finishes one, so the HBM stream never
+//    waits for a whole-grid phase change.
+//  * The CTA that completes a row's last score tile selects the row's top nk
+//    chunks right away (scores copied to shared memory, block_topk_small /
+//    block_topk) and publishes them with a release flag; the other CTAs keep
+//    streaming meanwhile.  Attend tiles with pages wait (time-bounded) on the
+//    flag; every page tile comes after every score tile in the queue, so the
+//    CTA that will set a flag is always already running.
+//  * An attend tile is 8 entries of 16 tokens; each warp owns 2 page slots.
+//    A page arrives as four 2-D TMA tensor copies (K and V, dims 0-63 and
+//    64-127, 16 rows x 128 B each) with the 128-byte swizzle, and is read with
+//    ldmatrix (K, B operand of S = Q K^T) and ldmatrix.trans (V, A operand of
+//    O^T = V^T P^T) into mma.sync m16n8k16 with an online softmax.
+//  * A tile writes its partial (m, l, o) to the workspace; the CTA that
+//    completes a row's last tile merges the row's partials into out / lse.
+//  * The last CTA to exit returns every control word to zero, so the next
+//    launch on the same workspace starts clean.
+#include <cuda.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "zkv_common.cuh"
+
+namespace zkv {
+namespace rawpg {
+
+constexpr int kThreads = 128;
+constexpr int kWarps = kThreads / 32;
+constexpr int kSlots = 2;                         // page slots per warp
+constexpr int kSlotBytes = 8192;                  // K 2 x 2 KiB + V 2 x 2 KiB
+constexpr int kRegion = kWarps * kSlots * kSlotBytes;  // 64 KiB
+constexpr int kTileEntries = kWarps * kSlots;     // entries per attend tile
+constexpr int kScoreTile = kWarps * kSlots * 16;  // chunks per score tile
+constexpr int kPartFloats = 16 + 8 * kHeadDim;    // m[8], l[8], o[8][128]
+constexpr int kMaxChunks = kRegion / 4;           // scores of one row fit the region
+constexpr uint64_t kFlagWaitNs = 2000000000ull;   // selection flag: give up after 2 s
+
+struct Args {
+    CUtensorMap tk;  // raw keys   as [rows * cap][128] bf16, box 64 x 16, 128-B swizzle
+    CUtensorMap tv;  // raw values as [rows * cap][128] bf16
+    const uint16_t* q;
+    const uint16_t* cmin;
+    const uint16_t* cmax;
+    const uint8_t* valid;
+    int64_t cap, page_base;
+    int R, G, n_max, n_c, nk, n_sink, near_start, n_near;
+    int ST, AT, RT, RS, RN, E, n_c_pad, per_row_a;
+    uint32_t total;
+    float sl2;
+    uint16_t* out;
+    float* lse;
+    int64_t* sel_out;
+    int32_t* status;
+    uint32_t* ctrl;  // [0] next item, [1] exited CTAs, then score_done[R], attend_done[R], sel_ready[R]
+    float* scores;   // [R][n_c_pad]
+    int32_t* sel;    // [R][nk]
+    float* parts;    // [R][AT][kPartFloats]
+};
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// 2-D tiled TMA load (no multicast): box (x .. x+63, y .. y+15) -> dst.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+
+struct WarpState {
+    float m;           // running max (log2 units) of head g = lane / 4
+    float l;           // running sum over this lane's tokens
+    float o[8][4];     // O^T accumulators, m-tile j = dims 16j..16j+15
+    uint32_t qa[8][2]; // A fragments of Q (rows = heads), k-step s
+};
+
+__device__ __forceinline__ void state_init(WarpState& st, const uint16_t* qrow, int G) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        st.qa[s][0] = g < G ? __ldg(reinterpret_cast<const uint32_t*>(qrow + g * kHeadDim + 16 * s + 2 * tig)) : 0u;
+        st.qa[s][1] = g < G ? __ldg(reinterpret_cast<const uint32_t*>(qrow + g * kHeadDim + 16 * s + 8 + 2 * tig)) : 0u;
+    }
+    st.m = -INFINITY;
+    st.l = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) st.o[j][e] = 0.f;
+}
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Online-softmax update with scores of tokens 2tig, 2tig+1, 8+2tig, 9+2tig of
+// head g; returns the B fragment of P^T for the PV product.
+__device__ __forceinline__ void softmax_step(WarpState& st, float (&x)[4], int G, uint32_t& b0, uint32_t& b1) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+    float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mnew = fmaxf(st.m, mx);
+    const float alpha = (st.m == -INFINITY) ? 0.f : ex2(st.m - mnew);
+    float p[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p[i] = (x[i] == -INFINITY) ? 0.f : ex2(x[i] - mnew);
+    st.l = st.l * alpha + ((p[0] + p[1]) + (p[2] + p[3]));
+    st.m = mnew;
+    const float a0 = __shfl_sync(0xffffffffu, alpha, (2 * tig) * 4);
+    const float a1 = __shfl_sync(0xffffffffu, alpha, (2 * tig + 1) * 4);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        st.o[j][0] *= a0;
+        st.o[j][1] *= a1;
+        st.o[j][2] *= a0;
+        st.o[j][3] *= a1;
+    }
+    b0 = g < G ? pack_bf162(p[0], p[1]) : 0u;
+    b1 = g < G ? pack_bf162(p[2], p[3]) : 0u;
+}
+
+// One 16-token page in a slot: K boxes at +0 (dims 0-63) and +2048 (dims
+// 64-127), V boxes at +4096 and +6144; token t's 16-byte chunk c sits at
+// byte 128 t + 16 (c ^ (t & 7)) of its box (the TMA 128-byte swizzle on a
+// 1024-byte-aligned box).  Bit t of `present` marks real tokens; absent
+// tokens score -inf and their V rows were zeroed.
+__device__ __forceinline__ void page_attend(WarpState& st, uint32_t slot, unsigned present, int G, float sl2) {
+    const int lane = threadIdx.x & 31, tig = lane & 3;
+    const int mtx = lane >> 3;                  // ldmatrix sub-matrix addressed by this lane
+    const int t = (lane & 7) + 8 * (mtx >> 1);  // its token row
+    const int hi = mtx & 1;                     // second 8-dim chunk of a 16-dim step
+    const uint32_t row = slot + 128u * (uint32_t)t;
+    float sacc[2][2][4] = {};  // [k-half][token tile][fragment]
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        const int c = 2 * s + hi;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(row + (uint32_t)((c >> 3) * 2048 + (((c & 7) ^ (t & 7)) << 4)), b0, b1, b2, b3);
+        mma_bf16_16816(sacc[s >> 2][0], st.qa[s][0], 0u, st.qa[s][1], 0u, b0, b1);
+        mma_bf16_16816(sacc[s >> 2][1], st.qa[s][0], 0u, st.qa[s][1], 0u, b2, b3);
+    }
+    float x[4] = {(sacc[0][0][0] + sacc[1][0][0]) * sl2, (sacc[0][0][1] + sacc[1][0][1]) * sl2,
+                  (sacc[0][1][0] + sacc[1][1][0]) * sl2, (sacc[0][1][1] + sacc[1][1][1]) * sl2};
+    if (present != 0xffffu) {
+        const int tk[4] = {2 * tig, 2 * tig + 1, 8 + 2 * tig, 9 + 2 * tig};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (!((present >> tk[i]) & 1u)) x[i] = -INFINITY;
+    }
+    uint32_t pb0, pb1;
+    softmax_step(st, x, G, pb0, pb1);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int c = 2 * j + hi;
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_t(row + 4096u + (uint32_t)((c >> 3) * 2048 + (((c & 7) ^ (t & 7)) << 4)), a0, a1, a2, a3);
+        mma_bf16_16816(st.o[j], a0, a1, a2, a3, pb0, pb1);
+    }
+}
+
+// Merge the warps' states into (cm, cl, co) in shared memory; scratch >=
+// kWarps * (8 * 128 + 16) floats.  Ends with the block synchronised.
+__device__ void merge_warps(const WarpState& st, int G, float* scratch, float* cm, float* cl, float* co) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, tig = lane & 3;
+    float l = st.l;
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    float* wm = scratch + warp * (8 * kHeadDim + 16);
+    float* wl = wm + 8;
+    float* wo = wm + 16;
+    if (tig == 0) {
+        wm[g] = st.m;
+        wl[g] = l;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int d = 16 * j + g;
+        const int h0 = 2 * tig, h1 = 2 * tig + 1;
+        if (h0 < G) {
+            wo[h0 * kHeadDim + d] = st.o[j][0];
+            wo[h0 * kHeadDim + d + 8] = st.o[j][2];
+        }
+        if (h1 < G) {
+            wo[h1 * kHeadDim + d] = st.o[j][1];
+            wo[h1 * kHeadDim + d + 8] = st.o[j][3];
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * kHeadDim; i += kThreads) {
+        const int h = i / kHeadDim, d = i % kHeadDim;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, scratch[w * (8 * kHeadDim + 16) + h]);
+        float Ls = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+            const float* b = scratch + w * (8 * kHeadDim + 16);
+            const float wt = (b[h] == -INFINITY) ? 0.f : ex2(b[h] - M);
+            Ls += wt * b[8 + h];
+            O += wt * b[16 + h * kHeadDim + d];
+        }
+        co[h * kHeadDim + d] = O;
+        if (d == 0) {
+            cm[h] = M;
+            cl[h] = Ls;
+        }
+    }
+    __syncthreads();
+}
+
+// Token start and present mask of entry e of a row (sink pseudo-pages, near
+// pseudo-pages, then selected pages); the page's chunk id comes from `chunk`.
+__device__ __forceinline__ int64_t entry_tokens(const Args& a, int e, int chunk, unsigned& present) {
+    if (e < a.RS) {
+        const int n = min(16, a.n_sink - 16 * e);
+        present = (1u << n) - 1u;
+        return 16 * e;
+    }
+    if (e < a.RS + a.RN) {
+        const int k = e - a.RS;
+        const int n = min(16, a.n_near - 16 * k);
+        present = (1u << n) - 1u;
+        return (int64_t)a.near_start + 16 * k;
+    }
+    present = 0xffffu;
+    return a.page_base + 16 * (int64_t)chunk;
+}
+
+__global__ void __launch_bounds__(kThreads, 3) raw_decode_kernel(const __grid_constant__ Args a) {
+    extern __shared__ uint8_t smem_raw[];
+    // the swizzled boxes need a 1024-byte-aligned region
+    const uint32_t base_u32 = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
+    uint8_t* region = smem;
+    float* region_f = reinterpret_cast<float*>(region);
+    int* hist = reinterpret_cast<int*>(smem + kRegion);
+    int* misc = hist + 512;
+    int* scan = misc + 8;
+    uint16_t* rq_s = reinterpret_cast<uint16_t*>(scan + 2 * kThreads);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(rq_s + kHeadDim);        // [warps][slots]
+    uint32_t* s_u = reinterpret_cast<uint32_t*>(bars + kWarps * kSlots);  // [0] item [1] flag [2] lo [3] hi [4] fail
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kWarps * kSlots; ++i) mbar_init(bars + i, 1);
+        mbar_fence_init();
+        s_u[4] = 0;
+    }
+    grid_dep_wait();  // q and the workspace may still be in use by the previous kernel
+    uint32_t* ctr_next = a.ctrl;
+    uint32_t* ctr_exit = a.ctrl + 1;
+    uint32_t* score_done = a.ctrl + 2;
+    uint32_t* attend_done = score_done + a.R;
+    uint32_t* sel_ready = attend_done + a.R;
+    const uint32_t slot0 = smem_u32(region) + (uint32_t)(warp * kSlots) * kSlotBytes;
+    uint64_t* wbar = bars + warp * kSlots;
+    uint32_t phase = 0;  // bit k: parity of slot k's next completion (warp-uniform)
+
+    if (threadIdx.x == 0) s_u[0] = atomicAdd(ctr_next, 1u);
+    __syncthreads();
+    uint32_t nxt = 0;  // thread 0: the claim prefetched for the next iteration
+    for (;;) {
+        const uint32_t item = s_u[0];
+        if (item >= a.total) break;
+        if (threadIdx.x == 0) nxt = atomicAdd(ctr_next, 1u);
+        int r, tile;
+        bool score;
+        if (item < (uint32_t)(a.R * a.per_row_a)) {
+            r = (int)(item / (uint32_t)a.per_row_a);
+            const int j = (int)(item % (uint32_t)a.per_row_a);
+            score = j < a.ST;
+            tile = score ? j : j - a.ST;
+        } else {
+            const int bt = a.AT - a.RT;
+            const uint32_t i2 = item - (uint32_t)(a.R * a.per_row_a);
+            r = (int)(i2 / (uint32_t)bt);
+            tile = a.RT + (int)(i2 % (uint32_t)bt);
+            score = false;
+        }
+        if (score) {
+            // ---------------------------------------------- Quest score tile
+            const int c0 = tile * kScoreTile;
+            const uint16_t* gmin = a.cmin + ((int64_t)r * a.n_max) * kHeadDim;
+            const uint16_t* gmax = a.cmax + ((int64_t)r * a.n_max) * kHeadDim;
+            int nch[kSlots];
+#pragma unroll
+            for (int k = 0; k < kSlots; ++k) {
+                const int cc = c0 + (warp * kSlots + k) * 16;
+                nch[k] = max(0, min(16, a.n_c - cc));
+                if (lane == 0 && nch[k] > 0) {
+                    uint8_t* dst = region + (warp * kSlots + k) * kSlotBytes;
+                    mbar_arrive_expect_tx(wbar + k, (uint32_t)nch[k] * kHeadDim * 2 * 2);
+                    bulk_g2s(dst, gmin + (int64_t)cc * kHeadDim, nch[k] * kHeadDim * 2, wbar + k);
+                    bulk_g2s(dst + 4096, gmax + (int64_t)cc * kHeadDim, nch[k] * kHeadDim * 2, wbar + k);
+                }
+            }
+            // GQA-mean query (compute() :1622-1626: fp32 sum in head order / G, bf16)
+            {
+                const uint16_t* qr = a.q + (int64_t)r * a.G * kHeadDim;
+                const int d = threadIdx.x;
+                float acc = 0.f;
+                for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, bfbits2f(__ldg(qr + g * kHeadDim + d)));
+                rq_s[d] = f2bfbits(__fdiv_rn(acc, (float)a.G));
+            }
+            __syncthreads();
+            const int hl = lane & 15, half = lane >> 4;
+            const uint4 qv = *reinterpret_cast<const uint4*>(rq_s + 8 * hl);
+            float* srow = a.scores + (int64_t)r * a.n_c_pad;
+#pragma unroll
+            for (int k = 0; k < kSlots; ++k) {
+                if (nch[k] == 0) continue;
+                const bool ok = mbar_wait(wbar + k, (phase >> k) & 1u, a.status);
+                phase ^= 1u << k;
+                const uint8_t* src = region + (warp * kSlots + k) * kSlotBytes;
+                const int cc = c0 + (warp * kSlots + k) * 16;
+#pragma unroll 4
+                for (int u = 0; u < 8; ++u) {
+                    const int lc = 2 * u + half;
+                    uint4 mn = make_uint4(0, 0, 0, 0), mx = mn;
+                    if (lc < nch[k]) {
+                        mn = *reinterpret_cast<const uint4*>(src + lc * 256 + 16 * hl);
+                        mx = *reinterpret_cast<const uint4*>(src + 4096 + lc * 256 + 16 * hl);
+                    }
+                    const float sc = quest_half(qv, mn, mx);
+                    if (hl == 0 && lc < nch[k]) {
+                        const int c = cc + lc;
+                        const bool v = !a.valid || a.valid[(int64_t)r * a.n_max + c];
+                        srow[c] = (ok && v) ? sc : -INFINITY;
+                    }
+                }
+                if (!ok && lane == 0) atomicOr(&s_u[4], 1u);
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                __threadfence();
+                const uint32_t done = atomicAdd(score_done + r, 1u);
+                s_u[1] = done == (uint32_t)(a.ST - 1);
+                if (s_u[1]) __threadfence();
+            }
+            __syncthreads();
+            if (s_u[1]) {
+                // ------------------------------------------ select (last score tile of row r)
+                if (threadIdx.x == 0) {
+                    s_u[2] = 0xffffffffu;
+                    s_u[3] = 0u;
+                }
+                __syncthreads();
+                uint32_t klo = 0xffffffffu, khi = 0u;
+                for (int i = 4 * threadIdx.x; i < a.n_c; i += 4 * kThreads) {
+                    const float4 f = __ldcg(reinterpret_cast<const float4*>(srow + i));
+                    const float fv[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        if (i + e < a.n_c) {
+                            region_f[i + e] = fv[e];
+                            const uint32_t kk = ordered_u32(fv[e]);
+                            if (kk > kOrderedNegInf) klo = min(klo, kk);
+                            khi = max(khi, kk);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) {
+                    klo = min(klo, __shfl_xor_sync(0xffffffffu, klo, off));
+                    khi = max(khi, __shfl_xor_sync(0xffffffffu, khi, off));
+                }
+                if (lane == 0) {
+                    atomicMin(&s_u[2], klo);
+                    atomicMax(&s_u[3], khi);
+                }
+                __syncthreads();
+                int32_t* selr = a.sel + (int64_t)r * a.nk;
+                int64_t* selo = a.sel_out ? a.sel_out + (int64_t)r * a.nk : nullptr;
+                auto emit = [&](int pos, int i) {
+                    selr[pos] = i;
+                    if (selo) selo[pos] = i;
+                };
+                if (a.n_c <= 16 * kThreads)
+                    block_topk_small<kThreads>(region_f, a.n_c, a.nk, s_u[2], s_u[3], hist, misc, scan, emit);
+                else
+                    block_topk<kThreads, true>([&](int i) { return ordered_u32(region_f[i]); }, a.n_c, a.nk, hist,
+                                               misc, scan, emit, true, s_u[2], s_u[3]);
+                __syncthreads();
+                if (threadIdx.x == 0) {
+                    __threadfence();
+                    st_release(sel_ready + r, 1u);
+                }
+            }
+        } else {
+            // ---------------------------------------------- attend tile
+            const int e0 = tile * kTileEntries;
+            const int e1 = min(a.E, e0 + kTileEntries);
+            const int pg0 = a.RS + a.RN;  // first page entry
+            bool ok = true;
+            if (a.ST > 0 && e1 > pg0) {   // the tile holds selected pages: wait for the selection
+                if (threadIdx.x == 0) {
+                    uint32_t f = ld_acquire(sel_ready + r);
+                    if (!f) {
+                        const uint64_t t0 = globaltimer_ns();
+                        while (!(f = ld_acquire(sel_ready + r))) {
+                            __nanosleep(128);
+                            if (globaltimer_ns() - t0 > kFlagWaitNs) break;
+                        }
+                    }
+                    if (!f) {
+                        set_status(a.status, ZKV_ERR_TIMEOUT);
+                        s_u[4] = 1u;
+                    }
+                    __threadfence();
+                }
+                __syncthreads();
+                ok = s_u[4] == 0u;
+            }
+            unsigned present[kSlots] = {0u, 0u};
+            bool have[kSlots] = {false, false};
+#pragma unroll
+            for (int k = 0; k < kSlots; ++k) {
+                const int e = e0 + warp * kSlots + k;
+                have[k] = ok && e < e1;
+                if (!have[k]) continue;
+                int chunk = 0;
+                if (e >= pg0) {
+                    const int p = e - pg0;
+                    chunk = a.ST > 0 ? (lane == 0 ? __ldcg(a.sel + (int64_t)r * a.nk + p) : 0) : p;
+                    chunk = __shfl_sync(0xffffffffu, chunk, 0);
+                    // every chunk selected (no select ran): the selection is the identity
+                    if (a.ST == 0 && a.sel_out && lane == 0) a.sel_out[(int64_t)r * a.nk + p] = p;
+                }
+                unsigned pr;
+                const int64_t y0 = entry_tokens(a, e, chunk, pr);
+                present[k] = pr;
+                if (lane == 0) {
+                    const int y = (int)((int64_t)r * a.cap + y0);
+                    const uint32_t dst = slot0 + (uint32_t)k * kSlotBytes;
+                    mbar_arrive_expect_tx(wbar + k, kSlotBytes);
+                    tma_load_2d(dst, &a.tk, 0, y, wbar + k);
+                    tma_load_2d(dst + 2048, &a.tk, 64, y, wbar + k);
+                    tma_load_2d(dst + 4096, &a.tv, 0, y, wbar + k);
+                    tma_load_2d(dst + 6144, &a.tv, 64, y, wbar + k);
+                }
+            }
+            WarpState st;
+            state_init(st, a.q + (int64_t)r * a.G * kHeadDim, a.G);
+#pragma unroll
+            for (int k = 0; k < kSlots; ++k) {
+                if (!have[k]) continue;
+                const bool landed = mbar_wait(wbar + k, (phase >> k) & 1u, a.status);
+                phase ^= 1u << k;
+                if (!landed) {
+                    if (lane == 0) atomicOr(&s_u[4], 1u);
+                    continue;
+                }
+                const uint32_t slot = slot0 + (uint32_t)k * kSlotBytes;
+                if (present[k] != 0xffffu) {  // zero the V rows of absent tokens (p = 0 must meet finite V)
+                    uint8_t* vs = region + (warp * kSlots + k) * kSlotBytes + 4096;
+                    for (int i = lane; i < 16 * 16; i += 32) {
+                        const int tkn = i >> 4, box = (i >> 3) & 1, c = i & 7;
+                        if (!((present[k] >> tkn) & 1u))
+                            *reinterpret_cast<uint4*>(vs + box * 2048 + tkn * 128 + c * 16) = make_uint4(0, 0, 0, 0);
+                    }
+                    __syncwarp();
+                }
+                page_attend(st, slot, present[k], a.G, a.sl2);
+            }
+            __syncthreads();
+            float* cm = region_f + 8192;  // past the warp scratch
+            float* cl = cm + 8;
+            float* co = cl + 8;
+            merge_warps(st, a.G, region_f, cm, cl, co);
+            float* part = a.parts + ((int64_t)r * a.AT + tile) * kPartFloats;
+            if (threadIdx.x < 8) {
+                part[threadIdx.x] = threadIdx.x < a.G ? cm[threadIdx.x] : -INFINITY;
+                part[8 + threadIdx.x] = threadIdx.x < a.G ? cl[threadIdx.x] : 0.f;
+            }
+            for (int i = threadIdx.x; i < a.G * kHeadDim / 4; i += kThreads)
+                reinterpret_cast<float4*>(part + 16)[i] = reinterpret_cast<const float4*>(co)[i];
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                __threadfence();
+                const uint32_t done = atomicAdd(attend_done + r, 1u);
+                s_u[1] = done == (uint32_t)(a.AT - 1);
+                if (s_u[1]) __threadfence();
+            }
+            __syncthreads();
+            if (s_u[1]) {
+                // ------------------------------------------ row merge (last attend tile of row r)
+                const float* pr = a.parts + (int64_t)r * a.AT * kPartFloats;
+                for (int i = threadIdx.x; i < a.G * kHeadDim; i += kThreads) {
+                    const int h = i / kHeadDim;
+                    float M = -INFINITY;
+                    for (int t = 0; t < a.AT; ++t) M = fmaxf(M, __ldcg(pr + t * kPartFloats + h));
+                    float Ls = 0.f, O = 0.f;
+                    for (int t = 0; t < a.AT; ++t) {
+                        const float* b = pr + t * kPartFloats;
+                        const float mt = __ldcg(b + h);
+                        const float wt = (mt == -INFINITY) ? 0.f : ex2(mt - M);
+                        Ls += wt * __ldcg(b + 8 + h);
+                        O += wt * __ldcg(b + 16 + i);
+                    }
+                    a.out[(int64_t)r * a.G * kHeadDim + i] = f2bfbits(Ls > 0.f ? O / Ls : 0.f);
+                    if ((i % kHeadDim) == 0 && a.lse)
+                        a.lse[(int64_t)r * a.G + h] =
+                            (Ls > 0.f) ? (M + __log2f(Ls)) * 0.69314718055994531f : -INFINITY;
+                }
+            }
+        }
+        // order this item's generic reads / writes of the region before the
+        // next item's TMA writes into it
+        fence_proxy_async();
+        __syncthreads();
+        if (threadIdx.x == 0) s_u[0] = nxt;
+        __syncthreads();
+    }
+
+    // ------------------------------------------------ exit: the last CTA resets the control words
+    grid_dep_launch_next();
+    if (threadIdx.x == 0) {
+        if (s_u[4]) set_status(a.status, ZKV_ERR_TIMEOUT);
+        __threadfence();
+        const uint32_t gone = atomicAdd(ctr_exit, 1u);
+        s_u[1] = gone == gridDim.x - 1;
+        if (s_u[1]) __threadfence();
+    }
+    __syncthreads();
+    if (s_u[1]) {
+        for (int i = threadIdx.x; i < 3 * a.R; i += kThreads) score_done[i] = 0u;
+        if (threadIdx.x == 0) {
+            *ctr_next = 0u;
+            *ctr_exit = 0u;
+        }
+        __threadfence();
+    }
+}
+
+// ---------------------------------------------------------------- host side
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult qr;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &qr) ==
+                cudaSuccess &&
+            qr == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+// [n_tok][128] bf16 rows, 16-row x 64-dim boxes, 128-byte swizzle, zero fill
+static bool encode_rows(CUtensorMap* map, const void* base, int64_t n_tok) {
+    EncodeTiled fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)kHeadDim, (cuuint64_t)n_tok};
+    const cuuint64_t strides[1] = {(cuuint64_t)kHeadDim * 2};
+    const cuuint32_t box[2] = {64, 16};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct Plan {
+    int ST, AT, RT, RS, RN, E, n_c_pad, per_row_a;
+    int64_t total;
+    size_t off_scores, off_sel, off_parts, bytes;
+};
+
+static size_t up256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near) {
+    Plan p;
+    const int nsel = n_c > 0 ? nk : 0;
+    p.ST = nk < n_c ? (n_c + kScoreTile - 1) / kScoreTile : 0;  // no scoring when every chunk is selected
+    p.RS = (n_sink + 15) / 16;
+    p.RN = (n_near + 15) / 16;
+    p.E = p.RS + p.RN + nsel;
+    p.AT = p.E > 0 ? (p.E + kTileEntries - 1) / kTileEntries : 1;
+    p.RT = (p.RS + p.RN) / kTileEntries;  // tiles of raw rows only (no selection needed)
+    if (p.RT > p.AT) p.RT = p.AT;
+    p.n_c_pad = (n_c + 31) & ~31;
+    p.per_row_a = p.ST + p.RT;
+    p.total = (int64_t)R * (p.ST + p.AT);
+    p.off_scores = up256(8 + (size_t)12 * R);
+    p.off_sel = p.off_scores + up256((size_t)R * p.n_c_pad * 4);
+    p.off_parts = p.off_sel + up256((size_t)R * (nk > 0 ? nk : 1) * 4);
+    p.bytes = p.off_parts + up256((size_t)R * p.AT * kPartFloats * 4);
+    return p;
+}
+
+static size_t smem_bytes() {
+    return 1024 + kRegion + (512 + 8 + 2 * kThreads) * 4 + kHeadDim * 2 + kWarps * kSlots * 8 + 8 * 4;
+}
+
+}  // namespace rawpg
+}  // namespace zkv
+
+using namespace zkv;
+
+extern "C" size_t zkv_page_decode_raw_ws_bytes(int rows, int n_c, int nk, int n_sink, int n_near) {
+    if (rows < 0 || n_c < 0 || nk < 0 || n_sink < 0 || n_near < 0) return 0;
+    return rawpg::make_plan(rows, n_c, nk, n_sink, n_near).bytes;
+}
+
+extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, int rows, int G, int n_max, int n_c,
+                                   int nk, int n_sink, int near_start, int n_near, float scale, void* out, float* lse,
+                                   int64_t* sel_out, int32_t* status, void* workspace, size_t ws_bytes,
+                                   void* stream) {
+    using namespace zkv::rawpg;
+    if (!q || !layer || !out || !workspace || rows < 0 || G < 1 || G > 8 || n_c < 0 || n_c > n_max || nk < 0 ||
+        (n_c > 0 && (nk < 1 || nk > n_c)) || n_sink < 0 || n_near < 0 || near_start < 0)
+        return ZKV_ERR_ARG;
+    const zkv_raw_layer& L = *layer;
+    if (!L.keys || !L.values || L.kv_ld_row < kHeadDim || (L.kv_ld_row % kHeadDim) || L.page_base < 0 ||
+        (n_c > 0 && (!L.chunk_min || !L.chunk_max)))
+        return ZKV_ERR_ARG;
+    const int64_t cap = L.kv_ld_row / kHeadDim;
+    if (L.page_base + 16 * (int64_t)n_c > cap || (int64_t)near_start + n_near > cap || n_sink > cap)
+        return ZKV_ERR_ARG;
+    if (n_c > kMaxChunks || nk > 65536 || (int64_t)rows * cap >= (int64_t)1 << 31) return ZKV_ERR_CAPACITY;
+    const Plan p = make_plan(rows, n_c, nk, n_sink, n_near);
+    if (ws_bytes < p.bytes) return ZKV_ERR_ARG;
+    if (p.total >= ((int64_t)1 << 31)) return ZKV_ERR_CAPACITY;
+    if (rows == 0) return ZKV_OK;
+    if (((uintptr_t)L.keys & 15) || ((uintptr_t)L.values & 15) || ((uintptr_t)L.chunk_min & 15) ||
+        ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)q & 3) || ((uintptr_t)workspace & 255))
+        return ZKV_ERR_ALIGN;
+    Args a;
+    memset(&a, 0, sizeof(a));
+    if (!encode_rows(&a.tk, L.keys, (int64_t)rows * cap) || !encode_rows(&a.tv, L.values, (int64_t)rows * cap))
+        return ZKV_ERR_LAUNCH;
+    a.q = (const uint16_t*)q;
+    a.cmin = (const uint16_t*)L.chunk_min;
+    a.cmax = (const uint16_t*)L.chunk_max;
+    a.valid = L.valid;
+    a.cap = cap;
+    a.page_base = L.page_base;
+    a.R = rows;
+    a.G = G;
+    a.n_max = n_max;
+    a.n_c = n_c;
+    a.nk = n_c > 0 ? nk : 0;
+    a.n_sink = n_sink;
+    a.near_start = near_start;
+    a.n_near = n_near;
+    a.ST = p.ST;
+    a.AT = p.AT;
+    a.RT = p.RT;
+    a.RS = p.RS;
+    a.RN = p.RN;
+    a.E = p.E;
+    a.n_c_pad = p.n_c_pad;
+    a.per_row_a = p.per_row_a;
+    a.total = (uint32_t)p.total;
+    a.sl2 = scale * 1.4426950408889634f;
+    a.out = (uint16_t*)out;
+    a.lse = lse;
+    a.sel_out = sel_out;
+    a.status = status;
+    uint8_t* ws = (uint8_t*)workspace;
+    a.ctrl = (uint32_t*)ws;
+    a.scores = (float*)(ws + p.off_scores);
+    a.sel = (int32_t*)(ws + p.off_sel);
+    a.parts = (float*)(ws + p.off_parts);
+
+    // persistent grid: the resident CTAs of every SM (capped by the item count)
+    static int occ[64] = {};
+    static int sms[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ZKV_ERR_LAUNCH;
+    const size_t smem = smem_bytes();
+    if (!occ[dev]) {
+        if (cudaFuncSetAttribute(raw_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return ZKV_ERR_LAUNCH;
+        int nb = 0, n_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, raw_decode_kernel, kThreads, smem) != cudaSuccess ||
+            cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || nb < 1)
+            return ZKV_ERR_LAUNCH;
+        sms[dev] = n_sm;
+        occ[dev] = nb;
+    }
+    int64_t grid = (int64_t)occ[dev] * sms[dev];
+    if (grid > p.total) grid = p.total;
+    if (grid < 1) grid = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, raw_decode_kernel, a) != cudaSuccess) return ZKV_ERR_LAUNCH;
+    return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH;
+}

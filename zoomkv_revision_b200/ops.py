@@ -18,7 +18,9 @@ kivi_encode_chunks                     polar_cache._compute_and_store_chunk_minm
                                        _kivi_pack_chunks (aligned chunks)
 attn_rows                              h2d_gather_kv + torch.cat + flash_attn_with_kvcache
 h2d_gather_kv / h2d_gather_kv_packed   cache_hub/gather_trans/trans_h2d.py:65-161 (offload tier)
-page_decode                            (fused page-mode decode; no single counterpart)
+page_decode_raw                        polar_cache.compute in page mode (REF:1589-1775): Quest top-nk
+                                       chunks, attention over their raw rows + sink + near (one launch)
+page_decode                            (fused page mode over 4-bit KIVI K/V pages, lossy; no counterpart)
 reference_select                       polar_cache.compute retrieval chain (REF:1589-1775) as one call
 vquant_encode                          (per-token 4-bit values; no counterpart)
 RqLayout / rq_encode / batch_encode    cache_hub/polar_cache.py batch_encode (:1130-1198)
@@ -49,7 +51,7 @@ __all__ = [
     "dense_mask_from_topk_cuda", "partial_chunk_kivi_qk_dense_sparse_cuda", "float_topk_gather_concat_3d",
     "lse_merge_cuda", "lse_merge_n", "kivi_encode_chunks", "vquant_encode", "attn_rows", "page_decode",
     "h2d_gather_kv", "h2d_gather_kv_packed", "h2d_gather_rows", "page_decode_scored",
-    "PageLayer", "page_attend", "gqa_mean", "reference_select", "reference_select_ws_bytes", "RqLayout", "rq_encode", "batch_encode", "rq_query", "get_cache_cnt_fused", "collision_topk",
+    "PageLayer", "page_attend", "RawLayer", "page_decode_raw", "page_decode_raw_ws_bytes", "gqa_mean", "reference_select", "reference_select_ws_bytes", "RqLayout", "rq_encode", "batch_encode", "rq_query", "get_cache_cnt_fused", "collision_topk",
     "partial_rerank_cuda", "coarse_2bit_score_cuda", "rq_popcount_topk", "MAG_CENTERS", "MAG_THRESHOLDS",
 ]
 
@@ -644,6 +646,73 @@ def page_decode_scored(q, layer: PageLayer, scores, n_c: int, nk: int, own_lo: i
                                        int(near_start), int(n_near), scale, int(parts), _p(out_f32), _p(lse),
                                        _p(sel_out), _p(status), int(cluster), _stream(q)), "zkv_page_decode_scored")
     return out_f32
+
+
+class RawLayer:
+    """One layer of the raw-page cache: Quest metadata chunk_min / chunk_max
+    [bs, H, n_max, 128] bf16 (+ valid [bs, H, n_max] or None) and the raw
+    keys / values [bs, H, cap, 128] bf16 at absolute token positions; chunk c
+    covers tokens page_base + 16 c .. + 15 (page_base = the sink size)."""
+
+    def __init__(self, chunk_min, chunk_max, valid, keys, values, page_base: int = 0):
+        for n, t in (("chunk_min", chunk_min), ("chunk_max", chunk_max), ("keys", keys), ("values", values)):
+            _dtype(n, t, torch.bfloat16)
+            _cuda((n, t))
+        for n, t in (("chunk_min", chunk_min), ("chunk_max", chunk_max)):
+            _contig(n, t)
+        for n, t in (("keys", keys), ("values", values)):
+            if t.dim() != 4 or t.shape[3] != 128 or t.stride(3) != 1 or t.stride(2) != 128 or \
+                    t.stride(0) != t.shape[1] * t.stride(1):
+                raise ValueError(f"{n} must be [bs, H, cap, 128] with rows of 128 contiguous elements")
+        if keys.shape != values.shape or keys.stride() != values.stride():
+            raise ValueError("keys and values must have the same shape and strides")
+        if valid is not None:
+            _contig("valid", valid)
+        self.tensors = (chunk_min, chunk_max, valid, keys, values)
+        self.page_base = int(page_base)
+        self.struct = _lib.ZkvRawLayer(_p(chunk_min), _p(chunk_max), _p(valid), _p(keys), _p(values),
+                                       keys.stride(1), self.page_base)
+
+
+_RAW_WS: dict = {}
+
+
+def page_decode_raw_ws_bytes(rows: int, n_c: int, nk: int, n_sink: int, n_near: int) -> int:
+    return int(lib().zkv_page_decode_raw_ws_bytes(int(rows), int(n_c), int(nk), int(n_sink), int(n_near)))
+
+
+def page_decode_raw(q, layer: RawLayer, n_c: int, nk: int, n_near: int, *, n_sink: int = 0, near_start: int = 0,
+                    scale=None, out=None, lse=None, sel_out=None, status=None, workspace=None):
+    """Page mode over raw rows: q [bs,1,H*G,128] -> out [bs,1,H*G,128] bf16.
+
+    Quest scores of chunks [0, n_c), top nk chunks, then attention over the
+    selected chunks' raw rows, the sink rows [0, n_sink) and the near rows
+    [near_start, near_start + n_near) of layer.keys / layer.values.
+    workspace: optional ZERO-FILLED uint8 device tensor of at least
+    page_decode_raw_ws_bytes(...) bytes (default: one cached buffer per
+    device, so calls on concurrent streams should pass their own)."""
+    cmin = layer.tensors[0]
+    bs, H, n_max, D = cmin.shape
+    _dtype("q", q, torch.bfloat16)
+    G = q.shape[2] // H
+    qc = q.contiguous()
+    if out is None:
+        out = torch.empty(bs, 1, H * G, D, dtype=torch.bfloat16, device=q.device)
+    scale = (1.0 / D ** 0.5) if scale is None else float(scale)
+    rows = bs * H
+    if workspace is None:
+        need = page_decode_raw_ws_bytes(rows, n_c, nk, n_sink, n_near)
+        key = q.device.index if q.device.index is not None else torch.cuda.current_device()
+        ws = _RAW_WS.get(key)
+        if ws is None or ws.numel() < need:
+            ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=q.device)
+            _RAW_WS[key] = ws
+        workspace = ws
+    check(lib().zkv_page_decode_raw(_p(qc), ctypes.byref(layer.struct), rows, G, n_max, int(n_c), int(nk),
+                                    int(n_sink), int(near_start), int(n_near), scale, _p(out), _p(lse),
+                                    _p(sel_out), _p(status), _p(workspace), int(workspace.numel()), _stream(q)),
+          "zkv_page_decode_raw")
+    return out
 
 
 def gqa_mean(q, heads: int, out=None):

@@ -138,6 +138,61 @@ def build_page_cache(seed: int, bs: int, heads: int, n_retrieval: int, n_near: i
     return pc, raw
 
 
+@dataclass
+class RawCache:
+    """One layer of the raw-page cache: Quest metadata over the retrieval zone
+    and the raw K/V rows at absolute positions [sink | retrieval | near]."""
+    chunk_min: torch.Tensor   # [bs,H,n_c,128] bf16
+    chunk_max: torch.Tensor
+    valid: torch.Tensor       # [bs,H,n_c] bool
+    keys: torch.Tensor        # [bs,H,cap,128] bf16
+    values: torch.Tensor
+    n_sink: int
+    n_c: int
+    near_start: int
+    n_near: int
+
+    def layer(self) -> ops.RawLayer:
+        return ops.RawLayer(self.chunk_min, self.chunk_max, self.valid, self.keys, self.values, self.n_sink)
+
+
+def build_raw_cache(seed: int, bs: int, heads: int, n_retrieval: int, n_near: int, device, n_sink: int = 0,
+                    slab: int = 4096) -> RawCache:
+    """Synthetic tokens laid out as the reference's unified cache: sink rows
+    [0, n_sink), retrieval rows [n_sink, n_sink + n_retrieval) (16-token
+    chunks with Quest min/max from the library's encode kernel) and near rows
+    after them.  Keys: N(0,1), 4 outlier channels x10 per head, RoPE at the
+    token position; values N(0,1)."""
+    assert n_retrieval % CHUNK == 0
+    gen = torch.Generator(device=device).manual_seed(seed)
+    chans = outlier_channels(gen, heads, device)
+    n_c = n_retrieval // CHUNK
+    cap = max(1, n_sink + n_retrieval + n_near)
+    keys = torch.empty(bs, heads, cap, HEAD_DIM, dtype=torch.bfloat16, device=device)
+    values = torch.empty_like(keys)
+    cmin = torch.zeros(bs, heads, max(n_c, 1), HEAD_DIM, dtype=torch.bfloat16, device=device)
+    cmax = torch.zeros_like(cmin)
+    valid = torch.zeros(bs, heads, max(n_c, 1), dtype=torch.bool, device=device)
+    packed = torch.empty(bs, heads, max(n_c, 1), 16, 16, dtype=torch.int32, device=device)
+    for t0 in range(0, cap, slab):
+        t1 = min(cap, t0 + slab)
+        g2 = torch.Generator(device=device).manual_seed(seed * 1000003 + t0)
+        keys[:, :, t0:t1] = synth_keys(g2, bs, heads, t1 - t0, device, pos0=t0, channels=chans)
+        values[:, :, t0:t1] = synth_values(g2, bs, heads, t1 - t0, device)
+    if n_c:
+        ops.kivi_encode_chunks(keys[:, :, n_sink:n_sink + n_retrieval], cmin, cmax, None, valid, packed, 0)
+    del packed
+    return RawCache(cmin, cmax, valid, keys, values, n_sink, n_c, n_sink + n_retrieval, n_near)
+
+
+def raw_algorithmic_bytes(rows: int, n_c: int, nk: int, n_raw: int, G: int = 4) -> int:
+    """Compulsory HBM bytes of one raw page-mode launch: Quest min/max of all
+    chunks (512 B each) + the selected pages' raw K and V rows (16 x 512 B)
+    + the sink / near raw rows (512 B each) + q in / out (bf16)."""
+    per_row = n_c * 512 + nk * 16 * 512 + n_raw * 512 + 2 * G * HEAD_DIM * 2
+    return rows * per_row
+
+
 def page_algorithmic_bytes(rows: int, n_c: int, nk: int, n_near: int, G: int = 4) -> int:
     """Compulsory HBM bytes of one page-mode decode launch: Quest min/max of
     all chunks + selected pages (K codes 1 KiB, V codes 1 KiB, V scale/zero
