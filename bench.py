@@ -63,12 +63,17 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
-def config(n_gpus):
-    return {"workload": "config1: Qwen3-8B-shape sparse decode step (page mode)", "layers": LAYERS,
-            "global_batch": BATCH * n_gpus, "kv_heads_per_gpu": KV_HEADS // n_gpus, "q_heads": Q_HEADS,
-            "head_dim": HEAD_DIM, "context": CONTEXT, "page": PAGE, "budget_tokens": BUDGET, "residual": RESIDUAL,
-            "kivi_bits": 4, "value_group": 32, "parallelism": f"kv-head shard x{n_gpus}",
-            "l2": "inputs per step ~3.4 GB (36 distinct layers) >> L2 126 MB (no flush needed)"}
+def config(n_gpus, mode="raw"):
+    names = {"raw": "config1: Qwen3-8B-shape sparse decode step, page mode over the selected pages' raw bf16 rows",
+             "page4": "config1: Qwen3-8B-shape sparse decode step, page mode over 4-bit KIVI K/V pages (lossy)"}
+    c = {"workload": names[mode], "layers": LAYERS,
+         "global_batch": BATCH * n_gpus, "kv_heads_per_gpu": KV_HEADS // n_gpus, "q_heads": Q_HEADS,
+         "head_dim": HEAD_DIM, "context": CONTEXT, "page": PAGE, "budget_tokens": BUDGET, "residual": RESIDUAL,
+         "parallelism": f"kv-head shard x{n_gpus}",
+         "l2": "inputs per step ~5 GB (36 distinct layers) >> L2 126 MB (no flush needed)"}
+    if mode == "page4":
+        c.update({"kivi_bits": 4, "value_group": 32})
+    return c
 
 
 class ClockSampler:
@@ -121,79 +126,83 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------- CPU arms
-def cpu_sample_layer(seed: int, threads: int):
-    """One layer of page-mode cache built by the oracle's encoder on the host:
-    8 distinct full-size rows (one sequence x 8 KV heads), tiled so every
-    host thread has rows to decode.  Returns the oracle's page-decode inputs."""
+def cpu_raw_layer(seed: int, rows: int):
+    """One layer of the raw-page cache on the host for the oracle: `rows`
+    full-size rows (32,640 retrieval tokens in 2,040 pages + 128 residual
+    rows), keys N(0,1) with 4 outlier channels x10 per row, values N(0,1),
+    Quest min/max from the oracle's encoder.  (RoPE is immaterial to CPU
+    timing; the GPU arm applies it.)"""
+    import torch
     import oracle as O
-    rng = np.random.default_rng(seed)
-    R = KV_HEADS
-    # keys/values drawn directly on the host for the CPU sample (N(0,1), 4
-    # outlier channels x10 per head; RoPE is immaterial to CPU timing)
-    k = rng.standard_normal((R, N_RETRIEVAL + RESIDUAL, HEAD_DIM), dtype=np.float32)
-    for r in range(R):
-        k[r, :, rng.choice(HEAD_DIM, 4, replace=False)] *= 10.0
-    v = rng.standard_normal((R, N_RETRIEVAL + RESIDUAL, HEAD_DIM), dtype=np.float32)
-    kb, vb = O.f32_to_bf16(k), O.f32_to_bf16(v)
-    mn, mx, _, kc = O.kivi_encode_chunks(kb[:, :N_RETRIEVAL])
-    codes, meta = O.vquant_tokens(vb[:, :N_RETRIEVAL])
-    vc, vm = O.page_layout_values(codes, meta)
-    q = O.f32_to_bf16(rng.standard_normal((R, G, HEAD_DIM), dtype=np.float32))
-    near_k = np.ascontiguousarray(kb[:, N_RETRIEVAL:])
-    near_v = np.ascontiguousarray(vb[:, N_RETRIEVAL:])
-    reps = max(1, -(-threads // R))
-    tile = lambda a: np.ascontiguousarray(np.concatenate([a] * reps, axis=0)) if reps > 1 else a
-    d = dict(q=q, mn=mn, mx=mx, kc=kc, vc=vc, vm=vm, near_k=near_k, near_v=near_v)
-    return {k: tile(v) for k, v in d.items()}
+    g = torch.Generator().manual_seed(seed)
+    T = N_RETRIEVAL + RESIDUAL
+    k = torch.randn(rows, T, HEAD_DIM, generator=g)
+    for r in range(rows):
+        k[r, :, torch.randperm(HEAD_DIM, generator=g)[:4]] *= 10.0
+    v = torch.randn(rows, T, HEAD_DIM, generator=g)
+    q = torch.randn(rows, G, HEAD_DIM, generator=g)
+    u16 = lambda t: t.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    kb, vb, qb = u16(k), u16(v), u16(q)
+    del k, v
+    mn, mx, _, _ = O.kivi_encode_chunks(kb[:, :N_RETRIEVAL])
+    return dict(q=qb, mn=mn, mx=mx, keys=kb, values=vb)
 
 
-def cpu_decode(data, threads):
+def cpu_raw_decode(data, threads):
     import oracle as O
     t0 = time.perf_counter()
-    O.page_decode(data["q"], data["mn"], data["mx"], None, data["kc"], data["vc"], data["vm"], data["near_k"],
-                  data["near_v"], N_PAGES, NK, RESIDUAL, 1.0 / HEAD_DIM ** 0.5, threads=threads)
+    O.page_decode_raw(data["q"], data["mn"], data["mx"], None, data["keys"], data["values"], N_PAGES, NK,
+                      near_start=N_RETRIEVAL, n_near=RESIDUAL, threads=threads)
     return time.perf_counter() - t0
 
 
 def cpu_baseline(threads, target_s=12.0):
-    """Time the oracle port of the path on a bounded sample: full-size rows
-    (32k context) of one layer, batch 1 x 8 heads, repeated; extrapolated to
-    the 36-layer step of batch 8 (tokens/s)."""
-    data = cpu_sample_layer(1, threads)
-    rows = data["q"].shape[0]
-    cpu_decode(data, threads)  # warm
+    """The oracle port of the page-mode step (Quest -> top-k -> gather of the
+    selected raw rows -> fp64 softmax attention) on the host cores, timed on a
+    bounded sample: 64 full-size rows (one layer of the batch-8 step) decoded
+    repeatedly; tokens/s = 8 / (36 x the per-layer time)."""
+    data = cpu_raw_layer(1, BATCH * KV_HEADS)
+    cpu_raw_decode(data, threads)  # warm
     times = []
     t_end = time.perf_counter() + target_s
     while time.perf_counter() < t_end or len(times) < 2:
-        times.append(cpu_decode(data, threads))
-    per_row = min(times) / rows
-    step = per_row * BATCH * KV_HEADS * LAYERS
-    return {"value": BATCH / step, "unit": "tokens/s", "cores": min(threads, rows), "kind": "port",
-            "sample": f"oracle page decode of {rows} full-size (32k ctx) rows of one layer x {len(times)} reps, "
-                      f"best rep, scaled to the 36-layer step of batch 8",
+        times.append(cpu_raw_decode(data, threads))
+    step = min(times) * LAYERS
+    return {"value": BATCH / step, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"oracle page decode (raw rows) of one full-size layer (64 rows x 32k ctx), {len(times)} reps, "
+                      f"best rep x 36 layers = one batch-8 step",
             "ms_per_step": step * 1e3}
 
 
 def run_reference(args, n_gpus, rank):
+    """The reference arm: the oracle restatement of the reference's page-mode
+    step on the host cores (all threads).  Each timed step is the work of one
+    GPU's share of the global step -- 36 layers x 64 full-size rows (one
+    layer's data, decoded 36 times) -- so ms_per_step is measured, not
+    extrapolated; tokens/s = 8 tokens per such step."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    data = cpu_sample_layer(1, threads)
-    rows = data["q"].shape[0]
+    data = cpu_raw_layer(1, BATCH * KV_HEADS)
+
+    def one_step():
+        t = 0.0
+        for _ in range(LAYERS):
+            t += cpu_raw_decode(data, threads)
+        return t
+
     for _ in range(args.warmup):
-        cpu_decode(data, threads)
-    times = [cpu_decode(data, threads) for _ in range(args.steps)]
-    per_row = sum(times) / len(times) / rows
-    global_batch = BATCH * n_gpus
-    step_s = per_row * global_batch * KV_HEADS * LAYERS  # the whole job's step on this host
-    value = global_batch / step_s
+        one_step()
+    times = [one_step() for _ in range(args.steps)]
+    step_s = sum(times) / len(times)
+    value = BATCH / step_s
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": n_gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config(n_gpus),
             "impl": "reference",
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": min(threads, rows), "kind": "port",
-                             "sample": f"each step = oracle page decode of {rows} full-size (32k ctx) rows of one "
-                                       "layer, scaled to the 36-layer step of the global batch"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": "each step = 36 x oracle page decode (raw rows) of 64 full-size rows "
+                                       "(32k ctx): one GPU's share of the step, 8 tokens"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -514,6 +523,62 @@ def run_config3(args):
 
 
 # --------------------------------------------------------------------- GPU arm
+def check_timed_launch(args, raw, caches, qs, outs, decode, sel_check, status, stream, dev, n_rows=4):
+    """Parity of the launches the bench timed: for the first and the last
+    layer, one eager call with the same inputs must reproduce the timed
+    output bit for bit and report its selection; sampled rows of both are
+    checked against the oracle (selection bit-exact, output within max-abs
+    2e-2 / mean-rel 1e-2).  Raises if either fails."""
+    import torch
+    import oracle as O
+    res = {"rows_checked": 0, "max_abs": 0.0, "mean_rel": 0.0, "sel_exact": True, "bitwise_repeat": True}
+    for l in sorted({0, len(caches) - 1}):
+        timed = outs[l].clone()
+        eager = torch.empty_like(timed)
+        with torch.cuda.stream(stream):
+            decode(l, qs[l], eager, sel_out=sel_check)
+        torch.cuda.synchronize()
+        if int(status.item()) != 0:
+            raise RuntimeError(f"device status {int(status.item())} in the parity call")
+        res["bitwise_repeat"] &= bool(torch.equal(timed, eager))
+        pc = caches[l]
+        bs, H = qs[l].shape[0], qs[l].shape[2] // G
+        R = bs * H
+        rows = np.linspace(0, R - 1, n_rows).astype(np.int64)
+        ri = torch.as_tensor(rows, device=dev)
+        u16 = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+        qq = u16(qs[l]).reshape(R, G, HEAD_DIM)[rows]
+        mn = u16(pc.chunk_min.reshape(R, -1, HEAD_DIM)[ri])
+        mx = u16(pc.chunk_max.reshape(R, -1, HEAD_DIM)[ri])
+        if raw:
+            cap = pc.keys.shape[2]
+            ro, _, rsel = O.page_decode_raw(qq, mn, mx, None, u16(pc.keys.reshape(R, cap, HEAD_DIM)[ri]),
+                                            u16(pc.values.reshape(R, cap, HEAD_DIM)[ri]), N_PAGES, NK,
+                                            near_start=N_RETRIEVAL, n_near=RESIDUAL, threads=8)
+        else:
+            ro, _, rsel = O.page_decode(qq, mn, mx, None, pc.kcodes.reshape(R, -1, 16, 16)[ri].cpu().numpy(),
+                                        pc.vcodes_t.reshape(R, -1, 128, 2)[ri].cpu().numpy(),
+                                        u16(pc.vmeta.reshape(R, -1, 2, 4, 16)[ri]),
+                                        u16(pc.near_k.reshape(R, -1, HEAD_DIM)[ri]),
+                                        u16(pc.near_v.reshape(R, -1, HEAD_DIM)[ri]), N_PAGES, NK, RESIDUAL,
+                                        1.0 / HEAD_DIM ** 0.5, threads=8)
+        res["sel_exact"] &= bool(np.array_equal(sel_check.cpu().numpy()[rows], rsel))
+        got = O.bf16_to_f32(u16(timed)).reshape(R, G, HEAD_DIM)[rows].astype(np.float64)
+        ref = O.bf16_to_f32(ro).astype(np.float64)
+        err = np.abs(got - ref)
+        res["rows_checked"] += len(rows)
+        res["max_abs"] = max(res["max_abs"], float(err.max()))
+        res["mean_rel"] = max(res["mean_rel"], float(err.mean() / max(np.abs(ref).mean(), 1e-12)))
+    res["tolerance"] = {"max_abs": 2e-2, "mean_rel": 1e-2,
+                        "against": "oracle fp64 softmax over the raw rows of the oracle's selection" if raw else
+                        "oracle restatement of the same 4-bit pages (the lossy variant)"}
+    ok = res["sel_exact"] and res["bitwise_repeat"] and res["max_abs"] <= 2e-2 and res["mean_rel"] <= 1e-2
+    res["ok"] = bool(ok)
+    if not ok:
+        raise RuntimeError(f"parity of the timed launch failed: {res}")
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -525,8 +590,10 @@ def main():
     ap.add_argument("--soak", type=float, default=1.5, help="seconds of load before timing (clock sampling)")
     ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 5],
                     help="5: the offload tier (retrieval zone in host-pinned memory)")
-    ap.add_argument("--mode", default="page", choices=["page", "reference"],
-                    help="config 1 only: page mode (the headline) or the drop-in's default reference mode")
+    ap.add_argument("--mode", default="raw", choices=["raw", "page4", "reference"],
+                    help="config 1 only: raw = page mode over the selected pages' raw bf16 rows (the headline, the "
+                         "reference's page mode); page4 = page mode over 4-bit KIVI K/V pages (lossy variant); "
+                         "reference = the drop-in's default reference mode with production knobs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config == 1 and args.mode == "reference" and args.impl == "ours":
@@ -566,9 +633,13 @@ def main():
     bs = BATCH * n_gpus if KV_HEADS % n_gpus == 0 else BATCH
     rows = bs * heads
     layers = args.layers
+    raw = args.mode == "raw"
     caches, qs, outs = [], [], []
     for l in range(layers):
-        pc, _ = W.build_page_cache(1000 * rank + l, bs, heads, N_RETRIEVAL, RESIDUAL, dev)
+        if raw:
+            pc = W.build_raw_cache(1000 * rank + l, bs, heads, N_RETRIEVAL, RESIDUAL, dev)
+        else:
+            pc, _ = W.build_page_cache(1000 * rank + l, bs, heads, N_RETRIEVAL, RESIDUAL, dev)
         caches.append(pc)
         g = torch.Generator(device=dev).manual_seed(77 + l + 1000 * rank)
         qs.append(W.synth_query(g, bs, heads * G, dev))
@@ -577,10 +648,19 @@ def main():
     layer_structs = [pc.layer() for pc in caches]
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = torch.cuda.Stream(device=dev)
+    ws = torch.zeros(ops.page_decode_raw_ws_bytes(rows, N_PAGES, NK, 0, RESIDUAL), dtype=torch.uint8, device=dev)
+    sel_check = torch.empty(rows, NK, dtype=torch.int64, device=dev)
+
+    def decode(l, q, out, sel_out=None):
+        if raw:
+            ops.page_decode_raw(q, layer_structs[l], N_PAGES, NK, RESIDUAL, near_start=N_RETRIEVAL, out=out,
+                                status=status, workspace=ws, sel_out=sel_out)
+        else:
+            ops.page_decode(q, layer_structs[l], N_PAGES, NK, RESIDUAL, out=out, status=status, sel_out=sel_out)
 
     def step():
         for l in range(layers):
-            ops.page_decode(qs[l], layer_structs[l], N_PAGES, NK, RESIDUAL, out=outs[l], status=status)
+            decode(l, qs[l], outs[l])
 
     with torch.cuda.stream(stream):
         step()  # warm / load
@@ -650,7 +730,7 @@ def main():
         for l in range(layers):
             if l % CH == 0:
                 stream.wait_event(h2d_done[l // CH])
-            ops.page_decode(q_dev[l], layer_structs[l], N_PAGES, NK, RESIDUAL, out=outs[l], status=status)
+            decode(l, q_dev[l], outs[l])
             if l % CH == CH - 1 or l == layers - 1:
                 k_done[l // CH].record(stream)
                 copy_stream.wait_event(k_done[l // CH])
@@ -685,8 +765,13 @@ def main():
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_ms = float(e2e_ms.item())
 
+    parity = check_timed_launch(args, raw, caches, qs, outs, decode, sel_check, status, stream, dev)
+
     peak, peak_kind = load_peaks()
-    bytes_launch = W.page_algorithmic_bytes(rows, N_PAGES, NK, RESIDUAL, G)
+    if raw:
+        bytes_launch = W.raw_algorithmic_bytes(rows, N_PAGES, NK, RESIDUAL, G)
+    else:
+        bytes_launch = W.page_algorithmic_bytes(rows, N_PAGES, NK, RESIDUAL, G)
     launch_s = ms / 1e3 / layers
     achieved = bytes_launch / launch_s / 1e9
     # head-sharded ranks all serve the same global batch; non-divisible N runs replicas
@@ -698,22 +783,23 @@ def main():
     line = {
         "metric": METRIC, "value": tokens_s, "unit": "tokens/s", "n_gpus": n_gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config(n_gpus),
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config(n_gpus, args.mode),
         "hbm_gbs_per_gpu": achieved, "hbm_frac_of_peak": achieved / peak,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "kernel": "page_decode_kernel",
+                     "peak_kind": peak_kind, "kernel": "raw_decode_kernel" if raw else "page_decode_kernel",
                      "bytes_per_launch": bytes_launch, "launch_us": launch_s * 1e6, "traffic": None},
         "e2e": {"value": e2e_tokens, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "mode": "CUDA graph per step: per layer H2D q (pinned) -> ops.page_decode -> D2H out (pinned), "
-                        "copies on a second stream in groups of 6 layers"},
+                "mode": "CUDA graph per step: per layer H2D q (pinned) -> ops.page_decode%s -> D2H out (pinned), "
+                        "copies on a second stream in groups of 6 layers" % ("_raw" if raw else "")},
         "gpu_launches": layers * args.steps,
         "clocks": clk.summary(),
+        "parity": parity,
     }
-    prof = os.path.join(ROOT, "profiles", "page_decode_traffic.json")
+    prof = os.path.join(ROOT, "profiles", "raw_decode_traffic.json" if raw else "page_decode_traffic.json")
     if os.path.exists(prof):
         with open(prof) as f:
             line["roofline"]["traffic"] = json.load(f).get("traffic_bytes_per_launch")
-    if rank == 0 and n_gpus == 1 and not args.no_cpu_baseline:
+    if rank == 0 and n_gpus == 1 and raw and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(os.cpu_count() or 1)
     if world > 1:
         dist.barrier()
