@@ -8,26 +8,28 @@
 // K/V rows + the near window (:1734-1750, attn_hub/flash_attn_compat.py:44-99).
 // This kernel does all of it in one launch with no bf16 K/V copy:
 //
-//  * Work items come from one queue (a global counter), in this order:
-//      phase A, row by row: the row's Quest score tiles (128 chunks, 64 KiB of
-//        min/max each) and the row's attend tiles that hold only raw rows
-//        (sink / near, which need no selection);
-//      phase B, row by row: the attend tiles that hold selected pages.
-//    A CTA takes the next item when it finishes one, so the HBM stream never
-//    waits for a whole-grid phase change.
+//  * Work items (32 KiB of HBM reads each) come from one queue, a global
+//    counter: Quest score tiles (64 chunks of min/max), attend tiles of raw
+//    rows only (sink / near, no selection needed) and attend tiles of
+//    selected pages (4 pages).  The order is skewed by D rows: step s holds
+//    the score and raw tiles of row s, then the page tiles of row s - D, so a
+//    row's selection runs while D later rows are still being scored.
+//  * Each CTA keeps two items in flight: while it computes one item from one
+//    half of its shared-memory region, the TMA loads of its next item fill
+//    the other half.
 //  * The CTA that completes a row's last score tile selects the row's top nk
-//    chunks right away (scores copied to shared memory, block_topk_small /
-//    block_topk) and publishes them with a release flag; the other CTAs keep
-//    streaming meanwhile.  Attend tiles with pages wait (time-bounded) on the
-//    flag; every page tile comes after every score tile in the queue, so the
-//    CTA that will set a flag is always already running.
-//  * An attend tile is 8 entries of 16 tokens; each warp owns 2 page slots.
-//    A page arrives as four 2-D TMA tensor copies (K and V, dims 0-63 and
+//    chunks (scores copied to shared memory, block_topk_small / block_topk)
+//    and publishes them with a release flag.  Page tiles wait (time-bounded)
+//    on the flag.  Every page tile of a row follows every score tile of that
+//    row in the queue, so the blocked item earliest in the queue can always
+//    proceed: the scheme cannot deadlock.
+//  * A page arrives as four 2-D TMA tensor copies (K and V, dims 0-63 and
 //    64-127, 16 rows x 128 B each) with the 128-byte swizzle, and is read with
 //    ldmatrix (K, B operand of S = Q K^T) and ldmatrix.trans (V, A operand of
 //    O^T = V^T P^T) into mma.sync m16n8k16 with an online softmax.
-//  * A tile writes its partial (m, l, o) to the workspace; the CTA that
-//    completes a row's last tile merges the row's partials into out / lse.
+//  * An attend tile writes its partial (m, l, o) to the workspace; the CTA
+//    that completes a row's last attend tile merges the row's partials into
+//    out / lse.
 //  * The last CTA to exit returns every control word to zero, so the next
 //    launch on the same workspace starts clean.
 #include <cuda.h>
@@ -42,13 +44,14 @@ namespace rawpg {
 
 constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
-constexpr int kSlots = 2;                         // page slots per warp
-constexpr int kSlotBytes = 8192;                  // K 2 x 2 KiB + V 2 x 2 KiB
-constexpr int kRegion = kWarps * kSlots * kSlotBytes;  // 64 KiB
-constexpr int kTileEntries = kWarps * kSlots;     // entries per attend tile
-constexpr int kScoreTile = kWarps * kSlots * 16;  // chunks per score tile
+constexpr int kSlotBytes = 8192;                  // one page: K 2 x 2 KiB + V 2 x 2 KiB
+constexpr int kBufBytes = kWarps * kSlotBytes;    // one item in flight: a slot per warp (32 KiB)
+constexpr int kRegion = 2 * kBufBytes;            // two items in flight
+constexpr int kTileEntries = kWarps;              // pages per attend tile
+constexpr int kScoreTile = kWarps * 16;           // chunks per score tile
 constexpr int kPartFloats = 16 + 8 * kHeadDim;    // m[8], l[8], o[8][128]
-constexpr int kMaxChunks = kRegion / 4;           // scores of one row fit the region
+constexpr int kMaxChunks = kBufBytes / 4;         // a row's scores fit one buffer
+constexpr int kMaxTiles = (kBufBytes / 4 - 16) / 8;  // a row's merge weights fit one buffer
 constexpr uint64_t kFlagWaitNs = 2000000000ull;   // selection flag: give up after 2 s
 
 struct Args {
@@ -60,7 +63,7 @@ struct Args {
     const uint8_t* valid;
     int64_t cap, page_base;
     int R, G, n_max, n_c, nk, n_sink, near_start, n_near;
-    int ST, AT, RT, RS, RN, E, n_c_pad, per_row_a;
+    int ST, AT, RT, RS, RN, E, n_c_pad, per_row_a, D;
     uint32_t total;
     float sl2;
     uint16_t* out;
@@ -276,304 +279,404 @@ __device__ __forceinline__ int64_t entry_tokens(const Args& a, int e, int chunk,
     return a.page_base + 16 * (int64_t)chunk;
 }
 
+__device__ __forceinline__ unsigned entry_present(const Args& a, int e) {
+    unsigned pr;
+    entry_tokens(a, e, 0, pr);
+    return pr;
+}
+
+struct Item {
+    int r, tile;
+    bool score;
+};
+
+// Queue position -> work item.  Step s (0 <= s < R + D) holds the per_row_a
+// score / raw-only tiles of row s (s < R) followed by the BT page tiles of row
+// s - D (s >= D).
+__device__ __forceinline__ Item decode_item(const Args& a, uint32_t item) {
+    const uint32_t A = (uint32_t)a.per_row_a, BT = (uint32_t)(a.AT - a.RT), D = (uint32_t)a.D, R = (uint32_t)a.R;
+    const uint32_t n1 = D * A, n2 = (R - D) * (A + BT);
+    Item it;
+    uint32_t j;
+    if (item < n1) {
+        it.r = (int)(item / A);
+        j = item % A;
+    } else if (item < n1 + n2) {
+        const uint32_t i2 = item - n1;
+        const uint32_t s = D + i2 / (A + BT);
+        j = i2 % (A + BT);
+        if (j >= A) {
+            it.r = (int)(s - D);
+            it.tile = a.RT + (int)(j - A);
+            it.score = false;
+            return it;
+        }
+        it.r = (int)s;
+    } else {
+        const uint32_t i3 = item - n1 - n2;
+        it.r = (int)(R - D + i3 / BT);
+        it.tile = a.RT + (int)(i3 % BT);
+        it.score = false;
+        return it;
+    }
+    it.score = (int)j < a.ST;
+    it.tile = it.score ? (int)j : (int)j - a.ST;
+    return it;
+}
+
+struct Smem {
+    uint8_t* region;  // two buffers of kBufBytes, 1024-byte aligned
+    int* hist;
+    int* misc;
+    int* scan;
+    uint16_t* rq;
+    uint64_t* bars;   // [warp][buffer]
+    uint32_t* u;      // [0..2] items, [3] flag, [4] fail, [5] lo, [6] hi, [7] issued, [8] ok
+};
+
+enum { kU_Flag = 3, kU_Fail = 4, kU_Lo = 5, kU_Hi = 6, kU_Issued = 7, kU_Ok = 8 };
+
+// Issue the TMA loads of `item` into buffer b.  Returns false (nothing issued)
+// when the item needs a selection that is not published yet and !blocking,
+// or when a blocking wait for it expired (status set).  CTA-uniform.
+__device__ bool issue_item(const Args& a, const Smem& S, uint32_t item, int b, bool blocking) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const Item it = decode_item(a, item);
+    uint8_t* slot = S.region + b * kBufBytes + warp * kSlotBytes;
+    uint64_t* bar = S.bars + warp * 2 + b;
+    if (it.score) {
+        const int cc = it.tile * kScoreTile + 16 * warp;
+        const int nch = max(0, min(16, a.n_c - cc));
+        if (lane == 0 && nch > 0) {
+            const uint16_t* gmin = a.cmin + ((int64_t)it.r * a.n_max + cc) * kHeadDim;
+            const uint16_t* gmax = a.cmax + ((int64_t)it.r * a.n_max + cc) * kHeadDim;
+            mbar_arrive_expect_tx(bar, (uint32_t)nch * kHeadDim * 2 * 2);
+            bulk_g2s(slot, gmin, nch * kHeadDim * 2, bar);
+            bulk_g2s(slot + 4096, gmax, nch * kHeadDim * 2, bar);
+        }
+        return true;
+    }
+    const int e0 = it.tile * kTileEntries;
+    const int e1 = min(a.E, e0 + kTileEntries);
+    const int pg0 = a.RS + a.RN;
+    if (a.ST > 0 && e1 > pg0) {  // the tile holds selected pages
+        uint32_t* flag = a.ctrl + 2 + 2 * a.R + it.r;
+        if (threadIdx.x == 0) {
+            uint32_t f = ld_acquire(flag);
+            if (!f && blocking) {
+                const uint64_t t0 = globaltimer_ns();
+                while (!(f = ld_acquire(flag))) {
+                    __nanosleep(128);
+                    if (globaltimer_ns() - t0 > kFlagWaitNs) break;
+                }
+                if (!f) {
+                    set_status(a.status, ZKV_ERR_TIMEOUT);
+                    S.u[kU_Fail] = 1u;
+                }
+            }
+            if (f) __threadfence();
+            S.u[kU_Ok] = f ? 1u : 0u;
+        }
+        __syncthreads();
+        const bool ok = S.u[kU_Ok] != 0u;
+        __syncthreads();
+        if (!ok) return false;
+    }
+    const int e = e0 + warp;
+    if (e < e1) {
+        int chunk = 0;
+        if (e >= pg0) {
+            const int p = e - pg0;
+            chunk = a.ST > 0 ? (lane == 0 ? __ldcg(a.sel + (int64_t)it.r * a.nk + p) : 0) : p;
+            chunk = __shfl_sync(0xffffffffu, chunk, 0);
+            // every chunk selected (no select ran): the selection is the identity
+            if (a.ST == 0 && a.sel_out && lane == 0) a.sel_out[(int64_t)it.r * a.nk + p] = p;
+        }
+        unsigned pr;
+        const int64_t y0 = entry_tokens(a, e, chunk, pr);
+        if (lane == 0) {
+            const int y = (int)((int64_t)it.r * a.cap + y0);
+            const uint32_t dst = smem_u32(slot);
+            mbar_arrive_expect_tx(bar, kSlotBytes);
+            tma_load_2d(dst, &a.tk, 0, y, bar);
+            tma_load_2d(dst + 2048, &a.tk, 64, y, bar);
+            tma_load_2d(dst + 4096, &a.tv, 0, y, bar);
+            tma_load_2d(dst + 6144, &a.tv, 64, y, bar);
+        }
+    }
+    return true;
+}
+
+// Select the top nk chunks of row r (its scores are complete) and publish them.
+__device__ void select_row(const Args& a, const Smem& S, int r, float* buf) {
+    const int lane = threadIdx.x & 31;
+    const float* srow = a.scores + (int64_t)r * a.n_c_pad;
+    if (threadIdx.x == 0) {
+        S.u[kU_Lo] = 0xffffffffu;
+        S.u[kU_Hi] = 0u;
+    }
+    __syncthreads();
+    uint32_t klo = 0xffffffffu, khi = 0u;
+    for (int i = 4 * threadIdx.x; i < a.n_c; i += 4 * kThreads) {
+        const float4 f = __ldcg(reinterpret_cast<const float4*>(srow + i));
+        const float fv[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            if (i + e < a.n_c) {
+                buf[i + e] = fv[e];
+                const uint32_t kk = ordered_u32(fv[e]);
+                if (kk > kOrderedNegInf) klo = min(klo, kk);
+                khi = max(khi, kk);
+            }
+        }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        klo = min(klo, __shfl_xor_sync(0xffffffffu, klo, off));
+        khi = max(khi, __shfl_xor_sync(0xffffffffu, khi, off));
+    }
+    if (lane == 0) {
+        atomicMin(&S.u[kU_Lo], klo);
+        atomicMax(&S.u[kU_Hi], khi);
+    }
+    __syncthreads();
+    int32_t* selr = a.sel + (int64_t)r * a.nk;
+    int64_t* selo = a.sel_out ? a.sel_out + (int64_t)r * a.nk : nullptr;
+    auto emit = [&](int pos, int i) {
+        selr[pos] = i;
+        if (selo) selo[pos] = i;
+    };
+    if (a.n_c <= 16 * kThreads)
+        block_topk_small<kThreads>(buf, a.n_c, a.nk, S.u[kU_Lo], S.u[kU_Hi], S.hist, S.misc, S.scan, emit);
+    else
+        block_topk<kThreads, true>([&](int i) { return ordered_u32(buf[i]); }, a.n_c, a.nk, S.hist, S.misc, S.scan,
+                                   emit, true, S.u[kU_Lo], S.u[kU_Hi]);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        st_release(a.ctrl + 2 + 2 * a.R + r, 1u);
+    }
+}
+
+// Merge the AT partials of row r into out / lse (weights staged in `buf`).
+__device__ void merge_row(const Args& a, int r, float* buf) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float* pr = a.parts + (int64_t)r * a.AT * kPartFloats;
+    float* w = buf;                  // [AT][8]
+    float* sL = buf + a.AT * 8;      // [8]
+    float* sM = sL + 8;              // [8]
+    for (int h = warp; h < a.G; h += kWarps) {
+        float M = -INFINITY;
+        for (int t = lane; t < a.AT; t += 32) M = fmaxf(M, __ldcg(pr + (int64_t)t * kPartFloats + h));
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        float L = 0.f;
+        for (int t = lane; t < a.AT; t += 32) {
+            const float* b = pr + (int64_t)t * kPartFloats;
+            const float mt = __ldcg(b + h);
+            const float wt = (mt == -INFINITY) ? 0.f : ex2(mt - M);
+            w[t * 8 + h] = wt;
+            L += wt * __ldcg(b + 8 + h);
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+        if (lane == 0) {
+            sL[h] = L;
+            sM[h] = M;
+        }
+    }
+    __syncthreads();
+    for (int i4 = threadIdx.x; i4 < a.G * (kHeadDim / 4); i4 += kThreads) {
+        const int h = i4 / (kHeadDim / 4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int t = 0; t < a.AT; ++t) {
+            const float wt = w[t * 8 + h];
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(pr + (int64_t)t * kPartFloats + 16) + i4);
+            acc.x += wt * v.x;
+            acc.y += wt * v.y;
+            acc.z += wt * v.z;
+            acc.w += wt * v.w;
+        }
+        const float L = sL[h];
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        uint2 o;
+        o.x = (uint32_t)f2bfbits(acc.x * inv) | ((uint32_t)f2bfbits(acc.y * inv) << 16);
+        o.y = (uint32_t)f2bfbits(acc.z * inv) | ((uint32_t)f2bfbits(acc.w * inv) << 16);
+        *reinterpret_cast<uint2*>(a.out + (int64_t)r * a.G * kHeadDim + 4 * i4) = o;
+        if ((i4 % (kHeadDim / 4)) == 0 && a.lse)
+            a.lse[(int64_t)r * a.G + h] = (L > 0.f) ? (sM[h] + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+    }
+}
+
+// Process `item` whose loads (if `issued`) target buffer b.  `phase` holds
+// the parity bits of this warp's two slot barriers.
+__device__ void process_item(const Args& a, const Smem& S, uint32_t item, int b, bool issued, uint32_t& phase) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const Item it = decode_item(a, item);
+    uint8_t* buf = S.region + b * kBufBytes;
+    uint8_t* slot = buf + warp * kSlotBytes;
+    uint64_t* bar = S.bars + warp * 2 + b;
+    float* buf_f = reinterpret_cast<float*>(buf);
+    const int r = it.r;
+    if (it.score) {
+        // ---------------------------------------------- Quest score tile
+        const int cc = it.tile * kScoreTile + 16 * warp;
+        const int nch = max(0, min(16, a.n_c - cc));
+        {   // GQA-mean query (compute() :1622-1626: fp32 sum in head order / G, bf16)
+            const uint16_t* qr = a.q + (int64_t)r * a.G * kHeadDim;
+            const int d = threadIdx.x;
+            float acc = 0.f;
+            for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, bfbits2f(__ldg(qr + g * kHeadDim + d)));
+            S.rq[d] = f2bfbits(__fdiv_rn(acc, (float)a.G));
+        }
+        __syncthreads();
+        float* srow = a.scores + (int64_t)r * a.n_c_pad;
+        if (nch > 0) {
+            bool ok = issued;
+            if (issued) {
+                ok = mbar_wait(bar, (phase >> b) & 1u, a.status);
+                phase ^= 1u << b;
+            }
+            const int hl = lane & 15, half = lane >> 4;
+            const uint4 qv = *reinterpret_cast<const uint4*>(S.rq + 8 * hl);
+#pragma unroll 4
+            for (int u = 0; u < 8; ++u) {
+                const int lc = 2 * u + half;
+                uint4 mn = make_uint4(0, 0, 0, 0), mx = mn;
+                if (ok && lc < nch) {
+                    mn = *reinterpret_cast<const uint4*>(slot + lc * 256 + 16 * hl);
+                    mx = *reinterpret_cast<const uint4*>(slot + 4096 + lc * 256 + 16 * hl);
+                }
+                const float sc = quest_half(qv, mn, mx);
+                if (hl == 0 && lc < nch) {
+                    const int c = cc + lc;
+                    const bool v = !a.valid || a.valid[(int64_t)r * a.n_max + c];
+                    srow[c] = (ok && v) ? sc : -INFINITY;
+                }
+            }
+            if (!ok && lane == 0) atomicOr(&S.u[kU_Fail], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const uint32_t done = atomicAdd(a.ctrl + 2 + r, 1u);
+            S.u[kU_Flag] = done == (uint32_t)(a.ST - 1);
+            if (S.u[kU_Flag]) __threadfence();
+        }
+        __syncthreads();
+        if (S.u[kU_Flag]) select_row(a, S, r, buf_f);  // the row's last score tile
+        return;
+    }
+    // ---------------------------------------------- attend tile
+    const int e = it.tile * kTileEntries + warp;
+    const bool have = issued && e < min(a.E, it.tile * kTileEntries + kTileEntries);
+    WarpState st;
+    state_init(st, a.q + (int64_t)r * a.G * kHeadDim, a.G);
+    if (have) {
+        const bool landed = mbar_wait(bar, (phase >> b) & 1u, a.status);
+        phase ^= 1u << b;
+        if (landed) {
+            const unsigned present = entry_present(a, e);
+            if (present != 0xffffu) {  // zero the V rows of absent tokens (p = 0 must meet finite V)
+                uint8_t* vs = slot + 4096;
+                for (int i = lane; i < 16 * 16; i += 32) {
+                    const int tkn = i >> 4, box = (i >> 3) & 1, c = i & 7;
+                    if (!((present >> tkn) & 1u))
+                        *reinterpret_cast<uint4*>(vs + box * 2048 + tkn * 128 + c * 16) = make_uint4(0, 0, 0, 0);
+                }
+                __syncwarp();
+            }
+            page_attend(st, smem_u32(slot), present, a.G, a.sl2);
+        } else if (lane == 0) {
+            atomicOr(&S.u[kU_Fail], 1u);
+        }
+    }
+    __syncthreads();
+    float* cm = buf_f + 4224;  // past the warp scratch (4 x 1040 floats)
+    float* cl = cm + 8;
+    float* co = cl + 8;
+    merge_warps(st, a.G, buf_f, cm, cl, co);
+    float* part = a.parts + ((int64_t)r * a.AT + it.tile) * kPartFloats;
+    if (threadIdx.x < 8) {
+        part[threadIdx.x] = (int)threadIdx.x < a.G ? cm[threadIdx.x] : -INFINITY;
+        part[8 + threadIdx.x] = (int)threadIdx.x < a.G ? cl[threadIdx.x] : 0.f;
+    }
+    for (int i = threadIdx.x; i < a.G * kHeadDim / 4; i += kThreads)
+        reinterpret_cast<float4*>(part + 16)[i] = reinterpret_cast<const float4*>(co)[i];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const uint32_t done = atomicAdd(a.ctrl + 2 + a.R + r, 1u);
+        S.u[kU_Flag] = done == (uint32_t)(a.AT - 1);
+        if (S.u[kU_Flag]) __threadfence();
+    }
+    __syncthreads();
+    if (S.u[kU_Flag]) merge_row(a, r, buf_f);  // the row's last attend tile
+}
+
 __global__ void __launch_bounds__(kThreads, 3) raw_decode_kernel(const __grid_constant__ Args a) {
     extern __shared__ uint8_t smem_raw[];
     // the swizzled boxes need a 1024-byte-aligned region
     const uint32_t base_u32 = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
-    uint8_t* region = smem;
-    float* region_f = reinterpret_cast<float*>(region);
-    int* hist = reinterpret_cast<int*>(smem + kRegion);
-    int* misc = hist + 512;
-    int* scan = misc + 8;
-    uint16_t* rq_s = reinterpret_cast<uint16_t*>(scan + 2 * kThreads);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(rq_s + kHeadDim);        // [warps][slots]
-    uint32_t* s_u = reinterpret_cast<uint32_t*>(bars + kWarps * kSlots);  // [0] item [1] flag [2] lo [3] hi [4] fail
+    Smem S;
+    S.region = smem;
+    S.hist = reinterpret_cast<int*>(smem + kRegion);
+    S.misc = S.hist + 512;
+    S.scan = S.misc + 8;
+    S.rq = reinterpret_cast<uint16_t*>(S.scan + 2 * kThreads);
+    S.bars = reinterpret_cast<uint64_t*>(S.rq + kHeadDim);
+    S.u = reinterpret_cast<uint32_t*>(S.bars + kWarps * 2);
 
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kWarps * kSlots; ++i) mbar_init(bars + i, 1);
+        for (int i = 0; i < kWarps * 2; ++i) mbar_init(S.bars + i, 1);
         mbar_fence_init();
-        s_u[4] = 0;
+        S.u[kU_Fail] = 0;
     }
     grid_dep_wait();  // q and the workspace may still be in use by the previous kernel
     uint32_t* ctr_next = a.ctrl;
     uint32_t* ctr_exit = a.ctrl + 1;
-    uint32_t* score_done = a.ctrl + 2;
-    uint32_t* attend_done = score_done + a.R;
-    uint32_t* sel_ready = attend_done + a.R;
-    const uint32_t slot0 = smem_u32(region) + (uint32_t)(warp * kSlots) * kSlotBytes;
-    uint64_t* wbar = bars + warp * kSlots;
-    uint32_t phase = 0;  // bit k: parity of slot k's next completion (warp-uniform)
-
-    if (threadIdx.x == 0) s_u[0] = atomicAdd(ctr_next, 1u);
+    if (threadIdx.x == 0) {
+        S.u[0] = atomicAdd(ctr_next, 1u);
+        S.u[1] = atomicAdd(ctr_next, 1u);
+    }
     __syncthreads();
-    uint32_t nxt = 0;  // thread 0: the claim prefetched for the next iteration
-    for (;;) {
-        const uint32_t item = s_u[0];
-        if (item >= a.total) break;
-        if (threadIdx.x == 0) nxt = atomicAdd(ctr_next, 1u);
-        int r, tile;
-        bool score;
-        if (item < (uint32_t)(a.R * a.per_row_a)) {
-            r = (int)(item / (uint32_t)a.per_row_a);
-            const int j = (int)(item % (uint32_t)a.per_row_a);
-            score = j < a.ST;
-            tile = score ? j : j - a.ST;
-        } else {
-            const int bt = a.AT - a.RT;
-            const uint32_t i2 = item - (uint32_t)(a.R * a.per_row_a);
-            r = (int)(i2 / (uint32_t)bt);
-            tile = a.RT + (int)(i2 % (uint32_t)bt);
-            score = false;
-        }
-        if (score) {
-            // ---------------------------------------------- Quest score tile
-            const int c0 = tile * kScoreTile;
-            const uint16_t* gmin = a.cmin + ((int64_t)r * a.n_max) * kHeadDim;
-            const uint16_t* gmax = a.cmax + ((int64_t)r * a.n_max) * kHeadDim;
-            int nch[kSlots];
-#pragma unroll
-            for (int k = 0; k < kSlots; ++k) {
-                const int cc = c0 + (warp * kSlots + k) * 16;
-                nch[k] = max(0, min(16, a.n_c - cc));
-                if (lane == 0 && nch[k] > 0) {
-                    uint8_t* dst = region + (warp * kSlots + k) * kSlotBytes;
-                    mbar_arrive_expect_tx(wbar + k, (uint32_t)nch[k] * kHeadDim * 2 * 2);
-                    bulk_g2s(dst, gmin + (int64_t)cc * kHeadDim, nch[k] * kHeadDim * 2, wbar + k);
-                    bulk_g2s(dst + 4096, gmax + (int64_t)cc * kHeadDim, nch[k] * kHeadDim * 2, wbar + k);
-                }
-            }
-            // GQA-mean query (compute() :1622-1626: fp32 sum in head order / G, bf16)
-            {
-                const uint16_t* qr = a.q + (int64_t)r * a.G * kHeadDim;
-                const int d = threadIdx.x;
-                float acc = 0.f;
-                for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, bfbits2f(__ldg(qr + g * kHeadDim + d)));
-                rq_s[d] = f2bfbits(__fdiv_rn(acc, (float)a.G));
-            }
-            __syncthreads();
-            const int hl = lane & 15, half = lane >> 4;
-            const uint4 qv = *reinterpret_cast<const uint4*>(rq_s + 8 * hl);
-            float* srow = a.scores + (int64_t)r * a.n_c_pad;
-#pragma unroll
-            for (int k = 0; k < kSlots; ++k) {
-                if (nch[k] == 0) continue;
-                const bool ok = mbar_wait(wbar + k, (phase >> k) & 1u, a.status);
-                phase ^= 1u << k;
-                const uint8_t* src = region + (warp * kSlots + k) * kSlotBytes;
-                const int cc = c0 + (warp * kSlots + k) * 16;
-#pragma unroll 4
-                for (int u = 0; u < 8; ++u) {
-                    const int lc = 2 * u + half;
-                    uint4 mn = make_uint4(0, 0, 0, 0), mx = mn;
-                    if (lc < nch[k]) {
-                        mn = *reinterpret_cast<const uint4*>(src + lc * 256 + 16 * hl);
-                        mx = *reinterpret_cast<const uint4*>(src + 4096 + lc * 256 + 16 * hl);
-                    }
-                    const float sc = quest_half(qv, mn, mx);
-                    if (hl == 0 && lc < nch[k]) {
-                        const int c = cc + lc;
-                        const bool v = !a.valid || a.valid[(int64_t)r * a.n_max + c];
-                        srow[c] = (ok && v) ? sc : -INFINITY;
-                    }
-                }
-                if (!ok && lane == 0) atomicOr(&s_u[4], 1u);
-            }
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                __threadfence();
-                const uint32_t done = atomicAdd(score_done + r, 1u);
-                s_u[1] = done == (uint32_t)(a.ST - 1);
-                if (s_u[1]) __threadfence();
-            }
-            __syncthreads();
-            if (s_u[1]) {
-                // ------------------------------------------ select (last score tile of row r)
-                if (threadIdx.x == 0) {
-                    s_u[2] = 0xffffffffu;
-                    s_u[3] = 0u;
-                }
-                __syncthreads();
-                uint32_t klo = 0xffffffffu, khi = 0u;
-                for (int i = 4 * threadIdx.x; i < a.n_c; i += 4 * kThreads) {
-                    const float4 f = __ldcg(reinterpret_cast<const float4*>(srow + i));
-                    const float fv[4] = {f.x, f.y, f.z, f.w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        if (i + e < a.n_c) {
-                            region_f[i + e] = fv[e];
-                            const uint32_t kk = ordered_u32(fv[e]);
-                            if (kk > kOrderedNegInf) klo = min(klo, kk);
-                            khi = max(khi, kk);
-                        }
-                    }
-                }
-#pragma unroll
-                for (int off = 16; off >= 1; off >>= 1) {
-                    klo = min(klo, __shfl_xor_sync(0xffffffffu, klo, off));
-                    khi = max(khi, __shfl_xor_sync(0xffffffffu, khi, off));
-                }
-                if (lane == 0) {
-                    atomicMin(&s_u[2], klo);
-                    atomicMax(&s_u[3], khi);
-                }
-                __syncthreads();
-                int32_t* selr = a.sel + (int64_t)r * a.nk;
-                int64_t* selo = a.sel_out ? a.sel_out + (int64_t)r * a.nk : nullptr;
-                auto emit = [&](int pos, int i) {
-                    selr[pos] = i;
-                    if (selo) selo[pos] = i;
-                };
-                if (a.n_c <= 16 * kThreads)
-                    block_topk_small<kThreads>(region_f, a.n_c, a.nk, s_u[2], s_u[3], hist, misc, scan, emit);
-                else
-                    block_topk<kThreads, true>([&](int i) { return ordered_u32(region_f[i]); }, a.n_c, a.nk, hist,
-                                               misc, scan, emit, true, s_u[2], s_u[3]);
-                __syncthreads();
-                if (threadIdx.x == 0) {
-                    __threadfence();
-                    st_release(sel_ready + r, 1u);
-                }
-            }
-        } else {
-            // ---------------------------------------------- attend tile
-            const int e0 = tile * kTileEntries;
-            const int e1 = min(a.E, e0 + kTileEntries);
-            const int pg0 = a.RS + a.RN;  // first page entry
-            bool ok = true;
-            if (a.ST > 0 && e1 > pg0) {   // the tile holds selected pages: wait for the selection
-                if (threadIdx.x == 0) {
-                    uint32_t f = ld_acquire(sel_ready + r);
-                    if (!f) {
-                        const uint64_t t0 = globaltimer_ns();
-                        while (!(f = ld_acquire(sel_ready + r))) {
-                            __nanosleep(128);
-                            if (globaltimer_ns() - t0 > kFlagWaitNs) break;
-                        }
-                    }
-                    if (!f) {
-                        set_status(a.status, ZKV_ERR_TIMEOUT);
-                        s_u[4] = 1u;
-                    }
-                    __threadfence();
-                }
-                __syncthreads();
-                ok = s_u[4] == 0u;
-            }
-            unsigned present[kSlots] = {0u, 0u};
-            bool have[kSlots] = {false, false};
-#pragma unroll
-            for (int k = 0; k < kSlots; ++k) {
-                const int e = e0 + warp * kSlots + k;
-                have[k] = ok && e < e1;
-                if (!have[k]) continue;
-                int chunk = 0;
-                if (e >= pg0) {
-                    const int p = e - pg0;
-                    chunk = a.ST > 0 ? (lane == 0 ? __ldcg(a.sel + (int64_t)r * a.nk + p) : 0) : p;
-                    chunk = __shfl_sync(0xffffffffu, chunk, 0);
-                    // every chunk selected (no select ran): the selection is the identity
-                    if (a.ST == 0 && a.sel_out && lane == 0) a.sel_out[(int64_t)r * a.nk + p] = p;
-                }
-                unsigned pr;
-                const int64_t y0 = entry_tokens(a, e, chunk, pr);
-                present[k] = pr;
-                if (lane == 0) {
-                    const int y = (int)((int64_t)r * a.cap + y0);
-                    const uint32_t dst = slot0 + (uint32_t)k * kSlotBytes;
-                    mbar_arrive_expect_tx(wbar + k, kSlotBytes);
-                    tma_load_2d(dst, &a.tk, 0, y, wbar + k);
-                    tma_load_2d(dst + 2048, &a.tk, 64, y, wbar + k);
-                    tma_load_2d(dst + 4096, &a.tv, 0, y, wbar + k);
-                    tma_load_2d(dst + 6144, &a.tv, 64, y, wbar + k);
-                }
-            }
-            WarpState st;
-            state_init(st, a.q + (int64_t)r * a.G * kHeadDim, a.G);
-#pragma unroll
-            for (int k = 0; k < kSlots; ++k) {
-                if (!have[k]) continue;
-                const bool landed = mbar_wait(wbar + k, (phase >> k) & 1u, a.status);
-                phase ^= 1u << k;
-                if (!landed) {
-                    if (lane == 0) atomicOr(&s_u[4], 1u);
-                    continue;
-                }
-                const uint32_t slot = slot0 + (uint32_t)k * kSlotBytes;
-                if (present[k] != 0xffffu) {  // zero the V rows of absent tokens (p = 0 must meet finite V)
-                    uint8_t* vs = region + (warp * kSlots + k) * kSlotBytes + 4096;
-                    for (int i = lane; i < 16 * 16; i += 32) {
-                        const int tkn = i >> 4, box = (i >> 3) & 1, c = i & 7;
-                        if (!((present[k] >> tkn) & 1u))
-                            *reinterpret_cast<uint4*>(vs + box * 2048 + tkn * 128 + c * 16) = make_uint4(0, 0, 0, 0);
-                    }
-                    __syncwarp();
-                }
-                page_attend(st, slot, present[k], a.G, a.sl2);
-            }
-            __syncthreads();
-            float* cm = region_f + 8192;  // past the warp scratch
-            float* cl = cm + 8;
-            float* co = cl + 8;
-            merge_warps(st, a.G, region_f, cm, cl, co);
-            float* part = a.parts + ((int64_t)r * a.AT + tile) * kPartFloats;
-            if (threadIdx.x < 8) {
-                part[threadIdx.x] = threadIdx.x < a.G ? cm[threadIdx.x] : -INFINITY;
-                part[8 + threadIdx.x] = threadIdx.x < a.G ? cl[threadIdx.x] : 0.f;
-            }
-            for (int i = threadIdx.x; i < a.G * kHeadDim / 4; i += kThreads)
-                reinterpret_cast<float4*>(part + 16)[i] = reinterpret_cast<const float4*>(co)[i];
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                __threadfence();
-                const uint32_t done = atomicAdd(attend_done + r, 1u);
-                s_u[1] = done == (uint32_t)(a.AT - 1);
-                if (s_u[1]) __threadfence();
-            }
-            __syncthreads();
-            if (s_u[1]) {
-                // ------------------------------------------ row merge (last attend tile of row r)
-                const float* pr = a.parts + (int64_t)r * a.AT * kPartFloats;
-                for (int i = threadIdx.x; i < a.G * kHeadDim; i += kThreads) {
-                    const int h = i / kHeadDim;
-                    float M = -INFINITY;
-                    for (int t = 0; t < a.AT; ++t) M = fmaxf(M, __ldcg(pr + t * kPartFloats + h));
-                    float Ls = 0.f, O = 0.f;
-                    for (int t = 0; t < a.AT; ++t) {
-                        const float* b = pr + t * kPartFloats;
-                        const float mt = __ldcg(b + h);
-                        const float wt = (mt == -INFINITY) ? 0.f : ex2(mt - M);
-                        Ls += wt * __ldcg(b + 8 + h);
-                        O += wt * __ldcg(b + 16 + i);
-                    }
-                    a.out[(int64_t)r * a.G * kHeadDim + i] = f2bfbits(Ls > 0.f ? O / Ls : 0.f);
-                    if ((i % kHeadDim) == 0 && a.lse)
-                        a.lse[(int64_t)r * a.G + h] =
-                            (Ls > 0.f) ? (M + __log2f(Ls)) * 0.69314718055994531f : -INFINITY;
-                }
-            }
-        }
-        // order this item's generic reads / writes of the region before the
-        // next item's TMA writes into it
+    uint32_t phase = 0;  // bit b: parity of this warp's buffer-b barrier (warp-uniform)
+    uint32_t cur = S.u[0], nxt = S.u[1];
+    int b = 0;
+    bool cur_issued = cur < a.total ? issue_item(a, S, cur, 0, true) : false;
+    while (cur < a.total) {
+        uint32_t after = 0;  // thread 0: the claim after `nxt`
+        if (threadIdx.x == 0) after = atomicAdd(ctr_next, 1u);
+        // the next item's loads go out before this item is computed (page
+        // tiles only once their row's selection is published)
+        const bool nxt_issued = nxt < a.total ? issue_item(a, S, nxt, b ^ 1, false) : false;
+        process_item(a, S, cur, b, cur_issued, phase);
+        // order this item's generic accesses to buffer b before later TMA writes into it
         fence_proxy_async();
         __syncthreads();
-        if (threadIdx.x == 0) s_u[0] = nxt;
+        if (threadIdx.x == 0) S.u[2] = after;
         __syncthreads();
+        cur = nxt;
+        nxt = S.u[2];
+        b ^= 1;
+        cur_issued = nxt_issued;
+        if (cur < a.total && !cur_issued) cur_issued = issue_item(a, S, cur, b, true);
     }
 
     // ------------------------------------------------ exit: the last CTA resets the control words
     grid_dep_launch_next();
     if (threadIdx.x == 0) {
-        if (s_u[4]) set_status(a.status, ZKV_ERR_TIMEOUT);
+        if (S.u[kU_Fail]) set_status(a.status, ZKV_ERR_TIMEOUT);
         __threadfence();
         const uint32_t gone = atomicAdd(ctr_exit, 1u);
-        s_u[1] = gone == gridDim.x - 1;
-        if (s_u[1]) __threadfence();
+        S.u[kU_Flag] = gone == gridDim.x - 1;
+        if (S.u[kU_Flag]) __threadfence();
     }
     __syncthreads();
-    if (s_u[1]) {
-        for (int i = threadIdx.x; i < 3 * a.R; i += kThreads) score_done[i] = 0u;
+    if (S.u[kU_Flag]) {
+        for (int i = threadIdx.x; i < 3 * a.R; i += kThreads) a.ctrl[2 + i] = 0u;
         if (threadIdx.x == 0) {
             *ctr_next = 0u;
             *ctr_exit = 0u;
@@ -615,7 +718,7 @@ static bool encode_rows(CUtensorMap* map, const void* base, int64_t n_tok) {
 }
 
 struct Plan {
-    int ST, AT, RT, RS, RN, E, n_c_pad, per_row_a;
+    int ST, AT, RT, RS, RN, E, n_c_pad, per_row_a, D;
     int64_t total;
     size_t off_scores, off_sel, off_parts, bytes;
 };
@@ -634,6 +737,8 @@ static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near) {
     if (p.RT > p.AT) p.RT = p.AT;
     p.n_c_pad = (n_c + 31) & ~31;
     p.per_row_a = p.ST + p.RT;
+    // queue skew: a row's page tiles follow the scoring of the next D rows
+    p.D = R > 1 ? (R + 1) / 2 : (R > 0 ? 1 : 0);
     p.total = (int64_t)R * (p.ST + p.AT);
     p.off_scores = up256(8 + (size_t)12 * R);
     p.off_sel = p.off_scores + up256((size_t)R * p.n_c_pad * 4);
@@ -643,7 +748,7 @@ static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near) {
 }
 
 static size_t smem_bytes() {
-    return 1024 + kRegion + (512 + 8 + 2 * kThreads) * 4 + kHeadDim * 2 + kWarps * kSlots * 8 + 8 * 4;
+    return 1024 + kRegion + (512 + 8 + 2 * kThreads) * 4 + kHeadDim * 2 + kWarps * 2 * 8 + 16 * 4;
 }
 
 }  // namespace rawpg
@@ -671,10 +776,10 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
     const int64_t cap = L.kv_ld_row / kHeadDim;
     if (L.page_base + 16 * (int64_t)n_c > cap || (int64_t)near_start + n_near > cap || n_sink > cap)
         return ZKV_ERR_ARG;
-    if (n_c > kMaxChunks || nk > 65536 || (int64_t)rows * cap >= (int64_t)1 << 31) return ZKV_ERR_CAPACITY;
+    if (n_c > kMaxChunks || (int64_t)rows * cap >= (int64_t)1 << 31) return ZKV_ERR_CAPACITY;
     const Plan p = make_plan(rows, n_c, nk, n_sink, n_near);
     if (ws_bytes < p.bytes) return ZKV_ERR_ARG;
-    if (p.total >= ((int64_t)1 << 31)) return ZKV_ERR_CAPACITY;
+    if (p.total >= ((int64_t)1 << 31) || p.AT > kMaxTiles) return ZKV_ERR_CAPACITY;
     if (rows == 0) return ZKV_OK;
     if (((uintptr_t)L.keys & 15) || ((uintptr_t)L.values & 15) || ((uintptr_t)L.chunk_min & 15) ||
         ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)q & 3) || ((uintptr_t)workspace & 255))
@@ -705,6 +810,7 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
     a.E = p.E;
     a.n_c_pad = p.n_c_pad;
     a.per_row_a = p.per_row_a;
+    a.D = p.D;
     a.total = (uint32_t)p.total;
     a.sl2 = scale * 1.4426950408889634f;
     a.out = (uint16_t*)out;
