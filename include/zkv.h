@@ -202,9 +202,10 @@ int zkv_reference_select(const void* q, int G, const zkv_ref_layer* layer,
  *   Limit: zkv_reference_select_ws_bytes(rows, n_chunks, nk, n_dense) <=
  *   ZKV_REFERENCE_SELECT_NOALLOC_MAX_BYTES (16 MiB), else ZKV_ERR_CAPACITY
  *   (e.g. 64 rows x 2048 chunks with nk = 816, n_dense = 244 needs ~12 MB).
- *   Setup: the first call on each device looks the buffer's address up
- *   (cudaGetSymbolAddress on the current device, which must be the
- *   stream's device); make that first call before any stream capture.
+ *   Setup: every call looks the buffer's address up (cudaGetSymbolAddress
+ *   on the current device, which must be the stream's device); the first
+ *   call on a device also loads the module there, so make it before any
+ *   stream capture.
  *   Calls that overlap on one device (concurrent streams or host threads)
  *   race on the one buffer: serialise them.  Nothing needs clearing: every
  *   byte the chain reads is written first by the same call.               */
@@ -558,6 +559,14 @@ int zkv_peer_exchange(const zkv_peer_seg* segs, int n_seg,
  * expiry ZKV_ERR_TIMEOUT is written to `status` and the kernel returns.    */
 int zkv_peer_wait(const uint32_t* flags, uint32_t* epoch, int world,
                   int32_t* status, void* stream);
+
+/* Time limit of the peer waits (zkv_peer_wait, zkv_peer_exchange) in ms on
+ * the GPU's global timer, 1..600000 (default 5000), for launches enqueued
+ * after the call.  On expiry the wait records ZKV_ERR_TIMEOUT in `status`
+ * and returns; the ranks' epochs then disagree, so the peer buffers must be
+ * re-created (a new peer group).  No reference counterpart: the reference
+ * exchanges nothing between GPUs on this path.                            */
+int zkv_peer_set_wait_ms(int ms);
 
 #ifdef __cplusplus
 }

@@ -225,6 +225,7 @@ def test_peer_wait_expires_on_a_missing_rank():
     from zoomkv_revision_b200 import _lib
     dev = torch.device("cuda", 0)
     pg = S.PeerGroup(1, 2, G, 64, 8, 1, 0, dev)  # one real buffer; its flag array has room for 8 ranks
+    S.set_peer_wait_ms(300)
     try:
         stream = torch.cuda.current_stream(dev).cuda_stream
         L = _lib.lib()
@@ -235,13 +236,16 @@ def test_peer_wait_expires_on_a_missing_rank():
         torch.cuda.synchronize()
         waited = time.perf_counter() - t0
         assert int(pg.status.item()) == _lib.ZKV_ERR_TIMEOUT
-        assert waited < 30.0
+        assert 0.25 < waited < 30.0, f"waited {waited:.3f} s; the limit was 0.3 s on the GPU timer"
+        with pytest.raises(RuntimeError, match="rebuilt"):
+            pg.check()
         # the context is still usable: a normal world-1 step afterwards succeeds
         pg.status.zero_()
         x = torch.arange(16, device=dev, dtype=torch.float32)
         torch.cuda.synchronize()
         assert float(x.sum().item()) == 120.0
     finally:
+        S.set_peer_wait_ms(5000)
         pg.close()
 
 

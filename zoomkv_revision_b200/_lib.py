@@ -91,6 +91,7 @@ _SIGNATURES = {
     "zkv_peer_exchange": [ctypes.POINTER(ZkvPeerSeg), _i32, ctypes.POINTER(_c_void_p), _i64, _i32, _i32, _c_void_p,
                           _c_void_p, _i32, _c_void_p, _c_void_p],
     "zkv_peer_wait": [_c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p],
+    "zkv_peer_set_wait_ms": [_i32],
     "zkv_h2d_gather_kv": [_c_void_p, _c_void_p, _i32, _i64, _c_void_p, _i64, _i32, _i64, _c_void_p, _c_void_p, _i64,
                           _i64, _c_void_p, _c_void_p],
     "zkv_h2d_gather_kv_packed": [_c_void_p, _c_void_p, _i32, _i64, _c_void_p, _c_void_p, _c_void_p, _i32, _i32,

@@ -106,6 +106,15 @@ __device__ __forceinline__ uint32_t ordered_u32(float x) {
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// ------------------------------------------------------------ time
+// Nanoseconds of the GPU's global timer: bounds waits by time rather than by
+// a count of polls (a sleeping poll can return early or late).
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 // ------------------------------------------------------------ status
 __device__ __forceinline__ void set_status(int32_t* status, int code) {
     if (status) atomicExch(status, code);

@@ -18,11 +18,15 @@
 //
 // The epoch lives in device memory and only the wait advances it, so a
 // captured CUDA graph replays correctly.  Every rank runs the same sequence
-// of puts and waits, so epochs agree across ranks.  A wait gives up after
-// kMaxPolls polls (well under a second of sleeping polls), records
-// ZKV_ERR_TIMEOUT in the status word and returns, so a rank that never
-// arrives ends in a host-side error, not a hung GPU.  No TMA and no
-// multicast are used: the copies are 16- or 4-byte thread stores.
+// of puts and waits, so epochs agree across ranks.  A wait gives up after a
+// time limit on the GPU's global timer (5 s unless zkv_peer_set_wait_ms
+// says otherwise; the limit is read when a launch is enqueued, so a
+// captured graph keeps the limit of its capture), records ZKV_ERR_TIMEOUT in
+// the status word and returns, so a rank that never arrives ends in a
+// host-side error, not a hung GPU.  After a timeout the epochs of the ranks
+// no longer agree: the peer group must be rebuilt.  No TMA and no multicast
+// are used: the copies are 16- or 4-byte thread stores.
+#include <atomic>
 #include <cstring>
 
 #include "zkv_common.cuh"
@@ -52,7 +56,10 @@ struct PutArgs {
     int32_t* status;
     int world;
     int chunks;                  // CTAs per peer
+    uint64_t wait_ns;            // exchange form: give up waiting after this long
 };
+
+std::atomic<uint64_t> g_wait_ns{5000000000ull};
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -120,10 +127,10 @@ __global__ void __launch_bounds__(kPutThreads) peer_put_kernel(const PutArgs a) 
             *a.done = 0u;
             if (a.wait_flags) {  // exchange form: this CTA also waits for every rank's put
                 bool ok = true;
+                const uint64_t t0 = globaltimer_ns();
                 for (int q = 0; q < a.world && ok; ++q) {
-                    uint32_t polls = 0;
                     while ((int32_t)(ld_acquire_sys(a.wait_flags + q) - target) < 0) {
-                        if (++polls > kMaxPolls) {
+                        if (globaltimer_ns() - t0 > a.wait_ns) {
                             ok = false;
                             break;
                         }
@@ -137,14 +144,15 @@ __global__ void __launch_bounds__(kPutThreads) peer_put_kernel(const PutArgs a) 
     }
 }
 
-__global__ void peer_wait_kernel(const uint32_t* flags, uint32_t* epoch, int world, int32_t* status) {
+__global__ void peer_wait_kernel(const uint32_t* flags, uint32_t* epoch, int world, int32_t* status,
+                                 uint64_t wait_ns) {
     const int lane = threadIdx.x;
     const uint32_t target = *epoch + 1u;
     bool ok = true;
     if (lane < world) {
-        uint32_t polls = 0;
+        const uint64_t t0 = globaltimer_ns();
         while ((int32_t)(ld_acquire_sys(flags + lane) - target) < 0) {
-            if (++polls > kMaxPolls) {
+            if (globaltimer_ns() - t0 > wait_ns) {
                 ok = false;
                 break;
             }
@@ -235,6 +243,7 @@ static int peer_put_launch(const zkv_peer_seg* segs, int n_seg, void* const* pee
     a.status = status;
     a.world = world;
     a.chunks = chunks > 0 ? chunks : (world <= 2 ? 8 : 2);
+    a.wait_ns = g_wait_ns.load();
     peer_put_kernel<<<world * a.chunks, kPutThreads, 0, (cudaStream_t)stream>>>(a);
     return launch_status();
 }
@@ -252,6 +261,12 @@ extern "C" int zkv_peer_exchange(const zkv_peer_seg* segs, int n_seg, void* cons
 
 extern "C" int zkv_peer_wait(const uint32_t* flags, uint32_t* epoch, int world, int32_t* status, void* stream) {
     if (!flags || !epoch || world < 1 || world > kMaxPeers) return ZKV_ERR_ARG;
-    peer_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flags, epoch, world, status);
+    peer_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flags, epoch, world, status, g_wait_ns.load());
     return launch_status();
+}
+
+extern "C" int zkv_peer_set_wait_ms(int ms) {
+    if (ms < 1 || ms > 600000) return ZKV_ERR_ARG;
+    g_wait_ns.store((uint64_t)ms * 1000000ull);
+    return ZKV_OK;
 }

@@ -137,26 +137,19 @@ extern "C" int zkv_reference_select(const void* q, int G, const zkv_ref_layer* L
 // decode loops that must not call cudaMalloc (it can synchronise the device).
 static __device__ __align__(256) uint8_t g_ref_select_ws[ZKV_REFERENCE_SELECT_NOALLOC_MAX_BYTES];
 
-#include <mutex>
-
 namespace {
-constexpr int kMaxDevices = 64;
-std::mutex g_ws_mutex;
-void* g_ws_addr[kMaxDevices] = {};
-
-// Address of g_ref_select_ws on the current device, looked up once per
-// device (cudaGetSymbolAddress with that device current); NULL on failure.
-void* noalloc_workspace(int dev) {
-    std::lock_guard<std::mutex> lock(g_ws_mutex);
-    if (!g_ws_addr[dev]) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_ref_select_ws) != cudaSuccess) {
-            cudaGetLastError();
-            return nullptr;
-        }
-        g_ws_addr[dev] = p;
+// Address of g_ref_select_ws on the current device (cudaGetSymbolAddress with
+// that device current), looked up on every call: after cudaDeviceReset or a
+// re-created primary context the module instance and its address change, so
+// a cached address could point at memory that no longer exists.  NULL on
+// failure.
+void* noalloc_workspace() {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_ref_select_ws) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
     }
-    return g_ws_addr[dev];
+    return p;
 }
 }  // namespace
 
@@ -164,9 +157,7 @@ extern "C" int zkv_reference_select_noalloc(const void* q, int G, const zkv_ref_
                                             int n_chunks, int n_valid_chunks, int nk, int n_dense, int dense_topk,
                                             int sparse_topk, int k, const int64_t* skipped, int64_t sk_ld, int sk,
                                             int64_t* final_out, int64_t final_ld, void* raw_q_out, void* stream) {
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return ZKV_ERR_LAUNCH;
-    void* ws = noalloc_workspace(dev);
+    void* ws = noalloc_workspace();
     if (!ws) return ZKV_ERR_LAUNCH;
     // sizes beyond the buffer come back as ZKV_ERR_CAPACITY from the chain
     return zkv_reference_select(q, G, L, rows, n_max, n_chunks, n_valid_chunks, nk, n_dense, dense_topk, sparse_topk,

@@ -272,6 +272,16 @@ class PeerGroup:
         _lib.check(_lib.lib().zkv_peer_wait(flags, self.epoch, self.world, self.status.data_ptr(), stream),
                    "zkv_peer_wait")
 
+    def check(self):
+        """Raise if a peer wait of this group gave up (a rank did not arrive
+        within the wait limit, zkv_peer_set_wait_ms).  Reads the status word,
+        so it synchronises with the group's stream work.  After a timeout the
+        ranks' epochs disagree: close this group and build a new one."""
+        st = int(self.status.item())
+        if st != 0:
+            raise RuntimeError(f"peer exchange failed: status {st} ({_lib.lib().zkv_status_string(st).decode()}); "
+                               "the peer group must be rebuilt")
+
     def close(self):
         """Unmap the peers and free the own buffer (after a barrier, so no
         peer still writes into it)."""
@@ -290,13 +300,18 @@ class PeerGroup:
 
 
 def decode_step_p2p(q, layer: ops.PageLayer, pg: PeerGroup, *, n_sink: int = 0, near_start: int = 0,
-                    n_near: int = 0):
+                    n_near: int = 0, check: bool = True):
     """decode_step over peer memory: score own pages -> put scores into every
     peer's score row -> wait -> select + attend the own selected pages in one
     kernel (zkv_page_decode_scored, P clusters per row) -> put the P partial
     (out, lse) into every peer -> wait -> LSE merge of all world*P partials.
     Returns the merged output [bs, 1, H*G, 128] bf16 (same on every rank)
-    and the selected global page ids [bs, H, nk]."""
+    and the selected global page ids [bs, H, nk].
+
+    check: raise (PeerGroup.check) when a peer wait of this step gave up
+    instead of returning a merge of stale partials; it synchronises the
+    stream once per step, and is skipped while the stream is being captured
+    into a CUDA graph (check the group after replaying the graph)."""
     stream = torch.cuda.current_stream(q.device).cuda_stream
     if pg.n_loc > 0:
         cmin, cmax, valid = layer.tensors[0], layer.tensors[1], layer.tensors[2]
@@ -308,4 +323,11 @@ def decode_step_p2p(q, layer: ops.PageLayer, pg: PeerGroup, *, n_sink: int = 0, 
                            sel_out=pg.sel, status=pg.status)
     pg._exchange(pg._seg_parts, 2, _FLAGS_B, stream)
     ops.lse_merge_n(pg.parts, pg.lses, pg.out.view(-1, 128))
+    if check and not torch.cuda.is_current_stream_capturing():
+        pg.check()
     return pg.out, pg.sel
+
+
+def set_peer_wait_ms(ms: int) -> None:
+    """Time limit of the peer waits for launches enqueued from now on."""
+    _lib.check(_lib.lib().zkv_peer_set_wait_ms(int(ms)), "zkv_peer_set_wait_ms")
