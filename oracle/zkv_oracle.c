@@ -44,6 +44,32 @@ uint16_t orc_kivi_scale(uint16_t mn, uint16_t mx) {
     return bdiv(bsub(mx, mn), orc_f2bf(15.0f));
 }
 
+/* a*b + c on bf16 operands with ONE rounding to bf16 (round to nearest
+ * even), i.e. a bf16 fused multiply-add.  The exact value is formed in
+ * double (a*b is exact there), narrowed to binary32 with round-to-odd (so
+ * the final rounding sees every discarded bit) and rounded once to bf16. */
+uint16_t orc_bfma(uint16_t a, uint16_t b, uint16_t c) {
+    const double x = fma((double)orc_bf2f(a), (double)orc_bf2f(b), (double)orc_bf2f(c));
+    float f = (float)x;
+    if ((double)f != x) {
+        uint32_t u;
+        memcpy(&u, &f, 4);
+        if (fabs((double)f) > fabs(x)) u -= 1u; /* the neighbour toward zero */
+        u |= 1u;                                /* sticky: round to odd */
+        memcpy(&f, &u, 4);
+    }
+    return orc_f2bf(f);
+}
+
+/* KIVI dequant as the production stage-2 kernel computes it:
+ * bf16(code*scale + mn) with one rounding.  kivi_qk_dot.cu:264-275 writes it
+ * as __hmul2 then __hadd2, but the kernel the reference builds rounds once
+ * (measured bit for bit against that kernel's outputs on a B200:
+ * tests/golden/ref_cuda.npz). */
+uint16_t orc_dequant_fused(int code, uint16_t scale, uint16_t zero) {
+    return orc_bfma(orc_f2bf((float)code), scale, zero);
+}
+
 uint16_t orc_dequant(int code, uint16_t scale, uint16_t zero) {
     /* code*scale then +mn, two bf16 ops, no FMA -- kivi_qk_dot.cu:264-275 */
     return badd(bmul(orc_f2bf((float)code), scale), zero);
@@ -277,8 +303,8 @@ void orc_kivi_qk(const int64_t* chunk_ids, const uint8_t* dense_mask,
                         uint32_t word = (uint32_t)pk[i * chunk + t];
                         for (j = 0; j < 8; ++j) {
                             int d = 8 * i + j;
-                            uint16_t kd = orc_dequant((int)((word >> (4 * j)) & 15u),
-                                                      orc_kivi_scale(cmn[d], cmx[d]), cmn[d]);
+                            uint16_t kd = orc_dequant_fused((int)((word >> (4 * j)) & 15u),
+                                                            orc_kivi_scale(cmn[d], cmx[d]), cmn[d]);
                             uint16_t prod = bmul(kd, raw_q[(size_t)r * D + d]);
                             acc += orc_bf2f(prod);
                         }

@@ -44,6 +44,11 @@ void orc_kivi_encode_chunk(const uint16_t* keys, int64_t ld, int D, int chunk,
 void orc_vquant_token(const uint16_t* v, int D, int group,
                       int32_t* codes, uint16_t* meta);
 
+/* bf16 fused multiply-add a*b + c, one rounding (see zkv_oracle.c).      */
+uint16_t orc_bfma(uint16_t a, uint16_t b, uint16_t c);
+/* KIVI dequant of the production stage-2 kernel: bf16(code*scale + mn),
+ * one rounding (kivi_qk_dot.cu:264-275 as built).                         */
+uint16_t orc_dequant_fused(int code, uint16_t scale, uint16_t zero);
 /* bf16 dequant ladder bf16(bf16(code*scale) + zero); kivi_qk_dot.cu:264-280 */
 uint16_t orc_dequant(int code, uint16_t scale, uint16_t zero);
 /* KIVI key scale bf16(bf16(mx-mn)/15); kivi_qk_dot.cu:213-217 */

@@ -248,12 +248,17 @@ void orc_update_cache_cnt_sorted(const int64_t* sorted_ids, const int32_t* hist,
     free(w);
 }
 
-/* 4-bit RaBitQ rerank score of candidate key idx (rerank.cu:52-143;
- * test_rerank_topk.py python_rabitq_scores:60-111): sequential bf16
- *   dot_b = (((0 + v0*q0) + v1*q1) + ...)      each * and + rounded to bf16
- *   res   = res + dot_b * w_b                   rounded
- *   score = res * |q|                           rounded
- * v_j = +-cen[t_j] (sign bit 3 of the nibble; even dim in the low nibble). */
+/* 4-bit RaBitQ rerank score of candidate key idx as the production kernel
+ * computes it (rerank.cu:52-143): sequential bf16 fused multiply-adds
+ *   dot_b = fma(v7, q7, ... fma(v1, q1, fma(v0, q0, 0)))   one rounding each
+ *   res   = fma(dot_b, w_b, res)                          one rounding
+ *   score = res * |q|                                     rounded
+ * v_j = +-cen[t_j] (sign bit 3 of the nibble; even dim in the low nibble).
+ * The source writes `temp += k * q` and `res += temp * w` on bf16 values;
+ * the kernel the reference builds fuses each into one rounding (measured bit
+ * for bit on a B200: tests/golden/ref_cuda.npz), whereas the Python check
+ * (test_rerank_topk.py python_rabitq_scores:60-111) rounds the product and
+ * the sum separately. */
 void orc_rerank4(const int64_t* cand, int C, const uint8_t* packed, const uint16_t* weight, int64_t cap,
                  const uint16_t* q_blocks, const uint16_t* q_norm, const uint16_t* cen8, int rows,
                  uint16_t* scores) {
@@ -269,9 +274,9 @@ void orc_rerank4(const int64_t* cand, int C, const uint8_t* packed, const uint16
                     const unsigned nib = (p[4 * b + j / 2] >> (4 * (j & 1))) & 0xFu;
                     uint16_t v = cen8[nib & 7u];
                     if (!(nib & 8u)) v ^= 0x8000u;
-                    dot = rb(bf(dot) + bf(rb(bf(v) * bf(q_blocks[(int64_t)r * RQ_D + RQ_M * b + j]))));
+                    dot = orc_bfma(v, q_blocks[(int64_t)r * RQ_D + RQ_M * b + j], dot);
                 }
-                res = rb(bf(res) + bf(rb(bf(dot) * bf(w[b]))));
+                res = orc_bfma(dot, w[b], res);
             }
             scores[(int64_t)r * C + i] = rb(bf(res) * bf(q_norm[r]));
         }

@@ -18,14 +18,16 @@ DEV = "cuda"
 
 
 def set_env(monkeypatch, mode):
-    """mode: 'reference', 'page', or 'host' (reference attention with the
-    retrieval zone in host-pinned memory)."""
+    """mode: 'reference', 'page', 'page4', or 'host' (reference attention
+    with the retrieval zone in host-pinned memory).  Page mode is the
+    reference run with dense_topk = sparse_topk = 16 (every token of a
+    selected chunk survives stage 2)."""
     monkeypatch.setenv("ZKV_HOST_RETRIEVAL", "1" if mode == "host" else "0")
     mode = "reference" if mode == "host" else mode
     env = {"POLAR_QUEST_CHUNK": "16", "POLAR_QUEST_CAND_RATIO": "0.4", "POLAR_QUEST_DYNAMIC_CAND_RATIO": "1",
            "POLAR_QUEST_DYNAMIC_CAND_THRESHOLDS": "5000,10001", "POLAR_QUEST_DYNAMIC_CAND_RATIOS": "0.7,0.5,0.4",
-           "POLAR_CDS_DENSE_RATIO": "0.3", "POLAR_CDS_DENSE_TOPK": "16", "POLAR_CDS_SPARSE_TOPK": "8",
-           "ZKV_ATTENTION_MODE": mode}
+           "POLAR_CDS_DENSE_RATIO": "0.3", "POLAR_CDS_DENSE_TOPK": "16",
+           "POLAR_CDS_SPARSE_TOPK": "16" if mode == "page" else "8", "ZKV_ATTENTION_MODE": mode}
     for k, v in env.items():
         monkeypatch.setenv(k, v)
     monkeypatch.delenv("POLAR_FORCE_CAND_TOKENS", raising=False)
@@ -82,7 +84,7 @@ def close(out, ref):
     assert err.max() <= 2e-2 and err.mean() / np.abs(ref).mean() <= 1e-2, (err.max(), err.mean())
 
 
-@pytest.mark.parametrize("mode", ["reference", "page", "host"])
+@pytest.mark.parametrize("mode", ["reference", "page", "page4", "host"])
 def test_polar_cache_replays_reference_and_matches_oracle(monkeypatch, mode):
     set_env(monkeypatch, mode)
     g = np.load(os.path.join(GOLDEN, "schedule.npz"))
@@ -111,6 +113,12 @@ def test_polar_cache_replays_reference_and_matches_oracle(monkeypatch, mode):
                 vl = to_u16(vals[:, :, :total])
                 if mode in ("reference", "host"):
                     ref, _ = oracle_reference_compute(cache, l, q, kl, vl, cache.final_topk)
+                    close(O.bf16_to_f32(to_u16(out)).reshape(ref.shape), ref)
+                elif mode == "page":
+                    # the reference's own chain with page knobs: final_topk = nk * 16 keeps
+                    # every token of every selected chunk
+                    nk = cache.sched.plan[1]
+                    ref, _ = oracle_reference_compute(cache, l, q, kl, vl, nk * 16)
                     close(O.bf16_to_f32(to_u16(out)).reshape(ref.shape), ref)
                 else:
                     R = bs * H

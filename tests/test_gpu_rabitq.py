@@ -147,7 +147,9 @@ def test_rerank4_matches_reference_scores():
         sc, fin = ops.partial_rerank_cuda(cand.reshape(H, C), lay, from_u16(g[f"c{i}_q_blocks"]).to(DEV).reshape(H, 128),
                                           from_u16(g[f"c{i}_q_norm"]).to(DEV).reshape(H), cen, final_topk=F)
         torch.cuda.synchronize()
-        ref = g[f"c{i}_scores"].reshape(H, C)
+        # the production kernel's scores (bf16 fused multiply-adds), measured
+        # from the reference's own build: tests/golden/ref_cuda.npz
+        ref = golden("ref_cuda.npz")[f"rerank_c{i}"].reshape(H, C)
         assert np.array_equal(to_u16(sc), ref), i
         sel = O.topk_f32(O.bf16_to_f32(ref) + np.float32(0.0), F)
         assert np.array_equal(fin.cpu().numpy(), np.take_along_axis(g[f"c{i}_cand"].reshape(H, C), sel, 1)), i

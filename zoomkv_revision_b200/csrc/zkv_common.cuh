@@ -91,6 +91,8 @@ __device__ __forceinline__ __nv_bfloat162 neg128(__nv_bfloat162 s) {
     return __hmul2_rn(s, bits_bf162_pre(m));
 }
 
+__device__ __forceinline__ __nv_bfloat16 bits_bf16(uint16_t v) { return __ushort_as_bfloat16(v); }
+__device__ __forceinline__ uint16_t bf16_bits(__nv_bfloat16 v) { return __bfloat16_as_ushort(v); }
 __device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
 __device__ __forceinline__ __nv_bfloat162 bits_bf162(uint32_t v) { return *reinterpret_cast<__nv_bfloat162*>(&v); }
 

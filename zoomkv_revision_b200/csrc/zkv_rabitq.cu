@@ -13,8 +13,9 @@
 //                          counts its key range into shared memory and the
 //                          cluster agrees on the top-C threshold through
 //                          distributed shared memory; ordered compaction.
-//  * rerank4_kernel        sequential-bf16 RaBitQ 4-bit scores through a
-//                          per-row product table, then block top-F.
+//  * rerank4_kernel        RaBitQ 4-bit scores as chains of bf16 fused
+//                          multiply-adds (the production rerank.cu as
+//                          built), then block top-F.
 //  * coarse2bit_kernel     six popcounts per block per key.
 //  * popcount_topk_kernel  1-bit x 4-bit popcount estimates, block top-K,
 //                          then exact fp32 inner products of the K winners.
@@ -680,7 +681,7 @@ struct Rerank4Args {
 // rank 0 then selects the top F.
 __global__ void __launch_bounds__(256, 4) rerank4_kernel(const Rerank4Args a) {
     extern __shared__ __align__(16) uint8_t smem[];
-    float* lut = reinterpret_cast<float*>(smem);           // [128 dims][16 nibbles] bf16-valued products
+    float* lut = reinterpret_cast<float*>(smem);           // q row [128] bf16, then the 16 nibble values bf16
     int* hist = reinterpret_cast<int*>(lut + 128 * 16);    // 512
     int* misc = hist + 512;                                // 8
     int* scan = misc + 8;                                  // 512
@@ -697,11 +698,10 @@ __global__ void __launch_bounds__(256, 4) rerank4_kernel(const Rerank4Args a) {
     const int64_t* cr = a.cand + (int64_t)row * a.C;
     for (int i = i0 + tid; i < i1; i += 256) ck[i - i0] = (int)cr[i];
     const uint16_t* qb = a.qb + (int64_t)row * kHeadDim;
-    for (int i = tid; i < 128 * 16; i += 256) {
-        const int d = i >> 4, nib = i & 15;
-        const float v = bfbits2f(a.cen[nib & 7]);
-        lut[i] = rbf(__fmul_rn((nib & 8) ? v : -v, bfbits2f(qb[d])));
-    }
+    __nv_bfloat16* q_s = reinterpret_cast<__nv_bfloat16*>(lut);  // [128]
+    __nv_bfloat16* v_s = q_s + 128;                              // [16]: nibble -> +-cen
+    for (int i = tid; i < 128; i += 256) q_s[i] = bits_bf16(qb[i]);
+    if (tid < 16) v_s[tid] = bits_bf16((tid & 8) ? a.cen[tid & 7] : (uint16_t)(a.cen[tid & 7] ^ 0x8000u));
     __syncthreads();
     cluster.barrier_wait();
     float* sc0 = cluster.map_shared_rank(sc, 0);
@@ -738,16 +738,17 @@ __global__ void __launch_bounds__(256, 4) rerank4_kernel(const Rerank4Args a) {
                 wv[b] = wt[b * a.L.weight_blk + k * a.L.weight_tok];
             }
         }
-        float res = 0.0f;
+        // rerank.cu:118-129 as built: temp = fma(k_j, q_j, temp) and res =
+        // fma(temp, w_b, res), each rounded once to bf16; then res * |q|
+        __nv_bfloat16 res = bits_bf16(0);
 #pragma unroll
         for (int b = 0; b < kB; ++b) {
-            const float* lb = lut + (kM * b) * 16;
-            float dot = rbf(__fadd_rn(0.0f, lb[pw[b] & 0xfu]));
+            __nv_bfloat16 dot = bits_bf16(0);
 #pragma unroll
-            for (int j = 1; j < kM; ++j) dot = rbf(__fadd_rn(dot, lb[j * 16 + ((pw[b] >> (4 * j)) & 0xfu)]));
-            res = rbf(__fadd_rn(res, rbf(__fmul_rn(dot, bfbits2f(wv[b])))));
+            for (int j = 0; j < kM; ++j) dot = __hfma(v_s[(pw[b] >> (4 * j)) & 0xfu], q_s[kM * b + j], dot);
+            res = __hfma(dot, bits_bf16(wv[b]), res);
         }
-        const uint16_t s = f2bfbits(__fmul_rn(res, qn));
+        const uint16_t s = bf16_bits(__hmul(res, bits_bf16(f2bfbits(qn))));
         if (a.scores) a.scores[(int64_t)row * a.C + i] = s;
         sc0[i] = __fadd_rn(bfbits2f(s), 0.0f);  // -0 -> +0 for the selection
     }

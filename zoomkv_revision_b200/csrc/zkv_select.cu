@@ -196,9 +196,13 @@ __global__ void mask_kernel(const int64_t* __restrict__ pos, uint8_t* __restrict
 
 // ----------------------------------------------------------- KIVI stage-2
 // Half-warp per selected chunk, lane = token (as the reference kernel).  The
-// dot product runs over dims 0..127 in order with the bf16 dequant ladder and
-// bf16 products accumulated in fp32 -- bit-identical to kivi_qk_dot.cu.  The
-// 16 lanes are then sorted by (score desc, token asc) with a bitonic network.
+// dot product runs over dims 0..127 in order: the dequant code*scale + min as
+// one bf16 fused multiply-add (one rounding), the product with q rounded to
+// bf16, the sum in fp32 -- bit-identical to the kernel the reference builds
+// from kivi_qk_dot.cu (checked against its outputs, tests/golden/ref_cuda.npz;
+// its source spells the dequant as __hmul2 + __hadd2, which its build fuses).
+// The 16 lanes are then sorted by (score desc, token asc) with a bitonic
+// network.
 __global__ void __launch_bounds__(128) kivi_qk_kernel(const int64_t* __restrict__ ids,
                                                       const uint8_t* __restrict__ dense,
                                                       const int32_t* __restrict__ packed, int n_pk, int pk_ld,
@@ -250,7 +254,8 @@ __global__ void __launch_bounds__(128) kivi_qk_kernel(const int64_t* __restrict_
 #pragma unroll
             for (int p = 0; p < 4; ++p) {
                 const __nv_bfloat162 c2 = codes2_to_bf162(w >> (8 * p), w >> (8 * p + 4));
-                const __nv_bfloat162 k2 = dequant2(c2, bits_bf162(s_sc[local][4 * i + p]), bits_bf162(s_mn[local][4 * i + p]));
+                const __nv_bfloat162 k2 =
+                    __hfma2(c2, bits_bf162(s_sc[local][4 * i + p]), bits_bf162(s_mn[local][4 * i + p]));
                 const __nv_bfloat162 pr = __hmul2_rn(k2, bits_bf162(q2[4 * i + p]));
                 acc = __fadd_rn(acc, __low2float(pr));
                 acc = __fadd_rn(acc, __high2float(pr));

@@ -44,11 +44,17 @@ trans_h2d.cu) and attends [sink + staged] and the near rows of the window.
 The chunk metadata and KIVI codes stay in HBM.
 
 Attention modes (env ZKV_ATTENTION_MODE):
-  "reference" (default)  attention over the raw bf16 rows of the selected
-                         tokens, as the reference does;
-  "page"                 the fused page-mode kernel: Quest top-nk pages
-                         attended with 4-bit K (KIVI) and 4-bit V (group 32)
-                         dequantised in registers + raw sink/near rows.
+  "reference" (default)  the production chain: Quest -> CDS -> KIVI stage 2
+                         -> top final_topk tokens, attention over the raw bf16
+                         rows of the selected tokens, as the reference does;
+  "page"                 the reference's page mode (dense_topk = sparse_topk =
+                         16, final_topk = the page budget): Quest top-nk
+                         chunks, attention over their raw bf16 rows + sink +
+                         near rows, in one persistent launch per layer
+                         (zkv_page_decode_raw);
+  "page4"                a lossy variant of page mode: the selected pages are
+                         read as 4-bit KIVI keys and 4-bit values (group 32),
+                         dequantised in registers (zkv_page_decode).
 
 Chunk size: this build implements the production chunk of 16 tokens
 (POLAR_QUEST_CHUNK=16, run/eval_math_aime.py:216); any other value raises.
@@ -104,8 +110,8 @@ def env_config(final_topk: int = 100) -> dict:
         raise ValueError(f"POLAR_QUEST_CHUNK={cfg['chunk']}: this build implements chunk 16 only")
     if cfg["kivi_bits"] != 4:
         raise ValueError(f"POLAR_KIVI_BITS={cfg['kivi_bits']}: this build implements 4-bit KIVI only")
-    if cfg["attention_mode"] not in ("reference", "page"):
-        raise ValueError(f"ZKV_ATTENTION_MODE must be 'reference' or 'page'; got {cfg['attention_mode']!r}")
+    if cfg["attention_mode"] not in ("reference", "page", "page4"):
+        raise ValueError(f"ZKV_ATTENTION_MODE must be 'reference', 'page' or 'page4'; got {cfg['attention_mode']!r}")
     return cfg
 
 
@@ -323,8 +329,8 @@ class polar_cache:
         if self.host_tier and not enable_offload:
             raise ValueError("ZKV_HOST_RETRIEVAL=1 needs enable_offload=True (the offload zone bookkeeping)")
         if self.host_tier and self.attention_mode != "reference":
-            raise ValueError("the host-pinned retrieval zone serves ZKV_ATTENTION_MODE=reference; page mode reads "
-                             "4-bit pages from HBM and never the raw retrieval rows")
+            raise ValueError("the host-pinned retrieval zone serves ZKV_ATTENTION_MODE=reference; the page modes "
+                             "read their pages from HBM")
         self.sched = CacheSchedule(layer_num, sink_size, local_size, self.dynamic_update_interval, self.input_length,
                                    self.cfg, offload=enable_offload)
         self.context = 0
@@ -361,7 +367,7 @@ class polar_cache:
             self.chunk_centroid.append(torch.zeros(bs, H, nm, D, dtype=torch.bfloat16, **d))
             self.chunk_valid.append(torch.zeros(bs, H, nm, dtype=torch.bool, **d))
             self.kivi_packed.append(torch.zeros(bs, H, nm, 16, 16, dtype=torch.int32, **d))
-            if self.attention_mode == "page":
+            if self.attention_mode == "page4":
                 self.vcodes_t.append(torch.zeros(bs, H, nm, D, 2, dtype=torch.int32, **d))
                 self.vmeta.append(torch.zeros(bs, H, nm, 2, 4, 16, dtype=torch.bfloat16, **d))
                 self.kscale.append(torch.zeros(bs, H, nm, D, dtype=torch.bfloat16, **d))
@@ -381,6 +387,7 @@ class polar_cache:
                 arange=torch.arange(self.cap, dtype=torch.int64, **d),
             )
         self._page_layers = [None] * layer_num
+        self._raw_layers = [None] * layer_num
 
     # ------------------------------------------------------------------ state (reference attribute names)
     @property
@@ -412,7 +419,7 @@ class polar_cache:
     def _encode_range(self, l: int, rows: slice, tok_lo: int, tok_hi: int, src_k=None) -> None:
         """Encode the retrieval-zone tokens [tok_lo, tok_hi) (zone coordinates,
         both multiples of 16) of layer l: chunk min/max/mean + KIVI codes
-        (+ 4-bit values in page mode).  src_k: the keys of exactly those
+        (+ 4-bit values in page4 mode).  src_k: the keys of exactly those
         tokens when they are not read from the HBM cache (offload tier)."""
         if tok_hi <= tok_lo:
             return
@@ -420,8 +427,8 @@ class polar_cache:
         k = self.keys[l][rows, :, s + tok_lo:s + tok_hi] if src_k is None else src_k
         ops.kivi_encode_chunks(k, self.chunk_min[l][rows], self.chunk_max[l][rows], self.chunk_centroid[l][rows],
                                self.chunk_valid[l][rows], self.kivi_packed[l][rows], tok_lo // CHUNK,
-                               kscale=self.kscale[l][rows] if self.attention_mode == "page" else None)
-        if self.attention_mode == "page":
+                               kscale=self.kscale[l][rows] if self.attention_mode == "page4" else None)
+        if self.attention_mode == "page4":
             v = self.values[l][rows, :, s + tok_lo:s + tok_hi]
             ops.vquant_encode(v, self.vcodes_t[l][rows], self.vmeta[l][rows], tok_lo)
 
@@ -596,6 +603,8 @@ class polar_cache:
         n_chunks, nk, n_dense, skipped = self.sched.plan
         n_valid_chunks = valid_length // CHUNK
         if self.attention_mode == "page":
+            return self._compute_page_raw(q, l, n_chunks, nk, total)
+        if self.attention_mode == "page4":
             return self._compute_page(q, l, n_chunks, nk, valid_length, total)
         torch.cuda.nvtx.range_push("stage1_stage2_select")
         k = min(self.final_topk, nk * CHUNK)
@@ -644,9 +653,23 @@ class polar_cache:
         return ops.attn_rows(q, self.win_k[l], self.win_v[l], seg0=(0, min(total, s) + n_h),
                              seg1=(off, off + max(0, total - base)), status=sc["status"])
 
+    def _compute_page_raw(self, q, l, n_chunks, nk, total):
+        """The reference's page mode: Quest top-nk of the encoded chunks, then
+        attention over their raw rows, the sink rows and every row from the
+        first unencoded token on (the skipped tail and the near zone), in one
+        launch (REF:1589-1775 with dense_topk = sparse_topk = 16 and
+        final_topk = nk * 16)."""
+        if self._raw_layers[l] is None:
+            self._raw_layers[l] = ops.RawLayer(self.chunk_min[l], self.chunk_max[l], self.chunk_valid[l],
+                                               self.keys[l], self.values[l], page_base=self.sink_size)
+        s = self.sink_size
+        near_start = s + n_chunks * CHUNK
+        return ops.page_decode_raw(q, self._raw_layers[l], n_chunks, nk, total - near_start, n_sink=s,
+                                   near_start=near_start, status=self._scratch[self._layer_dev[l]]["status"])
+
     def _compute_page(self, q, l, n_chunks, nk, valid_length, total):
-        """Fused page-mode decode over the encoded chunks; the carry tail and
-        the near zone are attended as raw rows."""
+        """Page4 (lossy) decode over the encoded chunks' 4-bit pages; the carry
+        tail and the near zone are attended as raw rows."""
         if self._page_layers[l] is None:
             self._page_layers[l] = ops.PageLayer(self.chunk_min[l], self.chunk_max[l], self.chunk_valid[l],
                                                  self.kivi_packed[l], self.vcodes_t[l], self.vmeta[l], self.keys[l],
