@@ -1,37 +1,30 @@
-// zkv_raw.cu -- page-mode decode over the RAW bf16 rows of the selected pages,
-// one persistent launch per layer.
+// zkv_raw.cu -- page-mode decode over the RAW bf16 rows of the selected pages:
+// two launches per layer chained by programmatic dependent launch.
 //
 // The reference's page mode (polar_cache.compute with dense_topk = sparse_topk
 // = 16 and final_topk = budget, cache_hub/polar_cache_quest_density_single_
 // layer_kivi.py:1589-1775) scores every 16-token chunk with Quest, keeps the
 // top nk chunks and runs flash-attention over sink + the selected chunks' raw
 // K/V rows + the near window (:1734-1750, attn_hub/flash_attn_compat.py:44-99).
-// This kernel does all of it in one launch with no bf16 K/V copy:
+// Here, with no bf16 K/V copy:
 //
-//  * Work items (32 KiB of HBM reads each) come from one queue, a global
-//    counter: Quest score tiles (64 chunks of min/max), attend tiles of raw
-//    rows only (sink / near, no selection needed) and attend tiles of
-//    selected pages (4 pages).  The order is skewed by D rows: step s holds
-//    the score and raw tiles of row s, then the page tiles of row s - D, so a
-//    row's selection runs while D later rows are still being scored.
-//  * Each CTA keeps two items in flight: while it computes one item from one
-//    half of its shared-memory region, the TMA loads of its next item fill
-//    the other half.
-//  * The CTA that completes a row's last score tile selects the row's top nk
-//    chunks (scores copied to shared memory, block_topk_small / block_topk)
-//    and publishes them with a release flag.  Page tiles wait (time-bounded)
-//    on the flag.  Every page tile of a row follows every score tile of that
-//    row in the queue, so the blocked item earliest in the queue can always
-//    proceed: the scheme cannot deadlock.
-//  * A page arrives as four 2-D TMA tensor copies (K and V, dims 0-63 and
-//    64-127, 16 rows x 128 B each) with the 128-byte swizzle, and is read with
-//    ldmatrix (K, B operand of S = Q K^T) and ldmatrix.trans (V, A operand of
-//    O^T = V^T P^T) into mma.sync m16n8k16 with an online softmax.
-//  * An attend tile writes its partial (m, l, o) to the workspace; the CTA
-//    that completes a row's last attend tile merges the row's partials into
-//    out / lse.
-//  * The last CTA to exit returns every control word to zero, so the next
-//    launch on the same workspace starts clean.
+//  * raw_score_kernel: one CTA per (row, 64 chunks).  Bulk copies bring the
+//    chunks' Quest min/max (32 KiB) into shared memory; each half-warp scores
+//    a chunk with the reference kernel's fp32 operation order.  The CTA that
+//    completes a row's scores (a per-row counter) selects the row's top nk
+//    chunks; rows finish in launch order, so most selections overlap the
+//    scoring of later rows.
+//  * raw_attend_kernel: one CTA per (row, 8 entries of 16 tokens): sink and
+//    near rows, then selected pages.  It waits for the score kernel through
+//    griddepcontrol.wait (no flag spinning between grids), brings each page in
+//    as four 2-D TMA tensor copies with the 128-byte swizzle (K and V, dims
+//    0-63 and 64-127) and reads them with ldmatrix (K, B operand of
+//    S = Q K^T) and ldmatrix.trans (V, A operand of O^T = V^T P^T) into
+//    mma.sync m16n8k16 with an online softmax.  The CTA writes its partial
+//    (m, l, o); the CTA that delivers a row's last partial merges the row
+//    into out / lse.
+//  * Every per-row counter is reset by the CTA that completes the row, so the
+//    workspace is ready for the next launch.
 #include <cuda.h>
 
 #include <cstring>
@@ -45,14 +38,14 @@ namespace rawpg {
 constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
 constexpr int kSlotBytes = 8192;                  // one page: K 2 x 2 KiB + V 2 x 2 KiB
-constexpr int kBufBytes = kWarps * kSlotBytes;    // one item in flight: a slot per warp (32 KiB)
-constexpr int kRegion = 2 * kBufBytes;            // two items in flight
-constexpr int kTileEntries = kWarps;              // pages per attend tile
-constexpr int kScoreTile = kWarps * 16;           // chunks per score tile
+constexpr int kSlots = 2;                         // pages per warp of an attend CTA
+constexpr int kTileEntries = kWarps * kSlots;     // pages per attend CTA
+constexpr int kAttRegion = kTileEntries * kSlotBytes;  // 64 KiB
+constexpr int kScoreTile = kWarps * 16;           // chunks per score CTA (32 KiB of min/max)
+constexpr int kScoreRegion = kWarps * kSlotBytes; // 32 KiB
 constexpr int kPartFloats = 16 + 8 * kHeadDim;    // m[8], l[8], o[8][128]
-constexpr int kMaxChunks = kBufBytes / 4;         // a row's scores fit one buffer
-constexpr int kMaxTiles = (kBufBytes / 4 - 16) / 8;  // a row's merge weights fit one buffer
-constexpr uint64_t kFlagWaitNs = 2000000000ull;   // selection flag: give up after 2 s
+constexpr int kMaxChunks = kScoreRegion / 4;      // a row's scores fit the score CTA's region
+constexpr int kMaxTiles = (kAttRegion / 4 - 16) / 16;  // a row's merge weights (m, l) fit the attend region
 
 struct Args {
     CUtensorMap tk;  // raw keys   as [rows * cap][128] bf16, box 64 x 16, 128-B swizzle
@@ -63,28 +56,17 @@ struct Args {
     const uint8_t* valid;
     int64_t cap, page_base;
     int R, G, n_max, n_c, nk, n_sink, near_start, n_near;
-    int ST, AT, RT, RS, RN, E, n_c_pad, per_row_a, D;
-    uint32_t total;
+    int ST, AT, RS, RN, E, n_c_pad;
     float sl2;
     uint16_t* out;
     float* lse;
     int64_t* sel_out;
     int32_t* status;
-    uint32_t* ctrl;  // [0] next item, [1] exited CTAs, then score_done[R], attend_done[R], sel_ready[R]
+    uint32_t* ctrl;  // score_done[R], attend_done[R] (zero between launches)
     float* scores;   // [R][n_c_pad]
     int32_t* sel;    // [R][nk]
     float* parts;    // [R][AT][kPartFloats]
 };
-
-__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
 // 2-D tiled TMA load (no multicast): box (x .. x+63, y .. y+15) -> dst.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -94,6 +76,8 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
+
+__device__ __forceinline__ void fence_acq_rel() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -273,141 +257,79 @@ __device__ __forceinline__ int64_t entry_tokens(const Args& a, int e, int chunk,
     return a.page_base + 16 * (int64_t)chunk;
 }
 
-__device__ __forceinline__ unsigned entry_present(const Args& a, int e) {
-    unsigned pr;
-    entry_tokens(a, e, 0, pr);
-    return pr;
-}
-
-struct Item {
-    int r, tile;
-    bool score;
-};
-
-// Queue position -> work item.  Step s (0 <= s < R + D) holds the per_row_a
-// score / raw-only tiles of row s (s < R) followed by the BT page tiles of row
-// s - D (s >= D).
-__device__ __forceinline__ Item decode_item(const Args& a, uint32_t item) {
-    const uint32_t A = (uint32_t)a.per_row_a, BT = (uint32_t)(a.AT - a.RT), D = (uint32_t)a.D, R = (uint32_t)a.R;
-    const uint32_t n1 = D * A, n2 = (R - D) * (A + BT);
-    Item it;
-    uint32_t j;
-    if (item < n1) {
-        it.r = (int)(item / A);
-        j = item % A;
-    } else if (item < n1 + n2) {
-        const uint32_t i2 = item - n1;
-        const uint32_t s = D + i2 / (A + BT);
-        j = i2 % (A + BT);
-        if (j >= A) {
-            it.r = (int)(s - D);
-            it.tile = a.RT + (int)(j - A);
-            it.score = false;
-            return it;
-        }
-        it.r = (int)s;
-    } else {
-        const uint32_t i3 = item - n1 - n2;
-        it.r = (int)(R - D + i3 / BT);
-        it.tile = a.RT + (int)(i3 % BT);
-        it.score = false;
-        return it;
-    }
-    it.score = (int)j < a.ST;
-    it.tile = it.score ? (int)j : (int)j - a.ST;
-    return it;
-}
-
-struct Smem {
-    uint8_t* region;  // two buffers of kBufBytes, 1024-byte aligned
-    int* hist;
-    int* misc;
-    int* scan;
-    uint16_t* rq;
-    uint64_t* bars;   // [warp][buffer]
-    uint32_t* u;      // [0..2] items, [3] flag, [4] fail, [5] lo, [6] hi, [7] issued, [8] ok
-};
-
-enum { kU_Flag = 3, kU_Fail = 4, kU_Lo = 5, kU_Hi = 6, kU_Issued = 7, kU_Ok = 8 };
-
-// Issue the TMA loads of `item` into buffer b.  Returns false (nothing issued)
-// when the item needs a selection that is not published yet and !blocking,
-// or when a blocking wait for it expired (status set).  CTA-uniform.
-__device__ bool issue_item(const Args& a, const Smem& S, uint32_t item, int b, bool blocking) {
+// ---------------------------------------------------------------- kernel A: scores + select
+// One CTA per (row, tile of 64 chunks).  The CTA that completes a row's last
+// tile selects the row's top nk chunks and resets the row's counter.
+__global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_constant__ Args a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* region = smem;                                   // [4 warps][8 KiB]: min 4 KiB, max 4 KiB
+    float* region_f = reinterpret_cast<float*>(region);
+    int* hist = reinterpret_cast<int*>(smem + kScoreRegion);
+    int* misc = hist + 512;
+    int* scan = misc + 8;
+    uint16_t* rq = reinterpret_cast<uint16_t*>(scan + 2 * kThreads);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(rq + kHeadDim);
+    uint32_t* su = reinterpret_cast<uint32_t*>(bars + kWarps);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const Item it = decode_item(a, item);
-    uint8_t* slot = S.region + b * kBufBytes + warp * kSlotBytes;
-    uint64_t* bar = S.bars + warp * 2 + b;
-    if (it.score) {
-        const int cc = it.tile * kScoreTile + 16 * warp;
-        const int nch = max(0, min(16, a.n_c - cc));
-        if (lane == 0 && nch > 0) {
-            const uint16_t* gmin = a.cmin + ((int64_t)it.r * a.n_max + cc) * kHeadDim;
-            const uint16_t* gmax = a.cmax + ((int64_t)it.r * a.n_max + cc) * kHeadDim;
-            mbar_arrive_expect_tx(bar, (uint32_t)nch * kHeadDim * 2 * 2);
-            bulk_g2s(slot, gmin, nch * kHeadDim * 2, bar);
-            bulk_g2s(slot + 4096, gmax, nch * kHeadDim * 2, bar);
-        }
-        return true;
-    }
-    const int e0 = it.tile * kTileEntries;
-    const int e1 = min(a.E, e0 + kTileEntries);
-    const int pg0 = a.RS + a.RN;
-    if (a.ST > 0 && e1 > pg0) {  // the tile holds selected pages
-        uint32_t* flag = a.ctrl + 2 + 2 * a.R + it.r;
-        if (threadIdx.x == 0) {
-            uint32_t f = ld_acquire(flag);
-            if (!f && blocking) {
-                const uint64_t t0 = globaltimer_ns();
-                while (!(f = ld_acquire(flag))) {
-                    __nanosleep(128);
-                    if (globaltimer_ns() - t0 > kFlagWaitNs) break;
-                }
-                if (!f) {
-                    set_status(a.status, ZKV_ERR_TIMEOUT);
-                    S.u[kU_Fail] = 1u;
-                }
-            }
-            if (f) __threadfence();
-            S.u[kU_Ok] = f ? 1u : 0u;
-        }
-        __syncthreads();
-        const bool ok = S.u[kU_Ok] != 0u;
-        __syncthreads();
-        if (!ok) return false;
-    }
-    const int e = e0 + warp;
-    if (e < e1) {
-        int chunk = 0;
-        if (e >= pg0) {
-            const int p = e - pg0;
-            chunk = a.ST > 0 ? (lane == 0 ? __ldcg(a.sel + (int64_t)it.r * a.nk + p) : 0) : p;
-            chunk = __shfl_sync(0xffffffffu, chunk, 0);
-            // every chunk selected (no select ran): the selection is the identity
-            if (a.ST == 0 && a.sel_out && lane == 0) a.sel_out[(int64_t)it.r * a.nk + p] = p;
-        }
-        unsigned pr;
-        const int64_t y0 = entry_tokens(a, e, chunk, pr);
-        if (lane == 0) {
-            const int y = (int)((int64_t)it.r * a.cap + y0);
-            const uint32_t dst = smem_u32(slot);
-            mbar_arrive_expect_tx(bar, kSlotBytes);
-            tma_load_2d(dst, &a.tk, 0, y, bar);
-            tma_load_2d(dst + 2048, &a.tk, 64, y, bar);
-            tma_load_2d(dst + 4096, &a.tv, 0, y, bar);
-            tma_load_2d(dst + 6144, &a.tv, 64, y, bar);
-        }
-    }
-    return true;
-}
-
-// Select the top nk chunks of row r (its scores are complete) and publish them.
-__device__ void select_row(const Args& a, const Smem& S, int r, float* buf) {
-    const int lane = threadIdx.x & 31;
-    const float* srow = a.scores + (int64_t)r * a.n_c_pad;
+    const int r = blockIdx.x / a.ST, tile = blockIdx.x % a.ST;
     if (threadIdx.x == 0) {
-        S.u[kU_Lo] = 0xffffffffu;
-        S.u[kU_Hi] = 0u;
+        for (int i = 0; i < kWarps; ++i) mbar_init(bars + i, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    grid_dep_wait();  // q is the previous kernel's output; the workspace is still read by the previous launch
+    grid_dep_launch_next();  // the attend kernel may become resident (it waits for this grid's completion)
+    const int cc = tile * kScoreTile + 16 * warp;
+    const int nch = max(0, min(16, a.n_c - cc));
+    uint8_t* slot = region + warp * kSlotBytes;
+    if (lane == 0 && nch > 0) {
+        mbar_arrive_expect_tx(bars + warp, (uint32_t)nch * kHeadDim * 2 * 2);
+        bulk_g2s(slot, a.cmin + ((int64_t)r * a.n_max + cc) * kHeadDim, nch * kHeadDim * 2, bars + warp);
+        bulk_g2s(slot + 4096, a.cmax + ((int64_t)r * a.n_max + cc) * kHeadDim, nch * kHeadDim * 2, bars + warp);
+    }
+    {   // GQA-mean query (compute() :1622-1626: fp32 sum in head order / G, bf16)
+        const uint16_t* qr = a.q + (int64_t)r * a.G * kHeadDim;
+        const int d = threadIdx.x;
+        float acc = 0.f;
+        for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, bfbits2f(__ldg(qr + g * kHeadDim + d)));
+        rq[d] = f2bfbits(__fdiv_rn(acc, (float)a.G));
+    }
+    __syncthreads();
+    float* srow = a.scores + (int64_t)r * a.n_c_pad;
+    if (nch > 0) {
+        const bool ok = mbar_wait(bars + warp, 0, a.status);
+        const int hl = lane & 15, half = lane >> 4;
+        const uint4 qv = *reinterpret_cast<const uint4*>(rq + 8 * hl);
+#pragma unroll 4
+        for (int u = 0; u < 8; ++u) {
+            const int lc = 2 * u + half;
+            uint4 mn = make_uint4(0, 0, 0, 0), mx = mn;
+            if (ok && lc < nch) {
+                mn = *reinterpret_cast<const uint4*>(slot + lc * 256 + 16 * hl);
+                mx = *reinterpret_cast<const uint4*>(slot + 4096 + lc * 256 + 16 * hl);
+            }
+            const float sc = quest_half(qv, mn, mx);
+            if (hl == 0 && lc < nch) {
+                const int c = cc + lc;
+                const bool v = !a.valid || a.valid[(int64_t)r * a.n_max + c];
+                srow[c] = (ok && v) ? sc : -INFINITY;
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        fence_acq_rel();
+        const uint32_t done = atomicAdd(a.ctrl + r, 1u);
+        su[0] = done == (uint32_t)(a.ST - 1);
+        if (su[0]) fence_acq_rel();
+    }
+    __syncthreads();
+    if (!su[0]) return;
+    // ------------------------------------------------ select (last tile of row r)
+    if (threadIdx.x == 0) {
+        su[1] = 0xffffffffu;
+        su[2] = 0u;
+        a.ctrl[r] = 0u;  // no other CTA touches this row's counter in this launch
     }
     __syncthreads();
     uint32_t klo = 0xffffffffu, khi = 0u;
@@ -417,7 +339,7 @@ __device__ void select_row(const Args& a, const Smem& S, int r, float* buf) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             if (i + e < a.n_c) {
-                buf[i + e] = fv[e];
+                region_f[i + e] = fv[e];
                 const uint32_t kk = ordered_u32(fv[e]);
                 if (kk > kOrderedNegInf) klo = min(klo, kk);
                 khi = max(khi, kk);
@@ -430,8 +352,8 @@ __device__ void select_row(const Args& a, const Smem& S, int r, float* buf) {
         khi = max(khi, __shfl_xor_sync(0xffffffffu, khi, off));
     }
     if (lane == 0) {
-        atomicMin(&S.u[kU_Lo], klo);
-        atomicMax(&S.u[kU_Hi], khi);
+        atomicMin(&su[1], klo);
+        atomicMax(&su[2], khi);
     }
     __syncthreads();
     int32_t* selr = a.sel + (int64_t)r * a.nk;
@@ -441,157 +363,86 @@ __device__ void select_row(const Args& a, const Smem& S, int r, float* buf) {
         if (selo) selo[pos] = i;
     };
     if (a.n_c <= 16 * kThreads)
-        block_topk_small<kThreads>(buf, a.n_c, a.nk, S.u[kU_Lo], S.u[kU_Hi], S.hist, S.misc, S.scan, emit);
+        block_topk_small<kThreads>(region_f, a.n_c, a.nk, su[1], su[2], hist, misc, scan, emit);
     else
-        block_topk<kThreads, true>([&](int i) { return ordered_u32(buf[i]); }, a.n_c, a.nk, S.hist, S.misc, S.scan,
-                                   emit, true, S.u[kU_Lo], S.u[kU_Hi]);
-    __syncthreads();
+        block_topk<kThreads, true>([&](int i) { return ordered_u32(region_f[i]); }, a.n_c, a.nk, hist, misc, scan,
+                                   emit, true, su[1], su[2]);
+}
+
+// ---------------------------------------------------------------- kernel B: attend + merge
+// One CTA per (row, tile of 8 entries); each warp attends 2 pages.  The CTA
+// that completes a row's last tile merges the row's partials.
+__global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_constant__ Args a) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t base_u32 = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);  // swizzled boxes: 1024-B aligned
+    uint8_t* region = smem;
+    float* region_f = reinterpret_cast<float*>(region);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kAttRegion);
+    uint32_t* su = reinterpret_cast<uint32_t*>(bars + kWarps * kSlots);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r = blockIdx.x / a.AT, tile = blockIdx.x % a.AT;
     if (threadIdx.x == 0) {
-        __threadfence();
-        st_release(a.ctrl + 2 + 2 * a.R + r, 1u);
-    }
-}
-
-// Merge the AT partials of row r into out / lse (weights staged in `buf`).
-__device__ void merge_row(const Args& a, int r, float* buf) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const float* pr = a.parts + (int64_t)r * a.AT * kPartFloats;
-    float* w = buf;                  // [AT][8]
-    float* sL = buf + a.AT * 8;      // [8]
-    float* sM = sL + 8;              // [8]
-    for (int h = warp; h < a.G; h += kWarps) {
-        float M = -INFINITY;
-        for (int t = lane; t < a.AT; t += 32) M = fmaxf(M, __ldcg(pr + (int64_t)t * kPartFloats + h));
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-        float L = 0.f;
-        for (int t = lane; t < a.AT; t += 32) {
-            const float* b = pr + (int64_t)t * kPartFloats;
-            const float mt = __ldcg(b + h);
-            const float wt = (mt == -INFINITY) ? 0.f : ex2(mt - M);
-            w[t * 8 + h] = wt;
-            L += wt * __ldcg(b + 8 + h);
-        }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-        if (lane == 0) {
-            sL[h] = L;
-            sM[h] = M;
-        }
+        for (int i = 0; i < kWarps * kSlots; ++i) mbar_init(bars + i, 1);
+        mbar_fence_init();
     }
     __syncthreads();
-    for (int i4 = threadIdx.x; i4 < a.G * (kHeadDim / 4); i4 += kThreads) {
-        const int h = i4 / (kHeadDim / 4);
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-        for (int t = 0; t < a.AT; ++t) {
-            const float wt = w[t * 8 + h];
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(pr + (int64_t)t * kPartFloats + 16) + i4);
-            acc.x += wt * v.x;
-            acc.y += wt * v.y;
-            acc.z += wt * v.z;
-            acc.w += wt * v.w;
+    grid_dep_wait();  // the selection of the score kernel
+    const int e0 = tile * kTileEntries;
+    const int e1 = min(a.E, e0 + kTileEntries);
+    const int pg0 = a.RS + a.RN;
+    unsigned present[kSlots];
+    bool have[kSlots];
+#pragma unroll
+    for (int k = 0; k < kSlots; ++k) {
+        const int e = e0 + warp * kSlots + k;
+        have[k] = e < e1;
+        present[k] = 0u;
+        if (!have[k]) continue;
+        int chunk = 0;
+        if (e >= pg0) {
+            const int p = e - pg0;
+            chunk = a.ST > 0 ? (lane == 0 ? __ldcg(a.sel + (int64_t)r * a.nk + p) : 0) : p;
+            chunk = __shfl_sync(0xffffffffu, chunk, 0);
+            if (a.ST == 0 && a.sel_out && lane == 0) a.sel_out[(int64_t)r * a.nk + p] = p;
         }
-        const float L = sL[h];
-        const float inv = L > 0.f ? 1.f / L : 0.f;
-        uint2 o;
-        o.x = (uint32_t)f2bfbits(acc.x * inv) | ((uint32_t)f2bfbits(acc.y * inv) << 16);
-        o.y = (uint32_t)f2bfbits(acc.z * inv) | ((uint32_t)f2bfbits(acc.w * inv) << 16);
-        *reinterpret_cast<uint2*>(a.out + (int64_t)r * a.G * kHeadDim + 4 * i4) = o;
-        if ((i4 % (kHeadDim / 4)) == 0 && a.lse)
-            a.lse[(int64_t)r * a.G + h] = (L > 0.f) ? (sM[h] + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+        unsigned pr;
+        const int64_t y0 = entry_tokens(a, e, chunk, pr);
+        present[k] = pr;
+        if (lane == 0) {
+            const int y = (int)((int64_t)r * a.cap + y0);
+            const uint32_t dst = smem_u32(region) + (uint32_t)((warp * kSlots + k) * kSlotBytes);
+            uint64_t* bar = bars + warp * kSlots + k;
+            mbar_arrive_expect_tx(bar, kSlotBytes);
+            tma_load_2d(dst, &a.tk, 0, y, bar);
+            tma_load_2d(dst + 2048, &a.tk, 64, y, bar);
+            tma_load_2d(dst + 4096, &a.tv, 0, y, bar);
+            tma_load_2d(dst + 6144, &a.tv, 64, y, bar);
+        }
     }
-}
-
-// Process `item` whose loads (if `issued`) target buffer b.  `phase` holds
-// the parity bits of this warp's two slot barriers.
-__device__ void process_item(const Args& a, const Smem& S, uint32_t item, int b, bool issued, uint32_t& phase) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const Item it = decode_item(a, item);
-    uint8_t* buf = S.region + b * kBufBytes;
-    uint8_t* slot = buf + warp * kSlotBytes;
-    uint64_t* bar = S.bars + warp * 2 + b;
-    float* buf_f = reinterpret_cast<float*>(buf);
-    const int r = it.r;
-    if (it.score) {
-        // ---------------------------------------------- Quest score tile
-        const int cc = it.tile * kScoreTile + 16 * warp;
-        const int nch = max(0, min(16, a.n_c - cc));
-        {   // GQA-mean query (compute() :1622-1626: fp32 sum in head order / G, bf16)
-            const uint16_t* qr = a.q + (int64_t)r * a.G * kHeadDim;
-            const int d = threadIdx.x;
-            float acc = 0.f;
-            for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, bfbits2f(__ldg(qr + g * kHeadDim + d)));
-            S.rq[d] = f2bfbits(__fdiv_rn(acc, (float)a.G));
-        }
-        __syncthreads();
-        float* srow = a.scores + (int64_t)r * a.n_c_pad;
-        if (nch > 0) {
-            bool ok = issued;
-            if (issued) {
-                ok = mbar_wait(bar, (phase >> b) & 1u, a.status);
-                phase ^= 1u << b;
-            }
-            const int hl = lane & 15, half = lane >> 4;
-            const uint4 qv = *reinterpret_cast<const uint4*>(S.rq + 8 * hl);
-#pragma unroll 4
-            for (int u = 0; u < 8; ++u) {
-                const int lc = 2 * u + half;
-                uint4 mn = make_uint4(0, 0, 0, 0), mx = mn;
-                if (ok && lc < nch) {
-                    mn = *reinterpret_cast<const uint4*>(slot + lc * 256 + 16 * hl);
-                    mx = *reinterpret_cast<const uint4*>(slot + 4096 + lc * 256 + 16 * hl);
-                }
-                const float sc = quest_half(qv, mn, mx);
-                if (hl == 0 && lc < nch) {
-                    const int c = cc + lc;
-                    const bool v = !a.valid || a.valid[(int64_t)r * a.n_max + c];
-                    srow[c] = (ok && v) ? sc : -INFINITY;
-                }
-            }
-            if (!ok && lane == 0) atomicOr(&S.u[kU_Fail], 1u);
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence();
-            const uint32_t done = atomicAdd(a.ctrl + 2 + r, 1u);
-            S.u[kU_Flag] = done == (uint32_t)(a.ST - 1);
-            if (S.u[kU_Flag]) __threadfence();
-        }
-        __syncthreads();
-        if (S.u[kU_Flag]) select_row(a, S, r, buf_f);  // the row's last score tile
-        return;
-    }
-    // ---------------------------------------------- attend tile
-    const int e = it.tile * kTileEntries + warp;
-    const bool have = issued && e < min(a.E, it.tile * kTileEntries + kTileEntries);
     WarpState st;
     state_init(st, a.q + (int64_t)r * a.G * kHeadDim, a.G);
-    if (have) {
-        const bool landed = mbar_wait(bar, (phase >> b) & 1u, a.status);
-        phase ^= 1u << b;
-        if (landed) {
-            const unsigned present = entry_present(a, e);
-            if (present != 0xffffu) {  // zero the V rows of absent tokens (p = 0 must meet finite V)
-                uint8_t* vs = slot + 4096;
-                for (int i = lane; i < 16 * 16; i += 32) {
-                    const int tkn = i >> 4, box = (i >> 3) & 1, c = i & 7;
-                    if (!((present >> tkn) & 1u))
-                        *reinterpret_cast<uint4*>(vs + box * 2048 + tkn * 128 + c * 16) = make_uint4(0, 0, 0, 0);
-                }
-                __syncwarp();
+#pragma unroll
+    for (int k = 0; k < kSlots; ++k) {
+        if (!have[k]) continue;
+        if (!mbar_wait(bars + warp * kSlots + k, 0, a.status)) continue;  // status set; the page is skipped
+        uint8_t* slot = region + (warp * kSlots + k) * kSlotBytes;
+        if (present[k] != 0xffffu) {  // zero the V rows of absent tokens (p = 0 must meet finite V)
+            for (int i = lane; i < 16 * 16; i += 32) {
+                const int tkn = i >> 4, box = (i >> 3) & 1, c = i & 7;
+                if (!((present[k] >> tkn) & 1u))
+                    *reinterpret_cast<uint4*>(slot + 4096 + box * 2048 + tkn * 128 + c * 16) = make_uint4(0, 0, 0, 0);
             }
-            page_attend(st, smem_u32(slot), present, a.G, a.sl2);
-        } else if (lane == 0) {
-            atomicOr(&S.u[kU_Fail], 1u);
+            __syncwarp();
         }
+        page_attend(st, smem_u32(slot), present[k], a.G, a.sl2);
     }
     __syncthreads();
-    float* cm = buf_f + 4224;  // past the warp scratch (4 x 1040 floats)
+    float* cm = region_f + 4224;
     float* cl = cm + 8;
     float* co = cl + 8;
-    merge_warps(st, a.G, buf_f, cm, cl, co);
-    float* part = a.parts + ((int64_t)r * a.AT + it.tile) * kPartFloats;
+    merge_warps(st, a.G, region_f, cm, cl, co);
+    float* part = a.parts + ((int64_t)r * a.AT + tile) * kPartFloats;
     if (threadIdx.x < 8) {
         part[threadIdx.x] = (int)threadIdx.x < a.G ? cm[threadIdx.x] : -INFINITY;
         part[8 + threadIdx.x] = (int)threadIdx.x < a.G ? cl[threadIdx.x] : 0.f;
@@ -600,82 +451,66 @@ __device__ void process_item(const Args& a, const Smem& S, uint32_t item, int b,
         reinterpret_cast<float4*>(part + 16)[i] = reinterpret_cast<const float4*>(co)[i];
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
-        const uint32_t done = atomicAdd(a.ctrl + 2 + a.R + r, 1u);
-        S.u[kU_Flag] = done == (uint32_t)(a.AT - 1);
-        if (S.u[kU_Flag]) __threadfence();
-    }
-    __syncthreads();
-    if (S.u[kU_Flag]) merge_row(a, r, buf_f);  // the row's last attend tile
-}
-
-__global__ void __launch_bounds__(kThreads, 3) raw_decode_kernel(const __grid_constant__ Args a) {
-    extern __shared__ uint8_t smem_raw[];
-    // the swizzled boxes need a 1024-byte-aligned region
-    const uint32_t base_u32 = smem_u32(smem_raw);
-    uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
-    Smem S;
-    S.region = smem;
-    S.hist = reinterpret_cast<int*>(smem + kRegion);
-    S.misc = S.hist + 512;
-    S.scan = S.misc + 8;
-    S.rq = reinterpret_cast<uint16_t*>(S.scan + 2 * kThreads);
-    S.bars = reinterpret_cast<uint64_t*>(S.rq + kHeadDim);
-    S.u = reinterpret_cast<uint32_t*>(S.bars + kWarps * 2);
-
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < kWarps * 2; ++i) mbar_init(S.bars + i, 1);
-        mbar_fence_init();
-        S.u[kU_Fail] = 0;
-    }
-    grid_dep_wait();  // q and the workspace may still be in use by the previous kernel
-    uint32_t* ctr_next = a.ctrl;
-    uint32_t* ctr_exit = a.ctrl + 1;
-    if (threadIdx.x == 0) {
-        S.u[0] = atomicAdd(ctr_next, 1u);
-        S.u[1] = atomicAdd(ctr_next, 1u);
-    }
-    __syncthreads();
-    uint32_t phase = 0;  // bit b: parity of this warp's buffer-b barrier (warp-uniform)
-    uint32_t cur = S.u[0], nxt = S.u[1];
-    int b = 0;
-    bool cur_issued = cur < a.total ? issue_item(a, S, cur, 0, true) : false;
-    while (cur < a.total) {
-        uint32_t after = 0;  // thread 0: the claim after `nxt`
-        if (threadIdx.x == 0) after = atomicAdd(ctr_next, 1u);
-        // the next item's loads go out before this item is computed (page
-        // tiles only once their row's selection is published)
-        const bool nxt_issued = nxt < a.total ? issue_item(a, S, nxt, b ^ 1, false) : false;
-        process_item(a, S, cur, b, cur_issued, phase);
-        // order this item's generic accesses to buffer b before later TMA writes into it
-        fence_proxy_async();
-        __syncthreads();
-        if (threadIdx.x == 0) S.u[2] = after;
-        __syncthreads();
-        cur = nxt;
-        nxt = S.u[2];
-        b ^= 1;
-        cur_issued = nxt_issued;
-        if (cur < a.total && !cur_issued) cur_issued = issue_item(a, S, cur, b, true);
-    }
-
-    // ------------------------------------------------ exit: the last CTA resets the control words
-    grid_dep_launch_next();
-    if (threadIdx.x == 0) {
-        if (S.u[kU_Fail]) set_status(a.status, ZKV_ERR_TIMEOUT);
-        __threadfence();
-        const uint32_t gone = atomicAdd(ctr_exit, 1u);
-        S.u[kU_Flag] = gone == gridDim.x - 1;
-        if (S.u[kU_Flag]) __threadfence();
-    }
-    __syncthreads();
-    if (S.u[kU_Flag]) {
-        for (int i = threadIdx.x; i < 3 * a.R; i += kThreads) a.ctrl[2 + i] = 0u;
-        if (threadIdx.x == 0) {
-            *ctr_next = 0u;
-            *ctr_exit = 0u;
+        fence_acq_rel();
+        const uint32_t done = atomicAdd(a.ctrl + a.R + r, 1u);
+        su[0] = done == (uint32_t)(a.AT - 1);
+        if (su[0]) {
+            fence_acq_rel();
+            a.ctrl[a.R + r] = 0u;
         }
-        __threadfence();
+    }
+    __syncthreads();
+    if (!su[0]) return;
+    // ------------------------------------------------ row merge (last tile of row r)
+    const float* pr = a.parts + (int64_t)r * a.AT * kPartFloats;
+    float* sm_m = region_f;              // [AT][8]
+    float* sm_l = sm_m + a.AT * 8;       // [AT][8]
+    float* sL = sm_l + a.AT * 8;         // [8]
+    for (int i = threadIdx.x; i < a.AT * a.G; i += kThreads) {
+        const int t = i / a.G, h = i % a.G;
+        sm_m[t * 8 + h] = __ldcg(pr + (int64_t)t * kPartFloats + h);
+        sm_l[t * 8 + h] = __ldcg(pr + (int64_t)t * kPartFloats + 8 + h);
+    }
+    __syncthreads();
+    if (threadIdx.x < a.G) {  // per head: max, weights (in place of m), weighted sum of l
+        const int h = threadIdx.x;
+        float M = -INFINITY;
+        for (int t = 0; t < a.AT; ++t) M = fmaxf(M, sm_m[t * 8 + h]);
+        float L = 0.f;
+        for (int t = 0; t < a.AT; ++t) {
+            const float mt = sm_m[t * 8 + h];
+            const float wt = (mt == -INFINITY) ? 0.f : ex2(mt - M);
+            sm_m[t * 8 + h] = wt;
+            L += wt * sm_l[t * 8 + h];
+        }
+        sL[h] = L;
+        if (a.lse) a.lse[(int64_t)r * a.G + h] = (L > 0.f) ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+    }
+    __syncthreads();
+    for (int i4 = threadIdx.x; i4 < a.G * (kHeadDim / 4); i4 += kThreads) {
+        const int h = i4 / (kHeadDim / 4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int t0 = 0; t0 < a.AT; t0 += 8) {  // 8 independent loads in flight per batch
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                v[u] = t0 + u < a.AT ? __ldcg(reinterpret_cast<const float4*>(pr + (int64_t)(t0 + u) * kPartFloats + 16) + i4)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float wt = t0 + u < a.AT ? sm_m[(t0 + u) * 8 + h] : 0.f;
+                acc.x += wt * v[u].x;
+                acc.y += wt * v[u].y;
+                acc.z += wt * v[u].z;
+                acc.w += wt * v[u].w;
+            }
+        }
+        const float L = sL[h];
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        uint2 o;
+        o.x = (uint32_t)f2bfbits(acc.x * inv) | ((uint32_t)f2bfbits(acc.y * inv) << 16);
+        o.y = (uint32_t)f2bfbits(acc.z * inv) | ((uint32_t)f2bfbits(acc.w * inv) << 16);
+        *reinterpret_cast<uint2*>(a.out + (int64_t)r * a.G * kHeadDim + 4 * i4) = o;
     }
 }
 
@@ -712,8 +547,7 @@ static bool encode_rows(CUtensorMap* map, const void* base, int64_t n_tok) {
 }
 
 struct Plan {
-    int ST, AT, RT, RS, RN, E, n_c_pad, per_row_a, D;
-    int64_t total;
+    int ST, AT, RS, RN, E, n_c_pad;
     size_t off_scores, off_sel, off_parts, bytes;
 };
 
@@ -727,22 +561,30 @@ static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near) {
     p.RN = (n_near + 15) / 16;
     p.E = p.RS + p.RN + nsel;
     p.AT = p.E > 0 ? (p.E + kTileEntries - 1) / kTileEntries : 1;
-    p.RT = (p.RS + p.RN) / kTileEntries;  // tiles of raw rows only (no selection needed)
-    if (p.RT > p.AT) p.RT = p.AT;
     p.n_c_pad = (n_c + 31) & ~31;
-    p.per_row_a = p.ST + p.RT;
-    // queue skew: a row's page tiles follow the scoring of the next D rows
-    p.D = R > 1 ? (R + 1) / 2 : (R > 0 ? 1 : 0);
-    p.total = (int64_t)R * (p.ST + p.AT);
-    p.off_scores = up256(8 + (size_t)12 * R);
+    p.off_scores = up256((size_t)8 * R);
     p.off_sel = p.off_scores + up256((size_t)R * p.n_c_pad * 4);
     p.off_parts = p.off_sel + up256((size_t)R * (nk > 0 ? nk : 1) * 4);
     p.bytes = p.off_parts + up256((size_t)R * p.AT * kPartFloats * 4);
     return p;
 }
 
-static size_t smem_bytes() {
-    return 1024 + kRegion + (512 + 8 + 2 * kThreads) * 4 + kHeadDim * 2 + kWarps * 2 * 8 + 16 * 4;
+static size_t score_smem() { return kScoreRegion + (512 + 8 + 2 * kThreads) * 4 + kHeadDim * 2 + kWarps * 8 + 16; }
+static size_t attend_smem() { return 1024 + kAttRegion + kWarps * kSlots * 8 + 16; }
+
+static int launch_pdl(const void* fn, int grid, size_t smem, cudaStream_t stream, void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelExC(&cfg, fn, args) != cudaSuccess) return ZKV_ERR_LAUNCH;
+    return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH;
 }
 
 }  // namespace rawpg
@@ -773,7 +615,7 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
     if (n_c > kMaxChunks || (int64_t)rows * cap >= (int64_t)1 << 31) return ZKV_ERR_CAPACITY;
     const Plan p = make_plan(rows, n_c, nk, n_sink, n_near);
     if (ws_bytes < p.bytes) return ZKV_ERR_ARG;
-    if (p.total >= ((int64_t)1 << 31) || p.AT > kMaxTiles) return ZKV_ERR_CAPACITY;
+    if (p.AT > kMaxTiles || (int64_t)rows * (p.ST + p.AT) >= ((int64_t)1 << 31)) return ZKV_ERR_CAPACITY;
     if (rows == 0) return ZKV_OK;
     if (((uintptr_t)L.keys & 15) || ((uintptr_t)L.values & 15) || ((uintptr_t)L.chunk_min & 15) ||
         ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)q & 3) || ((uintptr_t)workspace & 255))
@@ -798,14 +640,10 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
     a.n_near = n_near;
     a.ST = p.ST;
     a.AT = p.AT;
-    a.RT = p.RT;
     a.RS = p.RS;
     a.RN = p.RN;
     a.E = p.E;
     a.n_c_pad = p.n_c_pad;
-    a.per_row_a = p.per_row_a;
-    a.D = p.D;
-    a.total = (uint32_t)p.total;
     a.sl2 = scale * 1.4426950408889634f;
     a.out = (uint16_t*)out;
     a.lse = lse;
@@ -817,36 +655,21 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
     a.sel = (int32_t*)(ws + p.off_sel);
     a.parts = (float*)(ws + p.off_parts);
 
-    // persistent grid: the resident CTAs of every SM (capped by the item count)
-    static int occ[64] = {};
-    static int sms[64] = {};
+    static bool attr_set[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ZKV_ERR_LAUNCH;
-    const size_t smem = smem_bytes();
-    if (!occ[dev]) {
-        if (cudaFuncSetAttribute(raw_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
+    if (!attr_set[dev]) {
+        if (cudaFuncSetAttribute(raw_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem()) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(raw_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)attend_smem()) != cudaSuccess)
             return ZKV_ERR_LAUNCH;
-        int nb = 0, n_sm = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, raw_decode_kernel, kThreads, smem) != cudaSuccess ||
-            cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || nb < 1)
-            return ZKV_ERR_LAUNCH;
-        sms[dev] = n_sm;
-        occ[dev] = nb;
+        attr_set[dev] = true;
     }
-    int64_t grid = (int64_t)occ[dev] * sms[dev];
-    if (grid > p.total) grid = p.total;
-    if (grid < 1) grid = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = (cudaStream_t)stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, raw_decode_kernel, a) != cudaSuccess) return ZKV_ERR_LAUNCH;
-    return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH;
+    void* args[] = {&a};
+    int rc = ZKV_OK;
+    if (p.ST > 0)
+        rc = launch_pdl((const void*)raw_score_kernel, rows * p.ST, score_smem(), (cudaStream_t)stream, args);
+    if (rc != ZKV_OK) return rc;
+    return launch_pdl((const void*)raw_attend_kernel, rows * p.AT, attend_smem(), (cudaStream_t)stream, args);
 }
