@@ -787,12 +787,13 @@ def main():
         "hbm_gbs_per_gpu": achieved, "hbm_frac_of_peak": achieved / peak,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind,
-                     "kernel": "raw_score_kernel + raw_attend_kernel" if raw else "page_decode_kernel",
+                     "kernel": ("raw_score_kernel + raw_select_kernel + raw_attend_kernel + raw_merge_kernel"
+                                if raw else "page_decode_kernel"),
                      "bytes_per_launch": bytes_launch, "launch_us": launch_s * 1e6, "traffic": None},
         "e2e": {"value": e2e_tokens, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "mode": "CUDA graph per step: per layer H2D q (pinned) -> ops.page_decode%s -> D2H out (pinned), "
                         "copies on a second stream in groups of 6 layers" % ("_raw" if raw else "")},
-        "gpu_launches": layers * args.steps * (2 if raw else 1),  # raw: score + attend kernels per layer
+        "gpu_launches": layers * args.steps * (4 if raw else 1),  # raw: score, select, attend, merge per layer
         "clocks": clk.summary(),
         "parity": parity,
     }

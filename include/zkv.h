@@ -308,8 +308,8 @@ typedef struct zkv_raw_layer {
 size_t zkv_page_decode_raw_ws_bytes(int rows, int n_c, int nk, int n_sink,
                                     int n_near);
 
-/* Page-mode decode over the RAW bf16 rows of the selected pages, one
- * launch per layer: GQA-mean query -> Quest scores of chunks [0, n_c) ->
+/* Page-mode decode over the RAW bf16 rows of the selected pages:
+ * GQA-mean query -> Quest scores of chunks [0, n_c) ->
  * top nk chunks (ties to the lowest id, ascending) -> attention of the G
  * query heads over [selected chunks' 16 raw rows each, at token
  * page_base + 16 c] U [0, n_sink) U [near_start, near_start + n_near) ->
@@ -318,17 +318,17 @@ size_t zkv_page_decode_raw_ws_bytes(int rows, int n_c, int nk, int n_sink,
  * attends the raw rows of the selected chunks
  * (cache_hub/polar_cache_quest_density_single_layer_kivi.py:1589-1775,
  * :1734-1750; quest_chunk_score.cu:106-154; float_topk.cu:280-346;
- * attn_hub/flash_attn_compat.py:44-99).  Two launches chained by
- * programmatic dependent launch: Quest scores + per-row select, then the
- * attention (pages by 2-D TMA tensor copies) + per-row merge.
- * nk <= n_c (nk == n_c: every chunk, no select, one launch).
+ * attn_hub/flash_attn_compat.py:44-99).  Four launches chained by
+ * programmatic dependent launch: Quest scores, per-row select, attention
+ * (pages by 2-D TMA tensor copies) into per-CTA partials, per-row merge.
+ * nk <= n_c (nk == n_c: every chunk, no scores or select, two launches).
  *   q [rows][G][128] bf16; out [rows][G][128] bf16; lse [rows][G] fp32
  *   natural log (may be NULL); sel_out [rows][nk] int64 or NULL;
  *   status: device int32 set to ZKV_ERR_TIMEOUT if a bounded wait expires;
- *   workspace: device, 256-byte aligned, >= zkv_page_decode_raw_ws_bytes,
- *   ZERO-FILLED before its first use (every call leaves its control words
- *   at zero again); calls sharing a workspace must not overlap on the GPU.
- *   Limits: n_c <= 8192, (n_sink + n_near) / 16 + nk <= 8176,
+ *   workspace: device, 256-byte aligned, >= zkv_page_decode_raw_ws_bytes
+ *   (scratch only: no state carries between calls, no zero fill needed);
+ *   calls sharing a workspace must not overlap on the GPU.
+ *   Limits: n_c <= 16384, (n_sink + n_near) / 16 + nk <= 16384,
  *   rows * kv_ld_row / 128 < 2^31 (else ZKV_ERR_CAPACITY).               */
 int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, int rows,
                         int G, int n_max, int n_c, int nk, int n_sink,

@@ -66,10 +66,11 @@ def oracle_raw(rc, q, nk, rows=None):
     (2, 2, 4, 300, 24, 0, 37),     # ragged near window, no sink
     (1, 3, 4, 97, 97, 5, 0),       # every chunk selected (no select runs), partial sink page
     (2, 2, 4, 130, 16, 64, 128),   # reference default sink 64
-    (1, 2, 8, 3000, 200, 16, 40),  # n_c > 2048: the radix select path, G = 8
+    (1, 2, 8, 3000, 200, 16, 40),  # G = 8, shared-memory select
     (1, 2, 1, 500, 31, 3, 17),     # G = 1, odd sizes
     (3, 1, 2, 64, 8, 0, 0),        # pages only
-    (1, 1, 4, 2048, 128, 0, 128),  # one-level select at its largest n_c
+    (1, 1, 4, 4096, 128, 0, 128),  # shared-memory select at its largest n_c
+    (1, 1, 4, 5001, 300, 64, 64),  # n_c > 4096: the radix select path over global scores
 ])
 def test_raw_matches_oracle(bs, H, G, n_c, nk, n_sink, n_near):
     rc = W.build_raw_cache(11 + n_c, bs, H, 16 * n_c, n_near, DEV, n_sink=n_sink)
@@ -113,9 +114,10 @@ def test_raw_ties_invalid_chunks_and_empty_rows():
 
 
 def test_raw_workspace_reuse_across_shapes_and_repeats():
-    """The control words return to zero after every launch: the same
-    workspace serves different shapes back to back and repeats bit-exactly."""
-    ws = torch.zeros(ops.page_decode_raw_ws_bytes(16, 3000, 256, 64, 128), dtype=torch.uint8, device=DEV)
+    """The workspace is scratch only (no state carries between calls, no zero
+    fill): one workspace full of garbage bytes serves different shapes back
+    to back and repeats bit-exactly."""
+    ws = torch.full((ops.page_decode_raw_ws_bytes(16, 3000, 256, 64, 128),), 0x7F, dtype=torch.uint8, device=DEV)
     cases = []
     for bs, H, n_c, nk, s, nn in [(2, 8, 700, 64, 0, 128), (1, 2, 3000, 256, 64, 33), (2, 8, 700, 64, 0, 128)]:
         rc = W.build_raw_cache(40 + n_c, bs, H, 16 * n_c, nn, DEV, n_sink=s)

@@ -1,5 +1,5 @@
 // zkv_raw.cu -- page-mode decode over the RAW bf16 rows of the selected pages:
-// two launches per layer chained by programmatic dependent launch.
+// four launches per layer chained by programmatic dependent launch.
 //
 // The reference's page mode (polar_cache.compute with dense_topk = sparse_topk
 // = 16 and final_topk = budget, cache_hub/polar_cache_quest_density_single_
@@ -10,21 +10,22 @@
 //
 //  * raw_score_kernel: one CTA per (row, 64 chunks).  Bulk copies bring the
 //    chunks' Quest min/max (32 KiB) into shared memory; each half-warp scores
-//    a chunk with the reference kernel's fp32 operation order.  The CTA that
-//    completes a row's scores (a per-row counter) selects the row's top nk
-//    chunks; rows finish in launch order, so most selections overlap the
-//    scoring of later rows.
+//    a chunk with the reference kernel's fp32 operation order and writes the
+//    score to the workspace.
+//  * raw_select_kernel: one CTA per row: invalid chunks -> -inf, then the top
+//    nk chunk ids (ties to the lowest id, ascending).
 //  * raw_attend_kernel: one CTA per (row, 8 entries of 16 tokens): sink and
-//    near rows, then selected pages.  It waits for the score kernel through
-//    griddepcontrol.wait (no flag spinning between grids), brings each page in
-//    as four 2-D TMA tensor copies with the 128-byte swizzle (K and V, dims
-//    0-63 and 64-127) and reads them with ldmatrix (K, B operand of
-//    S = Q K^T) and ldmatrix.trans (V, A operand of O^T = V^T P^T) into
-//    mma.sync m16n8k16 with an online softmax.  The CTA writes its partial
-//    (m, l, o); the CTA that delivers a row's last partial merges the row
-//    into out / lse.
-//  * Every per-row counter is reset by the CTA that completes the row, so the
-//    workspace is ready for the next launch.
+//    near rows, then selected pages.  Each page comes in as four 2-D TMA
+//    tensor copies with the 128-byte swizzle (K and V, dims 0-63 and 64-127)
+//    and is read with ldmatrix (K, B operand of S = Q K^T) and ldmatrix.trans
+//    (V, A operand of O^T = V^T P^T) into mma.sync m16n8k16 with an online
+//    softmax.  The CTA merges its warps and writes one partial (m, l, o).
+//  * raw_merge_kernel: one CTA per row: the row's partials -> out / lse.
+//
+// Each kernel waits for its predecessor's grid with griddepcontrol.wait and
+// releases its successor right after, so a successor's CTAs become resident
+// while the predecessor drains: no flags, counters or atomics cross CTAs and
+// the workspace carries no state between calls.
 #include <cuda.h>
 
 #include <cstring>
@@ -44,8 +45,10 @@ constexpr int kAttRegion = kTileEntries * kSlotBytes;  // 64 KiB
 constexpr int kScoreTile = kWarps * 16;           // chunks per score CTA (32 KiB of min/max)
 constexpr int kScoreRegion = kWarps * kSlotBytes; // 32 KiB
 constexpr int kPartFloats = 16 + 8 * kHeadDim;    // m[8], l[8], o[8][128]
-constexpr int kMaxChunks = kScoreRegion / 4;      // a row's scores fit the score CTA's region
-constexpr int kMaxTiles = (kAttRegion / 4 - 16) / 16;  // a row's merge weights (m, l) fit the attend region
+constexpr int kSelThreads = 256;                  // threads of a select CTA
+constexpr int kSelSmall = 16 * kSelThreads;       // rows up to this many chunks select from shared memory
+constexpr int kMaxChunks = 16384;
+constexpr int kMaxTiles = 2048;                   // attend tiles per row (merge weights in shared memory)
 
 struct Args {
     CUtensorMap tk;  // raw keys   as [rows * cap][128] bf16, box 64 x 16, 128-B swizzle
@@ -62,7 +65,6 @@ struct Args {
     float* lse;
     int64_t* sel_out;
     int32_t* status;
-    uint32_t* ctrl;  // score_done[R], attend_done[R] (zero between launches)
     float* scores;   // [R][n_c_pad]
     int32_t* sel;    // [R][nk]
     float* parts;    // [R][AT][kPartFloats]
@@ -257,19 +259,15 @@ __device__ __forceinline__ int64_t entry_tokens(const Args& a, int e, int chunk,
     return a.page_base + 16 * (int64_t)chunk;
 }
 
-// ---------------------------------------------------------------- kernel A: scores + select
-// One CTA per (row, tile of 64 chunks).  The CTA that completes a row's last
-// tile selects the row's top nk chunks and resets the row's counter.
+// ---------------------------------------------------------------- kernel 1: scores
+// One CTA per (row, 64 chunks): each warp bulk-copies its 16 chunks' min and
+// max (8 KiB) into shared memory and scores them; the scores go to the
+// workspace.  Validity is applied by the select.
 __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_constant__ Args a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* region = smem;                                   // [4 warps][8 KiB]: min 4 KiB, max 4 KiB
-    float* region_f = reinterpret_cast<float*>(region);
-    int* hist = reinterpret_cast<int*>(smem + kScoreRegion);
-    int* misc = hist + 512;
-    int* scan = misc + 8;
-    uint16_t* rq = reinterpret_cast<uint16_t*>(scan + 2 * kThreads);
+    uint16_t* rq = reinterpret_cast<uint16_t*>(smem + kScoreRegion);
     uint64_t* bars = reinterpret_cast<uint64_t*>(rq + kHeadDim);
-    uint32_t* su = reinterpret_cast<uint32_t*>(bars + kWarps);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r = blockIdx.x / a.ST, tile = blockIdx.x % a.ST;
     if (threadIdx.x == 0) {
@@ -277,8 +275,8 @@ __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_consta
         mbar_fence_init();
     }
     __syncthreads();
-    grid_dep_wait();  // q is the previous kernel's output; the workspace is still read by the previous launch
-    grid_dep_launch_next();  // the attend kernel may become resident (it waits for this grid's completion)
+    grid_dep_wait();          // q is the previous kernel's output; the workspace may still be read by it
+    grid_dep_launch_next();   // the select kernel may become resident (it waits for this grid)
     const int cc = tile * kScoreTile + 16 * warp;
     const int nch = max(0, min(16, a.n_c - cc));
     uint8_t* slot = region + warp * kSlotBytes;
@@ -295,51 +293,54 @@ __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_consta
         rq[d] = f2bfbits(__fdiv_rn(acc, (float)a.G));
     }
     __syncthreads();
+    if (nch == 0) return;
+    const bool ok = mbar_wait(bars + warp, 0, a.status);
+    const int hl = lane & 15, half = lane >> 4;
+    const uint4 qv = *reinterpret_cast<const uint4*>(rq + 8 * hl);
     float* srow = a.scores + (int64_t)r * a.n_c_pad;
-    if (nch > 0) {
-        const bool ok = mbar_wait(bars + warp, 0, a.status);
-        const int hl = lane & 15, half = lane >> 4;
-        const uint4 qv = *reinterpret_cast<const uint4*>(rq + 8 * hl);
 #pragma unroll 4
-        for (int u = 0; u < 8; ++u) {
-            const int lc = 2 * u + half;
-            uint4 mn = make_uint4(0, 0, 0, 0), mx = mn;
-            if (ok && lc < nch) {
-                mn = *reinterpret_cast<const uint4*>(slot + lc * 256 + 16 * hl);
-                mx = *reinterpret_cast<const uint4*>(slot + 4096 + lc * 256 + 16 * hl);
-            }
-            const float sc = quest_half(qv, mn, mx);
-            if (hl == 0 && lc < nch) {
-                const int c = cc + lc;
-                const bool v = !a.valid || a.valid[(int64_t)r * a.n_max + c];
-                srow[c] = (ok && v) ? sc : -INFINITY;
-            }
+    for (int u = 0; u < 8; ++u) {
+        const int lc = 2 * u + half;
+        uint4 mn = make_uint4(0, 0, 0, 0), mx = mn;
+        if (ok && lc < nch) {
+            mn = *reinterpret_cast<const uint4*>(slot + lc * 256 + 16 * hl);
+            mx = *reinterpret_cast<const uint4*>(slot + 4096 + lc * 256 + 16 * hl);
         }
+        const float sc = quest_half(qv, mn, mx);
+        if (hl == 0 && lc < nch) srow[cc + lc] = ok ? sc : -INFINITY;
     }
-    __syncthreads();
+}
+
+// ---------------------------------------------------------------- kernel 2: select
+// One CTA of kSelThreads per row: the row's scores (invalid chunks -> -inf)
+// -> top nk chunk ids, ties to the lowest id, ascending.
+__global__ void __launch_bounds__(kSelThreads) raw_select_kernel(const __grid_constant__ Args a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    float* keys = reinterpret_cast<float*>(smem);             // [kSelSmall]
+    int* hist = reinterpret_cast<int*>(keys + kSelSmall);
+    int* misc = hist + 512;
+    int* scan = misc + 8;
+    uint32_t* lohi = reinterpret_cast<uint32_t*>(scan + 2 * kSelThreads);
+    const int r = blockIdx.x, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        fence_acq_rel();
-        const uint32_t done = atomicAdd(a.ctrl + r, 1u);
-        su[0] = done == (uint32_t)(a.ST - 1);
-        if (su[0]) fence_acq_rel();
+        lohi[0] = 0xffffffffu;
+        lohi[1] = 0u;
     }
     __syncthreads();
-    if (!su[0]) return;
-    // ------------------------------------------------ select (last tile of row r)
-    if (threadIdx.x == 0) {
-        su[1] = 0xffffffffu;
-        su[2] = 0u;
-        a.ctrl[r] = 0u;  // no other CTA touches this row's counter in this launch
-    }
-    __syncthreads();
+    grid_dep_wait();          // the scores of the score kernel
+    grid_dep_launch_next();   // the attend kernel may become resident (it waits for this grid)
+    const float* srow = a.scores + (int64_t)r * a.n_c_pad;
+    const uint8_t* vrow = a.valid ? a.valid + (int64_t)r * a.n_max : nullptr;
+    const bool small = a.n_c <= kSelSmall;
     uint32_t klo = 0xffffffffu, khi = 0u;
-    for (int i = 4 * threadIdx.x; i < a.n_c; i += 4 * kThreads) {
+    for (int i = 4 * threadIdx.x; i < a.n_c; i += 4 * kSelThreads) {
         const float4 f = __ldcg(reinterpret_cast<const float4*>(srow + i));
-        const float fv[4] = {f.x, f.y, f.z, f.w};
+        float fv[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             if (i + e < a.n_c) {
-                region_f[i + e] = fv[e];
+                if (vrow && !vrow[i + e]) fv[e] = -INFINITY;
+                if (small) keys[i + e] = fv[e];
                 const uint32_t kk = ordered_u32(fv[e]);
                 if (kk > kOrderedNegInf) klo = min(klo, kk);
                 khi = max(khi, kk);
@@ -352,8 +353,8 @@ __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_consta
         khi = max(khi, __shfl_xor_sync(0xffffffffu, khi, off));
     }
     if (lane == 0) {
-        atomicMin(&su[1], klo);
-        atomicMax(&su[2], khi);
+        atomicMin(&lohi[0], klo);
+        atomicMax(&lohi[1], khi);
     }
     __syncthreads();
     int32_t* selr = a.sel + (int64_t)r * a.nk;
@@ -362,16 +363,17 @@ __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_consta
         selr[pos] = i;
         if (selo) selo[pos] = i;
     };
-    if (a.n_c <= 16 * kThreads)
-        block_topk_small<kThreads>(region_f, a.n_c, a.nk, su[1], su[2], hist, misc, scan, emit);
+    if (small)
+        block_topk_small<kSelThreads>(keys, a.n_c, a.nk, lohi[0], lohi[1], hist, misc, scan, emit);
     else
-        block_topk<kThreads, true>([&](int i) { return ordered_u32(region_f[i]); }, a.n_c, a.nk, hist, misc, scan,
-                                   emit, true, su[1], su[2]);
+        block_topk<kSelThreads, true>(
+            [&](int i) { return (vrow && !vrow[i]) ? kOrderedNegInf : ordered_u32(__ldcg(srow + i)); }, a.n_c, a.nk,
+            hist, misc, scan, emit, true, lohi[0], lohi[1]);
 }
 
-// ---------------------------------------------------------------- kernel B: attend + merge
-// One CTA per (row, tile of 8 entries); each warp attends 2 pages.  The CTA
-// that completes a row's last tile merges the row's partials.
+// ---------------------------------------------------------------- kernel 3: attend
+// One CTA per (row, 8 entries of 16 tokens); each warp attends 2 pages and
+// the CTA writes one partial (m, l, o) of the row.
 __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_constant__ Args a) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t base_u32 = smem_u32(smem_raw);
@@ -379,7 +381,6 @@ __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_co
     uint8_t* region = smem;
     float* region_f = reinterpret_cast<float*>(region);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kAttRegion);
-    uint32_t* su = reinterpret_cast<uint32_t*>(bars + kWarps * kSlots);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r = blockIdx.x / a.AT, tile = blockIdx.x % a.AT;
     if (threadIdx.x == 0) {
@@ -387,25 +388,30 @@ __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_co
         mbar_fence_init();
     }
     __syncthreads();
-    grid_dep_wait();  // the selection of the score kernel
+    grid_dep_wait();          // the selection of the select kernel
+    grid_dep_launch_next();   // the merge kernel may become resident (it waits for this grid)
     const int e0 = tile * kTileEntries;
     const int e1 = min(a.E, e0 + kTileEntries);
     const int pg0 = a.RS + a.RN;
     unsigned present[kSlots];
     bool have[kSlots];
+    // lane k reads the chunk id of the warp's k-th entry (all in flight at once)
+    int my_chunk = 0;
+    {
+        const int e = e0 + warp * kSlots + lane;
+        if (lane < kSlots && e < e1 && e >= pg0) {
+            const int p = e - pg0;
+            my_chunk = a.ST > 0 ? __ldcg(a.sel + (int64_t)r * a.nk + p) : p;
+            if (a.ST == 0 && a.sel_out) a.sel_out[(int64_t)r * a.nk + p] = p;  // identity selection
+        }
+    }
 #pragma unroll
     for (int k = 0; k < kSlots; ++k) {
         const int e = e0 + warp * kSlots + k;
         have[k] = e < e1;
         present[k] = 0u;
+        const int chunk = __shfl_sync(0xffffffffu, my_chunk, k);
         if (!have[k]) continue;
-        int chunk = 0;
-        if (e >= pg0) {
-            const int p = e - pg0;
-            chunk = a.ST > 0 ? (lane == 0 ? __ldcg(a.sel + (int64_t)r * a.nk + p) : 0) : p;
-            chunk = __shfl_sync(0xffffffffu, chunk, 0);
-            if (a.ST == 0 && a.sel_out && lane == 0) a.sel_out[(int64_t)r * a.nk + p] = p;
-        }
         unsigned pr;
         const int64_t y0 = entry_tokens(a, e, chunk, pr);
         present[k] = pr;
@@ -438,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_co
         page_attend(st, smem_u32(slot), present[k], a.G, a.sl2);
     }
     __syncthreads();
-    float* cm = region_f + 4224;
+    float* cm = region_f + 4224;  // past the warp scratch (4 x 1040 floats)
     float* cl = cm + 8;
     float* co = cl + 8;
     merge_warps(st, a.G, region_f, cm, cl, co);
@@ -449,30 +455,26 @@ __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_co
     }
     for (int i = threadIdx.x; i < a.G * kHeadDim / 4; i += kThreads)
         reinterpret_cast<float4*>(part + 16)[i] = reinterpret_cast<const float4*>(co)[i];
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        fence_acq_rel();
-        const uint32_t done = atomicAdd(a.ctrl + a.R + r, 1u);
-        su[0] = done == (uint32_t)(a.AT - 1);
-        if (su[0]) {
-            fence_acq_rel();
-            a.ctrl[a.R + r] = 0u;
-        }
-    }
-    __syncthreads();
-    if (!su[0]) return;
-    // ------------------------------------------------ row merge (last tile of row r)
+}
+
+// ---------------------------------------------------------------- kernel 4: merge
+// One CTA per row: the AT partials -> out (bf16) and lse (natural log).
+__global__ void __launch_bounds__(kThreads) raw_merge_kernel(const __grid_constant__ Args a) {
+    extern __shared__ __align__(16) float msm[];   // m [AT][8], l [AT][8], L [8]
+    const int r = blockIdx.x;
+    grid_dep_wait();          // the partials of the attend kernel
+    grid_dep_launch_next();   // the next launch may become resident (it waits for this grid)
     const float* pr = a.parts + (int64_t)r * a.AT * kPartFloats;
-    float* sm_m = region_f;              // [AT][8]
-    float* sm_l = sm_m + a.AT * 8;       // [AT][8]
-    float* sL = sm_l + a.AT * 8;         // [8]
+    float* sm_m = msm;
+    float* sm_l = sm_m + a.AT * 8;
+    float* sL = sm_l + a.AT * 8;
     for (int i = threadIdx.x; i < a.AT * a.G; i += kThreads) {
         const int t = i / a.G, h = i % a.G;
         sm_m[t * 8 + h] = __ldcg(pr + (int64_t)t * kPartFloats + h);
         sm_l[t * 8 + h] = __ldcg(pr + (int64_t)t * kPartFloats + 8 + h);
     }
     __syncthreads();
-    if (threadIdx.x < a.G) {  // per head: max, weights (in place of m), weighted sum of l
+    if ((int)threadIdx.x < a.G) {  // per head: max, weights (in place of m), weighted sum of l
         const int h = threadIdx.x;
         float M = -INFINITY;
         for (int t = 0; t < a.AT; ++t) M = fmaxf(M, sm_m[t * 8 + h]);
@@ -494,8 +496,9 @@ __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_co
             float4 v[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u)
-                v[u] = t0 + u < a.AT ? __ldcg(reinterpret_cast<const float4*>(pr + (int64_t)(t0 + u) * kPartFloats + 16) + i4)
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[u] = t0 + u < a.AT
+                           ? __ldcg(reinterpret_cast<const float4*>(pr + (int64_t)(t0 + u) * kPartFloats + 16) + i4)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 const float wt = t0 + u < a.AT ? sm_m[(t0 + u) * 8 + h] : 0.f;
@@ -562,20 +565,22 @@ static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near) {
     p.E = p.RS + p.RN + nsel;
     p.AT = p.E > 0 ? (p.E + kTileEntries - 1) / kTileEntries : 1;
     p.n_c_pad = (n_c + 31) & ~31;
-    p.off_scores = up256((size_t)8 * R);
+    p.off_scores = 0;
     p.off_sel = p.off_scores + up256((size_t)R * p.n_c_pad * 4);
     p.off_parts = p.off_sel + up256((size_t)R * (nk > 0 ? nk : 1) * 4);
     p.bytes = p.off_parts + up256((size_t)R * p.AT * kPartFloats * 4);
     return p;
 }
 
-static size_t score_smem() { return kScoreRegion + (512 + 8 + 2 * kThreads) * 4 + kHeadDim * 2 + kWarps * 8 + 16; }
-static size_t attend_smem() { return 1024 + kAttRegion + kWarps * kSlots * 8 + 16; }
+static size_t score_smem() { return kScoreRegion + kHeadDim * 2 + kWarps * 8; }
+static size_t select_smem() { return (size_t)(kSelSmall + 512 + 8 + 2 * kSelThreads + 2) * 4; }
+static size_t attend_smem() { return 1024 + kAttRegion + kWarps * kSlots * 8; }
+static size_t merge_smem(int AT) { return (size_t)(2 * AT * 8 + 8) * 4; }
 
-static int launch_pdl(const void* fn, int grid, size_t smem, cudaStream_t stream, void** args) {
+static int launch_pdl(const void* fn, int grid, int threads, size_t smem, cudaStream_t stream, void** args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3((unsigned)threads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -650,7 +655,6 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
     a.sel_out = sel_out;
     a.status = status;
     uint8_t* ws = (uint8_t*)workspace;
-    a.ctrl = (uint32_t*)ws;
     a.scores = (float*)(ws + p.off_scores);
     a.sel = (int32_t*)(ws + p.off_sel);
     a.parts = (float*)(ws + p.off_parts);
@@ -661,15 +665,23 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
     if (!attr_set[dev]) {
         if (cudaFuncSetAttribute(raw_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem()) !=
                 cudaSuccess ||
+            cudaFuncSetAttribute(raw_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)select_smem()) != cudaSuccess ||
             cudaFuncSetAttribute(raw_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)attend_smem()) != cudaSuccess)
+                                 (int)attend_smem()) != cudaSuccess ||
+            cudaFuncSetAttribute(raw_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)merge_smem(kMaxTiles)) != cudaSuccess)
             return ZKV_ERR_LAUNCH;
         attr_set[dev] = true;
     }
     void* args[] = {&a};
+    const cudaStream_t st = (cudaStream_t)stream;
     int rc = ZKV_OK;
-    if (p.ST > 0)
-        rc = launch_pdl((const void*)raw_score_kernel, rows * p.ST, score_smem(), (cudaStream_t)stream, args);
-    if (rc != ZKV_OK) return rc;
-    return launch_pdl((const void*)raw_attend_kernel, rows * p.AT, attend_smem(), (cudaStream_t)stream, args);
+    if (p.ST > 0) {
+        rc = launch_pdl((const void*)raw_score_kernel, rows * p.ST, kThreads, score_smem(), st, args);
+        if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_select_kernel, rows, kSelThreads, select_smem(), st, args);
+    }
+    if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_attend_kernel, rows * p.AT, kThreads, attend_smem(), st, args);
+    if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_merge_kernel, rows, kThreads, merge_smem(p.AT), st, args);
+    return rc;
 }

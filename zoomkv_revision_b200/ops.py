@@ -705,7 +705,7 @@ def page_decode_raw(q, layer: RawLayer, n_c: int, nk: int, n_near: int, *, n_sin
         key = q.device.index if q.device.index is not None else torch.cuda.current_device()
         ws = _RAW_WS.get(key)
         if ws is None or ws.numel() < need:
-            ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=q.device)
+            ws = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=q.device)
             _RAW_WS[key] = ws
         workspace = ws
     check(lib().zkv_page_decode_raw(_p(qc), ctypes.byref(layer.struct), rows, G, n_max, int(n_c), int(nk),
