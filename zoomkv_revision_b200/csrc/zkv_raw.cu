@@ -20,7 +20,7 @@
 //    and is read with ldmatrix (K, B operand of S = Q K^T) and ldmatrix.trans
 //    (V, A operand of O^T = V^T P^T) into mma.sync m16n8k16 with an online
 //    softmax.  The CTA merges its warps and writes one partial (m, l, o).
-//  * raw_merge_kernel: one CTA per row: the row's partials -> out / lse.
+//  * raw_merge_kernel: one CTA per (row, head): the partials -> out / lse.
 //
 // Each kernel waits for its predecessor's grid with griddepcontrol.wait and
 // releases its successor right after, so a successor's CTAs become resident
@@ -48,7 +48,7 @@ constexpr int kPartFloats = 16 + 8 * kHeadDim;    // m[8], l[8], o[8][128]
 constexpr int kSelThreads = 256;                  // threads of a select CTA
 constexpr int kSelSmall = 16 * kSelThreads;       // rows up to this many chunks select from shared memory
 constexpr int kMaxChunks = 16384;
-constexpr int kMaxTiles = 2048;                   // attend tiles per row (merge weights in shared memory)
+constexpr int kMaxTiles = 2048;                   // attend tiles per row
 
 struct Args {
     CUtensorMap tk;  // raw keys   as [rows * cap][128] bf16, box 64 x 16, 128-B swizzle
@@ -458,63 +458,44 @@ __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_co
 }
 
 // ---------------------------------------------------------------- kernel 4: merge
-// One CTA per row: the AT partials -> out (bf16) and lse (natural log).
-__global__ void __launch_bounds__(kThreads) raw_merge_kernel(const __grid_constant__ Args a) {
-    extern __shared__ __align__(16) float msm[];   // m [AT][8], l [AT][8], L [8]
-    const int r = blockIdx.x;
+// One CTA per (row, head), one thread per dim: the row's AT partials of the
+// head -> out (bf16) and lse (natural log).  Partials come in batches of
+// kMergeBatch with every load of a batch in flight at once; batches combine
+// with an online rescale (one batch when AT <= kMergeBatch).
+constexpr int kMergeBatch = 32;
+__global__ void __launch_bounds__(kHeadDim) raw_merge_kernel(const __grid_constant__ Args a) {
+    const int r = blockIdx.x / a.G, h = blockIdx.x % a.G, d = threadIdx.x;
     grid_dep_wait();          // the partials of the attend kernel
     grid_dep_launch_next();   // the next launch may become resident (it waits for this grid)
     const float* pr = a.parts + (int64_t)r * a.AT * kPartFloats;
-    float* sm_m = msm;
-    float* sm_l = sm_m + a.AT * 8;
-    float* sL = sm_l + a.AT * 8;
-    for (int i = threadIdx.x; i < a.AT * a.G; i += kThreads) {
-        const int t = i / a.G, h = i % a.G;
-        sm_m[t * 8 + h] = __ldcg(pr + (int64_t)t * kPartFloats + h);
-        sm_l[t * 8 + h] = __ldcg(pr + (int64_t)t * kPartFloats + 8 + h);
-    }
-    __syncthreads();
-    if ((int)threadIdx.x < a.G) {  // per head: max, weights (in place of m), weighted sum of l
-        const int h = threadIdx.x;
-        float M = -INFINITY;
-        for (int t = 0; t < a.AT; ++t) M = fmaxf(M, sm_m[t * 8 + h]);
-        float L = 0.f;
-        for (int t = 0; t < a.AT; ++t) {
-            const float mt = sm_m[t * 8 + h];
-            const float wt = (mt == -INFINITY) ? 0.f : ex2(mt - M);
-            sm_m[t * 8 + h] = wt;
-            L += wt * sm_l[t * 8 + h];
-        }
-        sL[h] = L;
-        if (a.lse) a.lse[(int64_t)r * a.G + h] = (L > 0.f) ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
-    }
-    __syncthreads();
-    for (int i4 = threadIdx.x; i4 < a.G * (kHeadDim / 4); i4 += kThreads) {
-        const int h = i4 / (kHeadDim / 4);
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int t0 = 0; t0 < a.AT; t0 += 8) {  // 8 independent loads in flight per batch
-            float4 v[8];
+    float M = -INFINITY, L = 0.f, O = 0.f;
+    for (int t0 = 0; t0 < a.AT; t0 += kMergeBatch) {
+        float m[kMergeBatch], l[kMergeBatch], o[kMergeBatch];
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-                v[u] = t0 + u < a.AT
-                           ? __ldcg(reinterpret_cast<const float4*>(pr + (int64_t)(t0 + u) * kPartFloats + 16) + i4)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const float wt = t0 + u < a.AT ? sm_m[(t0 + u) * 8 + h] : 0.f;
-                acc.x += wt * v[u].x;
-                acc.y += wt * v[u].y;
-                acc.z += wt * v[u].z;
-                acc.w += wt * v[u].w;
-            }
+        for (int u = 0; u < kMergeBatch; ++u) {
+            const bool in = t0 + u < a.AT;
+            const float* pt = pr + (int64_t)(t0 + u) * kPartFloats;
+            m[u] = in ? __ldcg(pt + h) : -INFINITY;
+            l[u] = in ? __ldcg(pt + 8 + h) : 0.f;
+            o[u] = in ? __ldcg(pt + 16 + h * kHeadDim + d) : 0.f;
         }
-        const float L = sL[h];
-        const float inv = L > 0.f ? 1.f / L : 0.f;
-        uint2 o;
-        o.x = (uint32_t)f2bfbits(acc.x * inv) | ((uint32_t)f2bfbits(acc.y * inv) << 16);
-        o.y = (uint32_t)f2bfbits(acc.z * inv) | ((uint32_t)f2bfbits(acc.w * inv) << 16);
-        *reinterpret_cast<uint2*>(a.out + (int64_t)r * a.G * kHeadDim + 4 * i4) = o;
+        float Mb = M;
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; ++u) Mb = fmaxf(Mb, m[u]);
+        if (Mb == -INFINITY) continue;  // nothing attended so far
+        const float sc = (M == -INFINITY) ? 0.f : ex2(M - Mb);
+        L *= sc;
+        O *= sc;
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; ++u) {
+            const float wt = (m[u] == -INFINITY) ? 0.f : ex2(m[u] - Mb);
+            L += wt * l[u];
+            O += wt * o[u];
+        }
+        M = Mb;
     }
+    if (d == 0 && a.lse) a.lse[(int64_t)r * a.G + h] = (L > 0.f) ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+    a.out[((int64_t)r * a.G + h) * kHeadDim + d] = f2bfbits(L > 0.f ? O * (1.f / L) : 0.f);
 }
 
 // ---------------------------------------------------------------- host side
@@ -575,7 +556,6 @@ static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near) {
 static size_t score_smem() { return kScoreRegion + kHeadDim * 2 + kWarps * 8; }
 static size_t select_smem() { return (size_t)(kSelSmall + 512 + 8 + 2 * kSelThreads + 2) * 4; }
 static size_t attend_smem() { return 1024 + kAttRegion + kWarps * kSlots * 8; }
-static size_t merge_smem(int AT) { return (size_t)(2 * AT * 8 + 8) * 4; }
 
 static int launch_pdl(const void* fn, int grid, int threads, size_t smem, cudaStream_t stream, void** args) {
     cudaLaunchConfig_t cfg = {};
@@ -668,9 +648,7 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
             cudaFuncSetAttribute(raw_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)select_smem()) != cudaSuccess ||
             cudaFuncSetAttribute(raw_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)attend_smem()) != cudaSuccess ||
-            cudaFuncSetAttribute(raw_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)merge_smem(kMaxTiles)) != cudaSuccess)
+                                 (int)attend_smem()) != cudaSuccess)
             return ZKV_ERR_LAUNCH;
         attr_set[dev] = true;
     }
@@ -682,6 +660,6 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
         if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_select_kernel, rows, kSelThreads, select_smem(), st, args);
     }
     if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_attend_kernel, rows * p.AT, kThreads, attend_smem(), st, args);
-    if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_merge_kernel, rows, kThreads, merge_smem(p.AT), st, args);
+    if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_merge_kernel, rows * G, kHeadDim, 0, st, args);
     return rc;
 }
