@@ -14,12 +14,14 @@
 //    score to the workspace.
 //  * raw_select_kernel: one CTA per row: invalid chunks -> -inf, then the top
 //    nk chunk ids (ties to the lowest id, ascending).
-//  * raw_attend_kernel: one CTA per (row, 8 entries of 16 tokens): sink and
-//    near rows, then selected pages.  Each page comes in as four 2-D TMA
-//    tensor copies with the 128-byte swizzle (K and V, dims 0-63 and 64-127)
-//    and is read with ldmatrix (K, B operand of S = Q K^T) and ldmatrix.trans
-//    (V, A operand of O^T = V^T P^T) into mma.sync m16n8k16 with an online
-//    softmax.  The CTA merges its warps and writes one partial (m, l, o).
+//  * raw_attend_kernel: one CTA per (row, EPC entries of 16 tokens) with EPC
+//    chosen so that the grid is one wave (3 CTAs per SM): sink and near rows,
+//    then selected pages.  Each warp cycles two slots: a page comes in as
+//    four 2-D TMA tensor copies with the 128-byte swizzle (K and V, dims 0-63
+//    and 64-127), is read with ldmatrix (K, B operand of S = Q K^T) and
+//    ldmatrix.trans (V, A operand of O^T = V^T P^T) into mma.sync m16n8k16
+//    with an online softmax, and the slot's next copy is issued at once.  The
+//    CTA merges its warps and writes one partial (m, l, o).
 //  * raw_merge_kernel: one CTA per (row, head): the partials -> out / lse.
 //
 // Each kernel waits for its predecessor's grid with griddepcontrol.wait and
@@ -29,6 +31,7 @@
 #include <cuda.h>
 
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 
 #include "zkv_common.cuh"
@@ -59,7 +62,7 @@ struct Args {
     const uint8_t* valid;
     int64_t cap, page_base;
     int R, G, n_max, n_c, nk, n_sink, near_start, n_near;
-    int ST, AT, RS, RN, E, n_c_pad;
+    int ST, AT, RS, RN, E, n_c_pad, EPC;
     float sl2;
     uint16_t* out;
     float* lse;
@@ -372,7 +375,9 @@ __global__ void __launch_bounds__(kSelThreads) raw_select_kernel(const __grid_co
 }
 
 // ---------------------------------------------------------------- kernel 3: attend
-// One CTA per (row, 8 entries of 16 tokens); each warp attends 2 pages and
+// One CTA per (row, EPC entries of 16 tokens), sized so that the grid is one
+// wave; warp w attends entries e0 + w, e0 + w + 4, ... through two TMA slots
+// (the next page's copy is issued as soon as a slot's page is consumed) and
 // the CTA writes one partial (m, l, o) of the row.
 __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_constant__ Args a) {
     extern __shared__ uint8_t smem_raw[];
@@ -390,58 +395,61 @@ __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_co
     __syncthreads();
     grid_dep_wait();          // the selection of the select kernel
     grid_dep_launch_next();   // the merge kernel may become resident (it waits for this grid)
-    const int e0 = tile * kTileEntries;
-    const int e1 = min(a.E, e0 + kTileEntries);
+    const int e0 = tile * a.EPC;
+    const int e1 = min(a.E, e0 + a.EPC);
+    const int nw = e1 - e0 > warp ? (e1 - e0 - warp + kWarps - 1) / kWarps : 0;  // pages of this warp (<= 32)
     const int pg0 = a.RS + a.RN;
-    unsigned present[kSlots];
-    bool have[kSlots];
-    // lane k reads the chunk id of the warp's k-th entry (all in flight at once)
+    // lane j reads the chunk id of the warp's j-th entry (all in flight at once)
     int my_chunk = 0;
-    {
-        const int e = e0 + warp * kSlots + lane;
-        if (lane < kSlots && e < e1 && e >= pg0) {
+    if (lane < nw) {
+        const int e = e0 + warp + kWarps * lane;
+        if (e >= pg0) {
             const int p = e - pg0;
             my_chunk = a.ST > 0 ? __ldcg(a.sel + (int64_t)r * a.nk + p) : p;
             if (a.ST == 0 && a.sel_out) a.sel_out[(int64_t)r * a.nk + p] = p;  // identity selection
         }
     }
-#pragma unroll
-    for (int k = 0; k < kSlots; ++k) {
-        const int e = e0 + warp * kSlots + k;
-        have[k] = e < e1;
-        present[k] = 0u;
-        const int chunk = __shfl_sync(0xffffffffu, my_chunk, k);
-        if (!have[k]) continue;
+    const uint32_t slot0 = smem_u32(region) + (uint32_t)(warp * kSlots * kSlotBytes);
+    auto issue = [&](int j) -> unsigned {  // warp-uniform; returns the page's present mask
+        const int chunk = __shfl_sync(0xffffffffu, my_chunk, j & 31);
         unsigned pr;
-        const int64_t y0 = entry_tokens(a, e, chunk, pr);
-        present[k] = pr;
+        const int64_t y0 = entry_tokens(a, e0 + warp + kWarps * j, chunk, pr);
         if (lane == 0) {
             const int y = (int)((int64_t)r * a.cap + y0);
-            const uint32_t dst = smem_u32(region) + (uint32_t)((warp * kSlots + k) * kSlotBytes);
-            uint64_t* bar = bars + warp * kSlots + k;
+            const uint32_t dst = slot0 + (uint32_t)((j & 1) * kSlotBytes);
+            uint64_t* bar = bars + warp * kSlots + (j & 1);
             mbar_arrive_expect_tx(bar, kSlotBytes);
             tma_load_2d(dst, &a.tk, 0, y, bar);
             tma_load_2d(dst + 2048, &a.tk, 64, y, bar);
             tma_load_2d(dst + 4096, &a.tv, 0, y, bar);
             tma_load_2d(dst + 6144, &a.tv, 64, y, bar);
         }
-    }
+        return pr;
+    };
+    unsigned pres0 = nw > 0 ? issue(0) : 0u;
+    unsigned pres1 = nw > 1 ? issue(1) : 0u;
     WarpState st;
     state_init(st, a.q + (int64_t)r * a.G * kHeadDim, a.G);
-#pragma unroll
-    for (int k = 0; k < kSlots; ++k) {
-        if (!have[k]) continue;
-        if (!mbar_wait(bars + warp * kSlots + k, 0, a.status)) continue;  // status set; the page is skipped
-        uint8_t* slot = region + (warp * kSlots + k) * kSlotBytes;
-        if (present[k] != 0xffffu) {  // zero the V rows of absent tokens (p = 0 must meet finite V)
+    for (int j = 0; j < nw; ++j) {
+        const int sl = j & 1;
+        const unsigned pres = sl ? pres1 : pres0;
+        if (!mbar_wait(bars + warp * kSlots + sl, (uint32_t)((j >> 1) & 1), a.status)) break;  // status set
+        uint8_t* slot = region + (warp * kSlots + sl) * kSlotBytes;
+        if (pres != 0xffffu) {  // zero the V rows of absent tokens (p = 0 must meet finite V)
             for (int i = lane; i < 16 * 16; i += 32) {
                 const int tkn = i >> 4, box = (i >> 3) & 1, c = i & 7;
-                if (!((present[k] >> tkn) & 1u))
+                if (!((pres >> tkn) & 1u))
                     *reinterpret_cast<uint4*>(slot + 4096 + box * 2048 + tkn * 128 + c * 16) = make_uint4(0, 0, 0, 0);
             }
             __syncwarp();
         }
-        page_attend(st, smem_u32(slot), present[k], a.G, a.sl2);
+        page_attend(st, slot0 + (uint32_t)(sl * kSlotBytes), pres, a.G, a.sl2);
+        if (j + 2 < nw) {  // refill the slot: generic reads/writes of it before the async-proxy copy
+            fence_proxy_async();
+            __syncwarp();
+            const unsigned np = issue(j + 2);
+            if (sl) pres1 = np; else pres0 = np;
+        }
     }
     __syncthreads();
     float* cm = region_f + 4224;  // past the warp scratch (4 x 1040 floats)
@@ -531,11 +539,26 @@ static bool encode_rows(CUtensorMap* map, const void* base, int64_t n_tok) {
 }
 
 struct Plan {
-    int ST, AT, RS, RN, E, n_c_pad;
+    int ST, AT, RS, RN, E, n_c_pad, EPC;
     size_t off_scores, off_sel, off_parts, bytes;
 };
 
 static size_t up256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Attend CTAs resident per SM (shared memory: 3 x 66.6 KiB).
+constexpr int kAttendPerSm = 3;
+
+static int sm_count() {
+    static int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
 
 static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near) {
     Plan p;
@@ -544,12 +567,25 @@ static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near) {
     p.RS = (n_sink + 15) / 16;
     p.RN = (n_near + 15) / 16;
     p.E = p.RS + p.RN + nsel;
-    p.AT = p.E > 0 ? (p.E + kTileEntries - 1) / kTileEntries : 1;
+    // CTAs per row: one wave of attend CTAs when the rows allow it, at most
+    // 128 entries per CTA (a warp's chunk ids in one warp-wide load), at least
+    // kTileEntries entries per CTA
+    {
+        const int slots = kAttendPerSm * sm_count();
+        int c = R > 0 ? slots / R : 1;
+        c = std::max(1, std::min(c, (p.E + kTileEntries - 1) / kTileEntries));
+        c = std::max(c, (p.E + 127) / 128);
+        p.EPC = p.E > 0 ? (p.E + c - 1) / c : 1;
+        p.AT = p.E > 0 ? (p.E + p.EPC - 1) / p.EPC : 1;
+    }
     p.n_c_pad = (n_c + 31) & ~31;
     p.off_scores = 0;
     p.off_sel = p.off_scores + up256((size_t)R * p.n_c_pad * 4);
     p.off_parts = p.off_sel + up256((size_t)R * (nk > 0 ? nk : 1) * 4);
-    p.bytes = p.off_parts + up256((size_t)R * p.AT * kPartFloats * 4);
+    // partials for the most CTAs per row any device can use (kTileEntries
+    // entries each), so the size does not depend on the SM count
+    const int max_tiles = p.E > 0 ? (p.E + kTileEntries - 1) / kTileEntries : 1;
+    p.bytes = p.off_parts + up256((size_t)R * max_tiles * kPartFloats * 4);
     return p;
 }
 
@@ -629,6 +665,7 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
     a.RN = p.RN;
     a.E = p.E;
     a.n_c_pad = p.n_c_pad;
+    a.EPC = p.EPC;
     a.sl2 = scale * 1.4426950408889634f;
     a.out = (uint16_t*)out;
     a.lse = lse;
