@@ -71,6 +71,8 @@ def oracle_raw(rc, q, nk, rows=None):
     (3, 1, 2, 64, 8, 0, 0),        # pages only
     (1, 1, 4, 4096, 128, 0, 128),  # shared-memory select at its largest n_c
     (1, 1, 4, 5001, 300, 64, 64),  # n_c > 4096: the radix select path over global scores
+    (8, 8, 4, 300, 24, 5, 37),     # 64 rows: a few attend CTAs per row
+    (4, 8, 2, 200, 100, 0, 16),    # 32 rows, 13 entries per attend CTA
 ])
 def test_raw_matches_oracle(bs, H, G, n_c, nk, n_sink, n_near):
     rc = W.build_raw_cache(11 + n_c, bs, H, 16 * n_c, n_near, DEV, n_sink=n_sink)
