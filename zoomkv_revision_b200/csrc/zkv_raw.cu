@@ -538,6 +538,50 @@ static bool encode_rows(CUtensorMap* map, const void* base, int64_t n_tok) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Tensor maps of recently used (keys, values, rows) triples: encoding two
+// maps costs a few microseconds of host time per call, and a decode loop
+// calls the same layers over and over.  A map depends only on the base
+// address and the row count, both part of the key.
+struct MapEntry {
+    const void* keys;
+    const void* values;
+    int64_t n_tok;
+    int dev;
+    CUtensorMap tk, tv;
+};
+constexpr int kMapCache = 128;
+
+static bool cached_maps(CUtensorMap* tk, CUtensorMap* tv, const void* keys, const void* values, int64_t n_tok) {
+    static MapEntry cache[kMapCache];
+    static int used = 0, next = 0;
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (int i = 0; i < used; ++i) {
+            const MapEntry& e = cache[i];
+            if (e.keys == keys && e.values == values && e.n_tok == n_tok && e.dev == dev) {
+                *tk = e.tk;
+                *tv = e.tv;
+                return true;
+            }
+        }
+    }
+    if (!encode_rows(tk, keys, n_tok) || !encode_rows(tv, values, n_tok)) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    MapEntry& e = cache[next];
+    e.keys = keys;
+    e.values = values;
+    e.n_tok = n_tok;
+    e.dev = dev;
+    e.tk = *tk;
+    e.tv = *tv;
+    next = (next + 1) % kMapCache;
+    used = used < kMapCache ? used + 1 : used;
+    return true;
+}
+
 struct Plan {
     int ST, AT, RS, RN, E, n_c_pad, EPC;
     size_t off_scores, off_sel, off_parts, bytes;
@@ -643,8 +687,7 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
         return ZKV_ERR_ALIGN;
     Args a;
     memset(&a, 0, sizeof(a));
-    if (!encode_rows(&a.tk, L.keys, (int64_t)rows * cap) || !encode_rows(&a.tv, L.values, (int64_t)rows * cap))
-        return ZKV_ERR_LAUNCH;
+    if (!cached_maps(&a.tk, &a.tv, L.keys, L.values, (int64_t)rows * cap)) return ZKV_ERR_LAUNCH;
     a.q = (const uint16_t*)q;
     a.cmin = (const uint16_t*)L.chunk_min;
     a.cmax = (const uint16_t*)L.chunk_max;

@@ -56,7 +56,13 @@ __all__ = [
 ]
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(t: torch.Tensor) -> int:
+    """The current CUDA stream of t's device (its raw handle)."""
+    if _RAW_STREAM is not None and t.device.index is not None:
+        return _RAW_STREAM(t.device.index)
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
@@ -675,6 +681,7 @@ class RawLayer:
 
 
 _RAW_WS: dict = {}
+_RAW_NEED: dict = {}
 
 
 def page_decode_raw_ws_bytes(rows: int, n_c: int, nk: int, n_sink: int, n_near: int) -> int:
@@ -688,9 +695,10 @@ def page_decode_raw(q, layer: RawLayer, n_c: int, nk: int, n_near: int, *, n_sin
     Quest scores of chunks [0, n_c), top nk chunks, then attention over the
     selected chunks' raw rows, the sink rows [0, n_sink) and the near rows
     [near_start, near_start + n_near) of layer.keys / layer.values.
-    workspace: optional ZERO-FILLED uint8 device tensor of at least
-    page_decode_raw_ws_bytes(...) bytes (default: one cached buffer per
-    device, so calls on concurrent streams should pass their own)."""
+    workspace: optional uint8 device tensor of at least
+    page_decode_raw_ws_bytes(...) bytes, scratch only (default: one cached
+    buffer per device, so calls on concurrent streams should pass their
+    own)."""
     cmin = layer.tensors[0]
     bs, H, n_max, D = cmin.shape
     _dtype("q", q, torch.bfloat16)
@@ -701,7 +709,10 @@ def page_decode_raw(q, layer: RawLayer, n_c: int, nk: int, n_near: int, *, n_sin
     scale = (1.0 / D ** 0.5) if scale is None else float(scale)
     rows = bs * H
     if workspace is None:
-        need = page_decode_raw_ws_bytes(rows, n_c, nk, n_sink, n_near)
+        shape = (rows, int(n_c), int(nk), int(n_sink), int(n_near))
+        need = _RAW_NEED.get(shape)
+        if need is None:
+            need = _RAW_NEED[shape] = page_decode_raw_ws_bytes(*shape)
         key = q.device.index if q.device.index is not None else torch.cuda.current_device()
         ws = _RAW_WS.get(key)
         if ws is None or ws.numel() < need:
