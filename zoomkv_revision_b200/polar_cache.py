@@ -50,8 +50,8 @@ Attention modes (env ZKV_ATTENTION_MODE):
   "page"                 the reference's page mode (dense_topk = sparse_topk =
                          16, final_topk = the page budget): Quest top-nk
                          chunks, attention over their raw bf16 rows + sink +
-                         near rows, in one persistent launch per layer
-                         (zkv_page_decode_raw);
+                         near rows: zkv_page_decode_raw, four launches per
+                         layer chained by programmatic dependent launch;
   "page4"                a lossy variant of page mode: the selected pages are
                          read as 4-bit KIVI keys and 4-bit values (group 32),
                          dequantised in registers (zkv_page_decode).
@@ -656,9 +656,9 @@ class polar_cache:
     def _compute_page_raw(self, q, l, n_chunks, nk, total):
         """The reference's page mode: Quest top-nk of the encoded chunks, then
         attention over their raw rows, the sink rows and every row from the
-        first unencoded token on (the skipped tail and the near zone), in one
-        launch (REF:1589-1775 with dense_topk = sparse_topk = 16 and
-        final_topk = nk * 16)."""
+        first unencoded token on (the skipped tail and the near zone)
+        (REF:1589-1775 with dense_topk = sparse_topk = 16 and final_topk =
+        nk * 16)."""
         if self._raw_layers[l] is None:
             self._raw_layers[l] = ops.RawLayer(self.chunk_min[l], self.chunk_max[l], self.chunk_valid[l],
                                                self.keys[l], self.values[l], page_base=self.sink_size)
