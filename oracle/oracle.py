@@ -24,7 +24,8 @@ __all__ = [
     "topk_gather_concat", "attn_dense", "page_decode", "lse_merge", "kivi_dequant_chunk",
     "vdequant_tokens", "page_layout_values", "kivi_scale", "rq_mag_tables", "rq_encode", "rq_query", "collision_weights",
     "collision_count", "update_cache_cnt_sorted", "rerank4", "coarse2bit", "rq_query_4bit", "popcount_est",
-    "exact_ip", "h2d_gather", "h2d_gather_packed", "page_decode_raw",
+    "exact_ip", "h2d_gather", "h2d_gather_packed", "page_decode_raw", "large_minmax", "sub_chunk_score",
+    "map_back", "hier_select", "hier_plan",
 ]
 
 
@@ -159,6 +160,85 @@ def topk_f32(scores: np.ndarray, k: int) -> np.ndarray:
     out = np.empty((R, k), np.int64)
     L.orc_topk_f32(_p(s), R, n, ctypes.c_int64(n), k, _p(out))
     return out.reshape(s.shape[:-1] + (k,))
+
+
+# ----------------------------------------------------------------- hierarchical Quest
+def hier_plan(n_chunks: int, factor: int, large_ratio: float = 0.3, small_ratio: float = 0.3):
+    """(n_large, nk_large, nk_small) of _refresh_quest_chunk_cache's
+    hierarchical branch (polar_cache_kivi_quest_density_seperate_kernel.py:
+    1462-1468)."""
+    import math
+    n_large = n_chunks // factor
+    if n_large <= 0:
+        return 0, 0, 0
+    nk_large = min(max(1, int(math.ceil(n_large * large_ratio))), n_large)
+    nk_sub = nk_large * factor
+    nk_small = min(max(1, int(math.ceil(nk_sub * small_ratio))), nk_sub)
+    return n_large, nk_large, nk_small
+
+
+def large_minmax(mn, mx, valid_end: int, factor: int, n_max_large: int | None = None):
+    """_update_large_chunk_minmax (:1762-1798) over every group ->
+    (large_min, large_max, large_valid)."""
+    L = lib()
+    mn = np.ascontiguousarray(mn, np.uint16)
+    mx = np.ascontiguousarray(mx, np.uint16)
+    lead, n_max = mn.shape[:-2], mn.shape[-2]
+    R = int(np.prod(lead)) if lead else 1
+    nml = (n_max + factor - 1) // factor if n_max_large is None else int(n_max_large)
+    lmn = np.empty((R, nml, 128), np.uint16)
+    lmx = np.empty((R, nml, 128), np.uint16)
+    lv = np.empty((R, nml), np.uint8)
+    L.orc_large_minmax.argtypes = [ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 5 + [ctypes.c_void_p] * 3
+    L.orc_large_minmax(_p(mn), _p(mx), R, n_max, int(valid_end), int(factor), nml, _p(lmn), _p(lmx), _p(lv))
+    return lmn.reshape(lead + (nml, 128)), lmx.reshape(lead + (nml, 128)), lv.reshape(lead + (nml,))
+
+
+def sub_chunk_score(raw_q, mn, mx, large_idx, factor: int):
+    """quest_sub_chunk_score (quest/quest_chunk_score.cu:263-360)."""
+    L = lib()
+    q = np.ascontiguousarray(raw_q, np.uint16).reshape(-1, 128)
+    R = q.shape[0]
+    mn = np.ascontiguousarray(mn, np.uint16).reshape(R, -1, 128)
+    mx = np.ascontiguousarray(mx, np.uint16).reshape(R, -1, 128)
+    li = np.ascontiguousarray(large_idx, np.int64).reshape(R, -1)
+    out = np.empty((R, li.shape[1] * factor), np.float32)
+    L.orc_sub_chunk_score.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    L.orc_sub_chunk_score(_p(q), _p(mn), _p(mx), _p(li), R, mn.shape[1], li.shape[1], int(factor), _p(out))
+    return out
+
+
+def map_back(large_idx, sub_pos, factor: int, n_chunks: int):
+    """quest_map_back (quest/quest_chunk_score.cu:363-416)."""
+    L = lib()
+    li = np.ascontiguousarray(large_idx, np.int64)
+    sp = np.ascontiguousarray(sub_pos, np.int64)
+    R = int(np.prod(li.shape[:-1])) if li.ndim > 1 else 1
+    out = np.empty(sp.shape, np.int64)
+    L.orc_map_back.argtypes = [ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 5 + [ctypes.c_void_p]
+    L.orc_map_back(_p(li), _p(sp), R, li.shape[-1], sp.shape[-1], int(factor), int(n_chunks), _p(out))
+    return out
+
+
+def hier_select(raw_q, mn, mx, lmn, lmx, lvalid, n_chunks: int, factor: int, nk_large: int, nk_small: int):
+    """_quest_pick_coarse_indices_hierarchical (:1852-1940) -> (chunk ids
+    [R, nk_small], large ids [R, nk_large], sub scores [R, nk_large*factor])."""
+    L = lib()
+    q = np.ascontiguousarray(raw_q, np.uint16).reshape(-1, 128)
+    R = q.shape[0]
+    mn = np.ascontiguousarray(mn, np.uint16).reshape(R, -1, 128)
+    mx = np.ascontiguousarray(mx, np.uint16).reshape(R, -1, 128)
+    lmn = np.ascontiguousarray(lmn, np.uint16).reshape(R, -1, 128)
+    lmx = np.ascontiguousarray(lmx, np.uint16).reshape(R, -1, 128)
+    lv = None if lvalid is None else np.ascontiguousarray(lvalid, np.uint8).reshape(R, -1)
+    out = np.empty((R, nk_small), np.int64)
+    li = np.empty((R, nk_large), np.int64)
+    sub = np.empty((R, nk_large * factor), np.float32)
+    L.orc_hier_select.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] + [ctypes.c_void_p] * 3 + \
+        [ctypes.c_int] * 6 + [ctypes.c_void_p] * 3
+    L.orc_hier_select(_p(q), _p(mn), _p(mx), mn.shape[1], _p(lmn), _p(lmx), _p(lv), lmn.shape[1], R, int(n_chunks),
+                      int(factor), int(nk_large), int(nk_small), _p(out), _p(li), _p(sub))
+    return out, li, sub
 
 
 def topk_i32(vals: np.ndarray, k: int) -> np.ndarray:

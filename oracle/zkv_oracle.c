@@ -230,6 +230,99 @@ void orc_topk_f32(const float* scores, int rows, int len, int64_t row_stride,
     free(buf);
 }
 
+/* ---------------- hierarchical Quest ---------------- */
+void orc_large_minmax(const uint16_t* mn, const uint16_t* mx, int rows, int n_max, int valid_end, int factor,
+                      int n_max_large, uint16_t* lmn, uint16_t* lmx, uint8_t* lvalid) {
+    int r, g, b, d;
+    for (r = 0; r < rows; ++r)
+        for (g = 0; g < n_max_large; ++g) {
+            int b_lo = g * factor, b_hi = b_lo + factor;
+            size_t o = ((size_t)r * n_max_large + g) * 128;
+            if (b_hi > valid_end) b_hi = valid_end;
+            if (b_hi > n_max) b_hi = n_max;
+            lvalid[(size_t)r * n_max_large + g] = b_hi > b_lo;
+            for (d = 0; d < 128; ++d) {
+                uint16_t a = 0, z = 0;
+                if (b_hi > b_lo) {
+                    a = mn[((size_t)r * n_max + b_lo) * 128 + d];
+                    z = mx[((size_t)r * n_max + b_lo) * 128 + d];
+                    for (b = b_lo + 1; b < b_hi; ++b) {
+                        uint16_t u = mn[((size_t)r * n_max + b) * 128 + d];
+                        uint16_t v = mx[((size_t)r * n_max + b) * 128 + d];
+                        if (orc_bf2f(u) < orc_bf2f(a)) a = u;
+                        if (orc_bf2f(v) > orc_bf2f(z)) z = v;
+                    }
+                }
+                lmn[o + d] = a;
+                lmx[o + d] = z;
+            }
+        }
+}
+
+void orc_sub_chunk_score(const uint16_t* q, const uint16_t* mn, const uint16_t* mx, const int64_t* large_idx,
+                         int rows, int n_max, int n_sel, int factor, float* sub) {
+    int r, j, s;
+    for (r = 0; r < rows; ++r)
+        for (j = 0; j < n_sel; ++j)
+            for (s = 0; s < factor; ++s) {
+                int64_t c = large_idx[(size_t)r * n_sel + j] * factor + s;
+                float* o = sub + (size_t)r * n_sel * factor + (size_t)j * factor + s;
+                if (c < 0 || c >= n_max) {
+                    *o = -INFINITY;
+                    continue;
+                }
+                *o = quest_one(q + (size_t)r * 128, mn + ((size_t)r * n_max + c) * 128,
+                               mx + ((size_t)r * n_max + c) * 128);
+            }
+}
+
+void orc_map_back(const int64_t* large_idx, const int64_t* sub_pos, int rows, int nk_large, int nk_small,
+                  int factor, int n_chunks, int64_t* out) {
+    int r, k;
+    for (r = 0; r < rows; ++r)
+        for (k = 0; k < nk_small; ++k) {
+            int64_t p = sub_pos[(size_t)r * nk_small + k];
+            int64_t* o = out + (size_t)r * nk_small + k;
+            int64_t sel, c;
+            if (p < 0 || p >= (int64_t)nk_large * factor) {
+                *o = -1;
+                continue;
+            }
+            sel = p / factor;
+            c = large_idx[(size_t)r * nk_large + sel] * factor + (p - sel * factor);
+            if (c < 0) c = 0;
+            if (c >= n_chunks) c = n_chunks - 1;
+            *o = c;
+        }
+}
+
+void orc_hier_select(const uint16_t* q, const uint16_t* mn, const uint16_t* mx, int n_max, const uint16_t* lmn,
+                     const uint16_t* lmx, const uint8_t* lvalid, int n_max_large, int rows, int n_chunks,
+                     int factor, int nk_large, int nk_small, int64_t* out, int64_t* large_idx_out, float* sub_out) {
+    int n_large = n_chunks / factor, r;
+    int n_sub = nk_large * factor;
+    float* ls = (float*)malloc(sizeof(float) * (size_t)(n_large > 0 ? n_large : 1));
+    int64_t* li = (int64_t*)malloc(sizeof(int64_t) * (size_t)(nk_large > 0 ? nk_large : 1));
+    float* sub = (float*)malloc(sizeof(float) * (size_t)(n_sub > 0 ? n_sub : 1));
+    int64_t* pos = (int64_t*)malloc(sizeof(int64_t) * (size_t)(nk_small > 0 ? nk_small : 1));
+    for (r = 0; r < rows; ++r) {
+        const uint16_t* qr = q + (size_t)r * 128;
+        orc_quest_score(qr, lmn + (size_t)r * n_max_large * 128, lmx + (size_t)r * n_max_large * 128,
+                        lvalid ? lvalid + (size_t)r * n_max_large : NULL, ls, 1, n_large, n_max_large);
+        orc_topk_f32(ls, 1, n_large, n_large, nk_large, li);
+        orc_sub_chunk_score(qr, mn + (size_t)r * n_max * 128, mx + (size_t)r * n_max * 128, li, 1, n_max,
+                            nk_large, factor, sub);
+        orc_topk_f32(sub, 1, n_sub, n_sub, nk_small, pos);
+        orc_map_back(li, pos, 1, nk_large, nk_small, factor, n_chunks, out + (size_t)r * nk_small);
+        if (large_idx_out) memcpy(large_idx_out + (size_t)r * nk_large, li, sizeof(int64_t) * (size_t)nk_large);
+        if (sub_out) memcpy(sub_out + (size_t)r * n_sub, sub, sizeof(float) * (size_t)n_sub);
+    }
+    free(ls);
+    free(li);
+    free(sub);
+    free(pos);
+}
+
 void orc_topk_i32(const int32_t* vals, int rows, int len, int64_t row_stride,
                   int k, int64_t* out) {
     kv_t* buf = (kv_t*)malloc(sizeof(kv_t) * (size_t)(len > 0 ? len : 1));

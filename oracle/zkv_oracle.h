@@ -69,6 +69,38 @@ void orc_quest_score(const uint16_t* q, const uint16_t* mn, const uint16_t* mx,
 void orc_topk_f32(const float* scores, int rows, int len, int64_t row_stride,
                   int k, int64_t* out);
 
+/* Hierarchical Quest (cache_hub/polar_cache_kivi_quest_density_seperate_
+ * kernel.py; off in the single-layer KIVI cache, on by default in the
+ * separate-kernel one, :210-237).
+ * orc_large_minmax: _update_large_chunk_minmax (:1762-1798) over every
+ * group: group g covers chunks [g*factor, min(g*factor + factor, valid_end));
+ * its min/max are the element-wise bf16 min/max of those chunks' min/max
+ * and it is valid when non-empty (empty groups: zero bits, invalid).
+ * mn/mx [rows][n_max][128]; lmn/lmx [rows][n_max_large][128];
+ * lvalid [rows][n_max_large].                                             */
+void orc_large_minmax(const uint16_t* mn, const uint16_t* mx, int rows, int n_max, int valid_end, int factor,
+                      int n_max_large, uint16_t* lmn, uint16_t* lmx, uint8_t* lvalid);
+/* quest_sub_chunk_score (quest/quest_chunk_score.cu:263-360): for each of
+ * the n_sel selected large chunks of a row, the Quest scores of its factor
+ * small chunks, position j*factor + s; a chunk id outside [0, n_max) scores
+ * -inf.  large_idx [rows][n_sel]; sub [rows][n_sel*factor].              */
+void orc_sub_chunk_score(const uint16_t* q, const uint16_t* mn, const uint16_t* mx, const int64_t* large_idx,
+                         int rows, int n_max, int n_sel, int factor, float* sub);
+/* quest_map_back (quest/quest_chunk_score.cu:363-416): position p of the
+ * sub-chunk top-k -> large_idx[p / factor] * factor + p % factor, clamped to
+ * [0, n_chunks); p outside [0, nk_large*factor) -> -1.                    */
+void orc_map_back(const int64_t* large_idx, const int64_t* sub_pos, int rows, int nk_large, int nk_small,
+                  int factor, int n_chunks, int64_t* out);
+/* _quest_pick_coarse_indices_hierarchical (:1852-1940) for one layer:
+ * Quest over the n_chunks / factor large chunks (lvalid applied), their top
+ * nk_large, the sub-chunk scores of the selected ones, their top nk_small,
+ * mapped back to chunk ids.  Top-k as orc_topk_f32 (ties to the lowest
+ * index, ascending).  large_idx_out [rows][nk_large] and sub_out
+ * [rows][nk_large*factor] may be NULL.                                    */
+void orc_hier_select(const uint16_t* q, const uint16_t* mn, const uint16_t* mx, int n_max, const uint16_t* lmn,
+                     const uint16_t* lmx, const uint8_t* lvalid, int n_max_large, int rows, int n_chunks,
+                     int factor, int nk_large, int nk_small, int64_t* out, int64_t* large_idx_out, float* sub_out);
+
 /* Same selection over int32 rows (radix_topk_3d, topk/radix_topk.cu:157-240).*/
 void orc_topk_i32(const int32_t* vals, int rows, int len, int64_t row_stride,
                   int k, int64_t* out);
