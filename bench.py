@@ -432,6 +432,99 @@ def run_config1_reference(args):
         "clocks": clk.summary()}), flush=True)
 
 
+def run_config3_raw(args):
+    """Config 3 (Qwen3-4B shape, batch 1, 131072 context, budget 4096) in the
+    raw-row page mode on one GPU: the flat Quest pick against the hierarchical
+    one (large chunks of 16 pages, top 30 % of them, then the top 256 pages
+    among their sub-chunks, i.e. POLAR_QUEST_SMALL_RATIO chosen so that the
+    attended budget equals the flat one).  Prints one line; `value` is the
+    flat step, the hierarchical step and the bytes it cuts are extra keys."""
+    import torch
+    from zoomkv_revision_b200 import ops
+    from zoomkv_revision_b200 import workload as W
+    import math
+    dev = torch.device("cuda", 0)
+    layers, bs, H, ctx, budget = args.layers, 1, KV_HEADS, 131072, 4096
+    n_c, nk, n_near = (ctx - RESIDUAL) // PAGE, budget // PAGE, RESIDUAL
+    factor = 16
+    n_large = n_c // factor
+    nk_large = min(max(1, math.ceil(n_large * 0.3)), n_large)
+    small_ratio = nk / (nk_large * factor)
+    nk_small = min(max(1, math.ceil(nk_large * factor * small_ratio)), nk_large * factor)
+    caches, larges, qs = [], [], []
+    for l in range(layers):
+        rc = W.build_raw_cache(7000 + l, bs, H, n_c * PAGE, n_near, dev)
+        nml = (rc.chunk_min.shape[2] + factor - 1) // factor
+        lmn = torch.zeros(bs, H, nml, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+        lmx = torch.zeros_like(lmn)
+        lv = torch.zeros(bs, H, nml, dtype=torch.uint8, device=dev)
+        ops.quest_large_minmax(rc.chunk_min, rc.chunk_max, n_c, factor, lmn, lmx, lv)
+        caches.append(rc)
+        larges.append(ops.LargeLayer(lmn, lmx, lv))
+        qs.append(W.synth_query(torch.Generator(device=dev).manual_seed(900 + l), bs, H * G, dev))
+    lays = [rc.layer() for rc in caches]
+    rows = bs * H
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = torch.empty(bs, 1, H * G, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(max(ops.page_decode_raw_ws_bytes(rows, n_c, nk, 0, n_near),
+                         int(ops.lib().zkv_page_decode_raw_hier_ws_bytes(rows, n_c, factor, nk_large, nk_small, 0,
+                                                                          n_near))), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def flat():
+        for l in range(layers):
+            ops.page_decode_raw(qs[l], lays[l], n_c, nk, n_near, near_start=n_c * PAGE, out=out, status=status,
+                                workspace=ws)
+
+    def hier():
+        for l in range(layers):
+            ops.page_decode_raw_hier(qs[l], lays[l], larges[l], n_c, factor, nk_large, nk_small, n_near,
+                                     near_start=n_c * PAGE, out=out, status=status, workspace=ws)
+
+    res = {}
+    for name, fn in (("flat", flat), ("hier", hier)):
+        with torch.cuda.stream(stream):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+        res[name] = _timed(graph.replay, args.steps, args.warmup, stream)
+        del graph
+    if int(status.item()) != 0:
+        raise RuntimeError("device status set")
+    # how much of the flat top-256 the hierarchical pick keeps (layer 0)
+    sf = torch.empty(rows, nk, dtype=torch.int64, device=dev)
+    sh = torch.empty(rows, nk_small, dtype=torch.int64, device=dev)
+    ops.page_decode_raw(qs[0], lays[0], n_c, nk, n_near, near_start=n_c * PAGE, sel_out=sf, status=status)
+    ops.page_decode_raw_hier(qs[0], lays[0], larges[0], n_c, factor, nk_large, nk_small, n_near,
+                             near_start=n_c * PAGE, sel_out=sh, status=status)
+    torch.cuda.synchronize()
+    keep = np.mean([len(set(a) & set(b)) / nk for a, b in zip(sf.cpu().numpy(), sh.cpu().numpy())])
+    peak, peak_kind = load_peaks()
+    b_flat = W.raw_algorithmic_bytes(rows, n_c, nk, n_near, G)
+    b_hier = rows * ((n_large + nk_large * factor) * 512 + nk_small * 8192 + n_near * 512 + 2 * G * 256)
+    ach = b_flat / (res["flat"] / 1e3 / layers) / 1e9
+    line = {
+        "metric": "config3 sparse decode step tokens/s (Qwen3-4B shape, 131072 ctx, batch 1), raw-row page mode",
+        "value": bs / (res["flat"] / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": res["flat"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config3: 36 layers, bs 1, 8 KV / 32 q heads, 131072 ctx, budget 4096, residual 128, "
+                               "page mode over raw rows", "layers": layers},
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                     "peak_kind": peak_kind, "bytes_per_launch": b_flat},
+        "hierarchical": {"ms_per_step": res["hier"], "tokens_s": bs / (res["hier"] / 1e3),
+                         "bytes_per_layer": b_hier, "flat_bytes_per_layer": b_flat,
+                         "bytes_cut": 1 - b_hier / b_flat, "factor": factor, "n_large": n_large,
+                         "nk_large": nk_large, "nk_small": nk_small, "small_ratio": small_ratio,
+                         "kept_of_flat_top_pages": keep,
+                         "achieved_gbs": b_hier / (res["hier"] / 1e3 / layers) / 1e9},
+        "gpu_launches": layers * args.steps * 4,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_config3(args):
     """Qwen3-4B-shape decode step at 131072 context (36 layers, batch 1)."""
     import datetime
@@ -687,6 +780,8 @@ def main():
                     help="config 1 only: raw = page mode over the selected pages' raw bf16 rows (the headline, the "
                          "reference's page mode); page4 = page mode over 4-bit KIVI K/V pages (lossy variant); "
                          "reference = the drop-in's default reference mode with production knobs")
+    ap.add_argument("--raw3", action="store_true",
+                    help="config 3 on one GPU in the raw-row page mode: flat against hierarchical Quest")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config == 1 and args.mode == "reference" and args.impl == "ours":
@@ -696,7 +791,10 @@ def main():
         run_config2(args)
         return
     if args.config == 3 and args.impl == "ours":
-        run_config3(args)
+        if args.mode == "raw" and int(os.environ.get("WORLD_SIZE", "1")) == 1 and args.raw3:
+            run_config3_raw(args)
+        else:
+            run_config3(args)
         return
     if args.config == 5 and args.impl == "ours":
         run_offload(args)

@@ -336,6 +336,44 @@ int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, int rows,
                         float* lse, int64_t* sel_out, int32_t* status,
                         void* workspace, size_t ws_bytes, void* stream);
 
+/* Hierarchical Quest inputs: per-large-chunk min / max (bf16,
+ * [rows][n_max_large][128]) and validity ([rows][n_max_large]).            */
+typedef struct zkv_quest_large {
+    const void* large_min;
+    const void* large_max;
+    const uint8_t* large_valid;
+    int n_max_large;
+} zkv_quest_large;
+
+/* Large-chunk min / max of groups [g_lo, g_hi): group g covers chunks
+ * [g*factor, min(g*factor + factor, valid_end)); its min / max are the
+ * element-wise bf16 min / max of those chunks' min / max and it becomes
+ * valid; empty groups are left untouched.  Replaces
+ * _update_large_chunk_minmax (cache_hub/polar_cache_kivi_quest_density_
+ * seperate_kernel.py:1762-1798).  chunk_min/max [rows][n_max][128] bf16.   */
+int zkv_quest_large_minmax(const void* chunk_min, const void* chunk_max, int rows, int n_max, int valid_end,
+                           int factor, int g_lo, int g_hi, void* large_min, void* large_max, uint8_t* large_valid,
+                           int n_max_large, void* stream);
+
+/* Bytes of workspace zkv_page_decode_raw_hier needs.                     */
+size_t zkv_page_decode_raw_hier_ws_bytes(int rows, int n_c, int factor, int nk_large, int nk_small, int n_sink,
+                                         int n_near);
+
+/* zkv_page_decode_raw with the hierarchical Quest pick
+ * (_quest_pick_coarse_indices_hierarchical, :1852-1940, with
+ * quest_chunk_score / quest_sub_chunk_score / quest_map_back of
+ * cache_hub/quest/quest_chunk_score.cu and float_topk_3d): Quest over the
+ * n_c / factor large chunks (large_valid applied), their top nk_large, the
+ * Quest scores of those large chunks' factor sub-chunks each, the top
+ * nk_small sub-chunks mapped back to chunk ids (ascending) -> attention
+ * over those pages' raw rows + sink + near rows, as zkv_page_decode_raw.
+ * Six launches chained by programmatic dependent launch.  factor <= 16;
+ * 1 <= nk_large <= n_c / factor; 1 <= nk_small <= nk_large * factor.      */
+int zkv_page_decode_raw_hier(const void* q, const zkv_raw_layer* layer, const zkv_quest_large* large, int rows,
+                             int G, int n_max, int n_c, int factor, int nk_large, int nk_small, int n_sink,
+                             int near_start, int n_near, float scale, void* out, float* lse, int64_t* sel_out,
+                             int32_t* status, void* workspace, size_t ws_bytes, void* stream);
+
 /* Attention over externally selected pages (the sequence-split step):
  * the layer buffer holds pages [sel_lo, sel_hi) of the sequence as its
  * pages 0..; of the global page ids sel [rows][n_sel] (-1 = none) those in

@@ -16,8 +16,14 @@ reference's PyTorch fallbacks:
   collision  update_cache_cnt (collision.cu:446-463), int32 counts
   rerank     partial_rerank_scores (rerank.cu:230-299), bf16 scores
   coarse2bit coarse_2bit_score (coarse_2bit_score.cu:161-230), int32 scores
+  hier       hierarchical Quest as _quest_pick_coarse_indices_hierarchical
+             (polar_cache_kivi_quest_density_seperate_kernel.py:1852-1940)
+             calls it: quest_chunk_score over the large chunks, float_topk_3d,
+             quest_sub_chunk_score, float_topk_3d, quest_map_back
+             (quest_chunk_score.cu:263-416) -> tests/golden/ref_cuda_hier.npz
 
     python tests/golden/make_ref_cuda_golden.py OUT.npz     # needs a GPU
+    python tests/golden/make_ref_cuda_golden.py --hier OUT.npz
 """
 from __future__ import annotations
 
@@ -168,10 +174,45 @@ def gen_coarse2bit(dev, out):
     out.update(c2_packed=packed, c2_qs=qs, c2_qm=qm, c2_scores=sc.cpu().numpy())
 
 
-def main(path):
+def gen_hier(dev, out):
+    mq = load_ref("ref_quest")
+    mt = load_ref("ref_float_topk")
+    rng = np.random.default_rng(211)
+    bs, kv, n_max, n_c, factor = 2, 4, 2048, 2040, 16
+    keys = keys_bf16(rng, (bs * kv, n_max * 16, 128))
+    mn, mx, _, _ = O.kivi_encode_chunks(keys)
+    mn = mn.reshape(bs * kv, n_max, 128)
+    mx = mx.reshape(bs * kv, n_max, 128)
+    nml = n_max // factor
+    lmn, lmx, lv = O.large_minmax(mn, mx, n_c, factor, nml)
+    lv[1, 5] = 0
+    n_large, nk_large, nk_small = O.hier_plan(n_c, factor)
+    q = O.f32_to_bf16(rng.standard_normal((bs, kv, 128), dtype=np.float32))
+    shp = (bs, kv)
+    ls = torch.empty(bs, kv, n_large, dtype=torch.float32, device=dev)
+    mq.quest_chunk_score(t_bf16(q, dev), t_bf16(lmn.reshape(shp + (nml, 128)), dev),
+                         t_bf16(lmx.reshape(shp + (nml, 128)), dev), ls, n_large,
+                         torch.from_numpy(lv.reshape(shp + (nml,)).astype(bool)).to(dev))
+    li = mt.float_topk_3d(ls, nk_large).clamp(min=0, max=n_large - 1).contiguous()
+    sub = torch.empty(bs, kv, nk_large * factor, dtype=torch.float32, device=dev)
+    mq.quest_sub_chunk_score(t_bf16(q, dev), t_bf16(mn.reshape(shp + (n_max, 128)), dev),
+                             t_bf16(mx.reshape(shp + (n_max, 128)), dev), li, sub, nk_large, factor)
+    pos = mt.float_topk_3d(sub, nk_small).contiguous()
+    idx = torch.empty(bs, kv, nk_small, dtype=torch.int64, device=dev)
+    mq.quest_map_back(li, pos, idx, factor, n_c)
+    torch.cuda.synchronize()
+    out.update(hier_q=q, hier_min=mn.reshape(shp + (n_max, 128)), hier_max=mx.reshape(shp + (n_max, 128)),
+               hier_lmin=lmn.reshape(shp + (nml, 128)), hier_lmax=lmx.reshape(shp + (nml, 128)),
+               hier_lvalid=lv.reshape(shp + (nml,)), hier_n_c=np.int64(n_c), hier_factor=np.int64(factor),
+               hier_nk_large=np.int64(nk_large), hier_nk_small=np.int64(nk_small),
+               hier_large_scores=ls.cpu().numpy(), hier_large_idx=li.cpu().numpy(), hier_sub_scores=sub.cpu().numpy(),
+               hier_sub_pos=pos.cpu().numpy(), hier_chunk_idx=idx.cpu().numpy())
+
+
+def main(path, gens=None):
     dev = torch.device("cuda", 0)
     out = {}
-    for fn in (gen_quest, gen_kivi_qk, gen_density, gen_topk, gen_collision, gen_rerank, gen_coarse2bit):
+    for fn in gens or (gen_quest, gen_kivi_qk, gen_density, gen_topk, gen_collision, gen_rerank, gen_coarse2bit):
         fn(dev, out)
         print(fn.__name__, "ok", flush=True)
     np.savez_compressed(path, **out)
@@ -179,4 +220,7 @@ def main(path):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.path.join(HERE, "ref_cuda.npz"))
+    if len(sys.argv) > 1 and sys.argv[1] == "--hier":
+        main(sys.argv[2] if len(sys.argv) > 2 else os.path.join(HERE, "ref_cuda_hier.npz"), [gen_hier])
+    else:
+        main(sys.argv[1] if len(sys.argv) > 1 else os.path.join(HERE, "ref_cuda.npz"))

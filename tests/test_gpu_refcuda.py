@@ -90,3 +90,40 @@ def test_coarse2bit_vs_reference_kernel():
                                      L)
     torch.cuda.synchronize()
     assert np.array_equal(out.cpu().numpy().reshape(bs, kv, L), G["c2_scores"])
+
+
+def test_hierarchical_pick_vs_reference_kernels():
+    """zkv_page_decode_raw_hier's pick against the reference's hierarchical
+    Quest chain run on the GPU (ref_cuda_hier.npz): large min/max rebuilt by
+    zkv_quest_large_minmax bit-exact, the picked chunk ids equal as sets.
+    One query head per KV head, so the GQA mean is the fixture's raw q."""
+    H = golden("ref_cuda_hier.npz")
+    f, n_c = int(H["hier_factor"]), int(H["hier_n_c"])
+    nkl, nks = int(H["hier_nk_large"]), int(H["hier_nk_small"])
+    bs, kv, n_max, D = H["hier_min"].shape
+    mn, mx = from_u16(H["hier_min"]), from_u16(H["hier_max"])
+    nml = H["hier_lmin"].shape[2]
+    lmn = torch.zeros(bs, kv, nml, D, dtype=torch.bfloat16, device=DEV)
+    lmx = torch.zeros_like(lmn)
+    lv = torch.zeros(bs, kv, nml, dtype=torch.uint8, device=DEV)
+    ops.quest_large_minmax(mn, mx, n_c, f, lmn, lmx, lv)
+    torch.cuda.synchronize()
+    ref_v = H["hier_lvalid"].astype(bool)
+    ref_v_built = ref_v.copy()
+    ref_v_built[1 // kv, 1 % kv, 5] = True          # the fixture invalidated one group after building
+    assert np.array_equal(lv.cpu().numpy().astype(bool), ref_v_built)
+    assert np.array_equal(to_u16(lmn)[ref_v_built], H["hier_lmin"][ref_v_built])
+    assert np.array_equal(to_u16(lmx)[ref_v_built], H["hier_lmax"][ref_v_built])
+    lv.copy_(torch.from_numpy(H["hier_lvalid"].astype(np.uint8)))
+    g = torch.Generator(device=DEV).manual_seed(3)
+    keys = torch.randn(bs, kv, n_max * 16, D, generator=g, device=DEV).to(torch.bfloat16)
+    layer = ops.RawLayer(mn, mx, None, keys, keys)
+    q = from_u16(H["hier_q"]).reshape(bs, 1, kv, D)
+    sel = torch.empty(bs * kv, nks, dtype=torch.int64, device=DEV)
+    ops.page_decode_raw_hier(q, layer, ops.LargeLayer(lmn, lmx, lv), n_c, f, nkl, nks, 0, near_start=n_c * 16,
+                             sel_out=sel)
+    torch.cuda.synchronize()
+    ref = H["hier_chunk_idx"].reshape(bs * kv, -1)
+    got = sel.cpu().numpy()
+    for r in range(bs * kv):
+        assert set(got[r]) == set(ref[r]), r

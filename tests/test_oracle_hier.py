@@ -66,3 +66,27 @@ def test_selection_overlaps_reference():
         assert len(set(li[r]) & set(ref_l[r])) >= len(ref_l[r]) - 1
         assert len(set(out[r]) & set(ref[r])) >= 0.8 * ref.shape[1]
         assert (np.diff(out[r]) > 0).all()   # ascending chunk ids
+
+
+def test_drop_in_plan_matches_oracle():
+    from zoomkv_revision_b200 import polar_cache as P
+    for n_c in (0, 15, 16, 17, 100, 290, 2040, 8184):
+        for f in (4, 8, 16):
+            assert P.hier_plan(n_c, f, 0.3, 0.3) == O.hier_plan(n_c, f), (n_c, f)
+    assert P.hier_plan(2040, 16, 0.5, 0.1) == O.hier_plan(2040, 16, 0.5, 0.1)
+
+
+def test_drop_in_knobs(monkeypatch):
+    import pytest
+    from zoomkv_revision_b200 import polar_cache as P
+    monkeypatch.setenv("POLAR_QUEST_HIERARCHICAL", "1")
+    monkeypatch.setenv("ZKV_ATTENTION_MODE", "page")
+    cfg = P.env_config()
+    assert cfg["hierarchical"] and cfg["large_chunk"] == 256 and cfg["large_ratio"] == 0.3
+    monkeypatch.setenv("POLAR_QUEST_LARGE_CHUNK", "512")
+    with pytest.raises(ValueError):
+        P.env_config()
+    monkeypatch.setenv("POLAR_QUEST_LARGE_CHUNK", "128")
+    monkeypatch.setenv("ZKV_ATTENTION_MODE", "reference")
+    with pytest.raises(ValueError):
+        P.env_config()

@@ -6,6 +6,8 @@ B200 by tests/golden/make_ref_cuda_golden.py.  Where the reference's CUDA
 and PyTorch paths differ in rounding, these fixtures pin the CUDA semantics:
 scores bit for bit, index sets exactly (top-k ties compared as the
 reference's own test does, by the multiset of selected scores)."""
+import os
+
 import numpy as np
 
 import oracle as O
@@ -85,3 +87,31 @@ def test_coarse2bit_vs_reference_kernel():
     packed = G["c2_packed"].transpose(0, 1, 3, 2, 4).reshape(R, L, B * 4)
     out = O.coarse2bit(packed, G["c2_qs"].reshape(R, B), G["c2_qm"].reshape(R, B))
     assert np.array_equal(out, G["c2_scores"].reshape(R, L))
+
+
+def test_hierarchical_quest_vs_reference_kernels():
+    """Hierarchical Quest as the separate-kernel cache runs it on the GPU
+    (quest_chunk_score over large chunks, float_topk_3d, quest_sub_chunk_score,
+    float_topk_3d, quest_map_back; tests/golden/ref_cuda_hier.npz): the oracle's
+    stage scores are bit-exact, its picks equal as sets."""
+    d = np.load(os.path.join(os.path.dirname(__file__), "golden", "ref_cuda_hier.npz"))
+    f, n_c = int(d["hier_factor"]), int(d["hier_n_c"])
+    nkl, nks = int(d["hier_nk_large"]), int(d["hier_nk_small"])
+    assert O.hier_plan(n_c, f)[1:] == (nkl, nks)
+    q = d["hier_q"].reshape(-1, 128)
+    R = q.shape[0]
+    mn, mx = d["hier_min"].reshape(R, -1, 128), d["hier_max"].reshape(R, -1, 128)
+    lmn, lmx, lv = d["hier_lmin"].reshape(R, -1, 128), d["hier_lmax"].reshape(R, -1, 128), \
+        d["hier_lvalid"].reshape(R, -1)
+    ls = O.quest_score(q, lmn, lmx, lv, n_c // f)
+    assert np.array_equal(ls.view(np.uint32), d["hier_large_scores"].reshape(R, -1).view(np.uint32))
+    # sub-chunk scores of the reference's own large picks, in its order
+    ref_li = d["hier_large_idx"].reshape(R, -1)
+    sub = O.sub_chunk_score(q, mn, mx, ref_li, f)
+    assert np.array_equal(sub.view(np.uint32), d["hier_sub_scores"].reshape(R, -1).view(np.uint32))
+    assert np.array_equal(O.map_back(ref_li, d["hier_sub_pos"].reshape(R, -1), f, n_c),
+                          d["hier_chunk_idx"].reshape(R, -1))
+    out, li, _ = O.hier_select(q, mn, mx, lmn, lmx, lv, n_c, f, nkl, nks)
+    for r in range(R):
+        assert set(li[r]) == set(ref_li[r])
+        assert set(out[r]) == set(d["hier_chunk_idx"].reshape(R, -1)[r])

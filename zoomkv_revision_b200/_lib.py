@@ -40,6 +40,12 @@ class ZkvRawLayer(ctypes.Structure):
     ]
 
 
+class ZkvQuestLarge(ctypes.Structure):
+    """Mirror of `zkv_quest_large` (include/zkv.h)."""
+    _fields_ = [("large_min", _c_void_p), ("large_max", _c_void_p), ("large_valid", _c_void_p),
+                ("n_max_large", _i32)]
+
+
 class ZkvRqLayout(ctypes.Structure):
     """Mirror of `zkv_rq_layout` (include/zkv.h)."""
     _fields_ = [
@@ -107,6 +113,12 @@ _SIGNATURES = {
     "zkv_page_decode_raw_ws_bytes": [_i32, _i32, _i32, _i32, _i32],
     "zkv_page_decode_raw": [_c_void_p, ctypes.POINTER(ZkvRawLayer), _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                             _f32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
+    "zkv_quest_large_minmax": [_c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p,
+                               _c_void_p, _i32, _c_void_p],
+    "zkv_page_decode_raw_hier_ws_bytes": [_i32] * 7,
+    "zkv_page_decode_raw_hier": [_c_void_p, ctypes.POINTER(ZkvRawLayer), ctypes.POINTER(ZkvQuestLarge)] +
+                                [_i32] * 10 + [ctypes.c_float, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                               ctypes.c_size_t, _c_void_p],
     "zkv_lse_merge": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p],
     "zkv_lse_merge_n": [_c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p],
     "zkv_rq_encode": [_c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _RQ, _c_void_p],
@@ -130,7 +142,8 @@ _SIGNATURES = {
 }
 
 _RESTYPES = {"zkv_status_string": ctypes.c_char_p, "zkv_reference_select_ws_bytes": ctypes.c_size_t,
-             "zkv_page_decode_split_ws_bytes": ctypes.c_size_t, "zkv_page_decode_raw_ws_bytes": ctypes.c_size_t}
+             "zkv_page_decode_split_ws_bytes": ctypes.c_size_t, "zkv_page_decode_raw_ws_bytes": ctypes.c_size_t,
+             "zkv_page_decode_raw_hier_ws_bytes": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib = None

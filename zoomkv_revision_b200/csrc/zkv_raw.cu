@@ -71,6 +71,10 @@ struct Args {
     float* scores;   // [R][n_c_pad]
     int32_t* sel;    // [R][nk]
     float* parts;    // [R][AT][kPartFloats]
+    // hierarchical Quest
+    const int32_t* group_ids;  // score kernel: warp j scores the small chunks of large chunk group_ids[r][j]
+    const int32_t* map_ids;    // select kernel: position p -> map_ids[r][p / factor] * factor + p % factor
+    int n_groups, factor, n_chunks_map;
 };
 
 // 2-D tiled TMA load (no multicast): box (x .. x+63, y .. y+15) -> dst.
@@ -280,13 +284,26 @@ __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_consta
     __syncthreads();
     grid_dep_wait();          // q is the previous kernel's output; the workspace may still be read by it
     grid_dep_launch_next();   // the select kernel may become resident (it waits for this grid)
-    const int cc = tile * kScoreTile + 16 * warp;
-    const int nch = max(0, min(16, a.n_c - cc));
+    // cc: first score position of this warp; src: first chunk it reads
+    int cc, src, nch;
+    bool oob = false;
+    if (a.group_ids) {  // sub-chunk scores of the row's selected large chunks (quest_chunk_score.cu:263-360)
+        const int j = tile * kWarps + warp;
+        cc = j * a.factor;
+        nch = j < a.n_groups ? a.factor : 0;
+        const int lid = nch ? __ldcg(a.group_ids + (int64_t)r * a.n_groups + j) : 0;
+        src = lid * a.factor;
+        oob = lid < 0 || src + a.factor > a.n_max;  // scored -inf, as the reference's bound check
+    } else {
+        cc = tile * kScoreTile + 16 * warp;
+        src = cc;
+        nch = max(0, min(16, a.n_c - cc));
+    }
     uint8_t* slot = region + warp * kSlotBytes;
-    if (lane == 0 && nch > 0) {
+    if (lane == 0 && nch > 0 && !oob) {
         mbar_arrive_expect_tx(bars + warp, (uint32_t)nch * kHeadDim * 2 * 2);
-        bulk_g2s(slot, a.cmin + ((int64_t)r * a.n_max + cc) * kHeadDim, nch * kHeadDim * 2, bars + warp);
-        bulk_g2s(slot + 4096, a.cmax + ((int64_t)r * a.n_max + cc) * kHeadDim, nch * kHeadDim * 2, bars + warp);
+        bulk_g2s(slot, a.cmin + ((int64_t)r * a.n_max + src) * kHeadDim, nch * kHeadDim * 2, bars + warp);
+        bulk_g2s(slot + 4096, a.cmax + ((int64_t)r * a.n_max + src) * kHeadDim, nch * kHeadDim * 2, bars + warp);
     }
     {   // GQA-mean query (compute() :1622-1626: fp32 sum in head order / G, bf16)
         const uint16_t* qr = a.q + (int64_t)r * a.G * kHeadDim;
@@ -297,6 +314,11 @@ __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_consta
     }
     __syncthreads();
     if (nch == 0) return;
+    float* srow0 = a.scores + (int64_t)r * a.n_c_pad;
+    if (oob) {
+        if (lane < nch) srow0[cc + lane] = -INFINITY;
+        return;
+    }
     const bool ok = mbar_wait(bars + warp, 0, a.status);
     const int hl = lane & 15, half = lane >> 4;
     const uint4 qv = *reinterpret_cast<const uint4*>(rq + 8 * hl);
@@ -363,6 +385,11 @@ __global__ void __launch_bounds__(kSelThreads) raw_select_kernel(const __grid_co
     int32_t* selr = a.sel + (int64_t)r * a.nk;
     int64_t* selo = a.sel_out ? a.sel_out + (int64_t)r * a.nk : nullptr;
     auto emit = [&](int pos, int i) {
+        if (a.map_ids) {  // quest_map_back (quest_chunk_score.cu:363-416)
+            const int sel = i / a.factor;
+            i = __ldcg(a.map_ids + (int64_t)r * a.n_groups + sel) * a.factor + (i - sel * a.factor);
+            i = min(max(i, 0), a.n_chunks_map - 1);
+        }
         selr[pos] = i;
         if (selo) selo[pos] = i;
     };
@@ -506,6 +533,41 @@ __global__ void __launch_bounds__(kHeadDim) raw_merge_kernel(const __grid_consta
     a.out[((int64_t)r * a.G + h) * kHeadDim + d] = f2bfbits(L > 0.f ? O * (1.f / L) : 0.f);
 }
 
+// ---------------------------------------------------------------- large-chunk min/max
+// _update_large_chunk_minmax (polar_cache_kivi_quest_density_seperate_kernel.py:
+// 1762-1798): group g of a row covers chunks [g*factor, min(g*factor + factor,
+// valid_end)); its min / max are the element-wise bf16 min / max of those
+// chunks' min / max and the group becomes valid.  Empty groups are left as
+// they are.  One CTA of 64 threads (two dims each) per (group, row).
+__global__ void __launch_bounds__(64) large_minmax_kernel(const uint32_t* __restrict__ mn,
+                                                          const uint32_t* __restrict__ mx, int n_max, int valid_end,
+                                                          int factor, int g_lo, uint32_t* lmn, uint32_t* lmx,
+                                                          uint8_t* lvalid, int n_max_large) {
+    const int r = blockIdx.y, g = g_lo + blockIdx.x, t = threadIdx.x;
+    const int b_lo = g * factor;
+    const int b_hi = min(min(b_lo + factor, valid_end), n_max);
+    if (b_hi <= b_lo) return;
+    const int64_t src = ((int64_t)r * n_max + b_lo) * (kHeadDim / 2) + t;
+    uint32_t a = __ldg(mn + src), z = __ldg(mx + src);
+    for (int b = 1; b < b_hi - b_lo; ++b) {
+        const uint32_t u = __ldg(mn + src + (int64_t)b * (kHeadDim / 2));
+        const uint32_t v = __ldg(mx + src + (int64_t)b * (kHeadDim / 2));
+        uint32_t lo = a & 0xffffu, hi = a >> 16;
+        if (bfbits2f((uint16_t)(u & 0xffffu)) < bfbits2f((uint16_t)lo)) lo = u & 0xffffu;
+        if (bfbits2f((uint16_t)(u >> 16)) < bfbits2f((uint16_t)hi)) hi = u >> 16;
+        a = lo | (hi << 16);
+        lo = z & 0xffffu;
+        hi = z >> 16;
+        if (bfbits2f((uint16_t)(v & 0xffffu)) > bfbits2f((uint16_t)lo)) lo = v & 0xffffu;
+        if (bfbits2f((uint16_t)(v >> 16)) > bfbits2f((uint16_t)hi)) hi = v >> 16;
+        z = lo | (hi << 16);
+    }
+    const int64_t dst = ((int64_t)r * n_max_large + g) * (kHeadDim / 2) + t;
+    lmn[dst] = a;
+    lmx[dst] = z;
+    if (t == 0) lvalid[(int64_t)r * n_max_large + g] = 1;
+}
+
 // ---------------------------------------------------------------- host side
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -584,7 +646,16 @@ static bool cached_maps(CUtensorMap* tk, CUtensorMap* tv, const void* keys, cons
 
 struct Plan {
     int ST, AT, RS, RN, E, n_c_pad, EPC;
-    size_t off_scores, off_sel, off_parts, bytes;
+    int ST1, n_large, n_large_pad;  // hierarchical: stage-1 score CTAs per row, large chunks scored, row stride
+    size_t off_scores, off_sel, off_sel_large, off_parts, bytes;
+};
+
+// Hierarchical Quest inputs (zero `factor`: the flat select).
+struct Hier {
+    const void* lmin;
+    const void* lmax;
+    const uint8_t* lvalid;
+    int n_max_large, factor, nk_large;
 };
 
 static size_t up256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -604,10 +675,22 @@ static int sm_count() {
     return cached[dev];
 }
 
-static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near) {
+// n_c: chunks scored by the flat select, or the small chunks of a
+// hierarchical one (h.factor > 0: n_c / factor large chunks are scored, the
+// top h.nk_large of them expand to nk_large * factor sub-chunks, of which
+// the top nk are attended).
+static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near, const Hier& h) {
     Plan p;
     const int nsel = n_c > 0 ? nk : 0;
-    p.ST = nk < n_c ? (n_c + kScoreTile - 1) / kScoreTile : 0;  // no scoring when every chunk is selected
+    const bool hier = h.factor > 0;
+    p.n_large = hier ? n_c / h.factor : 0;
+    p.n_large_pad = (p.n_large + 31) & ~31;
+    p.ST1 = hier ? (p.n_large + kScoreTile - 1) / kScoreTile : 0;
+    if (hier)  // stage 2: one warp per selected large chunk
+        p.ST = (h.nk_large + kWarps - 1) / kWarps;
+    else       // no scoring when every chunk is selected
+        p.ST = nk < n_c ? (n_c + kScoreTile - 1) / kScoreTile : 0;
+    const int n_scored = hier ? h.nk_large * h.factor : n_c;
     p.RS = (n_sink + 15) / 16;
     p.RN = (n_near + 15) / 16;
     p.E = p.RS + p.RN + nsel;
@@ -622,10 +705,12 @@ static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near) {
         p.EPC = p.E > 0 ? (p.E + c - 1) / c : 1;
         p.AT = p.E > 0 ? (p.E + p.EPC - 1) / p.EPC : 1;
     }
-    p.n_c_pad = (n_c + 31) & ~31;
+    p.n_c_pad = (n_scored + 31) & ~31;
+    const int stride = std::max(p.n_c_pad, p.n_large_pad);
     p.off_scores = 0;
-    p.off_sel = p.off_scores + up256((size_t)R * p.n_c_pad * 4);
-    p.off_parts = p.off_sel + up256((size_t)R * (nk > 0 ? nk : 1) * 4);
+    p.off_sel = p.off_scores + up256((size_t)R * stride * 4);
+    p.off_sel_large = p.off_sel + up256((size_t)R * (nk > 0 ? nk : 1) * 4);
+    p.off_parts = p.off_sel_large + (hier ? up256((size_t)R * h.nk_large * 4) : 0);
     // partials for the most CTAs per row any device can use (kTileEntries
     // entries each), so the size does not depend on the SM count
     const int max_tiles = p.E > 0 ? (p.E + kTileEntries - 1) / kTileEntries : 1;
@@ -652,24 +737,19 @@ static int launch_pdl(const void* fn, int grid, int threads, size_t smem, cudaSt
     return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH;
 }
 
-}  // namespace rawpg
-}  // namespace zkv
-
-using namespace zkv;
-
-extern "C" size_t zkv_page_decode_raw_ws_bytes(int rows, int n_c, int nk, int n_sink, int n_near) {
-    if (rows < 0 || n_c < 0 || nk < 0 || n_sink < 0 || n_near < 0) return 0;
-    return rawpg::make_plan(rows, n_c, nk, n_sink, n_near).bytes;
-}
-
-extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, int rows, int G, int n_max, int n_c,
-                                   int nk, int n_sink, int near_start, int n_near, float scale, void* out, float* lse,
-                                   int64_t* sel_out, int32_t* status, void* workspace, size_t ws_bytes,
-                                   void* stream) {
-    using namespace zkv::rawpg;
+static int decode_raw(const void* q, const zkv_raw_layer* layer, int rows, int G, int n_max, int n_c, int nk,
+                      int n_sink, int near_start, int n_near, float scale, void* out, float* lse, int64_t* sel_out,
+                      int32_t* status, void* workspace, size_t ws_bytes, void* stream, const Hier& h) {
+    const bool hier = h.factor > 0;
     if (!q || !layer || !out || !workspace || rows < 0 || G < 1 || G > 8 || n_c < 0 || n_c > n_max || nk < 0 ||
         (n_c > 0 && (nk < 1 || nk > n_c)) || n_sink < 0 || n_near < 0 || near_start < 0)
         return ZKV_ERR_ARG;
+    if (hier) {
+        const int n_large = n_c / h.factor;
+        if (h.factor > 16 || !h.lmin || !h.lmax || n_large < 1 || h.n_max_large < n_large || h.nk_large < 1 ||
+            h.nk_large > n_large || nk > h.nk_large * h.factor)
+            return ZKV_ERR_ARG;
+    }
     const zkv_raw_layer& L = *layer;
     if (!L.keys || !L.values || L.kv_ld_row < kHeadDim || (L.kv_ld_row % kHeadDim) || L.page_base < 0 ||
         (n_c > 0 && (!L.chunk_min || !L.chunk_max)))
@@ -678,12 +758,13 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
     if (L.page_base + 16 * (int64_t)n_c > cap || (int64_t)near_start + n_near > cap || n_sink > cap)
         return ZKV_ERR_ARG;
     if (n_c > kMaxChunks || (int64_t)rows * cap >= (int64_t)1 << 31) return ZKV_ERR_CAPACITY;
-    const Plan p = make_plan(rows, n_c, nk, n_sink, n_near);
+    const Plan p = make_plan(rows, n_c, nk, n_sink, n_near, h);
     if (ws_bytes < p.bytes) return ZKV_ERR_ARG;
-    if (p.AT > kMaxTiles || (int64_t)rows * (p.ST + p.AT) >= ((int64_t)1 << 31)) return ZKV_ERR_CAPACITY;
+    if (p.AT > kMaxTiles || (int64_t)rows * (p.ST + p.ST1 + p.AT) >= ((int64_t)1 << 31)) return ZKV_ERR_CAPACITY;
     if (rows == 0) return ZKV_OK;
     if (((uintptr_t)L.keys & 15) || ((uintptr_t)L.values & 15) || ((uintptr_t)L.chunk_min & 15) ||
-        ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)q & 3) || ((uintptr_t)workspace & 255))
+        ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)q & 3) || ((uintptr_t)workspace & 255) ||
+        (hier && (((uintptr_t)h.lmin & 15) || ((uintptr_t)h.lmax & 15))))
         return ZKV_ERR_ALIGN;
     Args a;
     memset(&a, 0, sizeof(a));
@@ -718,6 +799,29 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
     a.scores = (float*)(ws + p.off_scores);
     a.sel = (int32_t*)(ws + p.off_sel);
     a.parts = (float*)(ws + p.off_parts);
+    Args a1;  // hierarchical stage 1: Quest over the large chunks, top nk_large of them
+    if (hier) {
+        int32_t* sel_large = (int32_t*)(ws + p.off_sel_large);
+        a1 = a;
+        a1.cmin = (const uint16_t*)h.lmin;
+        a1.cmax = (const uint16_t*)h.lmax;
+        a1.valid = h.lvalid;
+        a1.n_max = h.n_max_large;
+        a1.n_c = p.n_large;
+        a1.nk = h.nk_large;
+        a1.n_c_pad = p.n_large_pad;
+        a1.ST = p.ST1;
+        a1.sel = sel_large;
+        a1.sel_out = nullptr;
+        // stage 2 (in a): the sub-chunks of the selected large chunks, top nk
+        a.valid = nullptr;
+        a.n_c = h.nk_large * h.factor;
+        a.group_ids = sel_large;
+        a.map_ids = sel_large;
+        a.n_groups = h.nk_large;
+        a.factor = h.factor;
+        a.n_chunks_map = n_c;
+    }
 
     static bool attr_set[64] = {};
     int dev = 0;
@@ -733,8 +837,14 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
         attr_set[dev] = true;
     }
     void* args[] = {&a};
+    void* args1[] = {&a1};
     const cudaStream_t st = (cudaStream_t)stream;
     int rc = ZKV_OK;
+    if (hier) {
+        rc = launch_pdl((const void*)raw_score_kernel, rows * p.ST1, kThreads, score_smem(), st, args1);
+        if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_select_kernel, rows, kSelThreads, select_smem(), st, args1);
+        if (rc != ZKV_OK) return rc;
+    }
     if (p.ST > 0) {
         rc = launch_pdl((const void*)raw_score_kernel, rows * p.ST, kThreads, score_smem(), st, args);
         if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_select_kernel, rows, kSelThreads, select_smem(), st, args);
@@ -742,4 +852,59 @@ extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, in
     if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_attend_kernel, rows * p.AT, kThreads, attend_smem(), st, args);
     if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_merge_kernel, rows * G, kHeadDim, 0, st, args);
     return rc;
+}
+
+}  // namespace rawpg
+}  // namespace zkv
+
+using namespace zkv;
+
+extern "C" size_t zkv_page_decode_raw_ws_bytes(int rows, int n_c, int nk, int n_sink, int n_near) {
+    if (rows < 0 || n_c < 0 || nk < 0 || n_sink < 0 || n_near < 0) return 0;
+    return rawpg::make_plan(rows, n_c, nk, n_sink, n_near, rawpg::Hier{}).bytes;
+}
+
+extern "C" int zkv_page_decode_raw(const void* q, const zkv_raw_layer* layer, int rows, int G, int n_max, int n_c,
+                                   int nk, int n_sink, int near_start, int n_near, float scale, void* out, float* lse,
+                                   int64_t* sel_out, int32_t* status, void* workspace, size_t ws_bytes,
+                                   void* stream) {
+    return rawpg::decode_raw(q, layer, rows, G, n_max, n_c, nk, n_sink, near_start, n_near, scale, out, lse, sel_out,
+                             status, workspace, ws_bytes, stream, rawpg::Hier{});
+}
+
+extern "C" size_t zkv_page_decode_raw_hier_ws_bytes(int rows, int n_c, int factor, int nk_large, int nk_small,
+                                                    int n_sink, int n_near) {
+    if (rows < 0 || n_c < 0 || factor < 1 || nk_large < 1 || nk_small < 0 || n_sink < 0 || n_near < 0) return 0;
+    rawpg::Hier h{};
+    h.factor = factor;
+    h.nk_large = nk_large;
+    return rawpg::make_plan(rows, n_c, nk_small, n_sink, n_near, h).bytes;
+}
+
+extern "C" int zkv_page_decode_raw_hier(const void* q, const zkv_raw_layer* layer, const zkv_quest_large* large,
+                                        int rows, int G, int n_max, int n_c, int factor, int nk_large, int nk_small,
+                                        int n_sink, int near_start, int n_near, float scale, void* out, float* lse,
+                                        int64_t* sel_out, int32_t* status, void* workspace, size_t ws_bytes,
+                                        void* stream) {
+    if (!large || factor < 1) return ZKV_ERR_ARG;
+    rawpg::Hier h{large->large_min, large->large_max, large->large_valid, large->n_max_large, factor, nk_large};
+    return rawpg::decode_raw(q, layer, rows, G, n_max, n_c, nk_small, n_sink, near_start, n_near, scale, out, lse,
+                             sel_out, status, workspace, ws_bytes, stream, h);
+}
+
+extern "C" int zkv_quest_large_minmax(const void* chunk_min, const void* chunk_max, int rows, int n_max,
+                                      int valid_end, int factor, int g_lo, int g_hi, void* large_min,
+                                      void* large_max, uint8_t* large_valid, int n_max_large, void* stream) {
+    if (!chunk_min || !chunk_max || !large_min || !large_max || !large_valid || rows < 0 || n_max < 0 ||
+        factor < 1 || g_lo < 0 || g_hi < g_lo || g_hi > n_max_large || valid_end < 0)
+        return ZKV_ERR_ARG;
+    if (((uintptr_t)chunk_min & 3) || ((uintptr_t)chunk_max & 3) || ((uintptr_t)large_min & 3) ||
+        ((uintptr_t)large_max & 3))
+        return ZKV_ERR_ALIGN;
+    if (rows == 0 || g_hi == g_lo) return ZKV_OK;
+    if (rows > 65535) return ZKV_ERR_CAPACITY;
+    rawpg::large_minmax_kernel<<<dim3((unsigned)(g_hi - g_lo), (unsigned)rows), 64, 0, (cudaStream_t)stream>>>(
+        (const uint32_t*)chunk_min, (const uint32_t*)chunk_max, n_max, valid_end, factor, g_lo,
+        (uint32_t*)large_min, (uint32_t*)large_max, large_valid, n_max_large);
+    return launch_status();
 }

@@ -726,6 +726,74 @@ def page_decode_raw(q, layer: RawLayer, n_c: int, nk: int, n_near: int, *, n_sin
     return out
 
 
+class LargeLayer:
+    """Hierarchical Quest metadata of one layer: large_min / large_max
+    [bs, H, n_max_large, 128] bf16 and large_valid [bs, H, n_max_large]
+    (bool or uint8), the per-large-chunk bounding boxes of
+    polar_cache_kivi_quest_density_seperate_kernel.py:1762-1798."""
+
+    def __init__(self, large_min, large_max, large_valid):
+        for n, t in (("large_min", large_min), ("large_max", large_max), ("large_valid", large_valid)):
+            _cuda((n, t))
+            _contig(n, t)
+        _dtype("large_min", large_min, torch.bfloat16)
+        _dtype("large_max", large_max, torch.bfloat16)
+        if large_min.shape != large_max.shape or tuple(large_valid.shape) != tuple(large_min.shape[:3]):
+            raise ValueError("large_min / large_max [bs, H, n_max_large, 128] and large_valid [bs, H, n_max_large]")
+        self.tensors = (large_min, large_max, large_valid)
+        self.struct = _lib.ZkvQuestLarge(_p(large_min), _p(large_max), _p(large_valid), large_min.shape[2])
+
+
+def quest_large_minmax(chunk_min, chunk_max, valid_end: int, factor: int, large_min, large_max, large_valid,
+                       g_lo: int = 0, g_hi=None):
+    """_update_large_chunk_minmax (polar_cache_kivi_quest_density_seperate_
+    kernel.py:1762-1798) for groups [g_lo, g_hi) in place: group g covers
+    chunks [g*factor, min(g*factor + factor, valid_end))."""
+    bs, H, n_max, D = chunk_min.shape
+    nml = large_min.shape[2]
+    g_hi = nml if g_hi is None else int(g_hi)
+    for n, t in (("chunk_min", chunk_min), ("chunk_max", chunk_max)):
+        _contig(n, t)
+    check(lib().zkv_quest_large_minmax(_p(chunk_min), _p(chunk_max), bs * H, n_max, int(valid_end), int(factor),
+                                       int(g_lo), g_hi, _p(large_min), _p(large_max), _p(large_valid), nml,
+                                       _stream(chunk_min)), "zkv_quest_large_minmax")
+
+
+def page_decode_raw_hier(q, layer: RawLayer, large: LargeLayer, n_c: int, factor: int, nk_large: int, nk_small: int,
+                         n_near: int, *, n_sink: int = 0, near_start: int = 0, scale=None, out=None, lse=None,
+                         sel_out=None, status=None, workspace=None):
+    """page_decode_raw with the hierarchical Quest pick: Quest over the
+    n_c // factor large chunks, their top nk_large, the sub-chunk scores of
+    those, the top nk_small sub-chunks mapped back to chunk ids, attention
+    over those pages' raw rows + sink + near rows."""
+    cmin = layer.tensors[0]
+    bs, H, n_max, D = cmin.shape
+    _dtype("q", q, torch.bfloat16)
+    G = q.shape[2] // H
+    qc = q.contiguous()
+    if out is None:
+        out = torch.empty(bs, 1, H * G, D, dtype=torch.bfloat16, device=q.device)
+    scale = (1.0 / D ** 0.5) if scale is None else float(scale)
+    rows = bs * H
+    if workspace is None:
+        shape = ("hier", rows, int(n_c), int(factor), int(nk_large), int(nk_small), int(n_sink), int(n_near))
+        need = _RAW_NEED.get(shape)
+        if need is None:
+            need = _RAW_NEED[shape] = int(lib().zkv_page_decode_raw_hier_ws_bytes(*shape[1:]))
+        key = q.device.index if q.device.index is not None else torch.cuda.current_device()
+        ws = _RAW_WS.get(key)
+        if ws is None or ws.numel() < need:
+            ws = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=q.device)
+            _RAW_WS[key] = ws
+        workspace = ws
+    check(lib().zkv_page_decode_raw_hier(_p(qc), ctypes.byref(layer.struct), ctypes.byref(large.struct), rows, G,
+                                         n_max, int(n_c), int(factor), int(nk_large), int(nk_small), int(n_sink),
+                                         int(near_start), int(n_near), scale, _p(out), _p(lse), _p(sel_out),
+                                         _p(status), _p(workspace), int(workspace.numel()), _stream(q)),
+          "zkv_page_decode_raw_hier")
+    return out
+
+
 def gqa_mean(q, heads: int, out=None):
     """raw_q [bs, H, 128] bf16 = GQA mean of q [bs, 1, H*G, 128] (fp32 sum in
     head order / G, as the fused kernels compute it)."""

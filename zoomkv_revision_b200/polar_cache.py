@@ -95,6 +95,12 @@ def env_config(final_topk: int = 100) -> dict:
         stage1=e.get("POLAR_QUEST_STAGE1", "1") not in ("0", "false", "False", ""),
         attention_mode=e.get("ZKV_ATTENTION_MODE", "reference").strip().lower(),
         host_retrieval=e.get("ZKV_HOST_RETRIEVAL", "0") in _TRUE,
+        # hierarchical Quest knobs of the separate-kernel cache (its :210-237);
+        # off here, as in the single-layer cache this drop-in mirrors
+        hierarchical=e.get("POLAR_QUEST_HIERARCHICAL", "0") not in ("0", "false", "False", ""),
+        large_chunk=int(e.get("POLAR_QUEST_LARGE_CHUNK", "256")),
+        large_ratio=float(e.get("POLAR_QUEST_LARGE_RATIO", "0.3")),
+        small_ratio=float(e.get("POLAR_QUEST_SMALL_RATIO", "0.3")),
     )
     if cfg["dynamic"]:
         try:
@@ -112,7 +118,24 @@ def env_config(final_topk: int = 100) -> dict:
         raise ValueError(f"POLAR_KIVI_BITS={cfg['kivi_bits']}: this build implements 4-bit KIVI only")
     if cfg["attention_mode"] not in ("reference", "page", "page4"):
         raise ValueError(f"ZKV_ATTENTION_MODE must be 'reference', 'page' or 'page4'; got {cfg['attention_mode']!r}")
+    if cfg["hierarchical"]:
+        if cfg["large_chunk"] % cfg["chunk"] or not 1 <= cfg["large_chunk"] // cfg["chunk"] <= 16:
+            raise ValueError(f"POLAR_QUEST_LARGE_CHUNK={cfg['large_chunk']}: must be 16..256 in multiples of 16")
+        if cfg["attention_mode"] != "page":
+            raise ValueError("POLAR_QUEST_HIERARCHICAL=1 serves ZKV_ATTENTION_MODE=page")
     return cfg
+
+
+def hier_plan(n_chunks: int, factor: int, large_ratio: float, small_ratio: float):
+    """(n_large, nk_large, nk_small) of the hierarchical branch of
+    _refresh_quest_chunk_cache (separate-kernel cache :1462-1468)."""
+    n_large = n_chunks // factor
+    if n_large <= 0:
+        return 0, 0, 0
+    nk_large = min(max(1, int(math.ceil(n_large * large_ratio))), n_large)
+    nk_sub = nk_large * factor
+    nk_small = min(max(1, int(math.ceil(nk_sub * small_ratio))), nk_sub)
+    return n_large, nk_large, nk_small
 
 
 # --------------------------------------------------------------------------- host logic (CPU-testable)
@@ -388,6 +411,16 @@ class polar_cache:
             )
         self._page_layers = [None] * layer_num
         self._raw_layers = [None] * layer_num
+        # hierarchical Quest: per-large-chunk bounding boxes (separate-kernel cache :1762-1798)
+        self.hq_factor = self.cfg["large_chunk"] // CHUNK if self.cfg["hierarchical"] else 0
+        self.large_min, self.large_max, self.large_valid, self._large_layers = [], [], [], [None] * layer_num
+        if self.hq_factor:
+            nml = (nm + self.hq_factor - 1) // self.hq_factor
+            for l in range(layer_num):
+                d = dict(device=self._layer_dev[l])
+                self.large_min.append(torch.zeros(bs, H, nml, D, dtype=torch.bfloat16, **d))
+                self.large_max.append(torch.zeros(bs, H, nml, D, dtype=torch.bfloat16, **d))
+                self.large_valid.append(torch.zeros(bs, H, nml, dtype=torch.uint8, **d))
 
     # ------------------------------------------------------------------ state (reference attribute names)
     @property
@@ -431,6 +464,11 @@ class polar_cache:
         if self.attention_mode == "page4":
             v = self.values[l][rows, :, s + tok_lo:s + tok_hi]
             ops.vquant_encode(v, self.vcodes_t[l][rows], self.vmeta[l][rows], tok_lo)
+        if self.hq_factor:  # the large chunks the new chunks touch (:1762-1798)
+            f, c_lo, c_hi = self.hq_factor, tok_lo // CHUNK, tok_hi // CHUNK
+            ops.quest_large_minmax(self.chunk_min[l][rows], self.chunk_max[l][rows], c_hi, f,
+                                   self.large_min[l][rows], self.large_max[l][rows], self.large_valid[l][rows],
+                                   g_lo=c_lo // f, g_hi=min((c_hi + f - 1) // f, self.large_min[l].shape[2]))
 
     def _rows(self, batch_idx=None) -> slice:
         return slice(0, self.batch_size) if batch_idx is None else slice(batch_idx, batch_idx + 1)
@@ -663,9 +701,27 @@ class polar_cache:
             self._raw_layers[l] = ops.RawLayer(self.chunk_min[l], self.chunk_max[l], self.chunk_valid[l],
                                                self.keys[l], self.values[l], page_base=self.sink_size)
         s = self.sink_size
+        status = self._scratch[self._layer_dev[l]]["status"]
+        if self.hq_factor:
+            # hierarchical pick (separate-kernel cache :1852-1940): every token
+            # of the nk_small picked chunks is attended (the reference's result
+            # when final_topk >= 16 * nk_small); chunks past the last whole large
+            # chunk are its live skipped tokens and are attended with the near rows
+            f = self.hq_factor
+            n_large, nk_large, nk_small = hier_plan(n_chunks, f, self.cfg["large_ratio"], self.cfg["small_ratio"])
+            if n_large > 0:
+                if self._large_layers[l] is None:
+                    self._large_layers[l] = ops.LargeLayer(self.large_min[l], self.large_max[l], self.large_valid[l])
+                near_start = s + n_large * f * CHUNK
+                return ops.page_decode_raw_hier(q, self._raw_layers[l], self._large_layers[l], n_chunks, f, nk_large,
+                                                nk_small, total - near_start, n_sink=s, near_start=near_start,
+                                                status=status)
+            # no whole large chunk yet: every retrieval token is a live skipped one
+            return ops.page_decode_raw(q, self._raw_layers[l], 0, 0, total - s, n_sink=s, near_start=s,
+                                       status=status)
         near_start = s + n_chunks * CHUNK
         return ops.page_decode_raw(q, self._raw_layers[l], n_chunks, nk, total - near_start, n_sink=s,
-                                   near_start=near_start, status=self._scratch[self._layer_dev[l]]["status"])
+                                   near_start=near_start, status=status)
 
     def _compute_page(self, q, l, n_chunks, nk, valid_length, total):
         """Page4 (lossy) decode over the encoded chunks' 4-bit pages; the carry
