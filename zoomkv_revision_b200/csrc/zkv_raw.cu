@@ -12,8 +12,9 @@
 //    chunks' Quest min/max (32 KiB) into shared memory; each half-warp scores
 //    a chunk with the reference kernel's fp32 operation order and writes the
 //    score to the workspace.
-//  * raw_select_kernel: one CTA per row: invalid chunks -> -inf, then the top
-//    nk chunk ids (ties to the lowest id, ascending).
+//  * raw_select_kernel: one CTA of 1024 threads per row (2 or 4 keys per
+//    thread): invalid chunks -> -inf, then the top nk chunk ids (ties to the
+//    lowest id, ascending).
 //  * raw_attend_kernel: one CTA per (row, EPC entries of 16 tokens) with EPC
 //    chosen so that the grid is one wave (3 CTAs per SM): sink and near rows,
 //    then selected pages.  Each warp cycles two slots: a page comes in as
@@ -21,6 +22,7 @@
 //    and 64-127), is read with ldmatrix (K, B operand of S = Q K^T) and
 //    ldmatrix.trans (V, A operand of O^T = V^T P^T) into mma.sync m16n8k16
 //    with an online softmax, and the slot's next copy is issued at once.  The
+//    sink and near pages go out before the wait for the select kernel.  The
 //    CTA merges its warps and writes one partial (m, l, o).
 //  * raw_merge_kernel: one CTA per (row, head): the partials -> out / lse.
 //
@@ -48,8 +50,7 @@ constexpr int kAttRegion = kTileEntries * kSlotBytes;  // 64 KiB
 constexpr int kScoreTile = kWarps * 16;           // chunks per score CTA (32 KiB of min/max)
 constexpr int kScoreRegion = kWarps * kSlotBytes; // 32 KiB
 constexpr int kPartFloats = 16 + 8 * kHeadDim;    // m[8], l[8], o[8][128]
-constexpr int kSelThreads = 256;                  // threads of a select CTA
-constexpr int kSelSmall = 16 * kSelThreads;       // rows up to this many chunks select from shared memory
+constexpr int kSelThreads = 1024;                 // threads of a select CTA
 constexpr int kMaxChunks = 16384;
 constexpr int kMaxTiles = 2048;                   // attend tiles per row
 
@@ -338,38 +339,54 @@ __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_consta
 
 // ---------------------------------------------------------------- kernel 2: select
 // One CTA of kSelThreads per row: the row's scores (invalid chunks -> -inf)
-// -> top nk chunk ids, ties to the lowest id, ascending.
-__global__ void __launch_bounds__(kSelThreads) raw_select_kernel(const __grid_constant__ Args a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    float* keys = reinterpret_cast<float*>(smem);             // [kSelSmall]
-    int* hist = reinterpret_cast<int*>(keys + kSelSmall);
-    int* misc = hist + 512;
-    int* scan = misc + 8;
-    uint32_t* lohi = reinterpret_cast<uint32_t*>(scan + 2 * kSelThreads);
-    const int r = blockIdx.x, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        lohi[0] = 0xffffffffu;
-        lohi[1] = 0u;
-    }
-    __syncthreads();
-    grid_dep_wait();          // the scores of the score kernel
-    grid_dep_launch_next();   // the attend kernel may become resident (it waits for this grid)
-    const float* srow = a.scores + (int64_t)r * a.n_c_pad;
-    const uint8_t* vrow = a.valid ? a.valid + (int64_t)r * a.n_max : nullptr;
-    const bool small = a.n_c <= kSelSmall;
-    uint32_t klo = 0xffffffffu, khi = 0u;
-    for (int i = 4 * threadIdx.x; i < a.n_c; i += 4 * kSelThreads) {
-        const float4 f = __ldcg(reinterpret_cast<const float4*>(srow + i));
-        float fv[4] = {f.x, f.y, f.z, f.w};
+// -> top nk chunk ids, ties to the lowest id, ascending.  Rows of up to
+// 4 * kSelThreads chunks: thread t holds keys [E t, E t + E) in registers
+// (E = 2 or 4), so every warp holds keys and each thread's chains are short;
+// one kSelBins-bin histogram over the row's [min finite, max] key range (a
+// bucketing monotone in the key) gives the bin of the nk-th best; a warp
+// ranks that bin's keys exactly when it holds at most 32 (else the exact
+// radix select runs); an index-order scan of the kept flags writes the ids.
+constexpr int kSelBins = 2048;
+struct SelShared {
+    int hist[kSelBins];
+    int scan[2 * kSelThreads];  // fallback scratch
+    uint32_t wlo[32], whi[32], lohi[2];
+    int wsum[32], wcnt[32];
+    int misc[8];                // bin, count above it, its count, candidates, pivot key, pivot id
+    uint32_t cand_k[32];
+    int cand_i[32];
+};
+
+template <int E, typename Emit, typename GKey>
+__device__ __forceinline__ void select_small(SelShared& S, int n, int k, const float* srow, const uint8_t* vrow,
+                                             Emit& emit, GKey& gkey) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = kSelThreads / 32;
+    const int base = tid * E;
+    uint32_t kr[E];
+    {
+        float f[E];
+        if (E == 4) {
+            const float4 v = base < n ? __ldcg(reinterpret_cast<const float4*>(srow + base))
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            f[0] = v.x; f[1] = v.y; f[2 % E] = v.z; f[3 % E] = v.w;
+        } else {
+            const float2 v = base < n ? __ldcg(reinterpret_cast<const float2*>(srow + base)) : make_float2(0.f, 0.f);
+            f[0] = v.x; f[1] = v.y;
+        }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            if (i + e < a.n_c) {
-                if (vrow && !vrow[i + e]) fv[e] = -INFINITY;
-                if (small) keys[i + e] = fv[e];
-                const uint32_t kk = ordered_u32(fv[e]);
-                if (kk > kOrderedNegInf) klo = min(klo, kk);
-                khi = max(khi, kk);
-            }
+        for (int e = 0; e < E; ++e) {
+            const bool in = base + e < n;
+            const bool ok = !vrow || !in || vrow[base + e] != 0;
+            kr[e] = in ? (ok ? ordered_u32(f[e]) : kOrderedNegInf) : 0u;
+        }
+    }
+    uint32_t klo = 0xffffffffu, khi = 0u;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        if (base + e < n) {
+            if (kr[e] > kOrderedNegInf) klo = min(klo, kr[e]);
+            khi = max(khi, kr[e]);
         }
     }
 #pragma unroll
@@ -378,10 +395,150 @@ __global__ void __launch_bounds__(kSelThreads) raw_select_kernel(const __grid_co
         khi = max(khi, __shfl_xor_sync(0xffffffffu, khi, off));
     }
     if (lane == 0) {
-        atomicMin(&lohi[0], klo);
-        atomicMax(&lohi[1], khi);
+        S.wlo[warp] = klo;
+        S.whi[warp] = khi;
     }
     __syncthreads();
+    if (warp == 0) {
+        klo = lane < NW ? S.wlo[lane] : 0xffffffffu;
+        khi = lane < NW ? S.whi[lane] : 0u;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            klo = min(klo, __shfl_xor_sync(0xffffffffu, klo, off));
+            khi = max(khi, __shfl_xor_sync(0xffffffffu, khi, off));
+        }
+        if (lane == 0) {
+            S.lohi[0] = klo;
+            S.lohi[1] = khi;
+        }
+    }
+    __syncthreads();
+    const uint32_t lo = S.lohi[0], hi = S.lohi[1];
+    // bucket: monotone in the key; -inf (and every key when hi <= lo) -> bin 0
+    const bool same_sign = ((lo ^ hi) & 0x80000000u) == 0u;
+    const uint32_t span = hi > lo ? hi - lo : 0u;
+    const int bits = span ? 32 - __clz(span) : 0;
+    const int sh = bits > 11 ? bits - 11 : 0;
+    const float flo = float_of_ordered(lo), fhi = float_of_ordered(hi);
+    const float inv = (hi > lo) ? (float)kSelBins / (fhi - flo) : 0.0f;
+    uint32_t bk[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const uint32_t kk = kr[e];
+        if (same_sign) {
+            bk[e] = kk >= lo ? min((kk - lo) >> sh, (uint32_t)(kSelBins - 1)) : 0u;
+        } else {
+            const float fb = fminf(fmaxf((float_of_ordered(kk) - flo) * inv, 0.0f), (float)(kSelBins - 1));
+            bk[e] = (uint32_t)fb;
+        }
+        if (base + e < n) atomicAdd(&S.hist[bk[e]], 1);
+    }
+    __syncthreads();
+    {   // suffix counts: thread t owns bins [PL t, PL t + PL)
+        constexpr int PL = kSelBins / kSelThreads;
+        int h[PL], suf[PL];
+        int tot = 0;
+#pragma unroll
+        for (int j = PL - 1; j >= 0; --j) {
+            h[j] = S.hist[PL * tid + j];
+            tot += h[j];
+            suf[j] = tot;
+        }
+        int incl = tot;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int v = __shfl_down_sync(0xffffffffu, incl, off);
+            if (lane + off < 32) incl += v;
+        }
+        if (lane == 0) S.wsum[warp] = incl;
+        __syncthreads();
+        int above = lane < NW && lane > warp ? S.wsum[lane] : 0;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) above += __shfl_xor_sync(0xffffffffu, above, off);
+        above += incl - tot;
+#pragma unroll
+        for (int j = 0; j < PL; ++j) {
+            const int ge = above + suf[j], gt = ge - h[j];
+            if (gt < k && ge >= k) {
+                S.misc[0] = PL * tid + j;
+                S.misc[1] = gt;
+                S.misc[2] = h[j];
+            }
+        }
+    }
+    __syncthreads();
+    const uint32_t bstar = (uint32_t)S.misc[0];
+    const int rem = k - S.misc[1], m = S.misc[2];
+    uint32_t tk = 0u;
+    int ti = 0x7fffffff;  // rem == m: the whole bin is kept
+    if (rem < m) {
+        if (m > 32) {  // heavy ties or a narrow range: the exact radix select over the same keys
+            __syncthreads();
+            block_topk<kSelThreads, true>(gkey, n, k, S.hist, S.misc, S.scan, emit);
+            return;
+        }
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            if (base + e < n && bk[e] == bstar) {
+                const int p = atomicAdd(&S.misc[3], 1);
+                S.cand_k[p] = kr[e];
+                S.cand_i[p] = base + e;
+            }
+        }
+        __syncthreads();
+        if (warp == 0) {  // exact rank of each candidate: key descending, id ascending
+            const uint32_t ck = lane < m ? S.cand_k[lane] : 0u;
+            const int ci = lane < m ? S.cand_i[lane] : 0x7fffffff;
+            int rank = 0;
+            for (int j = 0; j < m; ++j) {
+                const uint32_t kj = __shfl_sync(0xffffffffu, ck, j);
+                const int ij = __shfl_sync(0xffffffffu, ci, j);
+                rank += (kj > ck) || (kj == ck && ij < ci);
+            }
+            if (lane < m && rank == rem - 1) {
+                S.misc[4] = (int)ck;
+                S.misc[5] = ci;
+            }
+        }
+        __syncthreads();
+        tk = (uint32_t)S.misc[4];
+        ti = S.misc[5];
+    }
+    unsigned fl = 0u;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const bool keep = base + e < n &&
+                          (bk[e] > bstar || (bk[e] == bstar && (kr[e] > tk || (kr[e] == tk && base + e <= ti))));
+        fl |= (unsigned)keep << e;
+    }
+    const int cnt = __popc(fl);
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += v;
+    }
+    if (lane == 31) S.wcnt[warp] = incl;
+    __syncthreads();
+    int pos = lane < NW && lane < warp ? S.wcnt[lane] : 0;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) pos += __shfl_xor_sync(0xffffffffu, pos, off);
+    pos += incl - cnt;
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+        if ((fl >> e) & 1u) emit(pos++, base + e);
+}
+
+__global__ void __launch_bounds__(kSelThreads) raw_select_kernel(const __grid_constant__ Args a) {
+    __shared__ SelShared S;
+    const int r = blockIdx.x, tid = threadIdx.x;
+    for (int i = tid; i < kSelBins; i += kSelThreads) S.hist[i] = 0;
+    if (tid == 0) S.misc[3] = 0;
+    grid_dep_wait();          // the scores of the score kernel
+    grid_dep_launch_next();   // the attend kernel may become resident (it waits for this grid)
+    const int n = a.n_c, k = a.nk;
+    const float* srow = a.scores + (int64_t)r * a.n_c_pad;
+    const uint8_t* vrow = a.valid ? a.valid + (int64_t)r * a.n_max : nullptr;
     int32_t* selr = a.sel + (int64_t)r * a.nk;
     int64_t* selo = a.sel_out ? a.sel_out + (int64_t)r * a.nk : nullptr;
     auto emit = [&](int pos, int i) {
@@ -393,12 +550,15 @@ __global__ void __launch_bounds__(kSelThreads) raw_select_kernel(const __grid_co
         selr[pos] = i;
         if (selo) selo[pos] = i;
     };
-    if (small)
-        block_topk_small<kSelThreads>(keys, a.n_c, a.nk, lohi[0], lohi[1], hist, misc, scan, emit);
-    else
-        block_topk<kSelThreads, true>(
-            [&](int i) { return (vrow && !vrow[i]) ? kOrderedNegInf : ordered_u32(__ldcg(srow + i)); }, a.n_c, a.nk,
-            hist, misc, scan, emit, true, lohi[0], lohi[1]);
+    auto gkey = [&](int i) { return (vrow && !vrow[i]) ? kOrderedNegInf : ordered_u32(__ldcg(srow + i)); };
+    if (n <= 2 * kSelThreads) {
+        select_small<2>(S, n, k, srow, vrow, emit, gkey);
+    } else if (n <= 4 * kSelThreads) {
+        select_small<4>(S, n, k, srow, vrow, emit, gkey);
+    } else {
+        __syncthreads();
+        block_topk<kSelThreads, true>(gkey, n, k, S.hist, S.misc, S.scan, emit);
+    }
 }
 
 // ---------------------------------------------------------------- kernel 3: attend
@@ -420,25 +580,12 @@ __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_co
         mbar_fence_init();
     }
     __syncthreads();
-    grid_dep_wait();          // the selection of the select kernel
-    grid_dep_launch_next();   // the merge kernel may become resident (it waits for this grid)
     const int e0 = tile * a.EPC;
     const int e1 = min(a.E, e0 + a.EPC);
     const int nw = e1 - e0 > warp ? (e1 - e0 - warp + kWarps - 1) / kWarps : 0;  // pages of this warp (<= 32)
     const int pg0 = a.RS + a.RN;
-    // lane j reads the chunk id of the warp's j-th entry (all in flight at once)
-    int my_chunk = 0;
-    if (lane < nw) {
-        const int e = e0 + warp + kWarps * lane;
-        if (e >= pg0) {
-            const int p = e - pg0;
-            my_chunk = a.ST > 0 ? __ldcg(a.sel + (int64_t)r * a.nk + p) : p;
-            if (a.ST == 0 && a.sel_out) a.sel_out[(int64_t)r * a.nk + p] = p;  // identity selection
-        }
-    }
     const uint32_t slot0 = smem_u32(region) + (uint32_t)(warp * kSlots * kSlotBytes);
-    auto issue = [&](int j) -> unsigned {  // warp-uniform; returns the page's present mask
-        const int chunk = __shfl_sync(0xffffffffu, my_chunk, j & 31);
+    auto issue_chunk = [&](int j, int chunk) -> unsigned {  // warp-uniform; returns the page's present mask
         unsigned pr;
         const int64_t y0 = entry_tokens(a, e0 + warp + kWarps * j, chunk, pr);
         if (lane == 0) {
@@ -453,10 +600,32 @@ __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_co
         }
         return pr;
     };
-    unsigned pres0 = nw > 0 ? issue(0) : 0u;
-    unsigned pres1 = nw > 1 ? issue(1) : 0u;
+    // Sink and near pages do not depend on the selection, and the K/V rows
+    // and q were written before the score kernel began: their copies and the
+    // query fragments are taken before waiting for the select kernel.
+    const bool pre0 = nw > 0 && e0 + warp < pg0;
+    const bool pre1 = nw > 1 && e0 + warp + kWarps < pg0;
+    unsigned pres0 = pre0 ? issue_chunk(0, 0) : 0u;
+    unsigned pres1 = pre1 ? issue_chunk(1, 0) : 0u;
     WarpState st;
     state_init(st, a.q + (int64_t)r * a.G * kHeadDim, a.G);
+    grid_dep_wait();          // the selection of the select kernel
+    grid_dep_launch_next();   // the merge kernel may become resident (it waits for this grid)
+    // lane j reads the chunk id of the warp's j-th entry (all in flight at once)
+    int my_chunk = 0;
+    if (lane < nw) {
+        const int e = e0 + warp + kWarps * lane;
+        if (e >= pg0) {
+            const int p = e - pg0;
+            my_chunk = a.ST > 0 ? __ldcg(a.sel + (int64_t)r * a.nk + p) : p;
+            if (a.ST == 0 && a.sel_out) a.sel_out[(int64_t)r * a.nk + p] = p;  // identity selection
+        }
+    }
+    auto issue = [&](int j) -> unsigned {
+        return issue_chunk(j, __shfl_sync(0xffffffffu, my_chunk, j & 31));
+    };
+    if (nw > 0 && !pre0) pres0 = issue(0);
+    if (nw > 1 && !pre1) pres1 = issue(1);
     for (int j = 0; j < nw; ++j) {
         const int sl = j & 1;
         const unsigned pres = sl ? pres1 : pres0;
@@ -719,7 +888,7 @@ static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near, const Hier
 }
 
 static size_t score_smem() { return kScoreRegion + kHeadDim * 2 + kWarps * 8; }
-static size_t select_smem() { return (size_t)(kSelSmall + 512 + 8 + 2 * kSelThreads + 2) * 4; }
+static size_t select_smem() { return 0; }
 static size_t attend_smem() { return 1024 + kAttRegion + kWarps * kSlots * 8; }
 
 static int launch_pdl(const void* fn, int grid, int threads, size_t smem, cudaStream_t stream, void** args) {
