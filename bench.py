@@ -432,6 +432,63 @@ def run_config1_reference(args):
         "clocks": clk.summary()}), flush=True)
 
 
+def run_config4(args):
+    """Config 4: the decode loop (zoomkv_revision_b200/decode_loop.py) on a
+    random-init Qwen3-8B (36 layers), batch 32, a 512-token prompt of ids
+    uniform over the vocabulary, args.gen generated tokens at temperature 0.6
+    / top-p 0.95 / top-k 20, seed 42; the cache refreshes its retrieval zone
+    every 512 steps and attends densely below 2048 tokens.  One GPU.  Prints
+    decode tokens/s (batch x generated / decode time) and the per-step time
+    of the dense and the sparse regimes."""
+    import torch
+    from zoomkv_revision_b200 import decode_loop as DL
+    from zoomkv_revision_b200 import polar_cache as P
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    shape = DL.Shape(layers=args.layers)
+    B, prompt, gen = 32, 512, args.gen
+    mode = "reference" if args.mode == "reference" else "page"
+    os.environ.update({"ZKV_ATTENTION_MODE": mode, "POLAR_QUEST_CHUNK": "16", "ZKV_HOST_RETRIEVAL": "0"})
+    if mode == "page":
+        os.environ.update({"POLAR_FORCE_CAND_TOKENS": str(BUDGET), "POLAR_CDS_DENSE_TOPK": "16",
+                           "POLAR_CDS_SPARSE_TOPK": "16"})
+    cache = P.polar_cache(**DL.config4_cache_kwargs(shape, B, prompt, gen + 16, dev))
+    w = DL.Weights(shape, dev, seed=0)
+    loop = DL.DecodeLoop(shape, w, cache, B, prompt + gen + 16, dev)
+    ids = torch.randint(0, shape.vocab, (B, prompt), generator=torch.Generator().manual_seed(42)).to(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    torch.cuda.synchronize()
+    ev[0].record()
+    tok = loop.prefill(ids)
+    ev[1].record()
+    cross = None
+    for i in range(gen - 1):
+        if cross is None and loop.position + 1 >= cache.FULL_ATTENTION_THRESHOLD:
+            cross = i
+            ev[2].record()
+        tok = loop.step(tok)
+    ev[3].record()
+    torch.cuda.synchronize()
+    prefill_ms = ev[0].elapsed_time(ev[1])
+    decode_ms = ev[1].elapsed_time(ev[3])
+    steps = gen - 1
+    line = {
+        "metric": "config4 decode tokens/s (random-init Qwen3-8B, batch 32, 512-token prompt)",
+        "value": B * steps / (decode_ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": 0,
+        "ms_per_step": decode_ms / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (random weights and prompt ids)",
+        "config": {"workload": f"config4: decode loop, attention mode {mode}", "layers": shape.layers, "batch": B,
+                   "prompt": prompt, "generated": gen, "sampling": "T 0.6, top-p 0.95, top-k 20, seed 42",
+                   "refresh_interval": 512, "dense_below": 2048},
+        "prefill_ms": prefill_ms,
+        "dense_ms_per_step": (ev[1].elapsed_time(ev[2]) / cross) if cross else None,
+        "sparse_ms_per_step": (ev[2].elapsed_time(ev[3]) / (steps - cross)) if cross is not None and steps > cross
+        else None,
+        "cuda_graphs": "one per layer for the dense segments between attention calls",
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_config3_raw(args):
     """Config 3 (Qwen3-4B shape, batch 1, 131072 context, budget 4096) in the
     raw-row page mode on one GPU: the flat Quest pick against the hierarchical
@@ -774,12 +831,13 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--soak", type=float, default=1.5, help="seconds of load before timing (clock sampling)")
-    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 5],
+    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4, 5],
                     help="5: the offload tier (retrieval zone in host-pinned memory)")
     ap.add_argument("--mode", default="raw", choices=["raw", "page4", "reference"],
                     help="config 1 only: raw = page mode over the selected pages' raw bf16 rows (the headline, the "
                          "reference's page mode); page4 = page mode over 4-bit KIVI K/V pages (lossy variant); "
                          "reference = the drop-in's default reference mode with production knobs")
+    ap.add_argument("--gen", type=int, default=8192, help="config 4: tokens generated per sequence")
     ap.add_argument("--raw3", action="store_true",
                     help="config 3 on one GPU in the raw-row page mode: flat against hierarchical Quest")
     args = ap.parse_args()
@@ -789,6 +847,9 @@ def main():
         return
     if args.config == 2 and args.impl == "ours":
         run_config2(args)
+        return
+    if args.config == 4 and args.impl == "ours":
+        run_config4(args)
         return
     if args.config == 3 and args.impl == "ours":
         if args.mode == "raw" and int(os.environ.get("WORLD_SIZE", "1")) == 1 and args.raw3:

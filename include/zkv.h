@@ -374,6 +374,22 @@ int zkv_page_decode_raw_hier(const void* q, const zkv_raw_layer* layer, const zk
                              int near_start, int n_near, float scale, void* out, float* lse, int64_t* sel_out,
                              int32_t* status, void* workspace, size_t ws_bytes, void* stream);
 
+/* Decode-loop caller kernels (the benchmark's config 4; no reference
+ * counterpart of their own: the reference's model code calls flashinfer's
+ * rmsnorm / apply_rope_with_cos_sin_cache_inplace / silu_and_mul for these
+ * steps, model_hub/qwen.py:481-612).  bf16 in and out, fp32 inside.
+ * zkv_rmsnorm: y = x * rsqrt(mean(x^2) + eps) * w per row of dim.
+ * zkv_qk_norm_rope: qkv [rows][(hq + 2 hkv) * 128] -> q [rows][hq][128],
+ *   k / v [rows][hkv][128]; q and k heads get RMSNorm over the head (q_norm,
+ *   k_norm [128]) then the rotate-half RoPE at position *pos (device int64;
+ *   cos_t / sin_t fp32 [max_pos][64]).
+ * zkv_silu_mul: out [rows][ffn] = silu(gu[:, :ffn]) * gu[:, ffn:].        */
+int zkv_rmsnorm(const void* x, const void* w, void* y, int rows, int dim, float eps, void* stream);
+int zkv_qk_norm_rope(const void* qkv, const void* q_norm, const void* k_norm, const float* cos_t,
+                     const float* sin_t, const int64_t* pos, int rows, int hq, int hkv, float eps, void* q,
+                     void* k, void* v, void* stream);
+int zkv_silu_mul(const void* gu, void* out, int rows, int ffn, void* stream);
+
 /* Attention over externally selected pages (the sequence-split step):
  * the layer buffer holds pages [sel_lo, sel_hi) of the sequence as its
  * pages 0..; of the global page ids sel [rows][n_sel] (-1 = none) those in

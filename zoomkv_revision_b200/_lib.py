@@ -113,6 +113,9 @@ _SIGNATURES = {
     "zkv_page_decode_raw_ws_bytes": [_i32, _i32, _i32, _i32, _i32],
     "zkv_page_decode_raw": [_c_void_p, ctypes.POINTER(ZkvRawLayer), _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                             _f32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
+    "zkv_rmsnorm": [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, ctypes.c_float, _c_void_p],
+    "zkv_qk_norm_rope": [_c_void_p] * 6 + [_i32, _i32, _i32, ctypes.c_float] + [_c_void_p] * 4,
+    "zkv_silu_mul": [_c_void_p, _c_void_p, _i32, _i32, _c_void_p],
     "zkv_quest_large_minmax": [_c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p,
                                _c_void_p, _i32, _c_void_p],
     "zkv_page_decode_raw_hier_ws_bytes": [_i32] * 7,

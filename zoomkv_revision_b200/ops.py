@@ -794,6 +794,34 @@ def page_decode_raw_hier(q, layer: RawLayer, large: LargeLayer, n_c: int, factor
     return out
 
 
+# ----------------------------------------------------------------- decode-loop caller
+def rmsnorm(x, w, eps: float, out=None):
+    """Row-wise RMSNorm of x [..., dim] bf16 with weight w [dim] (fp32 inside)."""
+    _dtype("x", x, torch.bfloat16)
+    _contig("x", x)
+    out = torch.empty_like(x) if out is None else out
+    check(lib().zkv_rmsnorm(_p(x), _p(w), _p(out), x.numel() // x.shape[-1], x.shape[-1], float(eps), _stream(x)),
+          "zkv_rmsnorm")
+    return out
+
+
+def qk_norm_rope(qkv, q_norm, k_norm, cos, sin, pos, hq: int, hkv: int, eps: float, q, k, v):
+    """qkv [rows, (hq + 2 hkv) * 128] -> q / k (per-head RMSNorm + rotate-half
+    RoPE at position pos[0], a device int64) and v, into the given buffers."""
+    _contig("qkv", qkv)
+    rows = qkv.numel() // ((hq + 2 * hkv) * 128)
+    check(lib().zkv_qk_norm_rope(_p(qkv), _p(q_norm), _p(k_norm), _p(cos), _p(sin), _p(pos), rows, hq, hkv,
+                                 float(eps), _p(q), _p(k), _p(v), _stream(qkv)), "zkv_qk_norm_rope")
+
+
+def silu_mul(gu, out):
+    """out [rows, ffn] = silu(gu[:, :ffn]) * gu[:, ffn:] (bf16, fp32 inside)."""
+    _contig("gu", gu)
+    ffn = gu.shape[-1] // 2
+    check(lib().zkv_silu_mul(_p(gu), _p(out), gu.numel() // gu.shape[-1], ffn, _stream(gu)), "zkv_silu_mul")
+    return out
+
+
 def gqa_mean(q, heads: int, out=None):
     """raw_q [bs, H, 128] bf16 = GQA mean of q [bs, 1, H*G, 128] (fp32 sum in
     head order / G, as the fused kernels compute it)."""
