@@ -12,7 +12,7 @@
 //    chunks' Quest min/max (32 KiB) into shared memory; each half-warp scores
 //    a chunk with the reference kernel's fp32 operation order and writes the
 //    score to the workspace.
-//  * raw_select_kernel: one CTA of 1024 threads per row (2 or 4 keys per
+//  * raw_select_kernel: one CTA of 1024 threads per row (2, 4 or 8 keys per
 //    thread): invalid chunks -> -inf, then the top nk chunk ids (ties to the
 //    lowest id, ascending).
 //  * raw_attend_kernel: one CTA per (row, EPC entries of 16 tokens) with EPC
@@ -340,8 +340,8 @@ __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_consta
 // ---------------------------------------------------------------- kernel 2: select
 // One CTA of kSelThreads per row: the row's scores (invalid chunks -> -inf)
 // -> top nk chunk ids, ties to the lowest id, ascending.  Rows of up to
-// 4 * kSelThreads chunks: thread t holds keys [E t, E t + E) in registers
-// (E = 2 or 4), so every warp holds keys and each thread's chains are short;
+// 8 * kSelThreads chunks: thread t holds keys [E t, E t + E) in registers
+// (E = 2, 4 or 8), so every warp holds keys and each thread's chains are short;
 // one kSelBins-bin histogram over the row's [min finite, max] key range (a
 // bucketing monotone in the key) gives the bin of the nk-th best; a warp
 // ranks that bin's keys exactly when it holds at most 32 (else the exact
@@ -366,10 +366,16 @@ __device__ __forceinline__ void select_small(SelShared& S, int n, int k, const f
     uint32_t kr[E];
     {
         float f[E];
-        if (E == 4) {
-            const float4 v = base < n ? __ldcg(reinterpret_cast<const float4*>(srow + base))
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-            f[0] = v.x; f[1] = v.y; f[2 % E] = v.z; f[3 % E] = v.w;
+        if (E >= 4) {
+#pragma unroll
+            for (int u = 0; u < E / 4; ++u) {
+                const float4 v = base + 4 * u < n ? __ldcg(reinterpret_cast<const float4*>(srow + base) + u)
+                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                f[(4 * u) % E] = v.x;
+                f[(4 * u + 1) % E] = v.y;
+                f[(4 * u + 2) % E] = v.z;
+                f[(4 * u + 3) % E] = v.w;
+            }
         } else {
             const float2 v = base < n ? __ldcg(reinterpret_cast<const float2*>(srow + base)) : make_float2(0.f, 0.f);
             f[0] = v.x; f[1] = v.y;
@@ -555,6 +561,8 @@ __global__ void __launch_bounds__(kSelThreads) raw_select_kernel(const __grid_co
         select_small<2>(S, n, k, srow, vrow, emit, gkey);
     } else if (n <= 4 * kSelThreads) {
         select_small<4>(S, n, k, srow, vrow, emit, gkey);
+    } else if (n <= 8 * kSelThreads) {
+        select_small<8>(S, n, k, srow, vrow, emit, gkey);
     } else {
         __syncthreads();
         block_topk<kSelThreads, true>(gkey, n, k, S.hist, S.misc, S.scan, emit);
