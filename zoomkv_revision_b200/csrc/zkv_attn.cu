@@ -758,6 +758,7 @@ struct RowsArgs {
 };
 
 __global__ void __launch_bounds__(kAttnThreads, 4) attn_rows_kernel(const RowsArgs a) {
+    pdl_begin();  // inputs may come from the previous kernel on the stream
     extern __shared__ __align__(128) uint8_t smem[];
     cg::cluster_group cluster = cg::this_cluster();
     const int CS = (int)cluster.num_blocks();
@@ -1085,7 +1086,8 @@ extern "C" int zkv_attn_rows(const void* q, const void* keys, const void* values
     a.status = status;
     const size_t smem = kRegionBytes + 8 * kHeadDim * 2 + (16 + 8 * kHeadDim) * 4 + 2 * kAttnWarps * 8 + 16;
     void* args[] = {&a};
-    return launch_clustered((const void*)attn_rows_kernel, rows * CS, kAttnThreads, CS, smem, (cudaStream_t)stream, args);
+    return launch_clustered((const void*)attn_rows_kernel, rows * CS, kAttnThreads, CS, smem, (cudaStream_t)stream, args,
+                            true);
 }
 
 extern "C" int zkv_lse_merge(const void* a, const float* la, const void* b, const float* lb, void* out,

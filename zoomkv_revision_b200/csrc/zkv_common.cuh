@@ -107,6 +107,13 @@ __device__ __forceinline__ uint32_t ordered_u32(float x) {
 // launch); allow the next kernel on the stream to be scheduled.
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Start of a kernel that may be launched with programmatic dependent launch:
+// wait for the previous grid on the stream (a no-op without the attribute)
+// before any memory access.  The next grid is not released early: in the
+// reference-mode chain, dependents made resident at a kernel's start took
+// slots from its later waves (3,534 tokens/s with the early release, 3,671
+// without programmatic launch, 3,951 with the wait alone).
+__device__ __forceinline__ void pdl_begin() { grid_dep_wait(); }
 
 // ------------------------------------------------------------ time
 // Nanoseconds of the GPU's global timer: bounds waits by time rather than by
@@ -697,6 +704,26 @@ __device__ __forceinline__ float quest_half(uint4 qv, uint4 mnv, uint4 mxv) {
 }  // namespace zkv
 
 static inline int launch_status() { return cudaGetLastError() == cudaSuccess ? ZKV_OK : ZKV_ERR_LAUNCH; }
+
+// Launch a kernel that begins with pdl_begin() with programmatic dependent
+// launch allowed: it may become resident while the previous kernel on the
+// stream drains, and waits for it before touching memory.
+template <typename... KArgs, typename... Args>
+static int launch_pdl_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...) != cudaSuccess) return ZKV_ERR_LAUNCH;
+    return launch_status();
+}
 
 // Internal launchers shared across translation units (not part of the C ABI).
 int quest_score_gqa_into(const void* q, int G, const void* chunk_min, const void* chunk_max, const uint8_t* valid,

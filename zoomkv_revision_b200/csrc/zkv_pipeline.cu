@@ -9,6 +9,7 @@ namespace zkv {
 // (the GQA mean of polar_cache.compute, REF:1622-1625).  One warp per row.
 __global__ void __launch_bounds__(256) gqa_mean_kernel(const uint16_t* __restrict__ q, int rows, int G,
                                                        uint16_t* __restrict__ raw_q) {
+    pdl_begin();  // inputs may come from the previous kernel on the stream
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     float s[4] = {0.f, 0.f, 0.f, 0.f};
@@ -62,8 +63,8 @@ extern "C" int zkv_gqa_mean(const void* q, int rows, int G, void* raw_q, void* s
     if (!q || !raw_q || rows < 0 || G < 1) return ZKV_ERR_ARG;
     if (((uintptr_t)q & 7) || ((uintptr_t)raw_q & 7)) return ZKV_ERR_ALIGN;
     if (rows == 0) return ZKV_OK;
-    gqa_mean_kernel<<<(rows + 7) / 8, 256, 0, (cudaStream_t)stream>>>((const uint16_t*)q, rows, G, (uint16_t*)raw_q);
-    return launch_status();
+    return launch_pdl_kernel(gqa_mean_kernel, dim3((rows + 7) / 8), dim3(256), 0, (cudaStream_t)stream,
+                             (const uint16_t*)q, rows, G, (uint16_t*)raw_q);
 }
 
 extern "C" size_t zkv_reference_select_ws_bytes(int rows, int n_chunks, int nk, int n_dense) {
@@ -103,8 +104,9 @@ extern "C" int zkv_reference_select(const void* q, int G, const zkv_ref_layer* L
                                       st)))
             return s;
     } else {
-        gqa_mean_kernel<<<(rows + 7) / 8, 256, 0, st>>>((const uint16_t*)q, rows, G, raw_q);
-        if ((s = launch_status())) return s;
+        if ((s = launch_pdl_kernel(gqa_mean_kernel, dim3((rows + 7) / 8), dim3(256), 0, st, (const uint16_t*)q, rows,
+                                   G, raw_q)))
+            return s;
         if ((s = zkv_quest_score(raw_q, L->chunk_min, L->chunk_max, L->valid, scores, rows, n_chunks, n_max, stream)))
             return s;
     }

@@ -13,6 +13,7 @@ __global__ void __launch_bounds__(256) quest_score_kernel(const uint16_t* __rest
                                                           float* __restrict__ scores, int n_chunks, int n_max,
                                                           const uint16_t* __restrict__ q = nullptr, int G = 0,
                                                           uint16_t* __restrict__ raw_q_out = nullptr) {
+    pdl_begin();  // inputs may come from the previous kernel on the stream
     const int r = blockIdx.y;
     const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
     const int warp = threadIdx.x >> 5;
@@ -102,6 +103,7 @@ __device__ __forceinline__ void stage_row(const float* __restrict__ src, int len
 template <typename KeyOf>
 __global__ void __launch_bounds__(kTopkThreads) topk_kernel(KeyOf keyof, int len, int64_t row_stride, int k,
                                                             int64_t* __restrict__ out) {
+    pdl_begin();  // inputs may come from the previous kernel on the stream
     __shared__ int hist[512];
     __shared__ int misc[8];
     __shared__ int scan[2 * kTopkThreads];
@@ -130,6 +132,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(KeyOf keyof, int len
 // mask_from_topk in one launch, same selection as topk_kernel.
 __global__ void __launch_bounds__(kTopkThreads) topk_mask_kernel(const float* __restrict__ dens, int nk, int n_dense,
                                                                  uint8_t* __restrict__ mask) {
+    pdl_begin();  // inputs may come from the previous kernel on the stream
     __shared__ int hist[512];
     __shared__ int misc[8];
     __shared__ int scan[2 * kTopkThreads];
@@ -162,6 +165,7 @@ __global__ void __launch_bounds__(256) density_kernel(const int64_t* __restrict_
                                                       const uint16_t* __restrict__ cent,
                                                       const uint16_t* __restrict__ raw_q, float* __restrict__ out,
                                                       int rows, int nk, int n_chunks, int n_max) {
+    pdl_begin();  // inputs may come from the previous kernel on the stream
     const int lane = threadIdx.x & 31;
     const int64_t job = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     if (job >= (int64_t)rows * nk) return;
@@ -184,6 +188,7 @@ __global__ void __launch_bounds__(256) density_kernel(const int64_t* __restrict_
 }
 
 __global__ void mask_kernel(const int64_t* __restrict__ pos, uint8_t* __restrict__ mask, int n_dense, int nk) {
+    pdl_begin();  // inputs may come from the previous kernel on the stream
     const int r = blockIdx.x;
     uint8_t* m = mask + (int64_t)r * nk;
     for (int i = threadIdx.x; i < nk; i += blockDim.x) m[i] = 0;
@@ -211,6 +216,7 @@ __global__ void __launch_bounds__(128) kivi_qk_kernel(const int64_t* __restrict_
                                                       const uint16_t* __restrict__ raw_q, int nk, int dense_topk,
                                                       int sparse_topk, float* __restrict__ out_s,
                                                       int64_t* __restrict__ out_i, int64_t out_ld) {
+    pdl_begin();  // inputs may come from the previous kernel on the stream
     __shared__ __align__(16) uint16_t s_q[kHeadDim];
     __shared__ __align__(16) uint32_t s_mn[8][kHeadDim / 2];
     __shared__ __align__(16) uint32_t s_sc[8][kHeadDim / 2];
@@ -296,6 +302,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_gather_concat_kernel(const 
                                                                           int64_t sk_ld,
                                                                           int64_t* __restrict__ out, int L, int k,
                                                                           int sk, int64_t out_ld) {
+    pdl_begin();  // inputs may come from the previous kernel on the stream
     __shared__ int hist[512];
     __shared__ int misc[8];
     __shared__ int scan[2 * kTopkThreads];
@@ -335,10 +342,10 @@ extern "C" int zkv_quest_score(const void* raw_q, const void* chunk_min, const v
     if (((uintptr_t)raw_q & 15) || ((uintptr_t)chunk_min & 15) || ((uintptr_t)chunk_max & 15)) return ZKV_ERR_ALIGN;
     constexpr int U = 4;
     dim3 grid((n_chunks + 8 * 2 * U - 1) / (8 * 2 * U), rows);
-    quest_score_kernel<U><<<grid, 256, 0, (cudaStream_t)stream>>>((const uint16_t*)raw_q, (const uint16_t*)chunk_min,
-                                                                  (const uint16_t*)chunk_max, valid, scores, n_chunks,
-                                                                  n_max);
-    return launch_status();
+    return launch_pdl_kernel(quest_score_kernel<U>, dim3(grid), dim3(256), 0, (cudaStream_t)stream,
+                             (const uint16_t*)raw_q, (const uint16_t*)chunk_min,
+                             (const uint16_t*)chunk_max, valid, scores, n_chunks,
+                             n_max, (const uint16_t*)nullptr, 0, (uint16_t*)nullptr);
 }
 
 int quest_score_gqa_into(const void* q, int G, const void* chunk_min, const void* chunk_max, const uint8_t* valid,
@@ -350,10 +357,10 @@ int quest_score_gqa_into(const void* q, int G, const void* chunk_min, const void
         return ZKV_ERR_ALIGN;
     constexpr int U = 4;
     dim3 grid((n_chunks + 8 * 2 * U - 1) / (8 * 2 * U), rows);
-    quest_score_kernel<U><<<grid, 256, 0, stream>>>(nullptr, (const uint16_t*)chunk_min, (const uint16_t*)chunk_max,
-                                                    valid, scores, n_chunks, n_max, (const uint16_t*)q, G,
-                                                    (uint16_t*)raw_q_out);
-    return launch_status();
+    return launch_pdl_kernel(quest_score_kernel<U>, dim3(grid), dim3(256), 0, stream,
+                             nullptr, (const uint16_t*)chunk_min, (const uint16_t*)chunk_max,
+                             valid, scores, n_chunks, n_max, (const uint16_t*)q, G,
+                             (uint16_t*)raw_q_out);
 }
 
 extern "C" int zkv_quest_score_gqa(const void* q, int G, const void* chunk_min, const void* chunk_max,
@@ -367,16 +374,16 @@ extern "C" int zkv_topk_f32(const float* scores, int rows, int len, int64_t row_
                             void* stream) {
     if (rows < 0 || len < 0 || k <= 0 || row_stride < len) return ZKV_ERR_ARG;
     if (rows == 0) return ZKV_OK;
-    topk_kernel<<<rows, kTopkThreads, 0, (cudaStream_t)stream>>>(F32Key{scores}, len, row_stride, k, out);
-    return launch_status();
+    return launch_pdl_kernel(topk_kernel<F32Key>, dim3(rows), dim3(kTopkThreads), 0, (cudaStream_t)stream,
+                             F32Key{scores}, len, row_stride, k, out);
 }
 
 extern "C" int zkv_topk_i32(const int32_t* vals, int rows, int len, int64_t row_stride, int k, int64_t* out,
                             void* stream) {
     if (rows < 0 || len < 0 || k <= 0 || row_stride < len) return ZKV_ERR_ARG;
     if (rows == 0) return ZKV_OK;
-    topk_kernel<<<rows, kTopkThreads, 0, (cudaStream_t)stream>>>(I32Key{vals}, len, row_stride, k, out);
-    return launch_status();
+    return launch_pdl_kernel(topk_kernel<I32Key>, dim3(rows), dim3(kTopkThreads), 0, (cudaStream_t)stream,
+                             I32Key{vals}, len, row_stride, k, out);
 }
 
 extern "C" int zkv_chunk_density(const int64_t* chunk_ids, const void* centroid, const void* raw_q, float* out,
@@ -384,24 +391,21 @@ extern "C" int zkv_chunk_density(const int64_t* chunk_ids, const void* centroid,
     if (rows < 0 || nk < 0 || n_chunks > n_max) return ZKV_ERR_ARG;
     if (rows == 0 || nk == 0) return ZKV_OK;
     const int64_t jobs = (int64_t)rows * nk;
-    density_kernel<<<(unsigned)((jobs + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
-        chunk_ids, (const uint16_t*)centroid, (const uint16_t*)raw_q, out, rows, nk, n_chunks, n_max);
-    return launch_status();
+    return launch_pdl_kernel(density_kernel, dim3((unsigned)((jobs + 7) / 8)), dim3(256), 0, (cudaStream_t)stream,
+                             chunk_ids, (const uint16_t*)centroid, (const uint16_t*)raw_q, out, rows, nk, n_chunks, n_max);
 }
 
 int topk_mask_launch(const float* dens, int rows, int nk, int n_dense, uint8_t* mask, cudaStream_t stream) {
     if (rows < 0 || nk < 1 || n_dense < 1 || nk > kTopkSmall) return ZKV_ERR_ARG;
     if (rows == 0) return ZKV_OK;
-    topk_mask_kernel<<<rows, kTopkThreads, 0, stream>>>(dens, nk, n_dense, mask);
-    return launch_status();
+    return launch_pdl_kernel(topk_mask_kernel, dim3(rows), dim3(kTopkThreads), 0, stream, dens, nk, n_dense, mask);
 }
 
 extern "C" int zkv_mask_from_topk(const int64_t* positions, uint8_t* mask, int rows, int n_dense, int nk,
                                   void* stream) {
     if (rows < 0 || n_dense < 0 || nk < 0) return ZKV_ERR_ARG;
     if (rows == 0 || nk == 0) return ZKV_OK;
-    mask_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>(positions, mask, n_dense, nk);
-    return launch_status();
+    return launch_pdl_kernel(mask_kernel, dim3(rows), dim3(256), 0, (cudaStream_t)stream, positions, mask, n_dense, nk);
 }
 
 extern "C" int zkv_kivi_qk(const int64_t* chunk_ids, const uint8_t* dense_mask, const int32_t* packed, int n_pk,
@@ -414,11 +418,11 @@ extern "C" int zkv_kivi_qk(const int64_t* chunk_ids, const uint8_t* dense_mask, 
     if (rows == 0 || nk == 0) return ZKV_OK;
     if (((uintptr_t)chunk_min & 15) || ((uintptr_t)chunk_max & 15) || ((uintptr_t)raw_q & 15)) return ZKV_ERR_ALIGN;
     dim3 grid((nk + 7) / 8, rows);
-    kivi_qk_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(chunk_ids, dense_mask, packed, n_pk, pk_ld,
-                                                           (const uint16_t*)chunk_min, (const uint16_t*)chunk_max,
-                                                           n_max, (const uint16_t*)raw_q, nk, dense_topk, sparse_topk,
-                                                           out_scores, out_idx, out_ld);
-    return launch_status();
+    return launch_pdl_kernel(kivi_qk_kernel, dim3(grid), dim3(128), 0, (cudaStream_t)stream,
+                             chunk_ids, dense_mask, packed, n_pk, pk_ld,
+                             (const uint16_t*)chunk_min, (const uint16_t*)chunk_max,
+                             n_max, (const uint16_t*)raw_q, nk, dense_topk, sparse_topk,
+                             out_scores, out_idx, out_ld);
 }
 
 extern "C" int zkv_topk_gather_concat(const float* scores, const int64_t* lut, const int64_t* skipped,
@@ -427,7 +431,7 @@ extern "C" int zkv_topk_gather_concat(const float* scores, const int64_t* lut, c
     if (rows < 0 || L < 0 || k <= 0 || sk < 0 || out_ld < (int64_t)k + sk || (sk > 0 && sk_ld < sk)) return ZKV_ERR_ARG;
     if (sk > 0 && !skipped) return ZKV_ERR_ARG;
     if (rows == 0) return ZKV_OK;
-    topk_gather_concat_kernel<<<rows, kTopkThreads, 0, (cudaStream_t)stream>>>(scores, lut, skipped, sk_ld, out, L,
-                                                                               k, sk, out_ld);
-    return launch_status();
+    return launch_pdl_kernel(topk_gather_concat_kernel, dim3(rows), dim3(kTopkThreads), 0, (cudaStream_t)stream,
+                             scores, lut, skipped, sk_ld, out, L,
+                             k, sk, out_ld);
 }
