@@ -439,12 +439,21 @@ def run_config4(args):
     / top-p 0.95 / top-k 20, seed 42; the cache refreshes its retrieval zone
     every 512 steps and attends densely below 2048 tokens.  One GPU.  Prints
     decode tokens/s (batch x generated / decode time) and the per-step time
-    of the dense and the sparse regimes."""
+    of the dense and the sparse regimes.  Under torchrun every rank runs its
+    own batch of 32 on its own GPU (replicas, weak scaling; the prompt seed is
+    42 + rank) and the decode time is the maximum over ranks."""
+    import datetime
     import torch
+    import torch.distributed as dist
     from zoomkv_revision_b200 import decode_loop as DL
     from zoomkv_revision_b200 import polar_cache as P
-    dev = torch.device("cuda", 0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     shape = DL.Shape(layers=args.layers)
     B, prompt, gen = 32, 512, args.gen
     mode = "reference" if args.mode == "reference" else "page"
@@ -455,9 +464,11 @@ def run_config4(args):
     cache = P.polar_cache(**DL.config4_cache_kwargs(shape, B, prompt, gen + 16, dev))
     w = DL.Weights(shape, dev, seed=0)
     loop = DL.DecodeLoop(shape, w, cache, B, prompt + gen + 16, dev)
-    ids = torch.randint(0, shape.vocab, (B, prompt), generator=torch.Generator().manual_seed(42)).to(dev)
+    ids = torch.randint(0, shape.vocab, (B, prompt), generator=torch.Generator().manual_seed(42 + rank)).to(dev)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     ev[0].record()
     tok = loop.prefill(ids)
     ev[1].record()
@@ -471,13 +482,19 @@ def run_config4(args):
     torch.cuda.synchronize()
     prefill_ms = ev[0].elapsed_time(ev[1])
     decode_ms = ev[1].elapsed_time(ev[3])
+    if world > 1:
+        t = torch.tensor([decode_ms, prefill_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        decode_ms, prefill_ms = float(t[0].item()), float(t[1].item())
     steps = gen - 1
     line = {
         "metric": "config4 decode tokens/s (random-init Qwen3-8B, batch 32, 512-token prompt)",
-        "value": B * steps / (decode_ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": 0,
+        "value": world * B * steps / (decode_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": 0,
         "ms_per_step": decode_ms / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (random weights and prompt ids)",
-        "config": {"workload": f"config4: decode loop, attention mode {mode}", "layers": shape.layers, "batch": B,
+        "config": {"workload": f"config4: decode loop, attention mode {mode}", "layers": shape.layers,
+                   "batch_per_gpu": B, "parallelism": f"replicas x{world}",
                    "prompt": prompt, "generated": gen, "sampling": "T 0.6, top-p 0.95, top-k 20, seed 42",
                    "refresh_interval": 512, "dense_below": 2048},
         "prefill_ms": prefill_ms,
@@ -486,7 +503,11 @@ def run_config4(args):
         else None,
         "cuda_graphs": "one per layer for the dense segments between attention calls",
     }
-    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 def run_config3_raw(args):
