@@ -729,6 +729,13 @@ static int launch_pdl_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
 int quest_score_gqa_into(const void* q, int G, const void* chunk_min, const void* chunk_max, const uint8_t* valid,
                          float* scores, void* raw_q_out, int rows, int n_chunks, int n_max, cudaStream_t stream);
 int topk_mask_launch(const float* dens, int rows, int nk, int n_dense, uint8_t* mask, cudaStream_t stream);
+// Quest scores + top-nk of the raw page decode's first two kernels (GQA mean
+// folded in), for the reference-mode chain: ids [rows][nk] int64 ascending,
+// the GQA mean into raw_q_out [rows][128]; scores [rows][n_c_pad] fp32 and
+// sel32 [rows][nk] are scratch.  n_c <= 16384.
+int raw_quest_topk(const void* q, int G, const void* cmin, const void* cmax, const uint8_t* valid, int rows,
+                   int n_max, int n_c, int nk, float* scores, int n_c_pad, int32_t* sel32, int64_t* ids,
+                   uint16_t* raw_q_out, cudaStream_t stream);
 
 // Launch `nblocks` CTAs of `nthreads` in clusters of CS (cudaLaunchKernelExC),
 // raising the kernel's dynamic shared-memory limit once per (kernel, device).

@@ -38,7 +38,7 @@ inline size_t up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 // Workspace sections (section-major, each 256-byte aligned).
 struct RefWs {
-    size_t raw_q, scores, chunk_ids, density, dense_pos, mask, kscores, kidx, total;
+    size_t raw_q, scores, sel32, chunk_ids, density, dense_pos, mask, kscores, kidx, total;
 };
 
 inline RefWs ref_ws_layout(int rows, int n_chunks, int nk, int n_dense) {
@@ -46,7 +46,8 @@ inline RefWs ref_ws_layout(int rows, int n_chunks, int nk, int n_dense) {
     size_t o = 0;
     const size_t R = (size_t)rows;
     w.raw_q = o;     o += up(R * kHeadDim * 2);
-    w.scores = o;    o += up(R * (size_t)n_chunks * 4);
+    w.scores = o;    o += up(R * (size_t)((n_chunks + 31) & ~31) * 4);   // rows padded to 32 scores
+    w.sel32 = o;     o += up(R * (size_t)nk * 4);
     w.chunk_ids = o; o += up(R * (size_t)nk * 8);
     w.density = o;   o += up(R * (size_t)nk * 4);
     w.dense_pos = o; o += up(R * (size_t)n_dense * 8);
@@ -97,20 +98,30 @@ extern "C" int zkv_reference_select(const void* q, int G, const zkv_ref_layer* L
     int64_t* kix = reinterpret_cast<int64_t*>(ws + w.kidx);
     cudaStream_t st = (cudaStream_t)stream;
     int s;
-    // Stage 1: the GQA-mean query (recorded for stage 2) and the Quest upper
-    // bounds over the retrieval chunks in one launch; top-nk chunks
-    if (((uintptr_t)q & 15) == 0) {
-        if ((s = quest_score_gqa_into(q, G, L->chunk_min, L->chunk_max, L->valid, scores, raw_q, rows, n_chunks, n_max,
-                                      st)))
+    // Stage 1: the GQA-mean query (recorded for stage 2), the Quest upper
+    // bounds over the retrieval chunks and the top-nk chunks: the raw page
+    // decode's score and select kernels up to 16384 chunks, else the Quest
+    // launch with the GQA mean folded in and the float top-k
+    if (n_chunks <= 16384 && G <= 8 && ((uintptr_t)q & 3) == 0 && ((uintptr_t)L->chunk_min & 15) == 0 &&
+        ((uintptr_t)L->chunk_max & 15) == 0) {
+        if ((s = raw_quest_topk(q, G, L->chunk_min, L->chunk_max, L->valid, rows, n_max, n_chunks, nk, scores,
+                                (n_chunks + 31) & ~31, reinterpret_cast<int32_t*>(ws + w.sel32), ids, raw_q, st)))
             return s;
     } else {
-        if ((s = launch_pdl_kernel(gqa_mean_kernel, dim3((rows + 7) / 8), dim3(256), 0, st, (const uint16_t*)q, rows,
-                                   G, raw_q)))
-            return s;
-        if ((s = zkv_quest_score(raw_q, L->chunk_min, L->chunk_max, L->valid, scores, rows, n_chunks, n_max, stream)))
-            return s;
+        if (((uintptr_t)q & 15) == 0) {
+            if ((s = quest_score_gqa_into(q, G, L->chunk_min, L->chunk_max, L->valid, scores, raw_q, rows, n_chunks,
+                                          n_max, st)))
+                return s;
+        } else {
+            if ((s = launch_pdl_kernel(gqa_mean_kernel, dim3((rows + 7) / 8), dim3(256), 0, st, (const uint16_t*)q,
+                                       rows, G, raw_q)))
+                return s;
+            if ((s = zkv_quest_score(raw_q, L->chunk_min, L->chunk_max, L->valid, scores, rows, n_chunks, n_max,
+                                     stream)))
+                return s;
+        }
+        if ((s = zkv_topk_f32(scores, rows, n_chunks, n_chunks, nk, ids, stream))) return s;
     }
-    if ((s = zkv_topk_f32(scores, rows, n_chunks, n_chunks, nk, ids, stream))) return s;
     // Stage 2 (CDS): centroid density, top-n_dense -> dense mask, KIVI qk per chunk.  (A one-CTA-per-row
     // fusion of the first three measured slower: one row's density loads need the whole grid in flight.)
     if ((s = zkv_chunk_density(ids, L->centroid, raw_q, dens, rows, nk, n_chunks, n_max, stream))) return s;

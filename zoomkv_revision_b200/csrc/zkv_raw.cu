@@ -76,6 +76,7 @@ struct Args {
     const int32_t* group_ids;  // score kernel: warp j scores the small chunks of large chunk group_ids[r][j]
     const int32_t* map_ids;    // select kernel: position p -> map_ids[r][p / factor] * factor + p % factor
     int n_groups, factor, n_chunks_map;
+    uint16_t* raw_q_out;       // score kernel: the GQA-mean query, written by each row's first CTA (or NULL)
 };
 
 // 2-D tiled TMA load (no multicast): box (x .. x+63, y .. y+15) -> dst.
@@ -312,6 +313,7 @@ __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_consta
         float acc = 0.f;
         for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, bfbits2f(__ldg(qr + g * kHeadDim + d)));
         rq[d] = f2bfbits(__fdiv_rn(acc, (float)a.G));
+        if (a.raw_q_out && tile == 0) a.raw_q_out[(int64_t)r * kHeadDim + d] = rq[d];
     }
     __syncthreads();
     if (nch == 0) return;
@@ -1032,9 +1034,53 @@ static int decode_raw(const void* q, const zkv_raw_layer* layer, int rows, int G
 }
 
 }  // namespace rawpg
+
 }  // namespace zkv
 
 using namespace zkv;
+
+int raw_quest_topk(const void* q, int G, const void* cmin, const void* cmax, const uint8_t* valid, int rows,
+                   int n_max, int n_c, int nk, float* scores, int n_c_pad, int32_t* sel32, int64_t* ids,
+                   uint16_t* raw_q_out, cudaStream_t stream) {
+    using namespace rawpg;
+    if (!q || !cmin || !cmax || !scores || !sel32 || !ids || rows < 0 || G < 1 || G > 8 || n_c < 1 ||
+        n_c > n_max || n_c > kMaxChunks || nk < 1 || nk > n_c || n_c_pad < ((n_c + 31) & ~31))
+        return ZKV_ERR_ARG;
+    if (((uintptr_t)cmin & 15) || ((uintptr_t)cmax & 15) || ((uintptr_t)q & 3) || ((uintptr_t)scores & 15))
+        return ZKV_ERR_ALIGN;
+    if (rows == 0) return ZKV_OK;
+    Args a;
+    memset(&a, 0, sizeof(a));
+    a.q = (const uint16_t*)q;
+    a.cmin = (const uint16_t*)cmin;
+    a.cmax = (const uint16_t*)cmax;
+    a.valid = valid;
+    a.R = rows;
+    a.G = G;
+    a.n_max = n_max;
+    a.n_c = n_c;
+    a.nk = nk;
+    a.ST = (n_c + kScoreTile - 1) / kScoreTile;
+    a.n_c_pad = n_c_pad;
+    a.scores = scores;
+    a.sel = sel32;
+    a.sel_out = ids;
+    a.raw_q_out = raw_q_out;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ZKV_ERR_LAUNCH;
+    if (!attr_set[dev]) {
+        if (cudaFuncSetAttribute(raw_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem()) !=
+            cudaSuccess)
+            return ZKV_ERR_LAUNCH;
+        attr_set[dev] = true;
+    }
+    void* args[] = {&a};
+    int rc = launch_pdl((const void*)raw_score_kernel, rows * a.ST, kThreads, score_smem(), stream, args);
+    if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_select_kernel, rows, kSelThreads, select_smem(), stream, args);
+    return rc;
+}
+
 
 extern "C" size_t zkv_page_decode_raw_ws_bytes(int rows, int n_c, int nk, int n_sink, int n_near) {
     if (rows < 0 || n_c < 0 || nk < 0 || n_sink < 0 || n_near < 0) return 0;
