@@ -667,6 +667,211 @@ __device__ void block_topk_small(const float* sc, int n, int k, uint32_t lo, uin
     __syncthreads();
 }
 
+// ----------------------------------------------------------- spread select
+// Top k of one row of n fp32 scores in global memory (srow; validity bytes
+// vrow or NULL: invalid -> -inf), ties to the lowest index, emitted as
+// emit(position, index) in ascending index order, by a CTA of NT threads
+// holding E = 2, 4 or 8 keys each (n <= E * NT).  Every warp holds keys,
+// so each thread's dependent chains stay short: one kSelBins-bin histogram
+// over the row's [min finite, max] key range (a bucketing monotone in the
+// key) gives the bin of the k-th best; a warp ranks that bin's keys exactly
+// when it holds at most 32 (else the exact radix select runs over gkey(i));
+// an index-order scan of the kept flags emits the ids.
+constexpr int kSelBins = 2048;
+template <int NT>
+struct SelSharedT {
+    int hist[kSelBins];
+    int scan[2 * NT];  // fallback scratch
+    uint32_t wlo[32], whi[32], lohi[2];
+    int wsum[32], wcnt[32];
+    int misc[8];                // bin, count above it, its count, candidates, pivot key, pivot id
+    uint32_t cand_k[32];
+    int cand_i[32];
+};
+
+template <int NT, int E, typename Emit, typename GKey>
+__device__ __forceinline__ void select_spread(SelSharedT<NT>& S, int n, int k, const float* srow, const uint8_t* vrow,
+                                             Emit& emit, GKey& gkey) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = NT / 32;
+    const int base = tid * E;
+    uint32_t kr[E];
+    {
+        float f[E];
+        const bool vec = ((uintptr_t)srow & (E >= 4 ? 15 : 7)) == 0 && base + E <= n;
+        if (vec && E >= 4) {
+#pragma unroll
+            for (int u = 0; u < E / 4; ++u) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(srow + base) + u);
+                f[(4 * u) % E] = v.x;
+                f[(4 * u + 1) % E] = v.y;
+                f[(4 * u + 2) % E] = v.z;
+                f[(4 * u + 3) % E] = v.w;
+            }
+        } else if (vec) {
+            const float2 v = __ldcg(reinterpret_cast<const float2*>(srow + base));
+            f[0] = v.x;
+            f[1 % E] = v.y;
+        } else {
+#pragma unroll
+            for (int e = 0; e < E; ++e) f[e] = base + e < n ? __ldcg(srow + base + e) : 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const bool in = base + e < n;
+            const bool ok = !vrow || !in || vrow[base + e] != 0;
+            kr[e] = in ? (ok ? ordered_u32(f[e]) : kOrderedNegInf) : 0u;
+        }
+    }
+    uint32_t klo = 0xffffffffu, khi = 0u;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        if (base + e < n) {
+            if (kr[e] > kOrderedNegInf) klo = min(klo, kr[e]);
+            khi = max(khi, kr[e]);
+        }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        klo = min(klo, __shfl_xor_sync(0xffffffffu, klo, off));
+        khi = max(khi, __shfl_xor_sync(0xffffffffu, khi, off));
+    }
+    if (lane == 0) {
+        S.wlo[warp] = klo;
+        S.whi[warp] = khi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        klo = lane < NW ? S.wlo[lane] : 0xffffffffu;
+        khi = lane < NW ? S.whi[lane] : 0u;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            klo = min(klo, __shfl_xor_sync(0xffffffffu, klo, off));
+            khi = max(khi, __shfl_xor_sync(0xffffffffu, khi, off));
+        }
+        if (lane == 0) {
+            S.lohi[0] = klo;
+            S.lohi[1] = khi;
+        }
+    }
+    __syncthreads();
+    const uint32_t lo = S.lohi[0], hi = S.lohi[1];
+    // bucket: monotone in the key; -inf (and every key when hi <= lo) -> bin 0
+    const bool same_sign = ((lo ^ hi) & 0x80000000u) == 0u;
+    const uint32_t span = hi > lo ? hi - lo : 0u;
+    const int bits = span ? 32 - __clz(span) : 0;
+    const int sh = bits > 11 ? bits - 11 : 0;
+    const float flo = float_of_ordered(lo), fhi = float_of_ordered(hi);
+    const float inv = (hi > lo) ? (float)kSelBins / (fhi - flo) : 0.0f;
+    uint32_t bk[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const uint32_t kk = kr[e];
+        if (same_sign) {
+            bk[e] = kk >= lo ? min((kk - lo) >> sh, (uint32_t)(kSelBins - 1)) : 0u;
+        } else {
+            const float fb = fminf(fmaxf((float_of_ordered(kk) - flo) * inv, 0.0f), (float)(kSelBins - 1));
+            bk[e] = (uint32_t)fb;
+        }
+        if (base + e < n) atomicAdd(&S.hist[bk[e]], 1);
+    }
+    __syncthreads();
+    {   // suffix counts: thread t owns bins [PL t, PL t + PL)
+        constexpr int PL = kSelBins / NT;
+        int h[PL], suf[PL];
+        int tot = 0;
+#pragma unroll
+        for (int j = PL - 1; j >= 0; --j) {
+            h[j] = S.hist[PL * tid + j];
+            tot += h[j];
+            suf[j] = tot;
+        }
+        int incl = tot;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int v = __shfl_down_sync(0xffffffffu, incl, off);
+            if (lane + off < 32) incl += v;
+        }
+        if (lane == 0) S.wsum[warp] = incl;
+        __syncthreads();
+        int above = lane < NW && lane > warp ? S.wsum[lane] : 0;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) above += __shfl_xor_sync(0xffffffffu, above, off);
+        above += incl - tot;
+#pragma unroll
+        for (int j = 0; j < PL; ++j) {
+            const int ge = above + suf[j], gt = ge - h[j];
+            if (gt < k && ge >= k) {
+                S.misc[0] = PL * tid + j;
+                S.misc[1] = gt;
+                S.misc[2] = h[j];
+            }
+        }
+    }
+    __syncthreads();
+    const uint32_t bstar = (uint32_t)S.misc[0];
+    const int rem = k - S.misc[1], m = S.misc[2];
+    uint32_t tk = 0u;
+    int ti = 0x7fffffff;  // rem == m: the whole bin is kept
+    if (rem < m) {
+        if (m > 32) {  // heavy ties or a narrow range: the exact radix select over the same keys
+            __syncthreads();
+            block_topk<NT, true>(gkey, n, k, S.hist, S.misc, S.scan, emit);
+            return;
+        }
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            if (base + e < n && bk[e] == bstar) {
+                const int p = atomicAdd(&S.misc[3], 1);
+                S.cand_k[p] = kr[e];
+                S.cand_i[p] = base + e;
+            }
+        }
+        __syncthreads();
+        if (warp == 0) {  // exact rank of each candidate: key descending, id ascending
+            const uint32_t ck = lane < m ? S.cand_k[lane] : 0u;
+            const int ci = lane < m ? S.cand_i[lane] : 0x7fffffff;
+            int rank = 0;
+            for (int j = 0; j < m; ++j) {
+                const uint32_t kj = __shfl_sync(0xffffffffu, ck, j);
+                const int ij = __shfl_sync(0xffffffffu, ci, j);
+                rank += (kj > ck) || (kj == ck && ij < ci);
+            }
+            if (lane < m && rank == rem - 1) {
+                S.misc[4] = (int)ck;
+                S.misc[5] = ci;
+            }
+        }
+        __syncthreads();
+        tk = (uint32_t)S.misc[4];
+        ti = S.misc[5];
+    }
+    unsigned fl = 0u;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const bool keep = base + e < n &&
+                          (bk[e] > bstar || (bk[e] == bstar && (kr[e] > tk || (kr[e] == tk && base + e <= ti))));
+        fl |= (unsigned)keep << e;
+    }
+    const int cnt = __popc(fl);
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += v;
+    }
+    if (lane == 31) S.wcnt[warp] = incl;
+    __syncthreads();
+    int pos = lane < NW && lane < warp ? S.wcnt[lane] : 0;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) pos += __shfl_xor_sync(0xffffffffu, pos, off);
+    pos += incl - cnt;
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+        if ((fl >> e) & 1u) emit(pos++, base + e);
+}
+
+
 // ----------------------------------------------------------- Quest score
 // Half-warp per chunk: lane hl (0..15) loads dims [8hl, 8hl+8) of q, min and
 // max as one 16-byte vector each.  The reference kernel's operation order
