@@ -70,7 +70,10 @@ def oracle_raw(rc, q, nk, rows=None):
     (1, 2, 1, 500, 31, 3, 17),     # G = 1, odd sizes
     (3, 1, 2, 64, 8, 0, 0),        # pages only
     (1, 1, 4, 4096, 128, 0, 128),  # shared-memory select at its largest n_c
-    (1, 1, 4, 5001, 300, 64, 64),  # n_c > 4096: the radix select path over global scores
+    (1, 1, 4, 5001, 300, 64, 64),  # 4096 < n_c <= 8192: 8 keys per select thread
+    (1, 1, 4, 8192, 256, 0, 16),   # the 8-keys path at its largest n_c
+    (1, 1, 2, 8193, 256, 0, 16),   # n_c > 8192: the radix select over global scores
+    (1, 1, 4, 16384, 64, 0, 8),    # the largest n_c the entry accepts
     (8, 8, 4, 300, 24, 5, 37),     # 64 rows: a few attend CTAs per row
     (4, 8, 2, 200, 100, 0, 16),    # 32 rows, 13 entries per attend CTA
 ])
