@@ -603,6 +603,113 @@ def run_config3_raw(args):
     print(json.dumps(line), flush=True)
 
 
+def run_config3_split(args):
+    """Config 3 (Qwen3-4B shape, batch 1, 131072 context, budget 4096) in the
+    raw-row page mode on N GPUs: one rank per GPU, each holding 1/N of every
+    layer's pages (rank 0 also the near rows), through
+    zkv_page_decode_raw_split -- the score rows and the partials cross NVLink
+    as tagged-word peer stores inside the decode's own four kernels.  At
+    N = 1 the step is the single-GPU page_decode_raw.  The 36-layer step is
+    one CUDA graph per rank; ms is the max over ranks."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from zoomkv_revision_b200 import ops
+    from zoomkv_revision_b200 import seqsplit as S
+    from zoomkv_revision_b200 import workload as W
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:  # the process group carries the IPC handles, barriers and the max over ranks
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    layers, bs, H, ctx, budget = args.layers, 1, KV_HEADS, 131072, 4096
+    n_c, nk, n_near = (ctx - RESIDUAL) // PAGE, budget // PAGE, RESIDUAL
+    rows = bs * H
+    grp = S.RawSplitGroup(rows, G, n_c, world, rank, dev) if world > 1 else None
+    lays, qs = [], []
+    for l in range(layers):
+        rc = W.build_raw_cache(7000 + l, bs, H, n_c * PAGE, n_near, dev)   # the same data on every rank
+        if grp is not None:
+            lays.append(S.local_raw_layer(rc, grp.lo, grp.hi, rank))
+        else:
+            lays.append((rc.layer(), rc.near_start))
+        del rc
+        qs.append(W.synth_query(torch.Generator(device=dev).manual_seed(900 + l), bs, H * G, dev))
+    out = torch.empty(bs, 1, H * G, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    sel = torch.empty(rows, nk, dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def layer_loop():
+        for l in range(layers):
+            lay, ns = lays[l]
+            if grp is not None:
+                grp.decode(qs[l], lay, nk, n_near, near_start=ns, out=out, status=status)
+            else:
+                ops.page_decode_raw(qs[l], lay, n_c, nk, n_near, near_start=ns, out=out, status=status)
+
+    with torch.cuda.stream(stream):
+        layer_loop()  # every rank makes the same calls; allocates the workspace outside the capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        layer_loop()
+    with torch.cuda.stream(stream):
+        graph.replay()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        if world == 1:  # ranks would run different iteration counts of the waits
+            _soak(graph.replay, args.soak, stream)
+        ms = _timed(graph.replay, args.steps, args.warmup, stream, world)
+    # parity of the timed configuration: layer 0's selection and output
+    # against the single-GPU decode of the same layer on this GPU
+    rc0 = W.build_raw_cache(7000, bs, H, n_c * PAGE, n_near, dev)
+    ref_sel = torch.empty(rows, nk, dtype=torch.int64, device=dev)
+    ref = ops.page_decode_raw(qs[0], rc0.layer(), n_c, nk, n_near, near_start=rc0.near_start, sel_out=ref_sel)
+    lay, ns = lays[0]
+    if grp is not None:
+        got = grp.decode(qs[0], lay, nk, n_near, near_start=ns, sel_out=sel, status=status)
+    else:
+        got = ops.page_decode_raw(qs[0], lay, n_c, nk, n_near, near_start=ns, sel_out=sel, status=status)
+    torch.cuda.synchronize()
+    err = (got.float() - ref.float()).abs()
+    parity = {"sel_equal": bool(torch.equal(sel, ref_sel)), "max_abs": float(err.max()),
+              "mean_rel": float(err.mean() / ref.float().abs().mean())}
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device status {int(status.item())} (a peer wait expired)")
+    if not parity["sel_equal"] or parity["max_abs"] > 2e-2 or parity["mean_rel"] > 1e-2:
+        raise RuntimeError(f"split decode differs from the single-GPU decode: {parity}")
+    peak, kind = load_peaks()
+    per_layer = W.raw_algorithmic_bytes(rows, n_c, nk, n_near, G)
+    ach = layers * per_layer / (ms / 1e3) / 1e9
+    line = {"metric": "config3 sparse decode tokens/s at Qwen3-4B shape, 131072 ctx, raw-row page mode "
+                      "(sequence split)",
+            "value": bs / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config3: 36 layers, bs 1, 8 KV / 32 q heads, 131072 ctx, budget 4096, "
+                                   "residual 128, page mode over raw rows", "layers": layers,
+                       "parallelism": (f"sequence split x{world}: score rows and partials as tagged-word peer "
+                                       "stores over NVLink inside the decode kernels, CUDA graph") if world > 1 else
+                                      "single GPU, CUDA graph",
+                       "l2": "inputs ~1.8 GB per step (36 distinct layers) > L2"},
+            "gpu_launches": layers * args.steps * 4,
+            "roofline": {"bound": "hbm", "achieved_per_gpu": ach / world, "peak": peak, "unit": "GB/s",
+                         "frac_per_gpu": ach / world / peak, "peak_kind": kind, "bytes_per_layer": per_layer},
+            "parity_layer0": parity,
+            "clocks": clk.summary()}
+    del graph
+    if grp is not None:
+        grp.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_config3(args):
     """Qwen3-4B-shape decode step at 131072 context (36 layers, batch 1)."""
     import datetime
@@ -872,9 +979,10 @@ def main():
     ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4, 5],
                     help="5: the offload tier (retrieval zone in host-pinned memory)")
     ap.add_argument("--mode", default="raw", choices=["raw", "page4", "reference"],
-                    help="config 1 only: raw = page mode over the selected pages' raw bf16 rows (the headline, the "
-                         "reference's page mode); page4 = page mode over 4-bit KIVI K/V pages (lossy variant); "
-                         "reference = the drop-in's default reference mode with production knobs")
+                    help="configs 1 and 3: raw = page mode over the selected pages' raw bf16 rows (the headline, "
+                         "the reference's page mode; config 3 on N GPUs: the raw sequence split); page4 = page "
+                         "mode over 4-bit KIVI K/V pages (lossy variant; config 3: its sequence split); "
+                         "reference = config 1 in the drop-in's default reference mode with production knobs")
     ap.add_argument("--gen", type=int, default=8192, help="config 4: tokens generated per sequence")
     ap.add_argument("--raw3", action="store_true",
                     help="config 3 on one GPU in the raw-row page mode: flat against hierarchical Quest")
@@ -892,6 +1000,8 @@ def main():
     if args.config == 3 and args.impl == "ours":
         if args.mode == "raw" and int(os.environ.get("WORLD_SIZE", "1")) == 1 and args.raw3:
             run_config3_raw(args)
+        elif args.mode == "raw":
+            run_config3_split(args)
         else:
             run_config3(args)
         return

@@ -374,6 +374,48 @@ int zkv_page_decode_raw_hier(const void* q, const zkv_raw_layer* layer, const zk
                              int near_start, int n_near, float scale, void* out, float* lse, int64_t* sel_out,
                              int32_t* status, void* workspace, size_t ws_bytes, void* stream);
 
+/* Sequence split of zkv_page_decode_raw over `world` ranks, one process per
+ * GPU (the benchmark's config 3; the reference has no multi-GPU form of
+ * compute(), whose single-device steps this splits).  Rank q holds the
+ * pages [q per, min(n_c, q per + per)) of every row, per = ceil(n_c / world)
+ * rounded up to 16 (zkv_raw_split_range), as its local pages 0, 1, ...;
+ * rank 0 also holds the sink and near rows.  Each rank owns one exchange
+ * buffer of zkv_raw_split_buffer_bytes, allocated zeroed with
+ * zkv_peer_alloc and mapped into every other rank with zkv_peer_open.   */
+typedef struct zkv_raw_split {
+    void* const* peer_base;  /* [world] every rank's exchange buffer as
+                                mapped in this process ([rank]: its own) */
+    int rank, world;         /* world <= 8                               */
+} zkv_raw_split;
+
+int zkv_raw_split_range(int n_c, int world, int rank, int* lo, int* hi);
+size_t zkv_raw_split_buffer_bytes(int rows, int G, int n_c, int world);
+size_t zkv_page_decode_raw_split_ws_bytes(int rows, int n_c, int world, int rank, int nk, int n_sink,
+                                          int n_near);
+
+/* One rank's share of a layer: Quest scores of its pages, stored straight
+ * into every rank's score row (peer stores over NVLink of 64-bit words
+ * {score, epoch of the call}) -> on every rank the top nk of the whole row
+ * (a bounded wait until every word carries the call's epoch, then the
+ * select of zkv_page_decode_raw: the same ids, ascending, on every rank) ->
+ * attention over the selected pages this rank holds (+ sink / near on rank
+ * 0) -> each (row, head)'s partial stored into every rank as tagged words,
+ * a bounded wait, and the world partials combined in rank order: out /
+ * lse, identical on every rank.  Four launches chained by programmatic
+ * dependent launch; no fence, flag, collective library or multicast.
+ * `layer` holds this rank's pages (chunk_min / chunk_max / valid
+ * [rows][n_max >= own pages], page j's rows at token page_base + 16 j);
+ * n_c / nk count the whole row's pages; 1 <= nk < n_c <= 16384, every rank
+ * holds a page.  sel_out [rows][nk]: the whole selection (global ids).
+ * Every rank makes the same sequence of calls with a buffer; a wait that
+ * expires (zkv_peer_set_wait_ms) sets ZKV_ERR_TIMEOUT in `status`, after
+ * which the group's buffers must be re-created.  Workspace as
+ * zkv_page_decode_raw (its own size).                                    */
+int zkv_page_decode_raw_split(const void* q, const zkv_raw_layer* layer, const zkv_raw_split* split, int rows,
+                              int G, int n_max, int n_c, int nk, int n_sink, int near_start, int n_near,
+                              float scale, void* out, float* lse, int64_t* sel_out, int32_t* status,
+                              void* workspace, size_t ws_bytes, void* stream);
+
 /* Decode-loop caller kernels (the benchmark's config 4; no reference
  * counterpart of their own: the reference's model code calls flashinfer's
  * rmsnorm / apply_rope_with_cos_sin_cache_inplace / silu_and_mul for these

@@ -43,7 +43,9 @@ def test_every_declared_symbol_is_exported_and_bound():
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
 def test_struct_layouts_match_c(tmp_path):
     structs = {"zkv_page_layer": _lib.ZkvPageLayer, "zkv_rq_layout": _lib.ZkvRqLayout,
-               "zkv_ref_layer": _lib.ZkvRefLayer, "zkv_peer_seg": _lib.ZkvPeerSeg}
+               "zkv_ref_layer": _lib.ZkvRefLayer, "zkv_peer_seg": _lib.ZkvPeerSeg,
+               "zkv_raw_layer": _lib.ZkvRawLayer, "zkv_quest_large": _lib.ZkvQuestLarge,
+               "zkv_raw_split": _lib.ZkvRawSplit}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void){"]
     for cname, cls in structs.items():
         lines.append(f'printf("%zu\\n", sizeof({cname}));')

@@ -40,6 +40,11 @@ class ZkvRawLayer(ctypes.Structure):
     ]
 
 
+class ZkvRawSplit(ctypes.Structure):
+    """Mirror of `zkv_raw_split` (include/zkv.h)."""
+    _fields_ = [("peer_base", ctypes.POINTER(_c_void_p)), ("rank", _i32), ("world", _i32)]
+
+
 class ZkvQuestLarge(ctypes.Structure):
     """Mirror of `zkv_quest_large` (include/zkv.h)."""
     _fields_ = [("large_min", _c_void_p), ("large_max", _c_void_p), ("large_valid", _c_void_p),
@@ -122,6 +127,12 @@ _SIGNATURES = {
     "zkv_page_decode_raw_hier": [_c_void_p, ctypes.POINTER(ZkvRawLayer), ctypes.POINTER(ZkvQuestLarge)] +
                                 [_i32] * 10 + [ctypes.c_float, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                                ctypes.c_size_t, _c_void_p],
+    "zkv_raw_split_range": [_i32, _i32, _i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32)],
+    "zkv_raw_split_buffer_bytes": [_i32] * 4,
+    "zkv_page_decode_raw_split_ws_bytes": [_i32] * 7,
+    "zkv_page_decode_raw_split": [_c_void_p, ctypes.POINTER(ZkvRawLayer), ctypes.POINTER(ZkvRawSplit)] +
+                                 [_i32] * 8 + [ctypes.c_float, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                               _c_void_p, ctypes.c_size_t, _c_void_p],
     "zkv_lse_merge": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p],
     "zkv_lse_merge_n": [_c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p],
     "zkv_rq_encode": [_c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _RQ, _c_void_p],
@@ -146,7 +157,8 @@ _SIGNATURES = {
 
 _RESTYPES = {"zkv_status_string": ctypes.c_char_p, "zkv_reference_select_ws_bytes": ctypes.c_size_t,
              "zkv_page_decode_split_ws_bytes": ctypes.c_size_t, "zkv_page_decode_raw_ws_bytes": ctypes.c_size_t,
-             "zkv_page_decode_raw_hier_ws_bytes": ctypes.c_size_t}
+             "zkv_page_decode_raw_hier_ws_bytes": ctypes.c_size_t, "zkv_raw_split_buffer_bytes": ctypes.c_size_t,
+             "zkv_page_decode_raw_split_ws_bytes": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib = None

@@ -129,6 +129,44 @@ __device__ __forceinline__ void set_status(int32_t* status, int code) {
     if (status) atomicExch(status, code);
 }
 
+// ------------------------------------------------------------ tagged words
+// A 32-bit value in the low half and the epoch of the call that wrote it in
+// the high half, stored and loaded as one naturally aligned 64-bit access
+// (single-copy atomic), so a reader that sees the epoch it waits for also
+// sees that call's value: no fence and no separate flag between a producer
+// (this GPU or a peer over NVLink) and its readers.
+__device__ __forceinline__ uint64_t tagged(uint32_t value, uint32_t tag) {
+    return ((uint64_t)tag << 32) | value;
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ bool tag_reached(uint64_t w, uint32_t tag) {
+    return (int32_t)((uint32_t)(w >> 32) - tag) >= 0;
+}
+// Re-read the tagged word at p (already loaded once as w) until its epoch
+// reaches `tag` or `wait_ns` of the global timer pass; ok becomes false on
+// expiry, and a caller whose ok is already false does not wait again.
+__device__ __forceinline__ uint64_t wait_tagged(const uint64_t* p, uint64_t w, uint32_t tag, uint64_t wait_ns,
+                                               bool& ok) {
+    if (tag_reached(w, tag) || !ok) return w;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        __nanosleep(32);
+        w = ld_relaxed_sys_u64(p);
+        if (tag_reached(w, tag)) return w;
+        if (globaltimer_ns() - t0 > wait_ns) {
+            ok = false;
+            return w;
+        }
+    }
+}
+
 // ------------------------------------------------------------ mbarrier / TMA bulk
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -941,6 +979,9 @@ int topk_mask_launch(const float* dens, int rows, int nk, int n_dense, uint8_t* 
 int raw_quest_topk(const void* q, int G, const void* cmin, const void* cmax, const uint8_t* valid, int rows,
                    int n_max, int n_c, int nk, float* scores, int n_c_pad, int32_t* sel32, int64_t* ids,
                    uint16_t* raw_q_out, cudaStream_t stream);
+// Time limit (ns) of the waits on peers for launches enqueued now
+// (zkv_peer_set_wait_ms; 5 s by default).
+uint64_t peer_wait_ns();
 
 // Launch `nblocks` CTAs of `nthreads` in clusters of CS (cudaLaunchKernelExC),
 // raising the kernel's dynamic shared-memory limit once per (kernel, device).

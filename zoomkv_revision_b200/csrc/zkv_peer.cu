@@ -172,6 +172,8 @@ __global__ void peer_wait_kernel(const uint32_t* flags, uint32_t* epoch, int wor
 
 using namespace zkv;
 
+uint64_t peer_wait_ns() { return g_wait_ns.load(); }
+
 extern "C" int zkv_peer_alloc(size_t bytes, void** ptr, void* handle) {
     if (!ptr || !handle || bytes == 0) return ZKV_ERR_ARG;
     void* p = nullptr;

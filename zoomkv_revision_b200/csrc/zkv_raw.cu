@@ -53,6 +53,8 @@ constexpr int kPartFloats = 16 + 8 * kHeadDim;    // m[8], l[8], o[8][128]
 constexpr int kSelThreads = 1024;                 // threads of a select CTA
 constexpr int kMaxChunks = 16384;
 constexpr int kMaxTiles = 2048;                   // attend tiles per row
+constexpr int kMaxRanks = 8;                      // sequence split: ranks of a group
+constexpr int kXPart = 130;                       // exchanged partial of a (row, head): o[128], m, l (tagged)
 
 struct Args {
     CUtensorMap tk;  // raw keys   as [rows * cap][128] bf16, box 64 x 16, 128-B swizzle
@@ -77,6 +79,16 @@ struct Args {
     const int32_t* map_ids;    // select kernel: position p -> map_ids[r][p / factor] * factor + p % factor
     int n_groups, factor, n_chunks_map;
     uint16_t* raw_q_out;       // score kernel: the GQA-mean query, written by each row's first CTA (or NULL)
+    // sequence split (the kSplit instantiations): this rank holds the global
+    // pages [chunk_lo, chunk_hi) of the row as its local pages 0, 1, ...; the
+    // score row and the selection use global page ids
+    int rank, world, chunk_lo, chunk_hi, n_total;  // n_total: pages of the whole row (the select's n)
+    uint64_t* xrow[kMaxRanks];     // every rank's tagged score row [R][n_c_pad] (as mapped in this process)
+    uint64_t* xpart[kMaxRanks];    // every rank's tagged partials [world][R * G][kXPart]
+    uint32_t* ep_s;                // own: [R] calls whose score row was complete
+    uint32_t* ep_m;                // own: [R * G] calls whose partials were complete
+    int32_t* own_range;            // workspace [R][2]: selection positions [a, b) of the own pages
+    uint64_t wait_ns;              // limit of each wait on a peer's words
 };
 
 // 2-D tiled TMA load (no multicast): box (x .. x+63, y .. y+15) -> dst.
@@ -269,9 +281,46 @@ __device__ __forceinline__ int64_t entry_tokens(const Args& a, int e, int chunk,
 }
 
 // ---------------------------------------------------------------- kernel 1: scores
+// Sequence-split tail of the score kernel (after the min/max copies and the
+// GQA mean): the warp scores its nch chunks (invalid ones -> -inf, the key
+// the select gives an invalid chunk, so the select needs no validity) and
+// stores each score into every rank's score row at its global id as a
+// tagged word {score, this call's epoch} (over NVLink for the peers).  No
+// fence or flag: the reader checks each word's epoch.
+__device__ __forceinline__ void split_scores(const Args& a, int r, int cc, int nch, const uint8_t* slot,
+                                             uint64_t* bar, const uint16_t* rq, float* sb) {
+    const int lane = threadIdx.x & 31;
+    if (nch <= 0) return;
+    const uint32_t tag = __ldcg(a.ep_s + r) + 1u;
+    const bool ok = mbar_wait(bar, 0, a.status);
+    const int hl = lane & 15, half = lane >> 4;
+    const uint4 qv = *reinterpret_cast<const uint4*>(rq + 8 * hl);
+    const uint8_t* vrow = a.valid ? a.valid + (int64_t)r * a.n_max + cc : nullptr;
+#pragma unroll 4
+    for (int u = 0; u < 8; ++u) {
+        const int lc = 2 * u + half;
+        uint4 mn = make_uint4(0, 0, 0, 0), mx = mn;
+        if (ok && lc < nch) {
+            mn = *reinterpret_cast<const uint4*>(slot + lc * 256 + 16 * hl);
+            mx = *reinterpret_cast<const uint4*>(slot + 4096 + lc * 256 + 16 * hl);
+        }
+        const float sc = quest_half(qv, mn, mx);
+        if (hl == 0 && lc < nch) sb[lc] = (ok && (!vrow || vrow[lc])) ? sc : -INFINITY;
+    }
+    __syncwarp();
+    for (int i = lane; i < 16 * a.world; i += 32) {  // lane i: chunk i % 16 to rank i / 16
+        const int q = i >> 4, c = i & 15;
+        if (c < nch)
+            st_relaxed_sys_u64(a.xrow[q] + (int64_t)r * a.n_c_pad + a.chunk_lo + cc + c,
+                               tagged(__float_as_uint(sb[c]), tag));
+    }
+}
+
 // One CTA per (row, 64 chunks): each warp bulk-copies its 16 chunks' min and
 // max (8 KiB) into shared memory and scores them; the scores go to the
-// workspace.  Validity is applied by the select.
+// workspace (kSplit: to every rank's score row, split_scores).  Validity is
+// applied by the select (kSplit: here).
+template <bool kSplit>
 __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_constant__ Args a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* region = smem;                                   // [4 warps][8 KiB]: min 4 KiB, max 4 KiB
@@ -316,6 +365,10 @@ __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_consta
         if (a.raw_q_out && tile == 0) a.raw_q_out[(int64_t)r * kHeadDim + d] = rq[d];
     }
     __syncthreads();
+    if constexpr (kSplit) {
+        split_scores(a, r, cc, nch, slot, bars + warp, rq, reinterpret_cast<float*>(bars + kWarps) + 16 * warp);
+        return;
+    }
     if (nch == 0) return;
     float* srow0 = a.scores + (int64_t)r * a.n_c_pad;
     if (oob) {
@@ -346,16 +399,66 @@ __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_consta
 // over global scores beyond).
 using SelShared = SelSharedT<kSelThreads>;
 
+// kSplit: the row is the whole tagged score row in this rank's exchange
+// buffer; every thread waits (bounded) until its words carry this call's
+// epoch and copies the scores into the workspace row, which the select then
+// reads as on one GPU.  The split select does not wait for the score grid
+// to complete (that completion includes the flush of the score kernel's
+// stores to the peers, about 3 us): it waits on the words themselves, this
+// rank's included.  It cannot wait on a producer that is not running: with
+// programmatic dependent launch this grid starts only after every score
+// CTA has executed its launch_dependents, i.e. every score CTA is resident
+// and none of them waits on this grid.  Nothing earlier needs ordering
+// here: those score CTAs passed their own dependency wait (the previous
+// call's merge, hence its attend, had completed) before the trigger.  The
+// CTA also records which selection positions are the pages this rank holds
+// (ids ascend, so they are one run [a, b)).
+template <bool kSplit>
 __global__ void __launch_bounds__(kSelThreads) raw_select_kernel(const __grid_constant__ Args a) {
     __shared__ SelShared S;
+    __shared__ int sx[4];  // kSplit: selected ids below the own range, inside it; a wait expired
     const int r = blockIdx.x, tid = threadIdx.x;
     for (int i = tid; i < kSelBins; i += kSelThreads) S.hist[i] = 0;
     if (tid == 0) S.misc[3] = 0;
-    grid_dep_wait();          // the scores of the score kernel
+    if (kSplit && tid < 4) sx[tid] = 0;
+    if constexpr (!kSplit) grid_dep_wait();  // the scores of the score kernel
     grid_dep_launch_next();   // the attend kernel may become resident (it waits for this grid)
-    const int n = a.n_c, k = a.nk;
+    if constexpr (kSplit) {
+        const uint32_t target = __ldcg(a.ep_s + r) + 1u;
+        const uint64_t* xr = a.xrow[a.rank] + (int64_t)r * a.n_c_pad;
+        float* plain = a.scores + (int64_t)r * a.n_c_pad;
+        bool ok = true;
+        for (int i0 = 0; i0 < a.n_total; i0 += 8 * kSelThreads) {  // 8 words of a thread in flight at once
+            uint64_t w[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + j * kSelThreads + tid;
+                w[j] = i < a.n_total ? ld_relaxed_sys_u64(xr + i) : 0ull;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + j * kSelThreads + tid;
+                if (i < a.n_total)
+                    plain[i] = __uint_as_float((uint32_t)wait_tagged(xr + i, w[j], target, a.wait_ns, ok));
+            }
+        }
+        if (!ok) {
+            set_status(a.status, ZKV_ERR_TIMEOUT);
+            sx[2] = 1;
+        }
+        __syncthreads();  // every word read (the epoch below) and the workspace row written
+        if (tid == 0) a.ep_s[r] = target;
+        if (sx[2]) {  // no pages of this row are attended
+            if (tid == 0) {
+                a.own_range[2 * r] = 0;
+                a.own_range[2 * r + 1] = 0;
+            }
+            return;
+        }
+    }
+    const int n = kSplit ? a.n_total : a.n_c, k = a.nk;
     const float* srow = a.scores + (int64_t)r * a.n_c_pad;
-    const uint8_t* vrow = a.valid ? a.valid + (int64_t)r * a.n_max : nullptr;
+    const uint8_t* vrow = (!kSplit && a.valid) ? a.valid + (int64_t)r * a.n_max : nullptr;
     int32_t* selr = a.sel + (int64_t)r * a.nk;
     int64_t* selo = a.sel_out ? a.sel_out + (int64_t)r * a.nk : nullptr;
     auto emit = [&](int pos, int i) {
@@ -366,6 +469,12 @@ __global__ void __launch_bounds__(kSelThreads) raw_select_kernel(const __grid_co
         }
         selr[pos] = i;
         if (selo) selo[pos] = i;
+        if constexpr (kSplit) {
+            if (i < a.chunk_lo)
+                atomicAdd(&sx[0], 1);
+            else if (i < a.chunk_hi)
+                atomicAdd(&sx[1], 1);
+        }
     };
     auto gkey = [&](int i) { return (vrow && !vrow[i]) ? kOrderedNegInf : ordered_u32(__ldcg(srow + i)); };
     if (n <= 2 * kSelThreads) {
@@ -378,13 +487,24 @@ __global__ void __launch_bounds__(kSelThreads) raw_select_kernel(const __grid_co
         __syncthreads();
         block_topk<kSelThreads, true>(gkey, n, k, S.hist, S.misc, S.scan, emit);
     }
+    if constexpr (kSplit) {
+        __syncthreads();
+        if (tid == 0) {
+            a.own_range[2 * r] = sx[0];
+            a.own_range[2 * r + 1] = sx[0] + sx[1];
+        }
+    }
 }
 
 // ---------------------------------------------------------------- kernel 3: attend
 // One CTA per (row, EPC entries of 16 tokens), sized so that the grid is one
 // wave; warp w attends entries e0 + w, e0 + w + 4, ... through two TMA slots
 // (the next page's copy is issued as soon as a slot's page is consumed) and
-// the CTA writes one partial (m, l, o) of the row.
+// the CTA writes one partial (m, l, o) of the row.  kSplit: the row's
+// entries are this rank's raw rows (rank 0: sink and near) and the selected
+// pages this rank holds, spread over the row's CTAs once the selection is
+// known (no copies are issued before it).
+template <bool kSplit>
 __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_constant__ Args a) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t base_u32 = smem_u32(smem_raw);
@@ -399,9 +519,9 @@ __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_co
         mbar_fence_init();
     }
     __syncthreads();
-    const int e0 = tile * a.EPC;
-    const int e1 = min(a.E, e0 + a.EPC);
-    const int nw = e1 - e0 > warp ? (e1 - e0 - warp + kWarps - 1) / kWarps : 0;  // pages of this warp (<= 32)
+    int e0 = tile * a.EPC;
+    int e1 = min(a.E, e0 + a.EPC);
+    int nw = e1 - e0 > warp ? (e1 - e0 - warp + kWarps - 1) / kWarps : 0;  // pages of this warp (<= 32)
     const int pg0 = a.RS + a.RN;
     const uint32_t slot0 = smem_u32(region) + (uint32_t)(warp * kSlots * kSlotBytes);
     auto issue_chunk = [&](int j, int chunk) -> unsigned {  // warp-uniform; returns the page's present mask
@@ -422,22 +542,35 @@ __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_co
     // Sink and near pages do not depend on the selection, and the K/V rows
     // and q were written before the score kernel began: their copies and the
     // query fragments are taken before waiting for the select kernel.
-    const bool pre0 = nw > 0 && e0 + warp < pg0;
-    const bool pre1 = nw > 1 && e0 + warp + kWarps < pg0;
+    const bool pre0 = !kSplit && nw > 0 && e0 + warp < pg0;
+    const bool pre1 = !kSplit && nw > 1 && e0 + warp + kWarps < pg0;
     unsigned pres0 = pre0 ? issue_chunk(0, 0) : 0u;
     unsigned pres1 = pre1 ? issue_chunk(1, 0) : 0u;
     WarpState st;
     state_init(st, a.q + (int64_t)r * a.G * kHeadDim, a.G);
     grid_dep_wait();          // the selection of the select kernel
     grid_dep_launch_next();   // the merge kernel may become resident (it waits for this grid)
+    int sel_a = 0;
+    if constexpr (kSplit) {  // own pages: selection positions [sel_a, b); entries spread over the AT CTAs
+        sel_a = __ldcg(a.own_range + 2 * r);
+        const int ed = pg0 + __ldcg(a.own_range + 2 * r + 1) - sel_a;
+        const int epc = (ed + a.AT - 1) / a.AT;
+        e0 = tile * epc;
+        e1 = min(ed, e0 + epc);
+        nw = e1 - e0 > warp ? (e1 - e0 - warp + kWarps - 1) / kWarps : 0;
+    }
     // lane j reads the chunk id of the warp's j-th entry (all in flight at once)
     int my_chunk = 0;
     if (lane < nw) {
         const int e = e0 + warp + kWarps * lane;
         if (e >= pg0) {
             const int p = e - pg0;
-            my_chunk = a.ST > 0 ? __ldcg(a.sel + (int64_t)r * a.nk + p) : p;
-            if (a.ST == 0 && a.sel_out) a.sel_out[(int64_t)r * a.nk + p] = p;  // identity selection
+            if constexpr (kSplit) {
+                my_chunk = __ldcg(a.sel + (int64_t)r * a.nk + sel_a + p) - a.chunk_lo;  // a local page
+            } else {
+                my_chunk = a.ST > 0 ? __ldcg(a.sel + (int64_t)r * a.nk + p) : p;
+                if (a.ST == 0 && a.sel_out) a.sel_out[(int64_t)r * a.nk + p] = p;  // identity selection
+            }
         }
     }
     auto issue = [&](int j) -> unsigned {
@@ -486,6 +619,67 @@ __global__ void __launch_bounds__(kThreads, 3) raw_attend_kernel(const __grid_co
 // kMergeBatch with every load of a batch in flight at once; batches combine
 // with an online rescale (one batch when AT <= kMergeBatch).
 constexpr int kMergeBatch = 32;
+
+// Sequence-split tail of the merge: this rank's (M, L, O) of (row r, head h)
+// (M in log2 units, L and O not normalised) goes to slot `rank` of every
+// rank's exchange buffer as tagged words {value, this call's epoch}; every
+// thread then waits (bounded) for its dim's word and the (M, L) words of
+// every rank in its own buffer and combines the world partials in rank
+// order, so every rank writes the same out / lse.  No fence or flag.
+__device__ __forceinline__ void split_combine(const Args& a, int r, int h, int d, float M, float L, float O) {
+    const int64_t rg = (int64_t)a.R * a.G, rh = (int64_t)r * a.G + h;
+    const uint32_t tag = __ldcg(a.ep_m + rh) + 1u;
+    for (int q = 0; q < a.world; ++q) {
+        uint64_t* dst = a.xpart[q] + ((int64_t)a.rank * rg + rh) * kXPart;
+        st_relaxed_sys_u64(dst + d, tagged(__float_as_uint(O), tag));
+        if (d == 0) {
+            st_relaxed_sys_u64(dst + kHeadDim, tagged(__float_as_uint(M), tag));
+            st_relaxed_sys_u64(dst + kHeadDim + 1, tagged(__float_as_uint(L), tag));
+        }
+    }
+    const uint64_t* src = a.xpart[a.rank] + rh * kXPart;
+    float mq[kMaxRanks], lq[kMaxRanks], oq[kMaxRanks];
+    uint64_t wm[kMaxRanks], wl[kMaxRanks], wo[kMaxRanks];
+#pragma unroll
+    for (int q = 0; q < kMaxRanks; ++q) {  // every load in flight before any wait
+        if (q < a.world) {
+            const uint64_t* pq = src + q * rg * kXPart;
+            wo[q] = ld_relaxed_sys_u64(pq + d);
+            wm[q] = ld_relaxed_sys_u64(pq + kHeadDim);
+            wl[q] = ld_relaxed_sys_u64(pq + kHeadDim + 1);
+        }
+    }
+    bool ok = true;
+    float Ms = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kMaxRanks; ++q) {
+        if (q < a.world) {
+            const uint64_t* pq = src + q * rg * kXPart;
+            oq[q] = __uint_as_float((uint32_t)wait_tagged(pq + d, wo[q], tag, a.wait_ns, ok));
+            mq[q] = __uint_as_float((uint32_t)wait_tagged(pq + kHeadDim, wm[q], tag, a.wait_ns, ok));
+            lq[q] = __uint_as_float((uint32_t)wait_tagged(pq + kHeadDim + 1, wl[q], tag, a.wait_ns, ok));
+            Ms = fmaxf(Ms, mq[q]);
+        }
+    }
+    if (!ok) set_status(a.status, ZKV_ERR_TIMEOUT);
+    float Ls = 0.f, Os = 0.f;
+    if (Ms != -INFINITY) {
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q) {
+            if (q < a.world) {
+                const float wt = (mq[q] == -INFINITY) ? 0.f : ex2(mq[q] - Ms);
+                Ls += wt * lq[q];
+                Os += wt * oq[q];
+            }
+        }
+    }
+    if (d == 0 && a.lse) a.lse[rh] = (Ls > 0.f) ? (Ms + __log2f(Ls)) * 0.69314718055994531f : -INFINITY;
+    a.out[rh * kHeadDim + d] = f2bfbits(Ls > 0.f ? Os * (1.f / Ls) : 0.f);
+    __syncthreads();  // every thread read the epoch above
+    if (d == 0) a.ep_m[rh] = tag;
+}
+
+template <bool kSplit>
 __global__ void __launch_bounds__(kHeadDim) raw_merge_kernel(const __grid_constant__ Args a) {
     const int r = blockIdx.x / a.G, h = blockIdx.x % a.G, d = threadIdx.x;
     grid_dep_wait();          // the partials of the attend kernel
@@ -516,6 +710,10 @@ __global__ void __launch_bounds__(kHeadDim) raw_merge_kernel(const __grid_consta
             O += wt * o[u];
         }
         M = Mb;
+    }
+    if constexpr (kSplit) {
+        split_combine(a, r, h, d, M, L, O);
+        return;
     }
     if (d == 0 && a.lse) a.lse[(int64_t)r * a.G + h] = (L > 0.f) ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
     a.out[((int64_t)r * a.G + h) * kHeadDim + d] = f2bfbits(L > 0.f ? O * (1.f / L) : 0.f);
@@ -815,11 +1013,11 @@ static int decode_raw(const void* q, const zkv_raw_layer* layer, int rows, int G
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ZKV_ERR_LAUNCH;
     if (!attr_set[dev]) {
-        if (cudaFuncSetAttribute(raw_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem()) !=
-                cudaSuccess ||
-            cudaFuncSetAttribute(raw_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(raw_score_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)score_smem()) != cudaSuccess ||
+            cudaFuncSetAttribute(raw_select_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)select_smem()) != cudaSuccess ||
-            cudaFuncSetAttribute(raw_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            cudaFuncSetAttribute(raw_attend_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)attend_smem()) != cudaSuccess)
             return ZKV_ERR_LAUNCH;
         attr_set[dev] = true;
@@ -829,16 +1027,184 @@ static int decode_raw(const void* q, const zkv_raw_layer* layer, int rows, int G
     const cudaStream_t st = (cudaStream_t)stream;
     int rc = ZKV_OK;
     if (hier) {
-        rc = launch_pdl((const void*)raw_score_kernel, rows * p.ST1, kThreads, score_smem(), st, args1);
-        if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_select_kernel, rows, kSelThreads, select_smem(), st, args1);
+        rc = launch_pdl((const void*)raw_score_kernel<false>, rows * p.ST1, kThreads, score_smem(), st, args1);
+        if (rc == ZKV_OK)
+            rc = launch_pdl((const void*)raw_select_kernel<false>, rows, kSelThreads, select_smem(), st, args1);
         if (rc != ZKV_OK) return rc;
     }
     if (p.ST > 0) {
-        rc = launch_pdl((const void*)raw_score_kernel, rows * p.ST, kThreads, score_smem(), st, args);
-        if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_select_kernel, rows, kSelThreads, select_smem(), st, args);
+        rc = launch_pdl((const void*)raw_score_kernel<false>, rows * p.ST, kThreads, score_smem(), st, args);
+        if (rc == ZKV_OK)
+            rc = launch_pdl((const void*)raw_select_kernel<false>, rows, kSelThreads, select_smem(), st, args);
     }
-    if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_attend_kernel, rows * p.AT, kThreads, attend_smem(), st, args);
-    if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_merge_kernel, rows * G, kHeadDim, 0, st, args);
+    if (rc == ZKV_OK)
+        rc = launch_pdl((const void*)raw_attend_kernel<false>, rows * p.AT, kThreads, attend_smem(), st, args);
+    if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_merge_kernel<false>, rows * G, kHeadDim, 0, st, args);
+    return rc;
+}
+
+// ---------------------------------------------------------------- sequence split
+// Pages of a row over `world` ranks: rank q holds [q per, min(n_c, q per + per)),
+// per = ceil(n_c / world) rounded up to 16 pages.
+static void split_range(int n_c, int world, int rank, int* lo, int* hi) {
+    int per = (n_c + world - 1) / world;
+    per = (per + 15) & ~15;
+    *lo = (int)std::min<int64_t>(n_c, (int64_t)rank * per);
+    *hi = std::min(n_c, *lo + per);
+}
+
+// The exchange buffer of a split group, the same layout on every rank: the
+// epochs of the two exchanges [R] and [R * G] (uint32, this rank's own
+// count of completed calls), the tagged score row [R][n_c_pad] and the
+// tagged partials [world][R * G][kXPart] (64-bit words {value, epoch}).
+struct XLayout {
+    size_t ep_s, ep_m, row, part, bytes;
+    int n_c_pad;
+};
+
+static XLayout x_layout(int R, int G, int n_c, int world) {
+    XLayout x;
+    size_t o = 0;
+    const size_t rg = (size_t)R * G;
+    x.n_c_pad = (n_c + 31) & ~31;
+    x.ep_s = o; o += up256((size_t)R * 4);
+    x.ep_m = o; o += up256(rg * 4);
+    x.row = o;  o += up256((size_t)R * x.n_c_pad * 8);
+    x.part = o; o += up256((size_t)world * rg * kXPart * 8);
+    x.bytes = o;
+    return x;
+}
+
+// Workspace of one rank: the whole row's scores [R][n_c_pad] fp32 (copied
+// out of the tagged row by the select), selection [R][nk] int32, own ranges
+// [R][2], the attend CTAs' partials.  Entries per row: this rank's raw rows
+// (rank 0) and at most min(nk, n_loc) own pages; the attend grid is sized
+// for the expected share, nk / world own pages (one wave, one merge batch
+// of partials), and a CTA takes more entries when a rank holds more.
+static Plan make_split_plan(int R, int n_c, int n_loc, int world, int nk, int n_sink, int n_near) {
+    Plan p = make_plan(R, n_loc, std::min(nk, n_loc), n_sink, n_near, Hier{});
+    p.ST = (n_loc + kScoreTile - 1) / kScoreTile;
+    if (p.E > 0) {
+        const int e_exp = p.RS + p.RN + std::min(n_loc, (nk + world - 1) / world);
+        int c = R > 0 ? kAttendPerSm * sm_count() / R : 1;
+        c = std::max(1, std::min({c, (e_exp + kTileEntries - 1) / kTileEntries, kMergeBatch}));
+        c = std::max(c, (p.E + 127) / 128);
+        p.AT = c;
+        p.EPC = (p.E + c - 1) / c;
+    }
+    const int max_tiles = p.E > 0 ? (p.E + kTileEntries - 1) / kTileEntries : 1;
+    p.off_scores = 0;
+    p.off_sel = up256((size_t)R * ((n_c + 31) & ~31) * 4);
+    p.off_sel_large = p.off_sel + up256((size_t)R * nk * 4);  // own ranges
+    p.off_parts = p.off_sel_large + up256((size_t)R * 2 * 4);
+    p.bytes = p.off_parts + up256((size_t)R * std::max(max_tiles, p.AT) * kPartFloats * 4);
+    return p;
+}
+
+static size_t split_score_smem() { return score_smem() + kWarps * 16 * 4; }
+
+static int decode_raw_split(const void* q, const zkv_raw_layer* layer, const zkv_raw_split* sp, int rows, int G,
+                            int n_max, int n_c, int nk, int n_sink, int near_start, int n_near, float scale,
+                            void* out, float* lse, int64_t* sel_out, int32_t* status, void* workspace,
+                            size_t ws_bytes, void* stream) {
+    if (!q || !layer || !sp || !sp->peer_base || !out || !workspace || rows < 0 || G < 1 || G > 8 ||
+        sp->world < 1 || sp->world > kMaxRanks || sp->rank < 0 || sp->rank >= sp->world || n_c < 2 || nk < 1 ||
+        nk >= n_c || n_sink < 0 || n_near < 0 || near_start < 0)
+        return ZKV_ERR_ARG;
+    if (n_c > kMaxChunks) return ZKV_ERR_CAPACITY;
+    int lo, hi, lo_last, hi_last;
+    split_range(n_c, sp->world, sp->rank, &lo, &hi);
+    split_range(n_c, sp->world, sp->world - 1, &lo_last, &hi_last);
+    if (hi_last <= lo_last) return ZKV_ERR_ARG;  // every rank holds at least one page
+    const int n_loc = hi - lo;
+    const bool raw_rows = sp->rank == 0;  // the sink and near rows live on rank 0
+    const int ns = raw_rows ? n_sink : 0, nn = raw_rows ? n_near : 0;
+    const zkv_raw_layer& L = *layer;
+    if (!L.keys || !L.values || !L.chunk_min || !L.chunk_max || L.kv_ld_row < kHeadDim || (L.kv_ld_row % kHeadDim) ||
+        L.page_base < 0 || n_max < n_loc)
+        return ZKV_ERR_ARG;
+    const int64_t cap = L.kv_ld_row / kHeadDim;
+    if (L.page_base + 16 * (int64_t)n_loc > cap || (int64_t)near_start + nn > cap || ns > cap) return ZKV_ERR_ARG;
+    if ((int64_t)rows * cap >= (int64_t)1 << 31) return ZKV_ERR_CAPACITY;
+    const Plan p = make_split_plan(rows, n_c, n_loc, sp->world, nk, ns, nn);
+    if (ws_bytes < p.bytes) return ZKV_ERR_ARG;
+    if (p.AT > kMaxTiles || (int64_t)rows * (p.ST + p.AT) >= ((int64_t)1 << 31) ||
+        (int64_t)rows * G * kXPart * sp->world >= ((int64_t)1 << 31))
+        return ZKV_ERR_CAPACITY;
+    for (int r = 0; r < sp->world; ++r)
+        if (!sp->peer_base[r] || ((uintptr_t)sp->peer_base[r] & 255)) return ZKV_ERR_ARG;
+    if (rows == 0) return ZKV_OK;
+    if (((uintptr_t)L.keys & 15) || ((uintptr_t)L.values & 15) || ((uintptr_t)L.chunk_min & 15) ||
+        ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)q & 3) || ((uintptr_t)workspace & 255))
+        return ZKV_ERR_ALIGN;
+    const XLayout x = x_layout(rows, G, n_c, sp->world);
+    Args a;
+    memset(&a, 0, sizeof(a));
+    if (!cached_maps(&a.tk, &a.tv, L.keys, L.values, (int64_t)rows * cap)) return ZKV_ERR_LAUNCH;
+    a.q = (const uint16_t*)q;
+    a.cmin = (const uint16_t*)L.chunk_min;
+    a.cmax = (const uint16_t*)L.chunk_max;
+    a.valid = L.valid;
+    a.cap = cap;
+    a.page_base = L.page_base;
+    a.R = rows;
+    a.G = G;
+    a.n_max = n_max;
+    a.n_c = n_loc;
+    a.nk = nk;
+    a.n_sink = ns;
+    a.near_start = near_start;
+    a.n_near = nn;
+    a.ST = p.ST;
+    a.AT = p.AT;
+    a.RS = p.RS;
+    a.RN = p.RN;
+    a.E = p.E;
+    a.EPC = p.EPC;
+    a.n_c_pad = x.n_c_pad;
+    a.sl2 = scale * 1.4426950408889634f;
+    a.out = (uint16_t*)out;
+    a.lse = lse;
+    a.sel_out = sel_out;
+    a.status = status;
+    a.rank = sp->rank;
+    a.world = sp->world;
+    a.chunk_lo = lo;
+    a.chunk_hi = hi;
+    a.n_total = n_c;
+    for (int r = 0; r < sp->world; ++r) {
+        uint8_t* b = (uint8_t*)sp->peer_base[r];
+        a.xrow[r] = (uint64_t*)(b + x.row);
+        a.xpart[r] = (uint64_t*)(b + x.part);
+    }
+    uint8_t* own = (uint8_t*)sp->peer_base[sp->rank];
+    a.ep_s = (uint32_t*)(own + x.ep_s);
+    a.ep_m = (uint32_t*)(own + x.ep_m);
+    uint8_t* ws = (uint8_t*)workspace;
+    a.scores = (float*)(ws + p.off_scores);
+    a.sel = (int32_t*)(ws + p.off_sel);
+    a.own_range = (int32_t*)(ws + p.off_sel_large);
+    a.parts = (float*)(ws + p.off_parts);
+    a.wait_ns = peer_wait_ns();
+
+    static bool attr_set[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ZKV_ERR_LAUNCH;
+    if (!attr_set[dev]) {
+        if (cudaFuncSetAttribute(raw_score_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)split_score_smem()) != cudaSuccess ||
+            cudaFuncSetAttribute(raw_attend_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)attend_smem()) != cudaSuccess)
+            return ZKV_ERR_LAUNCH;
+        attr_set[dev] = true;
+    }
+    void* args[] = {&a};
+    const cudaStream_t st = (cudaStream_t)stream;
+    int rc = launch_pdl((const void*)raw_score_kernel<true>, rows * p.ST, kThreads, split_score_smem(), st, args);
+    if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_select_kernel<true>, rows, kSelThreads, 0, st, args);
+    if (rc == ZKV_OK)
+        rc = launch_pdl((const void*)raw_attend_kernel<true>, rows * p.AT, kThreads, attend_smem(), st, args);
+    if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_merge_kernel<true>, rows * G, kHeadDim, 0, st, args);
     return rc;
 }
 
@@ -879,14 +1245,15 @@ int raw_quest_topk(const void* q, int G, const void* cmin, const void* cmax, con
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ZKV_ERR_LAUNCH;
     if (!attr_set[dev]) {
-        if (cudaFuncSetAttribute(raw_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem()) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(raw_score_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)score_smem()) != cudaSuccess)
             return ZKV_ERR_LAUNCH;
         attr_set[dev] = true;
     }
     void* args[] = {&a};
-    int rc = launch_pdl((const void*)raw_score_kernel, rows * a.ST, kThreads, score_smem(), stream, args);
-    if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_select_kernel, rows, kSelThreads, select_smem(), stream, args);
+    int rc = launch_pdl((const void*)raw_score_kernel<false>, rows * a.ST, kThreads, score_smem(), stream, args);
+    if (rc == ZKV_OK)
+        rc = launch_pdl((const void*)raw_select_kernel<false>, rows, kSelThreads, select_smem(), stream, args);
     return rc;
 }
 
@@ -939,4 +1306,35 @@ extern "C" int zkv_quest_large_minmax(const void* chunk_min, const void* chunk_m
         (const uint32_t*)chunk_min, (const uint32_t*)chunk_max, n_max, valid_end, factor, g_lo,
         (uint32_t*)large_min, (uint32_t*)large_max, large_valid, n_max_large);
     return launch_status();
+}
+
+extern "C" int zkv_raw_split_range(int n_c, int world, int rank, int* lo, int* hi) {
+    if (!lo || !hi || n_c < 0 || world < 1 || world > rawpg::kMaxRanks || rank < 0 || rank >= world)
+        return ZKV_ERR_ARG;
+    rawpg::split_range(n_c, world, rank, lo, hi);
+    return ZKV_OK;
+}
+
+extern "C" size_t zkv_raw_split_buffer_bytes(int rows, int G, int n_c, int world) {
+    if (rows < 0 || G < 1 || n_c < 0 || world < 1 || world > rawpg::kMaxRanks) return 0;
+    return rawpg::x_layout(rows, G, n_c, world).bytes;
+}
+
+extern "C" size_t zkv_page_decode_raw_split_ws_bytes(int rows, int n_c, int world, int rank, int nk, int n_sink,
+                                                     int n_near) {
+    if (rows < 0 || n_c < 0 || world < 1 || world > rawpg::kMaxRanks || rank < 0 || rank >= world || nk < 0 ||
+        n_sink < 0 || n_near < 0)
+        return 0;
+    int lo, hi;
+    rawpg::split_range(n_c, world, rank, &lo, &hi);
+    return rawpg::make_split_plan(rows, n_c, hi - lo, world, nk, rank == 0 ? n_sink : 0, rank == 0 ? n_near : 0)
+        .bytes;
+}
+
+extern "C" int zkv_page_decode_raw_split(const void* q, const zkv_raw_layer* layer, const zkv_raw_split* split,
+                                         int rows, int G, int n_max, int n_c, int nk, int n_sink, int near_start,
+                                         int n_near, float scale, void* out, float* lse, int64_t* sel_out,
+                                         int32_t* status, void* workspace, size_t ws_bytes, void* stream) {
+    return rawpg::decode_raw_split(q, layer, split, rows, G, n_max, n_c, nk, n_sink, near_start, n_near, scale, out,
+                                   lse, sel_out, status, workspace, ws_bytes, stream);
 }

@@ -726,6 +726,56 @@ def page_decode_raw(q, layer: RawLayer, n_c: int, nk: int, n_near: int, *, n_sin
     return out
 
 
+def raw_split_range(n_c: int, world: int, rank: int):
+    """(lo, hi): the global pages [lo, hi) rank holds in the raw sequence
+    split (per = ceil(n_c / world) rounded up to 16 pages)."""
+    lo, hi = ctypes.c_int(), ctypes.c_int()
+    check(lib().zkv_raw_split_range(int(n_c), int(world), int(rank), ctypes.byref(lo), ctypes.byref(hi)),
+          "zkv_raw_split_range")
+    return lo.value, hi.value
+
+
+def page_decode_raw_split(q, layer: RawLayer, split, n_c: int, nk: int, n_near: int, *, n_sink: int = 0,
+                          near_start: int = 0, scale=None, out=None, lse=None, sel_out=None, status=None,
+                          workspace=None):
+    """One rank's share of page_decode_raw under the sequence split:
+    q [bs,1,H*G,128] (the same on every rank) -> out [bs,1,H*G,128] bf16,
+    the same on every rank.  layer holds this rank's pages
+    raw_split_range(n_c, world, rank) as its local pages (rank 0 also the
+    sink / near rows); n_c and nk count the whole row's pages.  split: an
+    object with .struct (a ZkvRawSplit over the group's exchange buffers),
+    .rank and .world (seqsplit.RawSplitGroup).  sel_out [bs*H, nk] int64:
+    the whole selection (global ids).  workspace: uint8 device tensor of at
+    least zkv_page_decode_raw_split_ws_bytes(...) (default: one cached
+    buffer per device)."""
+    cmin = layer.tensors[0]
+    bs, H, n_max, D = cmin.shape
+    _dtype("q", q, torch.bfloat16)
+    G = q.shape[2] // H
+    qc = q.contiguous()
+    if out is None:
+        out = torch.empty(bs, 1, H * G, D, dtype=torch.bfloat16, device=q.device)
+    scale = (1.0 / D ** 0.5) if scale is None else float(scale)
+    rows = bs * H
+    if workspace is None:
+        shape = ("split", rows, int(n_c), split.world, split.rank, int(nk), int(n_sink), int(n_near))
+        need = _RAW_NEED.get(shape)
+        if need is None:
+            need = _RAW_NEED[shape] = int(lib().zkv_page_decode_raw_split_ws_bytes(*shape[1:]))
+        key = ("split", q.device.index if q.device.index is not None else torch.cuda.current_device())
+        ws = _RAW_WS.get(key)
+        if ws is None or ws.numel() < need:
+            ws = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=q.device)
+            _RAW_WS[key] = ws
+        workspace = ws
+    check(lib().zkv_page_decode_raw_split(_p(qc), ctypes.byref(layer.struct), ctypes.byref(split.struct), rows, G,
+                                          n_max, int(n_c), int(nk), int(n_sink), int(near_start), int(n_near),
+                                          scale, _p(out), _p(lse), _p(sel_out), _p(status), _p(workspace),
+                                          int(workspace.numel()), _stream(q)),
+          "zkv_page_decode_raw_split")
+    return out
+
+
 class LargeLayer:
     """Hierarchical Quest metadata of one layer: large_min / large_max
     [bs, H, n_max_large, 128] bf16 and large_valid [bs, H, n_max_large]

@@ -1,6 +1,10 @@
 """Sequence-split page-mode decode over one process per GPU (long contexts).
 
-The retrieval pages of a layer are split into contiguous ranges, one per
+Raw-row page mode: `RawSplitGroup` (zkv_page_decode_raw_split) -- the
+exchanges live inside the decode's own four kernels (scores and partials as
+tagged-word peer stores over NVLink with bounded waits); see its docstring.
+
+4-bit page mode: the retrieval pages of a layer are split into contiguous ranges, one per
 rank (rank r owns pages [r*per, min(n_c, (r+1)*per)), per = ceil(n_c/world));
 rank 0 also holds the sink and near rows.  One decode step per layer:
 
@@ -174,6 +178,30 @@ def _view(ptr: int, shape, dtype, device):
 _FLAGS_A, _FLAGS_B, _EPOCH, _DONE, _HEADER = 0, 32, 64, 68, 256
 
 
+def _share_buffer(nbytes: int, world: int, rank: int, group=None):
+    """Allocate this rank's zeroed exchange buffer (zkv_peer_alloc), send its
+    IPC handle to every rank (all_gather_object on `group`) and map every
+    peer's buffer (zkv_peer_open).  Returns (own base, the mappings this
+    process opened, a ctypes array of every rank's base in rank order)."""
+    L = _lib.lib()
+    ptr = ctypes.c_void_p()
+    handle = (ctypes.c_char * L.zkv_peer_handle_bytes())()
+    _lib.check(L.zkv_peer_alloc(int(nbytes), ctypes.byref(ptr), handle), "zkv_peer_alloc")
+    handles = [None] * world
+    if world > 1:
+        dist.all_gather_object(handles, bytes(handle), group=group)
+    bases, opened = [], []
+    for r in range(world):
+        if r == rank:
+            bases.append(ptr.value)
+            continue
+        p = ctypes.c_void_p()
+        _lib.check(L.zkv_peer_open(handles[r], ctypes.byref(p)), "zkv_peer_open")
+        opened.append(p.value)
+        bases.append(p.value)
+    return ptr.value, opened, (ctypes.c_void_p * world)(*bases)
+
+
 def peer_layout(rows: int, G: int, per: int, world: int, P: int) -> dict:
     """Byte offsets of the shared buffer (the same on every rank): header,
     score row [rows][world*per] fp32, partial outputs [world*P][rows*G][128]
@@ -211,27 +239,9 @@ class PeerGroup:
         # about two CTA waves' worth of clusters)
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.P = P = max(1, min(4, (2 * sms) // (rows * 8)))
-        L = _lib.lib()
         lay = peer_layout(rows, G, self.per, world, P)
         self.off_row, self.off_parts, self.off_lses, total = lay["row"], lay["parts"], lay["lses"], lay["total"]
-        ptr = ctypes.c_void_p()
-        handle = (ctypes.c_char * L.zkv_peer_handle_bytes())()
-        _lib.check(L.zkv_peer_alloc(total, ctypes.byref(ptr), handle), "zkv_peer_alloc")
-        self.base = ptr.value
-        self._opened = []
-        handles = [None] * world
-        if world > 1:
-            dist.all_gather_object(handles, bytes(handle), group=group)
-        bases = []
-        for r in range(world):
-            if r == rank:
-                bases.append(self.base)
-                continue
-            p = ctypes.c_void_p()
-            _lib.check(L.zkv_peer_open(handles[r], ctypes.byref(p)), "zkv_peer_open")
-            self._opened.append(p.value)
-            bases.append(p.value)
-        self.peer_base = (ctypes.c_void_p * world)(*bases)
+        self.base, self._opened, self.peer_base = _share_buffer(total, world, rank, group)
         dev = self.device
         self.row = _view(self.base + self.off_row, (bs, H, world * self.per), torch.float32, dev)
         self.parts = _view(self.base + self.off_parts, (world * P, rows * G, 128), torch.float32, dev)
@@ -326,6 +336,110 @@ def decode_step_p2p(q, layer: ops.PageLayer, pg: PeerGroup, *, n_sink: int = 0, 
     if check and not torch.cuda.is_current_stream_capturing():
         pg.check()
     return pg.out, pg.sel
+
+
+# --------------------------------------------------------------------------- raw-row split
+class RawSplitGroup:
+    """Sequence split of the raw-row page decode (ops.page_decode_raw) over
+    `world` ranks, one process per GPU, with the exchanges fused into the
+    decode's own kernels (zkv_page_decode_raw_split):
+
+      * the score kernel stores each rank's Quest scores straight into every
+        rank's score row (peer stores over NVLink) as 64-bit words {score,
+        epoch of the call}, so no fence or flag is needed;
+      * every rank's select kernel waits (bounded) until every word of its
+        row carries the call's epoch and picks the top nk of the whole row --
+        the same kernel and keys as on one GPU, so the selection is the
+        single-GPU selection exactly;
+      * each rank attends the selected pages it holds (rank 0 also the sink
+        and near rows), and the merge kernel stores each (row, head)'s
+        partial into every rank as tagged words, waits for all of them and
+        combines them in rank order: every rank ends with the same output.
+
+    Four launches per layer, as on one GPU; no collective and no separate
+    exchange launch.  Rank r holds the pages ops.raw_split_range(n_c, world,
+    r).  The exchange buffer (zkv_raw_split_buffer_bytes) is allocated
+    zeroed and shared once through CUDA IPC; its epochs live on the device,
+    so a captured CUDA graph replays correctly as long as every rank replays
+    the same calls.  One group serves any number of layers called in
+    sequence (the partial exchange of one call orders it before the next
+    call's score stores)."""
+
+    def __init__(self, rows: int, G: int, n_c: int, world: int, rank: int, device, group=None):
+        self.rows, self.G, self.n_c, self.world, self.rank = rows, G, n_c, world, rank
+        self.device = torch.device(device)
+        self.lo, self.hi = ops.raw_split_range(n_c, world, rank)
+        self.n_loc = self.hi - self.lo
+        L = _lib.lib()
+        nbytes = int(L.zkv_raw_split_buffer_bytes(rows, G, n_c, world))
+        if nbytes == 0:
+            raise ValueError("invalid raw split shape")
+        self.base, self._opened, self.peer_base = _share_buffer(nbytes, world, rank, group)
+        self.struct = _lib.ZkvRawSplit(ctypes.cast(self.peer_base, ctypes.POINTER(ctypes.c_void_p)), rank, world)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        torch.cuda.synchronize(self.device)
+        if world > 1:
+            dist.barrier(group=group)  # every mapping is open before the first store
+        self._group = group
+
+    def decode(self, q, layer: ops.RawLayer, nk: int, n_near: int, **kw):
+        """ops.page_decode_raw_split over this group's buffers (status word:
+        the group's unless given)."""
+        kw.setdefault("status", self.status)
+        return ops.page_decode_raw_split(q, layer, self, self.n_c, nk, n_near, **kw)
+
+    def check(self):
+        """Raise if a wait of this group gave up (a rank did not arrive within
+        the wait limit, zkv_peer_set_wait_ms); reads the status word, so it
+        synchronises.  After a timeout the ranks' epochs disagree: close this
+        group and build a new one."""
+        st = int(self.status.item())
+        if st != 0:
+            raise RuntimeError(f"raw split exchange failed: status {st} "
+                               f"({_lib.lib().zkv_status_string(st).decode()}); the group must be rebuilt")
+
+    def close(self):
+        """Unmap the peers and free the own buffer (after a barrier, so no
+        peer still writes into it)."""
+        if self.base is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self._group)
+        L = _lib.lib()
+        for p in self._opened:
+            L.zkv_peer_close(ctypes.c_void_p(p))
+        self._opened = []
+        L.zkv_peer_free(ctypes.c_void_p(self.base))
+        self.base = None
+
+
+def local_raw_layer(rc, lo: int, hi: int, rank: int):
+    """This rank's share of a full raw cache (workload.RawCache) as a
+    RawLayer: pages [lo, hi) as local pages 0.. (their Quest metadata and
+    raw rows copied out), and on rank 0 the sink rows in front and the near
+    rows behind them.  Returns (layer, near_start) for the rank's call."""
+    bs, H, _, D = rc.keys.shape
+    ns, nn = (rc.n_sink, rc.n_near) if rank == 0 else (0, 0)
+    n_loc = hi - lo
+    base = ns
+    near_start = base + 16 * n_loc
+    cap = max(1, near_start + nn)
+    keys = torch.zeros(bs, H, cap, D, dtype=rc.keys.dtype, device=rc.keys.device)
+    values = torch.zeros_like(keys)
+    t0 = rc.n_sink + 16 * lo
+    keys[:, :, base:near_start] = rc.keys[:, :, t0:t0 + 16 * n_loc]
+    values[:, :, base:near_start] = rc.values[:, :, t0:t0 + 16 * n_loc]
+    if ns:
+        keys[:, :, :ns] = rc.keys[:, :, :ns]
+        values[:, :, :ns] = rc.values[:, :, :ns]
+    if nn:
+        keys[:, :, near_start:near_start + nn] = rc.keys[:, :, rc.near_start:rc.near_start + nn]
+        values[:, :, near_start:near_start + nn] = rc.values[:, :, rc.near_start:rc.near_start + nn]
+    cmin = rc.chunk_min[:, :, lo:hi].contiguous()
+    cmax = rc.chunk_max[:, :, lo:hi].contiguous()
+    valid = rc.valid[:, :, lo:hi].contiguous()
+    return ops.RawLayer(cmin, cmax, valid, keys, values, base), near_start
 
 
 def set_peer_wait_ms(ms: int) -> None:
