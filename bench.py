@@ -660,8 +660,12 @@ def run_config3_split(args):
         graph.replay()
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as clk:
-        if world == 1:  # ranks would run different iteration counts of the waits
-            _soak(graph.replay, args.soak, stream)
+        # load for the clock samples: a fixed count of steps (every rank must
+        # replay the same number, so not a time budget), about args.soak s
+        with torch.cuda.stream(stream):
+            for _ in range(max(1, int(args.soak * 1000))):
+                graph.replay()
+        torch.cuda.synchronize()
         ms = _timed(graph.replay, args.steps, args.warmup, stream, world)
     # parity of the timed configuration: layer 0's selection and output
     # against the single-GPU decode of the same layer on this GPU
