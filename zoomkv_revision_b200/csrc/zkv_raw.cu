@@ -47,8 +47,10 @@ constexpr int kSlotBytes = 8192;                  // one page: K 2 x 2 KiB + V 2
 constexpr int kSlots = 2;                         // pages per warp of an attend CTA
 constexpr int kTileEntries = kWarps * kSlots;     // pages per attend CTA
 constexpr int kAttRegion = kTileEntries * kSlotBytes;  // 64 KiB
-constexpr int kScoreTile = kWarps * 16;           // chunks per score CTA (32 KiB of min/max)
-constexpr int kScoreRegion = kWarps * kSlotBytes; // 32 KiB
+constexpr int kScoreWarps = 4;                    // warps of a score CTA, 16 chunks each
+constexpr int kScoreThreads = kScoreWarps * 32;
+constexpr int kScoreTile = kScoreWarps * 16;      // chunks per score CTA (32 KiB of min/max)
+constexpr int kScoreRegion = kScoreWarps * kSlotBytes;
 constexpr int kPartFloats = 16 + 8 * kHeadDim;    // m[8], l[8], o[8][128]
 constexpr int kSelThreads = 1024;                 // threads of a select CTA
 constexpr int kMaxChunks = 16384;
@@ -321,15 +323,15 @@ __device__ __forceinline__ void split_scores(const Args& a, int r, int cc, int n
 // workspace (kSplit: to every rank's score row, split_scores).  Validity is
 // applied by the select (kSplit: here).
 template <bool kSplit>
-__global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_constant__ Args a) {
+__global__ void __launch_bounds__(kScoreThreads) raw_score_kernel(const __grid_constant__ Args a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* region = smem;                                   // [4 warps][8 KiB]: min 4 KiB, max 4 KiB
+    uint8_t* region = smem;                                   // [kScoreWarps][8 KiB]: min 4 KiB, max 4 KiB
     uint16_t* rq = reinterpret_cast<uint16_t*>(smem + kScoreRegion);
     uint64_t* bars = reinterpret_cast<uint64_t*>(rq + kHeadDim);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r = blockIdx.x / a.ST, tile = blockIdx.x % a.ST;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kWarps; ++i) mbar_init(bars + i, 1);
+        for (int i = 0; i < kScoreWarps; ++i) mbar_init(bars + i, 1);
         mbar_fence_init();
     }
     __syncthreads();
@@ -339,7 +341,7 @@ __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_consta
     int cc, src, nch;
     bool oob = false;
     if (a.group_ids) {  // sub-chunk scores of the row's selected large chunks (quest_chunk_score.cu:263-360)
-        const int j = tile * kWarps + warp;
+        const int j = tile * kScoreWarps + warp;
         cc = j * a.factor;
         nch = j < a.n_groups ? a.factor : 0;
         const int lid = nch ? __ldcg(a.group_ids + (int64_t)r * a.n_groups + j) : 0;
@@ -358,15 +360,16 @@ __global__ void __launch_bounds__(kThreads) raw_score_kernel(const __grid_consta
     }
     {   // GQA-mean query (compute() :1622-1626: fp32 sum in head order / G, bf16)
         const uint16_t* qr = a.q + (int64_t)r * a.G * kHeadDim;
-        const int d = threadIdx.x;
-        float acc = 0.f;
-        for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, bfbits2f(__ldg(qr + g * kHeadDim + d)));
-        rq[d] = f2bfbits(__fdiv_rn(acc, (float)a.G));
-        if (a.raw_q_out && tile == 0) a.raw_q_out[(int64_t)r * kHeadDim + d] = rq[d];
+        for (int d = threadIdx.x; d < kHeadDim; d += kScoreThreads) {
+            float acc = 0.f;
+            for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, bfbits2f(__ldg(qr + g * kHeadDim + d)));
+            rq[d] = f2bfbits(__fdiv_rn(acc, (float)a.G));
+            if (a.raw_q_out && tile == 0) a.raw_q_out[(int64_t)r * kHeadDim + d] = rq[d];
+        }
     }
     __syncthreads();
     if constexpr (kSplit) {
-        split_scores(a, r, cc, nch, slot, bars + warp, rq, reinterpret_cast<float*>(bars + kWarps) + 16 * warp);
+        split_scores(a, r, cc, nch, slot, bars + warp, rq, reinterpret_cast<float*>(bars + kScoreWarps) + 16 * warp);
         return;
     }
     if (nch == 0) return;
@@ -873,7 +876,7 @@ static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near, const Hier
     p.n_large_pad = (p.n_large + 31) & ~31;
     p.ST1 = hier ? (p.n_large + kScoreTile - 1) / kScoreTile : 0;
     if (hier)  // stage 2: one warp per selected large chunk
-        p.ST = (h.nk_large + kWarps - 1) / kWarps;
+        p.ST = (h.nk_large + kScoreWarps - 1) / kScoreWarps;
     else       // no scoring when every chunk is selected
         p.ST = nk < n_c ? (n_c + kScoreTile - 1) / kScoreTile : 0;
     const int n_scored = hier ? h.nk_large * h.factor : n_c;
@@ -904,7 +907,7 @@ static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near, const Hier
     return p;
 }
 
-static size_t score_smem() { return kScoreRegion + kHeadDim * 2 + kWarps * 8; }
+static size_t score_smem() { return kScoreRegion + kHeadDim * 2 + kScoreWarps * 8; }
 static size_t select_smem() { return 0; }
 static size_t attend_smem() { return 1024 + kAttRegion + kWarps * kSlots * 8; }
 
@@ -1027,13 +1030,13 @@ static int decode_raw(const void* q, const zkv_raw_layer* layer, int rows, int G
     const cudaStream_t st = (cudaStream_t)stream;
     int rc = ZKV_OK;
     if (hier) {
-        rc = launch_pdl((const void*)raw_score_kernel<false>, rows * p.ST1, kThreads, score_smem(), st, args1);
+        rc = launch_pdl((const void*)raw_score_kernel<false>, rows * p.ST1, kScoreThreads, score_smem(), st, args1);
         if (rc == ZKV_OK)
             rc = launch_pdl((const void*)raw_select_kernel<false>, rows, kSelThreads, select_smem(), st, args1);
         if (rc != ZKV_OK) return rc;
     }
     if (p.ST > 0) {
-        rc = launch_pdl((const void*)raw_score_kernel<false>, rows * p.ST, kThreads, score_smem(), st, args);
+        rc = launch_pdl((const void*)raw_score_kernel<false>, rows * p.ST, kScoreThreads, score_smem(), st, args);
         if (rc == ZKV_OK)
             rc = launch_pdl((const void*)raw_select_kernel<false>, rows, kSelThreads, select_smem(), st, args);
     }
@@ -1101,7 +1104,7 @@ static Plan make_split_plan(int R, int n_c, int n_loc, int world, int nk, int n_
     return p;
 }
 
-static size_t split_score_smem() { return score_smem() + kWarps * 16 * 4; }
+static size_t split_score_smem() { return score_smem() + kScoreWarps * 16 * 4; }
 
 static int decode_raw_split(const void* q, const zkv_raw_layer* layer, const zkv_raw_split* sp, int rows, int G,
                             int n_max, int n_c, int nk, int n_sink, int near_start, int n_near, float scale,
@@ -1200,7 +1203,7 @@ static int decode_raw_split(const void* q, const zkv_raw_layer* layer, const zkv
     }
     void* args[] = {&a};
     const cudaStream_t st = (cudaStream_t)stream;
-    int rc = launch_pdl((const void*)raw_score_kernel<true>, rows * p.ST, kThreads, split_score_smem(), st, args);
+    int rc = launch_pdl((const void*)raw_score_kernel<true>, rows * p.ST, kScoreThreads, split_score_smem(), st, args);
     if (rc == ZKV_OK) rc = launch_pdl((const void*)raw_select_kernel<true>, rows, kSelThreads, 0, st, args);
     if (rc == ZKV_OK)
         rc = launch_pdl((const void*)raw_attend_kernel<true>, rows * p.AT, kThreads, attend_smem(), st, args);
@@ -1251,7 +1254,7 @@ int raw_quest_topk(const void* q, int G, const void* cmin, const void* cmax, con
         attr_set[dev] = true;
     }
     void* args[] = {&a};
-    int rc = launch_pdl((const void*)raw_score_kernel<false>, rows * a.ST, kThreads, score_smem(), stream, args);
+    int rc = launch_pdl((const void*)raw_score_kernel<false>, rows * a.ST, kScoreThreads, score_smem(), stream, args);
     if (rc == ZKV_OK)
         rc = launch_pdl((const void*)raw_select_kernel<false>, rows, kSelThreads, select_smem(), stream, args);
     return rc;
