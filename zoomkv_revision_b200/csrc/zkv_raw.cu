@@ -885,11 +885,14 @@ static Plan make_plan(int R, int n_c, int nk, int n_sink, int n_near, const Hier
     p.E = p.RS + p.RN + nsel;
     // CTAs per row: one wave of attend CTAs when the rows allow it, at most
     // 128 entries per CTA (a warp's chunk ids in one warp-wide load), at least
-    // kTileEntries entries per CTA
+    // kTileEntries entries per CTA; a count just above one merge batch is
+    // trimmed to it (one round of partial loads in the merge for at most a
+    // quarter more entries per CTA)
     {
         const int slots = kAttendPerSm * sm_count();
         int c = R > 0 ? slots / R : 1;
         c = std::max(1, std::min(c, (p.E + kTileEntries - 1) / kTileEntries));
+        if (c > kMergeBatch && c <= kMergeBatch + kMergeBatch / 4) c = kMergeBatch;
         c = std::max(c, (p.E + 127) / 128);
         p.EPC = p.E > 0 ? (p.E + c - 1) / c : 1;
         p.AT = p.E > 0 ? (p.E + p.EPC - 1) / p.EPC : 1;
