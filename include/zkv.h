@@ -385,6 +385,9 @@ int zkv_page_decode_raw_hier(const void* q, const zkv_raw_layer* layer, const zk
 typedef struct zkv_raw_split {
     void* const* peer_base;  /* [world] every rank's exchange buffer as
                                 mapped in this process ([rank]: its own) */
+    size_t bytes;            /* size of each buffer (the same on every
+                                rank); a call whose shape needs more
+                                returns ZKV_ERR_CAPACITY                 */
     int rank, world;         /* world <= 8                               */
 } zkv_raw_split;
 

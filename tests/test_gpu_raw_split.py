@@ -161,7 +161,7 @@ def test_split_wait_expires_on_a_missing_rank():
 
     class Split:
         rank, world = 0, 2
-        struct = _lib.ZkvRawSplit(ctypes.cast(bases, ctypes.POINTER(ctypes.c_void_p)), 0, 2)
+        struct = _lib.ZkvRawSplit(ctypes.cast(bases, ctypes.POINTER(ctypes.c_void_p)), nbytes, 0, 2)
 
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
     S.set_peer_wait_ms(300)

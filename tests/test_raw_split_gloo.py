@@ -171,3 +171,29 @@ def test_split_buffer_and_workspace_sizes():
     # argument checks run before any launch
     assert L.zkv_page_decode_raw_split(None, None, None, R, G, 1, n_c, 256, 0, 0, 0, 1.0, None, None, None,
                                        None, None, 0, None) == 1  # ZKV_ERR_ARG
+
+
+def test_split_rejects_undersized_exchange_buffers():
+    """The call checks the declared size of the exchange buffers against its
+    shape before any device work: a group built for fewer rows (or a shorter
+    row) gets ZKV_ERR_CAPACITY (3) instead of stores past a peer's buffer.
+    The pointers are never dereferenced by these host-side checks."""
+    import ctypes
+    from zoomkv_revision_b200 import _lib
+    L = _lib.lib()
+    R, G, n_c, nk, world = 8, 4, 8184, 256, 2
+    need = int(L.zkv_raw_split_buffer_bytes(R, G, n_c, world))
+    fake = 1 << 20                                   # 256-byte aligned, never dereferenced here
+    bases = (ctypes.c_void_p * world)(fake, fake + (1 << 24))
+    lo, hi = ctypes.c_int(), ctypes.c_int()
+    assert L.zkv_raw_split_range(n_c, world, 0, ctypes.byref(lo), ctypes.byref(hi)) == 0
+    lay = _lib.ZkvRawLayer(fake, fake, None, fake, fake, 128 * (16 * hi.value + 128), 0)
+    ws = int(L.zkv_page_decode_raw_split_ws_bytes(R, n_c, world, 0, nk, 0, 128))
+
+    def call(nbytes):
+        sp = _lib.ZkvRawSplit(ctypes.cast(bases, ctypes.POINTER(ctypes.c_void_p)), nbytes, 0, world)
+        return L.zkv_page_decode_raw_split(fake, ctypes.byref(lay), ctypes.byref(sp), R, G, hi.value, n_c, nk, 0,
+                                           16 * hi.value, 128, 1.0, fake, None, None, None, fake, ws, None)
+
+    assert call(need - 256) == 3   # ZKV_ERR_CAPACITY
+    assert call(int(L.zkv_raw_split_buffer_bytes(R // 2, G, n_c, world))) == 3

@@ -42,7 +42,8 @@ class ZkvRawLayer(ctypes.Structure):
 
 class ZkvRawSplit(ctypes.Structure):
     """Mirror of `zkv_raw_split` (include/zkv.h)."""
-    _fields_ = [("peer_base", ctypes.POINTER(_c_void_p)), ("rank", _i32), ("world", _i32)]
+    _fields_ = [("peer_base", ctypes.POINTER(_c_void_p)), ("bytes", ctypes.c_size_t), ("rank", _i32),
+                ("world", _i32)]
 
 
 class ZkvQuestLarge(ctypes.Structure):

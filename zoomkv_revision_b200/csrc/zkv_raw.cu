@@ -1144,6 +1144,7 @@ static int decode_raw_split(const void* q, const zkv_raw_layer* layer, const zkv
         ((uintptr_t)L.chunk_max & 15) || ((uintptr_t)q & 3) || ((uintptr_t)workspace & 255))
         return ZKV_ERR_ALIGN;
     const XLayout x = x_layout(rows, G, n_c, sp->world);
+    if (sp->bytes < x.bytes) return ZKV_ERR_CAPACITY;  // the exchange buffers are too small for this shape
     Args a;
     memset(&a, 0, sizeof(a));
     if (!cached_maps(&a.tk, &a.tv, L.keys, L.values, (int64_t)rows * cap)) return ZKV_ERR_LAUNCH;

@@ -375,7 +375,9 @@ class RawSplitGroup:
         if nbytes == 0:
             raise ValueError("invalid raw split shape")
         self.base, self._opened, self.peer_base = _share_buffer(nbytes, world, rank, group)
-        self.struct = _lib.ZkvRawSplit(ctypes.cast(self.peer_base, ctypes.POINTER(ctypes.c_void_p)), rank, world)
+        self.nbytes = nbytes
+        self.struct = _lib.ZkvRawSplit(ctypes.cast(self.peer_base, ctypes.POINTER(ctypes.c_void_p)), nbytes, rank,
+                                       world)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         torch.cuda.synchronize(self.device)
         if world > 1:
@@ -386,6 +388,10 @@ class RawSplitGroup:
         """ops.page_decode_raw_split over this group's buffers (status word:
         the group's unless given)."""
         kw.setdefault("status", self.status)
+        bs, H = layer.tensors[0].shape[:2]
+        if bs * H != self.rows or q.shape[2] != self.rows // bs * self.G:
+            raise ValueError(f"this group was built for {self.rows} rows of G = {self.G}; got {bs * H} rows of "
+                             f"G = {q.shape[2] // H}")
         return ops.page_decode_raw_split(q, layer, self, self.n_c, nk, n_near, **kw)
 
     def check(self):
