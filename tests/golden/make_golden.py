@@ -474,7 +474,11 @@ def gen_rerank4(ref_root, out):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    # the reference checkout: ZKV_REFERENCE_ROOT, else a sibling directory of
+    # the repository named "reference"
+    repo = os.path.dirname(os.path.dirname(HERE))
+    ap.add_argument("--ref", default=os.environ.get("ZKV_REFERENCE_ROOT") or
+                    os.path.join(os.path.dirname(repo), "reference"))
     ap.add_argument("--out", default=HERE)
     a = ap.parse_args()
     sys.path.insert(0, os.path.join(a.ref, RUNTIME))
